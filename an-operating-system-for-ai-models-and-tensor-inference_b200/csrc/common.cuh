@@ -1,0 +1,98 @@
+// Device helpers shared by the sm_100a kernels.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#define MYOS_DEV __device__ __forceinline__
+
+namespace myos {
+
+constexpr int kWarp = 32;
+
+// BF16 is the top half of an f32 (crates/tensor_core/src/bf16.rs:61-63), so
+// promotion is a shift or a mask: exact, no rounding.
+MYOS_DEV float bf16_lo(uint32_t u) { return __uint_as_float(u << 16); }
+MYOS_DEV float bf16_hi(uint32_t u) { return __uint_as_float(u & 0xffff0000u); }
+MYOS_DEV float bf16_at(const uint16_t* p) { return __uint_as_float((uint32_t)(*p) << 16); }
+
+// Weights are read once per token: stream them past L1.
+MYOS_DEV uint4 ld_stream(const uint4* p) {
+  uint4 r;
+  asm("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+      : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+      : "l"(p));
+  return r;
+}
+
+MYOS_DEV float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+MYOS_DEV float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Programmatic dependent launch. wait: block until the preceding grid in the
+// stream has completed and its writes are visible (a no-op when the launch
+// carried no programmatic edge). launch: allow the next grid to be scheduled.
+MYOS_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+MYOS_DEV void pdl_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Fire-and-forget bulk prefetch of [p, p+bytes) into L2. p and bytes must be
+// 16-byte multiples; callers round.
+MYOS_DEV void prefetch_l2(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// Prefetch a byte range split into <=64 KiB pieces across the block's threads.
+MYOS_DEV void prefetch_range(const void* base, size_t bytes) {
+  uintptr_t a = (uintptr_t)base;
+  uintptr_t start = (a + 15) & ~(uintptr_t)15;
+  uintptr_t end = (a + bytes) & ~(uintptr_t)15;
+  if (end <= start) return;
+  const size_t piece = 65536;
+  size_t n = (end - start + piece - 1) / piece;
+  for (size_t i = threadIdx.x; i < n; i += blockDim.x) {
+    uintptr_t p = start + i * piece;
+    uintptr_t q = p + piece < end ? p + piece : end;
+    prefetch_l2((const void*)p, (uint32_t)(q - p));
+  }
+}
+
+// Sum over the block in a fixed order (deterministic). red holds >= 33 floats.
+MYOS_DEV float block_sum(float v, float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nwarps = (blockDim.x + 31) >> 5;
+  v = warp_sum(v);
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    float s = lane < nwarps ? red[lane] : 0.0f;
+    s = warp_sum(s);
+    if (lane == 0) red[32] = s;
+  }
+  __syncthreads();
+  float s = red[32];
+  __syncthreads();
+  return s;
+}
+
+// 8 promoted weights (one 16-byte chunk) against 8 staged activations.
+MYOS_DEV float dot8(const uint4& u, const float4& lo, const float4& hi, float acc) {
+  acc = fmaf(bf16_lo(u.x), lo.x, acc);
+  acc = fmaf(bf16_hi(u.x), lo.y, acc);
+  acc = fmaf(bf16_lo(u.y), lo.z, acc);
+  acc = fmaf(bf16_hi(u.y), lo.w, acc);
+  acc = fmaf(bf16_lo(u.z), hi.x, acc);
+  acc = fmaf(bf16_hi(u.z), hi.y, acc);
+  acc = fmaf(bf16_lo(u.w), hi.z, acc);
+  acc = fmaf(bf16_hi(u.w), hi.w, acc);
+  return acc;
+}
+
+}  // namespace myos

@@ -1,0 +1,981 @@
+// Engine: HBM weight arena, KV cache, token-step orchestration and the C ABI.
+//
+// A token step (model_core::forward_token, qwen25_block.rs:220-304) is 5
+// kernels per layer plus the head:
+//   QKV   fused RMSNorm(input_layernorm) -> [q|k|v] GEMV -> +bias
+//         (layer 0 also gathers the embedding row of the step's token)
+//   ATTN  RoPE(q,k) -> KV write at pos -> split-KV GQA -> combine
+//   O     o_proj GEMV -> residual += (attn_wire.rs:286-312)
+//   GU    fused RMSNorm(post_attention_layernorm) -> gate,up GEMV -> SiLU*up
+//   DOWN  down_proj GEMV -> residual += (qwen25_block.rs:280-288)
+//   HEAD  final RMSNorm -> tied/untied head GEMV -> logits + argmax ->
+//         advance the cursor (KvCache::advance once per token)
+// Every launch carries a programmatic-dependency edge so each kernel's
+// weight prefetch overlaps its predecessor; steps are replayed from CUDA
+// graphs, with token and position living in device memory (StepCtl).
+#include <fcntl.h>
+#include <math.h>
+#include <string.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "../../include/myos_cuda.h"
+#include "kernels.h"
+#include "safetensors.h"
+
+using namespace myos;
+
+namespace {
+
+constexpr int kSuffixes = 12;
+const char* kSuffix[kSuffixes] = {
+    "input_layernorm.weight",  "self_attn.q_proj.weight", "self_attn.q_proj.bias",
+    "self_attn.k_proj.weight", "self_attn.k_proj.bias",   "self_attn.v_proj.weight",
+    "self_attn.v_proj.bias",   "self_attn.o_proj.weight", "post_attention_layernorm.weight",
+    "mlp.gate_proj.weight",    "mlp.up_proj.weight",      "mlp.down_proj.weight"};
+const char* kEmbed = "model.embed_tokens.weight";
+const char* kFinalNorm = "model.norm.weight";
+const char* kLmHead = "lm_head.weight";
+
+struct LayerW {
+  uint16_t *wqkv, *wo, *wg, *wu, *wd;
+  float *bqkv, *ln1, *ln2;
+};
+
+enum GraphKind { G_FEED_NOHEAD = 0, G_FEED_HEAD = 1, G_ARGMAX_HEAD = 2 };
+
+size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+}  // namespace
+
+struct myos_ctx {
+  myos_shape s;
+  myos_opts o;
+  int device = 0;
+  int num_sms = 148;
+  cudaStream_t st = nullptr, copy_st = nullptr;
+  std::string err;
+  size_t qd = 0, kvd = 0, G = 1;
+  // HBM
+  uint8_t* warena = nullptr;
+  size_t warena_bytes = 0;
+  uint16_t *embed = nullptr, *lm_head = nullptr;
+  float* final_norm = nullptr;
+  std::vector<LayerW> layers;
+  void *kcache = nullptr, *vcache = nullptr;
+  size_t kv_layer_elems = 0;
+  float *resid = nullptr, *qkv = nullptr, *attn = nullptr, *act = nullptr, *logits = nullptr;
+  float *part_val = nullptr, *part_o = nullptr, *part_m = nullptr, *part_l = nullptr;
+  uint32_t* part_idx = nullptr;
+  unsigned* counters = nullptr;  // [0] head, [1..Hkv] attention
+  StepCtl* ctl = nullptr;
+  uint32_t *feed = nullptr, *rec_fed = nullptr, *rec_argmax = nullptr;
+  float *cos_t = nullptr, *sin_t = nullptr;
+  // pinned staging
+  uint8_t* pin[2] = {nullptr, nullptr};
+  size_t pin_bytes = 0;
+  cudaEvent_t pin_ev[2] = {nullptr, nullptr};
+  int pin_slot = 0;
+  cudaEvent_t load_ev = nullptr;  // recorded on copy_st after each load
+  StepCtl* ctl_host = nullptr;  // pinned mirror for uploads
+  // launch geometry
+  int grid_qkv = 0, grid_o = 0, grid_gu = 0, grid_down = 0, grid_head = 0;
+  int attn_chunk = 0, attn_nsplit = 0;
+  size_t prefetch_total = 40ull << 20;
+  // loaded-tensor bookkeeping
+  std::vector<uint8_t> have;  // per layer x suffix, then embed, final norm, lm_head
+  size_t len = 0;             // KV cursor (host mirror of ctl->pos)
+  std::map<std::pair<int, int>, cudaGraphExec_t> graphs;
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr, ev2 = nullptr;
+  float prefill_ms = 0.f, decode_ms = 0.f;
+  int steps_per_graph = 16;
+  bool profiling = false;
+};
+
+namespace {
+
+int fail(myos_ctx* c, int code, const std::string& msg) {
+  if (c) c->err = msg;
+  return code;
+}
+
+#define CK(call)                                                                   \
+  do {                                                                             \
+    cudaError_t e_ = (call);                                                       \
+    if (e_ != cudaSuccess)                                                         \
+      return fail(c, MYOS_ERR_CUDA, std::string(#call) + ": " + cudaGetErrorString(e_)); \
+  } while (0)
+
+size_t have_index(const myos_ctx* c, int layer, int suffix) {
+  return (size_t)layer * kSuffixes + suffix;
+}
+size_t have_embed(const myos_ctx* c) { return (size_t)c->s.num_layers * kSuffixes; }
+
+int grid_for(const myos_ctx* c, size_t rows) {
+  size_t g = (rows + 7) / 8;
+  size_t cap = (size_t)c->num_sms * 2;
+  if (g > cap) g = cap;
+  if (g < 1) g = 1;
+  return (int)g;
+}
+
+size_t prefetch_cap(const myos_ctx* c, int grid) {
+  if (c->prefetch_total == 0) return 0;
+  return (c->prefetch_total / (size_t)grid + 15) & ~(size_t)15;
+}
+
+// Host-built RoPE table: cos/sin of f32(pos) * (1 / powf(theta, 2i/d)) with
+// glibc libm, exactly rope.rs:186-194, so the device applies bit-identical
+// rotations.
+void rope_table(const myos_shape& s, size_t max_seq, std::vector<float>* cs,
+                std::vector<float>* sn) {
+  size_t half = s.head_dim / 2;
+  cs->assign(max_seq * half, 0.f);
+  sn->assign(max_seq * half, 0.f);
+  std::vector<float> inv(half);
+  for (size_t i = 0; i < half; ++i) {
+    volatile float exponent = (float)(2 * i) / (float)s.head_dim;
+    inv[i] = 1.0f / powf(s.rope_theta, exponent);
+  }
+  for (size_t p = 0; p < max_seq; ++p)
+    for (size_t i = 0; i < half; ++i) {
+      volatile float angle = (float)p * inv[i];
+      (*cs)[p * half + i] = cosf(angle);
+      (*sn)[p * half + i] = sinf(angle);
+    }
+}
+
+int check_shape(const myos_shape& s) {
+  if (s.hidden == 0 || s.num_q_heads == 0 || s.num_kv_heads == 0 || s.head_dim == 0 ||
+      s.head_dim % 2 != 0 || s.num_q_heads % s.num_kv_heads != 0 || s.intermediate == 0 ||
+      s.vocab == 0 || s.num_layers == 0)
+    return MYOS_ERR_SHAPE;
+  if (s.num_q_heads / s.num_kv_heads > 8 || s.head_dim > 256) return MYOS_ERR_SHAPE;
+  return MYOS_OK;
+}
+
+// Copy host bytes to device through the pinned ring (double-buffered).
+int stage_h2d(myos_ctx* c, void* dst, const void* src, size_t n) {
+  const uint8_t* s = (const uint8_t*)src;
+  uint8_t* d = (uint8_t*)dst;
+  int& slot = c->pin_slot;
+  while (n) {
+    size_t chunk = n < c->pin_bytes ? n : c->pin_bytes;
+    CK(cudaEventSynchronize(c->pin_ev[slot]));
+    memcpy(c->pin[slot], s, chunk);
+    CK(cudaMemcpyAsync(d, c->pin[slot], chunk, cudaMemcpyHostToDevice, c->copy_st));
+    CK(cudaEventRecord(c->pin_ev[slot], c->copy_st));
+    slot ^= 1;
+    s += chunk;
+    d += chunk;
+    n -= chunk;
+  }
+  return MYOS_OK;
+}
+
+int stage_bf16_as_f32(myos_ctx* c, float* dst, const void* src, size_t n) {
+  std::vector<float> tmp(n);
+  const uint8_t* b = (const uint8_t*)src;
+  for (size_t i = 0; i < n; ++i) {
+    uint32_t bits = ((uint32_t)b[2 * i] | ((uint32_t)b[2 * i + 1] << 8)) << 16;
+    memcpy(&tmp[i], &bits, 4);
+  }
+  return stage_h2d(c, dst, tmp.data(), n * 4);
+}
+
+int sync_copies(myos_ctx* c) {
+  CK(cudaStreamSynchronize(c->copy_st));
+  return MYOS_OK;
+}
+
+// ---------------------------------------------------------------- step enqueue
+enum KernelKind { K_QKV = 0, K_ATTN = 1, K_O = 2, K_GU = 3, K_DOWN = 4, K_HEAD = 5, K_END = 6 };
+
+int launch_kind(myos_ctx* c, int kind, int l, const uint32_t* feed, bool pdl, bool embed_l0) {
+  const myos_shape& s = c->s;
+  const int H = (int)s.hidden, I = (int)s.intermediate;
+  const int kv_bf16 = c->o.kv_dtype == MYOS_KV_BF16;
+  const size_t kv_elt = kv_bf16 ? 2 : 4;
+  if (kind == K_END) {
+    CK(launch_step_end(c->ctl, c->st, pdl));
+    return MYOS_OK;
+  }
+  if (kind == K_HEAD) {
+    GemvArgs h = {};
+    h.w = s.tied_head ? c->embed : c->lm_head;
+    h.M = (int)s.vocab;
+    h.K = H;
+    h.in.x = c->resid;
+    h.in.ctl = c->ctl;
+    h.in.gamma = c->final_norm;
+    h.in.eps = s.rms_eps;
+    h.y = c->logits;
+    h.prefetch_cap = prefetch_cap(c, c->grid_head);
+    h.part_val = c->part_val;
+    h.part_idx = c->part_idx;
+    h.counter = c->counters;
+    // While profiling, the head runs many times per step index: no records.
+    h.rec_fed = c->profiling ? nullptr : c->rec_fed;
+    h.rec_argmax = c->profiling ? nullptr : c->rec_argmax;
+    CK(launch_gemv(EPI_ARGMAX, h, c->grid_head, c->st, pdl));
+    return MYOS_OK;
+  }
+  const LayerW& w = c->layers[l];
+  if (kind == K_QKV) {
+    GemvArgs q = {};
+    q.w = w.wqkv;
+    q.M = (int)(c->qd + 2 * c->kvd);
+    q.K = H;
+    q.in.x = c->resid;
+    q.in.embed = (l == 0 && embed_l0) ? c->embed : nullptr;
+    q.in.feed = feed;
+    q.in.ctl = c->ctl;
+    q.in.x_store = (l == 0 && embed_l0) ? c->resid : nullptr;
+    q.in.gamma = w.ln1;
+    q.in.eps = s.rms_eps;
+    q.y = c->qkv;
+    q.bias = w.bqkv;
+    q.prefetch_cap = prefetch_cap(c, c->grid_qkv);
+    CK(launch_gemv(EPI_BIAS, q, c->grid_qkv, c->st, pdl));
+  } else if (kind == K_ATTN) {
+    AttnArgs at = {};
+    at.q = c->qkv;
+    at.kc = (uint8_t*)c->kcache + (size_t)l * c->kv_layer_elems * kv_elt;
+    at.vc = (uint8_t*)c->vcache + (size_t)l * c->kv_layer_elems * kv_elt;
+    at.S = (int)c->o.max_seq;
+    at.Hq = (int)s.num_q_heads;
+    at.Hkv = (int)s.num_kv_heads;
+    at.d = (int)s.head_dim;
+    at.G = (int)c->G;
+    at.ctl = c->ctl;
+    at.cos_t = c->cos_t;
+    at.sin_t = c->sin_t;
+    at.chunk = c->attn_chunk;
+    at.nsplit = c->attn_nsplit;
+    at.scale = 1.0f / sqrtf((float)s.head_dim);
+    at.part_o = c->part_o;
+    at.part_m = c->part_m;
+    at.part_l = c->part_l;
+    at.counters = c->counters + 1;
+    at.out = c->attn;
+    at.decode = 1;
+    CK(launch_attention(at, kv_bf16, c->st, pdl));
+  } else if (kind == K_O) {
+    GemvArgs o = {};
+    o.w = w.wo;
+    o.M = H;
+    o.K = (int)c->qd;
+    o.in.x = c->attn;
+    o.in.ctl = c->ctl;
+    o.y = c->resid;
+    o.prefetch_cap = prefetch_cap(c, c->grid_o);
+    CK(launch_gemv(EPI_RESID, o, c->grid_o, c->st, pdl));
+  } else if (kind == K_GU) {
+    GemvArgs gu = {};
+    gu.w = w.wg;
+    gu.w2 = w.wu;
+    gu.M = I;
+    gu.K = H;
+    gu.in.x = c->resid;
+    gu.in.ctl = c->ctl;
+    gu.in.gamma = w.ln2;
+    gu.in.eps = s.rms_eps;
+    gu.y = c->act;
+    gu.prefetch_cap = prefetch_cap(c, c->grid_gu);
+    CK(launch_gemv(EPI_SWIGLU, gu, c->grid_gu, c->st, pdl));
+  } else if (kind == K_DOWN) {
+    GemvArgs dn = {};
+    dn.w = w.wd;
+    dn.M = H;
+    dn.K = I;
+    dn.in.x = c->act;
+    dn.in.ctl = c->ctl;
+    dn.y = c->resid;
+    dn.prefetch_cap = prefetch_cap(c, c->grid_down);
+    CK(launch_gemv(EPI_RESID, dn, c->grid_down, c->st, pdl));
+  }
+  return MYOS_OK;
+}
+
+int enqueue_step(myos_ctx* c, bool head, const uint32_t* feed, bool first_pdl) {
+  const int L = (int)c->s.num_layers;
+  for (int l = 0; l < L; ++l) {
+    for (int k = K_QKV; k <= K_DOWN; ++k) {
+      int st = launch_kind(c, k, l, feed, (l > 0 || k > K_QKV) || first_pdl, true);
+      if (st) return st;
+    }
+  }
+  return launch_kind(c, head ? K_HEAD : K_END, 0, feed, true, true);
+}
+
+// Algorithmic bytes of one launch of each kind (weights + activations + KV).
+double kind_bytes(const myos_ctx* c, int kind) {
+  const myos_shape& s = c->s;
+  const double H = s.hidden, I = s.intermediate, V = s.vocab, qd = c->qd, kvd = c->kvd;
+  const double kv_elt = c->o.kv_dtype == MYOS_KV_BF16 ? 2 : 4;
+  switch (kind) {
+    case K_QKV: return (qd + 2 * kvd) * H * 2 + (qd + 2 * kvd) * 8 + H * 8;
+    case K_ATTN: return 2.0 * s.num_kv_heads * (double)(c->len + 1) * s.head_dim * kv_elt +
+                        (qd + 2 * kvd) * 4 + qd * 4;
+    case K_O: return H * qd * 2 + qd * 4 + H * 8;
+    case K_GU: return 2 * I * H * 2 + H * 8 + I * 4;
+    case K_DOWN: return H * I * 2 + I * 4 + H * 8;
+    case K_HEAD: return V * H * 2 + H * 8 + V * 4;
+  }
+  return 0;
+}
+
+int run_steps(myos_ctx* c, int kind, size_t nsteps) {
+  const bool head = kind != G_FEED_NOHEAD;
+  const uint32_t* feed = kind == G_ARGMAX_HEAD ? nullptr : c->feed;
+  if (!c->o.use_graphs) {
+    for (size_t i = 0; i < nsteps; ++i) {
+      int st = enqueue_step(c, head, feed, i > 0);
+      if (st) return st;
+    }
+    return MYOS_OK;
+  }
+  size_t done = 0;
+  while (done < nsteps) {
+    int chunk = (int)((nsteps - done) >= (size_t)c->steps_per_graph ? c->steps_per_graph : 1);
+    auto key = std::make_pair(kind, chunk);
+    auto it = c->graphs.find(key);
+    if (it == c->graphs.end()) {
+      cudaGraph_t g;
+      CK(cudaStreamBeginCapture(c->st, cudaStreamCaptureModeThreadLocal));
+      int st = MYOS_OK;
+      for (int i = 0; i < chunk && st == MYOS_OK; ++i) st = enqueue_step(c, head, feed, i > 0);
+      cudaError_t ce = cudaStreamEndCapture(c->st, &g);
+      if (st) return st;
+      if (ce != cudaSuccess)
+        return fail(c, MYOS_ERR_CUDA, std::string("graph capture: ") + cudaGetErrorString(ce));
+      cudaGraphExec_t ge;
+      ce = cudaGraphInstantiate(&ge, g, 0);
+      cudaGraphDestroy(g);
+      if (ce != cudaSuccess)
+        return fail(c, MYOS_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(ce));
+      it = c->graphs.emplace(key, ge).first;
+    }
+    CK(cudaGraphLaunch(it->second, c->st));
+    done += (size_t)chunk;
+  }
+  return MYOS_OK;
+}
+
+// Upload ctl.step = 0 (and pos when asked) before a call.
+int set_ctl(myos_ctx* c, bool set_pos) {
+  CK(cudaStreamWaitEvent(c->st, c->load_ev, 0));
+  c->ctl_host->step = 0;
+  c->ctl_host->pos = (uint32_t)c->len;
+  if (set_pos) {
+    CK(cudaMemcpyAsync(c->ctl, c->ctl_host, 8, cudaMemcpyHostToDevice, c->st));
+  } else {
+    CK(cudaMemcpyAsync(&c->ctl->step, &c->ctl_host->step, 4, cudaMemcpyHostToDevice, c->st));
+  }
+  return MYOS_OK;
+}
+
+int finish(myos_ctx* c) {
+  cudaError_t e = cudaStreamSynchronize(c->st);
+  if (e != cudaSuccess) return fail(c, MYOS_ERR_CUDA, std::string("step: ") + cudaGetErrorString(e));
+  return MYOS_OK;
+}
+
+int missing_weight(myos_ctx* c) {
+  const myos_shape& s = c->s;
+  if (!c->have[have_embed(c)]) return fail(c, MYOS_ERR_WEIGHT_MISSING, std::string("tensor not found: ") + kEmbed);
+  if (!c->have[have_embed(c) + 1])
+    return fail(c, MYOS_ERR_WEIGHT_MISSING, std::string("tensor not found: ") + kFinalNorm);
+  for (uint32_t l = 0; l < s.num_layers; ++l)
+    for (int k = 0; k < kSuffixes; ++k)
+      if (!c->have[have_index(c, (int)l, k)])
+        return fail(c, MYOS_ERR_WEIGHT_MISSING, "tensor not found: model.layers." +
+                                                   std::to_string(l) + "." + kSuffix[k]);
+  if (!s.tied_head && !c->have[have_embed(c) + 2])
+    return fail(c, MYOS_ERR_WEIGHT_MISSING, std::string("tensor not found: ") + kLmHead);
+  return MYOS_OK;
+}
+
+}  // namespace
+
+// ================================================================ C ABI
+extern "C" {
+
+const char* myos_version(void) { return "myos-b200 0.1 (sm_100a)"; }
+
+myos_shape myos_shape_qwen25_1_5b(void) {
+  myos_shape s;
+  s.hidden = 1536;
+  s.num_q_heads = 12;
+  s.num_kv_heads = 2;
+  s.head_dim = 128;
+  s.rope_theta = 1000000.0f;
+  s.intermediate = 8960;
+  s.vocab = 151936;
+  s.num_layers = 28;
+  s.rms_eps = 1e-6f;
+  s.tied_head = 1;
+  return s;
+}
+
+myos_shape myos_shape_qwen25_14b(void) {
+  myos_shape s;
+  s.hidden = 5120;
+  s.num_q_heads = 40;
+  s.num_kv_heads = 8;
+  s.head_dim = 128;
+  s.rope_theta = 1000000.0f;
+  s.intermediate = 13824;
+  s.vocab = 152064;
+  s.num_layers = 48;
+  s.rms_eps = 1e-6f;
+  s.tied_head = 0;
+  return s;
+}
+
+const char* myos_last_error(const myos_ctx* c) { return c ? c->err.c_str() : "null context"; }
+
+static int create_impl(myos_ctx* c, const myos_shape* shape, const myos_opts* opts) {
+  c->s = *shape;
+  c->o = *opts;
+  c->device = opts->device;
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev <= opts->device || opts->device < 0) {
+    cudaGetLastError();
+    return fail(c, MYOS_ERR_CUDA, "no CUDA device with this ordinal");
+  }
+  CK(cudaSetDevice(opts->device));
+  cudaDeviceProp prop;
+  CK(cudaGetDeviceProperties(&prop, opts->device));
+  if (prop.major != 10) return fail(c, MYOS_ERR_CUDA, "device is not sm_100 (B200)");
+  c->num_sms = prop.multiProcessorCount;
+  CK(kernels_init());
+  if (const char* e = getenv("MYOS_PREFETCH_MB")) c->prefetch_total = (size_t)atol(e) << 20;
+  if (const char* e = getenv("MYOS_STEPS_PER_GRAPH")) c->steps_per_graph = atoi(e) > 0 ? atoi(e) : 1;
+  const myos_shape& s = c->s;
+  c->qd = (size_t)s.num_q_heads * s.head_dim;
+  c->kvd = (size_t)s.num_kv_heads * s.head_dim;
+  c->G = s.num_q_heads / s.num_kv_heads;
+  const size_t H = s.hidden, I = s.intermediate, V = s.vocab, L = s.num_layers;
+  // weight arena
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    size_t o = off;
+    off = align256(off + bytes);
+    return o;
+  };
+  size_t o_embed = take(V * H * 2);
+  size_t o_lm = s.tied_head ? 0 : take(V * H * 2);
+  size_t o_fn = take(H * 4);
+  std::vector<size_t> lo(L * 8);
+  for (size_t l = 0; l < L; ++l) {
+    lo[l * 8 + 0] = take((c->qd + 2 * c->kvd) * H * 2);
+    lo[l * 8 + 1] = take(H * c->qd * 2);
+    lo[l * 8 + 2] = take(I * H * 2);
+    lo[l * 8 + 3] = take(I * H * 2);
+    lo[l * 8 + 4] = take(H * I * 2);
+    lo[l * 8 + 5] = take((c->qd + 2 * c->kvd) * 4);
+    lo[l * 8 + 6] = take(H * 4);
+    lo[l * 8 + 7] = take(H * 4);
+  }
+  c->warena_bytes = off;
+  CK(cudaMalloc(&c->warena, c->warena_bytes));
+  CK(cudaMemset(c->warena, 0, c->warena_bytes));
+  c->embed = (uint16_t*)(c->warena + o_embed);
+  c->lm_head = s.tied_head ? nullptr : (uint16_t*)(c->warena + o_lm);
+  c->final_norm = (float*)(c->warena + o_fn);
+  c->layers.resize(L);
+  for (size_t l = 0; l < L; ++l) {
+    LayerW& w = c->layers[l];
+    w.wqkv = (uint16_t*)(c->warena + lo[l * 8 + 0]);
+    w.wo = (uint16_t*)(c->warena + lo[l * 8 + 1]);
+    w.wg = (uint16_t*)(c->warena + lo[l * 8 + 2]);
+    w.wu = (uint16_t*)(c->warena + lo[l * 8 + 3]);
+    w.wd = (uint16_t*)(c->warena + lo[l * 8 + 4]);
+    w.bqkv = (float*)(c->warena + lo[l * 8 + 5]);
+    w.ln1 = (float*)(c->warena + lo[l * 8 + 6]);
+    w.ln2 = (float*)(c->warena + lo[l * 8 + 7]);
+  }
+  c->have.assign(L * kSuffixes + 3, 0);
+  // KV cache [L][Hkv][max_seq][d]
+  const size_t S = opts->max_seq, d = s.head_dim, kv_elt = opts->kv_dtype == MYOS_KV_BF16 ? 2 : 4;
+  c->kv_layer_elems = (size_t)s.num_kv_heads * S * d;
+  CK(cudaMalloc(&c->kcache, L * c->kv_layer_elems * kv_elt));
+  CK(cudaMalloc(&c->vcache, L * c->kv_layer_elems * kv_elt));
+  CK(cudaMemset(c->kcache, 0, L * c->kv_layer_elems * kv_elt));
+  CK(cudaMemset(c->vcache, 0, L * c->kv_layer_elems * kv_elt));
+  // geometry
+  c->grid_qkv = grid_for(c, c->qd + 2 * c->kvd);
+  c->grid_o = grid_for(c, H);
+  c->grid_gu = grid_for(c, I);
+  c->grid_down = grid_for(c, H);
+  c->grid_head = grid_for(c, V);
+  size_t nsplit = (S + 31) / 32;
+  size_t cap = (size_t)c->num_sms / s.num_kv_heads;
+  if (cap < 1) cap = 1;
+  if (nsplit > cap) nsplit = cap;
+  c->attn_nsplit = (int)nsplit;
+  c->attn_chunk = (int)((S + nsplit - 1) / nsplit);
+  // workspace
+  CK(cudaMalloc(&c->resid, H * 4));
+  CK(cudaMalloc(&c->qkv, (c->qd + 2 * c->kvd) * 4));
+  CK(cudaMalloc(&c->attn, c->qd * 4));
+  CK(cudaMalloc(&c->act, I * 4));
+  CK(cudaMalloc(&c->logits, V * 4));
+  CK(cudaMemset(c->logits, 0, V * 4));
+  CK(cudaMemset(c->resid, 0, H * 4));
+  CK(cudaMalloc(&c->part_val, (size_t)c->grid_head * 4));
+  CK(cudaMalloc(&c->part_idx, (size_t)c->grid_head * 4));
+  CK(cudaMalloc(&c->part_o, (size_t)s.num_kv_heads * nsplit * c->G * d * 4));
+  CK(cudaMalloc(&c->part_m, (size_t)s.num_kv_heads * nsplit * c->G * 4));
+  CK(cudaMalloc(&c->part_l, (size_t)s.num_kv_heads * nsplit * c->G * 4));
+  CK(cudaMalloc(&c->counters, (1 + s.num_kv_heads) * 4));
+  CK(cudaMemset(c->counters, 0, (1 + s.num_kv_heads) * 4));
+  CK(cudaMalloc(&c->ctl, sizeof(StepCtl)));
+  CK(cudaMemset(c->ctl, 0, sizeof(StepCtl)));
+  CK(cudaMalloc(&c->feed, (S + 1) * 4));
+  CK(cudaMalloc(&c->rec_fed, (S + 1) * 4));
+  CK(cudaMalloc(&c->rec_argmax, (S + 1) * 4));
+  std::vector<float> cs, sn;
+  rope_table(s, S, &cs, &sn);
+  CK(cudaMalloc(&c->cos_t, cs.size() * 4));
+  CK(cudaMalloc(&c->sin_t, sn.size() * 4));
+  CK(cudaMemcpy(c->cos_t, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
+  CK(cudaMemcpy(c->sin_t, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice));
+  // streams, staging
+  CK(cudaStreamCreateWithFlags(&c->st, cudaStreamNonBlocking));
+  CK(cudaStreamCreateWithFlags(&c->copy_st, cudaStreamNonBlocking));
+  c->pin_bytes = 32ull << 20;
+  for (int i = 0; i < 2; ++i) {
+    CK(cudaHostAlloc(&c->pin[i], c->pin_bytes, cudaHostAllocDefault));
+    CK(cudaEventCreateWithFlags(&c->pin_ev[i], cudaEventDisableTiming));
+    CK(cudaEventRecord(c->pin_ev[i], c->copy_st));
+  }
+  CK(cudaHostAlloc(&c->ctl_host, sizeof(StepCtl), cudaHostAllocDefault));
+  memset(c->ctl_host, 0, sizeof(StepCtl));
+  CK(cudaEventCreateWithFlags(&c->load_ev, cudaEventDisableTiming));
+  CK(cudaEventRecord(c->load_ev, c->copy_st));
+  CK(cudaEventCreate(&c->ev0));
+  CK(cudaEventCreate(&c->ev1));
+  CK(cudaEventCreate(&c->ev2));
+  CK(cudaDeviceSynchronize());
+  return MYOS_OK;
+}
+
+int myos_ctx_create(const myos_shape* shape, const myos_opts* opts, myos_ctx** out) {
+  if (!shape || !opts || !out) return MYOS_ERR_ARG;
+  *out = nullptr;
+  if (check_shape(*shape)) return MYOS_ERR_SHAPE;
+  if (opts->max_seq == 0) return MYOS_ERR_SHAPE;
+  if (opts->kv_dtype != MYOS_KV_F32 && opts->kv_dtype != MYOS_KV_BF16) return MYOS_ERR_ARG;
+  myos_ctx* c = new myos_ctx();
+  int st = create_impl(c, shape, opts);
+  if (st) {
+    myos_ctx_destroy(c);
+    return st;
+  }
+  *out = c;
+  return MYOS_OK;
+}
+
+void myos_ctx_destroy(myos_ctx* c) {
+  if (!c) return;
+  cudaSetDevice(c->device);
+  if (c->st) cudaStreamSynchronize(c->st);
+  for (auto& kv : c->graphs) cudaGraphExecDestroy(kv.second);
+  void* dev[] = {c->warena, c->kcache, c->vcache, c->resid, c->qkv, c->attn, c->act, c->logits,
+                 c->part_val, c->part_idx, c->part_o, c->part_m, c->part_l, c->counters, c->ctl,
+                 c->feed, c->rec_fed, c->rec_argmax, c->cos_t, c->sin_t};
+  for (void* p : dev)
+    if (p) cudaFree(p);
+  for (int i = 0; i < 2; ++i) {
+    if (c->pin[i]) cudaFreeHost(c->pin[i]);
+    if (c->pin_ev[i]) cudaEventDestroy(c->pin_ev[i]);
+  }
+  if (c->ctl_host) cudaFreeHost(c->ctl_host);
+  if (c->load_ev) cudaEventDestroy(c->load_ev);
+  if (c->ev0) cudaEventDestroy(c->ev0);
+  if (c->ev1) cudaEventDestroy(c->ev1);
+  if (c->ev2) cudaEventDestroy(c->ev2);
+  if (c->st) cudaStreamDestroy(c->st);
+  if (c->copy_st) cudaStreamDestroy(c->copy_st);
+  delete c;
+}
+
+int myos_load_tensor(myos_ctx* c, const char* name, int32_t dtype, const int64_t* shape,
+                     int32_t rank, const void* bytes, size_t nbytes) {
+  if (!c) return MYOS_ERR_ARG;
+  if (!name || !*name) return fail(c, MYOS_ERR_EMPTY_NAME, "tensor name is empty");
+  if (rank < 0 || (rank > 0 && !shape) || (nbytes && !bytes)) return fail(c, MYOS_ERR_ARG, "bad tensor arguments");
+  CK(cudaSetDevice(c->device));
+  const myos_shape& s = c->s;
+  const uint64_t H = s.hidden, I = s.intermediate, V = s.vocab, qd = c->qd, kvd = c->kvd;
+  std::string n(name);
+  int layer = -1, suffix = -1, global = -1;  // global: 0 embed, 1 final norm, 2 lm_head
+  std::vector<uint64_t> expect;
+  if (n == kEmbed) {
+    global = 0;
+    expect = {V, H};
+  } else if (n == kFinalNorm) {
+    global = 1;
+    expect = {H};
+  } else if (n == kLmHead) {
+    if (s.tied_head) return MYOS_OK;  // the tied model never reads it (qwen25_block.rs:290-301)
+    global = 2;
+    expect = {V, H};
+  } else if (n.compare(0, 13, "model.layers.") == 0) {
+    size_t dot = n.find('.', 13);
+    if (dot == std::string::npos) return MYOS_OK;
+    std::string idx = n.substr(13, dot - 13);
+    if (idx.empty() || idx.find_first_not_of("0123456789") != std::string::npos) return MYOS_OK;
+    if (idx.size() > 1 && idx[0] == '0') return MYOS_OK;
+    unsigned long li = strtoul(idx.c_str(), nullptr, 10);
+    if (li >= s.num_layers) return MYOS_OK;
+    std::string suf = n.substr(dot + 1);
+    for (int k = 0; k < kSuffixes; ++k)
+      if (suf == kSuffix[k]) suffix = k;
+    if (suffix < 0) return MYOS_OK;  // e.g. o_proj.bias: never read
+    layer = (int)li;
+    switch (suffix) {
+      case 0: case 8: expect = {H}; break;
+      case 1: expect = {qd, H}; break;
+      case 2: expect = {qd}; break;
+      case 3: case 5: expect = {kvd, H}; break;
+      case 4: case 6: expect = {kvd}; break;
+      case 7: expect = {H, qd}; break;
+      case 9: case 10: expect = {I, H}; break;
+      case 11: expect = {H, I}; break;
+    }
+  } else {
+    return MYOS_OK;
+  }
+  if (dtype != MYOS_BF16)
+    return fail(c, MYOS_ERR_WEIGHT_DTYPE, "tensor dtype is not bf16: " + n);
+  unsigned __int128 numel = 1;
+  for (int i = 0; i < rank; ++i) {
+    if (shape[i] < 0) return fail(c, MYOS_ERR_WEIGHT_SHAPE, "negative dimension: " + n);
+    numel *= (unsigned __int128)shape[i];
+  }
+  if (numel * 2 != (unsigned __int128)nbytes)
+    return fail(c, MYOS_ERR_WEIGHT_LENGTH, "tensor byte length does not match shape: " + n);
+  bool same = (size_t)rank == expect.size();
+  for (int i = 0; same && i < rank; ++i) same = (uint64_t)shape[i] == expect[i];
+  if (!same) return fail(c, MYOS_ERR_WEIGHT_SHAPE, "tensor shape does not match the layout: " + n);
+  int st = MYOS_OK;
+  if (global == 0) st = stage_h2d(c, c->embed, bytes, nbytes);
+  else if (global == 1) st = stage_bf16_as_f32(c, c->final_norm, bytes, H);
+  else if (global == 2) st = stage_h2d(c, c->lm_head, bytes, nbytes);
+  else {
+    const LayerW& w = c->layers[layer];
+    switch (suffix) {
+      case 0: st = stage_bf16_as_f32(c, w.ln1, bytes, H); break;
+      case 1: st = stage_h2d(c, w.wqkv, bytes, nbytes); break;
+      case 2: st = stage_bf16_as_f32(c, w.bqkv, bytes, qd); break;
+      case 3: st = stage_h2d(c, w.wqkv + qd * H, bytes, nbytes); break;
+      case 4: st = stage_bf16_as_f32(c, w.bqkv + qd, bytes, kvd); break;
+      case 5: st = stage_h2d(c, w.wqkv + (qd + kvd) * H, bytes, nbytes); break;
+      case 6: st = stage_bf16_as_f32(c, w.bqkv + qd + kvd, bytes, kvd); break;
+      case 7: st = stage_h2d(c, w.wo, bytes, nbytes); break;
+      case 8: st = stage_bf16_as_f32(c, w.ln2, bytes, H); break;
+      case 9: st = stage_h2d(c, w.wg, bytes, nbytes); break;
+      case 10: st = stage_h2d(c, w.wu, bytes, nbytes); break;
+      case 11: st = stage_h2d(c, w.wd, bytes, nbytes); break;
+    }
+  }
+  if (st) return st;
+  CK(cudaEventRecord(c->load_ev, c->copy_st));
+  if (global >= 0) c->have[have_embed(c) + global] = 1;
+  else c->have[have_index(c, layer, suffix)] = 1;
+  return MYOS_OK;
+}
+
+int myos_load_safetensors(myos_ctx* c, const char* path) {
+  if (!c || !path) return MYOS_ERR_ARG;
+  int fd = open(path, O_RDONLY);
+  if (fd < 0) return fail(c, MYOS_ERR_IO, std::string(path) + ": " + strerror(errno));
+  struct stat stbuf;
+  if (fstat(fd, &stbuf) != 0) {
+    int e = errno;
+    close(fd);
+    return fail(c, MYOS_ERR_IO, std::string(path) + ": " + strerror(e));
+  }
+  size_t len = (size_t)stbuf.st_size;
+  const uint8_t* buf = nullptr;
+  void* map = nullptr;
+  if (len > 0) {
+    map = mmap(nullptr, len, PROT_READ, MAP_PRIVATE, fd, 0);
+    if (map == MAP_FAILED) {
+      int e = errno;
+      close(fd);
+      return fail(c, MYOS_ERR_IO, std::string(path) + ": " + strerror(e));
+    }
+    buf = (const uint8_t*)map;
+    madvise(map, len, MADV_SEQUENTIAL);
+  }
+  close(fd);
+  std::vector<StTensor> ts;
+  size_t data_off = 0;
+  std::string why;
+  int rc = MYOS_OK;
+  if (st_parse(buf, len, &ts, &data_off, &why)) {
+    rc = fail(c, MYOS_ERR_PARSE, "weight buffer could not be parsed: " + why);
+  } else {
+    for (auto& t : ts)
+      if (t.dtype != "F32" && t.dtype != "F16" && t.dtype != "BF16") {
+        rc = fail(c, MYOS_ERR_UNSUPPORTED, "tensor dtype is not supported: " + t.name);
+        break;
+      }
+    for (size_t i = 0; rc == MYOS_OK && i < ts.size(); ++i)
+      if (ts[i].name.empty()) rc = fail(c, MYOS_ERR_EMPTY_NAME, "tensor name is empty");
+    for (size_t i = 0; rc == MYOS_OK && i < ts.size(); ++i) {
+      const StTensor& t = ts[i];
+      int dt = t.dtype == "F32" ? MYOS_F32 : t.dtype == "F16" ? MYOS_F16 : MYOS_BF16;
+      rc = myos_load_tensor(c, t.name.c_str(), dt, t.shape.data(), (int32_t)t.shape.size(),
+                            buf + data_off + t.begin, t.end - t.begin);
+    }
+    if (rc == MYOS_OK) rc = sync_copies(c);
+  }
+  if (map) munmap(map, len);
+  return rc;
+}
+
+int myos_check_safetensors(const char* path, size_t* n_tensors, char* err, size_t err_len) {
+  auto say = [&](int code, const std::string& msg) {
+    if (err && err_len) {
+      size_t n = msg.size() < err_len - 1 ? msg.size() : err_len - 1;
+      memcpy(err, msg.data(), n);
+      err[n] = 0;
+    }
+    return code;
+  };
+  if (!path) return MYOS_ERR_ARG;
+  int fd = open(path, O_RDONLY);
+  if (fd < 0) return say(MYOS_ERR_IO, std::string(path) + ": " + strerror(errno));
+  struct stat stbuf;
+  if (fstat(fd, &stbuf) != 0) {
+    int e = errno;
+    close(fd);
+    return say(MYOS_ERR_IO, std::string(path) + ": " + strerror(e));
+  }
+  size_t len = (size_t)stbuf.st_size;
+  void* map = nullptr;
+  if (len > 0) {
+    map = mmap(nullptr, len, PROT_READ, MAP_PRIVATE, fd, 0);
+    if (map == MAP_FAILED) {
+      int e = errno;
+      close(fd);
+      return say(MYOS_ERR_IO, std::string(path) + ": " + strerror(e));
+    }
+  }
+  close(fd);
+  std::vector<StTensor> ts;
+  size_t data_off = 0;
+  std::string why;
+  int rc = MYOS_OK;
+  if (st_parse((const uint8_t*)map, len, &ts, &data_off, &why)) {
+    rc = say(MYOS_ERR_PARSE, "weight buffer could not be parsed: " + why);
+  } else {
+    for (auto& t : ts) {
+      if (t.dtype != "F32" && t.dtype != "F16" && t.dtype != "BF16") {
+        rc = say(MYOS_ERR_UNSUPPORTED, "tensor dtype is not supported: " + t.name);
+        break;
+      }
+      if (t.name.empty()) {
+        rc = say(MYOS_ERR_EMPTY_NAME, "tensor name is empty");
+        break;
+      }
+    }
+  }
+  if (rc == MYOS_OK && n_tensors) *n_tensors = ts.size();
+  if (map) munmap(map, len);
+  return rc;
+}
+
+int myos_weights_ready(myos_ctx* c) {
+  if (!c) return 0;
+  return missing_weight(c) == MYOS_OK ? 1 : 0;
+}
+
+int myos_kv_len(const myos_ctx* c, size_t* len) {
+  if (!c || !len) return MYOS_ERR_ARG;
+  *len = c->len;
+  return MYOS_OK;
+}
+
+int myos_reset(myos_ctx* c) {
+  if (!c) return MYOS_ERR_ARG;
+  CK(cudaSetDevice(c->device));
+  c->len = 0;
+  int st = set_ctl(c, true);
+  if (st) return st;
+  return finish(c);
+}
+
+int myos_logits(myos_ctx* c, float* out) {
+  if (!c || !out) return MYOS_ERR_ARG;
+  CK(cudaSetDevice(c->device));
+  CK(cudaMemcpyAsync(out, c->logits, (size_t)c->s.vocab * 4, cudaMemcpyDeviceToHost, c->st));
+  return finish(c);
+}
+
+int myos_profile_kernels(myos_ctx* c, int iters, float* ms_out, double* bytes_out) {
+  if (!c || !ms_out || iters <= 0) return MYOS_ERR_ARG;
+  CK(cudaSetDevice(c->device));
+  int st = missing_weight(c);
+  if (st) return st;
+  if (c->len >= c->o.max_seq) return fail(c, MYOS_ERR_CACHE_FULL, "kv cache is full");
+  CK(cudaStreamWaitEvent(c->st, c->load_ev, 0));
+  StepCtl saved;
+  CK(cudaMemcpyAsync(&saved, c->ctl, sizeof saved, cudaMemcpyDeviceToHost, c->st));
+  std::vector<float> saved_logits(c->s.vocab);
+  CK(cudaMemcpyAsync(saved_logits.data(), c->logits, c->s.vocab * 4, cudaMemcpyDeviceToHost, c->st));
+  if ((st = finish(c))) return st;
+  const int L = (int)c->s.num_layers;
+  c->profiling = true;
+  for (int kind = K_QKV; kind <= K_HEAD; ++kind) {
+    // one untimed pass to warm instruction caches and the launch path
+    for (int l = 0; l < L; ++l)
+      if ((st = launch_kind(c, kind, l, nullptr, false, false))) break;
+    CK(cudaEventRecord(c->ev0, c->st));
+    int n = 0;
+    for (int it = 0; it < iters && !st; ++it)
+      for (int l = 0; l < L && !st; ++l, ++n) st = launch_kind(c, kind, l, nullptr, false, false);
+    CK(cudaEventRecord(c->ev1, c->st));
+    if (!st) st = finish(c);
+    if (st) {
+      c->profiling = false;
+      return st;
+    }
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, c->ev0, c->ev1);
+    ms_out[kind] = ms / (float)n;
+    if (bytes_out) bytes_out[kind] = kind_bytes(c, kind);
+  }
+  c->profiling = false;
+  CK(cudaMemcpyAsync(c->ctl, &saved, sizeof saved, cudaMemcpyHostToDevice, c->st));
+  CK(cudaMemcpyAsync(c->logits, saved_logits.data(), c->s.vocab * 4, cudaMemcpyHostToDevice, c->st));
+  return finish(c);
+}
+
+int myos_last_timing(const myos_ctx* c, float* prefill_ms, float* decode_ms) {
+  if (!c) return MYOS_ERR_ARG;
+  if (prefill_ms) *prefill_ms = c->prefill_ms;
+  if (decode_ms) *decode_ms = c->decode_ms;
+  return MYOS_OK;
+}
+
+int myos_kv_head(myos_ctx* c, uint32_t layer, uint32_t head, size_t pos, float* k, float* v) {
+  if (!c || !k || !v) return MYOS_ERR_ARG;
+  if (layer >= c->s.num_layers || head >= c->s.num_kv_heads || pos >= c->o.max_seq)
+    return fail(c, MYOS_ERR_CACHE_RANGE, "kv index is out of range");
+  CK(cudaSetDevice(c->device));
+  const size_t d = c->s.head_dim;
+  const size_t off = ((size_t)layer * c->s.num_kv_heads + head) * c->o.max_seq * d + pos * d;
+  if (c->o.kv_dtype == MYOS_KV_F32) {
+    CK(cudaMemcpyAsync(k, (float*)c->kcache + off, d * 4, cudaMemcpyDeviceToHost, c->st));
+    CK(cudaMemcpyAsync(v, (float*)c->vcache + off, d * 4, cudaMemcpyDeviceToHost, c->st));
+    return finish(c);
+  }
+  std::vector<uint16_t> kb(d), vb(d);
+  CK(cudaMemcpyAsync(kb.data(), (uint16_t*)c->kcache + off, d * 2, cudaMemcpyDeviceToHost, c->st));
+  CK(cudaMemcpyAsync(vb.data(), (uint16_t*)c->vcache + off, d * 2, cudaMemcpyDeviceToHost, c->st));
+  int st = finish(c);
+  if (st) return st;
+  for (size_t i = 0; i < d; ++i) {
+    uint32_t kb32 = (uint32_t)kb[i] << 16, vb32 = (uint32_t)vb[i] << 16;
+    memcpy(&k[i], &kb32, 4);
+    memcpy(&v[i], &vb32, 4);
+  }
+  return MYOS_OK;
+}
+
+int myos_forward_token(myos_ctx* c, uint32_t token, size_t pos, float* logits) {
+  if (!c) return MYOS_ERR_ARG;
+  CK(cudaSetDevice(c->device));
+  if (pos != c->len) return fail(c, MYOS_ERR_POSITION, "block position does not match the kv cursor");
+  if (pos >= c->o.max_seq) return fail(c, MYOS_ERR_CACHE_FULL, "kv cache is full");
+  int st = missing_weight(c);
+  if (st) return st;
+  if (token >= c->s.vocab) return fail(c, MYOS_ERR_TOKEN, "token id is out of range");
+  CK(cudaMemcpyAsync(c->feed, &token, 4, cudaMemcpyHostToDevice, c->st));
+  if ((st = set_ctl(c, false))) return st;
+  CK(cudaEventRecord(c->ev0, c->st));
+  if ((st = run_steps(c, G_FEED_HEAD, 1))) return st;
+  CK(cudaEventRecord(c->ev1, c->st));
+  if (logits) CK(cudaMemcpyAsync(logits, c->logits, (size_t)c->s.vocab * 4, cudaMemcpyDeviceToHost, c->st));
+  if ((st = finish(c))) return st;
+  cudaEventElapsedTime(&c->decode_ms, c->ev0, c->ev1);
+  c->len += 1;
+  return MYOS_OK;
+}
+
+int myos_prefill(myos_ctx* c, const uint32_t* ids, size_t n, float* logits) {
+  if (!c) return MYOS_ERR_ARG;
+  if (n == 0 || !ids) return fail(c, MYOS_ERR_SHAPE, "block shape does not match the buffers");
+  CK(cudaSetDevice(c->device));
+  size_t start = c->len;
+  if (start >= c->o.max_seq || start + n > c->o.max_seq) return fail(c, MYOS_ERR_CACHE_FULL, "kv cache is full");
+  for (size_t i = 0; i < n; ++i)
+    if (ids[i] >= c->s.vocab) return fail(c, MYOS_ERR_TOKEN, "token id is out of range");
+  int st = missing_weight(c);
+  if (st) return st;
+  CK(cudaMemcpyAsync(c->feed, ids, n * 4, cudaMemcpyHostToDevice, c->st));
+  if ((st = set_ctl(c, false))) return st;
+  CK(cudaEventRecord(c->ev0, c->st));
+  if (n > 1 && (st = run_steps(c, G_FEED_NOHEAD, n - 1))) return st;
+  if ((st = run_steps(c, G_FEED_HEAD, 1))) return st;
+  CK(cudaEventRecord(c->ev1, c->st));
+  if (logits) CK(cudaMemcpyAsync(logits, c->logits, (size_t)c->s.vocab * 4, cudaMemcpyDeviceToHost, c->st));
+  if ((st = finish(c))) return st;
+  cudaEventElapsedTime(&c->prefill_ms, c->ev0, c->ev1);
+  c->len += n;
+  return MYOS_OK;
+}
+
+int myos_greedy_decode(myos_ctx* c, size_t steps, uint32_t* out_ids) {
+  if (!c || (steps && !out_ids)) return MYOS_ERR_ARG;
+  CK(cudaSetDevice(c->device));
+  int st = missing_weight(c);
+  if (st) return st;
+  size_t room = c->len < c->o.max_seq ? c->o.max_seq - c->len : 0;
+  size_t run = steps < room ? steps : room;
+  if ((st = set_ctl(c, false))) return st;
+  CK(cudaEventRecord(c->ev0, c->st));
+  if (run && (st = run_steps(c, G_ARGMAX_HEAD, run))) return st;
+  CK(cudaEventRecord(c->ev1, c->st));
+  if (run) CK(cudaMemcpyAsync(out_ids, c->rec_fed, run * 4, cudaMemcpyDeviceToHost, c->st));
+  if ((st = finish(c))) return st;
+  cudaEventElapsedTime(&c->decode_ms, c->ev0, c->ev1);
+  c->len += run;
+  if (run < steps) return fail(c, MYOS_ERR_CACHE_FULL, "kv cache is full");
+  return MYOS_OK;
+}
+
+int myos_forced_decode(myos_ctx* c, const uint32_t* ids, size_t steps, uint32_t* argmax_out) {
+  if (!c || (steps && (!ids || !argmax_out))) return MYOS_ERR_ARG;
+  CK(cudaSetDevice(c->device));
+  int st = missing_weight(c);
+  if (st) return st;
+  if (c->len + steps > c->o.max_seq) return fail(c, MYOS_ERR_CACHE_FULL, "kv cache is full");
+  for (size_t i = 0; i < steps; ++i)
+    if (ids[i] >= c->s.vocab) return fail(c, MYOS_ERR_TOKEN, "token id is out of range");
+  if (!steps) return MYOS_OK;
+  CK(cudaMemcpyAsync(c->feed, ids, steps * 4, cudaMemcpyHostToDevice, c->st));
+  if ((st = set_ctl(c, false))) return st;
+  CK(cudaEventRecord(c->ev0, c->st));
+  if ((st = run_steps(c, G_FEED_HEAD, steps))) return st;
+  CK(cudaEventRecord(c->ev1, c->st));
+  CK(cudaMemcpyAsync(argmax_out, c->rec_argmax, steps * 4, cudaMemcpyDeviceToHost, c->st));
+  if ((st = finish(c))) return st;
+  cudaEventElapsedTime(&c->decode_ms, c->ev0, c->ev1);
+  c->len += steps;
+  return MYOS_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,88 @@
+// Kernel argument blocks and host-side launchers for the decode step.
+#pragma once
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace myos {
+
+// Device-resident step control. Kernels read it only after their
+// programmatic-dependency wait, so a whole token step (or several) can run
+// from a CUDA graph with no host round trip.
+struct StepCtl {
+  uint32_t pos;     // KV slot this step writes (KvCache cursor)
+  uint32_t step;    // index of this step within the current call
+  uint32_t argmax;  // first maximum of the most recent logits
+  uint32_t fed;     // token embedded by this step
+  uint32_t err;     // sticky error bits
+  uint32_t pad[3];
+};
+
+// How a GEMV block stages its input vector in shared memory.
+struct GemvInput {
+  const float* x;         // f32 [K] (ignored in embed mode)
+  const uint16_t* embed;  // embed mode: x[j] = bf16(embed[token*K + j])
+  const uint32_t* feed;   // embed mode token: feed[ctl->step], else ctl->argmax
+  StepCtl* ctl;
+  float* x_store;         // embed mode: block 0 writes the gathered row here
+  const float* gamma;     // RMSNorm weight (promoted f32) or null
+  float eps;
+};
+
+enum EpiKind { EPI_STORE = 0, EPI_BIAS = 1, EPI_RESID = 2, EPI_SWIGLU = 3, EPI_ARGMAX = 4 };
+
+struct GemvArgs {
+  const uint16_t* w;   // [M, K] row-major bf16
+  const uint16_t* w2;  // EPI_SWIGLU: up_proj [M, K]
+  int M, K;
+  GemvInput in;
+  float* y;            // output [M]; EPI_RESID: residual updated in place
+  const float* bias;   // EPI_BIAS
+  size_t prefetch_cap; // bytes of this block's rows to pull into L2 before the wait
+  // EPI_ARGMAX
+  float* part_val;
+  uint32_t* part_idx;
+  unsigned* counter;
+  uint32_t* rec_fed;
+  uint32_t* rec_argmax;
+};
+
+struct AttnArgs {
+  const float* q;        // decode: qkv buffer [q | k | v] before RoPE; op: q [Hq*d]
+  void* kc;              // this layer's K: [Hkv][S][d] of the cache type
+  void* vc;
+  int S;                 // slot stride (max_seq)
+  int Hq, Hkv, d, G;
+  int nkeys_fixed;       // op mode: keys 0..nkeys_fixed-1
+  StepCtl* ctl;          // decode mode: keys 0..ctl->pos, new key at ctl->pos
+  const float* cos_t;    // [S][d/2], host-built with libm
+  const float* sin_t;
+  int chunk, nsplit;
+  float scale;           // 1/sqrtf(d), computed on the host as the reference does
+  float* part_o;         // [Hkv][nsplit][G][d]
+  float* part_m;         // [Hkv][nsplit][G]
+  float* part_l;
+  unsigned* counters;    // [Hkv], zero between launches
+  float* out;            // [Hq*d]
+  int decode;
+};
+
+// Launchers. pdl=true attaches a programmatic-serialization edge to the
+// previous launch in the stream.
+cudaError_t launch_gemv(int epi, const GemvArgs& a, int grid, cudaStream_t st, bool pdl);
+cudaError_t launch_attention(const AttnArgs& a, int kv_bf16, cudaStream_t st, bool pdl);
+cudaError_t launch_step_end(StepCtl* ctl, cudaStream_t st, bool pdl);
+cudaError_t launch_argmax(const float* v, int n, float* part_val, uint32_t* part_idx,
+                          unsigned* counter, uint32_t* out, int grid, cudaStream_t st);
+cudaError_t launch_swiglu_mul(float* h, const float* gate, const float* up, int n, cudaStream_t st);
+cudaError_t launch_rope(float* y, const float* x, int len, int head_dim, const float* cos_row,
+                        const float* sin_row, cudaStream_t st);
+cudaError_t launch_rmsnorm(float* y, const float* x, const float* gamma, int n, float eps,
+                           cudaStream_t st);
+cudaError_t kernels_init();  // raises dynamic shared-memory limits once per device
+
+size_t gemv_smem_bytes(int K);
+size_t attn_smem_bytes(int G, int d);
+int attn_dpl(int d);
+
+}  // namespace myos

@@ -973,12 +973,13 @@ int orc_prefill(orc_model* md, const orc_map* m, const uint32_t* tokens, size_t 
 int orc_greedy_decode(orc_model* md, const orc_map* m, size_t steps, uint32_t* out,
                       float* logits_dump, float* gap) {
   for (size_t i = 0; i < steps; ++i) {
+    // gap[i] belongs to the logits that chose out[i] (before this forward).
     uint32_t tok = orc_greedy_token(md->logits.data(), md->s.vocab);
+    if (gap) gap[i] = top2_gap(md->logits.data(), md->s.vocab);
     int st = orc_forward_token(md, m, tok, md->len);
     if (st) return st;
     out[i] = tok;
     if (logits_dump) memcpy(logits_dump + i * md->s.vocab, md->logits.data(), md->s.vocab * 4);
-    if (gap) gap[i] = top2_gap(md->logits.data(), md->s.vocab);
   }
   return ORC_OK;
 }

@@ -21,3 +21,14 @@ def orc():
 
     orc_mod.build()
     return orc_mod
+
+
+def pytest_collection_modifyitems(config, items):
+    """GPU tests need a CUDA device; on a CPU-only host they are skipped."""
+    has_gpu = os.path.exists("/dev/nvidiactl") or os.path.exists("/dev/nvidia0")
+    if has_gpu:
+        return
+    skip = pytest.mark.skip(reason="no CUDA device on this host")
+    for item in items:
+        if "gpu" in item.keywords:
+            item.add_marker(skip)
