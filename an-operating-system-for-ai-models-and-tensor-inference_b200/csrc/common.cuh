@@ -64,6 +64,79 @@ MYOS_DEV void prefetch_range(const void* base, size_t bytes) {
   }
 }
 
+// ---------------------------------------------------------------- mbarrier + bulk copy
+// Shared-memory mbarriers track the bulk (TMA-engine) copies of weight
+// stages. Every wait is bounded: after kWaitLimit polls it gives up, raises
+// a bit in *err and returns false, so a broken pipeline ends the kernel with
+// an error the host reads instead of hanging the GPU.
+constexpr uint32_t kWaitLimit = 1u << 25;
+constexpr uint32_t kErrWaitFull = 1u, kErrWaitEmpty = 2u;
+
+MYOS_DEV uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+MYOS_DEV void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+MYOS_DEV void mbar_fence_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+MYOS_DEV void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+MYOS_DEV void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+MYOS_DEV bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+MYOS_DEV uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Bounded wait for the phase with the given parity to complete: gives up
+// after kWaitLimit polls or one second, whichever comes first.
+MYOS_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* err, uint32_t code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t i = 1; i < kWaitLimit; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 1023u) == 0 && global_ns() - t0 > 1000000000ull) break;
+  }
+  if (err) atomicOr(err, code);
+  return false;
+}
+
+// 1-D bulk copy global -> this CTA's shared memory, completing on bar.
+// dst, src 16-byte aligned; bytes a multiple of 16.
+MYOS_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Named barrier over the first nthreads threads of the block (id 1..15).
+MYOS_DEV void named_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
 // Sum over the block in a fixed order (deterministic). red holds >= 33 floats.
 MYOS_DEV float block_sum(float v, float* red) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;

@@ -87,7 +87,7 @@ struct myos_ctx {
   // launch geometry
   int grid_qkv = 0, grid_o = 0, grid_gu = 0, grid_down = 0, grid_head = 0;
   int attn_chunk = 0, attn_nsplit = 0;
-  size_t prefetch_total = 40ull << 20;
+  size_t prefetch_total = 0;  // bulk L2 prefetch (MYOS_PREFETCH_MB); measured slower, off
   // loaded-tensor bookkeeping
   std::vector<uint8_t> have;  // per layer x suffix, then embed, final norm, lm_head
   size_t len = 0;             // KV cursor (host mirror of ctl->pos)
@@ -116,14 +116,6 @@ size_t have_index(const myos_ctx* c, int layer, int suffix) {
   return (size_t)layer * kSuffixes + suffix;
 }
 size_t have_embed(const myos_ctx* c) { return (size_t)c->s.num_layers * kSuffixes; }
-
-int grid_for(const myos_ctx* c, size_t rows) {
-  size_t g = (rows + 7) / 8;
-  size_t cap = (size_t)c->num_sms * 2;
-  if (g > cap) g = cap;
-  if (g < 1) g = 1;
-  return (int)g;
-}
 
 size_t prefetch_cap(const myos_ctx* c, int grid) {
   if (c->prefetch_total == 0) return 0;
@@ -221,6 +213,7 @@ int launch_kind(myos_ctx* c, int kind, int l, const uint32_t* feed, bool pdl, bo
     h.part_idx = c->part_idx;
     h.counter = c->counters;
     // While profiling, the head runs many times per step index: no records.
+    h.err = &c->ctl->err;
     h.rec_fed = c->profiling ? nullptr : c->rec_fed;
     h.rec_argmax = c->profiling ? nullptr : c->rec_argmax;
     CK(launch_gemv(EPI_ARGMAX, h, c->grid_head, c->st, pdl));
@@ -241,6 +234,7 @@ int launch_kind(myos_ctx* c, int kind, int l, const uint32_t* feed, bool pdl, bo
     q.in.eps = s.rms_eps;
     q.y = c->qkv;
     q.bias = w.bqkv;
+    q.err = &c->ctl->err;
     q.prefetch_cap = prefetch_cap(c, c->grid_qkv);
     CK(launch_gemv(EPI_BIAS, q, c->grid_qkv, c->st, pdl));
   } else if (kind == K_ATTN) {
@@ -274,6 +268,7 @@ int launch_kind(myos_ctx* c, int kind, int l, const uint32_t* feed, bool pdl, bo
     o.in.x = c->attn;
     o.in.ctl = c->ctl;
     o.y = c->resid;
+    o.err = &c->ctl->err;
     o.prefetch_cap = prefetch_cap(c, c->grid_o);
     CK(launch_gemv(EPI_RESID, o, c->grid_o, c->st, pdl));
   } else if (kind == K_GU) {
@@ -287,6 +282,7 @@ int launch_kind(myos_ctx* c, int kind, int l, const uint32_t* feed, bool pdl, bo
     gu.in.gamma = w.ln2;
     gu.in.eps = s.rms_eps;
     gu.y = c->act;
+    gu.err = &c->ctl->err;
     gu.prefetch_cap = prefetch_cap(c, c->grid_gu);
     CK(launch_gemv(EPI_SWIGLU, gu, c->grid_gu, c->st, pdl));
   } else if (kind == K_DOWN) {
@@ -297,6 +293,7 @@ int launch_kind(myos_ctx* c, int kind, int l, const uint32_t* feed, bool pdl, bo
     dn.in.x = c->act;
     dn.in.ctl = c->ctl;
     dn.y = c->resid;
+    dn.err = &c->ctl->err;
     dn.prefetch_cap = prefetch_cap(c, c->grid_down);
     CK(launch_gemv(EPI_RESID, dn, c->grid_down, c->st, pdl));
   }
@@ -382,8 +379,16 @@ int set_ctl(myos_ctx* c, bool set_pos) {
 }
 
 int finish(myos_ctx* c) {
-  cudaError_t e = cudaStreamSynchronize(c->st);
+  cudaError_t e = cudaMemcpyAsync(&c->ctl_host->err, &c->ctl->err, 4, cudaMemcpyDeviceToHost, c->st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(c->st);
   if (e != cudaSuccess) return fail(c, MYOS_ERR_CUDA, std::string("step: ") + cudaGetErrorString(e));
+  if (c->ctl_host->err) {
+    const uint32_t bits = c->ctl_host->err;
+    c->ctl_host->err = 0;
+    cudaMemcpy(&c->ctl->err, &c->ctl_host->err, 4, cudaMemcpyHostToDevice);
+    return fail(c, MYOS_ERR_TIMEOUT,
+                "a bounded device wait gave up (bits " + std::to_string(bits) + ")");
+  }
   return MYOS_OK;
 }
 
@@ -511,11 +516,11 @@ static int create_impl(myos_ctx* c, const myos_shape* shape, const myos_opts* op
   CK(cudaMemset(c->kcache, 0, L * c->kv_layer_elems * kv_elt));
   CK(cudaMemset(c->vcache, 0, L * c->kv_layer_elems * kv_elt));
   // geometry
-  c->grid_qkv = grid_for(c, c->qd + 2 * c->kvd);
-  c->grid_o = grid_for(c, H);
-  c->grid_gu = grid_for(c, I);
-  c->grid_down = grid_for(c, H);
-  c->grid_head = grid_for(c, V);
+  c->grid_qkv = gemv_grid((int)(c->qd + 2 * c->kvd), (int)H, 1, c->num_sms);
+  c->grid_o = gemv_grid((int)H, (int)c->qd, 1, c->num_sms);
+  c->grid_gu = gemv_grid((int)I, (int)H, 2, c->num_sms);
+  c->grid_down = gemv_grid((int)H, (int)I, 1, c->num_sms);
+  c->grid_head = gemv_grid((int)V, (int)H, 1, c->num_sms);
   size_t nsplit = (S + 31) / 32;
   size_t cap = (size_t)c->num_sms / s.num_kv_heads;
   if (cap < 1) cap = 1;

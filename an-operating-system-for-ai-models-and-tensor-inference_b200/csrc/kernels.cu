@@ -15,6 +15,7 @@
 // Reductions use a fixed shuffle tree per row, so results are identical run
 // to run (the reference's DET gate), though not the serial chain's bits.
 #include <math.h>
+#include <stdlib.h>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -27,6 +28,22 @@ constexpr int kMaxG = 8;
 // ------------------------------------------------------------------ staging
 // Vector layout (K % 8 == 0): chunk c's first four values at xs[4c..], its
 // last four at xs[K/2 + 4c..], so a lane's two float4 reads hit distinct banks.
+//
+// The input is read with 16-byte loads issued in batches of kStageBatch per
+// thread before any shared-memory store, so staging costs about one L2 round
+// trip instead of one per element.
+constexpr int kStageBatch = 4;
+
+// Weights (never written): read-only path. Activations written by the
+// previous kernel: L2 only (__ldcg), read once per block then kept in smem.
+MYOS_DEV float4 ldg4(const float* p) { return __ldg(reinterpret_cast<const float4*>(p)); }
+MYOS_DEV float4 ldcg4(const float* p) { return __ldcg(reinterpret_cast<const float4*>(p)); }
+
+MYOS_DEV void unpack8(const uint4& u, float4& lo, float4& hi) {
+  lo = make_float4(bf16_lo(u.x), bf16_hi(u.x), bf16_lo(u.y), bf16_hi(u.y));
+  hi = make_float4(bf16_lo(u.z), bf16_hi(u.z), bf16_lo(u.w), bf16_hi(u.w));
+}
+
 MYOS_DEV void stage_input(float* xs, int K, bool vec, const GemvInput& in, float* red) {
   const int nt = blockDim.x;
   const uint16_t* erow = nullptr;
@@ -35,6 +52,60 @@ MYOS_DEV void stage_input(float* xs, int K, bool vec, const GemvInput& in, float
     erow = in.embed + (size_t)tok * (size_t)K;
     if (blockIdx.x == 0 && threadIdx.x == 0) in.ctl->fed = tok;
   }
+  const int half = K >> 1;
+  if (vec) {
+    // 1. raw copy into the split layout (block 0 also stores the embedding row)
+    const int nchunk = K >> 3;
+    float4* xlo = reinterpret_cast<float4*>(xs);
+    float4* xhi = reinterpret_cast<float4*>(xs + half);
+    for (int c0 = threadIdx.x; c0 < nchunk; c0 += nt * kStageBatch) {
+      float4 lo[kStageBatch], hi[kStageBatch];
+#pragma unroll
+      for (int i = 0; i < kStageBatch; ++i) {
+        const int c = c0 + i * nt;
+        if (c < nchunk) {
+          if (erow) {
+            unpack8(__ldg(reinterpret_cast<const uint4*>(erow) + c), lo[i], hi[i]);
+          } else {
+            lo[i] = ldcg4(in.x + 8 * c);
+            hi[i] = ldcg4(in.x + 8 * c + 4);
+          }
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < kStageBatch; ++i) {
+        const int c = c0 + i * nt;
+        if (c < nchunk) {
+          xlo[c] = lo[i];
+          xhi[c] = hi[i];
+          if (erow && in.x_store && blockIdx.x == 0) {
+            reinterpret_cast<float4*>(in.x_store)[2 * c] = lo[i];
+            reinterpret_cast<float4*>(in.x_store)[2 * c + 1] = hi[i];
+          }
+        }
+      }
+    }
+    __syncthreads();
+    if (!in.gamma) return;
+    // 2. RMSNorm in place: gamma * (x * inv), inv = 1 / sqrtf(mean + eps)
+    float ss = 0.0f;
+    for (int j = threadIdx.x; j < K; j += nt) ss = fmaf(xs[j], xs[j], ss);
+    ss = block_sum(ss, red);
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), in.eps)));
+    for (int c = threadIdx.x; c < nchunk; c += nt) {
+      const float4 g0 = ldg4(in.gamma + 8 * c), g1 = ldg4(in.gamma + 8 * c + 4);
+      float4 a = xlo[c], b = xhi[c];
+      a = make_float4(__fmul_rn(g0.x, __fmul_rn(a.x, inv)), __fmul_rn(g0.y, __fmul_rn(a.y, inv)),
+                      __fmul_rn(g0.z, __fmul_rn(a.z, inv)), __fmul_rn(g0.w, __fmul_rn(a.w, inv)));
+      b = make_float4(__fmul_rn(g1.x, __fmul_rn(b.x, inv)), __fmul_rn(g1.y, __fmul_rn(b.y, inv)),
+                      __fmul_rn(g1.z, __fmul_rn(b.z, inv)), __fmul_rn(g1.w, __fmul_rn(b.w, inv)));
+      xlo[c] = a;
+      xhi[c] = b;
+    }
+    __syncthreads();
+    return;
+  }
+  // Generic widths (test fixtures): element-wise.
   float inv = 1.0f;
   if (in.gamma) {
     float ss = 0.0f;
@@ -43,21 +114,12 @@ MYOS_DEV void stage_input(float* xs, int K, bool vec, const GemvInput& in, float
       ss = fmaf(v, v, ss);
     }
     ss = block_sum(ss, red);
-    // 1 / sqrtf(mean + eps): IEEE sqrt and division, as bf16.rs:263-270.
     inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), in.eps)));
   }
-  const int half = K >> 1;
   for (int j = threadIdx.x; j < K; j += nt) {
     const float v = erow ? bf16_at(erow + j) : in.x[j];
     if (erow && in.x_store && blockIdx.x == 0) in.x_store[j] = v;
-    // gamma * (x * inv): two rounded products, reference order.
-    const float s = in.gamma ? __fmul_rn(in.gamma[j], __fmul_rn(v, inv)) : v;
-    int dst = j;
-    if (vec) {
-      const int c = j >> 3, e = j & 7;
-      dst = e < 4 ? (c * 4 + e) : (half + c * 4 + (e - 4));
-    }
-    xs[dst] = s;
+    xs[j] = in.gamma ? __fmul_rn(in.gamma[j], __fmul_rn(v, inv)) : v;
   }
   __syncthreads();
 }
@@ -128,6 +190,57 @@ MYOS_DEV void epilogue(const GemvArgs& a, int row, float v, float v2, float& bv,
   if (EPI == EPI_SWIGLU) a.y[row] = silu_mul(v, v2);
 }
 
+// Block-level first maximum, then the last block to arrive reduces the
+// per-block results in block order and advances the step control
+// (greedy_token then KvCache::advance, qwen25_block.rs:765-780).
+MYOS_DEV void argmax_finish(const GemvArgs& a, float bv, uint32_t bi, float* wbv, uint32_t* wbi,
+                            int* last_block) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  const int G = gridDim.x, b = blockIdx.x;
+  if (lane == 0) {
+    wbv[warp] = bv;
+    wbi[warp] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float v = -INFINITY;
+    uint32_t i = 0xffffffffu;
+    for (int w = 0; w < nw; ++w)
+      if (better(wbv[w], wbi[w], v, i)) {
+        v = wbv[w];
+        i = wbi[w];
+      }
+    a.part_val[b] = v;
+    a.part_idx[b] = i;
+    __threadfence();
+    const unsigned prev = atomicAdd(a.counter, 1u);
+    *last_block = prev == (unsigned)(G - 1);
+  }
+  __syncthreads();
+  if (*last_block && threadIdx.x == 0) {
+    __threadfence();
+    float v = -INFINITY;
+    uint32_t i = 0xffffffffu;
+    for (int q = 0; q < G; ++q) {
+      const float pv = __ldcg(a.part_val + q);
+      const uint32_t pi = __ldcg(a.part_idx + q);
+      if (better(pv, pi, v, i)) {
+        v = pv;
+        i = pi;
+      }
+    }
+    const uint32_t tok = i == 0xffffffffu ? 0u : i;
+    StepCtl* ctl = a.in.ctl;
+    const uint32_t s = ctl->step;
+    if (a.rec_fed) a.rec_fed[s] = ctl->fed;
+    if (a.rec_argmax) a.rec_argmax[s] = ctl->argmax;
+    ctl->argmax = tok;
+    ctl->pos = ctl->pos + 1;
+    ctl->step = s + 1;
+    *a.counter = 0u;
+  }
+}
+
 template <int EPI>
 __global__ void __launch_bounds__(kThreads) k_gemv(GemvArgs a) {
   extern __shared__ float4 smem4[];
@@ -196,50 +309,252 @@ __global__ void __launch_bounds__(kThreads) k_gemv(GemvArgs a) {
     }
   }
 
-  if (EPI == EPI_ARGMAX) {
-    if (lane == 0) {
-      wbv[warp] = bv;
-      wbi[warp] = bi;
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      float v = -INFINITY;
-      uint32_t i = 0xffffffffu;
-      for (int w = 0; w < nw; ++w)
-        if (better(wbv[w], wbi[w], v, i)) {
-          v = wbv[w];
-          i = wbi[w];
-        }
-      a.part_val[b] = v;
-      a.part_idx[b] = i;
-      __threadfence();
-      const unsigned prev = atomicAdd(a.counter, 1u);
-      last_block = prev == (unsigned)(G - 1);
-    }
-    __syncthreads();
-    if (last_block && threadIdx.x == 0) {
-      __threadfence();
-      float v = -INFINITY;
-      uint32_t i = 0xffffffffu;
-      for (int q = 0; q < G; ++q) {
-        const float pv = __ldcg(a.part_val + q);
-        const uint32_t pi = __ldcg(a.part_idx + q);
-        if (better(pv, pi, v, i)) {
-          v = pv;
-          i = pi;
-        }
-      }
-      const uint32_t tok = i == 0xffffffffu ? 0u : i;
-      StepCtl* ctl = a.in.ctl;
-      const uint32_t s = ctl->step;
-      if (a.rec_fed) a.rec_fed[s] = ctl->fed;
-      if (a.rec_argmax) a.rec_argmax[s] = ctl->argmax;
-      ctl->argmax = tok;
-      ctl->pos = ctl->pos + 1;
-      ctl->step = s + 1;
-      *a.counter = 0u;
+  if (EPI == EPI_ARGMAX) argmax_finish(a, bv, bi, wbv, wbi, &last_block);
+}
+
+// ------------------------------------------------------------------ streaming GEMV
+// K % 256 == 0 (every Qwen2.5 width): each lane owns P = K/256 chunks of
+// 16 bytes per row (chunk lane + 32j, so a warp reads 512 contiguous bytes
+// per j). A warp walks its rows as a flat sequence of batches of U chunks
+// (NR weight rows per output row), double-buffered in registers: batch b+1
+// is in flight while batch b is consumed, across row boundaries. Batch 0 is
+// issued before the programmatic-dependency wait, so its DRAM latency
+// overlaps the predecessor kernel and the input staging.
+template <int NR, int U>
+MYOS_DEV void load_batch(uint4 (&buf)[NR][U], const uint16_t* const* wbase, int K, int row,
+                         int j0, int P, int lane) {
+#pragma unroll
+  for (int r = 0; r < NR; ++r) {
+    const uint4* w = reinterpret_cast<const uint4*>(wbase[r] + (size_t)row * K);
+#pragma unroll
+    for (int i = 0; i < U; ++i) {
+      const int j = j0 + i;
+      if (j < P) buf[r][i] = ld_stream(w + lane + 32 * j);
+      else buf[r][i] = make_uint4(0u, 0u, 0u, 0u);
     }
   }
+}
+
+template <int EPI, int NR, int U>
+__global__ void __launch_bounds__(kThreads, 2) k_gemv_stream(GemvArgs a) {
+  extern __shared__ float4 smem4[];
+  float* xs = reinterpret_cast<float*>(smem4);
+  __shared__ float red[33];
+  __shared__ float wbv[kThreads / 32];
+  __shared__ uint32_t wbi[kThreads / 32];
+  __shared__ int last_block;
+
+  const int G = gridDim.x, b = blockIdx.x;
+  const int r0 = (int)((long long)b * a.M / G);
+  const int r1 = (int)((long long)(b + 1) * a.M / G);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  const int P = a.K >> 8;                   // chunks per lane per row
+  const int nbr = (P + U - 1) / U;          // batches per row
+  const int nrw = r1 - r0 > warp ? (r1 - r0 - warp + nw - 1) / nw : 0;  // rows of this warp
+  const int nb = nrw * nbr;
+  const uint16_t* wbase[NR];
+  wbase[0] = a.w;
+  if (NR > 1) wbase[NR - 1] = a.w2;
+
+  if (a.prefetch_cap) {
+    size_t bytes = (size_t)(r1 - r0) * (size_t)a.K * 2;
+    const size_t cap = NR > 1 ? a.prefetch_cap / 2 : a.prefetch_cap;
+    if (bytes > cap) bytes = cap;
+#pragma unroll
+    for (int r = 0; r < NR; ++r) prefetch_range(wbase[r] + (size_t)r0 * a.K, bytes);
+  }
+  uint4 cur[NR][U], nxt[NR][U];
+  if (nb > 0) load_batch<NR, U>(cur, wbase, a.K, r0 + warp, 0, P, lane);
+  pdl_wait();
+  pdl_launch();
+  stage_input(xs, a.K, true, a.in, red);
+
+  const float4* xlo = reinterpret_cast<const float4*>(xs);
+  const float4* xhi = reinterpret_cast<const float4*>(xs + (a.K >> 1));
+  float bv = -INFINITY;
+  uint32_t bi = 0xffffffffu;
+  float acc[NR];
+#pragma unroll
+  for (int r = 0; r < NR; ++r) acc[r] = 0.0f;
+  for (int bt = 0; bt < nb; ++bt) {
+    const int rb = bt / nbr, jb = bt - rb * nbr;
+    if (bt + 1 < nb) {
+      const int rn = (bt + 1) / nbr;
+      load_batch<NR, U>(nxt, wbase, a.K, r0 + warp + nw * rn, ((bt + 1) - rn * nbr) * U, P, lane);
+    }
+    const int j0 = jb * U;
+#pragma unroll
+    for (int i = 0; i < U; ++i) {
+      const int j = j0 + i;
+      if (j < P) {
+        const float4 lo = xlo[lane + 32 * j], hi = xhi[lane + 32 * j];
+#pragma unroll
+        for (int r = 0; r < NR; ++r) acc[r] = dot8(cur[r][i], lo, hi, acc[r]);
+      }
+    }
+    if (jb == nbr - 1) {
+      const int row = r0 + warp + nw * rb;
+      float o[NR];
+#pragma unroll
+      for (int r = 0; r < NR; ++r) {
+        o[r] = warp_sum(acc[r]);
+        acc[r] = 0.0f;
+      }
+      epilogue<EPI>(a, row, o[0], NR > 1 ? o[NR - 1] : 0.0f, bv, bi, lane);
+    }
+#pragma unroll
+    for (int r = 0; r < NR; ++r)
+#pragma unroll
+      for (int i = 0; i < U; ++i) cur[r][i] = nxt[r][i];
+  }
+
+  if (EPI == EPI_ARGMAX) argmax_finish(a, bv, bi, wbv, wbi, &last_block);
+}
+
+// ------------------------------------------------------------------ bulk-copy GEMV
+// A block owns rows [r0, r1): for each weight matrix that is one contiguous
+// byte range, streamed by a producer warp as stages of rs rows with 1-D bulk
+// copies (the TMA engine) into an nst-deep shared-memory ring. The first nst
+// stages are issued before the programmatic-dependency wait, so they load
+// while the previous kernel is still running. Eight consumer warps take one
+// row each (rs = 8), or split a row's K range (spl = 8 / rs warps per row,
+// partials summed in warp order) and release the slot through an mbarrier.
+constexpr int kConsumerWarps = 8;
+constexpr int kBulkThreads = (kConsumerWarps + 1) * 32;
+
+MYOS_DEV size_t align_up(size_t x, size_t a) { return (x + a - 1) & ~(a - 1); }
+
+template <int EPI, int NR>
+__global__ void __launch_bounds__(kBulkThreads, 1) k_gemv_bulk(GemvArgs a) {
+  extern __shared__ float4 smem4[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(smem4);
+  __shared__ float red[33];
+  __shared__ float wbv[kBulkThreads / 32];
+  __shared__ uint32_t wbi[kBulkThreads / 32];
+  __shared__ int last_block;
+
+  const int K = a.K, rs = a.rs, spl = a.spl, nst = a.nst;
+  const size_t row_bytes = (size_t)K * 2;
+  const size_t slot_bytes = (size_t)NR * rs * row_bytes;
+  float* xs = reinterpret_cast<float*>(smem);
+  uint8_t* ring = smem + align_up((size_t)K * 4, 128);
+  float* part = reinterpret_cast<float*>(ring + (size_t)nst * slot_bytes);  // [2][NR][8]
+  uint64_t* full = reinterpret_cast<uint64_t*>(part + 2 * NR * kConsumerWarps);
+  uint64_t* empty = full + nst;
+
+  const int G = gridDim.x, b = blockIdx.x;
+  const int r0 = (int)((long long)b * a.M / G);
+  const int r1 = (int)((long long)(b + 1) * a.M / G);
+  const int nstage = (r1 - r0 + rs - 1) / rs;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const bool producer = warp == kConsumerWarps;
+  const uint16_t* wbase[NR];
+  wbase[0] = a.w;
+  if (NR > 1) wbase[NR - 1] = a.w2;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < nst; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kConsumerWarps);
+    }
+    mbar_fence_init();
+  }
+  __syncthreads();
+
+  auto prefetch_stage = [&](int s) {
+    if (s >= nstage) return;
+    const int row0 = r0 + s * rs;
+    const int n = min(rs, r1 - row0);
+#pragma unroll
+    for (int r = 0; r < NR; ++r)
+      prefetch_l2(wbase[r] + (size_t)row0 * K, (uint32_t)(n * row_bytes));
+  };
+  auto issue = [&](int s) {
+    const int slot = s % nst;
+    const int row0 = r0 + s * rs;
+    const int n = min(rs, r1 - row0);
+    const uint32_t bytes = (uint32_t)(n * row_bytes);
+    mbar_arrive_expect_tx(&full[slot], NR * bytes);
+#pragma unroll
+    for (int r = 0; r < NR; ++r)
+      bulk_g2s(ring + (size_t)slot * slot_bytes + (size_t)r * rs * row_bytes,
+               wbase[r] + (size_t)row0 * K, bytes, &full[slot]);
+  };
+  const int la = a.lookahead;
+  if (producer && lane == 0) {
+    const int first = min(nst, nstage);
+    for (int s = 0; s < first; ++s) issue(s);
+    for (int s = nst; s < nst + la; ++s) prefetch_stage(s);
+  }
+  pdl_wait();
+  pdl_launch();
+  stage_input(xs, K, true, a.in, red);
+
+  float bv = -INFINITY;
+  uint32_t bi = 0xffffffffu;
+  if (producer) {
+    if (lane == 0) {
+      for (int s = nst; s < nstage; ++s) {
+        const int slot = s % nst;
+        mbar_wait(&empty[slot], (uint32_t)((s / nst) - 1) & 1u, a.err, kErrWaitEmpty);
+        issue(s);
+        if (la) prefetch_stage(s + la);
+      }
+    }
+    __syncwarp();
+  } else {
+    const float4* xlo = reinterpret_cast<const float4*>(xs);
+    const float4* xhi = reinterpret_cast<const float4*>(xs + (K >> 1));
+    const int rr = warp / spl, cs = warp - rr * spl;
+    const int cps = (K >> 3) / spl;
+    const int c0 = cs * cps;
+    for (int s = 0; s < nstage; ++s) {
+      const int slot = s % nst;
+      mbar_wait(&full[slot], (uint32_t)(s / nst) & 1u, a.err, kErrWaitFull);
+      const int row0 = r0 + s * rs;
+      const int n = min(rs, r1 - row0);
+      float acc[NR];
+#pragma unroll
+      for (int r = 0; r < NR; ++r) acc[r] = 0.0f;
+      if (rr < n) {
+        const uint8_t* base = ring + (size_t)slot * slot_bytes + (size_t)rr * row_bytes;
+#pragma unroll 4
+        for (int c = c0 + lane; c < c0 + cps; c += 32) {
+          const float4 lo = xlo[c], hi = xhi[c];
+#pragma unroll
+          for (int r = 0; r < NR; ++r) {
+            const uint4 u = *reinterpret_cast<const uint4*>(base + (size_t)r * rs * row_bytes +
+                                                            (size_t)c * 16);
+            acc[r] = dot8(u, lo, hi, acc[r]);
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[slot]);
+#pragma unroll
+      for (int r = 0; r < NR; ++r) acc[r] = warp_sum(acc[r]);
+      if (spl == 1) {
+        if (rr < n) epilogue<EPI>(a, row0 + rr, acc[0], NR > 1 ? acc[NR - 1] : 0.0f, bv, bi, lane);
+      } else {
+        float* pp = part + (s & 1) * NR * kConsumerWarps;
+        if (lane == 0) {
+#pragma unroll
+          for (int r = 0; r < NR; ++r) pp[r * kConsumerWarps + warp] = acc[r];
+        }
+        named_sync(1, kConsumerWarps * 32);
+        if (cs == 0 && rr < n) {
+          float v[NR];
+#pragma unroll
+          for (int r = 0; r < NR; ++r) {
+            v[r] = 0.0f;
+            for (int q = 0; q < spl; ++q) v[r] += pp[r * kConsumerWarps + rr * spl + q];
+          }
+          epilogue<EPI>(a, row0 + rr, v[0], NR > 1 ? v[NR - 1] : 0.0f, bv, bi, lane);
+        }
+      }
+    }
+  }
+  if (EPI == EPI_ARGMAX) argmax_finish(a, bv, bi, wbv, wbi, &last_block);
 }
 
 // ------------------------------------------------------------------ attention
@@ -264,6 +579,20 @@ MYOS_DEV __nv_bfloat16 kv_from<__nv_bfloat16>(float v) {
   return __float2bfloat16_rn(v);
 }
 
+// Four consecutive cache elements (16 B of f32 or 8 B of bf16), via L2:
+// the cache is written by earlier launches.
+template <typename KT>
+MYOS_DEV float4 kv_load4(const KT* p);
+template <>
+MYOS_DEV float4 kv_load4<float>(const float* p) {
+  return __ldcg(reinterpret_cast<const float4*>(p));
+}
+template <>
+MYOS_DEV float4 kv_load4<__nv_bfloat16>(const __nv_bfloat16* p) {
+  const uint2 u = __ldcg(reinterpret_cast<const uint2*>(p));
+  return make_float4(bf16_lo(u.x), bf16_hi(u.x), bf16_lo(u.y), bf16_hi(u.y));
+}
+
 // NeoX half-rotate (rope.rs:145-184): y0 = x0*c - x1*s, y1 = x1*c + x0*s,
 // each product rounded before the add; c, s from the host libm table.
 MYOS_DEV float rope_lane(const float* x, int e, int d, const float* cs, const float* sn) {
@@ -275,22 +604,33 @@ MYOS_DEV float rope_lane(const float* x, int e, int d, const float* cs, const fl
                   : __fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, s));
 }
 
-// Split-KV decode attention (flash-decoding). Block (s, g): keys of split s
-// for KV head g, serving its G query heads (gqa.rs:96-105: heads
-// [g*G, (g+1)*G) read KV head g). Each warp runs an online softmax over
-// its keys; warps merge in shared memory; splits merge in the last block
-// to arrive, in split order.
+// Split-KV decode attention (flash-decoding). Block (s, g) covers keys
+// [s*chunk, (s+1)*chunk) for KV head g and its G query heads (gqa.rs:96-105:
+// heads [g*G, (g+1)*G) read KV head g). Keys are processed in tiles of 32:
+//   1. the tile's K and V rows are copied to shared memory (coalesced);
+//   2. one thread per (head, key) forms score = (q . k) * scale
+//      (gqa.rs:189-191, scale = 1/sqrtf(d));
+//   3. one warp per head runs the online softmax over the tile's 32 scores
+//      (running max, expf(s - max), running sum);
+//   4. threads accumulate p * v for their (head, lane) outputs.
+// The block writes (unnormalised output, max, sum) per head; the last block
+// of KV head g to finish merges the splits in split order and divides by the
+// sum (the reference's e / sum, gqa.rs:283-307, up to reassociation).
+constexpr int kTile = 32;
+
 template <int DPL, typename KT>
 __global__ void __launch_bounds__(kThreads) k_attn(AttnArgs a) {
   extern __shared__ float4 smem4[];
   float* sm = reinterpret_cast<float*>(smem4);
   const int d = a.d, G = a.G;
-  float* qs = sm;                    // [G][d]
-  float* knew = qs + G * d;          // [d]
-  float* vnew = knew + d;            // [d]
-  float* wm = vnew + d;              // [8][G]
-  float* wl = wm + 8 * G;            // [8][G]
-  float* wo = wl + 8 * G;            // [8][G][d]
+  const int ds = d + 4;                   // padded row stride (float4 reads conflict-free)
+  float* qs = sm;                         // [G][d]
+  float* ks = qs + G * d;                 // [kTile][ds]
+  float* vs = ks + kTile * ds;            // [kTile][ds]
+  float* ps = vs + kTile * ds;            // [G][kTile]
+  float* corr = ps + G * kTile;           // [G]
+  float* knew = corr + kMaxG;             // [d]
+  float* vnew = knew + d;                 // [d]
   __shared__ int last_block;
 
   const int s = blockIdx.x, g = blockIdx.y;
@@ -314,113 +654,175 @@ __global__ void __launch_bounds__(kThreads) k_attn(AttnArgs a) {
   const float* cs = a.decode ? a.cos_t + (size_t)pos * half : nullptr;
   const float* sn = a.decode ? a.sin_t + (size_t)pos * half : nullptr;
 
-  for (int i = threadIdx.x; i < G * d; i += nt) {
-    const int hh = i / d, e = i - hh * d;
-    const float* qh = a.q + (size_t)(g * G + hh) * d;
-    qs[i] = a.decode ? rope_lane(qh, e, d, cs, sn) : qh[e];
-  }
   const bool has_new = a.decode && pos >= kb && pos < ke;
-  if (has_new) {
-    const float* kh = a.q + (size_t)a.Hq * d + (size_t)g * d;
-    const float* vh = a.q + (size_t)(a.Hq + a.Hkv) * d + (size_t)g * d;
-    KT* kdst = const_cast<KT*>(kc) + (size_t)pos * d;
-    KT* vdst = const_cast<KT*>(vc) + (size_t)pos * d;
-    for (int e = threadIdx.x; e < d; e += nt) {
-      const KT kq = kv_from<KT>(rope_lane(kh, e, d, cs, sn));
-      const KT vq = kv_from<KT>(vh[e]);
-      knew[e] = kv_load<KT>(&kq);
-      vnew[e] = kv_load<KT>(&vq);
-      kdst[e] = kq;  // the cache slot for this position (KvCache::store)
-      vdst[e] = vq;
-    }
-  }
-  __syncthreads();
-
-  float qr[kMaxG][DPL];
+  {
+    // Stage q (G heads), and in decode mode the cos/sin row and this KV
+    // head's new k and v, with every load issued before the first store.
+    float* qraw = a.decode ? ks : qs;  // tile buffers are free until the first tile
+    float* cst = vs;
+    float* snt = vs + half;
+    float* kraw = vs + d;
+    float* vraw = vs + 2 * d;
+    const int nq = G * d;
+    const int ntot = a.decode ? nq + d + (has_new ? 2 * d : 0) : nq;
+    const float* qsrc = a.q + (size_t)g * G * d;
+    const float* ksrc = a.q + (size_t)a.Hq * d + (size_t)g * d;
+    const float* vsrc = a.q + (size_t)(a.Hq + a.Hkv) * d + (size_t)g * d;
+    constexpr int kJ = 12;  // (8*256 + 3*256) / 256 elements per thread at most
+    float val[kJ];
 #pragma unroll
-  for (int hh = 0; hh < kMaxG; ++hh)
-#pragma unroll
-    for (int j = 0; j < DPL; ++j) {
-      const int e = lane + 32 * j;
-      qr[hh][j] = (hh < G && e < d) ? qs[hh * d + e] : 0.0f;
-    }
-  float m[kMaxG], l[kMaxG], acc[kMaxG][DPL];
-#pragma unroll
-  for (int hh = 0; hh < kMaxG; ++hh) {
-    m[hh] = -INFINITY;
-    l[hh] = 0.0f;
-#pragma unroll
-    for (int j = 0; j < DPL; ++j) acc[hh][j] = 0.0f;
-  }
-
-  for (int t = kb + warp; t < ke; t += (nt >> 5)) {
-    float kv[DPL], vv[DPL];
-    const bool is_new = has_new && t == pos;
-#pragma unroll
-    for (int j = 0; j < DPL; ++j) {
-      const int e = lane + 32 * j;
-      if (e < d) {
-        kv[j] = is_new ? knew[e] : kv_load<KT>(kc + (size_t)t * d + e);
-        vv[j] = is_new ? vnew[e] : kv_load<KT>(vc + (size_t)t * d + e);
-      } else {
-        kv[j] = 0.0f;
-        vv[j] = 0.0f;
+    for (int j = 0; j < kJ; ++j) {
+      const int v = threadIdx.x + nt * j;
+      if (v < ntot) {
+        if (v < nq) val[j] = __ldcg(qsrc + v);
+        else if (v < nq + half) val[j] = __ldg(cs + (v - nq));
+        else if (v < nq + d) val[j] = __ldg(sn + (v - nq - half));
+        else if (v < nq + 2 * d) val[j] = __ldcg(ksrc + (v - nq - d));
+        else val[j] = __ldcg(vsrc + (v - nq - 2 * d));
       }
     }
 #pragma unroll
-    for (int hh = 0; hh < kMaxG; ++hh) {
-      if (hh < G) {
-        float part = 0.0f;
-#pragma unroll
-        for (int j = 0; j < DPL; ++j) part = fmaf(qr[hh][j], kv[j], part);
-        // score = dot * scale (gqa.rs:189-191), scale = 1/sqrtf(d)
-        const float sc = __fmul_rn(warp_sum(part), a.scale);
-        const float mn = fmaxf(m[hh], sc);
-        const float corr = expf(m[hh] - mn);
-        const float p = expf(sc - mn);
-        l[hh] = fmaf(l[hh], corr, p);
-#pragma unroll
-        for (int j = 0; j < DPL; ++j) acc[hh][j] = fmaf(acc[hh][j], corr, p * vv[j]);
-        m[hh] = mn;
+    for (int j = 0; j < kJ; ++j) {
+      const int v = threadIdx.x + nt * j;
+      if (v < ntot) {
+        if (v < nq) qraw[v] = val[j];
+        else if (v < nq + half) cst[v - nq] = val[j];
+        else if (v < nq + d) snt[v - nq - half] = val[j];
+        else if (v < nq + 2 * d) kraw[v - nq - d] = val[j];
+        else vraw[v - nq - 2 * d] = val[j];
+      }
+    }
+    if (a.decode) {
+      __syncthreads();
+      for (int i = threadIdx.x; i < nq; i += nt) {
+        const int hh = i / d, e = i - hh * d;
+        qs[i] = rope_lane(qraw + hh * d, e, d, cst, snt);
+      }
+      if (has_new) {
+        KT* kdst = const_cast<KT*>(kc) + (size_t)pos * d;
+        KT* vdst = const_cast<KT*>(vc) + (size_t)pos * d;
+        for (int e = threadIdx.x; e < d; e += nt) {
+          const KT kq = kv_from<KT>(rope_lane(kraw, e, d, cst, snt));
+          const KT vq = kv_from<KT>(vraw[e]);
+          knew[e] = kv_load<KT>(&kq);
+          vnew[e] = kv_load<KT>(&vq);
+          kdst[e] = kq;  // the cache slot for this position (KvCache::store)
+          vdst[e] = vq;
+        }
       }
     }
   }
 
-  // Merge warps.
+  // Output slots: thread owns outputs o = threadIdx.x + nt*i of G*d.
+  constexpr int kMaxOut = kMaxG * 256 / kThreads;
+  float acc[kMaxOut];
 #pragma unroll
-  for (int hh = 0; hh < kMaxG; ++hh) {
-    if (hh < G) {
-      if (lane == 0) {
-        wm[warp * G + hh] = m[hh];
-        wl[warp * G + hh] = l[hh];
+  for (int i = 0; i < kMaxOut; ++i) acc[i] = 0.0f;
+  float m_run = -INFINITY, l_run = 0.0f;  // valid in lane 0.. of warp h < G (head h)
+
+  for (int t0 = kb; t0 < ke; t0 += kTile) {
+    const int nk = min(kTile, ke - t0);
+    __syncthreads();  // previous tile fully consumed; qs/knew staged
+    if ((d & 3) == 0) {
+      // quads of 4 elements; all of this thread's loads in flight together
+      const int qpr = d >> 2, nqd = nk * qpr;
+      constexpr int kQ = kTile * 64 / kThreads;  // d <= 256: at most 8 quads per thread
+      float4 kq[kQ], vq[kQ];
+#pragma unroll
+      for (int j = 0; j < kQ; ++j) {
+        const int i = threadIdx.x + nt * j;
+        if (i < nqd) {
+          const int tt = i / qpr, e = (i - tt * qpr) * 4;
+          const int t = t0 + tt;
+          if (!(has_new && t == pos)) {
+            kq[j] = kv_load4<KT>(kc + (size_t)t * d + e);
+            vq[j] = kv_load4<KT>(vc + (size_t)t * d + e);
+          }
+        }
       }
 #pragma unroll
-      for (int j = 0; j < DPL; ++j) {
-        const int e = lane + 32 * j;
-        if (e < d) wo[(warp * G + hh) * d + e] = acc[hh][j];
+      for (int j = 0; j < kQ; ++j) {
+        const int i = threadIdx.x + nt * j;
+        if (i < nqd) {
+          const int tt = i / qpr, e = (i - tt * qpr) * 4;
+          const int t = t0 + tt;
+          if (has_new && t == pos) {
+            kq[j] = make_float4(knew[e], knew[e + 1], knew[e + 2], knew[e + 3]);
+            vq[j] = make_float4(vnew[e], vnew[e + 1], vnew[e + 2], vnew[e + 3]);
+          }
+          *reinterpret_cast<float4*>(ks + tt * ds + e) = kq[j];
+          *reinterpret_cast<float4*>(vs + tt * ds + e) = vq[j];
+        }
+      }
+    } else {
+      for (int i = threadIdx.x; i < nk * d; i += nt) {
+        const int tt = i / d, e = i - tt * d;
+        const int t = t0 + tt;
+        const bool nw_ = has_new && t == pos;
+        ks[tt * ds + e] = nw_ ? knew[e] : kv_load<KT>(kc + (size_t)t * d + e);
+        vs[tt * ds + e] = nw_ ? vnew[e] : kv_load<KT>(vc + (size_t)t * d + e);
+      }
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < G * kTile; i += nt) {
+      const int hh = i / kTile, tt = i - hh * kTile;
+      float sc = -INFINITY;
+      if (tt < nk) {
+        const float* qh = qs + hh * d;
+        const float* kr = ks + tt * ds;
+        float dot = 0.0f;
+        if ((d & 3) == 0) {
+          for (int e = 0; e < d; e += 4) {
+            const float4 qv = *reinterpret_cast<const float4*>(qh + e);
+            const float4 kv = *reinterpret_cast<const float4*>(kr + e);
+            dot = fmaf(qv.x, kv.x, dot);
+            dot = fmaf(qv.y, kv.y, dot);
+            dot = fmaf(qv.z, kv.z, dot);
+            dot = fmaf(qv.w, kv.w, dot);
+          }
+        } else {
+          for (int e = 0; e < d; ++e) dot = fmaf(qh[e], kr[e], dot);
+        }
+        sc = __fmul_rn(dot, a.scale);
+      }
+      ps[hh * kTile + tt] = sc;
+    }
+    __syncthreads();
+    if (warp < G) {
+      const float sc = ps[warp * kTile + lane];
+      const float mt = warp_max(sc);
+      const float mn = fmaxf(m_run, mt);
+      const float cf = expf(m_run - mn);  // 0 on the first tile (m_run = -inf)
+      const float p = lane < nk ? expf(sc - mn) : 0.0f;
+      l_run = fmaf(l_run, cf, warp_sum(p));
+      m_run = mn;
+      ps[warp * kTile + lane] = p;
+      if (lane == 0) corr[warp] = cf;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int i = 0; i < kMaxOut; ++i) {
+      const int o = threadIdx.x + nt * i;
+      if (o < G * d) {
+        const int hh = o / d, e = o - hh * d;
+        const float* ph = ps + hh * kTile;
+        float v = acc[i] * corr[hh];
+        for (int tt = 0; tt < nk; ++tt) v = fmaf(ph[tt], vs[tt * ds + e], v);
+        acc[i] = v;
       }
     }
   }
-  __syncthreads();
-  const int nwarps = nt >> 5;
-  for (int i = threadIdx.x; i < G * d; i += nt) {
-    const int hh = i / d, e = i - hh * d;
-    float M = -INFINITY;
-    for (int w = 0; w < nwarps; ++w) M = fmaxf(M, wm[w * G + hh]);
-    float L = 0.0f, O = 0.0f;
-    if (M != -INFINITY) {
-      for (int w = 0; w < nwarps; ++w) {
-        const float f = expf(wm[w * G + hh] - M);
-        L = fmaf(wl[w * G + hh], f, L);
-        O = fmaf(wo[(w * G + hh) * d + e], f, O);
-      }
-    }
-    const size_t pidx = ((size_t)g * a.nsplit + s) * G + hh;
-    a.part_o[pidx * d + e] = O;
-    if (e == 0) {
-      a.part_m[pidx] = M;
-      a.part_l[pidx] = L;
-    }
+
+  // This split's partial: (sum_t e_t v_t, max, sum) per head.
+  const size_t pbase = ((size_t)g * a.nsplit + s) * G;
+#pragma unroll
+  for (int i = 0; i < kMaxOut; ++i) {
+    const int o = threadIdx.x + nt * i;
+    if (o < G * d) a.part_o[pbase * d + o] = acc[i];
+  }
+  if (warp < G && lane == 0) {
+    a.part_m[pbase + warp] = m_run;
+    a.part_l[pbase + warp] = l_run;
   }
   __threadfence();
   __syncthreads();
@@ -431,21 +833,45 @@ __global__ void __launch_bounds__(kThreads) k_attn(AttnArgs a) {
   __syncthreads();
   if (!last_block) return;
   __threadfence();
-  for (int i = threadIdx.x; i < G * d; i += nt) {
-    const int hh = i / d, e = i - hh * d;
+  // Merge: factor f_q = expf(m_q - M) per (split, head), staged in shared memory.
+  float* fs = sm;                    // [nsplit][G]
+  float* ls = sm + a.nsplit * G;     // [nsplit][G]
+  float* Ls = ls + a.nsplit * G;     // [G]
+  const size_t gbase = (size_t)g * a.nsplit * G;
+  for (int i = threadIdx.x; i < a.nsplit * G; i += nt) {
+    const float mq = __ldcg(a.part_m + gbase + i);
+    const float lq = __ldcg(a.part_l + gbase + i);
+    fs[i] = mq;
+    ls[i] = lq;
+  }
+  __syncthreads();
+  if (threadIdx.x < G) {
+    const int hh = threadIdx.x;
     float M = -INFINITY;
-    for (int q = 0; q < a.nsplit; ++q)
-      M = fmaxf(M, __ldcg(a.part_m + ((size_t)g * a.nsplit + q) * G + hh));
-    float L = 0.0f, O = 0.0f;
+    for (int q = 0; q < a.nsplit; ++q) M = fmaxf(M, fs[q * G + hh]);
+    float L = 0.0f;
     for (int q = 0; q < a.nsplit; ++q) {
-      const size_t pidx = ((size_t)g * a.nsplit + q) * G + hh;
-      const float mq = __ldcg(a.part_m + pidx);
-      if (mq == -INFINITY) continue;
-      const float f = expf(mq - M);
-      L = fmaf(__ldcg(a.part_l + pidx), f, L);
-      O = fmaf(__ldcg(a.part_o + pidx * d + e), f, O);
+      const float mq = fs[q * G + hh];
+      const float f = mq == -INFINITY ? 0.0f : expf(mq - M);
+      fs[q * G + hh] = f;
+      L = fmaf(ls[q * G + hh], f, L);
     }
-    a.out[(size_t)(g * G + hh) * d + e] = __fdiv_rn(O, L);
+    Ls[hh] = L;
+  }
+  __syncthreads();
+  for (int o = threadIdx.x; o < G * d; o += nt) {
+    const int hh = o / d;
+    float O = 0.0f;
+    int q = 0;
+    for (; q + 8 <= a.nsplit; q += 8) {
+      float po[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) po[u] = __ldcg(a.part_o + (gbase + (size_t)(q + u) * G) * d + o);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) O = fmaf(po[u], fs[(q + u) * G + hh], O);
+    }
+    for (; q < a.nsplit; ++q) O = fmaf(__ldcg(a.part_o + (gbase + (size_t)q * G) * d + o), fs[q * G + hh], O);
+    a.out[(size_t)g * G * d + o] = __fdiv_rn(O, Ls[hh]);
   }
   if (threadIdx.x == 0) a.counters[g] = 0u;
 }
@@ -546,6 +972,21 @@ __global__ void k_rope(float* y, const float* x, int len, int d, const float* cs
 }
 
 // ------------------------------------------------------------------ launchers
+// MYOS_GEMV_KIND selects the GEMV implementation for A/B timing:
+// "bulk" (default: bulk-copy ring), "stream" (register double buffer),
+// "legacy" (row at a time).
+static int gemv_kind() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("MYOS_GEMV_KIND");
+    v = 0;
+    if (e && e[0] == 's') v = 1;
+    if (e && e[0] == 'l') v = 2;
+  }
+  return v;
+}
+static bool getenv_legacy() { return gemv_kind() == 2; }
+
 static cudaLaunchConfig_t make_cfg(dim3 grid, dim3 block, size_t smem, cudaStream_t st,
                                    bool pdl, cudaLaunchAttribute* attr) {
   cudaLaunchConfig_t cfg = {};
@@ -562,9 +1003,105 @@ static cudaLaunchConfig_t make_cfg(dim3 grid, dim3 block, size_t smem, cudaStrea
 
 size_t gemv_smem_bytes(int K) { return (size_t)((K + 7) & ~7) * sizeof(float); }
 
-cudaError_t launch_gemv(int epi, const GemvArgs& a, int grid, cudaStream_t st, bool pdl) {
+// Batch width U for the streaming GEMV: the largest U <= 8 that divides the
+// per-lane chunk count P (so no batch is partly empty), else 8. Two weight
+// matrices (SwiGLU) halve the budget so both buffers fit in registers.
+static int pick_batch(int P, int NR) {
+  const int umax = NR > 1 ? 4 : 8;
+  if (P <= umax) return P < 3 ? 3 : P;
+  for (int u = umax; u >= 3; --u)
+    if (P % u == 0) return u;
+  return umax;
+}
+
+template <int EPI, int NR>
+static cudaError_t launch_stream(const GemvArgs& a, int U, cudaLaunchConfig_t& cfg) {
+  switch (U) {
+    case 3: return cudaLaunchKernelEx(&cfg, k_gemv_stream<EPI, NR, 3>, a);
+    case 4: return cudaLaunchKernelEx(&cfg, k_gemv_stream<EPI, NR, 4>, a);
+    case 5: return cudaLaunchKernelEx(&cfg, k_gemv_stream<EPI, NR, 5>, a);
+    case 6: return cudaLaunchKernelEx(&cfg, k_gemv_stream<EPI, NR, 6>, a);
+    case 7: return cudaLaunchKernelEx(&cfg, k_gemv_stream<EPI, NR, 7>, a);
+    default: return cudaLaunchKernelEx(&cfg, k_gemv_stream<EPI, NR, 8>, a);
+  }
+}
+
+// Tuning knobs (read at launch; a captured graph keeps the values it saw):
+// MYOS_BULK_STAGE_KB target stage size, MYOS_BULK_RING_KB ring size,
+// MYOS_BULK_LOOKAHEAD stages prefetched into L2 ahead of the ring,
+// MYOS_BULK_GRID_MULT blocks per SM.
+static int env_int(const char* name, int def) {
+  const char* e = getenv(name);
+  return e && *e ? atoi(e) : def;
+}
+
+// Bulk-pipeline geometry: rows per stage so a stage is about STAGE_KB, as
+// many stages as fit in RING_KB (2..16).
+static void bulk_geometry(int K, int NR, int* rs, int* spl, int* nst, size_t* smem) {
+  const size_t row_bytes = (size_t)K * 2;
+  const size_t stage_target = (size_t)env_int("MYOS_BULK_STAGE_KB", 24) << 10;
+  int r = 8;
+  while (r > 1 && (size_t)NR * r * row_bytes > stage_target) r >>= 1;
+  const size_t slot = (size_t)NR * r * row_bytes;
+  int n = (int)(((size_t)env_int("MYOS_BULK_RING_KB", 96) << 10) / slot);
+  if (n < 2) n = 2;
+  if (n > 16) n = 16;
+  *rs = r;
+  *spl = kConsumerWarps / r;
+  *nst = n;
+  *smem = ((size_t)K * 4 + 127) / 128 * 128 + (size_t)n * slot + 2 * NR * kConsumerWarps * 4 +
+          2 * (size_t)n * 8 + 16;
+}
+
+int gemv_grid(int M, int K, int NR, int num_sms) {
+  if (K % 256 == 0 && gemv_kind() == 0) {
+    int rs, spl, nst;
+    size_t smem;
+    bulk_geometry(K, NR, &rs, &spl, &nst, &smem);
+    const int g = (M + rs - 1) / rs;
+    const int cap = num_sms * env_int("MYOS_BULK_GRID_MULT", 1);
+    return g < cap ? (g < 1 ? 1 : g) : cap;
+  }
+  int g = (M + 7) / 8;
+  if (g > 2 * num_sms) g = 2 * num_sms;
+  return g < 1 ? 1 : g;
+}
+
+cudaError_t launch_gemv(int epi, const GemvArgs& a0, int grid, cudaStream_t st, bool pdl) {
   cudaLaunchAttribute attr[1];
+  const bool bulk_ok = (a0.K % 256) == 0 && ((uintptr_t)a0.w & 15) == 0 &&
+                       (epi != EPI_SWIGLU || ((uintptr_t)a0.w2 & 15) == 0) && gemv_kind() == 0;
+  if (bulk_ok) {
+    GemvArgs a = a0;
+    const int NR = epi == EPI_SWIGLU ? 2 : 1;
+    size_t smem;
+    bulk_geometry(a.K, NR, &a.rs, &a.spl, &a.nst, &smem);
+    a.lookahead = env_int("MYOS_BULK_LOOKAHEAD", 0);
+    cudaLaunchConfig_t cfg = make_cfg(dim3(grid), dim3(kBulkThreads), smem, st, pdl, attr);
+    switch (epi) {
+      case EPI_STORE: return cudaLaunchKernelEx(&cfg, k_gemv_bulk<EPI_STORE, 1>, a);
+      case EPI_BIAS: return cudaLaunchKernelEx(&cfg, k_gemv_bulk<EPI_BIAS, 1>, a);
+      case EPI_RESID: return cudaLaunchKernelEx(&cfg, k_gemv_bulk<EPI_RESID, 1>, a);
+      case EPI_SWIGLU: return cudaLaunchKernelEx(&cfg, k_gemv_bulk<EPI_SWIGLU, 2>, a);
+      case EPI_ARGMAX: return cudaLaunchKernelEx(&cfg, k_gemv_bulk<EPI_ARGMAX, 1>, a);
+    }
+    return cudaErrorInvalidValue;
+  }
+  const GemvArgs& a = a0;
   cudaLaunchConfig_t cfg = make_cfg(dim3(grid), dim3(kThreads), gemv_smem_bytes(a.K), st, pdl, attr);
+  const bool stream = (a.K % 256) == 0 && ((uintptr_t)a.w & 15) == 0 &&
+                      (epi != EPI_SWIGLU || ((uintptr_t)a.w2 & 15) == 0) && !getenv_legacy();
+  if (stream) {
+    const int P = a.K / 256;
+    switch (epi) {
+      case EPI_STORE: return launch_stream<EPI_STORE, 1>(a, pick_batch(P, 1), cfg);
+      case EPI_BIAS: return launch_stream<EPI_BIAS, 1>(a, pick_batch(P, 1), cfg);
+      case EPI_RESID: return launch_stream<EPI_RESID, 1>(a, pick_batch(P, 1), cfg);
+      case EPI_SWIGLU: return launch_stream<EPI_SWIGLU, 2>(a, pick_batch(P, 2), cfg);
+      case EPI_ARGMAX: return launch_stream<EPI_ARGMAX, 1>(a, pick_batch(P, 1), cfg);
+    }
+    return cudaErrorInvalidValue;
+  }
   switch (epi) {
     case EPI_STORE: return cudaLaunchKernelEx(&cfg, k_gemv<EPI_STORE>, a);
     case EPI_BIAS: return cudaLaunchKernelEx(&cfg, k_gemv<EPI_BIAS>, a);
@@ -578,7 +1115,8 @@ cudaError_t launch_gemv(int epi, const GemvArgs& a, int grid, cudaStream_t st, b
 int attn_dpl(int d) { return d <= 32 ? 1 : d <= 64 ? 2 : d <= 128 ? 4 : 8; }
 
 size_t attn_smem_bytes(int G, int d) {
-  return (size_t)(G * d + 2 * d + 16 * G + 8 * G * d) * sizeof(float);
+  // qs, two padded tiles, probabilities, corrections, new K/V row
+  return (size_t)(G * d + 2 * kTile * (d + 4) + G * kTile + kMaxG + 2 * d) * sizeof(float);
 }
 
 template <int DPL>
@@ -590,8 +1128,11 @@ static cudaError_t launch_attn_dpl(const AttnArgs& a, int kv_bf16, cudaLaunchCon
 cudaError_t launch_attention(const AttnArgs& a, int kv_bf16, cudaStream_t st, bool pdl) {
   if (a.G > kMaxG || a.d > 256 || a.d <= 0) return cudaErrorInvalidValue;
   cudaLaunchAttribute attr[1];
-  cudaLaunchConfig_t cfg = make_cfg(dim3(a.nsplit, a.Hkv), dim3(kThreads),
-                                    attn_smem_bytes(a.G, a.d), st, pdl, attr);
+  // The split merge reuses the tile buffers for (2 nsplit + 1) * G floats.
+  size_t smem = attn_smem_bytes(a.G, a.d);
+  const size_t merge = (size_t)(2 * a.nsplit + 1) * a.G * sizeof(float);
+  if (merge > smem) smem = merge;
+  cudaLaunchConfig_t cfg = make_cfg(dim3(a.nsplit, a.Hkv), dim3(kThreads), smem, st, pdl, attr);
   switch (attn_dpl(a.d)) {
     case 1: return launch_attn_dpl<1>(a, kv_bf16, cfg);
     case 2: return launch_attn_dpl<2>(a, kv_bf16, cfg);
@@ -655,6 +1196,24 @@ cudaError_t kernels_init() {
   MYOS_SET(k_gemv<EPI_RESID>, gemv_max)
   MYOS_SET(k_gemv<EPI_SWIGLU>, gemv_max)
   MYOS_SET(k_gemv<EPI_ARGMAX>, gemv_max)
+#define MYOS_SET_STREAM(EPI, NR)                 \
+  MYOS_SET((k_gemv_stream<EPI, NR, 3>), gemv_max) \
+  MYOS_SET((k_gemv_stream<EPI, NR, 4>), gemv_max) \
+  MYOS_SET((k_gemv_stream<EPI, NR, 5>), gemv_max) \
+  MYOS_SET((k_gemv_stream<EPI, NR, 6>), gemv_max) \
+  MYOS_SET((k_gemv_stream<EPI, NR, 7>), gemv_max) \
+  MYOS_SET((k_gemv_stream<EPI, NR, 8>), gemv_max)
+  MYOS_SET_STREAM(EPI_STORE, 1)
+  MYOS_SET_STREAM(EPI_BIAS, 1)
+  MYOS_SET_STREAM(EPI_RESID, 1)
+  MYOS_SET_STREAM(EPI_SWIGLU, 2)
+  MYOS_SET_STREAM(EPI_ARGMAX, 1)
+#undef MYOS_SET_STREAM
+  MYOS_SET((k_gemv_bulk<EPI_STORE, 1>), gemv_max)
+  MYOS_SET((k_gemv_bulk<EPI_BIAS, 1>), gemv_max)
+  MYOS_SET((k_gemv_bulk<EPI_RESID, 1>), gemv_max)
+  MYOS_SET((k_gemv_bulk<EPI_SWIGLU, 2>), gemv_max)
+  MYOS_SET((k_gemv_bulk<EPI_ARGMAX, 1>), gemv_max)
   MYOS_SET((k_attn<1, float>), attn_max)
   MYOS_SET((k_attn<2, float>), attn_max)
   MYOS_SET((k_attn<4, float>), attn_max)

@@ -33,13 +33,11 @@ struct DBuf {
 
 bool mul_ok(size_t a, size_t b, size_t* out) { return !__builtin_mul_overflow(a, b, out); }
 
-int grid_rows(size_t rows) {
+int num_sms() {
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  size_t g = (rows + 7) / 8, cap = (size_t)sms * 2;
-  if (g > cap) g = cap;
-  return (int)(g < 1 ? 1 : g);
+  return sms;
 }
 
 #define OPCK(call)                             \
@@ -55,7 +53,7 @@ int gemv_device(float* y, const uint16_t* w, const float* x, size_t m, size_t k,
   a.K = (int)k;
   a.in.x = x;
   a.y = y;
-  OPCK(launch_gemv(EPI_STORE, a, grid_rows(m), st, false));
+  OPCK(launch_gemv(EPI_STORE, a, gemv_grid((int)m, (int)k, 1, num_sms()), st, false));
   return MYOS_OK;
 }
 

@@ -320,7 +320,7 @@ def main():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--kv", choices=["f32", "bf16"], default="bf16")
+    ap.add_argument("--kv", choices=["f32", "bf16"], default="f32")
     ap.add_argument("--cpu-decode", type=int, default=16)
     ap.add_argument("--ref-decode", type=int, default=8)
     ap.add_argument("--no-cpu", action="store_true")

@@ -18,6 +18,10 @@ pytestmark = [pytest.mark.gpu, pytest.mark.slow]
 SEED = 1234
 N_PROMPT, N_GEN = 128, 128
 ATOL, RTOL = 1e-2, 1e-3
+# A bf16 KV cache rounds every cached K and V element to 8 mantissa bits
+# (relative 2^-9), which the reference's f32 cache never does; its logits
+# are held to this wider bound instead.
+TOL = {"f32": (ATOL, RTOL), "bf16": (6e-2, 6e-3)}
 
 
 @pytest.fixture(scope="module")
@@ -46,23 +50,24 @@ def test_s1_greedy_ids_and_logits(model, golden, kv):
     shape, table, prompt = model
     e = myos.Engine(shape, N_PROMPT + N_GEN, kv_dtype=kv)
     e.load_table(table)
+    atol, rtol = TOL[kv]
     pl = e.prefill(prompt)
-    np.testing.assert_allclose(pl, golden["prefill_logits"], atol=ATOL, rtol=RTOL)
+    np.testing.assert_allclose(pl, golden["prefill_logits"], atol=atol, rtol=rtol)
     ids = e.greedy_decode(N_GEN)
     ref = golden["ids"]
     # First step where the reference's top-2 gap is below tolerance; the
     # sequences must agree strictly before it.
-    first_close = next((i for i in range(N_GEN) if golden["gap"][i] < ATOL), N_GEN)
+    first_close = next((i for i in range(N_GEN) if golden["gap"][i] < atol), N_GEN)
     diverge = next((i for i in range(N_GEN) if ids[i] != ref[i]), N_GEN)
     assert diverge >= first_close, (diverge, first_close, ids[:diverge + 1], ref[:diverge + 1])
     if diverge == N_GEN:
-        np.testing.assert_allclose(e.logits(), golden["final"], atol=ATOL, rtol=RTOL)
+        np.testing.assert_allclose(e.logits(), golden["final"], atol=atol, rtol=rtol)
 
     # Teacher-forced: every step comparable.
     e.reset()
     e.prefill(prompt)
     am = e.forced_decode(ref)
     # am[i] is the argmax of the logits that chose ref[i]
-    bad = [i for i in range(N_GEN) if am[i] != ref[i] and golden["gap"][i] >= ATOL]
+    bad = [i for i in range(N_GEN) if am[i] != ref[i] and golden["gap"][i] >= atol]
     assert not bad, bad
-    np.testing.assert_allclose(e.logits(), golden["final"], atol=ATOL, rtol=RTOL)
+    np.testing.assert_allclose(e.logits(), golden["final"], atol=atol, rtol=rtol)
