@@ -28,6 +28,7 @@
 #include "../../include/myos_cuda.h"
 #include "kernels.h"
 #include "safetensors.h"
+#include "step_kernel.h"
 
 using namespace myos;
 
@@ -96,6 +97,13 @@ struct myos_ctx {
   float prefill_ms = 0.f, decode_ms = 0.f;
   int steps_per_graph = 16;
   bool profiling = false;
+  // persistent step kernel (one launch per token), when the shape allows
+  bool mega = false;
+  MegaArgs margs = {};
+  MegaLayer* d_layers = nullptr;
+  unsigned* bar = nullptr;  // [5L] phase counters + attention + head counters
+  uint64_t* trace = nullptr;  // MYOS_TRACE_FILE: per-phase timer stamps of the step kernel
+  std::string trace_file;
 };
 
 namespace {
@@ -302,6 +310,14 @@ int launch_kind(myos_ctx* c, int kind, int l, const uint32_t* feed, bool pdl, bo
 
 int enqueue_step(myos_ctx* c, bool head, const uint32_t* feed, bool first_pdl) {
   const int L = (int)c->s.num_layers;
+  if (c->mega) {
+    MegaArgs a = c->margs;
+    a.head = head ? 1 : 0;
+    a.feed = feed;
+    CK(cudaMemsetAsync(c->bar, 0, (size_t)5 * L * sizeof(unsigned), c->st));
+    CK(launch_step_mega(a, c->st));
+    return MYOS_OK;
+  }
   for (int l = 0; l < L; ++l) {
     for (int k = K_QKV; k <= K_DOWN; ++k) {
       int st = launch_kind(c, k, l, feed, (l > 0 || k > K_QKV) || first_pdl, true);
@@ -382,6 +398,16 @@ int finish(myos_ctx* c) {
   cudaError_t e = cudaMemcpyAsync(&c->ctl_host->err, &c->ctl->err, 4, cudaMemcpyDeviceToHost, c->st);
   if (e == cudaSuccess) e = cudaStreamSynchronize(c->st);
   if (e != cudaSuccess) return fail(c, MYOS_ERR_CUDA, std::string("step: ") + cudaGetErrorString(e));
+  if (c->trace) {  // last step's stamps, for offline analysis
+    const size_t nt = (size_t)c->num_sms * (5 * c->s.num_layers + 1) * 4;
+    std::vector<uint64_t> h(nt);
+    if (cudaMemcpy(h.data(), c->trace, nt * 8, cudaMemcpyDeviceToHost) == cudaSuccess) {
+      if (FILE* f = fopen(c->trace_file.c_str(), "wb")) {
+        fwrite(h.data(), 8, nt, f);
+        fclose(f);
+      }
+    }
+  }
   if (c->ctl_host->err) {
     const uint32_t bits = c->ctl_host->err;
     c->ctl_host->err = 0;
@@ -553,6 +579,89 @@ static int create_impl(myos_ctx* c, const myos_shape* shape, const myos_opts* op
   CK(cudaMalloc(&c->sin_t, sn.size() * 4));
   CK(cudaMemcpy(c->cos_t, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
   CK(cudaMemcpy(c->sin_t, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice));
+  // persistent step kernel
+  {
+    const char* e = getenv("MYOS_MEGA");
+    const bool want = !(e && e[0] == '0');
+    const int slot = 24 * 1024;
+    if (want && mega_supported((int)H, (int)I, (int)c->qd, (int)c->kvd, (int)d, (int)c->G, slot) &&
+        (size_t)s.num_kv_heads * nsplit <= (size_t)c->num_sms) {
+      std::vector<MegaLayer> hl(L);
+      for (size_t l = 0; l < L; ++l) {
+        const LayerW& w = c->layers[l];
+        hl[l] = MegaLayer{w.wqkv, w.wo, w.wg, w.wu, w.wd, w.bqkv, w.ln1, w.ln2};
+      }
+      CK(cudaMalloc(&c->d_layers, L * sizeof(MegaLayer)));
+      CK(cudaMemcpy(c->d_layers, hl.data(), L * sizeof(MegaLayer), cudaMemcpyHostToDevice));
+      const size_t nbar = 5 * L + s.num_kv_heads + 1;
+      CK(cudaMalloc(&c->bar, nbar * sizeof(unsigned)));
+      CK(cudaMemset(c->bar, 0, nbar * sizeof(unsigned)));
+      float* mpv = nullptr;
+      uint32_t* mpi = nullptr;
+      CK(cudaMalloc(&mpv, (size_t)c->num_sms * 4));
+      CK(cudaMalloc(&mpi, (size_t)c->num_sms * 4));
+      MegaArgs& a = c->margs;
+      a.L = (int)L;
+      a.H = (int)H;
+      a.I = (int)I;
+      a.V = (int)V;
+      a.qd = (int)c->qd;
+      a.kvd = (int)c->kvd;
+      a.Hq = (int)s.num_q_heads;
+      a.Hkv = (int)s.num_kv_heads;
+      a.d = (int)d;
+      a.G = (int)c->G;
+      a.eps = s.rms_eps;
+      a.scale = 1.0f / sqrtf((float)d);
+      a.embed = c->embed;
+      a.head_w = s.tied_head ? c->embed : c->lm_head;
+      a.final_norm = c->final_norm;
+      a.layers = c->d_layers;
+      a.ctl = c->ctl;
+      a.rec_fed = c->rec_fed;
+      a.rec_argmax = c->rec_argmax;
+      a.resid = c->resid;
+      a.qkv = c->qkv;
+      a.attn = c->attn;
+      a.act = c->act;
+      a.logits = c->logits;
+      a.kcache = c->kcache;
+      a.vcache = c->vcache;
+      a.kv_layer_elems = c->kv_layer_elems;
+      a.S = (int)S;
+      a.kv_bf16 = opts->kv_dtype == MYOS_KV_BF16;
+      a.cos_t = c->cos_t;
+      a.sin_t = c->sin_t;
+      a.nsplit = c->attn_nsplit;
+      a.chunk = c->attn_chunk;
+      a.part_o = c->part_o;
+      a.part_m = c->part_m;
+      a.part_l = c->part_l;
+      a.attn_cnt = c->bar + 5 * L;
+      a.bar = c->bar;
+      a.head_cnt = c->bar + 5 * L + s.num_kv_heads;
+      a.part_val = mpv;
+      a.part_idx = mpi;
+      a.grid = c->num_sms;
+      {
+        const char* la = getenv("MYOS_MEGA_LA");
+        a.lookahead = la ? atoi(la) : 16;
+      }
+      a.scratch_bytes = mega_scratch_bytes((int)H, (int)I, (int)c->qd, (int)d, (int)c->G);
+      a.slot_bytes = slot;
+      int max_smem = 0;
+      CK(cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, c->device));
+      // leave room for the kernel's static shared memory
+      if (mega_configure(&a, max_smem - 2048) == cudaSuccess) c->mega = true;
+      if (const char* tf = getenv("MYOS_TRACE_FILE")) {
+        c->trace_file = tf;
+        const size_t nt = (size_t)c->num_sms * (5 * L + 1) * 4;
+        CK(cudaMalloc(&c->trace, nt * 8));
+        CK(cudaMemset(c->trace, 0, nt * 8));
+        a.trace = c->trace;
+      }
+    }
+  }
   // streams, staging
   CK(cudaStreamCreateWithFlags(&c->st, cudaStreamNonBlocking));
   CK(cudaStreamCreateWithFlags(&c->copy_st, cudaStreamNonBlocking));
@@ -596,7 +705,8 @@ void myos_ctx_destroy(myos_ctx* c) {
   for (auto& kv : c->graphs) cudaGraphExecDestroy(kv.second);
   void* dev[] = {c->warena, c->kcache, c->vcache, c->resid, c->qkv, c->attn, c->act, c->logits,
                  c->part_val, c->part_idx, c->part_o, c->part_m, c->part_l, c->counters, c->ctl,
-                 c->feed, c->rec_fed, c->rec_argmax, c->cos_t, c->sin_t};
+                 c->feed, c->rec_fed, c->rec_argmax, c->cos_t, c->sin_t, c->d_layers, c->bar,
+                 (void*)c->margs.part_val, (void*)c->margs.part_idx, (void*)c->trace};
   for (void* p : dev)
     if (p) cudaFree(p);
   for (int i = 0; i < 2; ++i) {
