@@ -314,7 +314,10 @@ int enqueue_step(myos_ctx* c, bool head, const uint32_t* feed, bool first_pdl) {
     MegaArgs a = c->margs;
     a.head = head ? 1 : 0;
     a.feed = feed;
-    CK(cudaMemsetAsync(c->bar, 0, (size_t)5 * L * sizeof(unsigned), c->st));
+    // phase counters, and the merge / head counters in case an aborted
+    // launch left them non-zero
+    CK(cudaMemsetAsync(c->bar, 0, ((size_t)5 * L + c->s.num_kv_heads + 1) * sizeof(unsigned),
+                       c->st));
     CK(launch_step_mega(a, c->st));
     return MYOS_OK;
   }
@@ -581,10 +584,10 @@ static int create_impl(myos_ctx* c, const myos_shape* shape, const myos_opts* op
   CK(cudaMemcpy(c->sin_t, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice));
   // persistent step kernel
   {
+    // opt-in until it outruns the per-kernel step (MYOS_MEGA=1)
     const char* e = getenv("MYOS_MEGA");
-    const bool want = !(e && e[0] == '0');
-    const int slot = 24 * 1024;
-    if (want && mega_supported((int)H, (int)I, (int)c->qd, (int)c->kvd, (int)d, (int)c->G, slot) &&
+    const bool want = e && e[0] == '1';
+    if (want && mega_supported((int)H, (int)I, (int)c->qd, (int)c->kvd, (int)d, (int)c->G) &&
         (size_t)s.num_kv_heads * nsplit <= (size_t)c->num_sms) {
       std::vector<MegaLayer> hl(L);
       for (size_t l = 0; l < L; ++l) {
@@ -645,10 +648,12 @@ static int create_impl(myos_ctx* c, const myos_shape* shape, const myos_opts* op
       a.grid = c->num_sms;
       {
         const char* la = getenv("MYOS_MEGA_LA");
-        a.lookahead = la ? atoi(la) : 16;
+        a.lookahead = la ? atoi(la) : 3;
+        const char* kb = getenv("MYOS_MEGA_PF_KB");
+        a.pf_kb = kb ? atoi(kb) : 1024;
+        const char* pm = getenv("MYOS_MEGA_PF_MODE");
+        a.pf_mode = pm ? atoi(pm) : 0;
       }
-      a.scratch_bytes = mega_scratch_bytes((int)H, (int)I, (int)c->qd, (int)d, (int)c->G);
-      a.slot_bytes = slot;
       int max_smem = 0;
       CK(cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, c->device));
       // leave room for the kernel's static shared memory

@@ -973,14 +973,15 @@ __global__ void k_rope(float* y, const float* x, int len, int d, const float* cs
 
 // ------------------------------------------------------------------ launchers
 // MYOS_GEMV_KIND selects the GEMV implementation for A/B timing:
-// "bulk" (default: bulk-copy ring), "stream" (register double buffer),
+// "stream" (default: register double buffer, the fastest measured),
+// "bulk" (bulk-copy ring, limited by the per-SM copy-engine rate),
 // "legacy" (row at a time).
 static int gemv_kind() {
   static int v = -1;
   if (v < 0) {
     const char* e = getenv("MYOS_GEMV_KIND");
-    v = 0;
-    if (e && e[0] == 's') v = 1;
+    v = 1;
+    if (e && e[0] == 'b') v = 0;
     if (e && e[0] == 'l') v = 2;
   }
   return v;

@@ -1,28 +1,29 @@
 // One token step of the Qwen2.5 block stack as a single persistent kernel.
 //
 // Why: every phase of a decode step (QKV, attention, o_proj, gate/up, down,
-// head) depends on the whole output of the previous one, and as separate
-// launches each boundary costs several microseconds of drain / launch /
-// re-staging while HBM sits idle. Here one block per SM runs the whole step:
+// head) depends on the whole output of the previous one. As separate
+// launches each boundary costs several microseconds of drain, launch and
+// re-staging with HBM idle, and a step has 5 * layers + 1 of them. Here one
+// block per SM runs the whole step, and phases are separated by device-wide
+// arrival counters (one per phase, zeroed before each launch):
 //
-//   * a producer warp walks a static schedule of every weight stage this
-//     block will consume in the step (all layers, all phases, then the head)
-//     and streams them with 1-D bulk copies (the TMA engine) into an
-//     nslot-deep shared-memory ring, gated only by free slots. Weights never
-//     depend on activations, so HBM keeps streaming through phase boundaries;
-//   * eight consumer warps run the phases in order. Between phases they wait
-//     on a device-wide arrival counter (one per phase, zeroed before each
-//     launch) instead of a kernel boundary;
-//   * every wait (ring slots, phase counters) is bounded in polls and time;
-//     a wait that gives up raises a bit in ctl->err, which makes every later
-//     wait of every block return at once, so the launch always ends and the
-//     host reports MYOS_ERR_TIMEOUT.
-// The launch is cooperative (one block per SM, all resident), so the phase
-// counters never wait on a block that cannot run.
-//
-// Arithmetic is the same as the multi-kernel path (kernels.cu): RMSNorm
-// fused into input staging, f32 accumulation of bf16 weights, fixed-order
-// reductions, epilogues for bias / residual / SiLU*up / argmax.
+//   * each of the 16 warps of a block owns rows of the block's row range of
+//     every weight matrix and streams them with 16-byte loads, double
+//     buffered in registers (the measured fastest way to pull HBM here; a
+//     bulk-copy ring was throughput-limited per SM);
+//   * the first weight batch of a phase is loaded BEFORE the phase's counter
+//     wait, so its HBM latency hides behind the wait and the input staging;
+//   * input staging (RMSNorm fused, crates/tensor_core/src/bf16.rs:231-270)
+//     issues all its loads at once: one L2 round trip per phase;
+//   * attention tasks (KV head, key split) preload their cached K/V tile
+//     before the wait; with few splits their merge is folded into the o_proj
+//     staging, otherwise the last task of a head group merges;
+//   * every counter wait is bounded in polls and time; a wait that gives up
+//     raises a bit in ctl->err, which ends every later wait of every block at
+//     once, so the launch always finishes and the host reports
+//     MYOS_ERR_TIMEOUT.
+// The launch is cooperative (one block per SM, all resident), so a counter
+// never waits on a block that cannot run.
 #include <math.h>
 
 #include "common.cuh"
@@ -32,29 +33,22 @@ namespace myos {
 
 namespace {
 
-constexpr int kCW = 8;                  // consumer warps
-constexpr int kCT = kCW * 32;           // consumer threads
-constexpr int kStepThreads = kCT + 32;  // + producer warp
-constexpr int kTile = 32;               // attention key tile
+constexpr int kW = 16;       // warps per block
+constexpr int kT = kW * 32;  // threads per block
+constexpr int kTile = 32;    // attention key tile
 constexpr int kMaxG = 8;
+constexpr int kCombineMax = 32;  // attention tasks merged in the o_proj staging
 
 enum Phase { PH_QKV = 0, PH_ATTN = 1, PH_O = 2, PH_GU = 3, PH_DOWN = 4, PH_HEAD = 5 };
 
 struct PhaseW {
   const uint16_t* w0;
   const uint16_t* w1;
-  int M, K, NR, rs;
+  int M, K, NR;
 };
 
-MYOS_DEV int rows_per_stage(int K, int NR, int slot_bytes) {
-  int r = 8;
-  while (r > 1 && NR * r * K * 2 > slot_bytes) r >>= 1;
-  return r;
-}
-
-// Weight matrix of phase p (layer l), or M = 0 for attention.
 MYOS_DEV PhaseW phase_w(const MegaArgs& a, int kind, int l) {
-  PhaseW w = {nullptr, nullptr, 0, 0, 1, 1};
+  PhaseW w = {nullptr, nullptr, 0, 0, 1};
   if (kind == PH_HEAD) {
     w.w0 = a.head_w;
     w.M = a.V;
@@ -81,7 +75,6 @@ MYOS_DEV PhaseW phase_w(const MegaArgs& a, int kind, int l) {
       w.K = a.I;
     }
   }
-  if (w.M) w.rs = rows_per_stage(w.K, w.NR, a.slot_bytes);
   return w;
 }
 
@@ -101,126 +94,268 @@ MYOS_DEV uint32_t ld_volatile(const uint32_t* p) {
   return *reinterpret_cast<const volatile uint32_t*>(p);
 }
 
-// Bounded ring wait that also gives up at once when another block failed.
-MYOS_DEV void ring_wait(uint64_t* bar, uint32_t parity, uint32_t* err, uint32_t code) {
-  if (mbar_try_wait(bar, parity)) return;
-  const uint64_t t0 = global_ns();
-  for (uint32_t i = 1; i < kWaitLimit; ++i) {
-    if (mbar_try_wait(bar, parity)) return;
-    if ((i & 255u) == 0) {
-      if (ld_volatile(err)) return;
-      if (global_ns() - t0 > 1000000000ull) break;
-    }
-  }
-  atomicOr(err, code);
-}
-
-// Phase arrival: every consumer thread fences its writes, then one thread
-// counts the block in.
+// Phase arrival: every thread fences its writes, then one thread counts the
+// block in. Returns the previous count (thread 0 only).
 MYOS_DEV uint32_t phase_arrive(unsigned* cnt) {
   __threadfence();
-  named_sync(1, kCT);
+  __syncthreads();
   uint32_t prev = 0;
   if (threadIdx.x == 0) prev = atomicAdd(cnt, 1u);
   return prev;
 }
 
+// Wait until every block arrived; bounded (polls and one second), and
+// abandoned at once when another block already reported a failure.
 MYOS_DEV void phase_wait(const unsigned* cnt, uint32_t target, uint32_t* err) {
-  if (threadIdx.x == 0) {
-    if (ld_acquire(cnt) < target) {
-      const uint64_t t0 = global_ns();
-      for (uint32_t i = 0;; ++i) {
-        if (ld_acquire(cnt) >= target) break;
-        if ((i & 63u) == 0) {
-          if (ld_volatile(err)) break;
-          if (i > kWaitLimit || global_ns() - t0 > 1000000000ull) {
-            atomicOr(err, kErrPhase);
-            break;
-          }
+  if (threadIdx.x == 0 && ld_acquire(cnt) < target) {
+    const uint64_t t0 = global_ns();
+    for (uint32_t i = 0;; ++i) {
+      if (ld_acquire(cnt) >= target) break;
+      if ((i & 63u) == 0) {
+        if (ld_volatile(err)) break;
+        if (i > kWaitLimit || global_ns() - t0 > 1000000000ull) {
+          atomicOr(err, kErrPhase);
+          break;
         }
       }
     }
   }
-  named_sync(1, kCT);
+  __syncthreads();
 }
 
-MYOS_DEV float csum(float v, float* red) {
+MYOS_DEV float bsum(float v, float* red) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   v = warp_sum(v);
   if (lane == 0) red[warp] = v;
-  named_sync(2, kCT);
+  __syncthreads();
   if (warp == 0) {
-    float s = lane < kCW ? red[lane] : 0.0f;
+    float s = lane < kW ? red[lane] : 0.0f;
     s = warp_sum(s);
     if (lane == 0) red[32] = s;
   }
-  named_sync(2, kCT);
+  __syncthreads();
   const float s = red[32];
-  named_sync(2, kCT);
+  __syncthreads();
   return s;
 }
 
-// ---------------------------------------------------------------- staging
-// x (f32 activations, or a bf16 embedding row) into the split layout, with
-// the optional RMSNorm gamma * (x * inv) of crates/tensor_core/src/bf16.rs:231-270.
-__device__ __noinline__ void stage_c(float* xs, int K, const float* xf, const uint16_t* xb,
-                                     const float* gamma,
-                      float eps, float* x_store, float* red) {
-  const int nchunk = K >> 3, half = K >> 1;
-  float4* xlo = reinterpret_cast<float4*>(xs);
-  float4* xhi = reinterpret_cast<float4*>(xs + half);
-  constexpr int B = 4;
-  for (int c0 = threadIdx.x; c0 < nchunk; c0 += kCT * B) {
-    float4 lo[B], hi[B];
-#pragma unroll
-    for (int i = 0; i < B; ++i) {
-      const int c = c0 + i * kCT;
-      if (c < nchunk) {
-        if (xb) {
-          const uint4 u = __ldg(reinterpret_cast<const uint4*>(xb) + c);
-          lo[i] = make_float4(bf16_lo(u.x), bf16_hi(u.x), bf16_lo(u.y), bf16_hi(u.y));
-          hi[i] = make_float4(bf16_lo(u.z), bf16_hi(u.z), bf16_lo(u.w), bf16_hi(u.w));
-        } else {
-          lo[i] = __ldcg(reinterpret_cast<const float4*>(xf) + 2 * c);
-          hi[i] = __ldcg(reinterpret_cast<const float4*>(xf) + 2 * c + 1);
-        }
-      }
-    }
-#pragma unroll
-    for (int i = 0; i < B; ++i) {
-      const int c = c0 + i * kCT;
-      if (c < nchunk) {
-        xlo[c] = lo[i];
-        xhi[c] = hi[i];
-        if (x_store) {
-          __stcg(reinterpret_cast<float4*>(x_store) + 2 * c, lo[i]);
-          __stcg(reinterpret_cast<float4*>(x_store) + 2 * c + 1, hi[i]);
-        }
-      }
-    }
-  }
-  named_sync(2, kCT);
-  if (!gamma) return;
-  float ss = 0.0f;
-  for (int j = threadIdx.x; j < K; j += kCT) ss = fmaf(xs[j], xs[j], ss);
-  ss = csum(ss, red);
-  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), eps)));
-  for (int c = threadIdx.x; c < nchunk; c += kCT) {
-    const float4 g0 = __ldg(reinterpret_cast<const float4*>(gamma) + 2 * c);
-    const float4 g1 = __ldg(reinterpret_cast<const float4*>(gamma) + 2 * c + 1);
-    float4 p = xlo[c], q = xhi[c];
-    p = make_float4(__fmul_rn(g0.x, __fmul_rn(p.x, inv)), __fmul_rn(g0.y, __fmul_rn(p.y, inv)),
-                    __fmul_rn(g0.z, __fmul_rn(p.z, inv)), __fmul_rn(g0.w, __fmul_rn(p.w, inv)));
-    q = make_float4(__fmul_rn(g1.x, __fmul_rn(q.x, inv)), __fmul_rn(g1.y, __fmul_rn(q.y, inv)),
-                    __fmul_rn(g1.z, __fmul_rn(q.z, inv)), __fmul_rn(g1.w, __fmul_rn(q.w, inv)));
-    xlo[c] = p;
-    xhi[c] = q;
-  }
-  named_sync(2, kCT);
+// ---------------------------------------------------------------- L2 prefetch
+// Weight slices of phases ahead are requested into L2 while this block still
+// waits on the dependency chain (counters, staging, attention), so HBM keeps
+// streaming through the latency-bound phases. Block b's rows of a row-major
+// matrix are one contiguous byte range.
+MYOS_DEV void prefetch_line_range(const void* base, size_t bytes) {
+  const uintptr_t a0 = (uintptr_t)base & ~(uintptr_t)127;
+  const uintptr_t end = (uintptr_t)base + bytes;
+  for (uintptr_t p = a0 + (uintptr_t)threadIdx.x * 128; p < end; p += (uintptr_t)kT * 128)
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
 }
 
-MYOS_DEV float dot8s(const uint4& u, const float4& lo, const float4& hi, float acc) {
-  return dot8(u, lo, hi, acc);
+MYOS_DEV void prefetch_phase(const MegaArgs& a, int q) {
+  const int nph = 5 * a.L + (a.head ? 1 : 0);
+  if (q >= nph) return;
+  const int kind = q < 5 * a.L ? q % 5 : PH_HEAD;
+  if (kind == PH_ATTN) return;
+  const PhaseW w = phase_w(a, kind, q / 5);
+  int r0, r1;
+  block_rows(w.M, &r0, &r1);
+  size_t bytes = (size_t)(r1 - r0) * w.K * 2;
+  const size_t cap = (size_t)a.pf_kb << 10;
+  if (bytes > cap) bytes = cap;
+  const uint16_t* m[2] = {w.w0, w.w1};
+  for (int r = 0; r < w.NR; ++r) {
+    const uint16_t* p = m[r] + (size_t)r0 * w.K;
+    if (a.pf_mode) prefetch_line_range(p, bytes);
+    else prefetch_range(p, bytes);
+  }
+}
+
+// ---------------------------------------------------------------- staging
+// Inputs land in shared memory through cp.async (no registers held, so the
+// first weight batch stays in flight meanwhile), in the split layout the
+// GEMV loop reads: chunk c of 8 values puts 4 at xs[4c] and 4 at
+// xs[K/2 + 4c]. Each thread copies and later reads back only its own
+// chunks, so its own cp.async wait orders them.
+MYOS_DEV void cpa16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
+               : "memory");
+}
+MYOS_DEV void cpa_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// Split-layout copy of K f32 values.
+MYOS_DEV void copy_split(float* xs, const float* x, int K) {
+  const float4* x4 = reinterpret_cast<const float4*>(x);
+  float4* lo = reinterpret_cast<float4*>(xs);
+  float4* hi = reinterpret_cast<float4*>(xs + (K >> 1));
+  for (int c = threadIdx.x; c < (K >> 3); c += kT) {
+    cpa16(lo + c, x4 + 2 * c);
+    cpa16(hi + c, x4 + 2 * c + 1);
+  }
+}
+
+// Embedding row (bf16) into the split layout via a raw copy in eb.
+MYOS_DEV void copy_embed(float* xs, const uint16_t* row, int K, uint4* eb) {
+  const uint4* r4 = reinterpret_cast<const uint4*>(row);
+  for (int c = threadIdx.x; c < (K >> 3); c += kT) cpa16(eb + c, r4 + c);
+  cpa_wait_all();
+  float4* lo = reinterpret_cast<float4*>(xs);
+  float4* hi = reinterpret_cast<float4*>(xs + (K >> 1));
+  for (int c = threadIdx.x; c < (K >> 3); c += kT) {
+    const uint4 u = eb[c];
+    lo[c] = make_float4(bf16_lo(u.x), bf16_hi(u.x), bf16_lo(u.y), bf16_hi(u.y));
+    hi[c] = make_float4(bf16_lo(u.z), bf16_hi(u.z), bf16_lo(u.w), bf16_hi(u.w));
+  }
+}
+
+// RMSNorm in place over the staged split layout, gamma staged the same way
+// in gs: y = gamma * (x * inv), inv = 1 / sqrtf(mean(x^2) + eps)
+// (crates/tensor_core/src/bf16.rs:231-270); optionally stores the raw x
+// (natural order) to x_store first.
+MYOS_DEV void norm_split(float* xs, const float* gs, int K, float eps, float* x_store, float* red) {
+  const int half = K >> 1;
+  float4* lo = reinterpret_cast<float4*>(xs);
+  float4* hi = reinterpret_cast<float4*>(xs + half);
+  const float4* glo = reinterpret_cast<const float4*>(gs);
+  const float4* ghi = reinterpret_cast<const float4*>(gs + half);
+  float ss = 0.0f;
+  for (int c = threadIdx.x; c < (K >> 3); c += kT) {
+    const float4 u = lo[c], v = hi[c];
+    ss = fmaf(u.x, u.x, ss);
+    ss = fmaf(u.y, u.y, ss);
+    ss = fmaf(u.z, u.z, ss);
+    ss = fmaf(u.w, u.w, ss);
+    ss = fmaf(v.x, v.x, ss);
+    ss = fmaf(v.y, v.y, ss);
+    ss = fmaf(v.z, v.z, ss);
+    ss = fmaf(v.w, v.w, ss);
+  }
+  ss = bsum(ss, red);
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), eps)));
+  for (int c = threadIdx.x; c < (K >> 3); c += kT) {
+    const float4 u = lo[c], v = hi[c], g = glo[c], h = ghi[c];
+    if (x_store) {
+      __stcg(reinterpret_cast<float4*>(x_store) + 2 * c, u);
+      __stcg(reinterpret_cast<float4*>(x_store) + 2 * c + 1, v);
+    }
+    lo[c] = make_float4(__fmul_rn(g.x, __fmul_rn(u.x, inv)), __fmul_rn(g.y, __fmul_rn(u.y, inv)),
+                        __fmul_rn(g.z, __fmul_rn(u.z, inv)), __fmul_rn(g.w, __fmul_rn(u.w, inv)));
+    hi[c] = make_float4(__fmul_rn(h.x, __fmul_rn(v.x, inv)), __fmul_rn(h.y, __fmul_rn(v.y, inv)),
+                        __fmul_rn(h.z, __fmul_rn(v.z, inv)), __fmul_rn(h.w, __fmul_rn(v.w, inv)));
+  }
+}
+
+MYOS_DEV void put_split(float* xs, int K, int j, float v) {
+  const int c = j >> 3, e = j & 7;
+  xs[e < 4 ? (c * 4 + e) : ((K >> 1) + c * 4 + (e - 4))] = v;
+}
+
+// Per (head group, split) merge factors f = expf(m - M) and per-head sums
+// L = sum l * f for head rows [h0, h0 + nh), from split partials m, l laid
+// out [Hkv][nsplit][G]; fs is overwritten by the factors.
+MYOS_DEV void merge_factors(const MegaArgs& a, float* fs, const float* ls, float* Ls, int h0,
+                            int nh) {
+  const int G = a.G, ns = a.nsplit;
+  if (threadIdx.x < nh) {
+    const int h = h0 + threadIdx.x, g = h / G, hh = h - g * G;
+    float M = -INFINITY;
+    for (int q = 0; q < ns; ++q) M = fmaxf(M, fs[(g * ns + q) * G + hh]);
+    float L = 0.0f;
+    for (int q = 0; q < ns; ++q) {
+      const int i = (g * ns + q) * G + hh;
+      const float mq = fs[i];
+      const float f = mq == -INFINITY ? 0.0f : expf(mq - M);
+      fs[i] = f;
+      L = fmaf(ls[i], f, L);
+    }
+    Ls[threadIdx.x] = L;
+  }
+  __syncthreads();
+}
+
+// o_proj input from the split partials (few splits): every partial copied
+// into shared memory at once, then out = sum_q part_o * f / L (the
+// reference's e / sum, reassociated) written in the split layout.
+MYOS_DEV void merge_stage(const MegaArgs& a, float* xs, int K, float* mb) {
+  const int T = a.Hkv * a.nsplit, Tg = T * a.G, d = a.d, G = a.G, ns = a.nsplit;
+  float* po = mb;             // [T][G][d]
+  float* fs = po + Tg * d;    // [T][G]
+  float* ls = fs + Tg;        // [T][G]
+  float* Ls = ls + Tg;        // [Hq]
+  const float4* s4 = reinterpret_cast<const float4*>(a.part_o);
+  for (int i = threadIdx.x; i < (Tg * d) >> 2; i += kT) cpa16(reinterpret_cast<float4*>(po) + i, s4 + i);
+  for (int i = threadIdx.x; i < Tg; i += kT) {
+    fs[i] = __ldcg(a.part_m + i);
+    ls[i] = __ldcg(a.part_l + i);
+  }
+  cpa_wait_all();
+  __syncthreads();
+  merge_factors(a, fs, ls, Ls, 0, a.Hq);
+  for (int o = threadIdx.x; o < K; o += kT) {
+    const int h = o / d, e = o - h * d, g = h / G, hh = h - g * G;
+    float O = 0.0f;
+    for (int q = 0; q < ns; ++q) {
+      const int i = (g * ns + q) * G + hh;
+      O = fmaf(po[i * d + e], fs[i], O);
+    }
+    put_split(xs, K, o, __fdiv_rn(O, Ls[h]));
+  }
+}
+
+// Many splits: the merge of head group g from global partials, in groups of
+// 2 outputs x 8 splits per load round.
+MYOS_DEV void merge_group(const MegaArgs& a, int g, float* sm, float* att) {
+  const int G = a.G, d = a.d, ns = a.nsplit, n = G * d;
+  float* fs = sm;
+  float* ls = fs + ns * G;
+  float* Ls = ls + ns * G;
+  for (int i = threadIdx.x; i < ns * G; i += kT) {
+    fs[i] = __ldcg(a.part_m + (size_t)g * ns * G + i);
+    ls[i] = __ldcg(a.part_l + (size_t)g * ns * G + i);
+  }
+  __syncthreads();
+  // factors for this group's heads (local indices: group 0 of the tables)
+  if (threadIdx.x < G) {
+    const int hh = threadIdx.x;
+    float M = -INFINITY;
+    for (int q = 0; q < ns; ++q) M = fmaxf(M, fs[q * G + hh]);
+    float L = 0.0f;
+    for (int q = 0; q < ns; ++q) {
+      const float mq = fs[q * G + hh];
+      const float f = mq == -INFINITY ? 0.0f : expf(mq - M);
+      fs[q * G + hh] = f;
+      L = fmaf(ls[q * G + hh], f, L);
+    }
+    Ls[hh] = L;
+  }
+  __syncthreads();
+  constexpr int kO = 2, kS = 8;
+  for (int ob = 0; ob < n; ob += kO * kT) {
+    float O[kO] = {0.0f, 0.0f};
+    for (int q0 = 0; q0 < ns; q0 += kS) {
+      float v[kO][kS];
+#pragma unroll
+      for (int k = 0; k < kO; ++k) {
+        const int o = ob + threadIdx.x + kT * k, hh = o / d, e = o - hh * d;
+#pragma unroll
+        for (int u = 0; u < kS; ++u)
+          v[k][u] = (o < n && q0 + u < ns)
+                        ? __ldcg(a.part_o + (((size_t)g * ns + q0 + u) * G + hh) * d + e)
+                        : 0.0f;
+      }
+#pragma unroll
+      for (int k = 0; k < kO; ++k) {
+        const int o = ob + threadIdx.x + kT * k, hh = o / d;
+#pragma unroll
+        for (int u = 0; u < kS; ++u)
+          if (o < n && q0 + u < ns) O[k] = fmaf(v[k][u], fs[(q0 + u) * G + hh], O[k]);
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < kO; ++k) {
+      const int o = ob + threadIdx.x + kT * k;
+      if (o < n) __stcg(att + o, __fdiv_rn(O[k], Ls[o / d]));
+    }
+  }
 }
 
 MYOS_DEV bool better(float v, uint32_t i, float bv, uint32_t bi) {
@@ -232,18 +367,116 @@ MYOS_DEV float silu_mul(float g, float u) {
   return __fmul_rn(s, u);
 }
 
+// ---------------------------------------------------------------- GEMV phase
+// One GEMV phase on this block's rows: the first weight batch is loaded,
+// then the phase waits for its inputs and stages them, then streams the
+// rest. Warp w owns rows r0 + w + kW*i; per row K/256 chunks of 16 bytes per
+// lane, in batches of kU double-buffered in registers. One loop serves every
+// phase kind (gate/up streams two matrices, the others one) so the kernel
+// holds a single copy of it.
+constexpr int kU = 4;
+
+MYOS_DEV void gemv_phase(const MegaArgs& a, int p, int kind, uint32_t tok, float* xs, float* red,
+                         float* bvp, uint32_t* bip) {
+  const int l = p / 5;
+  const PhaseW w = phase_w(a, kind, l);
+  const bool two = w.NR == 2;
+  uint64_t* tr = a.trace ? a.trace + ((size_t)blockIdx.x * (5 * a.L + 1) + p) * 4 : nullptr;
+  int r0, r1;
+  block_rows(w.M, &r0, &r1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int K = w.K, P = K >> 8, nbr = (P + kU - 1) / kU;
+  const int nrw = r1 - r0 > warp ? (r1 - r0 - warp + kW - 1) / kW : 0;
+  const int nb = nrw * nbr;
+  uint4 cur[2][kU], nxt[2][kU];
+  auto load = [&](uint4(&buf)[2][kU], int bt) {
+    const int rb = bt / nbr, j0 = (bt - rb * nbr) * kU;
+    const size_t off = (size_t)(r0 + warp + kW * rb) * K;
+    const uint4* s0 = reinterpret_cast<const uint4*>(w.w0 + off) + lane;
+    const uint4* s1 = reinterpret_cast<const uint4*>((two ? w.w1 : w.w0) + off) + lane;
+#pragma unroll
+    for (int i = 0; i < kU; ++i) {
+      const int j = j0 + i;
+      buf[0][i] = j < P ? ld_stream(s0 + 32 * j) : make_uint4(0u, 0u, 0u, 0u);
+      buf[1][i] = (two && j < P) ? ld_stream(s1 + 32 * j) : make_uint4(0u, 0u, 0u, 0u);
+    }
+  };
+  if (nb > 0) load(cur, 0);
+  // ---- inputs: gamma needs no wait; x does
+  const MegaLayer* Ly = kind == PH_HEAD ? nullptr : &a.layers[l];
+  const float* gamma = kind == PH_QKV ? Ly->ln1
+                       : kind == PH_GU ? Ly->ln2
+                       : kind == PH_HEAD ? a.final_norm
+                                         : nullptr;
+  float* gs = xs + a.x_floats;
+  if (gamma) copy_split(gs, gamma, K);
+  if (p > 0) phase_wait(&a.bar[p - 1], gridDim.x, &a.ctl->err);
+  if (tr && threadIdx.x == 0) tr[0] = global_ns();
+  if (kind == PH_QKV && l == 0) {
+    copy_embed(xs, a.embed + (size_t)tok * a.H, K, reinterpret_cast<uint4*>(gs + a.H));
+  } else if (kind == PH_O && a.merge_in_stage) {
+    merge_stage(a, xs, K, gs);
+  } else {
+    copy_split(xs, kind == PH_O ? a.attn : kind == PH_DOWN ? a.act : a.resid, K);
+  }
+  cpa_wait_all();
+  if (gamma)
+    norm_split(xs, gs, K, a.eps, (kind == PH_QKV && l == 0 && blockIdx.x == 0) ? a.resid : nullptr,
+               red);
+  __syncthreads();
+  if (tr && threadIdx.x == 0) tr[1] = global_ns();
+  // ---- stream
+  const float4* xlo = reinterpret_cast<const float4*>(xs);
+  const float4* xhi = reinterpret_cast<const float4*>(xs + (K >> 1));
+  float* const out = kind == PH_QKV ? a.qkv
+                     : kind == PH_GU ? a.act
+                     : kind == PH_HEAD ? a.logits
+                                       : a.resid;
+  float bv = -INFINITY;
+  uint32_t bi = 0xffffffffu;
+  float acc0 = 0.0f, acc1 = 0.0f;
+  for (int bt = 0; bt < nb; ++bt) {
+    const int rb = bt / nbr, jb = bt - rb * nbr;
+    if (bt + 1 < nb) load(nxt, bt + 1);
+#pragma unroll
+    for (int i = 0; i < kU; ++i) {
+      const int j = jb * kU + i;
+      if (j < P) {
+        const float4 lo = xlo[lane + 32 * j], hi = xhi[lane + 32 * j];
+        acc0 = dot8(cur[0][i], lo, hi, acc0);
+        if (two) acc1 = dot8(cur[1][i], lo, hi, acc1);
+      }
+    }
+    if (jb == nbr - 1) {
+      const int row = r0 + warp + kW * rb;
+      const float v0 = warp_sum(acc0);
+      const float v1 = two ? warp_sum(acc1) : 0.0f;
+      acc0 = acc1 = 0.0f;
+      if (kind == PH_HEAD && better(v0, (uint32_t)row, bv, bi)) {
+        bv = v0;
+        bi = (uint32_t)row;
+      }
+      if (lane == 0) {
+        if (kind == PH_QKV) __stcg(out + row, __fadd_rn(v0, __ldg(Ly->bqkv + row)));
+        else if (kind == PH_O || kind == PH_DOWN) __stcg(out + row, __fadd_rn(__ldcg(out + row), v0));
+        else if (kind == PH_GU) __stcg(out + row, silu_mul(v0, v1));
+        else __stcg(out + row, v0);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < kU; ++i) {
+      cur[0][i] = nxt[0][i];
+      cur[1][i] = nxt[1][i];
+    }
+  }
+  if (tr && threadIdx.x == 0) tr[2] = global_ns();
+  if (kind == PH_HEAD && lane == 0) {
+    bvp[warp] = bv;
+    bip[warp] = bi;
+  }
+}
+
 // ---------------------------------------------------------------- attention
-template <typename KT>
-MYOS_DEV float4 kvl4(const KT* p);
-template <>
-MYOS_DEV float4 kvl4<float>(const float* p) {
-  return __ldcg(reinterpret_cast<const float4*>(p));
-}
-template <>
-MYOS_DEV float4 kvl4<__nv_bfloat16>(const __nv_bfloat16* p) {
-  const uint2 u = __ldcg(reinterpret_cast<const uint2*>(p));
-  return make_float4(bf16_lo(u.x), bf16_hi(u.x), bf16_lo(u.y), bf16_hi(u.y));
-}
 template <typename KT>
 MYOS_DEV KT kv_round(float v);
 template <>
@@ -255,134 +488,171 @@ MYOS_DEV __nv_bfloat16 kv_round<__nv_bfloat16>(float v) {
   return __float2bfloat16_rn(v);
 }
 
-MYOS_DEV float rope1(const float* x, int e, int d, const float* cs, const float* sn) {
-  const int half = d >> 1;
-  const int p = e < half ? e : e - half;
-  const float x0 = x[p], x1 = x[p + half];
-  return e < half ? __fsub_rn(__fmul_rn(x0, cs[p]), __fmul_rn(x1, sn[p]))
-                  : __fadd_rn(__fmul_rn(x1, cs[p]), __fmul_rn(x0, sn[p]));
+struct AttnSmem {
+  float *qs, *ks, *vs, *ps, *corr, *knew, *vnew, *cs, *sn;
+  uint4* raw;  // bf16 tile rows before widening: [2][kTile][d / 8]
+};
+
+MYOS_DEV AttnSmem attn_smem(float* sm, int G, int d) {
+  AttnSmem s;
+  const int ds = d + 4;
+  s.qs = sm;
+  s.ks = s.qs + G * d;
+  s.vs = s.ks + kTile * ds;
+  s.ps = s.vs + kTile * ds;
+  s.corr = s.ps + G * kTile;
+  s.knew = s.corr + kMaxG;
+  s.vnew = s.knew + d;
+  s.cs = s.vnew + d;
+  s.sn = s.cs + d / 2;
+  s.raw = reinterpret_cast<uint4*>(s.sn + d / 2);  // 16-byte aligned: offsets are multiples of 4
+  return s;
 }
 
-// Attention task (KV head g, key split s) for the decode position pos, by
-// the 256 consumer threads, in the shared scratch sm. Same math as k_attn.
 template <typename KT>
-__device__ __noinline__ void attention_task(const MegaArgs& a, int layer, int g, int s, int pos,
-                                            float* sm, int* flag) {
+MYOS_DEV KT* kv_base(const MegaArgs& a, void* cache, int layer, int g) {
+  return reinterpret_cast<KT*>(reinterpret_cast<uint8_t*>(cache) +
+                               (size_t)layer * a.kv_layer_elems * sizeof(KT)) +
+         (size_t)g * a.S * a.d;
+}
+
+// Cached rows [t0, t0 + nk) except `skip` (the new position) into the
+// padded K/V tiles through cp.async: f32 rows straight into the tiles, bf16
+// rows into a raw buffer that tile_finish widens. Each thread widens only
+// the 16-byte pieces it copied itself, after its own cp.async wait.
+template <typename KT>
+MYOS_DEV void tile_issue(const KT* kc, const KT* vc, int d, int t0, int nk, int skip, float* ks,
+                         float* vs, uint4* raw) {
+  constexpr int per = 16 / sizeof(KT);  // elements per 16-byte piece
+  const int ppr = d / per, n = nk * ppr, ds = d + 4;
+  for (int i = threadIdx.x; i < n; i += kT) {
+    const int tt = i / ppr, e = (i - tt * ppr) * per;
+    if (t0 + tt == skip) continue;
+    const KT* ksrc = kc + (size_t)(t0 + tt) * d + e;
+    const KT* vsrc = vc + (size_t)(t0 + tt) * d + e;
+    if (sizeof(KT) == 4) {
+      cpa16(ks + tt * ds + e, ksrc);
+      cpa16(vs + tt * ds + e, vsrc);
+    } else {
+      cpa16(raw + i, ksrc);
+      cpa16(raw + kTile * ppr + i, vsrc);
+    }
+  }
+}
+
+template <typename KT>
+MYOS_DEV void tile_finish(int d, int t0, int nk, int skip, float* ks, float* vs, const uint4* raw) {
+  cpa_wait_all();
+  if (sizeof(KT) == 4) return;
+  const int ppr = d / 8, n = nk * ppr, ds = d + 4;
+  for (int i = threadIdx.x; i < n; i += kT) {
+    const int tt = i / ppr, e = (i - tt * ppr) * 8;
+    if (t0 + tt == skip) continue;
+    const uint4 u = raw[i], v = raw[kTile * ppr + i];
+    float4* kd = reinterpret_cast<float4*>(ks + tt * ds + e);
+    float4* vd = reinterpret_cast<float4*>(vs + tt * ds + e);
+    kd[0] = make_float4(bf16_lo(u.x), bf16_hi(u.x), bf16_lo(u.y), bf16_hi(u.y));
+    kd[1] = make_float4(bf16_lo(u.z), bf16_hi(u.z), bf16_lo(u.w), bf16_hi(u.w));
+    vd[0] = make_float4(bf16_lo(v.x), bf16_hi(v.x), bf16_lo(v.y), bf16_hi(v.y));
+    vd[1] = make_float4(bf16_lo(v.z), bf16_hi(v.z), bf16_lo(v.w), bf16_hi(v.w));
+  }
+}
+
+// Attention task (KV head g, key split s) at decode position pos: scores,
+// online softmax and value mix over the split's keys (the math of
+// crates/tensor_core/src/gqa.rs:174-218 reassociated as flash decoding);
+// writes the split's (sum e*v, max, sum e). The first tile of cached keys
+// and the rotation table row are already in shared memory.
+template <typename KT>
+MYOS_DEV void attention_task(const MegaArgs& a, int layer, int g, int s, int pos, float* sm) {
   const int d = a.d, G = a.G, half = d >> 1, ds = d + 4;
-  float* qs = sm;
-  float* ks = qs + G * d;
-  float* vs = ks + kTile * ds;
-  float* ps = vs + kTile * ds;
-  float* corr = ps + G * kTile;
-  float* knew = corr + kMaxG;
-  float* vnew = knew + d;
+  const AttnSmem S = attn_smem(sm, G, d);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const size_t kv_elt = sizeof(KT);
-  KT* kc = reinterpret_cast<KT*>(reinterpret_cast<uint8_t*>(a.kcache) +
-                                 (size_t)layer * a.kv_layer_elems * kv_elt) + (size_t)g * a.S * d;
-  KT* vc = reinterpret_cast<KT*>(reinterpret_cast<uint8_t*>(a.vcache) +
-                                 (size_t)layer * a.kv_layer_elems * kv_elt) + (size_t)g * a.S * d;
-  const int nkeys = pos + 1;
-  const int kb = s * a.chunk, ke = min(kb + a.chunk, nkeys);
+  KT* kc = kv_base<KT>(a, a.kcache, layer, g);
+  KT* vc = kv_base<KT>(a, a.vcache, layer, g);
+  const int kb = s * a.chunk, ke = min(kb + a.chunk, pos + 1);
   const bool has_new = pos >= kb && pos < ke;
-  const float* cs = a.cos_t + (size_t)pos * half;
-  const float* sn = a.sin_t + (size_t)pos * half;
   {
-    float* qraw = ks;
-    float* cst = vs;
-    float* snt = vs + half;
-    float* kraw = vs + d;
-    float* vraw = vs + 2 * d;
-    const int nq = G * d;
-    const int ntot = nq + d + (has_new ? 2 * d : 0);
-    const float* qsrc = a.qkv + (size_t)g * G * d;
-    const float* ksrc = a.qkv + (size_t)a.Hq * d + (size_t)g * d;
-    const float* vsrc = a.qkv + (size_t)(a.Hq + a.Hkv) * d + (size_t)g * d;
-    constexpr int kJ = 12;
-    float val[kJ];
+    // q of the G heads, and this KV head's new k and v: one float4 each
+    const int nq4 = G * d / 4, d4 = d / 4;
+    const int ntot = nq4 + (has_new ? 2 * d4 : 0);
+    const float4* qsrc = reinterpret_cast<const float4*>(a.qkv + (size_t)g * G * d);
+    const float4* ksrc = reinterpret_cast<const float4*>(a.qkv + (size_t)a.Hq * d + (size_t)g * d);
+    const float4* vsrc =
+        reinterpret_cast<const float4*>(a.qkv + (size_t)(a.Hq + a.Hkv) * d + (size_t)g * d);
+    constexpr int kJ = (kMaxG * 64 + 128 + kT - 1) / kT;
+    float4 val[kJ];
 #pragma unroll
     for (int j = 0; j < kJ; ++j) {
-      const int v = threadIdx.x + kCT * j;
-      if (v < ntot) {
-        if (v < nq) val[j] = __ldcg(qsrc + v);
-        else if (v < nq + half) val[j] = __ldg(cs + (v - nq));
-        else if (v < nq + d) val[j] = __ldg(sn + (v - nq - half));
-        else if (v < nq + 2 * d) val[j] = __ldcg(ksrc + (v - nq - d));
-        else val[j] = __ldcg(vsrc + (v - nq - 2 * d));
-      }
+      const int v = threadIdx.x + kT * j;
+      if (v < ntot)
+        val[j] = v < nq4 ? __ldcg(qsrc + v)
+                         : (v < nq4 + d4 ? __ldcg(ksrc + (v - nq4)) : __ldcg(vsrc + (v - nq4 - d4)));
     }
 #pragma unroll
     for (int j = 0; j < kJ; ++j) {
-      const int v = threadIdx.x + kCT * j;
+      const int v = threadIdx.x + kT * j;
       if (v < ntot) {
-        if (v < nq) qraw[v] = val[j];
-        else if (v < nq + half) cst[v - nq] = val[j];
-        else if (v < nq + d) snt[v - nq - half] = val[j];
-        else if (v < nq + 2 * d) kraw[v - nq - d] = val[j];
-        else vraw[v - nq - 2 * d] = val[j];
+        float4* dst = v < nq4 ? reinterpret_cast<float4*>(S.qs) + v
+                              : (v < nq4 + d4 ? reinterpret_cast<float4*>(S.knew) + (v - nq4)
+                                              : reinterpret_cast<float4*>(S.vnew) + (v - nq4 - d4));
+        *dst = val[j];
       }
     }
-    named_sync(2, kCT);
-    for (int i = threadIdx.x; i < nq; i += kCT) {
-      const int hh = i / d, e = i - hh * d;
-      qs[i] = rope1(qraw + hh * d, e, d, cst, snt);
+    __syncthreads();
+    // NeoX rotation in place, one (lane i, lane i + d/2) pair per thread,
+    // y0 = x0*c - x1*s, y1 = x1*c + x0*s (crates/tensor_core/src/rope.rs:145-184)
+    const int npair = (G + (has_new ? 1 : 0)) * half;
+    for (int i = threadIdx.x; i < npair; i += kT) {
+      const int hh = i / half, p = i - hh * half;
+      float* x = hh < G ? S.qs + hh * d : S.knew;
+      const float x0 = x[p], x1 = x[p + half];
+      const float c = S.cs[p], sv = S.sn[p];
+      x[p] = __fsub_rn(__fmul_rn(x0, c), __fmul_rn(x1, sv));
+      x[p + half] = __fadd_rn(__fmul_rn(x1, c), __fmul_rn(x0, sv));
     }
+    __syncthreads();
     if (has_new) {
-      for (int e = threadIdx.x; e < d; e += kCT) {
-        const KT kq = kv_round<KT>(rope1(kraw, e, d, cst, snt));
-        const KT vq = kv_round<KT>(vraw[e]);
-        knew[e] = (float)kq;
-        vnew[e] = (float)vq;
+      for (int e = threadIdx.x; e < d; e += kT) {
+        const KT kq = kv_round<KT>(S.knew[e]);
+        const KT vq = kv_round<KT>(S.vnew[e]);
         kc[(size_t)pos * d + e] = kq;  // KvCache::store for this position
         vc[(size_t)pos * d + e] = vq;
+        S.knew[e] = (float)kq;
+        S.vnew[e] = (float)vq;
       }
     }
   }
-  constexpr int kMaxOut = kMaxG * 256 / kCT;
+  constexpr int kMaxOut = kMaxG * 256 / kT;
   float acc[kMaxOut];
 #pragma unroll
   for (int i = 0; i < kMaxOut; ++i) acc[i] = 0.0f;
   float m_run = -INFINITY, l_run = 0.0f;
   for (int t0 = kb; t0 < ke; t0 += kTile) {
     const int nk = min(kTile, ke - t0);
-    named_sync(2, kCT);
-    const int qpr = d >> 2, nqd = nk * qpr;
-    constexpr int kQ = kTile * 64 / kCT;
-    float4 kq[kQ], vq[kQ];
-#pragma unroll
-    for (int j = 0; j < kQ; ++j) {
-      const int i = threadIdx.x + kCT * j;
-      if (i < nqd) {
-        const int tt = i / qpr, e = (i - tt * qpr) * 4;
-        const int t = t0 + tt;
-        if (!(has_new && t == pos)) {
-          kq[j] = kvl4<KT>(kc + (size_t)t * d + e);
-          vq[j] = kvl4<KT>(vc + (size_t)t * d + e);
-        }
-      }
+    if (t0 != kb) {  // later tiles (the first was preloaded)
+      __syncthreads();
+      tile_issue<KT>(kc, vc, d, t0, nk, has_new ? pos : -1, S.ks, S.vs, S.raw);
+      tile_finish<KT>(d, t0, nk, has_new ? pos : -1, S.ks, S.vs, S.raw);
     }
-#pragma unroll
-    for (int j = 0; j < kQ; ++j) {
-      const int i = threadIdx.x + kCT * j;
-      if (i < nqd) {
-        const int tt = i / qpr, e = (i - tt * qpr) * 4;
-        if (has_new && t0 + tt == pos) {
-          kq[j] = make_float4(knew[e], knew[e + 1], knew[e + 2], knew[e + 3]);
-          vq[j] = make_float4(vnew[e], vnew[e + 1], vnew[e + 2], vnew[e + 3]);
-        }
-        *reinterpret_cast<float4*>(ks + tt * ds + e) = kq[j];
-        *reinterpret_cast<float4*>(vs + tt * ds + e) = vq[j];
+    __syncthreads();
+    if (has_new && pos >= t0 && pos < t0 + nk) {
+      const int tt = pos - t0;
+      for (int e = threadIdx.x; e < d; e += kT) {
+        S.ks[tt * ds + e] = S.knew[e];
+        S.vs[tt * ds + e] = S.vnew[e];
       }
+      __syncthreads();
     }
-    named_sync(2, kCT);
-    for (int i = threadIdx.x; i < G * kTile; i += kCT) {
-      const int hh = i / kTile, tt = i - hh * kTile;
-      float sc = -INFINITY;
+    // scores: two threads per (head, key), halves of d summed by a shuffle
+    for (int i = threadIdx.x; i < 2 * G * kTile; i += kT) {
+      const int hk = i >> 1, part = i & 1;
+      const int hh = hk / kTile, tt = hk - hh * kTile;
+      float dot = 0.0f;
       if (tt < nk) {
-        const float* qh = qs + hh * d;
-        const float* kr = ks + tt * ds;
-        float dot = 0.0f;
-        for (int e = 0; e < d; e += 4) {
+        const float* qh = S.qs + hh * d + part * half;
+        const float* kr = S.ks + tt * ds + part * half;
+        for (int e = 0; e < half; e += 4) {
           const float4 qv = *reinterpret_cast<const float4*>(qh + e);
           const float4 kv = *reinterpret_cast<const float4*>(kr + e);
           dot = fmaf(qv.x, kv.x, dot);
@@ -390,31 +660,31 @@ __device__ __noinline__ void attention_task(const MegaArgs& a, int layer, int g,
           dot = fmaf(qv.z, kv.z, dot);
           dot = fmaf(qv.w, kv.w, dot);
         }
-        sc = __fmul_rn(dot, a.scale);
       }
-      ps[hh * kTile + tt] = sc;
+      dot += __shfl_xor_sync(0xffffffffu, dot, 1);
+      if (part == 0) S.ps[hh * kTile + tt] = tt < nk ? __fmul_rn(dot, a.scale) : -INFINITY;
     }
-    named_sync(2, kCT);
+    __syncthreads();
     if (warp < G) {
-      const float sc = ps[warp * kTile + lane];
+      const float sc = S.ps[warp * kTile + lane];
       const float mt = warp_max(sc);
       const float mn = fmaxf(m_run, mt);
       const float cf = expf(m_run - mn);
-      const float p = lane < nk ? expf(sc - mn) : 0.0f;
-      l_run = fmaf(l_run, cf, warp_sum(p));
+      const float pr = lane < nk ? expf(sc - mn) : 0.0f;
+      l_run = fmaf(l_run, cf, warp_sum(pr));
       m_run = mn;
-      ps[warp * kTile + lane] = p;
-      if (lane == 0) corr[warp] = cf;
+      S.ps[warp * kTile + lane] = pr;
+      if (lane == 0) S.corr[warp] = cf;
     }
-    named_sync(2, kCT);
+    __syncthreads();
 #pragma unroll
     for (int i = 0; i < kMaxOut; ++i) {
-      const int o = threadIdx.x + kCT * i;
+      const int o = threadIdx.x + kT * i;
       if (o < G * d) {
         const int hh = o / d, e = o - hh * d;
-        const float* ph = ps + hh * kTile;
-        float v = acc[i] * corr[hh];
-        for (int tt = 0; tt < nk; ++tt) v = fmaf(ph[tt], vs[tt * ds + e], v);
+        const float* ph = S.ps + hh * kTile;
+        float v = acc[i] * S.corr[hh];
+        for (int tt = 0; tt < nk; ++tt) v = fmaf(ph[tt], S.vs[tt * ds + e], v);
         acc[i] = v;
       }
     }
@@ -422,266 +692,93 @@ __device__ __noinline__ void attention_task(const MegaArgs& a, int layer, int g,
   const size_t pbase = ((size_t)g * a.nsplit + s) * G;
 #pragma unroll
   for (int i = 0; i < kMaxOut; ++i) {
-    const int o = threadIdx.x + kCT * i;
+    const int o = threadIdx.x + kT * i;
     if (o < G * d) __stcg(a.part_o + pbase * d + o, acc[i]);
   }
   if (warp < G && lane == 0) {
     __stcg(a.part_m + pbase + warp, m_run);
     __stcg(a.part_l + pbase + warp, l_run);
   }
-  __threadfence();
-  named_sync(2, kCT);
-  if (threadIdx.x == 0) *flag = atomicAdd(a.attn_cnt + g, 1u) == (unsigned)(a.nsplit - 1);
-  named_sync(2, kCT);
-  if (!*flag) return;
-  __threadfence();
-  float* fs = sm;
-  float* ls = sm + a.nsplit * G;
-  float* Ls = ls + a.nsplit * G;
-  const size_t gbase = (size_t)g * a.nsplit * G;
-  for (int i = threadIdx.x; i < a.nsplit * G; i += kCT) {
-    fs[i] = __ldcg(a.part_m + gbase + i);
-    ls[i] = __ldcg(a.part_l + gbase + i);
-  }
-  named_sync(2, kCT);
-  if (threadIdx.x < G) {
-    const int hh = threadIdx.x;
-    float M = -INFINITY;
-    for (int q = 0; q < a.nsplit; ++q) M = fmaxf(M, fs[q * G + hh]);
-    float L = 0.0f;
-    for (int q = 0; q < a.nsplit; ++q) {
-      const float mq = fs[q * G + hh];
-      const float f = mq == -INFINITY ? 0.0f : expf(mq - M);
-      fs[q * G + hh] = f;
-      L = fmaf(ls[q * G + hh], f, L);
+}
+
+// The attention phase: tasks (KV head g, split s) on blocks [0, Hkv*nsplit).
+// With many splits, the last task of a head group (by arrival) merges the
+// group's partials into a.attn; otherwise the o_proj staging merges.
+template <typename KT>
+MYOS_DEV void attn_phase(const MegaArgs& a, int p, int pos, float* sm, int* flag) {
+  const int l = p / 5, T = a.Hkv * a.nsplit;
+  uint64_t* tr = a.trace ? a.trace + ((size_t)blockIdx.x * (5 * a.L + 1) + p) * 4 : nullptr;
+  const bool task = (int)blockIdx.x < T;
+  const int g = (int)blockIdx.x / a.nsplit, s = (int)blockIdx.x % a.nsplit;
+  const int kb = s * a.chunk, ke = min(kb + a.chunk, pos + 1);
+  const AttnSmem S = attn_smem(sm, a.G, a.d);
+  if (task && kb < ke) {  // inputs that do not depend on this step: before the wait
+    tile_issue<KT>(kv_base<KT>(a, a.kcache, l, g), kv_base<KT>(a, a.vcache, l, g), a.d, kb,
+                   min(kTile, ke - kb), pos, S.ks, S.vs, S.raw);
+    const int half4 = a.d >> 3;  // rotation table row: d/2 floats each
+    const float4* c4 = reinterpret_cast<const float4*>(a.cos_t + (size_t)pos * (a.d >> 1));
+    const float4* s4 = reinterpret_cast<const float4*>(a.sin_t + (size_t)pos * (a.d >> 1));
+    for (int i = threadIdx.x; i < half4; i += kT) {
+      cpa16(reinterpret_cast<float4*>(S.cs) + i, c4 + i);
+      cpa16(reinterpret_cast<float4*>(S.sn) + i, s4 + i);
     }
-    Ls[hh] = L;
+    tile_finish<KT>(a.d, kb, min(kTile, ke - kb), pos, S.ks, S.vs, S.raw);
   }
-  named_sync(2, kCT);
-  for (int o = threadIdx.x; o < G * d; o += kCT) {
-    const int hh = o / d;
-    float O = 0.0f;
-    int q = 0;
-    for (; q + 8 <= a.nsplit; q += 8) {
-      float po[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) po[u] = __ldcg(a.part_o + (gbase + (size_t)(q + u) * G) * d + o);
-#pragma unroll
-      for (int u = 0; u < 8; ++u) O = fmaf(po[u], fs[(q + u) * G + hh], O);
+  phase_wait(&a.bar[p - 1], gridDim.x, &a.ctl->err);
+  if (tr && threadIdx.x == 0) tr[0] = tr[1] = global_ns();
+  if (task) {
+    if (kb < ke) {
+      attention_task<KT>(a, l, g, s, pos, sm);
+    } else {  // empty split: neutral partial
+      const size_t pbase = ((size_t)g * a.nsplit + s) * a.G;
+      for (int i = threadIdx.x; i < a.G * a.d; i += kT) __stcg(a.part_o + pbase * a.d + i, 0.0f);
+      if (threadIdx.x < a.G) {
+        __stcg(a.part_m + pbase + threadIdx.x, -INFINITY);
+        __stcg(a.part_l + pbase + threadIdx.x, 0.0f);
+      }
     }
-    for (; q < a.nsplit; ++q) O = fmaf(__ldcg(a.part_o + (gbase + (size_t)q * G) * d + o), fs[q * G + hh], O);
-    __stcg(a.attn + (size_t)g * G * d + o, __fdiv_rn(O, Ls[hh]));
+    if (!a.merge_in_stage) {
+      __threadfence();
+      __syncthreads();
+      if (threadIdx.x == 0) *flag = atomicAdd(a.attn_cnt + g, 1u) == (unsigned)(a.nsplit - 1);
+      __syncthreads();
+      if (*flag) {
+        __threadfence();
+        merge_group(a, g, sm, a.attn + (size_t)g * a.G * a.d);
+        if (threadIdx.x == 0) a.attn_cnt[g] = 0u;
+      }
+    }
   }
-  if (threadIdx.x == 0) a.attn_cnt[g] = 0u;
-  named_sync(2, kCT);
+  if (tr && threadIdx.x == 0) tr[2] = global_ns();
 }
 
 // ---------------------------------------------------------------- the kernel
 template <typename KT>
-__global__ void __launch_bounds__(kStepThreads, 1) k_step(MegaArgs a) {
+__global__ void __launch_bounds__(kT, 1) k_step(MegaArgs a) {
   extern __shared__ float4 smem4[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>(smem4);
+  float* sm = reinterpret_cast<float*>(smem4);  // staged input, or attention tiles
   __shared__ float red[33];
-  __shared__ float wbv[kCW];
-  __shared__ uint32_t wbi[kCW];
+  __shared__ float wbv[kW];
+  __shared__ uint32_t wbi[kW];
   __shared__ int flag;
-
-  float* scratch = reinterpret_cast<float*>(smem);  // staged x, or attention scratch
-  uint8_t* ring = smem + a.scratch_bytes;
-  float* part = reinterpret_cast<float*>(ring + (size_t)a.nslot * a.slot_bytes);  // [2][2][8]
-  uint64_t* full = reinterpret_cast<uint64_t*>(part + 2 * 2 * kCW);
-  uint64_t* empty = full + a.nslot;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int nslot = a.nslot;
-  uint32_t* err = &a.ctl->err;
-
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < nslot; ++i) {
-      mbar_init(&full[i], 1);
-      mbar_init(&empty[i], kCW);
-    }
-    mbar_fence_init();
-  }
-  __syncthreads();
-  const int nphase = 5 * a.L + (a.head ? 1 : 0);
-
-  if (warp == kCW) {
-    // ------------------------------------------------ producer
-    if (lane == 0) {
-      // A second cursor runs `lookahead` stages ahead of the ring and pulls
-      // those rows into L2, so each bulk copy is served from L2.
-      int pp = 0, prow = 0, pr1 = 0;
-      PhaseW pw = {};
-      bool pvalid = false;
-      auto pnext = [&]() {
-        if (pvalid) {
-          prow += pw.rs;
-          if (prow < pr1) return;
-          ++pp;
-        }
-        pvalid = false;
-        for (; pp < nphase; ++pp) {
-          const int kind = pp < 5 * a.L ? pp % 5 : PH_HEAD;
-          if (kind == PH_ATTN) continue;
-          pw = phase_w(a, kind, pp / 5);
-          block_rows(pw.M, &prow, &pr1);
-          if (prow < pr1) {
-            pvalid = true;
-            return;
-          }
-        }
-      };
-      auto pissue = [&]() {
-        if (!pvalid) return;
-        const uint32_t n = (uint32_t)min(pw.rs, pr1 - prow);
-        const uint32_t bytes = n * (uint32_t)pw.K * 2u;
-        prefetch_l2(pw.w0 + (size_t)prow * pw.K, bytes);
-        if (pw.NR > 1) prefetch_l2(pw.w1 + (size_t)prow * pw.K, bytes);
-        pnext();
-      };
-      pnext();
-      for (int i = 0; i < a.lookahead; ++i) pissue();
-      uint32_t seq = 0;
-      for (int p = 0; p < nphase; ++p) {
-        const int kind = p < 5 * a.L ? p % 5 : PH_HEAD;
-        if (kind == PH_ATTN) continue;
-        const PhaseW w = phase_w(a, kind, p / 5);
-        int r0, r1;
-        block_rows(w.M, &r0, &r1);
-        const size_t row_bytes = (size_t)w.K * 2;
-        if (a.trace) a.trace[((size_t)blockIdx.x * nphase + p) * 4 + 3] = global_ns();
-        for (int row0 = r0; row0 < r1; row0 += w.rs, ++seq) {
-          const int slot = (int)(seq % nslot);
-          if (seq >= (uint32_t)nslot) ring_wait(&empty[slot], ((seq / nslot) - 1) & 1u, err, kErrWaitEmpty);
-          const int n = min(w.rs, r1 - row0);
-          const uint32_t bytes = (uint32_t)(n * row_bytes);
-          mbar_arrive_expect_tx(&full[slot], w.NR * bytes);
-          uint8_t* dst = ring + (size_t)slot * a.slot_bytes;
-          bulk_g2s(dst, w.w0 + (size_t)row0 * w.K, bytes, &full[slot]);
-          if (w.NR > 1)
-            bulk_g2s(dst + (size_t)w.rs * row_bytes, w.w1 + (size_t)row0 * w.K, bytes, &full[slot]);
-          pissue();
-        }
-      }
-    }
-    return;
-  }
-
-  // -------------------------------------------------- consumers (256 threads)
   const uint32_t pos = a.ctl->pos;
   const uint32_t step = a.ctl->step;
   const uint32_t tok = a.feed ? a.feed[step] : a.ctl->argmax;
   const uint32_t G = gridDim.x;
-  float bv = -INFINITY;
-  uint32_t bi = 0xffffffffu;
-  uint32_t seq = 0;
+  const int nphase = 5 * a.L + (a.head ? 1 : 0);
+  int pf_next = 0;
+
   for (int p = 0; p < nphase; ++p) {
     const int kind = p < 5 * a.L ? p % 5 : PH_HEAD;
-    const int l = p / 5;
-    if (p > 0) phase_wait(&a.bar[p - 1], G, err);
-    uint64_t* tr = a.trace ? a.trace + ((size_t)blockIdx.x * nphase + p) * 4 : nullptr;
-    if (tr && threadIdx.x == 0) tr[0] = global_ns();
-    if (kind == PH_ATTN) {
-      const int T = a.Hkv * a.nsplit;
-      if ((int)blockIdx.x < T)
-        attention_task<KT>(a, l, (int)blockIdx.x / a.nsplit, (int)blockIdx.x % a.nsplit, (int)pos,
-                           scratch, &flag);
-      if (tr && threadIdx.x == 0) tr[1] = tr[2] = global_ns();
-      phase_arrive(&a.bar[p]);
-      continue;
-    }
-    const PhaseW w = phase_w(a, kind, l);
-    const MegaLayer* Ly = kind == PH_HEAD ? nullptr : &a.layers[l];
-    // stage the phase input
-    if (kind == PH_QKV) {
-      const bool emb = l == 0;
-      stage_c(scratch, w.K, emb ? nullptr : a.resid, emb ? a.embed + (size_t)tok * a.H : nullptr,
-              Ly->ln1, a.eps, (emb && blockIdx.x == 0) ? a.resid : nullptr, red);
-    } else if (kind == PH_O) {
-      stage_c(scratch, w.K, a.attn, nullptr, nullptr, 0.0f, nullptr, red);
-    } else if (kind == PH_GU) {
-      stage_c(scratch, w.K, a.resid, nullptr, Ly->ln2, a.eps, nullptr, red);
-    } else if (kind == PH_DOWN) {
-      stage_c(scratch, w.K, a.act, nullptr, nullptr, 0.0f, nullptr, red);
-    } else {
-      stage_c(scratch, w.K, a.resid, nullptr, a.final_norm, a.eps, nullptr, red);
-    }
-    if (tr && threadIdx.x == 0) tr[1] = global_ns();
-    const float4* xlo = reinterpret_cast<const float4*>(scratch);
-    const float4* xhi = reinterpret_cast<const float4*>(scratch + (w.K >> 1));
-    int r0, r1;
-    block_rows(w.M, &r0, &r1);
-    const size_t row_bytes = (size_t)w.K * 2;
-    const int spl = kCW / w.rs;
-    const int rr = warp / spl, cs = warp - rr * spl;
-    const int cps = (w.K >> 3) / spl, c0 = cs * cps;
-    for (int row0 = r0; row0 < r1; row0 += w.rs, ++seq) {
-      const int slot = (int)(seq % nslot);
-      ring_wait(&full[slot], (seq / nslot) & 1u, err, kErrWaitFull);
-      const int n = min(w.rs, r1 - row0);
-      float acc0 = 0.0f, acc1 = 0.0f;
-      if (rr < n) {
-        const uint8_t* base = ring + (size_t)slot * a.slot_bytes + (size_t)rr * row_bytes;
-        if (w.NR == 1) {
-#pragma unroll 4
-          for (int c = c0 + lane; c < c0 + cps; c += 32) {
-            const uint4 u = *reinterpret_cast<const uint4*>(base + (size_t)c * 16);
-            acc0 = dot8s(u, xlo[c], xhi[c], acc0);
-          }
-        } else {
-          const uint8_t* base1 = base + (size_t)w.rs * row_bytes;
-#pragma unroll 4
-          for (int c = c0 + lane; c < c0 + cps; c += 32) {
-            const float4 lo = xlo[c], hi = xhi[c];
-            acc0 = dot8s(*reinterpret_cast<const uint4*>(base + (size_t)c * 16), lo, hi, acc0);
-            acc1 = dot8s(*reinterpret_cast<const uint4*>(base1 + (size_t)c * 16), lo, hi, acc1);
-          }
-        }
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[slot]);
-      acc0 = warp_sum(acc0);
-      if (w.NR > 1) acc1 = warp_sum(acc1);
-      int row = -1;
-      if (spl == 1) {
-        if (rr < n) row = row0 + rr;
-      } else {
-        float* pp = part + (seq & 1) * 2 * kCW;
-        if (lane == 0) {
-          pp[warp] = acc0;
-          pp[kCW + warp] = acc1;
-        }
-        named_sync(3, kCT);
-        if (cs == 0 && rr < n) {
-          row = row0 + rr;
-          acc0 = 0.0f;
-          acc1 = 0.0f;
-          for (int q = 0; q < spl; ++q) {
-            acc0 += pp[rr * spl + q];
-            acc1 += pp[kCW + rr * spl + q];
-          }
-        }
-      }
-      if (row >= 0) {
-        if (kind == PH_HEAD && better(acc0, (uint32_t)row, bv, bi)) {
-          bv = acc0;
-          bi = (uint32_t)row;
-        }
-        if (lane == 0) {
-          if (kind == PH_QKV) __stcg(a.qkv + row, __fadd_rn(acc0, __ldg(Ly->bqkv + row)));
-          else if (kind == PH_O || kind == PH_DOWN)
-            __stcg(a.resid + row, __fadd_rn(__ldcg(a.resid + row), acc0));
-          else if (kind == PH_GU) __stcg(a.act + row, silu_mul(acc0, acc1));
-          else __stcg(a.logits + row, acc0);
-        }
-      }
-    }
-    if (tr && threadIdx.x == 0) tr[2] = global_ns();
+    for (; pf_next <= p + a.lookahead && pf_next < nphase; ++pf_next)
+      if (pf_next > p) prefetch_phase(a, pf_next);
+    if (kind == PH_ATTN) attn_phase<KT>(a, p, (int)pos, sm, &flag);
+    else gemv_phase(a, p, kind, tok, sm, red, wbv, wbi);
     if (kind != PH_HEAD) {
-      const uint32_t prev = phase_arrive(&a.bar[p]);
-      // Step without a head: the last block through the final phase advances
-      // the cursor (every block has read the step control by then).
+      const uint32_t prev = phase_arrive(&a.bar[p]);  // includes a block barrier
       if (!a.head && p == nphase - 1 && threadIdx.x == 0 && prev == G - 1) {
+        // Step without a head: the last block through the final phase
+        // advances the cursor; every block has read the step control.
         a.ctl->pos = pos + 1;
         a.ctl->step = step + 1;
       }
@@ -689,15 +786,11 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(MegaArgs a) {
   }
   if (!a.head) return;
   // ---------------------------------------------------- argmax finalize
-  if (lane == 0) {
-    wbv[warp] = bv;
-    wbi[warp] = bi;
-  }
-  named_sync(1, kCT);
+  __syncthreads();
   if (threadIdx.x == 0) {
     float v = -INFINITY;
     uint32_t i = 0xffffffffu;
-    for (int q = 0; q < kCW; ++q)
+    for (int q = 0; q < kW; ++q)
       if (better(wbv[q], wbi[q], v, i)) {
         v = wbv[q];
         i = wbi[q];
@@ -705,8 +798,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(MegaArgs a) {
     __stcg(a.part_val + blockIdx.x, v);
     __stcg(a.part_idx + blockIdx.x, i);
     __threadfence();
-    const bool last = atomicAdd(a.head_cnt, 1u) == G - 1;
-    if (last) {
+    if (atomicAdd(a.head_cnt, 1u) == G - 1) {
       __threadfence();
       v = -INFINITY;
       i = 0xffffffffu;
@@ -730,40 +822,38 @@ __global__ void __launch_bounds__(kStepThreads, 1) k_step(MegaArgs a) {
 
 }  // namespace
 
-bool mega_supported(int H, int I, int qd, int kvd, int d, int G, int slot_bytes) {
+bool mega_supported(int H, int I, int qd, int kvd, int d, int G) {
+  (void)kvd;
   if (H % 256 || I % 256 || qd % 256) return false;
-  if (d % 4 || d > 256 || G > kMaxG) return false;
-  // a whole row of every matrix must fit one ring slot
-  const int kmax = H > I ? (H > qd ? H : qd) : (I > qd ? I : qd);
-  return kmax * 2 <= slot_bytes && 2 * H * 2 <= slot_bytes;
+  if (d % 8 || d > 256 || G > kMaxG || qd / d > kT) return false;
+  return true;
 }
 
-size_t mega_scratch_bytes(int H, int I, int qd, int d, int G) {
-  size_t x = (size_t)(H > I ? (H > qd ? H : qd) : (I > qd ? I : qd)) * 4;
-  size_t at = (size_t)(G * d + 2 * kTile * (d + 4) + G * kTile + kMaxG + 2 * d) * 4;
-  size_t s = x > at ? x : at;
-  return (s + 127) / 128 * 128;
-}
-
-int mega_threads() { return kStepThreads; }
+int mega_threads() { return kT; }
 
 cudaError_t mega_configure(MegaArgs* a, int max_smem) {
-  // ring slots as large as the biggest stage, as many as fit
-  const size_t fixed = a->scratch_bytes + 2 * 2 * kCW * 4 + 16;
-  int n = (int)((max_smem - fixed) / (a->slot_bytes + 16));
-  if (n > 16) n = 16;
-  if (n < 2) return cudaErrorInvalidValue;
-  a->nslot = n;
-  return cudaSuccess;
+  const int kmax = a->H > a->I ? (a->H > a->qd ? a->H : a->qd) : (a->I > a->qd ? a->I : a->qd);
+  a->x_floats = (kmax + 31) / 32 * 32;
+  const int T = a->Hkv * a->nsplit, Tg = T * a->G;
+  const size_t norm_area = (size_t)a->H + a->H / 2;            // gamma, raw embedding row
+  const size_t merge_area = (size_t)Tg * a->d + 2 * Tg + a->Hq;  // partials, factors, sums
+  const size_t tiles = (size_t)a->G * a->d + 2 * kTile * (a->d + 4) + a->G * kTile + kMaxG +
+                       3 * a->d + 2 * kTile * a->d / 2;  // + raw bf16 rows
+  const size_t mgroup = 2 * (size_t)a->nsplit * a->G + a->G;
+  const size_t attn = tiles > mgroup ? tiles : mgroup;
+  auto bytes = [&](size_t second) {
+    const size_t x = (size_t)a->x_floats + second;
+    return ((x > attn ? x : attn) * 4 + 127) / 128 * 128;
+  };
+  const size_t with_merge = bytes(norm_area > merge_area ? norm_area : merge_area);
+  a->merge_in_stage = T <= kCombineMax && with_merge <= (size_t)max_smem;
+  a->scratch_bytes = a->merge_in_stage ? with_merge : bytes(norm_area);
+  return a->scratch_bytes <= (size_t)max_smem ? cudaSuccess : cudaErrorInvalidValue;
 }
 
-size_t mega_smem_bytes(const MegaArgs& a) {
-  return a.scratch_bytes + (size_t)a.nslot * a.slot_bytes + 2 * 2 * kCW * 4 + 16 * (size_t)a.nslot + 16;
-}
+size_t mega_smem_bytes(const MegaArgs& a) { return a.scratch_bytes; }
 
 cudaError_t launch_step_mega(const MegaArgs& a, cudaStream_t st) {
-  // Raise the dynamic shared-memory limit to exactly what this launch uses
-  // (once per device and size).
   static int configured_dev = -1;
   static size_t configured_smem = 0;
   const size_t smem = mega_smem_bytes(a);
@@ -783,7 +873,7 @@ cudaError_t launch_step_mega(const MegaArgs& a, cudaStream_t st) {
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(a.grid);
-  cfg.blockDim = dim3(kStepThreads);
+  cfg.blockDim = dim3(kT);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];

@@ -1,4 +1,5 @@
-// Persistent one-launch-per-token step kernel (see step_kernel.cu).
+// Persistent one-launch-per-token step kernel (kernel and design notes in
+// step_kernel.cu).
 #pragma once
 #include <cuda_runtime.h>
 #include <stddef.h>
@@ -41,16 +42,20 @@ struct MegaArgs {
   uint32_t* part_idx;
   int head;                 // 1: final norm + head + argmax, else only advance
   int grid;
-  size_t scratch_bytes;
-  int slot_bytes;
-  int nslot;
+  size_t scratch_bytes;     // dynamic shared memory of the launch
+  int x_floats;             // staged-input region; gamma / embedding / merge area follows
+  int merge_in_stage;       // 1: o_proj staging merges the attention splits
   uint64_t* trace;          // optional [grid][nphase][4] global-timer stamps
-  int lookahead;            // stages the producer prefetches into L2 ahead of the ring
+  int lookahead;            // phases whose weight slices are prefetched into L2 ahead
+  int pf_kb;                // cap of one block's prefetch per phase, KiB
+  int pf_mode;              // 0: bulk prefetch (TMA engine), 1: per-line prefetch
 };
 
-bool mega_supported(int H, int I, int qd, int kvd, int d, int G, int slot_bytes);
-size_t mega_scratch_bytes(int H, int I, int qd, int d, int G);
+bool mega_supported(int H, int I, int qd, int kvd, int d, int G);
 int mega_threads();
+// Shared-memory layout from the shape fields of *a (H, I, qd, Hq, Hkv, d, G,
+// nsplit): fills scratch_bytes, x_floats and merge_in_stage; fails when the
+// layout exceeds max_smem.
 cudaError_t mega_configure(MegaArgs* a, int max_smem);
 size_t mega_smem_bytes(const MegaArgs& a);
 cudaError_t launch_step_mega(const MegaArgs& a, cudaStream_t st);

@@ -9,6 +9,7 @@ crates/runtime/src/meter.rs:48-78), with prefill tok/s and the HBM
 roofline fraction beside it.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                  [--n-prompt P --n-gen G]   (smaller cases for profiler captures)
 
 N>1 runs one independent S1 replica per GPU (the path has no exchange
 step: independent sequences, weak scaling), timed as the max over ranks.
@@ -132,7 +133,7 @@ def max_over_ranks(pg, value: float, local: int) -> float:
 
 
 # ---------------------------------------------------------------- CPU baseline
-def cpu_decode_sample(shape, table, prompt, n_decode: int, threads: int):
+def cpu_decode_sample(shape, table, prompt, n_decode: int, threads: int, max_seq: int):
     """Reference --threads path (oracle restatement): prefill + n_decode greedy."""
     from oracle import oracle as orc
     sys.path.insert(0, os.path.join(REPO, "tests"))
@@ -141,7 +142,7 @@ def cpu_decode_sample(shape, table, prompt, n_decode: int, threads: int):
     orc.build()
     orc.set_threads(threads)
     wm = rf.load_into_oracle(orc, table)
-    md = orc.Model(rf.oracle_shape(orc, shape), N_PROMPT + N_GEN)
+    md = orc.Model(rf.oracle_shape(orc, shape), max_seq)
     t0 = time.perf_counter()
     assert md.prefill(wm, prompt) == 0
     t1 = time.perf_counter()
@@ -170,8 +171,9 @@ def run_reference(args, world, rank):
     prompt = synth.prompt_ids(SEED, N_PROMPT, shape["vocab"])
     n_dec = args.ref_decode
     for _ in range(args.warmup):
-        cpu_decode_sample(shape, table, prompt, 1, threads)
-    samples = [cpu_decode_sample(shape, table, prompt, n_dec, threads) for _ in range(args.steps)]
+        cpu_decode_sample(shape, table, prompt, 1, threads, N_PROMPT + N_GEN)
+    samples = [cpu_decode_sample(shape, table, prompt, n_dec, threads, N_PROMPT + N_GEN)
+               for _ in range(args.steps)]
     t_dec = sum(s["t_decode"] for s in samples)
     t_pre = sum(s["t_prefill"] for s in samples)
     value = n_dec * len(samples) / t_dec
@@ -209,15 +211,16 @@ def run_ours(args, world, rank, local, pg):
     shape = synth.shape_qwen25_1_5b()
     threads = max(1, host_threads() // max(world, 1))
     table = synth.weights(shape, SEED, threads=threads)
-    prompt = synth.prompt_ids(SEED, N_PROMPT, shape["vocab"])
-    eng = myos.Engine(shape, N_PROMPT + N_GEN, device=local, kv_dtype=args.kv)
+    n_prompt, n_gen = args.n_prompt, args.n_gen
+    prompt = synth.prompt_ids(SEED, n_prompt, shape["vocab"])
+    eng = myos.Engine(shape, n_prompt + n_gen, device=local, kv_dtype=args.kv)
     eng.load_table(table)
 
     def one_step():
         eng.reset()
         eng.prefill(prompt, want_logits=False)
         p_ms, _ = eng.last_timing()
-        ids = eng.greedy_decode(N_GEN)
+        ids = eng.greedy_decode(n_gen)
         _, d_ms = eng.last_timing()
         return p_ms, d_ms, ids
 
@@ -237,8 +240,8 @@ def run_ours(args, world, rank, local, pg):
     barrier(pg)
     tot_dec = max_over_ranks(pg, sum(dec_ms), local)
     tot_pre = max_over_ranks(pg, sum(pre_ms), local)
-    value = world * N_GEN * args.steps / (tot_dec / 1000.0)
-    prefill_tps = world * N_PROMPT * args.steps / (tot_pre / 1000.0)
+    value = world * n_gen * args.steps / (tot_dec / 1000.0)
+    prefill_tps = world * n_prompt * args.steps / (tot_pre / 1000.0)
 
     # end to end through the C ABI with host buffers: prompt ids in, ids out
     barrier(pg)
@@ -246,9 +249,9 @@ def run_ours(args, world, rank, local, pg):
     for _ in range(args.steps):
         eng.reset()
         eng.prefill(prompt, want_logits=False)
-        eng.greedy_decode(N_GEN)
+        eng.greedy_decode(n_gen)
     wall = max_over_ranks(pg, time.perf_counter() - t0, local)
-    e2e = world * N_GEN * args.steps / wall
+    e2e = world * n_gen * args.steps / wall
 
     # dominant kernel (gate/up GEMV: ~60% of the weight bytes) timed alone
     eng.reset()
@@ -262,17 +265,17 @@ def run_ours(args, world, rank, local, pg):
     if os.path.exists(tp):
         traffic = json.load(open(tp)).get("gate_up_bytes_per_launch")
     step_bytes = synth.weight_bytes(shape)
-    step_gbs = step_bytes * N_GEN * args.steps / (sum(dec_ms) / 1000.0) / 1e9
+    step_gbs = step_bytes * n_gen * args.steps / (sum(dec_ms) / 1000.0) / 1e9
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         t = host_threads()
-        smp = cpu_decode_sample(shape, table, prompt, args.cpu_decode, t)
+        smp = cpu_decode_sample(shape, table, prompt, args.cpu_decode, t, n_prompt + n_gen)
         cpu = {"value": round(args.cpu_decode / smp["t_decode"], 4), "unit": "tok/s", "cores": t,
                "kind": "port",
-               "sample": f"prefill {N_PROMPT} ids + {args.cpu_decode} greedy steps of S1 on the "
+               "sample": f"prefill {n_prompt} ids + {args.cpu_decode} greedy steps of S1 on the "
                          f"reference's --threads path restated in C++ (oracle/), {t} threads",
-               "prefill_tok_s": round(N_PROMPT / smp["t_prefill"], 3),
+               "prefill_tok_s": round(n_prompt / smp["t_prefill"], 3),
                "ids_match_gpu_prefix": bool(np.array_equal(smp["ids"], ids[:args.cpu_decode]))}
 
     if rank == 0:
@@ -285,12 +288,13 @@ def run_ours(args, world, rank, local, pg):
             "vs_baseline": round(value / PUBLISHED_DECODE, 2),
             "dtype": "bf16 weights, f32 activations/accumulate",
             "data": "synthetic (seeded random-init Qwen2.5-1.5B BF16 weights, uniform prompt ids)",
-            "config": {"workload": "S1: Qwen2.5-1.5B, 128-id prompt + 128 greedy steps, batch 1",
+            "config": {"workload": f"S1: Qwen2.5-1.5B, {n_prompt}-id prompt + {n_gen} greedy "
+                                   f"steps, batch 1",
                        "seed": SEED, "kv_dtype": args.kv,
                        "parallelism": f"replicas x{world} (independent sequences)",
                        "l2": "each decode step streams 3.09 GB of weights (> 126 MB L2); no flush"},
             "prefill_tok_s": round(prefill_tps, 1),
-            "decode_ms_per_token": round(tot_dec / (args.steps * N_GEN), 4),
+            "decode_ms_per_token": round(tot_dec / (args.steps * n_gen), 4),
             "step_hbm": {"bytes_per_token": step_bytes, "achieved_gbs": round(step_gbs, 1),
                          "frac_of_measured": round(step_gbs / peak, 4),
                          "frac_of_8tbs_nominal": round(step_gbs / 8000.0, 4)},
@@ -302,11 +306,11 @@ def run_ours(args, world, rank, local, pg):
             "kernels": {k: {"ms": round(v[0], 5), "gbs": round(v[1] / (v[0] / 1000) / 1e9, 1)}
                         for k, v in prof.items()},
             "cpu_baseline": cpu,
-            "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": N_PROMPT * 4,
-                    "d2h_bytes_per_step": N_GEN * 4,
+            "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": n_prompt * 4,
+                    "d2h_bytes_per_step": n_gen * 4,
                     "note": "generated tokens / wall time of reset+prefill(host ids)+"
                             "greedy_decode(host ids) through the C ABI"},
-            "gpu_launches": launches_per_token * (N_PROMPT + N_GEN) * args.steps,
+            "gpu_launches": launches_per_token * (n_prompt + n_gen) * args.steps,
             "clocks": clk,
         }
         print(json.dumps(line))
@@ -324,6 +328,8 @@ def main():
     ap.add_argument("--cpu-decode", type=int, default=16)
     ap.add_argument("--ref-decode", type=int, default=8)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--n-prompt", type=int, default=N_PROMPT)
+    ap.add_argument("--n-gen", type=int, default=N_GEN)
     args = ap.parse_args()
     world, rank, local, pg = dist_setup(args) if args.impl == "ours" else (
         int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")), 0, None)
