@@ -25,7 +25,8 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",
                      "-Xcompiler", "-fvisibility=hidden", "-I" + INCLUDE,
                      "--expt-relaxed-constexpr"]
-CUDA_SOURCES = ["kernels.cu", "step_kernel.cu", "engine.cu", "ops.cu", "safetensors.cpp"]
+CUDA_SOURCES = ["kernels.cu", "step_kernel.cu", "engine.cu", "ops.cu", "noalloc.cu",
+                "safetensors.cpp"]
 HEADERS = ["common.cuh", "kernels.h", "safetensors.h", "step_kernel.h"]
 
 

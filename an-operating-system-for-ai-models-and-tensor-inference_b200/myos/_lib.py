@@ -18,12 +18,12 @@ OK = 0
 ERR_SHAPE, ERR_TOKEN, ERR_ROW_OOB, ERR_POSITION, ERR_CACHE_FULL, ERR_CACHE_RANGE = 1, 2, 3, 4, 5, 6
 ERR_WEIGHT_MISSING, ERR_WEIGHT_DTYPE, ERR_WEIGHT_SHAPE, ERR_WEIGHT_LENGTH = 7, 8, 9, 10
 ERR_DUPLICATE, ERR_EMPTY_NAME, ERR_PARSE, ERR_UNSUPPORTED, ERR_IO = 11, 12, 13, 14, 15
-ERR_CUDA, ERR_NCCL, ERR_TIMEOUT, ERR_ARG = 16, 17, 18, 19
+ERR_CUDA, ERR_NCCL, ERR_TIMEOUT, ERR_ARG, ERR_SCRATCH_LIMIT = 16, 17, 18, 19, 20
 STATUS_NAMES = {
     0: "Ok", 1: "Shape", 2: "Token", 3: "RowOutOfBounds", 4: "Position", 5: "CacheFull",
     6: "CacheRange", 7: "WeightMissing", 8: "WeightDType", 9: "WeightShape", 10: "WeightLength",
     11: "Duplicate", 12: "EmptyName", 13: "Parse", 14: "UnsupportedDType", 15: "Io", 16: "Cuda",
-    17: "Nccl", 18: "Timeout", 19: "Arg",
+    17: "Nccl", 18: "Timeout", 19: "Arg", 20: "ScratchLimit",
 }
 F32, F16, BF16 = 0, 1, 2
 KV_F32, KV_BF16 = 0, 1
@@ -95,6 +95,8 @@ SIGNATURES = {
     "myos_rope_f32": (C.c_int, [_f32p, sz, _f32p, sz, C.c_uint32, sz, C.c_float]),
     "myos_greedy_token": (C.c_int, [_f32p, sz, _u32p]),
     "myos_dev_gemv_bf16": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, sz, sz, C.c_void_p]),
+    "myos_dev_gqa_attn_f32_noalloc": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                                sz, sz, sz, sz, C.c_int32, sz, C.c_void_p]),
 }
 
 _lib = None

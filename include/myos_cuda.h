@@ -58,6 +58,8 @@ enum myos_status {
   MYOS_ERR_NCCL = 17,          /* collective failure (tensor-parallel contexts) */
   MYOS_ERR_TIMEOUT = 18,       /* a bounded device-side wait gave up */
   MYOS_ERR_ARG = 19,           /* null pointer or invalid option */
+  MYOS_ERR_SCRATCH_LIMIT = 20, /* request needs more than the fixed no-allocation scratch
+                                  (MYOS_NOALLOC_SCRATCH_BYTES); no reference counterpart */
 };
 
 /* Tensor storage tags, weight_loader::DType (crates/weight_loader/src/lib.rs:36-49). */
@@ -208,6 +210,32 @@ int myos_greedy_token(const float* logits, size_t n, uint32_t* out);
 /* y[m] (f32) = W[m,k] (bf16, row-major, 16-byte aligned rows when k%8==0) x[k] (f32). */
 int myos_dev_gemv_bf16(float* d_y, const void* d_w, const float* d_x, size_t m, size_t k,
                        void* stream);
+
+/* Size of the fixed device array that myos_dev_gqa_attn_f32_noalloc takes its
+ * scratch from (one per device). */
+#define MYOS_NOALLOC_SCRATCH_BYTES (2u << 20)
+
+/* No counterpart in the reference (its attention runs on the host). The same
+ * split-KV attention as myos_gqa_attn_f32 (tensor_core::gqa_attn_f32,
+ * crates/tensor_core/src/gqa.rs:174-218; same arguments and shape rules, same
+ * split geometry and so the same results) on caller-held device buffers
+ * y[hq*d], q[hq*d], k[hkv][seq][d], v[hkv][seq][d], for callers that must not
+ * allocate: code running while a device-memory budget is fixed (an allocator
+ * that owns all free HBM, a pool sized at start-up) or on a path that may not
+ * call cudaMalloc/cudaFree, which synchronize the device. It allocates
+ * nothing: the split partials and merge counters live in one static device
+ * array of MYOS_NOALLOC_SCRATCH_BYTES (2 MiB); a request needing more
+ * ((hkv*4 + hq*nsplit*(d+2)*4 bytes, each part rounded up to 256, with
+ * nsplit = min(64, ceil(keys/32))) returns MYOS_ERR_SCRATCH_LIMIT before any
+ * device work. The counters must be zero at kernel start; each call clears
+ * them on its stream first. The first call on a device resolves the array's
+ * address (cudaGetSymbolAddress); make that call before any stream capture.
+ * Calls share the array: calls that run concurrently (different streams or
+ * unordered threads) race and corrupt each other's results. stream may be 0;
+ * asynchronous (no sync). */
+int myos_dev_gqa_attn_f32_noalloc(float* d_y, const float* d_q, const float* d_k,
+                                  const float* d_v, size_t hq, size_t hkv, size_t d, size_t seq,
+                                  int32_t mask_kind, size_t query_pos, void* stream);
 
 /* Library version string and the build's target architecture. */
 const char* myos_version(void);
