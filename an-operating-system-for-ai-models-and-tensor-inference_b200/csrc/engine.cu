@@ -88,6 +88,7 @@ struct myos_ctx {
   // launch geometry
   int grid_qkv = 0, grid_o = 0, grid_gu = 0, grid_down = 0, grid_head = 0;
   int attn_chunk = 0, attn_nsplit = 0;
+  int defer_merge = 0;  // o_proj staging merges the attention splits
   size_t prefetch_total = 0;  // bulk L2 prefetch (MYOS_PREFETCH_MB); measured slower, off
   // loaded-tensor bookkeeping
   std::vector<uint8_t> have;  // per layer x suffix, then embed, final norm, lm_head
@@ -104,6 +105,9 @@ struct myos_ctx {
   unsigned* bar = nullptr;  // [5L] phase counters + attention + head counters
   uint64_t* trace = nullptr;  // MYOS_TRACE_FILE: per-phase timer stamps of the step kernel
   std::string trace_file;
+  uint64_t* ktrace = nullptr;  // MYOS_KTRACE_FILE: launch timeline of the per-kernel step
+  std::string ktrace_file;
+  std::vector<uint64_t> ktrace_init;
 };
 
 namespace {
@@ -197,6 +201,16 @@ int sync_copies(myos_ctx* c) {
 // ---------------------------------------------------------------- step enqueue
 enum KernelKind { K_QKV = 0, K_ATTN = 1, K_O = 2, K_GU = 3, K_DOWN = 4, K_HEAD = 5, K_END = 6 };
 
+KTrace ktrace_at(const myos_ctx* c, int slot) {
+  KTrace t = {};
+  if (c->ktrace && !c->profiling) {
+    t.buf = c->ktrace;
+    t.slot = slot;
+    t.nslot = 5 * (int)c->s.num_layers + 1;
+  }
+  return t;
+}
+
 int launch_kind(myos_ctx* c, int kind, int l, const uint32_t* feed, bool pdl, bool embed_l0) {
   const myos_shape& s = c->s;
   const int H = (int)s.hidden, I = (int)s.intermediate;
@@ -224,6 +238,7 @@ int launch_kind(myos_ctx* c, int kind, int l, const uint32_t* feed, bool pdl, bo
     h.err = &c->ctl->err;
     h.rec_fed = c->profiling ? nullptr : c->rec_fed;
     h.rec_argmax = c->profiling ? nullptr : c->rec_argmax;
+    h.tr = ktrace_at(c, 5 * (int)s.num_layers);
     CK(launch_gemv(EPI_ARGMAX, h, c->grid_head, c->st, pdl));
     return MYOS_OK;
   }
@@ -244,6 +259,7 @@ int launch_kind(myos_ctx* c, int kind, int l, const uint32_t* feed, bool pdl, bo
     q.bias = w.bqkv;
     q.err = &c->ctl->err;
     q.prefetch_cap = prefetch_cap(c, c->grid_qkv);
+    q.tr = ktrace_at(c, 5 * l + K_QKV);
     CK(launch_gemv(EPI_BIAS, q, c->grid_qkv, c->st, pdl));
   } else if (kind == K_ATTN) {
     AttnArgs at = {};
@@ -267,6 +283,8 @@ int launch_kind(myos_ctx* c, int kind, int l, const uint32_t* feed, bool pdl, bo
     at.counters = c->counters + 1;
     at.out = c->attn;
     at.decode = 1;
+    at.defer_merge = c->defer_merge;
+    at.tr = ktrace_at(c, 5 * l + K_ATTN);
     CK(launch_attention(at, kv_bf16, c->st, pdl));
   } else if (kind == K_O) {
     GemvArgs o = {};
@@ -275,9 +293,19 @@ int launch_kind(myos_ctx* c, int kind, int l, const uint32_t* feed, bool pdl, bo
     o.K = (int)c->qd;
     o.in.x = c->attn;
     o.in.ctl = c->ctl;
+    if (c->defer_merge) {  // the staging merges the attention splits
+      o.in.part_o = c->part_o;
+      o.in.part_m = c->part_m;
+      o.in.part_l = c->part_l;
+      o.in.m_G = (int)c->G;
+      o.in.m_d = (int)s.head_dim;
+      o.in.m_nsplit = c->attn_nsplit;
+      o.in.m_chunk = c->attn_chunk;
+    }
     o.y = c->resid;
     o.err = &c->ctl->err;
     o.prefetch_cap = prefetch_cap(c, c->grid_o);
+    o.tr = ktrace_at(c, 5 * l + K_O);
     CK(launch_gemv(EPI_RESID, o, c->grid_o, c->st, pdl));
   } else if (kind == K_GU) {
     GemvArgs gu = {};
@@ -292,6 +320,7 @@ int launch_kind(myos_ctx* c, int kind, int l, const uint32_t* feed, bool pdl, bo
     gu.y = c->act;
     gu.err = &c->ctl->err;
     gu.prefetch_cap = prefetch_cap(c, c->grid_gu);
+    gu.tr = ktrace_at(c, 5 * l + K_GU);
     CK(launch_gemv(EPI_SWIGLU, gu, c->grid_gu, c->st, pdl));
   } else if (kind == K_DOWN) {
     GemvArgs dn = {};
@@ -303,6 +332,7 @@ int launch_kind(myos_ctx* c, int kind, int l, const uint32_t* feed, bool pdl, bo
     dn.y = c->resid;
     dn.err = &c->ctl->err;
     dn.prefetch_cap = prefetch_cap(c, c->grid_down);
+    dn.tr = ktrace_at(c, 5 * l + K_DOWN);
     CK(launch_gemv(EPI_RESID, dn, c->grid_down, c->st, pdl));
   }
   return MYOS_OK;
@@ -387,6 +417,9 @@ int run_steps(myos_ctx* c, int kind, size_t nsteps) {
 // Upload ctl.step = 0 (and pos when asked) before a call.
 int set_ctl(myos_ctx* c, bool set_pos) {
   CK(cudaStreamWaitEvent(c->st, c->load_ev, 0));
+  if (c->ktrace)
+    CK(cudaMemcpyAsync(c->ktrace, c->ktrace_init.data(), c->ktrace_init.size() * 8,
+                       cudaMemcpyHostToDevice, c->st));
   c->ctl_host->step = 0;
   c->ctl_host->pos = (uint32_t)c->len;
   if (set_pos) {
@@ -401,6 +434,16 @@ int finish(myos_ctx* c) {
   cudaError_t e = cudaMemcpyAsync(&c->ctl_host->err, &c->ctl->err, 4, cudaMemcpyDeviceToHost, c->st);
   if (e == cudaSuccess) e = cudaStreamSynchronize(c->st);
   if (e != cudaSuccess) return fail(c, MYOS_ERR_CUDA, std::string("step: ") + cudaGetErrorString(e));
+  if (c->ktrace) {  // launch timeline of the last call, for offline analysis
+    const size_t nt = (size_t)kTraceSteps * (5 * c->s.num_layers + 1) * kTraceWidth;
+    std::vector<uint64_t> h(nt);
+    if (cudaMemcpy(h.data(), c->ktrace, nt * 8, cudaMemcpyDeviceToHost) == cudaSuccess) {
+      if (FILE* f = fopen(c->ktrace_file.c_str(), "wb")) {
+        fwrite(h.data(), 8, nt, f);
+        fclose(f);
+      }
+    }
+  }
   if (c->trace) {  // last step's stamps, for offline analysis
     const size_t nt = (size_t)c->num_sms * (5 * c->s.num_layers + 1) * 4;
     std::vector<uint64_t> h(nt);
@@ -556,6 +599,15 @@ static int create_impl(myos_ctx* c, const myos_shape* shape, const myos_opts* op
   if (nsplit > cap) nsplit = cap;
   c->attn_nsplit = (int)nsplit;
   c->attn_chunk = (int)((S + nsplit - 1) / nsplit);
+  {
+    // MYOS_DEFER_MERGE=1: merge the attention splits in the o_proj staging
+    // (saves the attention kernel's fence and counter, but every o_proj block
+    // then reads all partials; measured slower for the 1.5B step).
+    const char* e = getenv("MYOS_DEFER_MERGE");
+    const bool want = e && e[0] == '1';
+    c->defer_merge = want && s.num_q_heads <= 256 &&
+                     merge_smem_bytes((int)s.num_q_heads, (int)nsplit, (int)d) <= (96u << 10);
+  }
   // workspace
   CK(cudaMalloc(&c->resid, H * 4));
   CK(cudaMalloc(&c->qkv, (c->qd + 2 * c->kvd) * 4));
@@ -667,6 +719,14 @@ static int create_impl(myos_ctx* c, const myos_shape* shape, const myos_opts* op
       }
     }
   }
+  if (const char* kf = getenv("MYOS_KTRACE_FILE")) {
+    c->ktrace_file = kf;
+    const size_t rows = (size_t)kTraceSteps * (5 * L + 1);
+    c->ktrace_init.assign(rows * kTraceWidth, 0);  // max fields start at 0
+    for (size_t r = 0; r < rows; ++r)
+      c->ktrace_init[kTraceWidth * r] = c->ktrace_init[kTraceWidth * r + 1] = ~0ull;  // min fields
+    CK(cudaMalloc(&c->ktrace, rows * kTraceWidth * 8));
+  }
   // streams, staging
   CK(cudaStreamCreateWithFlags(&c->st, cudaStreamNonBlocking));
   CK(cudaStreamCreateWithFlags(&c->copy_st, cudaStreamNonBlocking));
@@ -711,7 +771,8 @@ void myos_ctx_destroy(myos_ctx* c) {
   void* dev[] = {c->warena, c->kcache, c->vcache, c->resid, c->qkv, c->attn, c->act, c->logits,
                  c->part_val, c->part_idx, c->part_o, c->part_m, c->part_l, c->counters, c->ctl,
                  c->feed, c->rec_fed, c->rec_argmax, c->cos_t, c->sin_t, c->d_layers, c->bar,
-                 (void*)c->margs.part_val, (void*)c->margs.part_idx, (void*)c->trace};
+                 (void*)c->margs.part_val, (void*)c->margs.part_idx, (void*)c->trace,
+                 (void*)c->ktrace};
   for (void* p : dev)
     if (p) cudaFree(p);
   for (int i = 0; i < 2; ++i) {

@@ -44,8 +44,105 @@ MYOS_DEV void unpack8(const uint4& u, float4& lo, float4& hi) {
   hi = make_float4(bf16_lo(u.z), bf16_hi(u.z), bf16_lo(u.w), bf16_hi(u.w));
 }
 
+// Timeline stamps (KTrace): called by thread 0 of each block after the
+// dependency wait (the step counter is only stable then).
+MYOS_DEV uint64_t* trace_begin(const KTrace& t, const StepCtl* ctl, uint64_t t_start) {
+  if (!t.buf || threadIdx.x != 0) return nullptr;
+  uint64_t* row = t.buf + ((size_t)(ctl->step % kTraceSteps) * t.nslot + t.slot) * kTraceWidth;
+  atomicMin(reinterpret_cast<unsigned long long*>(row), (unsigned long long)t_start);
+  atomicMin(reinterpret_cast<unsigned long long*>(row + 1), (unsigned long long)global_ns());
+  return row;
+}
+MYOS_DEV void trace_end(uint64_t* row) {
+  if (row) atomicMax(reinterpret_cast<unsigned long long*>(row + 2), (unsigned long long)global_ns());
+}
+MYOS_DEV void trace_mark(uint64_t* row, int k) {
+  if (row) atomicMax(reinterpret_cast<unsigned long long*>(row + k), (unsigned long long)global_ns());
+}
+
+MYOS_DEV void cpa16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
+               : "memory");
+}
+MYOS_DEV void cpa_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// Attention-merge staging: x = merge of the split partials of the splits
+// holding keys 0..pos. Per head h (KV head g = h / G): M = max_q m_q,
+// f_q = expf(m_q - M), L = sum_q l_q f_q, x = (sum_q o_q f_q) / L, sums in
+// split order (the reference's e / sum, gqa.rs:283-307, reassociated).
+// All partials are copied into shared memory at once (scratch after xs).
+MYOS_DEV void stage_merge(float* xs, int K, bool vec, const GemvInput& in, float* mb) {
+  const int nt = blockDim.x;
+  const int G = in.m_G, d = in.m_d, ns = in.m_nsplit, Hq = K / d, Hkv = Hq / G;
+  const int nkeys = (int)in.ctl->pos + 1;
+  int ne = (nkeys + in.m_chunk - 1) / in.m_chunk;
+  if (ne > ns) ne = ns;
+  float* po = mb;                       // [Hkv][ns][G][d] (valid splits filled)
+  float* fs = po + (size_t)Hkv * ns * G * d;  // [Hkv][ns][G]
+  float* ls = fs + Hkv * ns * G;
+  float* Ls = ls + Hkv * ns * G;        // [Hq]
+  const int per_g = ne * G * d;         // contiguous floats of one KV head's valid splits
+  if ((d & 3) == 0) {
+    const int q4 = per_g >> 2;
+    for (int i = threadIdx.x; i < Hkv * q4; i += nt) {
+      const int g = i / q4, r = i - g * q4;
+      const size_t off = (size_t)g * ns * G * d + 4 * (size_t)r;
+      cpa16(po + off, in.part_o + off);
+    }
+  } else {
+    for (int i = threadIdx.x; i < Hkv * per_g; i += nt) {
+      const int g = i / per_g, r = i - g * per_g;
+      const size_t off = (size_t)g * ns * G * d + r;
+      po[off] = __ldcg(in.part_o + off);
+    }
+  }
+  const int per_m = ne * G;
+  for (int i = threadIdx.x; i < Hkv * per_m; i += nt) {
+    const int g = i / per_m, r = i - g * per_m;
+    const int off = g * ns * G + r;
+    fs[off] = __ldcg(in.part_m + off);
+    ls[off] = __ldcg(in.part_l + off);
+  }
+  cpa_wait_all();
+  __syncthreads();
+  if (threadIdx.x < Hq) {
+    const int h = threadIdx.x, g = h / G, hh = h - g * G;
+    float M = -INFINITY;
+    for (int q = 0; q < ne; ++q) M = fmaxf(M, fs[(g * ns + q) * G + hh]);
+    float L = 0.0f;
+    for (int q = 0; q < ne; ++q) {
+      const int i = (g * ns + q) * G + hh;
+      const float f = fs[i] == -INFINITY ? 0.0f : expf(fs[i] - M);
+      fs[i] = f;
+      L = fmaf(ls[i], f, L);
+    }
+    Ls[h] = L;
+  }
+  __syncthreads();
+  for (int o = threadIdx.x; o < K; o += nt) {
+    const int h = o / d, e = o - h * d, g = h / G, hh = h - g * G;
+    float O = 0.0f;
+    for (int q = 0; q < ne; ++q) {
+      const int i = (g * ns + q) * G + hh;
+      O = fmaf(po[(size_t)i * d + e], fs[i], O);
+    }
+    const float v = __fdiv_rn(O, Ls[h]);
+    if (vec) {
+      const int c = o >> 3, r = o & 7;
+      xs[r < 4 ? (c * 4 + r) : ((K >> 1) + c * 4 + (r - 4))] = v;
+    } else {
+      xs[o] = v;
+    }
+  }
+  __syncthreads();
+}
+
 MYOS_DEV void stage_input(float* xs, int K, bool vec, const GemvInput& in, float* red) {
   const int nt = blockDim.x;
+  if (in.part_o) {
+    stage_merge(xs, K, vec, in, xs + ((K + 7) & ~7));
+    return;
+  }
   const uint16_t* erow = nullptr;
   if (in.embed) {
     const uint32_t tok = in.feed ? in.feed[in.ctl->step] : in.ctl->argmax;
@@ -363,11 +460,14 @@ __global__ void __launch_bounds__(kThreads, 2) k_gemv_stream(GemvArgs a) {
 #pragma unroll
     for (int r = 0; r < NR; ++r) prefetch_range(wbase[r] + (size_t)r0 * a.K, bytes);
   }
+  const uint64_t t_start = a.tr.buf ? global_ns() : 0;
   uint4 cur[NR][U], nxt[NR][U];
   if (nb > 0) load_batch<NR, U>(cur, wbase, a.K, r0 + warp, 0, P, lane);
   pdl_wait();
   pdl_launch();
+  uint64_t* trow = trace_begin(a.tr, a.in.ctl, t_start);
   stage_input(xs, a.K, true, a.in, red);
+  trace_mark(trow, 3);  // input staged
 
   const float4* xlo = reinterpret_cast<const float4*>(xs);
   const float4* xhi = reinterpret_cast<const float4*>(xs + (a.K >> 1));
@@ -409,6 +509,10 @@ __global__ void __launch_bounds__(kThreads, 2) k_gemv_stream(GemvArgs a) {
   }
 
   if (EPI == EPI_ARGMAX) argmax_finish(a, bv, bi, wbv, wbi, &last_block);
+  if (a.tr.buf) {  // block-uniform
+    __syncthreads();
+    trace_end(trow);
+  }
 }
 
 // ------------------------------------------------------------------ bulk-copy GEMV
@@ -607,40 +711,88 @@ MYOS_DEV float rope_lane(const float* x, int e, int d, const float* cs, const fl
 // Split-KV decode attention (flash-decoding). Block (s, g) covers keys
 // [s*chunk, (s+1)*chunk) for KV head g and its G query heads (gqa.rs:96-105:
 // heads [g*G, (g+1)*G) read KV head g). Keys are processed in tiles of 32:
-//   1. the tile's K and V rows are copied to shared memory (coalesced);
-//   2. one thread per (head, key) forms score = (q . k) * scale
-//      (gqa.rs:189-191, scale = 1/sqrtf(d));
+//   1. the tile's K and V rows are copied to shared memory (coalesced); the
+//      first tile, and the rotation row, are loaded before the dependency
+//      wait: cached keys below pos do not depend on the preceding kernel;
+//   2. (head, key) scores = (q . k) * scale (gqa.rs:189-191,
+//      scale = 1/sqrtf(d)), four threads per dot product when d % 16 == 0;
 //   3. one warp per head runs the online softmax over the tile's 32 scores
 //      (running max, expf(s - max), running sum);
 //   4. threads accumulate p * v for their (head, lane) outputs.
-// The block writes (unnormalised output, max, sum) per head; the last block
-// of KV head g to finish merges the splits in split order and divides by the
-// sum (the reference's e / sum, gqa.rs:283-307, up to reassociation).
+// The block writes (unnormalised output, max, sum) per head. With
+// defer_merge the o_proj staging merges the splits; otherwise the last block
+// of KV head g to finish merges them in split order and divides by the sum
+// (the reference's e / sum, gqa.rs:283-307, up to reassociation).
 constexpr int kTile = 32;
+
+template <typename KT>
+MYOS_DEV void attn_tile_load(const KT* kc, const KT* vc, int d, int t0, int nk, int skip,
+                             float* ks, float* vs) {
+  const int nt = blockDim.x, ds = d + 4;
+  if ((d & 3) == 0) {
+    // quads of 4 elements; all of this thread's loads in flight together
+    const int qpr = d >> 2, nqd = nk * qpr;
+    constexpr int kQ = kTile * 64 / kThreads;  // d <= 256: at most 8 quads per thread
+    float4 kq[kQ], vq[kQ];
+#pragma unroll
+    for (int j = 0; j < kQ; ++j) {
+      const int i = threadIdx.x + nt * j;
+      if (i < nqd) {
+        const int tt = i / qpr, e = (i - tt * qpr) * 4;
+        if (t0 + tt != skip) {
+          kq[j] = kv_load4<KT>(kc + (size_t)(t0 + tt) * d + e);
+          vq[j] = kv_load4<KT>(vc + (size_t)(t0 + tt) * d + e);
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kQ; ++j) {
+      const int i = threadIdx.x + nt * j;
+      if (i < nqd) {
+        const int tt = i / qpr, e = (i - tt * qpr) * 4;
+        if (t0 + tt != skip) {
+          *reinterpret_cast<float4*>(ks + tt * ds + e) = kq[j];
+          *reinterpret_cast<float4*>(vs + tt * ds + e) = vq[j];
+        }
+      }
+    }
+  } else {
+    for (int i = threadIdx.x; i < nk * d; i += nt) {
+      const int tt = i / d, e = i - tt * d;
+      if (t0 + tt == skip) continue;
+      ks[tt * ds + e] = kv_load<KT>(kc + (size_t)(t0 + tt) * d + e);
+      vs[tt * ds + e] = kv_load<KT>(vc + (size_t)(t0 + tt) * d + e);
+    }
+  }
+}
 
 template <int DPL, typename KT>
 __global__ void __launch_bounds__(kThreads) k_attn(AttnArgs a) {
   extern __shared__ float4 smem4[];
   float* sm = reinterpret_cast<float*>(smem4);
-  const int d = a.d, G = a.G;
+  const int d = a.d, G = a.G, half = d >> 1;
   const int ds = d + 4;                   // padded row stride (float4 reads conflict-free)
-  float* qs = sm;                         // [G][d]
+  float* qs = sm;                         // [G][d] rotated q
   float* ks = qs + G * d;                 // [kTile][ds]
   float* vs = ks + kTile * ds;            // [kTile][ds]
   float* ps = vs + kTile * ds;            // [G][kTile]
   float* corr = ps + G * kTile;           // [G]
-  float* knew = corr + kMaxG;             // [d]
+  float* knew = corr + kMaxG;             // [d] rotated new k (as cached)
   float* vnew = knew + d;                 // [d]
+  float* qraw = vnew + d;                 // [G][d] q before rotation
+  float* cst = qraw + G * d;              // [d/2] rotation row
+  float* snt = cst + half;                // [d/2]
+  float* kraw = snt + half;               // [d]
+  float* vraw = kraw + d;                 // [d]
   __shared__ int last_block;
 
   const int s = blockIdx.x, g = blockIdx.y;
   const int nt = blockDim.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const KT* kc = reinterpret_cast<const KT*>(a.kc) + (size_t)g * a.S * d;
-  const KT* vc = reinterpret_cast<const KT*>(a.vc) + (size_t)g * a.S * d;
+  KT* kc = reinterpret_cast<KT*>(a.kc) + (size_t)g * a.S * d;
+  KT* vc = reinterpret_cast<KT*>(a.vc) + (size_t)g * a.S * d;
 
-  pdl_wait();
-  pdl_launch();
-
+  // The position is set before the step's first kernel started, and the
+  // cached keys below it by earlier steps, so both are read before the wait.
   int nkeys, pos = -1;
   if (a.decode) {
     pos = (int)a.ctl->pos;
@@ -650,46 +802,45 @@ __global__ void __launch_bounds__(kThreads) k_attn(AttnArgs a) {
   }
   const int kb = s * a.chunk;
   const int ke = min(kb + a.chunk, nkeys);
-  const int half = d >> 1;
-  const float* cs = a.decode ? a.cos_t + (size_t)pos * half : nullptr;
-  const float* sn = a.decode ? a.sin_t + (size_t)pos * half : nullptr;
-
   const bool has_new = a.decode && pos >= kb && pos < ke;
+  if (a.defer_merge && kb >= ke) return;  // no keys: the merge skips this split
+  const uint64_t t_start = a.tr.buf ? global_ns() : 0;
+  if (kb < ke) attn_tile_load<KT>(kc, vc, d, kb, min(kTile, ke - kb), has_new ? pos : -1, ks, vs);
+  if (a.decode)
+    for (int i = threadIdx.x; i < half; i += nt) {
+      cst[i] = __ldg(a.cos_t + (size_t)pos * half + i);
+      snt[i] = __ldg(a.sin_t + (size_t)pos * half + i);
+    }
+
+  pdl_wait();
+  pdl_launch();
+  uint64_t* trow = a.decode ? trace_begin(a.tr, a.ctl, t_start) : nullptr;
+
   {
-    // Stage q (G heads), and in decode mode the cos/sin row and this KV
-    // head's new k and v, with every load issued before the first store.
-    float* qraw = a.decode ? ks : qs;  // tile buffers are free until the first tile
-    float* cst = vs;
-    float* snt = vs + half;
-    float* kraw = vs + d;
-    float* vraw = vs + 2 * d;
+    // q of the G heads and, when this split holds the new key, its k and v:
+    // every load issued before the first store.
+    float* qdst = a.decode ? qraw : qs;
     const int nq = G * d;
-    const int ntot = a.decode ? nq + d + (has_new ? 2 * d : 0) : nq;
+    const int ntot = nq + (has_new ? 2 * d : 0);
     const float* qsrc = a.q + (size_t)g * G * d;
     const float* ksrc = a.q + (size_t)a.Hq * d + (size_t)g * d;
     const float* vsrc = a.q + (size_t)(a.Hq + a.Hkv) * d + (size_t)g * d;
-    constexpr int kJ = 12;  // (8*256 + 3*256) / 256 elements per thread at most
+    constexpr int kJ = (kMaxG * 256 + 2 * 256) / kThreads;
     float val[kJ];
 #pragma unroll
     for (int j = 0; j < kJ; ++j) {
       const int v = threadIdx.x + nt * j;
-      if (v < ntot) {
-        if (v < nq) val[j] = __ldcg(qsrc + v);
-        else if (v < nq + half) val[j] = __ldg(cs + (v - nq));
-        else if (v < nq + d) val[j] = __ldg(sn + (v - nq - half));
-        else if (v < nq + 2 * d) val[j] = __ldcg(ksrc + (v - nq - d));
-        else val[j] = __ldcg(vsrc + (v - nq - 2 * d));
-      }
+      if (v < ntot)
+        val[j] = v < nq ? __ldcg(qsrc + v)
+                        : (v < nq + d ? __ldcg(ksrc + (v - nq)) : __ldcg(vsrc + (v - nq - d)));
     }
 #pragma unroll
     for (int j = 0; j < kJ; ++j) {
       const int v = threadIdx.x + nt * j;
       if (v < ntot) {
-        if (v < nq) qraw[v] = val[j];
-        else if (v < nq + half) cst[v - nq] = val[j];
-        else if (v < nq + d) snt[v - nq - half] = val[j];
-        else if (v < nq + 2 * d) kraw[v - nq - d] = val[j];
-        else vraw[v - nq - 2 * d] = val[j];
+        if (v < nq) qdst[v] = val[j];
+        else if (v < nq + d) kraw[v - nq] = val[j];
+        else vraw[v - nq - d] = val[j];
       }
     }
     if (a.decode) {
@@ -699,20 +850,24 @@ __global__ void __launch_bounds__(kThreads) k_attn(AttnArgs a) {
         qs[i] = rope_lane(qraw + hh * d, e, d, cst, snt);
       }
       if (has_new) {
-        KT* kdst = const_cast<KT*>(kc) + (size_t)pos * d;
-        KT* vdst = const_cast<KT*>(vc) + (size_t)pos * d;
+        const int tt = pos - kb;  // the new key sits in the first tile when tt < kTile
         for (int e = threadIdx.x; e < d; e += nt) {
           const KT kq = kv_from<KT>(rope_lane(kraw, e, d, cst, snt));
           const KT vq = kv_from<KT>(vraw[e]);
           knew[e] = kv_load<KT>(&kq);
           vnew[e] = kv_load<KT>(&vq);
-          kdst[e] = kq;  // the cache slot for this position (KvCache::store)
-          vdst[e] = vq;
+          kc[(size_t)pos * d + e] = kq;  // the cache slot for this position (KvCache::store)
+          vc[(size_t)pos * d + e] = vq;
+          if (tt < kTile) {
+            ks[tt * ds + e] = knew[e];
+            vs[tt * ds + e] = vnew[e];
+          }
         }
       }
     }
   }
 
+  trace_mark(trow, 3);  // q staged and rotated (this thread's part)
   // Output slots: thread owns outputs o = threadIdx.x + nt*i of G*d.
   constexpr int kMaxOut = kMaxG * 256 / kThreads;
   float acc[kMaxOut];
@@ -722,57 +877,27 @@ __global__ void __launch_bounds__(kThreads) k_attn(AttnArgs a) {
 
   for (int t0 = kb; t0 < ke; t0 += kTile) {
     const int nk = min(kTile, ke - t0);
-    __syncthreads();  // previous tile fully consumed; qs/knew staged
-    if ((d & 3) == 0) {
-      // quads of 4 elements; all of this thread's loads in flight together
-      const int qpr = d >> 2, nqd = nk * qpr;
-      constexpr int kQ = kTile * 64 / kThreads;  // d <= 256: at most 8 quads per thread
-      float4 kq[kQ], vq[kQ];
-#pragma unroll
-      for (int j = 0; j < kQ; ++j) {
-        const int i = threadIdx.x + nt * j;
-        if (i < nqd) {
-          const int tt = i / qpr, e = (i - tt * qpr) * 4;
-          const int t = t0 + tt;
-          if (!(has_new && t == pos)) {
-            kq[j] = kv_load4<KT>(kc + (size_t)t * d + e);
-            vq[j] = kv_load4<KT>(vc + (size_t)t * d + e);
-          }
+    if (t0 != kb) {
+      __syncthreads();  // previous tile fully consumed
+      attn_tile_load<KT>(kc, vc, d, t0, nk, has_new ? pos : -1, ks, vs);
+      if (has_new && pos >= t0 && pos < t0 + nk)
+        for (int e = threadIdx.x; e < d; e += nt) {
+          ks[(pos - t0) * ds + e] = knew[e];
+          vs[(pos - t0) * ds + e] = vnew[e];
         }
-      }
-#pragma unroll
-      for (int j = 0; j < kQ; ++j) {
-        const int i = threadIdx.x + nt * j;
-        if (i < nqd) {
-          const int tt = i / qpr, e = (i - tt * qpr) * 4;
-          const int t = t0 + tt;
-          if (has_new && t == pos) {
-            kq[j] = make_float4(knew[e], knew[e + 1], knew[e + 2], knew[e + 3]);
-            vq[j] = make_float4(vnew[e], vnew[e + 1], vnew[e + 2], vnew[e + 3]);
-          }
-          *reinterpret_cast<float4*>(ks + tt * ds + e) = kq[j];
-          *reinterpret_cast<float4*>(vs + tt * ds + e) = vq[j];
-        }
-      }
-    } else {
-      for (int i = threadIdx.x; i < nk * d; i += nt) {
-        const int tt = i / d, e = i - tt * d;
-        const int t = t0 + tt;
-        const bool nw_ = has_new && t == pos;
-        ks[tt * ds + e] = nw_ ? knew[e] : kv_load<KT>(kc + (size_t)t * d + e);
-        vs[tt * ds + e] = nw_ ? vnew[e] : kv_load<KT>(vc + (size_t)t * d + e);
-      }
     }
     __syncthreads();
-    for (int i = threadIdx.x; i < G * kTile; i += nt) {
-      const int hh = i / kTile, tt = i - hh * kTile;
-      float sc = -INFINITY;
-      if (tt < nk) {
-        const float* qh = qs + hh * d;
-        const float* kr = ks + tt * ds;
+    if ((d & 15) == 0) {
+      // four threads per (head, key): quarter dot products, then two shuffles
+      const int qd4 = d >> 2;
+      for (int i = threadIdx.x; i < G * kTile * 4; i += nt) {
+        const int hk = i >> 2, part = i & 3;
+        const int hh = hk / kTile, tt = hk - hh * kTile;
         float dot = 0.0f;
-        if ((d & 3) == 0) {
-          for (int e = 0; e < d; e += 4) {
+        if (tt < nk) {
+          const float* qh = qs + hh * d + part * qd4;
+          const float* kr = ks + tt * ds + part * qd4;
+          for (int e = 0; e < qd4; e += 4) {
             const float4 qv = *reinterpret_cast<const float4*>(qh + e);
             const float4 kv = *reinterpret_cast<const float4*>(kr + e);
             dot = fmaf(qv.x, kv.x, dot);
@@ -780,12 +905,24 @@ __global__ void __launch_bounds__(kThreads) k_attn(AttnArgs a) {
             dot = fmaf(qv.z, kv.z, dot);
             dot = fmaf(qv.w, kv.w, dot);
           }
-        } else {
-          for (int e = 0; e < d; ++e) dot = fmaf(qh[e], kr[e], dot);
         }
-        sc = __fmul_rn(dot, a.scale);
+        dot += __shfl_xor_sync(0xffffffffu, dot, 1);
+        dot += __shfl_xor_sync(0xffffffffu, dot, 2);
+        if (part == 0) ps[hh * kTile + tt] = tt < nk ? __fmul_rn(dot, a.scale) : -INFINITY;
       }
-      ps[hh * kTile + tt] = sc;
+    } else {
+      for (int i = threadIdx.x; i < G * kTile; i += nt) {
+        const int hh = i / kTile, tt = i - hh * kTile;
+        float sc = -INFINITY;
+        if (tt < nk) {
+          const float* qh = qs + hh * d;
+          const float* kr = ks + tt * ds;
+          float dot = 0.0f;
+          for (int e = 0; e < d; ++e) dot = fmaf(qh[e], kr[e], dot);
+          sc = __fmul_rn(dot, a.scale);
+        }
+        ps[hh * kTile + tt] = sc;
+      }
     }
     __syncthreads();
     if (warp < G) {
@@ -813,6 +950,7 @@ __global__ void __launch_bounds__(kThreads) k_attn(AttnArgs a) {
     }
   }
 
+  trace_mark(trow, 4);  // tiles done (thread 0's view)
   // This split's partial: (sum_t e_t v_t, max, sum) per head.
   const size_t pbase = ((size_t)g * a.nsplit + s) * G;
 #pragma unroll
@@ -824,6 +962,13 @@ __global__ void __launch_bounds__(kThreads) k_attn(AttnArgs a) {
     a.part_m[pbase + warp] = m_run;
     a.part_l[pbase + warp] = l_run;
   }
+  if (a.defer_merge) {
+    if (a.tr.buf) {  // block-uniform
+      __syncthreads();
+      trace_end(trow);
+    }
+    return;
+  }
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -831,6 +976,7 @@ __global__ void __launch_bounds__(kThreads) k_attn(AttnArgs a) {
     last_block = prev == (unsigned)(a.nsplit - 1);
   }
   __syncthreads();
+  trace_mark(trow, 5);  // counted in
   if (!last_block) return;
   __threadfence();
   // Merge: factor f_q = expf(m_q - M) per (split, head), staged in shared memory.
@@ -874,6 +1020,256 @@ __global__ void __launch_bounds__(kThreads) k_attn(AttnArgs a) {
     a.out[(size_t)g * G * d + o] = __fdiv_rn(O, Ls[hh]);
   }
   if (threadIdx.x == 0) a.counters[g] = 0u;
+  if (a.tr.buf) {  // block-uniform
+    __syncthreads();
+    trace_end(trow);
+  }
+}
+
+// Compact decode attention. The per-kernel step launches this kernel on a
+// handful of SMs once per layer, so its instructions are fetched cold on
+// every launch: the code is kept short (copies through cp.async, rolled
+// loops) and the work per thread simple. Block (s, g) covers keys
+// [s*chunk, (s+1)*chunk) of KV head g; warp h < G serves query head g*G + h:
+//   lane t scores key t of the tile: (q . k_t) * scale (gqa.rs:189-191);
+//   the warp runs the online softmax over the tile (max, expf(s - max), sum);
+//   lane l accumulates p_t * v_t for dims [4l, 4l+4) (+128 for d > 128).
+// The first tile and the rotation row are copied before the dependency wait.
+// The split partials are merged by the o_proj staging (defer_merge) or by
+// the last block of the KV head to finish, one warp per head, splits in order.
+template <typename KT>
+MYOS_DEV void dec_tile_issue(const KT* kc, const KT* vc, int d, int t0, int nk, int skip,
+                             float* ks, float* vs, uint4* raw) {
+  constexpr int per = 16 / sizeof(KT);  // elements per 16-byte piece
+  const int ppr = d / per, ds = d + 4;
+  for (int i = threadIdx.x; i < nk * ppr; i += blockDim.x) {
+    const int tt = i / ppr, e = (i - tt * ppr) * per;
+    if (t0 + tt == skip) continue;
+    const KT* ksrc = kc + (size_t)(t0 + tt) * d + e;
+    const KT* vsrc = vc + (size_t)(t0 + tt) * d + e;
+    if (sizeof(KT) == 4) {
+      cpa16(ks + tt * ds + e, ksrc);
+      cpa16(vs + tt * ds + e, vsrc);
+    } else {
+      cpa16(raw + i, ksrc);
+      cpa16(raw + kTile * ppr + i, vsrc);
+    }
+  }
+}
+
+// Completes this thread's copies; bf16 rows are widened by the thread that
+// copied them.
+template <typename KT>
+MYOS_DEV void dec_tile_finish(int d, int t0, int nk, int skip, float* ks, float* vs,
+                              const uint4* raw) {
+  cpa_wait_all();
+  if (sizeof(KT) == 4) return;
+  const int ppr = d / 8, ds = d + 4;
+  for (int i = threadIdx.x; i < nk * ppr; i += blockDim.x) {
+    const int tt = i / ppr, e = (i - tt * ppr) * 8;
+    if (t0 + tt == skip) continue;
+    float4 lo, hi;
+    unpack8(raw[i], lo, hi);
+    *reinterpret_cast<float4*>(ks + tt * ds + e) = lo;
+    *reinterpret_cast<float4*>(ks + tt * ds + e + 4) = hi;
+    unpack8(raw[kTile * ppr + i], lo, hi);
+    *reinterpret_cast<float4*>(vs + tt * ds + e) = lo;
+    *reinterpret_cast<float4*>(vs + tt * ds + e + 4) = hi;
+  }
+}
+
+size_t attn_dec_smem_bytes(int G, int d) {
+  // q, two padded tiles, new k/v, rotation row, raw bf16 tile rows
+  return ((size_t)G * d + 2 * kTile * (d + 4) + 3 * (size_t)d + (size_t)kTile * d) * sizeof(float);
+}
+
+template <typename KT>
+__global__ void __launch_bounds__(kThreads) k_attn_dec(AttnArgs a) {
+  extern __shared__ float4 smem4[];
+  float* sm = reinterpret_cast<float*>(smem4);
+  const int d = a.d, G = a.G, half = d >> 1, ds = d + 4;
+  float* qs = sm;                   // [G][d]
+  float* ks = qs + G * d;           // [kTile][ds]
+  float* vs = ks + kTile * ds;      // [kTile][ds]
+  float* kn = vs + kTile * ds;      // [d] new k
+  float* vn = kn + d;               // [d] new v
+  float* cs = vn + d;               // [d/2]
+  float* sn = cs + half;            // [d/2]
+  uint4* raw = reinterpret_cast<uint4*>(sn + half);
+  __shared__ int last_block;
+  const int s = blockIdx.x, g = blockIdx.y, ns = a.nsplit;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  KT* kc = reinterpret_cast<KT*>(a.kc) + (size_t)g * a.S * d;
+  KT* vc = reinterpret_cast<KT*>(a.vc) + (size_t)g * a.S * d;
+  // The position is set before the step's first kernel started, and the
+  // cached keys below it by earlier steps: both are read before the wait.
+  const int pos = (int)a.ctl->pos;
+  const int kb = s * a.chunk, ke = min(kb + a.chunk, pos + 1);
+  const bool has_new = pos >= kb && pos < ke;
+  if (a.defer_merge && kb >= ke) return;  // no keys: the merge skips this split
+  const uint64_t t_start = a.tr.buf ? global_ns() : 0;
+  if (kb < ke) dec_tile_issue<KT>(kc, vc, d, kb, min(kTile, ke - kb), pos, ks, vs, raw);
+  const float4* c4 = reinterpret_cast<const float4*>(a.cos_t + (size_t)pos * half);
+  const float4* s4 = reinterpret_cast<const float4*>(a.sin_t + (size_t)pos * half);
+  for (int i = threadIdx.x; i < (half >> 2); i += blockDim.x) {
+    cpa16(reinterpret_cast<float4*>(cs) + i, c4 + i);
+    cpa16(reinterpret_cast<float4*>(sn) + i, s4 + i);
+  }
+
+  pdl_wait();
+  pdl_launch();
+  uint64_t* trow = trace_begin(a.tr, a.ctl, t_start);
+
+  // q of the G heads; the new k and v when this split holds position pos
+  const int nq4 = G * d / 4, d4 = d / 4;
+  const float4* q4 = reinterpret_cast<const float4*>(a.q + (size_t)g * G * d);
+  const float4* k4 = reinterpret_cast<const float4*>(a.q + (size_t)(a.Hq + g) * d);
+  const float4* v4 = reinterpret_cast<const float4*>(a.q + (size_t)(a.Hq + a.Hkv + g) * d);
+  for (int i = threadIdx.x; i < nq4 + (has_new ? 2 * d4 : 0); i += blockDim.x) {
+    if (i < nq4) cpa16(reinterpret_cast<float4*>(qs) + i, q4 + i);
+    else if (i < nq4 + d4) cpa16(reinterpret_cast<float4*>(kn) + (i - nq4), k4 + (i - nq4));
+    else cpa16(reinterpret_cast<float4*>(vn) + (i - nq4 - d4), v4 + (i - nq4 - d4));
+  }
+  if (kb < ke) dec_tile_finish<KT>(d, kb, min(kTile, ke - kb), pos, ks, vs, raw);
+  cpa_wait_all();
+  __syncthreads();
+  // NeoX rotation in place (rope.rs:145-184): y0 = x0*c - x1*s, y1 = x1*c + x0*s
+  for (int i = threadIdx.x; i < (G + (has_new ? 1 : 0)) * half; i += blockDim.x) {
+    const int h = i / half, p = i - h * half;
+    float* x = h < G ? qs + h * d : kn;
+    const float x0 = x[p], x1 = x[p + half];
+    x[p] = __fsub_rn(__fmul_rn(x0, cs[p]), __fmul_rn(x1, sn[p]));
+    x[p + half] = __fadd_rn(__fmul_rn(x1, cs[p]), __fmul_rn(x0, sn[p]));
+  }
+  __syncthreads();
+  if (has_new) {
+    for (int e = threadIdx.x; e < d; e += blockDim.x) {
+      const KT kq = kv_from<KT>(kn[e]), vq = kv_from<KT>(vn[e]);
+      kc[(size_t)pos * d + e] = kq;  // KvCache::store for this position
+      vc[(size_t)pos * d + e] = vq;
+      kn[e] = kv_load<KT>(&kq);
+      vn[e] = kv_load<KT>(&vq);
+      if (pos - kb < kTile) {
+        ks[(pos - kb) * ds + e] = kn[e];
+        vs[(pos - kb) * ds + e] = vn[e];
+      }
+    }
+    __syncthreads();
+  }
+
+  float4 acc[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
+  float m_run = -INFINITY, l_run = 0.0f;
+  for (int t0 = kb; t0 < ke; t0 += kTile) {
+    const int nk = min(kTile, ke - t0);
+    if (t0 != kb) {  // later tiles
+      __syncthreads();
+      dec_tile_issue<KT>(kc, vc, d, t0, nk, pos, ks, vs, raw);
+      dec_tile_finish<KT>(d, t0, nk, pos, ks, vs, raw);
+      if (has_new && pos >= t0 && pos < t0 + nk)
+        for (int e = threadIdx.x; e < d; e += blockDim.x) {
+          ks[(pos - t0) * ds + e] = kn[e];
+          vs[(pos - t0) * ds + e] = vn[e];
+        }
+      __syncthreads();
+    }
+    if (warp < G) {
+      const float* qh = qs + warp * d;
+      float sc = -INFINITY;
+      if (lane < nk) {
+        const float* kr = ks + lane * ds;
+        float p0 = 0.f, p1 = 0.f, p2 = 0.f, p3 = 0.f;
+        for (int e = 0; e < d; e += 4) {
+          const float4 q = *reinterpret_cast<const float4*>(qh + e);
+          const float4 k = *reinterpret_cast<const float4*>(kr + e);
+          p0 = fmaf(q.x, k.x, p0);
+          p1 = fmaf(q.y, k.y, p1);
+          p2 = fmaf(q.z, k.z, p2);
+          p3 = fmaf(q.w, k.w, p3);
+        }
+        sc = __fmul_rn((p0 + p1) + (p2 + p3), a.scale);
+      }
+      const float mn = fmaxf(m_run, warp_max(sc));
+      const float cf = expf(m_run - mn);  // 0 on the first tile (m_run = -inf)
+      const float p = lane < nk ? expf(sc - mn) : 0.0f;
+      l_run = fmaf(l_run, cf, warp_sum(p));
+      m_run = mn;
+      for (int j = 0; j < 2; ++j) {
+        acc[j].x *= cf;
+        acc[j].y *= cf;
+        acc[j].z *= cf;
+        acc[j].w *= cf;
+      }
+      for (int t = 0; t < nk; ++t) {
+        const float pt = __shfl_sync(0xffffffffu, p, t);
+        for (int j = 0; j < 2; ++j) {
+          const int e = 4 * lane + 128 * j;
+          if (e < d) {
+            const float4 v = *reinterpret_cast<const float4*>(vs + t * ds + e);
+            acc[j].x = fmaf(pt, v.x, acc[j].x);
+            acc[j].y = fmaf(pt, v.y, acc[j].y);
+            acc[j].z = fmaf(pt, v.z, acc[j].z);
+            acc[j].w = fmaf(pt, v.w, acc[j].w);
+          }
+        }
+      }
+    }
+  }
+  const size_t pb = ((size_t)g * ns + s) * G;  // partial row of (g, s, head 0)
+  if (warp < G) {
+    for (int j = 0; j < 2; ++j) {
+      const int e = 4 * lane + 128 * j;
+      if (e < d) *reinterpret_cast<float4*>(a.part_o + (pb + warp) * d + e) = acc[j];
+    }
+    if (lane == 0) {
+      a.part_m[pb + warp] = m_run;
+      a.part_l[pb + warp] = l_run;
+    }
+  }
+  if (!a.defer_merge) {
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) last_block = atomicAdd(a.counters + g, 1u) == (unsigned)(ns - 1);
+    __syncthreads();
+    if (last_block) {
+      __threadfence();
+      // warp h merges head h over the splits that hold keys, in split order
+      const int ne = min(ns, (pos + a.chunk) / a.chunk);
+      if (warp < G) {
+        float M = -INFINITY;
+        for (int q = 0; q < ne; ++q) M = fmaxf(M, __ldcg(a.part_m + ((size_t)g * ns + q) * G + warp));
+        float L = 0.0f;
+        float4 O[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
+        for (int q = 0; q < ne; ++q) {
+          const size_t r = ((size_t)g * ns + q) * G + warp;
+          const float mq = __ldcg(a.part_m + r);
+          const float f = mq == -INFINITY ? 0.0f : expf(mq - M);
+          L = fmaf(__ldcg(a.part_l + r), f, L);
+          for (int j = 0; j < 2; ++j) {
+            const int e = 4 * lane + 128 * j;
+            if (e < d) {
+              const float4 o = __ldcg(reinterpret_cast<const float4*>(a.part_o + r * d + e));
+              O[j].x = fmaf(o.x, f, O[j].x);
+              O[j].y = fmaf(o.y, f, O[j].y);
+              O[j].z = fmaf(o.z, f, O[j].z);
+              O[j].w = fmaf(o.w, f, O[j].w);
+            }
+          }
+        }
+        for (int j = 0; j < 2; ++j) {
+          const int e = 4 * lane + 128 * j;
+          if (e < d)
+            *reinterpret_cast<float4*>(a.out + ((size_t)g * G + warp) * d + e) =
+                make_float4(__fdiv_rn(O[j].x, L), __fdiv_rn(O[j].y, L), __fdiv_rn(O[j].z, L),
+                            __fdiv_rn(O[j].w, L));
+        }
+      }
+      if (threadIdx.x == 0) a.counters[g] = 0u;
+    }
+  }
+  if (a.tr.buf) {  // block-uniform
+    __syncthreads();
+    trace_end(trow);
+  }
 }
 
 // ------------------------------------------------------------------ small kernels
@@ -988,6 +1384,16 @@ static int gemv_kind() {
 }
 static bool getenv_legacy() { return gemv_kind() == 2; }
 
+// MYOS_ATTN=tiled selects the general attention kernel for decode too.
+static bool attn_compact() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("MYOS_ATTN");
+    v = !(e && e[0] == 't');
+  }
+  return v != 0;
+}
+
 static cudaLaunchConfig_t make_cfg(dim3 grid, dim3 block, size_t smem, cudaStream_t st,
                                    bool pdl, cudaLaunchAttribute* attr) {
   cudaLaunchConfig_t cfg = {};
@@ -1063,7 +1469,9 @@ int gemv_grid(int M, int K, int NR, int num_sms) {
     const int cap = num_sms * env_int("MYOS_BULK_GRID_MULT", 1);
     return g < cap ? (g < 1 ? 1 : g) : cap;
   }
-  int g = (M + 7) / 8;
+  // Up to two blocks per SM, at least MYOS_GEMV_MIN_ROWS (8) rows a block.
+  const int min_rows = env_int("MYOS_GEMV_MIN_ROWS", 8);
+  int g = (M + min_rows - 1) / min_rows;
   if (g > 2 * num_sms) g = 2 * num_sms;
   return g < 1 ? 1 : g;
 }
@@ -1071,7 +1479,8 @@ int gemv_grid(int M, int K, int NR, int num_sms) {
 cudaError_t launch_gemv(int epi, const GemvArgs& a0, int grid, cudaStream_t st, bool pdl) {
   cudaLaunchAttribute attr[1];
   const bool bulk_ok = (a0.K % 256) == 0 && ((uintptr_t)a0.w & 15) == 0 &&
-                       (epi != EPI_SWIGLU || ((uintptr_t)a0.w2 & 15) == 0) && gemv_kind() == 0;
+                       (epi != EPI_SWIGLU || ((uintptr_t)a0.w2 & 15) == 0) && gemv_kind() == 0 &&
+                       !a0.in.part_o;
   if (bulk_ok) {
     GemvArgs a = a0;
     const int NR = epi == EPI_SWIGLU ? 2 : 1;
@@ -1089,7 +1498,9 @@ cudaError_t launch_gemv(int epi, const GemvArgs& a0, int grid, cudaStream_t st, 
     return cudaErrorInvalidValue;
   }
   const GemvArgs& a = a0;
-  cudaLaunchConfig_t cfg = make_cfg(dim3(grid), dim3(kThreads), gemv_smem_bytes(a.K), st, pdl, attr);
+  size_t smem = gemv_smem_bytes(a.K);
+  if (a.in.part_o) smem += merge_smem_bytes(a.K / a.in.m_d, a.in.m_nsplit, a.in.m_d);
+  cudaLaunchConfig_t cfg = make_cfg(dim3(grid), dim3(kThreads), smem, st, pdl, attr);
   const bool stream = (a.K % 256) == 0 && ((uintptr_t)a.w & 15) == 0 &&
                       (epi != EPI_SWIGLU || ((uintptr_t)a.w2 & 15) == 0) && !getenv_legacy();
   if (stream) {
@@ -1116,8 +1527,14 @@ cudaError_t launch_gemv(int epi, const GemvArgs& a0, int grid, cudaStream_t st, 
 int attn_dpl(int d) { return d <= 32 ? 1 : d <= 64 ? 2 : d <= 128 ? 4 : 8; }
 
 size_t attn_smem_bytes(int G, int d) {
-  // qs, two padded tiles, probabilities, corrections, new K/V row
-  return (size_t)(G * d + 2 * kTile * (d + 4) + G * kTile + kMaxG + 2 * d) * sizeof(float);
+  // qs, two padded tiles, probabilities, corrections, new K/V row, raw q,
+  // rotation row, raw new K/V
+  return (size_t)(2 * G * d + 2 * kTile * (d + 4) + G * kTile + kMaxG + 5 * d) * sizeof(float);
+}
+
+size_t merge_smem_bytes(int Hq, int nsplit, int d) {
+  // partials [Hq*nsplit*d], factors and sums [2*Hq*nsplit], per-head totals [Hq]
+  return ((size_t)Hq * nsplit * d + 2 * (size_t)Hq * nsplit + Hq) * sizeof(float);
 }
 
 template <int DPL>
@@ -1129,6 +1546,12 @@ static cudaError_t launch_attn_dpl(const AttnArgs& a, int kv_bf16, cudaLaunchCon
 cudaError_t launch_attention(const AttnArgs& a, int kv_bf16, cudaStream_t st, bool pdl) {
   if (a.G > kMaxG || a.d > 256 || a.d <= 0) return cudaErrorInvalidValue;
   cudaLaunchAttribute attr[1];
+  if (a.decode && a.d % 8 == 0 && attn_compact()) {
+    cudaLaunchConfig_t cfg = make_cfg(dim3(a.nsplit, a.Hkv), dim3(kThreads),
+                                      attn_dec_smem_bytes(a.G, a.d), st, pdl, attr);
+    if (kv_bf16) return cudaLaunchKernelEx(&cfg, k_attn_dec<__nv_bfloat16>, a);
+    return cudaLaunchKernelEx(&cfg, k_attn_dec<float>, a);
+  }
   // The split merge reuses the tile buffers for (2 nsplit + 1) * G floats.
   size_t smem = attn_smem_bytes(a.G, a.d);
   const size_t merge = (size_t)(2 * a.nsplit + 1) * a.G * sizeof(float);
@@ -1215,6 +1638,8 @@ cudaError_t kernels_init() {
   MYOS_SET((k_gemv_bulk<EPI_RESID, 1>), gemv_max)
   MYOS_SET((k_gemv_bulk<EPI_SWIGLU, 2>), gemv_max)
   MYOS_SET((k_gemv_bulk<EPI_ARGMAX, 1>), gemv_max)
+  MYOS_SET(k_attn_dec<float>, attn_max)
+  MYOS_SET(k_attn_dec<__nv_bfloat16>, attn_max)
   MYOS_SET((k_attn<1, float>), attn_max)
   MYOS_SET((k_attn<2, float>), attn_max)
   MYOS_SET((k_attn<4, float>), attn_max)

@@ -18,6 +18,17 @@ struct StepCtl {
   uint32_t pad[3];
 };
 
+// Optional launch timeline (diagnostics): per (step mod kTraceSteps, slot)
+// kTraceWidth u64 %globaltimer stamps: earliest block start, earliest return
+// from the dependency wait, latest block end, then kernel-specific latest
+// stage marks. Null buf disables it.
+constexpr int kTraceSteps = 64;
+constexpr int kTraceWidth = 8;
+struct KTrace {
+  uint64_t* buf;
+  int slot, nslot;
+};
+
 // How a GEMV block stages its input vector in shared memory.
 struct GemvInput {
   const float* x;         // f32 [K] (ignored in embed mode)
@@ -27,6 +38,13 @@ struct GemvInput {
   float* x_store;         // embed mode: block 0 writes the gathered row here
   const float* gamma;     // RMSNorm weight (promoted f32) or null
   float eps;
+  // Attention-merge mode (o_proj input, decode): x is the merge of the
+  // split-KV partials [Hkv][nsplit][G][d] of the splits that hold keys
+  // 0..ctl->pos; the staging does the merge the attention kernel deferred.
+  const float* part_o;    // non-null selects this mode
+  const float* part_m;
+  const float* part_l;
+  int m_G, m_d, m_nsplit, m_chunk;
 };
 
 enum EpiKind { EPI_STORE = 0, EPI_BIAS = 1, EPI_RESID = 2, EPI_SWIGLU = 3, EPI_ARGMAX = 4 };
@@ -51,6 +69,7 @@ struct GemvArgs {
   int nst;             // stages in the shared-memory ring
   int lookahead;       // stages prefetched into L2 beyond the ring
   uint32_t* err;       // bounded-wait failure bits (nullable)
+  KTrace tr;
 };
 
 struct AttnArgs {
@@ -71,7 +90,13 @@ struct AttnArgs {
   unsigned* counters;    // [Hkv], zero between launches
   float* out;            // [Hq*d]
   int decode;
+  int defer_merge;       // decode: write the split partials only; the o_proj
+                         // staging merges them (GemvInput attention-merge mode)
+  KTrace tr;
 };
+
+// Shared memory of the attention-merge staging beyond the staged input.
+size_t merge_smem_bytes(int Hq, int nsplit, int d);
 
 // Launchers. pdl=true attaches a programmatic-serialization edge to the
 // previous launch in the stream.
