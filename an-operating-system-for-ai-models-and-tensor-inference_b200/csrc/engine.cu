@@ -89,6 +89,7 @@ struct myos_ctx {
   int grid_qkv = 0, grid_o = 0, grid_gu = 0, grid_down = 0, grid_head = 0;
   int attn_chunk = 0, attn_nsplit = 0;
   int defer_merge = 0;  // o_proj staging merges the attention splits
+  int l2pf_mode = 0;    // MYOS_L2PF: qkv kernels prefetch the layer's MLP weights into L2
   size_t prefetch_total = 0;  // bulk L2 prefetch (MYOS_PREFETCH_MB); measured slower, off
   // loaded-tensor bookkeeping
   std::vector<uint8_t> have;  // per layer x suffix, then embed, final norm, lm_head
@@ -260,6 +261,14 @@ int launch_kind(myos_ctx* c, int kind, int l, const uint32_t* feed, bool pdl, bo
     q.err = &c->ctl->err;
     q.prefetch_cap = prefetch_cap(c, c->grid_qkv);
     q.tr = ktrace_at(c, 5 * l + K_QKV);
+    if (c->l2pf_mode) {  // this layer's MLP weights, for gate/up and down
+      const size_t mat = (size_t)I * H * 2;
+      q.pf_ptr[0] = w.wg;
+      q.pf_ptr[1] = w.wu;
+      q.pf_ptr[2] = w.wd;
+      q.pf_bytes[0] = q.pf_bytes[1] = q.pf_bytes[2] = mat;
+      q.pf_mode = c->l2pf_mode;
+    }
     CK(launch_gemv(EPI_BIAS, q, c->grid_qkv, c->st, pdl));
   } else if (kind == K_ATTN) {
     AttnArgs at = {};
@@ -605,6 +614,8 @@ static int create_impl(myos_ctx* c, const myos_shape* shape, const myos_opts* op
     // then reads all partials; measured slower for the 1.5B step).
     const char* e = getenv("MYOS_DEFER_MERGE");
     const bool want = e && e[0] == '1';
+    const char* pf = getenv("MYOS_L2PF");
+    c->l2pf_mode = pf ? atoi(pf) : 0;
     c->defer_merge = want && s.num_q_heads <= 256 &&
                      merge_smem_bytes((int)s.num_q_heads, (int)nsplit, (int)d) <= (96u << 10);
   }

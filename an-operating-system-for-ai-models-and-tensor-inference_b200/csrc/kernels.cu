@@ -417,6 +417,23 @@ __global__ void __launch_bounds__(kThreads) k_gemv(GemvArgs a) {
 // is in flight while batch b is consumed, across row boundaries. Batch 0 is
 // issued before the programmatic-dependency wait, so its DRAM latency
 // overlaps the predecessor kernel and the input staging.
+// This block's slice of each range in a.pf_ptr, requested into L2.
+MYOS_DEV void l2_prefetch_slices(const GemvArgs& a) {
+  for (int r = 0; r < 3; ++r) {
+    if (!a.pf_ptr[r]) continue;
+    const size_t n = a.pf_bytes[r];
+    const size_t b0 = (n * blockIdx.x / gridDim.x) & ~(size_t)127;
+    const size_t b1 = blockIdx.x + 1 == gridDim.x ? n : (n * (blockIdx.x + 1) / gridDim.x) & ~(size_t)127;
+    const char* base = static_cast<const char*>(a.pf_ptr[r]);
+    if (a.pf_mode == 1) {
+      for (size_t o = b0 + (size_t)threadIdx.x * 128; o < b1; o += (size_t)blockDim.x * 128)
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(base + o));
+    } else {
+      prefetch_range(base + b0, b1 - b0);
+    }
+  }
+}
+
 template <int NR, int U>
 MYOS_DEV void load_batch(uint4 (&buf)[NR][U], const uint16_t* const* wbase, int K, int row,
                          int j0, int P, int lane) {
@@ -463,6 +480,7 @@ __global__ void __launch_bounds__(kThreads, 2) k_gemv_stream(GemvArgs a) {
   const uint64_t t_start = a.tr.buf ? global_ns() : 0;
   uint4 cur[NR][U], nxt[NR][U];
   if (nb > 0) load_batch<NR, U>(cur, wbase, a.K, r0 + warp, 0, P, lane);
+  if (a.pf_mode) l2_prefetch_slices(a);
   pdl_wait();
   pdl_launch();
   uint64_t* trow = trace_begin(a.tr, a.in.ctl, t_start);

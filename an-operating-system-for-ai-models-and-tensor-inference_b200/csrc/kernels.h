@@ -70,6 +70,12 @@ struct GemvArgs {
   int lookahead;       // stages prefetched into L2 beyond the ring
   uint32_t* err;       // bounded-wait failure bits (nullable)
   KTrace tr;
+  // Weights of later kernels to pull into L2 while this one waits on its
+  // inputs (each block takes an equal slice of each range); pf_mode 1: one
+  // prefetch per 128-byte line from every thread, 2: bulk prefetches.
+  const void* pf_ptr[3];
+  size_t pf_bytes[3];
+  int pf_mode;
 };
 
 struct AttnArgs {
