@@ -90,6 +90,7 @@ struct myos_ctx {
   int attn_chunk = 0, attn_nsplit = 0;
   int defer_merge = 0;  // o_proj staging merges the attention splits
   int l2pf_mode = 0;    // MYOS_L2PF: qkv kernels prefetch the layer's MLP weights into L2
+  int attn_cluster = 0; // attention splits merge across a thread-block cluster
   size_t prefetch_total = 0;  // bulk L2 prefetch (MYOS_PREFETCH_MB); measured slower, off
   // loaded-tensor bookkeeping
   std::vector<uint8_t> have;  // per layer x suffix, then embed, final norm, lm_head
@@ -293,6 +294,7 @@ int launch_kind(myos_ctx* c, int kind, int l, const uint32_t* feed, bool pdl, bo
     at.out = c->attn;
     at.decode = 1;
     at.defer_merge = c->defer_merge;
+    at.cluster = c->attn_cluster;
     at.tr = ktrace_at(c, 5 * l + K_ATTN);
     CK(launch_attention(at, kv_bf16, c->st, pdl));
   } else if (kind == K_O) {
@@ -618,6 +620,9 @@ static int create_impl(myos_ctx* c, const myos_shape* shape, const myos_opts* op
     c->l2pf_mode = pf ? atoi(pf) : 0;
     c->defer_merge = want && s.num_q_heads <= 256 &&
                      merge_smem_bytes((int)s.num_q_heads, (int)nsplit, (int)d) <= (96u << 10);
+    // MYOS_ATTN_CLUSTER=0 keeps the global-memory last-block merge
+    const char* ce = getenv("MYOS_ATTN_CLUSTER");
+    c->attn_cluster = !(ce && ce[0] == '0') && !c->defer_merge && nsplit <= 8 && d % 8 == 0;
   }
   // workspace
   CK(cudaMalloc(&c->resid, H * 4));

@@ -17,8 +17,12 @@
 #include <math.h>
 #include <stdlib.h>
 
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 #include "kernels.h"
+
+namespace cg = cooperative_groups;
 
 namespace myos {
 
@@ -1097,9 +1101,87 @@ MYOS_DEV void dec_tile_finish(int d, int t0, int nk, int skip, float* ks, float*
 }
 
 size_t attn_dec_smem_bytes(int G, int d) {
-  // q, two padded tiles, new k/v, rotation row, raw bf16 tile rows
-  return ((size_t)G * d + 2 * kTile * (d + 4) + 3 * (size_t)d + (size_t)kTile * d) * sizeof(float);
+  // q, two padded tiles, new k/v, rotation row, raw bf16 tile rows, and the
+  // block's partial (output, max, sum) for the cluster merge
+  return ((size_t)G * d + 2 * kTile * (d + 4) + 3 * (size_t)d + (size_t)kTile * d +
+          (size_t)G * d + 2 * kMaxG) * sizeof(float);
 }
+
+// One warp merges one head over the splits q < ne that hold keys:
+// M = max m_q, f_q = expf(m_q - M), L = sum l_q f_q, out = (sum o_q f_q) / L
+// (the reference's e / sum, gqa.rs:283-307, reassociated). Lane q holds split
+// q's max and sum (32 splits per round); the outputs accumulate in split
+// order, 8 splits' loads in flight at a time. src.m(q), src.l(q) and
+// src.o(q, e) read split q's partial (float4 at dim e).
+template <class Src>
+MYOS_DEV void merge_head(const Src& src, int ne, int d, int lane, float* out) {
+  float M = -INFINITY;
+  for (int q0 = 0; q0 < ne; q0 += 32)
+    M = fmaxf(M, warp_max(q0 + lane < ne ? src.m(q0 + lane) : -INFINITY));
+  float Lp = 0.0f;
+  float4 O[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
+  for (int q0 = 0; q0 < ne; q0 += 32) {
+    const int q = q0 + lane;
+    const float mq = q < ne ? src.m(q) : -INFINITY;
+    const float f = mq == -INFINITY ? 0.0f : expf(mq - M);
+    if (q < ne) Lp = fmaf(src.l(q), f, Lp);
+    const int nr = min(32, ne - q0);
+    for (int u0 = 0; u0 < nr; u0 += 8) {
+      float4 po[2][8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int e = 4 * lane + 128 * j;
+          po[j][u] = (u0 + u < nr && e < d) ? src.o(q0 + u0 + u, e) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const float fu = __shfl_sync(0xffffffffu, f, (u0 + u) & 31);
+        if (u0 + u < nr)
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            O[j].x = fmaf(po[j][u].x, fu, O[j].x);
+            O[j].y = fmaf(po[j][u].y, fu, O[j].y);
+            O[j].z = fmaf(po[j][u].z, fu, O[j].z);
+            O[j].w = fmaf(po[j][u].w, fu, O[j].w);
+          }
+      }
+    }
+  }
+  const float L = warp_sum(Lp);
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int e = 4 * lane + 128 * j;
+    if (e < d)
+      *reinterpret_cast<float4*>(out + e) = make_float4(
+          __fdiv_rn(O[j].x, L), __fdiv_rn(O[j].y, L), __fdiv_rn(O[j].z, L), __fdiv_rn(O[j].w, L));
+  }
+}
+
+// Split partials in global memory (head row r(q) = (g*ns + q)*G + h).
+struct GlobalPartials {
+  const float *pm, *pl, *po;
+  size_t base;  // (g*ns)*G + h
+  int G, d;
+  MYOS_DEV size_t row(int q) const { return base + (size_t)q * G; }
+  MYOS_DEV float m(int q) const { return __ldcg(pm + row(q)); }
+  MYOS_DEV float l(int q) const { return __ldcg(pl + row(q)); }
+  MYOS_DEV float4 o(int q, int e) const {
+    return __ldcg(reinterpret_cast<const float4*>(po + row(q) * d + e));
+  }
+};
+
+// Split partials in the shared memory of the cluster's blocks (rank q = split q).
+struct ClusterPartials {
+  float *pso, *psm, *psl;  // this block's copies; peers hold theirs at the same offsets
+  int h, d;
+  MYOS_DEV float m(int q) const { return cg::this_cluster().map_shared_rank(psm, q)[h]; }
+  MYOS_DEV float l(int q) const { return cg::this_cluster().map_shared_rank(psl, q)[h]; }
+  MYOS_DEV float4 o(int q, int e) const {
+    return *reinterpret_cast<const float4*>(cg::this_cluster().map_shared_rank(pso, q) + h * d + e);
+  }
+};
 
 template <typename KT>
 __global__ void __launch_bounds__(kThreads) k_attn_dec(AttnArgs a) {
@@ -1232,56 +1314,57 @@ __global__ void __launch_bounds__(kThreads) k_attn_dec(AttnArgs a) {
       }
     }
   }
-  const size_t pb = ((size_t)g * ns + s) * G;  // partial row of (g, s, head 0)
-  if (warp < G) {
-    for (int j = 0; j < 2; ++j) {
-      const int e = 4 * lane + 128 * j;
-      if (e < d) *reinterpret_cast<float4*>(a.part_o + (pb + warp) * d + e) = acc[j];
-    }
-    if (lane == 0) {
-      a.part_m[pb + warp] = m_run;
-      a.part_l[pb + warp] = l_run;
-    }
-  }
-  if (!a.defer_merge) {
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) last_block = atomicAdd(a.counters + g, 1u) == (unsigned)(ns - 1);
-    __syncthreads();
-    if (last_block) {
-      __threadfence();
-      // warp h merges head h over the splits that hold keys, in split order
-      const int ne = min(ns, (pos + a.chunk) / a.chunk);
-      if (warp < G) {
-        float M = -INFINITY;
-        for (int q = 0; q < ne; ++q) M = fmaxf(M, __ldcg(a.part_m + ((size_t)g * ns + q) * G + warp));
-        float L = 0.0f;
-        float4 O[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
-        for (int q = 0; q < ne; ++q) {
-          const size_t r = ((size_t)g * ns + q) * G + warp;
-          const float mq = __ldcg(a.part_m + r);
-          const float f = mq == -INFINITY ? 0.0f : expf(mq - M);
-          L = fmaf(__ldcg(a.part_l + r), f, L);
-          for (int j = 0; j < 2; ++j) {
-            const int e = 4 * lane + 128 * j;
-            if (e < d) {
-              const float4 o = __ldcg(reinterpret_cast<const float4*>(a.part_o + r * d + e));
-              O[j].x = fmaf(o.x, f, O[j].x);
-              O[j].y = fmaf(o.y, f, O[j].y);
-              O[j].z = fmaf(o.z, f, O[j].z);
-              O[j].w = fmaf(o.w, f, O[j].w);
-            }
-          }
-        }
-        for (int j = 0; j < 2; ++j) {
-          const int e = 4 * lane + 128 * j;
-          if (e < d)
-            *reinterpret_cast<float4*>(a.out + ((size_t)g * G + warp) * d + e) =
-                make_float4(__fdiv_rn(O[j].x, L), __fdiv_rn(O[j].y, L), __fdiv_rn(O[j].z, L),
-                            __fdiv_rn(O[j].w, L));
-        }
+  const int ne = min(ns, (pos + a.chunk) / a.chunk);  // splits that hold keys
+  if (a.cluster) {
+    // The blocks of KV head g form one cluster (rank = split): partials stay
+    // in shared memory and the merge reads them across the cluster.
+    float* pso = reinterpret_cast<float*>(raw) + kTile * d;  // [G][d]
+    float* psm = pso + G * d;                                // [kMaxG]
+    float* psl = psm + kMaxG;
+    if (warp < G) {
+      for (int j = 0; j < 2; ++j) {
+        const int e = 4 * lane + 128 * j;
+        if (e < d) *reinterpret_cast<float4*>(pso + warp * d + e) = acc[j];
       }
-      if (threadIdx.x == 0) a.counters[g] = 0u;
+      if (lane == 0) {
+        psm[warp] = m_run;
+        psl[warp] = l_run;
+      }
+    }
+    cg::this_cluster().sync();
+    // block s merges heads s, s + ns, ... one warp each
+    const int h = s + ns * warp;
+    if (h < G) {
+      ClusterPartials src = {pso, psm, psl, h, d};
+      merge_head(src, ne, d, lane, a.out + ((size_t)g * G + h) * d);
+    }
+    cg::this_cluster().sync();  // peers' shared memory stays valid until every read is done
+  } else {
+    const size_t pb = ((size_t)g * ns + s) * G;  // partial row of (g, s, head 0)
+    if (warp < G) {
+      for (int j = 0; j < 2; ++j) {
+        const int e = 4 * lane + 128 * j;
+        if (e < d) *reinterpret_cast<float4*>(a.part_o + (pb + warp) * d + e) = acc[j];
+      }
+      if (lane == 0) {
+        a.part_m[pb + warp] = m_run;
+        a.part_l[pb + warp] = l_run;
+      }
+    }
+    if (!a.defer_merge) {
+      __threadfence();
+      __syncthreads();
+      if (threadIdx.x == 0) last_block = atomicAdd(a.counters + g, 1u) == (unsigned)(ns - 1);
+      __syncthreads();
+      if (last_block) {
+        __threadfence();
+        // warp h merges head h over the splits that hold keys, in split order
+        if (warp < G) {
+          GlobalPartials src = {a.part_m, a.part_l, a.part_o, (size_t)g * ns * G + warp, G, d};
+          merge_head(src, ne, d, lane, a.out + ((size_t)g * G + warp) * d);
+        }
+        if (threadIdx.x == 0) a.counters[g] = 0u;
+      }
     }
   }
   if (a.tr.buf) {  // block-uniform
@@ -1565,8 +1648,17 @@ cudaError_t launch_attention(const AttnArgs& a, int kv_bf16, cudaStream_t st, bo
   if (a.G > kMaxG || a.d > 256 || a.d <= 0) return cudaErrorInvalidValue;
   cudaLaunchAttribute attr[1];
   if (a.decode && a.d % 8 == 0 && attn_compact()) {
+    if (a.cluster && (a.nsplit > 8 || a.defer_merge)) return cudaErrorInvalidValue;
+    cudaLaunchAttribute attrs[2];
     cudaLaunchConfig_t cfg = make_cfg(dim3(a.nsplit, a.Hkv), dim3(kThreads),
-                                      attn_dec_smem_bytes(a.G, a.d), st, pdl, attr);
+                                      attn_dec_smem_bytes(a.G, a.d), st, pdl, attrs);
+    if (a.cluster) {
+      attrs[cfg.numAttrs].id = cudaLaunchAttributeClusterDimension;
+      attrs[cfg.numAttrs].val.clusterDim.x = a.nsplit;
+      attrs[cfg.numAttrs].val.clusterDim.y = 1;
+      attrs[cfg.numAttrs].val.clusterDim.z = 1;
+      ++cfg.numAttrs;
+    }
     if (kv_bf16) return cudaLaunchKernelEx(&cfg, k_attn_dec<__nv_bfloat16>, a);
     return cudaLaunchKernelEx(&cfg, k_attn_dec<float>, a);
   }

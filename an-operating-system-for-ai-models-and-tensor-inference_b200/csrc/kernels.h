@@ -98,6 +98,8 @@ struct AttnArgs {
   int decode;
   int defer_merge;       // decode: write the split partials only; the o_proj
                          // staging merges them (GemvInput attention-merge mode)
+  int cluster;           // decode, nsplit <= 8: the splits of a KV head form one
+                         // thread-block cluster and merge through shared memory
   KTrace tr;
 };
 
