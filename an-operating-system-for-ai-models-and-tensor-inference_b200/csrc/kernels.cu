@@ -141,6 +141,100 @@ MYOS_DEV void stage_merge(float* xs, int K, bool vec, const GemvInput& in, float
   __syncthreads();
 }
 
+// Staging for K % 256 == 0 in one round trip. Thread t owns chunks
+// c = t + i*blockDim.x (8 values: 4 at xs[4c], 4 at xs[K/2 + 4c]); all its
+// x (or bf16 embedding) loads are issued at once (K <= kStageOne * 8 *
+// blockDim.x). The RMSNorm weight of the thread's chunks arrives in
+// registers, loaded before the dependency wait (it depends on no kernel);
+// the norm y = gamma * (x * inv), inv = 1 / sqrtf(mean(x^2) + eps)
+// (bf16.rs:231-270) then needs one block reduction and no further load.
+constexpr int kStageOne = 5;
+constexpr int kGammaRegs = 3;
+
+template <int NG>
+MYOS_DEV void gamma_preload(const GemvInput& in, int K, float4 (&g0)[NG], float4 (&g1)[NG]) {
+#pragma unroll
+  for (int i = 0; i < NG; ++i) {
+    const int c = threadIdx.x + i * blockDim.x;
+    if (c < (K >> 3)) {
+      g0[i] = ldg4(in.gamma + 8 * c);
+      g1[i] = ldg4(in.gamma + 8 * c + 4);
+    }
+  }
+}
+
+template <int NG>
+MYOS_DEV void stage_one_trip(float* xs, int K, const GemvInput& in, float* red, bool has_g,
+                             const float4 (&g0)[NG], const float4 (&g1)[NG]) {
+  const int nt = blockDim.x, nchunk = K >> 3, half = K >> 1;
+  float4* xlo = reinterpret_cast<float4*>(xs);
+  float4* xhi = reinterpret_cast<float4*>(xs + half);
+  const uint16_t* erow = nullptr;
+  if (in.embed) {
+    const uint32_t tok = in.feed ? in.feed[in.ctl->step] : in.ctl->argmax;
+    erow = in.embed + (size_t)tok * (size_t)K;
+    if (blockIdx.x == 0 && threadIdx.x == 0) in.ctl->fed = tok;
+  }
+  float4 lo[kStageOne], hi[kStageOne];
+#pragma unroll
+  for (int i = 0; i < kStageOne; ++i) {
+    const int c = threadIdx.x + i * nt;
+    if (c < nchunk) {
+      if (erow) {
+        unpack8(__ldg(reinterpret_cast<const uint4*>(erow) + c), lo[i], hi[i]);
+      } else {
+        lo[i] = ldcg4(in.x + 8 * c);
+        hi[i] = ldcg4(in.x + 8 * c + 4);
+      }
+    }
+  }
+  if (erow && in.x_store && blockIdx.x == 0) {  // block 0 also stores the embedding row
+#pragma unroll
+    for (int i = 0; i < kStageOne; ++i) {
+      const int c = threadIdx.x + i * nt;
+      if (c < nchunk) {
+        reinterpret_cast<float4*>(in.x_store)[2 * c] = lo[i];
+        reinterpret_cast<float4*>(in.x_store)[2 * c + 1] = hi[i];
+      }
+    }
+  }
+  if (has_g) {
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kStageOne; ++i) {
+      if (threadIdx.x + i * nt < nchunk) {
+        ss = fmaf(lo[i].x, lo[i].x, ss);
+        ss = fmaf(lo[i].y, lo[i].y, ss);
+        ss = fmaf(lo[i].z, lo[i].z, ss);
+        ss = fmaf(lo[i].w, lo[i].w, ss);
+        ss = fmaf(hi[i].x, hi[i].x, ss);
+        ss = fmaf(hi[i].y, hi[i].y, ss);
+        ss = fmaf(hi[i].z, hi[i].z, ss);
+        ss = fmaf(hi[i].w, hi[i].w, ss);
+      }
+    }
+    ss = block_sum(ss, red);
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), in.eps)));
+#pragma unroll
+    for (int i = 0; i < NG; ++i) {
+      const float4 a = lo[i], b = hi[i], ga = g0[i], gb = g1[i];
+      lo[i] = make_float4(__fmul_rn(ga.x, __fmul_rn(a.x, inv)), __fmul_rn(ga.y, __fmul_rn(a.y, inv)),
+                          __fmul_rn(ga.z, __fmul_rn(a.z, inv)), __fmul_rn(ga.w, __fmul_rn(a.w, inv)));
+      hi[i] = make_float4(__fmul_rn(gb.x, __fmul_rn(b.x, inv)), __fmul_rn(gb.y, __fmul_rn(b.y, inv)),
+                          __fmul_rn(gb.z, __fmul_rn(b.z, inv)), __fmul_rn(gb.w, __fmul_rn(b.w, inv)));
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < kStageOne; ++i) {
+    const int c = threadIdx.x + i * nt;
+    if (c < nchunk) {
+      xlo[c] = lo[i];
+      xhi[c] = hi[i];
+    }
+  }
+  __syncthreads();
+}
+
 MYOS_DEV void stage_input(float* xs, int K, bool vec, const GemvInput& in, float* red) {
   const int nt = blockDim.x;
   if (in.part_o) {
@@ -482,13 +576,20 @@ __global__ void __launch_bounds__(kThreads, 2) k_gemv_stream(GemvArgs a) {
     for (int r = 0; r < NR; ++r) prefetch_range(wbase[r] + (size_t)r0 * a.K, bytes);
   }
   const uint64_t t_start = a.tr.buf ? global_ns() : 0;
+  // one-trip staging when the thread's chunks fit the register budget
+  const int nchunk = a.K >> 3, nt = blockDim.x;
+  const bool has_g = a.in.gamma != nullptr;
+  const bool one = !a.in.part_o && nchunk <= kStageOne * nt && (!has_g || nchunk <= kGammaRegs * nt);
+  float4 g0[kGammaRegs], g1[kGammaRegs];
+  if (one && has_g) gamma_preload<kGammaRegs>(a.in, a.K, g0, g1);
   uint4 cur[NR][U], nxt[NR][U];
   if (nb > 0) load_batch<NR, U>(cur, wbase, a.K, r0 + warp, 0, P, lane);
   if (a.pf_mode) l2_prefetch_slices(a);
   pdl_wait();
   pdl_launch();
   uint64_t* trow = trace_begin(a.tr, a.in.ctl, t_start);
-  stage_input(xs, a.K, true, a.in, red);
+  if (one) stage_one_trip<kGammaRegs>(xs, a.K, a.in, red, has_g, g0, g1);
+  else stage_input(xs, a.K, true, a.in, red);
   trace_mark(trow, 3);  // input staged
 
   const float4* xlo = reinterpret_cast<const float4*>(xs);
