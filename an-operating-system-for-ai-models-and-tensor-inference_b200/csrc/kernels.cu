@@ -1216,6 +1216,43 @@ size_t attn_dec_smem_bytes(int G, int d) {
 // src.o(q, e) read split q's partial (float4 at dim e).
 template <class Src>
 MYOS_DEV void merge_head(const Src& src, int ne, int d, int lane, float* out) {
+  if (ne <= 8) {
+    // one round of loads: the outputs, maxima and sums of every split at once
+    float4 po[2][8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int e = 4 * lane + 128 * j;
+        po[j][u] = (u < ne && e < d) ? src.o(u, e) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    const float mq = lane < ne ? src.m(lane) : -INFINITY;
+    const float lq = lane < ne ? src.l(lane) : 0.0f;
+    const float M = warp_max(mq);
+    const float f = mq == -INFINITY ? 0.0f : expf(mq - M);
+    const float L = warp_sum(lq * f);
+    float4 O[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const float fu = __shfl_sync(0xffffffffu, f, u);
+      if (u < ne)
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          O[j].x = fmaf(po[j][u].x, fu, O[j].x);
+          O[j].y = fmaf(po[j][u].y, fu, O[j].y);
+          O[j].z = fmaf(po[j][u].z, fu, O[j].z);
+          O[j].w = fmaf(po[j][u].w, fu, O[j].w);
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int e = 4 * lane + 128 * j;
+      if (e < d)
+        *reinterpret_cast<float4*>(out + e) = make_float4(
+            __fdiv_rn(O[j].x, L), __fdiv_rn(O[j].y, L), __fdiv_rn(O[j].z, L), __fdiv_rn(O[j].w, L));
+    }
+    return;
+  }
   float M = -INFINITY;
   for (int q0 = 0; q0 < ne; q0 += 32)
     M = fmaxf(M, warp_max(q0 + lane < ne ? src.m(q0 + lane) : -INFINITY));
@@ -1284,11 +1321,12 @@ struct ClusterPartials {
   }
 };
 
-template <typename KT>
+template <typename KT, int D>
 __global__ void __launch_bounds__(kThreads) k_attn_dec(AttnArgs a) {
   extern __shared__ float4 smem4[];
   float* sm = reinterpret_cast<float*>(smem4);
-  const int d = a.d, G = a.G, half = d >> 1, ds = d + 4;
+  constexpr int d = D, half = D / 2, ds = D + 4;  // head dim fixed at compile time
+  const int G = a.G;
   float* qs = sm;                   // [G][d]
   float* ks = qs + G * d;           // [kTile][ds]
   float* vs = ks + kTile * ds;      // [kTile][ds]
@@ -1334,6 +1372,7 @@ __global__ void __launch_bounds__(kThreads) k_attn_dec(AttnArgs a) {
   if (kb < ke) dec_tile_finish<KT>(d, kb, min(kTile, ke - kb), pos, ks, vs, raw);
   cpa_wait_all();
   __syncthreads();
+  trace_mark(trow, 3);  // q, new k/v and the first tile in shared memory
   // NeoX rotation in place (rope.rs:145-184): y0 = x0*c - x1*s, y1 = x1*c + x0*s
   for (int i = threadIdx.x; i < (G + (has_new ? 1 : 0)) * half; i += blockDim.x) {
     const int h = i / half, p = i - h * half;
@@ -1358,6 +1397,7 @@ __global__ void __launch_bounds__(kThreads) k_attn_dec(AttnArgs a) {
     __syncthreads();
   }
 
+  trace_mark(trow, 4);  // rotated, new key stored
   float4 acc[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
   float m_run = -INFINITY, l_run = 0.0f;
   for (int t0 = kb; t0 < ke; t0 += kTile) {
@@ -1379,6 +1419,7 @@ __global__ void __launch_bounds__(kThreads) k_attn_dec(AttnArgs a) {
       if (lane < nk) {
         const float* kr = ks + lane * ds;
         float p0 = 0.f, p1 = 0.f, p2 = 0.f, p3 = 0.f;
+#pragma unroll
         for (int e = 0; e < d; e += 4) {
           const float4 q = *reinterpret_cast<const float4*>(qh + e);
           const float4 k = *reinterpret_cast<const float4*>(kr + e);
@@ -1400,8 +1441,10 @@ __global__ void __launch_bounds__(kThreads) k_attn_dec(AttnArgs a) {
         acc[j].z *= cf;
         acc[j].w *= cf;
       }
+#pragma unroll 8
       for (int t = 0; t < nk; ++t) {
         const float pt = __shfl_sync(0xffffffffu, p, t);
+#pragma unroll
         for (int j = 0; j < 2; ++j) {
           const int e = 4 * lane + 128 * j;
           if (e < d) {
@@ -1415,6 +1458,7 @@ __global__ void __launch_bounds__(kThreads) k_attn_dec(AttnArgs a) {
       }
     }
   }
+  trace_mark(trow, 5);  // tiles done
   const int ne = min(ns, (pos + a.chunk) / a.chunk);  // splits that hold keys
   if (a.cluster) {
     // The blocks of KV head g form one cluster (rank = split): partials stay
@@ -1433,12 +1477,14 @@ __global__ void __launch_bounds__(kThreads) k_attn_dec(AttnArgs a) {
       }
     }
     cg::this_cluster().sync();
+    trace_mark(trow, 6);  // partials visible across the cluster
     // block s merges heads s, s + ns, ... one warp each
     const int h = s + ns * warp;
     if (h < G) {
       ClusterPartials src = {pso, psm, psl, h, d};
       merge_head(src, ne, d, lane, a.out + ((size_t)g * G + h) * d);
     }
+    trace_mark(trow, 7);  // merged
     cg::this_cluster().sync();  // peers' shared memory stays valid until every read is done
   } else {
     const size_t pb = ((size_t)g * ns + s) * G;  // partial row of (g, s, head 0)
@@ -1748,7 +1794,7 @@ static cudaError_t launch_attn_dpl(const AttnArgs& a, int kv_bf16, cudaLaunchCon
 cudaError_t launch_attention(const AttnArgs& a, int kv_bf16, cudaStream_t st, bool pdl) {
   if (a.G > kMaxG || a.d > 256 || a.d <= 0) return cudaErrorInvalidValue;
   cudaLaunchAttribute attr[1];
-  if (a.decode && a.d % 8 == 0 && attn_compact()) {
+  if (a.decode && (a.d == 64 || a.d == 128 || a.d == 256) && attn_compact()) {
     if (a.cluster && (a.nsplit > 8 || a.defer_merge)) return cudaErrorInvalidValue;
     cudaLaunchAttribute attrs[2];
     cudaLaunchConfig_t cfg = make_cfg(dim3(a.nsplit, a.Hkv), dim3(kThreads),
@@ -1760,8 +1806,15 @@ cudaError_t launch_attention(const AttnArgs& a, int kv_bf16, cudaStream_t st, bo
       attrs[cfg.numAttrs].val.clusterDim.z = 1;
       ++cfg.numAttrs;
     }
-    if (kv_bf16) return cudaLaunchKernelEx(&cfg, k_attn_dec<__nv_bfloat16>, a);
-    return cudaLaunchKernelEx(&cfg, k_attn_dec<float>, a);
+    switch (a.d) {
+      case 64: return kv_bf16 ? cudaLaunchKernelEx(&cfg, k_attn_dec<__nv_bfloat16, 64>, a)
+                              : cudaLaunchKernelEx(&cfg, k_attn_dec<float, 64>, a);
+      case 128: return kv_bf16 ? cudaLaunchKernelEx(&cfg, k_attn_dec<__nv_bfloat16, 128>, a)
+                               : cudaLaunchKernelEx(&cfg, k_attn_dec<float, 128>, a);
+      case 256: return kv_bf16 ? cudaLaunchKernelEx(&cfg, k_attn_dec<__nv_bfloat16, 256>, a)
+                               : cudaLaunchKernelEx(&cfg, k_attn_dec<float, 256>, a);
+    }
+    return cudaErrorInvalidValue;
   }
   // The split merge reuses the tile buffers for (2 nsplit + 1) * G floats.
   size_t smem = attn_smem_bytes(a.G, a.d);
@@ -1849,8 +1902,12 @@ cudaError_t kernels_init() {
   MYOS_SET((k_gemv_bulk<EPI_RESID, 1>), gemv_max)
   MYOS_SET((k_gemv_bulk<EPI_SWIGLU, 2>), gemv_max)
   MYOS_SET((k_gemv_bulk<EPI_ARGMAX, 1>), gemv_max)
-  MYOS_SET(k_attn_dec<float>, attn_max)
-  MYOS_SET(k_attn_dec<__nv_bfloat16>, attn_max)
+  MYOS_SET((k_attn_dec<float, 64>), attn_max)
+  MYOS_SET((k_attn_dec<__nv_bfloat16, 64>), attn_max)
+  MYOS_SET((k_attn_dec<float, 128>), attn_max)
+  MYOS_SET((k_attn_dec<__nv_bfloat16, 128>), attn_max)
+  MYOS_SET((k_attn_dec<float, 256>), attn_max)
+  MYOS_SET((k_attn_dec<__nv_bfloat16, 256>), attn_max)
   MYOS_SET((k_attn<1, float>), attn_max)
   MYOS_SET((k_attn<2, float>), attn_max)
   MYOS_SET((k_attn<4, float>), attn_max)
