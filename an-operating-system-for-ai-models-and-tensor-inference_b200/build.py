@@ -25,9 +25,22 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",
                      "-Xcompiler", "-fvisibility=hidden", "-I" + INCLUDE,
                      "--expt-relaxed-constexpr"]
+
+
+def cutlass_include() -> list:
+    """CUTLASS/CuTe header trees (SM100 collectives) vendored in the Python
+    environment; only gemm_sm100.cu includes them."""
+    import site
+    for sp in site.getsitepackages():
+        root = os.path.join(sp, "flashinfer", "data", "cutlass")
+        if os.path.exists(os.path.join(root, "include", "cutlass", "version.h")):
+            return ["-I" + os.path.join(root, "include"),
+                    "-I" + os.path.join(root, "tools", "util", "include")]
+    raise RuntimeError("CUTLASS headers (sm100 collectives) not found")
 CUDA_SOURCES = ["kernels.cu", "step_kernel.cu", "engine.cu", "ops.cu", "noalloc.cu",
-                "safetensors.cpp"]
-HEADERS = ["common.cuh", "kernels.h", "safetensors.h", "step_kernel.h"]
+                "prefill.cu", "gemm_sm100.cu", "safetensors.cpp"]
+HEADERS = ["common.cuh", "kernels.h", "safetensors.h", "step_kernel.h", "prefill.h",
+           "gemm_sm100.h"]
 
 
 def nvcc() -> str:
@@ -62,6 +75,8 @@ def build(force: bool = False, verbose: bool = False) -> dict:
         objs.append(o)
         if force or _stale(o, [s] + hdrs):
             cmd = [nvcc()] + NVCC_FLAGS + ["-c", s, "-o", o]
+            if src == "gemm_sm100.cu":
+                cmd = [nvcc()] + NVCC_FLAGS + cutlass_include() + ["-c", s, "-o", o]
             if src.endswith(".cpp"):
                 cmd = [nvcc()] + NVCC_FLAGS + ["-x", "cu", "-c", s, "-o", o]
             if verbose:

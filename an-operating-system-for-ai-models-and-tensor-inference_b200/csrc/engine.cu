@@ -20,13 +20,16 @@
 #include <sys/stat.h>
 #include <unistd.h>
 
+#include <algorithm>
 #include <map>
 #include <memory>
 #include <string>
 #include <vector>
 
 #include "../../include/myos_cuda.h"
+#include "gemm_sm100.h"
 #include "kernels.h"
+#include "prefill.h"
 #include "safetensors.h"
 #include "step_kernel.h"
 
@@ -91,6 +94,13 @@ struct myos_ctx {
   int defer_merge = 0;  // o_proj staging merges the attention splits
   int l2pf_mode = 0;    // MYOS_L2PF: qkv kernels prefetch the layer's MLP weights into L2
   int attn_cluster = 0; // attention splits merge across a thread-block cluster
+  // GEMM prefill (chunks of pf_chunk prompt tokens through the tensor cores)
+  bool pf_ok = false;
+  int pf_chunk = 0;
+  float *pf_X = nullptr, *pf_D = nullptr, *pf_Q = nullptr, *pf_att = nullptr;
+  uint16_t* pf_A = nullptr;
+  void* pf_ws = nullptr;
+  size_t pf_ws_bytes = 0;
   size_t prefetch_total = 0;  // bulk L2 prefetch (MYOS_PREFETCH_MB); measured slower, off
   // loaded-tensor bookkeeping
   std::vector<uint8_t> have;  // per layer x suffix, then embed, final norm, lm_head
@@ -735,6 +745,34 @@ static int create_impl(myos_ctx* c, const myos_shape* shape, const myos_opts* op
       }
     }
   }
+  {
+    // GEMM prefill: hidden, q and MLP widths 16-byte aligned for TMA, gate and
+    // up rows adjacent (one [2I, H] projection), a supported head dim.
+    const char* e = getenv("MYOS_PREFILL");
+    const bool want = !(e && e[0] == 's');
+    bool ok = want && pf_attn_supported((int)d, (int)c->G) && H % 64 == 0 && I % 64 == 0 &&
+              c->qd % 64 == 0 && (c->qd + 2 * c->kvd) % 64 == 0;
+    for (size_t l = 0; ok && l < L; ++l) ok = c->layers[l].wu == c->layers[l].wg + I * H;
+    if (ok) {
+      const int nc = 128;
+      const size_t M = 2 * (size_t)nc;
+      const size_t kmax = std::max(H, std::max((size_t)c->qd, I));
+      const size_t nmax = std::max(c->qd + 2 * c->kvd, std::max(H, 2 * I));
+      const int shapes[4][2] = {{(int)(c->qd + 2 * c->kvd), (int)H}, {(int)H, (int)c->qd},
+                                {(int)(2 * I), (int)H}, {(int)H, (int)I}};
+      size_t ws = 256;
+      for (auto& sh : shapes) ws = std::max(ws, gemm_workspace_bytes((int)M, sh[0], sh[1]));
+      CK(cudaMalloc(&c->pf_X, (size_t)nc * H * 4));
+      CK(cudaMalloc(&c->pf_A, M * kmax * 2));
+      CK(cudaMalloc(&c->pf_D, M * nmax * 4));
+      CK(cudaMalloc(&c->pf_Q, (size_t)nc * (c->qd + 2 * c->kvd) * 4));
+      CK(cudaMalloc(&c->pf_att, (size_t)nc * c->qd * 4));
+      CK(cudaMalloc(&c->pf_ws, ws));
+      c->pf_ws_bytes = ws;
+      c->pf_chunk = nc;
+      c->pf_ok = true;
+    }
+  }
   if (const char* kf = getenv("MYOS_KTRACE_FILE")) {
     c->ktrace_file = kf;
     const size_t rows = (size_t)kTraceSteps * (5 * L + 1);
@@ -788,7 +826,7 @@ void myos_ctx_destroy(myos_ctx* c) {
                  c->part_val, c->part_idx, c->part_o, c->part_m, c->part_l, c->counters, c->ctl,
                  c->feed, c->rec_fed, c->rec_argmax, c->cos_t, c->sin_t, c->d_layers, c->bar,
                  (void*)c->margs.part_val, (void*)c->margs.part_idx, (void*)c->trace,
-                 (void*)c->ktrace};
+                 (void*)c->ktrace, c->pf_X, c->pf_D, c->pf_Q, c->pf_att, c->pf_A, c->pf_ws};
   for (void* p : dev)
     if (p) cudaFree(p);
   for (int i = 0; i < 2; ++i) {
@@ -1112,6 +1150,46 @@ int myos_forward_token(myos_ctx* c, uint32_t token, size_t pos, float* logits) {
   return MYOS_OK;
 }
 
+// One chunk of n prompt tokens at positions p0.. through every layer
+// (GEMM prefill); leaves the chunk's residual rows in pf_X and their K/V in
+// the cache.
+int prefill_chunk(myos_ctx* c, const uint32_t* d_ids, int n, int p0) {
+  const myos_shape& s = c->s;
+  const int H = (int)s.hidden, I = (int)s.intermediate, qd = (int)c->qd;
+  const int Nq = (int)(c->qd + 2 * c->kvd), Hq = (int)s.num_q_heads, Hkv = (int)s.num_kv_heads;
+  const int d = (int)s.head_dim, S = (int)c->o.max_seq, M = 2 * n;
+  const int kv_bf16 = c->o.kv_dtype == MYOS_KV_BF16;
+  const size_t kv_elt = kv_bf16 ? 2 : 4;
+  const float scale = 1.0f / sqrtf((float)d);
+  cudaStream_t st = c->st;
+  auto gemm = [&](int N, int K, const uint16_t* W) {
+    const cudaError_t e =
+        gemm_bf16_f32(M, N, K, c->pf_A, W, nullptr, c->pf_D, 0.0f, c->pf_ws, c->pf_ws_bytes, st);
+    return e == cudaSuccess ? MYOS_OK : fail(c, MYOS_ERR_CUDA, std::string("prefill gemm: ") + cudaGetErrorString(e));
+  };
+  int rc;
+  CK(pf_embed(c->pf_X, c->embed, d_ids, n, H, st));
+  for (int l = 0; l < (int)s.num_layers; ++l) {
+    const LayerW& w = c->layers[l];
+    void* kc = (uint8_t*)c->kcache + (size_t)l * c->kv_layer_elems * kv_elt;
+    void* vc = (uint8_t*)c->vcache + (size_t)l * c->kv_layer_elems * kv_elt;
+    CK(pf_norm_split(c->pf_A, c->pf_X, w.ln1, n, H, s.rms_eps, st));
+    if ((rc = gemm(Nq, H, w.wqkv))) return rc;
+    CK(pf_bias(c->pf_Q, c->pf_D, w.bqkv, n, Nq, st));
+    CK(pf_rope_store(c->pf_Q, kc, vc, kv_bf16, c->cos_t, c->sin_t, p0, n, Hq, Hkv, d, S, st));
+    CK(pf_attn(c->pf_att, c->pf_Q, kc, vc, kv_bf16, p0, n, Hq, Hkv, d, S, scale, st));
+    CK(pf_norm_split(c->pf_A, c->pf_att, nullptr, n, qd, 0.0f, st));
+    if ((rc = gemm(H, qd, w.wo))) return rc;
+    CK(pf_resid(c->pf_X, c->pf_D, n, H, st));
+    CK(pf_norm_split(c->pf_A, c->pf_X, w.ln2, n, H, s.rms_eps, st));
+    if ((rc = gemm(2 * I, H, w.wg))) return rc;  // gate rows then up rows
+    CK(pf_swiglu_split(c->pf_A, c->pf_D, n, I, st));
+    if ((rc = gemm(H, I, w.wd))) return rc;
+    CK(pf_resid(c->pf_X, c->pf_D, n, H, st));
+  }
+  return MYOS_OK;
+}
+
 int myos_prefill(myos_ctx* c, const uint32_t* ids, size_t n, float* logits) {
   if (!c) return MYOS_ERR_ARG;
   if (n == 0 || !ids) return fail(c, MYOS_ERR_SHAPE, "block shape does not match the buffers");
@@ -1125,8 +1203,22 @@ int myos_prefill(myos_ctx* c, const uint32_t* ids, size_t n, float* logits) {
   CK(cudaMemcpyAsync(c->feed, ids, n * 4, cudaMemcpyHostToDevice, c->st));
   if ((st = set_ctl(c, false))) return st;
   CK(cudaEventRecord(c->ev0, c->st));
-  if (n > 1 && (st = run_steps(c, G_FEED_NOHEAD, n - 1))) return st;
-  if ((st = run_steps(c, G_FEED_HEAD, 1))) return st;
+  if (c->pf_ok && n > 1) {
+    // all prompt tokens through the GEMM path; the head on the last one
+    for (size_t c0 = 0; c0 < n; c0 += (size_t)c->pf_chunk) {
+      const int nc = (int)std::min((size_t)c->pf_chunk, n - c0);
+      if ((st = prefill_chunk(c, c->feed + c0, nc, (int)(start + c0)))) return st;
+      if (c0 + nc == n)
+        CK(cudaMemcpyAsync(c->resid, c->pf_X + (size_t)(nc - 1) * c->s.hidden, c->s.hidden * 4,
+                           cudaMemcpyDeviceToDevice, c->st));
+    }
+    c->ctl_host->pos = (uint32_t)(start + n - 1);
+    CK(cudaMemcpyAsync(&c->ctl->pos, &c->ctl_host->pos, 4, cudaMemcpyHostToDevice, c->st));
+    if ((st = launch_kind(c, K_HEAD, 0, nullptr, false, false))) return st;
+  } else {
+    if (n > 1 && (st = run_steps(c, G_FEED_NOHEAD, n - 1))) return st;
+    if ((st = run_steps(c, G_FEED_HEAD, 1))) return st;
+  }
   CK(cudaEventRecord(c->ev1, c->st));
   if (logits) CK(cudaMemcpyAsync(logits, c->logits, (size_t)c->s.vocab * 4, cudaMemcpyDeviceToHost, c->st));
   if ((st = finish(c))) return st;

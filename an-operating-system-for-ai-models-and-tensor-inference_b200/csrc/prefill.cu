@@ -1,0 +1,283 @@
+// Prefill of a chunk of n prompt tokens as dense projections (gemm_sm100.cu)
+// with these kernels around them; the structure of the reference's prefill
+// (crates/model_core/src/qwen25_block.rs:323-543): GEMM QKV, per-token bias,
+// RoPE and KV store, per-position causal GQA, GEMM o_proj + residual,
+// RMSNorm, GEMM gate|up, SwiGLU, GEMM down + residual.
+//
+// Activations reach the tensor cores as stacked bf16 halves: row t of A is
+// hi = bf16(x_t) and row n + t is lo = bf16(x_t - hi) (both exact
+// roundings), so D[t] + D[n + t] is the projection of the activation to 16
+// mantissa bits with exact products. The element-wise steps keep the
+// reference's operation order (no contraction).
+#include <math.h>
+
+#include "common.cuh"
+#include "prefill.h"
+
+namespace myos {
+namespace {
+
+constexpr int kT = 256;
+
+MYOS_DEV uint16_t bf16_rn(float v) {
+  return __bfloat16_as_ushort(__float2bfloat16_rn(v));
+}
+
+MYOS_DEV void put_split(uint16_t* A, int n, int t, int K, int j, float y) {
+  const uint16_t hi = bf16_rn(y);
+  const float hv = __uint_as_float((uint32_t)hi << 16);
+  A[(size_t)t * K + j] = hi;
+  A[(size_t)(n + t) * K + j] = bf16_rn(__fsub_rn(y, hv));
+}
+
+MYOS_DEV float bsum(float v, float* red) { return block_sum(v, red); }
+
+// X[t] = embedding row of ids[t] (exact promotion).
+__global__ void k_pf_embed(float* X, const uint16_t* embed, const uint32_t* ids, int K) {
+  const int t = blockIdx.x;
+  const uint16_t* row = embed + (size_t)ids[t] * K;
+  for (int j = threadIdx.x; j < K; j += blockDim.x) X[(size_t)t * K + j] = bf16_at(row + j);
+}
+
+// A[t], A[n + t] = halves of gamma * (x * inv), inv = 1 / sqrtf(mean(x^2) + eps)
+// (bf16.rs:231-270); gamma null: halves of x.
+__global__ void __launch_bounds__(kT) k_pf_norm_split(uint16_t* A, const float* X, const float* gamma,
+                                                      int n, int K, float eps) {
+  __shared__ float red[33];
+  const int t = blockIdx.x;
+  const float* x = X + (size_t)t * K;
+  float inv = 1.0f;
+  if (gamma) {
+    float ss = 0.0f;
+    for (int j = threadIdx.x; j < K; j += blockDim.x) ss = fmaf(x[j], x[j], ss);
+    ss = bsum(ss, red);
+    inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), eps)));
+  }
+  for (int j = threadIdx.x; j < K; j += blockDim.x)
+    put_split(A, n, t, K, j, gamma ? __fmul_rn(gamma[j], __fmul_rn(x[j], inv)) : x[j]);
+}
+
+// Q[t] = (D[t] + D[n + t]) + bias: the projection, then the bias (bf16.rs:147-158).
+__global__ void k_pf_bias(float* Q, const float* D, const float* bias, int n, int N) {
+  const int t = blockIdx.x;
+  for (int j = threadIdx.x; j < N; j += blockDim.x)
+    Q[(size_t)t * N + j] =
+        __fadd_rn(__fadd_rn(D[(size_t)t * N + j], D[(size_t)(n + t) * N + j]), bias[j]);
+}
+
+// NeoX rotation of token t's q heads and KV heads at position p0 + t
+// (rope.rs:145-184), then K and V stored at that slot (KvCache::store_at).
+template <typename KT>
+__global__ void k_pf_rope_store(float* Q, KT* kc, KT* vc, const float* cos_t, const float* sin_t,
+                                int p0, int Hq, int Hkv, int d, int S, size_t layer_elems) {
+  const int t = blockIdx.x, pos = p0 + t, half = d >> 1, N = (Hq + 2 * Hkv) * d;
+  float* q = Q + (size_t)t * N;
+  const float* cs = cos_t + (size_t)pos * half;
+  const float* sn = sin_t + (size_t)pos * half;
+  for (int i = threadIdx.x; i < (Hq + Hkv) * half; i += blockDim.x) {
+    const int h = i / half, p = i - h * half;
+    float* x = q + h * d;  // heads 0..Hq-1 are q, Hq.. are k
+    const float x0 = x[p], x1 = x[p + half];
+    x[p] = __fsub_rn(__fmul_rn(x0, cs[p]), __fmul_rn(x1, sn[p]));
+    x[p + half] = __fadd_rn(__fmul_rn(x1, cs[p]), __fmul_rn(x0, sn[p]));
+  }
+  __syncthreads();
+  (void)layer_elems;
+  for (int i = threadIdx.x; i < Hkv * d; i += blockDim.x) {
+    const int g = i / d, e = i - g * d;
+    const size_t slot = ((size_t)g * S + pos) * d + e;
+    if constexpr (sizeof(KT) == 4) {
+      kc[slot] = q[(Hq + g) * d + e];
+      vc[slot] = q[(Hq + Hkv + g) * d + e];
+    } else {
+      kc[slot] = __float2bfloat16_rn(q[(Hq + g) * d + e]);
+      vc[slot] = __float2bfloat16_rn(q[(Hq + Hkv + g) * d + e]);
+    }
+  }
+}
+
+template <typename KT>
+MYOS_DEV float4 kv4(const KT* p);
+template <>
+MYOS_DEV float4 kv4<float>(const float* p) {
+  return __ldcg(reinterpret_cast<const float4*>(p));
+}
+template <>
+MYOS_DEV float4 kv4<__nv_bfloat16>(const __nv_bfloat16* p) {
+  const uint2 u = __ldcg(reinterpret_cast<const uint2*>(p));
+  return make_float4(bf16_lo(u.x), bf16_hi(u.x), bf16_lo(u.y), bf16_hi(u.y));
+}
+
+// Causal GQA for token t (position p0 + t) and KV head g: keys 0..pos from
+// the cache, online softmax over tiles of 32 (one warp per query head, lane
+// per key), p * v accumulated per lane over dims [4 lane, 4 lane + 4)
+// (+128 for d > 128); out = sum / L (gqa.rs:174-218, reassociated).
+template <typename KT, int D>
+__global__ void __launch_bounds__(kT) k_pf_attn(float* out, const float* Q, const KT* kcache,
+                                                const KT* vcache, int p0, int Hq, int Hkv, int S,
+                                                float scale) {
+  constexpr int kTile = 32, ds = D + 4;
+  __shared__ __align__(16) float qs[8 * D];
+  __shared__ __align__(16) float ks[kTile * ds];
+  __shared__ __align__(16) float vs[kTile * ds];
+  const int t = blockIdx.x, g = blockIdx.y, G = Hq / Hkv, pos = p0 + t;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int N = (Hq + 2 * Hkv) * D;
+  const float* q = Q + (size_t)t * N + (size_t)g * G * D;
+  for (int i = threadIdx.x; i < G * D; i += blockDim.x) qs[i] = q[i];
+  const KT* kc = kcache + (size_t)g * S * D;
+  const KT* vc = vcache + (size_t)g * S * D;
+  float4 acc[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
+  float m_run = -INFINITY, l_run = 0.0f;
+  for (int t0 = 0; t0 <= pos; t0 += kTile) {
+    const int nk = min(kTile, pos + 1 - t0);
+    __syncthreads();  // qs staged / previous tile consumed
+    for (int i = threadIdx.x; i < nk * (D / 4); i += blockDim.x) {
+      const int tt = i / (D / 4), e = (i - tt * (D / 4)) * 4;
+      *reinterpret_cast<float4*>(ks + tt * ds + e) = kv4<KT>(kc + (size_t)(t0 + tt) * D + e);
+      *reinterpret_cast<float4*>(vs + tt * ds + e) = kv4<KT>(vc + (size_t)(t0 + tt) * D + e);
+    }
+    __syncthreads();
+    if (warp < G) {
+      const float* qh = qs + warp * D;
+      float sc = -INFINITY;
+      if (lane < nk) {
+        const float* kr = ks + lane * ds;
+        float p0s = 0.f, p1 = 0.f, p2 = 0.f, p3 = 0.f;
+#pragma unroll
+        for (int e = 0; e < D; e += 4) {
+          const float4 a = *reinterpret_cast<const float4*>(qh + e);
+          const float4 b = *reinterpret_cast<const float4*>(kr + e);
+          p0s = fmaf(a.x, b.x, p0s);
+          p1 = fmaf(a.y, b.y, p1);
+          p2 = fmaf(a.z, b.z, p2);
+          p3 = fmaf(a.w, b.w, p3);
+        }
+        sc = __fmul_rn((p0s + p1) + (p2 + p3), scale);
+      }
+      const float mn = fmaxf(m_run, warp_max(sc));
+      const float cf = expf(m_run - mn);
+      const float p = lane < nk ? expf(sc - mn) : 0.0f;
+      l_run = fmaf(l_run, cf, warp_sum(p));
+      m_run = mn;
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        acc[j].x *= cf;
+        acc[j].y *= cf;
+        acc[j].z *= cf;
+        acc[j].w *= cf;
+      }
+#pragma unroll 8
+      for (int k = 0; k < nk; ++k) {
+        const float pk = __shfl_sync(0xffffffffu, p, k);
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int e = 4 * lane + 128 * j;
+          if (e < D) {
+            const float4 v = *reinterpret_cast<const float4*>(vs + k * ds + e);
+            acc[j].x = fmaf(pk, v.x, acc[j].x);
+            acc[j].y = fmaf(pk, v.y, acc[j].y);
+            acc[j].z = fmaf(pk, v.z, acc[j].z);
+            acc[j].w = fmaf(pk, v.w, acc[j].w);
+          }
+        }
+      }
+    }
+  }
+  if (warp < G) {
+    float* o = out + (size_t)t * Hq * D + (size_t)(g * G + warp) * D;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int e = 4 * lane + 128 * j;
+      if (e < D)
+        *reinterpret_cast<float4*>(o + e) =
+            make_float4(__fdiv_rn(acc[j].x, l_run), __fdiv_rn(acc[j].y, l_run),
+                        __fdiv_rn(acc[j].z, l_run), __fdiv_rn(acc[j].w, l_run));
+    }
+  }
+}
+
+// X[t] += D[t] + D[n + t] (residual after o_proj / down_proj).
+__global__ void k_pf_resid(float* X, const float* D, int n, int N) {
+  const int t = blockIdx.x;
+  for (int j = threadIdx.x; j < N; j += blockDim.x)
+    X[(size_t)t * N + j] =
+        __fadd_rn(X[(size_t)t * N + j], __fadd_rn(D[(size_t)t * N + j], D[(size_t)(n + t) * N + j]));
+}
+
+// h = (g / (1 + expf(-g))) * u (swiglu.rs:113-131) from the stacked gate|up
+// projection, written as bf16 halves for the down projection.
+__global__ void k_pf_swiglu_split(uint16_t* A, const float* D, int n, int I) {
+  const int t = blockIdx.x, N = 2 * I;
+  for (int j = threadIdx.x; j < I; j += blockDim.x) {
+    const float g = __fadd_rn(D[(size_t)t * N + j], D[(size_t)(n + t) * N + j]);
+    const float u = __fadd_rn(D[(size_t)t * N + I + j], D[(size_t)(n + t) * N + I + j]);
+    const float s = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
+    put_split(A, n, t, I, j, __fmul_rn(s, u));
+  }
+}
+
+}  // namespace
+
+cudaError_t pf_embed(float* X, const uint16_t* embed, const uint32_t* ids, int n, int K,
+                     cudaStream_t st) {
+  k_pf_embed<<<n, kT, 0, st>>>(X, embed, ids, K);
+  return cudaGetLastError();
+}
+
+cudaError_t pf_norm_split(uint16_t* A, const float* X, const float* gamma, int n, int K, float eps,
+                          cudaStream_t st) {
+  k_pf_norm_split<<<n, kT, 0, st>>>(A, X, gamma, n, K, eps);
+  return cudaGetLastError();
+}
+
+cudaError_t pf_bias(float* Q, const float* D, const float* bias, int n, int N, cudaStream_t st) {
+  k_pf_bias<<<n, kT, 0, st>>>(Q, D, bias, n, N);
+  return cudaGetLastError();
+}
+
+cudaError_t pf_rope_store(float* Q, void* kc, void* vc, int kv_bf16, const float* cos_t,
+                          const float* sin_t, int p0, int n, int Hq, int Hkv, int d, int S,
+                          cudaStream_t st) {
+  if (kv_bf16)
+    k_pf_rope_store<__nv_bfloat16><<<n, kT, 0, st>>>(Q, (__nv_bfloat16*)kc, (__nv_bfloat16*)vc,
+                                                      cos_t, sin_t, p0, Hq, Hkv, d, S, 0);
+  else
+    k_pf_rope_store<float><<<n, kT, 0, st>>>(Q, (float*)kc, (float*)vc, cos_t, sin_t, p0, Hq, Hkv,
+                                             d, S, 0);
+  return cudaGetLastError();
+}
+
+bool pf_attn_supported(int d, int G) { return (d == 64 || d == 128) && G <= 8; }
+
+cudaError_t pf_attn(float* out, const float* Q, const void* kc, const void* vc, int kv_bf16, int p0,
+                    int n, int Hq, int Hkv, int d, int S, float scale, cudaStream_t st) {
+  const dim3 grid(n, Hkv);
+#define MYOS_PF_ATTN(D)                                                                     \
+  if (d == D) {                                                                             \
+    if (kv_bf16)                                                                            \
+      k_pf_attn<__nv_bfloat16, D><<<grid, kT, 0, st>>>(out, Q, (const __nv_bfloat16*)kc,    \
+                                                       (const __nv_bfloat16*)vc, p0, Hq,    \
+                                                       Hkv, S, scale);                      \
+    else                                                                                    \
+      k_pf_attn<float, D><<<grid, kT, 0, st>>>(out, Q, (const float*)kc, (const float*)vc, \
+                                               p0, Hq, Hkv, S, scale);                      \
+    return cudaGetLastError();                                                              \
+  }
+  MYOS_PF_ATTN(64)
+  MYOS_PF_ATTN(128)
+#undef MYOS_PF_ATTN
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t pf_resid(float* X, const float* D, int n, int N, cudaStream_t st) {
+  k_pf_resid<<<n, kT, 0, st>>>(X, D, n, N);
+  return cudaGetLastError();
+}
+
+cudaError_t pf_swiglu_split(uint16_t* A, const float* D, int n, int I, cudaStream_t st) {
+  k_pf_swiglu_split<<<n, kT, 0, st>>>(A, D, n, I);
+  return cudaGetLastError();
+}
+
+}  // namespace myos

@@ -1,0 +1,22 @@
+// Element-wise and attention kernels of the GEMM prefill (prefill.cu).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace myos {
+
+cudaError_t pf_embed(float* X, const uint16_t* embed, const uint32_t* ids, int n, int K,
+                     cudaStream_t st);
+cudaError_t pf_norm_split(uint16_t* A, const float* X, const float* gamma, int n, int K, float eps,
+                          cudaStream_t st);
+cudaError_t pf_bias(float* Q, const float* D, const float* bias, int n, int N, cudaStream_t st);
+cudaError_t pf_rope_store(float* Q, void* kc, void* vc, int kv_bf16, const float* cos_t,
+                          const float* sin_t, int p0, int n, int Hq, int Hkv, int d, int S,
+                          cudaStream_t st);
+bool pf_attn_supported(int d, int G);
+cudaError_t pf_attn(float* out, const float* Q, const void* kc, const void* vc, int kv_bf16, int p0,
+                    int n, int Hq, int Hkv, int d, int S, float scale, cudaStream_t st);
+cudaError_t pf_resid(float* X, const float* D, int n, int N, cudaStream_t st);
+cudaError_t pf_swiglu_split(uint16_t* A, const float* D, int n, int I, cudaStream_t st);
+
+}  // namespace myos

@@ -74,3 +74,27 @@ def test_s1_greedy_ids_and_logits(model, golden, kv, step, monkeypatch):
     bad = [i for i in range(N_GEN) if am[i] != ref[i] and golden["gap"][i] >= atol]
     assert not bad, bad
     np.testing.assert_allclose(e.logits(), golden["final"], atol=atol, rtol=rtol)
+
+
+def test_gemm_prefill_matches_token_steps(model, monkeypatch):
+    """The tensor-core prefill (two 128-token chunks and a ragged third) against
+    the same prompt run as single-token steps: final logits within the logit
+    tolerance and the cached K/V of early, chunk-boundary and last positions
+    close; greedy continuations agree."""
+    shape, table, _ = model
+    prompt = synth.prompt_ids(SEED + 7, 300, shape["vocab"])
+    out = {}
+    for mode in ("gemm", "steps"):
+        monkeypatch.setenv("MYOS_PREFILL", "gemm" if mode == "gemm" else "steps")
+        e = myos.Engine(shape, 320)
+        e.load_table(table)
+        logits = e.prefill(prompt)
+        kv = [e.kv_head(l, h, p) for l, h, p in ((0, 0, 5), (13, 1, 127), (27, 0, 128), (27, 1, 299))]
+        ids = e.greedy_decode(8)
+        out[mode] = (logits, kv, ids)
+        e.close()
+    np.testing.assert_allclose(out["gemm"][0], out["steps"][0], atol=ATOL, rtol=RTOL)
+    for (kg, vg), (ks, vs) in zip(out["gemm"][1], out["steps"][1]):
+        np.testing.assert_allclose(kg, ks, atol=2e-3, rtol=2e-3)
+        np.testing.assert_allclose(vg, vs, atol=2e-3, rtol=2e-3)
+    assert out["gemm"][2].tolist() == out["steps"][2].tolist()
