@@ -101,6 +101,14 @@ struct myos_ctx {
   uint16_t* pf_A = nullptr;
   void* pf_ws = nullptr;
   size_t pf_ws_bytes = 0;
+  // batched decode (myos_batch_generate): per-sequence KV slabs and buffers
+  void *bt_k = nullptr, *bt_v = nullptr;
+  size_t bt_kv_bytes = 0;
+  float *bt_X = nullptr, *bt_D = nullptr;
+  size_t bt_D_bytes = 0;
+  int *bt_pos = nullptr, *bt_rows = nullptr;
+  uint32_t *bt_tok = nullptr, *bt_out = nullptr, *bt_ids = nullptr;
+  size_t bt_out_n = 0, bt_ids_n = 0;
   size_t prefetch_total = 0;  // bulk L2 prefetch (MYOS_PREFETCH_MB); measured slower, off
   // loaded-tensor bookkeeping
   std::vector<uint8_t> have;  // per layer x suffix, then embed, final norm, lm_head
@@ -503,6 +511,17 @@ int missing_weight(myos_ctx* c) {
 }  // namespace
 
 // ================================================================ C ABI
+// (Re)allocates *p to at least `need` bytes; keeps a large enough buffer.
+template <class T>
+static int grow(myos_ctx* c, T** p, size_t* have, size_t need) {
+  if (*have >= need && *p) return MYOS_OK;
+  if (*p) cudaFree(*p);
+  *p = nullptr;
+  CK(cudaMalloc(p, need));
+  *have = need;
+  return MYOS_OK;
+}
+
 extern "C" {
 
 const char* myos_version(void) { return "myos-b200 0.1 (sm_100a)"; }
@@ -826,7 +845,9 @@ void myos_ctx_destroy(myos_ctx* c) {
                  c->part_val, c->part_idx, c->part_o, c->part_m, c->part_l, c->counters, c->ctl,
                  c->feed, c->rec_fed, c->rec_argmax, c->cos_t, c->sin_t, c->d_layers, c->bar,
                  (void*)c->margs.part_val, (void*)c->margs.part_idx, (void*)c->trace,
-                 (void*)c->ktrace, c->pf_X, c->pf_D, c->pf_Q, c->pf_att, c->pf_A, c->pf_ws};
+                 (void*)c->ktrace, c->pf_X, c->pf_D, c->pf_Q, c->pf_att, c->pf_A, c->pf_ws,
+                 c->bt_k, c->bt_v, c->bt_X, c->bt_D, c->bt_pos, c->bt_rows, c->bt_tok,
+                 c->bt_out, c->bt_ids};
   for (void* p : dev)
     if (p) cudaFree(p);
   for (int i = 0; i < 2; ++i) {
@@ -1153,11 +1174,18 @@ int myos_forward_token(myos_ctx* c, uint32_t token, size_t pos, float* logits) {
 // One chunk of n prompt tokens at positions p0.. through every layer
 // (GEMM prefill); leaves the chunk's residual rows in pf_X and their K/V in
 // the cache.
-int prefill_chunk(myos_ctx* c, const uint32_t* d_ids, int n, int p0) {
+int prefill_chunk(myos_ctx* c, const uint32_t* d_ids, int n, int p0, void* kcache = nullptr,
+                  void* vcache = nullptr, int S_ = 0) {
+  // default: the context's own cache; batched decode passes a sequence's slab
   const myos_shape& s = c->s;
   const int H = (int)s.hidden, I = (int)s.intermediate, qd = (int)c->qd;
   const int Nq = (int)(c->qd + 2 * c->kvd), Hq = (int)s.num_q_heads, Hkv = (int)s.num_kv_heads;
-  const int d = (int)s.head_dim, S = (int)c->o.max_seq, M = 2 * n;
+  const int d = (int)s.head_dim, S = S_ ? S_ : (int)c->o.max_seq, M = 2 * n;
+  if (!kcache) {
+    kcache = c->kcache;
+    vcache = c->vcache;
+  }
+  const size_t layer_elems = (size_t)Hkv * S * d;
   const int kv_bf16 = c->o.kv_dtype == MYOS_KV_BF16;
   const size_t kv_elt = kv_bf16 ? 2 : 4;
   const float scale = 1.0f / sqrtf((float)d);
@@ -1171,8 +1199,8 @@ int prefill_chunk(myos_ctx* c, const uint32_t* d_ids, int n, int p0) {
   CK(pf_embed(c->pf_X, c->embed, d_ids, n, H, st));
   for (int l = 0; l < (int)s.num_layers; ++l) {
     const LayerW& w = c->layers[l];
-    void* kc = (uint8_t*)c->kcache + (size_t)l * c->kv_layer_elems * kv_elt;
-    void* vc = (uint8_t*)c->vcache + (size_t)l * c->kv_layer_elems * kv_elt;
+    void* kc = (uint8_t*)kcache + (size_t)l * layer_elems * kv_elt;
+    void* vc = (uint8_t*)vcache + (size_t)l * layer_elems * kv_elt;
     CK(pf_norm_split(c->pf_A, c->pf_X, w.ln1, n, H, s.rms_eps, st));
     if ((rc = gemm(Nq, H, w.wqkv))) return rc;
     CK(pf_bias(c->pf_Q, c->pf_D, w.bqkv, n, Nq, st));
@@ -1187,6 +1215,128 @@ int prefill_chunk(myos_ctx* c, const uint32_t* d_ids, int n, int p0) {
     if ((rc = gemm(H, I, w.wd))) return rc;
     CK(pf_resid(c->pf_X, c->pf_D, n, H, st));
   }
+  return MYOS_OK;
+}
+
+int myos_batch_generate(myos_ctx* c, size_t nseq, const uint32_t* ids, const uint32_t* lens,
+                        size_t steps, uint32_t* out_ids) {
+  if (!c || !ids || !lens || (steps && !out_ids)) return MYOS_ERR_ARG;
+  if (!c->pf_ok) return fail(c, MYOS_ERR_SHAPE, "batched decode needs the tensor-core path's shape");
+  if (nseq == 0 || nseq > (size_t)c->pf_chunk)
+    return fail(c, MYOS_ERR_SHAPE, "batch size must be 1.." + std::to_string(c->pf_chunk));
+  const myos_shape& s = c->s;
+  size_t total = 0, maxlen = 0;
+  for (size_t b = 0; b < nseq; ++b) {
+    if (lens[b] == 0) return fail(c, MYOS_ERR_SHAPE, "block shape does not match the buffers");
+    total += lens[b];
+    maxlen = std::max(maxlen, (size_t)lens[b]);
+  }
+  for (size_t i = 0; i < total; ++i)
+    if (ids[i] >= s.vocab) return fail(c, MYOS_ERR_TOKEN, "token id is out of range");
+  if (maxlen + steps > c->o.max_seq) return fail(c, MYOS_ERR_CACHE_FULL, "kv cache is full");
+  int st = missing_weight(c);
+  if (st) return st;
+  CK(cudaSetDevice(c->device));
+  const int B = (int)nseq, H = (int)s.hidden, I = (int)s.intermediate, qd = (int)c->qd;
+  const int Nq = (int)(c->qd + 2 * c->kvd), Hq = (int)s.num_q_heads, Hkv = (int)s.num_kv_heads;
+  const int d = (int)s.head_dim, V = (int)s.vocab, L = (int)s.num_layers, M = 2 * B;
+  const int Sb = (int)(maxlen + steps);  // slots per sequence
+  const int kv_bf16 = c->o.kv_dtype == MYOS_KV_BF16;
+  const size_t kv_elt = kv_bf16 ? 2 : 4;
+  const size_t layer_elems = (size_t)Hkv * Sb * d, seq_elems = (size_t)L * layer_elems;
+  const float scale = 1.0f / sqrtf((float)d);
+  const uint16_t* head_w = s.tied_head ? c->embed : c->lm_head;
+  cudaStream_t stq = c->st;
+  // buffers (kept for later calls of the same or smaller size)
+  size_t have_k = c->bt_kv_bytes, have_v = c->bt_kv_bytes;
+  if ((st = grow(c, &c->bt_k, &have_k, (size_t)B * seq_elems * kv_elt))) return st;
+  if ((st = grow(c, &c->bt_v, &have_v, (size_t)B * seq_elems * kv_elt))) return st;
+  c->bt_kv_bytes = std::min(have_k, have_v);
+  size_t have_x = c->bt_X ? (size_t)c->pf_chunk * H * 4 : 0;
+  if ((st = grow(c, &c->bt_X, &have_x, (size_t)c->pf_chunk * H * 4))) return st;
+  if ((st = grow(c, &c->bt_D, &c->bt_D_bytes, (size_t)M * V * 4))) return st;
+  size_t have_small = c->bt_pos ? (size_t)c->pf_chunk * 4 : 0;
+  size_t h2 = have_small, h3 = have_small, h4 = have_small;
+  if ((st = grow(c, &c->bt_pos, &have_small, (size_t)c->pf_chunk * 4))) return st;
+  if ((st = grow(c, &c->bt_rows, &h2, (size_t)c->pf_chunk * 4))) return st;
+  if ((st = grow(c, &c->bt_tok, &h3, (size_t)c->pf_chunk * 4))) return st;
+  (void)h4;
+  size_t have_out = c->bt_out_n * 4, have_ids = c->bt_ids_n * 4;
+  if ((st = grow(c, &c->bt_out, &have_out, std::max<size_t>(1, (size_t)B * steps) * 4))) return st;
+  c->bt_out_n = have_out / 4;
+  if ((st = grow(c, &c->bt_ids, &have_ids, total * 4))) return st;
+  c->bt_ids_n = have_ids / 4;
+  const size_t ws = gemm_workspace_bytes(M, V, H);
+  if (ws > c->pf_ws_bytes && (st = grow(c, &c->pf_ws, &c->pf_ws_bytes, ws))) return st;
+
+  CK(cudaStreamWaitEvent(stq, c->load_ev, 0));
+  CK(cudaMemcpyAsync(c->bt_ids, ids, total * 4, cudaMemcpyHostToDevice, stq));
+  std::vector<int> pos(B);
+  CK(cudaEventRecord(c->ev0, stq));
+  // 1. each prompt through the GEMM prefill into its own slab; its last
+  //    residual row becomes row b of the batch
+  size_t off = 0;
+  for (int b = 0; b < B; ++b) {
+    void* kb = (uint8_t*)c->bt_k + (size_t)b * seq_elems * kv_elt;
+    void* vb = (uint8_t*)c->bt_v + (size_t)b * seq_elems * kv_elt;
+    for (size_t c0 = 0; c0 < lens[b]; c0 += (size_t)c->pf_chunk) {
+      const int nc = (int)std::min((size_t)c->pf_chunk, lens[b] - c0);
+      if ((st = prefill_chunk(c, c->bt_ids + off + c0, nc, (int)c0, kb, vb, Sb))) return st;
+      if (c0 + nc == lens[b])
+        CK(cudaMemcpyAsync(c->bt_X + (size_t)b * H, c->pf_X + (size_t)(nc - 1) * H, (size_t)H * 4,
+                           cudaMemcpyDeviceToDevice, stq));
+    }
+    off += lens[b];
+    pos[b] = (int)lens[b];
+  }
+  CK(cudaMemcpyAsync(c->bt_pos, pos.data(), (size_t)B * 4, cudaMemcpyHostToDevice, stq));
+  auto head = [&](int step) -> int {
+    CK(pf_norm_split(c->pf_A, c->bt_X, c->final_norm, B, H, s.rms_eps, stq));
+    const cudaError_t e = gemm_bf16_f32(M, V, H, c->pf_A, head_w, nullptr, c->bt_D, 0.0f, c->pf_ws,
+                                        c->pf_ws_bytes, stq);
+    if (e != cudaSuccess) return fail(c, MYOS_ERR_CUDA, std::string("batch head gemm: ") + cudaGetErrorString(e));
+    CK(pf_row_argmax(c->bt_tok, step < (int)steps ? c->bt_out : nullptr, (int)steps, step, c->bt_D, B,
+                     V, stq));
+    return MYOS_OK;
+  };
+  auto gemm = [&](int N, int K, const uint16_t* W) -> int {
+    const cudaError_t e =
+        gemm_bf16_f32(M, N, K, c->pf_A, W, nullptr, c->pf_D, 0.0f, c->pf_ws, c->pf_ws_bytes, stq);
+    return e == cudaSuccess ? MYOS_OK : fail(c, MYOS_ERR_CUDA, std::string("batch gemm: ") + cudaGetErrorString(e));
+  };
+  // 2. greedy: token s of every sequence is the argmax of its current
+  //    logits; each is then forwarded (model_core greedy_decode, per sequence)
+  if ((st = head(0))) return st;
+  for (size_t step = 0; step < steps; ++step) {
+    CK(pf_embed(c->bt_X, c->embed, c->bt_tok, B, H, stq));
+    for (int l = 0; l < L; ++l) {
+      const LayerW& w = c->layers[l];
+      void* kc = (uint8_t*)c->bt_k + (size_t)l * layer_elems * kv_elt;
+      void* vc = (uint8_t*)c->bt_v + (size_t)l * layer_elems * kv_elt;
+      CK(pf_norm_split(c->pf_A, c->bt_X, w.ln1, B, H, s.rms_eps, stq));
+      if ((st = gemm(Nq, H, w.wqkv))) return st;
+      CK(pf_bias(c->pf_Q, c->pf_D, w.bqkv, B, Nq, stq));
+      CK(pf_rope_store(c->pf_Q, kc, vc, kv_bf16, c->cos_t, c->sin_t, 0, B, Hq, Hkv, d, Sb, stq,
+                       c->bt_pos, seq_elems));
+      CK(pf_attn(c->pf_att, c->pf_Q, kc, vc, kv_bf16, 0, B, Hq, Hkv, d, Sb, scale, stq, c->bt_pos,
+                 seq_elems));
+      CK(pf_norm_split(c->pf_A, c->pf_att, nullptr, B, qd, 0.0f, stq));
+      if ((st = gemm(H, qd, w.wo))) return st;
+      CK(pf_resid(c->bt_X, c->pf_D, B, H, stq));
+      CK(pf_norm_split(c->pf_A, c->bt_X, w.ln2, B, H, s.rms_eps, stq));
+      if ((st = gemm(2 * I, H, w.wg))) return st;
+      CK(pf_swiglu_split(c->pf_A, c->pf_D, B, I, stq));
+      if ((st = gemm(H, I, w.wd))) return st;
+      CK(pf_resid(c->bt_X, c->pf_D, B, H, stq));
+    }
+    CK(pf_pos_advance(c->bt_pos, B, stq));
+    if ((st = head((int)step + 1))) return st;
+  }
+  CK(cudaEventRecord(c->ev1, stq));
+  if (steps)
+    CK(cudaMemcpyAsync(out_ids, c->bt_out, (size_t)B * steps * 4, cudaMemcpyDeviceToHost, stq));
+  if ((st = finish(c))) return st;
+  cudaEventElapsedTime(&c->decode_ms, c->ev0, c->ev1);
   return MYOS_OK;
 }
 

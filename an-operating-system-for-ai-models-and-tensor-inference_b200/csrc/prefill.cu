@@ -69,8 +69,16 @@ __global__ void k_pf_bias(float* Q, const float* D, const float* bias, int n, in
 // (rope.rs:145-184), then K and V stored at that slot (KvCache::store_at).
 template <typename KT>
 __global__ void k_pf_rope_store(float* Q, KT* kc, KT* vc, const float* cos_t, const float* sin_t,
-                                int p0, int Hq, int Hkv, int d, int S, size_t layer_elems) {
-  const int t = blockIdx.x, pos = p0 + t, half = d >> 1, N = (Hq + 2 * Hkv) * d;
+                                int p0, int Hq, int Hkv, int d, int S, const int* rowpos,
+                                size_t rowstride) {
+  // row t is token t of one sequence (position p0 + t), or with rowpos the
+  // next token of sequence t (position rowpos[t], cache rowstride elements on)
+  const int t = blockIdx.x, pos = rowpos ? rowpos[t] : p0 + t, half = d >> 1;
+  const int N = (Hq + 2 * Hkv) * d;
+  if (rowpos) {
+    kc += (size_t)t * rowstride;
+    vc += (size_t)t * rowstride;
+  }
   float* q = Q + (size_t)t * N;
   const float* cs = cos_t + (size_t)pos * half;
   const float* sn = sin_t + (size_t)pos * half;
@@ -82,7 +90,6 @@ __global__ void k_pf_rope_store(float* Q, KT* kc, KT* vc, const float* cos_t, co
     x[p + half] = __fadd_rn(__fmul_rn(x1, cs[p]), __fmul_rn(x0, sn[p]));
   }
   __syncthreads();
-  (void)layer_elems;
   for (int i = threadIdx.x; i < Hkv * d; i += blockDim.x) {
     const int g = i / d, e = i - g * d;
     const size_t slot = ((size_t)g * S + pos) * d + e;
@@ -115,12 +122,16 @@ MYOS_DEV float4 kv4<__nv_bfloat16>(const __nv_bfloat16* p) {
 template <typename KT, int D>
 __global__ void __launch_bounds__(kT) k_pf_attn(float* out, const float* Q, const KT* kcache,
                                                 const KT* vcache, int p0, int Hq, int Hkv, int S,
-                                                float scale) {
+                                                float scale, const int* rowpos, size_t rowstride) {
   constexpr int kTile = 32, ds = D + 4;
   __shared__ __align__(16) float qs[8 * D];
   __shared__ __align__(16) float ks[kTile * ds];
   __shared__ __align__(16) float vs[kTile * ds];
-  const int t = blockIdx.x, g = blockIdx.y, G = Hq / Hkv, pos = p0 + t;
+  const int t = blockIdx.x, g = blockIdx.y, G = Hq / Hkv, pos = rowpos ? rowpos[t] : p0 + t;
+  if (rowpos) {
+    kcache += (size_t)t * rowstride;
+    vcache += (size_t)t * rowstride;
+  }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int N = (Hq + 2 * Hkv) * D;
   const float* q = Q + (size_t)t * N + (size_t)g * G * D;
@@ -217,7 +228,80 @@ __global__ void k_pf_swiglu_split(uint16_t* A, const float* D, int n, int I) {
   }
 }
 
+// Greedy token of each row from the stacked logit halves: logits_b[j] =
+// D[b][j] + D[B + b][j]; the first maximum with strict >, NaN and -inf never
+// win, none -> 0 (model_core/src/lib.rs:157-167). Records the token.
+__global__ void __launch_bounds__(kT) k_row_argmax(uint32_t* tok, uint32_t* out, int out_stride,
+                                                   int step, const float* D, int B, int V) {
+  __shared__ float bvs[kT / 32];
+  __shared__ uint32_t bis[kT / 32];
+  const int b = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  float bv = -INFINITY;
+  uint32_t bi = 0xffffffffu;
+  for (int j = threadIdx.x; j < V; j += blockDim.x) {
+    const float v = __fadd_rn(D[(size_t)b * V + j], D[(size_t)(B + b) * V + j]);
+    if (v > bv) {  // j grows per thread: strict > keeps the first
+      bv = v;
+      bi = (uint32_t)j;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > bv || (ov == bv && oi < bi)) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  if (lane == 0) {
+    bvs[warp] = bv;
+    bis[warp] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float v = -INFINITY;
+    uint32_t i = 0xffffffffu;
+    for (int w = 0; w < kT / 32; ++w)
+      if (bvs[w] > v || (bvs[w] == v && bis[w] < i)) {
+        v = bvs[w];
+        i = bis[w];
+      }
+    const uint32_t t = i == 0xffffffffu ? 0u : i;
+    tok[b] = t;
+    if (out) out[(size_t)b * out_stride + step] = t;
+  }
+}
+
+__global__ void k_rows_copy(float* dst, const float* src, const int* src_row, int K) {
+  const int b = blockIdx.x;
+  for (int j = threadIdx.x; j < K; j += blockDim.x)
+    dst[(size_t)b * K + j] = src[(size_t)src_row[b] * K + j];
+}
+
+__global__ void k_pos_advance(int* rowpos, int B) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b < B) rowpos[b] += 1;
+}
+
 }  // namespace
+
+cudaError_t pf_row_argmax(uint32_t* tok, uint32_t* out, int out_stride, int step, const float* D,
+                          int B, int V, cudaStream_t st) {
+  k_row_argmax<<<B, kT, 0, st>>>(tok, out, out_stride, step, D, B, V);
+  return cudaGetLastError();
+}
+
+cudaError_t pf_rows_copy(float* dst, const float* src, const int* src_row, int B, int K,
+                         cudaStream_t st) {
+  k_rows_copy<<<B, kT, 0, st>>>(dst, src, src_row, K);
+  return cudaGetLastError();
+}
+
+cudaError_t pf_pos_advance(int* rowpos, int B, cudaStream_t st) {
+  k_pos_advance<<<(B + 127) / 128, 128, 0, st>>>(rowpos, B);
+  return cudaGetLastError();
+}
 
 cudaError_t pf_embed(float* X, const uint16_t* embed, const uint32_t* ids, int n, int K,
                      cudaStream_t st) {
@@ -238,30 +322,32 @@ cudaError_t pf_bias(float* Q, const float* D, const float* bias, int n, int N, c
 
 cudaError_t pf_rope_store(float* Q, void* kc, void* vc, int kv_bf16, const float* cos_t,
                           const float* sin_t, int p0, int n, int Hq, int Hkv, int d, int S,
-                          cudaStream_t st) {
+                          cudaStream_t st, const int* rowpos, size_t rowstride) {
   if (kv_bf16)
     k_pf_rope_store<__nv_bfloat16><<<n, kT, 0, st>>>(Q, (__nv_bfloat16*)kc, (__nv_bfloat16*)vc,
-                                                      cos_t, sin_t, p0, Hq, Hkv, d, S, 0);
+                                                      cos_t, sin_t, p0, Hq, Hkv, d, S, rowpos,
+                                                      rowstride);
   else
     k_pf_rope_store<float><<<n, kT, 0, st>>>(Q, (float*)kc, (float*)vc, cos_t, sin_t, p0, Hq, Hkv,
-                                             d, S, 0);
+                                             d, S, rowpos, rowstride);
   return cudaGetLastError();
 }
 
 bool pf_attn_supported(int d, int G) { return (d == 64 || d == 128) && G <= 8; }
 
 cudaError_t pf_attn(float* out, const float* Q, const void* kc, const void* vc, int kv_bf16, int p0,
-                    int n, int Hq, int Hkv, int d, int S, float scale, cudaStream_t st) {
+                    int n, int Hq, int Hkv, int d, int S, float scale, cudaStream_t st,
+                    const int* rowpos, size_t rowstride) {
   const dim3 grid(n, Hkv);
 #define MYOS_PF_ATTN(D)                                                                     \
   if (d == D) {                                                                             \
     if (kv_bf16)                                                                            \
       k_pf_attn<__nv_bfloat16, D><<<grid, kT, 0, st>>>(out, Q, (const __nv_bfloat16*)kc,    \
                                                        (const __nv_bfloat16*)vc, p0, Hq,    \
-                                                       Hkv, S, scale);                      \
+                                                       Hkv, S, scale, rowpos, rowstride);   \
     else                                                                                    \
       k_pf_attn<float, D><<<grid, kT, 0, st>>>(out, Q, (const float*)kc, (const float*)vc, \
-                                               p0, Hq, Hkv, S, scale);                      \
+                                               p0, Hq, Hkv, S, scale, rowpos, rowstride);   \
     return cudaGetLastError();                                                              \
   }
   MYOS_PF_ATTN(64)

@@ -111,6 +111,18 @@ class Engine:
         self._check(self.L.myos_greedy_decode(self.h, steps, out.ctypes.data_as(_lib._u32p)))
         return out[:steps]
 
+    def batch_generate(self, prompts, steps: int) -> np.ndarray:
+        """Greedy ids [len(prompts), steps] for independent prompts decoded
+        together (myos_batch_generate); the context's own cache is untouched."""
+        lens = np.array([len(p) for p in prompts], np.uint32)
+        ids = np.ascontiguousarray(np.concatenate([np.asarray(p, np.uint32) for p in prompts]),
+                                   np.uint32)
+        out = np.zeros(max(len(prompts) * steps, 1), np.uint32)
+        self._check(self.L.myos_batch_generate(self.h, len(prompts), ids.ctypes.data_as(_lib._u32p),
+                                               lens.ctypes.data_as(_lib._u32p), steps,
+                                               out.ctypes.data_as(_lib._u32p)))
+        return out[:len(prompts) * steps].reshape(len(prompts), steps)
+
     def forced_decode(self, ids) -> np.ndarray:
         ids = np.ascontiguousarray(ids, np.uint32)
         am = np.zeros(max(ids.size, 1), np.uint32)

@@ -211,6 +211,21 @@ int myos_greedy_token(const float* logits, size_t n, uint32_t* out);
 int myos_dev_gemv_bf16(float* d_y, const void* d_w, const float* d_x, size_t m, size_t k,
                        void* stream);
 
+/* Greedy generation for nseq independent sequences at once. No direct
+ * counterpart in the reference, which decodes one sequence per process
+ * (model_core greedy_decode, qwen25_block.rs:765-780): this stands in for
+ * running greedy_decode on each prompt. Sequence b's prompt is
+ * ids[off_b .. off_b + lens[b]) (prompts concatenated in order);
+ * out_ids[b * steps + s] receives its s-th generated id. Every prompt runs
+ * through the tensor-core prefill into its own KV slab; each decode step then
+ * runs the projections and the head of all sequences as GEMMs (the bf16
+ * halves of nseq activations stacked, M = 2 nseq). 1 <= nseq <= 128 and
+ * lens[b] + steps <= max_seq; needs a shape the GEMM prefill supports
+ * (MYOS_ERR_SHAPE otherwise). The context's own cache and cursor are not
+ * touched. */
+int myos_batch_generate(myos_ctx* ctx, size_t nseq, const uint32_t* ids, const uint32_t* lens,
+                        size_t steps, uint32_t* out_ids);
+
 /* Size of the fixed device array that myos_dev_gqa_attn_f32_noalloc takes its
  * scratch from (one per device). */
 #define MYOS_NOALLOC_SCRATCH_BYTES (2u << 20)
