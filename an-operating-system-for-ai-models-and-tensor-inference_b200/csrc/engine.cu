@@ -1098,10 +1098,12 @@ int myos_profile_kernels(myos_ctx* c, int iters, float* ms_out, double* bytes_ou
     // one untimed pass to warm instruction caches and the launch path
     for (int l = 0; l < L; ++l)
       if ((st = launch_kind(c, kind, l, nullptr, false, false))) break;
+    // back to back with programmatic dependent launch, as inside the step:
+    // each launch's pre-wait prologue overlaps the previous launch's tail
     CK(cudaEventRecord(c->ev0, c->st));
     int n = 0;
     for (int it = 0; it < iters && !st; ++it)
-      for (int l = 0; l < L && !st; ++l, ++n) st = launch_kind(c, kind, l, nullptr, false, false);
+      for (int l = 0; l < L && !st; ++l, ++n) st = launch_kind(c, kind, l, nullptr, n > 0, false);
     CK(cudaEventRecord(c->ev1, c->st));
     if (!st) st = finish(c);
     if (st) {

@@ -123,13 +123,20 @@ def barrier(pg):
 
 
 def max_over_ranks(pg, value: float, local: int) -> float:
+    """The slowest rank's value (NCCL on the rank's GPU; gloo on the host)."""
     if pg is None:
         return value
     import torch
 
-    t = torch.tensor([value], dtype=torch.float64, device=f"cuda:{local}")
+    dev = f"cuda:{local}" if pg.get_backend() == "nccl" else "cpu"
+    t = torch.tensor([value], dtype=torch.float64, device=dev)
     pg.all_reduce(t, op=pg.ReduceOp.MAX)
     return float(t.item())
+
+
+def aggregate_tok_s(world: int, tokens_per_rank_step: int, steps: int, max_ms: float) -> float:
+    """Whole-job throughput: every rank's tokens over the slowest rank's time."""
+    return world * tokens_per_rank_step * steps / (max_ms / 1000.0)
 
 
 # ---------------------------------------------------------------- CPU baseline
@@ -240,8 +247,8 @@ def run_ours(args, world, rank, local, pg):
     barrier(pg)
     tot_dec = max_over_ranks(pg, sum(dec_ms), local)
     tot_pre = max_over_ranks(pg, sum(pre_ms), local)
-    value = world * n_gen * args.steps / (tot_dec / 1000.0)
-    prefill_tps = world * n_prompt * args.steps / (tot_pre / 1000.0)
+    value = aggregate_tok_s(world, n_gen, args.steps, tot_dec)
+    prefill_tps = aggregate_tok_s(world, n_prompt, args.steps, tot_pre)
 
     # end to end through the C ABI with host buffers: prompt ids in, ids out
     barrier(pg)

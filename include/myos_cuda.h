@@ -167,8 +167,9 @@ int myos_logits(myos_ctx* ctx, float* out);
  * (+ residual), 3 gate/up (RMSNorm + GEMV + SiLU*up), 4 down (+ residual),
  * 5 head (final norm + GEMV + argmax). A pass launches each kind once per
  * layer, each launch on that layer's weights, so the weights a pass touches
- * exceed L2; ms_out[6] gets the mean device time of one launch over iters
- * passes, bytes_out[6] the algorithmic bytes one launch moves (weights +
+ * exceed L2; launches follow each other with programmatic dependent launch
+ * as inside a token step; ms_out[6] gets the mean device time of one launch
+ * over iters passes, bytes_out[6] the algorithmic bytes one launch moves (weights +
  * activations + KV read at the current length). Needs kv_len < max_seq;
  * the KV cursor, logits and argmax are left as they were. */
 int myos_profile_kernels(myos_ctx* ctx, int iters, float* ms_out, double* bytes_out);
