@@ -38,9 +38,9 @@ def cutlass_include() -> list:
                     "-I" + os.path.join(root, "tools", "util", "include")]
     raise RuntimeError("CUTLASS headers (sm100 collectives) not found")
 CUDA_SOURCES = ["kernels.cu", "step_kernel.cu", "engine.cu", "ops.cu", "noalloc.cu",
-                "prefill.cu", "gemm_sm100.cu", "safetensors.cpp"]
+                "prefill.cu", "gemm_sm100.cu", "safetensors.cpp", "tp.cpp"]
 HEADERS = ["common.cuh", "kernels.h", "safetensors.h", "step_kernel.h", "prefill.h",
-           "gemm_sm100.h"]
+           "gemm_sm100.h", "tp.h"]
 
 
 def nvcc() -> str:

@@ -122,6 +122,53 @@ MYOS_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* err, uint32_t 
   return false;
 }
 
+// ---------------------------------------------------------------- tensor-parallel peers
+// Ranks of a tensor-parallel group are processes on different GPUs. A rank
+// stores each value of its part of a result straight into every rank's
+// inbox (peer memory over NVLink) as one 8-byte word (value bits, epoch):
+// an aligned 8-byte store is seen whole or not at all, so the word carries
+// its own validity and needs no fence or counter. The consumer polls each
+// word until its epoch is the current one. Epochs count the exchanges of a
+// context (every rank makes the same ones in the same order). Another rank
+// may reach the same step later than this one (its host enqueued later), so
+// a wait is bounded in time rather than in polls; once one wait has given
+// up, later waits of the context return at once with the error bit set.
+constexpr uint32_t kErrTpWait = 4u;
+constexpr uint64_t kTpWaitNs = 60000000000ull;  // 60 s
+
+MYOS_DEV void tp_store(float* slot, float v, unsigned epoch) {
+  const unsigned long long w = ((unsigned long long)epoch << 32) | __float_as_uint(v);
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(slot), "l"(w) : "memory");
+}
+
+MYOS_DEV unsigned long long tp_load(const float* slot) {
+  unsigned long long w;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(w) : "l"(slot) : "memory");
+  return w;
+}
+
+// The value of word `slot` once it carries `epoch`; false (and the error bit)
+// when the time bound passes first, or an earlier wait already gave up.
+MYOS_DEV bool tp_wait_word(const float* slot, unsigned epoch, uint32_t* err, float* v) {
+  unsigned long long w = tp_load(slot);
+  if ((unsigned)(w >> 32) != epoch) {
+    const uint64_t t0 = global_ns();
+    for (uint32_t i = 1;; ++i) {
+      if ((i & 63u) == 0) {
+        if (*(volatile uint32_t*)err & kErrTpWait) return false;
+        if (global_ns() - t0 > kTpWaitNs) {
+          atomicOr(err, kErrTpWait);
+          return false;
+        }
+      }
+      w = tp_load(slot);
+      if ((unsigned)(w >> 32) == epoch) break;
+    }
+  }
+  *v = __uint_as_float((unsigned)w);
+  return true;
+}
+
 // 1-D bulk copy global -> this CTA's shared memory, completing on bar.
 // dst, src 16-byte aligned; bytes a multiple of 16.
 MYOS_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {

@@ -32,6 +32,7 @@
 #include "prefill.h"
 #include "safetensors.h"
 #include "step_kernel.h"
+#include "tp.h"
 
 using namespace myos;
 
@@ -59,7 +60,7 @@ size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 }  // namespace
 
 struct myos_ctx {
-  myos_shape s;
+  myos_shape s;  // this rank's slice of the model (the whole model without tensor parallelism)
   myos_opts o;
   int device = 0;
   int num_sms = 148;
@@ -128,6 +129,25 @@ struct myos_ctx {
   uint64_t* ktrace = nullptr;  // MYOS_KTRACE_FILE: launch timeline of the per-kernel step
   std::string ktrace_file;
   std::vector<uint64_t> ktrace_init;
+  // tensor parallelism (myos_ctx_create_tp): heads, MLP columns and head rows
+  // split over tp_size ranks; residual updates summed over NCCL
+  int tp_size = 1, tp_rank = 0;
+  myos_shape full = {};      // the whole model (the loader checks tensors against it)
+  uint32_t i_cut = 0;        // MLP columns of this rank before padding to s.intermediate
+  uint32_t head_rows = 0, head_row0 = 0;  // this rank's vocabulary rows of the head
+  ncclComm_t comm = nullptr;
+  float* tp_part = nullptr;  // [hidden] this rank's partial residual update
+  float* tp_cand = nullptr;  // [2] this rank's (value, index), then [2 * tp_size] all ranks'
+  // Peer-memory exchange (default when every rank can map every other's
+  // memory; MYOS_TP_COMM=nccl uses NCCL collectives instead): the o_proj and
+  // down_proj epilogues push their rows into every rank's inbox, a one-block
+  // kernel sums them; the head pushes its candidate the same way.
+  bool tp_p2p = false;
+  uint8_t* tp_link = nullptr;         // this rank's inboxes and arrival counters
+  void* tp_peer[kMaxTp] = {};         // every rank's tp_link as mapped here
+  TpPush push_o = {}, push_d = {}, push_c = {};
+  float *inbox_o = nullptr, *inbox_d = nullptr, *inbox_c = nullptr;  // 8-byte words
+  unsigned* tp_seq = nullptr;         // [0] exchanges completed by this rank, [1] reduce blocks done
 };
 
 namespace {
@@ -231,6 +251,44 @@ KTrace ktrace_at(const myos_ctx* c, int slot) {
   return t;
 }
 
+// Tensor parallel residual update: each rank's projection writes its partial
+// sum to tp_part (rank 0 adds the residual), then the ranks' parts are summed
+// into every rank's residual.
+void tp_partial(const myos_ctx* c, GemvArgs* a, int kind) {
+  if (c->tp_size == 1) return;
+  a->y = c->tp_part;
+  a->res = c->tp_rank == 0 ? c->resid : nullptr;
+  a->res_zero = c->tp_rank == 0 ? 0 : 1;
+  if (c->tp_p2p) a->push = kind == K_O ? c->push_o : c->push_d;
+}
+
+int tp_sum_resid(myos_ctx* c, int kind) {
+  if (c->tp_size == 1) return MYOS_OK;
+  if (c->tp_p2p) {
+    TpReduceArgs r = {};
+    r.n = c->tp_size;
+    r.H = (int)c->s.hidden;
+    r.inbox = kind == K_O ? c->inbox_o : c->inbox_d;
+    r.seq = c->tp_seq;
+    r.done = c->tp_seq + 1;
+    r.out = c->resid;
+    r.err = &c->ctl->err;
+    CK(launch_tp_reduce(r, c->st, true));
+    return MYOS_OK;
+  }
+  if (!tp_allreduce_sum(c->tp_part, c->resid, c->s.hidden, c->comm, c->st))
+    return fail(c, MYOS_ERR_NCCL, "allreduce of the residual update failed");
+  return MYOS_OK;
+}
+
+// After a head pass, every rank's logits slice to every rank (in place).
+int tp_gather_logits(myos_ctx* c) {
+  if (c->tp_size == 1) return MYOS_OK;
+  if (!tp_allgather(c->logits + c->head_row0, c->logits, (size_t)c->head_rows * 4, c->comm, c->st))
+    return fail(c, MYOS_ERR_NCCL, "allgather of the logits failed");
+  return MYOS_OK;
+}
+
 int launch_kind(myos_ctx* c, int kind, int l, const uint32_t* feed, bool pdl, bool embed_l0) {
   const myos_shape& s = c->s;
   const int H = (int)s.hidden, I = (int)s.intermediate;
@@ -242,14 +300,14 @@ int launch_kind(myos_ctx* c, int kind, int l, const uint32_t* feed, bool pdl, bo
   }
   if (kind == K_HEAD) {
     GemvArgs h = {};
-    h.w = s.tied_head ? c->embed : c->lm_head;
-    h.M = (int)s.vocab;
+    h.w = s.tied_head ? c->embed + (size_t)c->head_row0 * H : c->lm_head;
+    h.M = (int)c->head_rows;
     h.K = H;
     h.in.x = c->resid;
     h.in.ctl = c->ctl;
     h.in.gamma = c->final_norm;
     h.in.eps = s.rms_eps;
-    h.y = c->logits;
+    h.y = c->logits + c->head_row0;
     h.prefetch_cap = prefetch_cap(c, c->grid_head);
     h.part_val = c->part_val;
     h.part_idx = c->part_idx;
@@ -259,7 +317,23 @@ int launch_kind(myos_ctx* c, int kind, int l, const uint32_t* feed, bool pdl, bo
     h.rec_fed = c->profiling ? nullptr : c->rec_fed;
     h.rec_argmax = c->profiling ? nullptr : c->rec_argmax;
     h.tr = ktrace_at(c, 5 * (int)s.num_layers);
+    if (c->tp_size > 1) {
+      h.row0 = c->head_row0;
+      if (c->tp_p2p) h.push = c->push_c;
+      else h.tp_cand = c->tp_cand;
+    }
     CK(launch_gemv(EPI_ARGMAX, h, c->grid_head, c->st, pdl));
+    if (c->tp_size > 1) {  // every rank's slice maximum, then the first global one
+      uint32_t* rf = c->profiling ? nullptr : c->rec_fed;
+      uint32_t* ra = c->profiling ? nullptr : c->rec_argmax;
+      if (c->tp_p2p) {
+        CK(launch_tp_pick(c->inbox_c, c->tp_size, c->tp_seq, c->ctl, rf, ra, c->st));
+      } else {
+        if (!tp_allgather(c->tp_cand, c->tp_cand + 2, 8, c->comm, c->st))
+          return fail(c, MYOS_ERR_NCCL, "allgather of the head candidates failed");
+        CK(launch_tp_pick(c->tp_cand + 2, c->tp_size, nullptr, c->ctl, rf, ra, c->st));
+      }
+    }
     return MYOS_OK;
   }
   const LayerW& w = c->layers[l];
@@ -335,7 +409,9 @@ int launch_kind(myos_ctx* c, int kind, int l, const uint32_t* feed, bool pdl, bo
     o.err = &c->ctl->err;
     o.prefetch_cap = prefetch_cap(c, c->grid_o);
     o.tr = ktrace_at(c, 5 * l + K_O);
+    tp_partial(c, &o, K_O);
     CK(launch_gemv(EPI_RESID, o, c->grid_o, c->st, pdl));
+    if (int st = tp_sum_resid(c, K_O)) return st;
   } else if (kind == K_GU) {
     GemvArgs gu = {};
     gu.w = w.wg;
@@ -362,7 +438,9 @@ int launch_kind(myos_ctx* c, int kind, int l, const uint32_t* feed, bool pdl, bo
     dn.err = &c->ctl->err;
     dn.prefetch_cap = prefetch_cap(c, c->grid_down);
     dn.tr = ktrace_at(c, 5 * l + K_DOWN);
+    tp_partial(c, &dn, K_DOWN);
     CK(launch_gemv(EPI_RESID, dn, c->grid_down, c->st, pdl));
+    if (int st = tp_sum_resid(c, K_DOWN)) return st;
   }
   return MYOS_OK;
 }
@@ -446,6 +524,10 @@ int run_steps(myos_ctx* c, int kind, size_t nsteps) {
 // Upload ctl.step = 0 (and pos when asked) before a call.
 int set_ctl(myos_ctx* c, bool set_pos) {
   CK(cudaStreamWaitEvent(c->st, c->load_ev, 0));
+  // Peer-memory waits are bounded in time: start every rank's call together
+  // (a one-float NCCL allreduce holds each GPU until all ranks are here).
+  if (c->tp_p2p && !tp_allreduce_sum(c->tp_cand, c->tp_cand, 1, c->comm, c->st))
+    return fail(c, MYOS_ERR_NCCL, "tensor-parallel call alignment failed");
   if (c->ktrace)
     CK(cudaMemcpyAsync(c->ktrace, c->ktrace_init.data(), c->ktrace_init.size() * 8,
                        cudaMemcpyHostToDevice, c->st));
@@ -558,9 +640,103 @@ myos_shape myos_shape_qwen25_14b(void) {
 
 const char* myos_last_error(const myos_ctx* c) { return c ? c->err.c_str() : "null context"; }
 
-static int create_impl(myos_ctx* c, const myos_shape* shape, const myos_opts* opts) {
+// Peer-memory exchange for a tensor-parallel context: every rank's inboxes
+// and counters in one allocation, its IPC handle and device UUID gathered
+// over NCCL, every other rank's allocation mapped here. The ranks agree on
+// the outcome (all map every peer, or all keep the NCCL collectives).
+static int setup_tp_p2p(myos_ctx* c) {
+  const int n = c->tp_size, me = c->tp_rank;
+  const size_t H = c->s.hidden;
+  const size_t in_bytes = align256((size_t)n * H * 8);  // one (value, epoch) word per row
+  const size_t off_c = 2 * in_bytes, off_f = off_c + 256, total = off_f + 256;
+  CK(cudaMalloc(&c->tp_link, total));
+  CK(cudaMemset(c->tp_link, 0, total));
+  struct Card {
+    cudaIpcMemHandle_t h;
+    uint8_t uuid[16];
+    int32_t ok;
+    uint8_t pad[12];
+  };
+  Card mine = {};
+  mine.ok = cudaIpcGetMemHandle(&mine.h, c->tp_link) == cudaSuccess;
+  cudaGetLastError();
+  cudaDeviceProp prop;
+  CK(cudaGetDeviceProperties(&prop, c->device));
+  memcpy(mine.uuid, &prop.uuid, 16);
+  std::vector<Card> all(n);
+  Card* d = nullptr;
+  CK(cudaMalloc(&d, n * sizeof(Card)));
+  CK(cudaMemcpy(d + me, &mine, sizeof(Card), cudaMemcpyHostToDevice));
+  const bool sent = tp_allgather(d + me, d, sizeof(Card), c->comm, c->st);
+  cudaError_t e = cudaStreamSynchronize(c->st);
+  if (e == cudaSuccess) e = cudaMemcpy(all.data(), d, n * sizeof(Card), cudaMemcpyDeviceToHost);
+  cudaFree(d);
+  if (!sent) return fail(c, MYOS_ERR_NCCL, "exchange of peer handles failed");
+  CK(e);
+  // the bounded waits assume each rank has a GPU of its own
+  for (int p = 0; p < n; ++p)
+    for (int q = p + 1; q < n; ++q)
+      if (memcmp(all[p].uuid, all[q].uuid, 16) == 0)
+        return fail(c, MYOS_ERR_ARG, "two tensor-parallel ranks share one GPU");
+  bool ok = true;
+  for (int p = 0; p < n; ++p) ok = ok && all[p].ok;
+  for (int p = 0; p < n && ok; ++p) {
+    if (p == me) continue;
+    if (cudaIpcOpenMemHandle(&c->tp_peer[p], all[p].h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+      cudaGetLastError();
+      c->tp_peer[p] = nullptr;
+      ok = false;
+    }
+  }
+  // every rank mapped every peer?
+  const float one = ok ? 1.0f : 0.0f;
+  CK(cudaMemcpy(c->tp_cand, &one, 4, cudaMemcpyHostToDevice));
+  if (!tp_allreduce_sum(c->tp_cand, c->tp_cand, 1, c->comm, c->st))
+    return fail(c, MYOS_ERR_NCCL, "peer-mapping agreement failed");
+  float agreed = 0.0f;
+  CK(cudaStreamSynchronize(c->st));
+  CK(cudaMemcpy(&agreed, c->tp_cand, 4, cudaMemcpyDeviceToHost));
+  if (agreed != (float)n) {  // keep the NCCL collectives
+    for (int p = 0; p < n; ++p)
+      if (p != me && c->tp_peer[p]) cudaIpcCloseMemHandle(c->tp_peer[p]);
+    memset(c->tp_peer, 0, sizeof c->tp_peer);
+    return MYOS_OK;
+  }
+  c->tp_peer[me] = c->tp_link;
+  c->tp_seq = (unsigned*)(c->tp_link + off_f);
+  for (int p = 0; p < n; ++p) {
+    uint8_t* base = (uint8_t*)c->tp_peer[p];
+    c->push_o.out[p] = (float*)base + 2 * (size_t)me * H;
+    c->push_d.out[p] = (float*)(base + in_bytes) + 2 * (size_t)me * H;
+    c->push_c.out[p] = (float*)(base + off_c) + 4 * me;  // two words per rank
+  }
+  c->push_o.n = c->push_d.n = c->push_c.n = n;
+  c->push_o.seq = c->push_d.seq = c->push_c.seq = c->tp_seq;
+  c->inbox_o = (float*)c->tp_link;
+  c->inbox_d = (float*)(c->tp_link + in_bytes);
+  c->inbox_c = (float*)(c->tp_link + off_c);
+  c->tp_p2p = true;
+  return MYOS_OK;
+}
+
+static int create_impl(myos_ctx* c, const myos_shape* shape, const myos_opts* opts,
+                       const myos_tp* tp) {
+  c->full = *shape;
   c->s = *shape;
   c->o = *opts;
+  c->i_cut = shape->intermediate;
+  c->head_rows = shape->vocab;
+  if (tp && tp->size > 1) {  // this rank's slice (divisibility checked by the caller)
+    const uint32_t N = (uint32_t)tp->size;
+    c->tp_size = tp->size;
+    c->tp_rank = tp->rank;
+    c->s.num_q_heads /= N;
+    c->s.num_kv_heads /= N;
+    c->i_cut = shape->intermediate / N;
+    c->s.intermediate = (c->i_cut + 255) / 256 * 256;  // zero rows/columns pad the GEMV width
+    c->head_rows = shape->vocab / N;
+    c->head_row0 = (uint32_t)tp->rank * c->head_rows;
+  }
   c->device = opts->device;
   int ndev = 0;
   if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev <= opts->device || opts->device < 0) {
@@ -588,7 +764,7 @@ static int create_impl(myos_ctx* c, const myos_shape* shape, const myos_opts* op
     return o;
   };
   size_t o_embed = take(V * H * 2);
-  size_t o_lm = s.tied_head ? 0 : take(V * H * 2);
+  size_t o_lm = s.tied_head ? 0 : take((size_t)c->head_rows * H * 2);
   size_t o_fn = take(H * 4);
   std::vector<size_t> lo(L * 8);
   for (size_t l = 0; l < L; ++l) {
@@ -632,7 +808,7 @@ static int create_impl(myos_ctx* c, const myos_shape* shape, const myos_opts* op
   c->grid_o = gemv_grid((int)H, (int)c->qd, 1, c->num_sms);
   c->grid_gu = gemv_grid((int)I, (int)H, 2, c->num_sms);
   c->grid_down = gemv_grid((int)H, (int)I, 1, c->num_sms);
-  c->grid_head = gemv_grid((int)V, (int)H, 1, c->num_sms);
+  c->grid_head = gemv_grid((int)c->head_rows, (int)H, 1, c->num_sms);
   size_t nsplit = (S + 31) / 32;
   size_t cap = (size_t)c->num_sms / s.num_kv_heads;
   if (cap < 1) cap = 1;
@@ -684,7 +860,7 @@ static int create_impl(myos_ctx* c, const myos_shape* shape, const myos_opts* op
     // opt-in until it outruns the per-kernel step (MYOS_MEGA=1)
     const char* e = getenv("MYOS_MEGA");
     const bool want = e && e[0] == '1';
-    if (want && mega_supported((int)H, (int)I, (int)c->qd, (int)c->kvd, (int)d, (int)c->G) &&
+    if (want && c->tp_size == 1 && mega_supported((int)H, (int)I, (int)c->qd, (int)c->kvd, (int)d, (int)c->G) &&
         (size_t)s.num_kv_heads * nsplit <= (size_t)c->num_sms) {
       std::vector<MegaLayer> hl(L);
       for (size_t l = 0; l < L; ++l) {
@@ -769,7 +945,7 @@ static int create_impl(myos_ctx* c, const myos_shape* shape, const myos_opts* op
     // up rows adjacent (one [2I, H] projection), a supported head dim.
     const char* e = getenv("MYOS_PREFILL");
     const bool want = !(e && e[0] == 's');
-    bool ok = want && pf_attn_supported((int)d, (int)c->G) && H % 64 == 0 && I % 64 == 0 &&
+    bool ok = want && c->tp_size == 1 && pf_attn_supported((int)d, (int)c->G) && H % 64 == 0 && I % 64 == 0 &&
               c->qd % 64 == 0 && (c->qd + 2 * c->kvd) % 64 == 0;
     for (size_t l = 0; ok && l < L; ++l) ok = c->layers[l].wu == c->layers[l].wg + I * H;
     if (ok) {
@@ -816,18 +992,52 @@ static int create_impl(myos_ctx* c, const myos_shape* shape, const myos_opts* op
   CK(cudaEventCreate(&c->ev0));
   CK(cudaEventCreate(&c->ev1));
   CK(cudaEventCreate(&c->ev2));
+  if (c->tp_size > 1) {
+    CK(cudaMalloc(&c->tp_part, H * 4));
+    CK(cudaMalloc(&c->tp_cand, (2 + 2 * (size_t)c->tp_size) * 4));
+    CK(cudaMemset(c->tp_cand, 0, (2 + 2 * (size_t)c->tp_size) * 4));
+  }
   CK(cudaDeviceSynchronize());
+  if (c->tp_size > 1) {  // blocks until every rank has joined
+    std::string why;
+    if (!tp_comm_init(&c->comm, c->tp_size, c->tp_rank, tp->unique_id, &why))
+      return fail(c, MYOS_ERR_NCCL, "tensor-parallel communicator: " + why);
+    const char* m = getenv("MYOS_TP_COMM");
+    if (!(m && strcmp(m, "nccl") == 0)) {
+      int st = setup_tp_p2p(c);
+      if (st) return st;
+    }
+  }
   return MYOS_OK;
 }
 
 int myos_ctx_create(const myos_shape* shape, const myos_opts* opts, myos_ctx** out) {
+  return myos_ctx_create_tp(shape, opts, nullptr, out);
+}
+
+int myos_tp_unique_id(uint8_t out[128]) {
+  if (!out) return MYOS_ERR_ARG;
+  std::string why;
+  return tp_unique_id(out, &why) ? MYOS_OK : MYOS_ERR_NCCL;
+}
+
+int myos_ctx_create_tp(const myos_shape* shape, const myos_opts* opts, const myos_tp* tp,
+                       myos_ctx** out) {
   if (!shape || !opts || !out) return MYOS_ERR_ARG;
   *out = nullptr;
   if (check_shape(*shape)) return MYOS_ERR_SHAPE;
   if (opts->max_seq == 0) return MYOS_ERR_SHAPE;
   if (opts->kv_dtype != MYOS_KV_F32 && opts->kv_dtype != MYOS_KV_BF16) return MYOS_ERR_ARG;
+  if (tp) {
+    if (tp->size < 1 || tp->size > kMaxTp || tp->rank < 0 || tp->rank >= tp->size)
+      return MYOS_ERR_ARG;
+    const uint32_t N = (uint32_t)tp->size;
+    if (shape->num_q_heads % N || shape->num_kv_heads % N || shape->intermediate % N ||
+        shape->vocab % N || (shape->num_q_heads / N) * shape->head_dim % 256)
+      return MYOS_ERR_SHAPE;
+  }
   myos_ctx* c = new myos_ctx();
-  int st = create_impl(c, shape, opts);
+  int st = create_impl(c, shape, opts, tp);
   if (st) {
     myos_ctx_destroy(c);
     return st;
@@ -840,14 +1050,18 @@ void myos_ctx_destroy(myos_ctx* c) {
   if (!c) return;
   cudaSetDevice(c->device);
   if (c->st) cudaStreamSynchronize(c->st);
-  for (auto& kv : c->graphs) cudaGraphExecDestroy(kv.second);
+  for (auto& kv : c->graphs) cudaGraphExecDestroy(kv.second);  // they hold NCCL calls
+  c->graphs.clear();
+  for (int p = 0; p < kMaxTp; ++p)
+    if (c->tp_peer[p] && c->tp_peer[p] != c->tp_link) cudaIpcCloseMemHandle(c->tp_peer[p]);
+  tp_comm_destroy(c->comm);
   void* dev[] = {c->warena, c->kcache, c->vcache, c->resid, c->qkv, c->attn, c->act, c->logits,
                  c->part_val, c->part_idx, c->part_o, c->part_m, c->part_l, c->counters, c->ctl,
                  c->feed, c->rec_fed, c->rec_argmax, c->cos_t, c->sin_t, c->d_layers, c->bar,
                  (void*)c->margs.part_val, (void*)c->margs.part_idx, (void*)c->trace,
                  (void*)c->ktrace, c->pf_X, c->pf_D, c->pf_Q, c->pf_att, c->pf_A, c->pf_ws,
                  c->bt_k, c->bt_v, c->bt_X, c->bt_D, c->bt_pos, c->bt_rows, c->bt_tok,
-                 c->bt_out, c->bt_ids};
+                 c->bt_out, c->bt_ids, c->tp_part, c->tp_cand, c->tp_link};
   for (void* p : dev)
     if (p) cudaFree(p);
   for (int i = 0; i < 2; ++i) {
@@ -870,8 +1084,9 @@ int myos_load_tensor(myos_ctx* c, const char* name, int32_t dtype, const int64_t
   if (!name || !*name) return fail(c, MYOS_ERR_EMPTY_NAME, "tensor name is empty");
   if (rank < 0 || (rank > 0 && !shape) || (nbytes && !bytes)) return fail(c, MYOS_ERR_ARG, "bad tensor arguments");
   CK(cudaSetDevice(c->device));
-  const myos_shape& s = c->s;
-  const uint64_t H = s.hidden, I = s.intermediate, V = s.vocab, qd = c->qd, kvd = c->kvd;
+  const myos_shape& s = c->full;  // tensors arrive whole; a tensor-parallel rank keeps its slice
+  const uint64_t H = s.hidden, I = s.intermediate, V = s.vocab;
+  const uint64_t qd = (uint64_t)s.num_q_heads * s.head_dim, kvd = (uint64_t)s.num_kv_heads * s.head_dim;
   std::string n(name);
   int layer = -1, suffix = -1, global = -1;  // global: 0 embed, 1 final norm, 2 lm_head
   std::vector<uint64_t> expect;
@@ -923,25 +1138,41 @@ int myos_load_tensor(myos_ctx* c, const char* name, int32_t dtype, const int64_t
   bool same = (size_t)rank == expect.size();
   for (int i = 0; same && i < rank; ++i) same = (uint64_t)shape[i] == expect[i];
   if (!same) return fail(c, MYOS_ERR_WEIGHT_SHAPE, "tensor shape does not match the layout: " + n);
+  // This rank's slice: rows [r0, r0 + nr) of a row-major tensor, or columns
+  // [c0, c0 + nc) of every row stored at a row stride of `ld` elements (the
+  // padding columns stay zero from the arena's initial clear).
+  const uint8_t* src = (const uint8_t*)bytes;
+  auto rows = [&](void* dst, uint64_t r0, uint64_t nr, uint64_t row_elems) {
+    return stage_h2d(c, dst, src + r0 * row_elems * 2, nr * row_elems * 2);
+  };
+  auto cols = [&](uint16_t* dst, uint64_t nrows, uint64_t ncols, uint64_t c0, uint64_t nc,
+                  uint64_t ld) {
+    if (c0 == 0 && nc == ncols && ld == ncols) return stage_h2d(c, dst, src, nrows * ncols * 2);
+    std::vector<uint16_t> tmp(nrows * ld, 0);
+    for (uint64_t r = 0; r < nrows; ++r) memcpy(&tmp[r * ld], src + (r * ncols + c0) * 2, nc * 2);
+    return stage_h2d(c, dst, tmp.data(), tmp.size() * 2);
+  };
+  const uint64_t rk = (uint64_t)c->tp_rank, qdl = c->qd, kvdl = c->kvd, Ic = c->i_cut,
+                 Il = c->s.intermediate;
   int st = MYOS_OK;
   if (global == 0) st = stage_h2d(c, c->embed, bytes, nbytes);
   else if (global == 1) st = stage_bf16_as_f32(c, c->final_norm, bytes, H);
-  else if (global == 2) st = stage_h2d(c, c->lm_head, bytes, nbytes);
+  else if (global == 2) st = rows(c->lm_head, c->head_row0, c->head_rows, H);
   else {
     const LayerW& w = c->layers[layer];
     switch (suffix) {
       case 0: st = stage_bf16_as_f32(c, w.ln1, bytes, H); break;
-      case 1: st = stage_h2d(c, w.wqkv, bytes, nbytes); break;
-      case 2: st = stage_bf16_as_f32(c, w.bqkv, bytes, qd); break;
-      case 3: st = stage_h2d(c, w.wqkv + qd * H, bytes, nbytes); break;
-      case 4: st = stage_bf16_as_f32(c, w.bqkv + qd, bytes, kvd); break;
-      case 5: st = stage_h2d(c, w.wqkv + (qd + kvd) * H, bytes, nbytes); break;
-      case 6: st = stage_bf16_as_f32(c, w.bqkv + qd + kvd, bytes, kvd); break;
-      case 7: st = stage_h2d(c, w.wo, bytes, nbytes); break;
+      case 1: st = rows(w.wqkv, rk * qdl, qdl, H); break;
+      case 2: st = stage_bf16_as_f32(c, w.bqkv, src + rk * qdl * 2, qdl); break;
+      case 3: st = rows(w.wqkv + qdl * H, rk * kvdl, kvdl, H); break;
+      case 4: st = stage_bf16_as_f32(c, w.bqkv + qdl, src + rk * kvdl * 2, kvdl); break;
+      case 5: st = rows(w.wqkv + (qdl + kvdl) * H, rk * kvdl, kvdl, H); break;
+      case 6: st = stage_bf16_as_f32(c, w.bqkv + qdl + kvdl, src + rk * kvdl * 2, kvdl); break;
+      case 7: st = cols(w.wo, H, qd, rk * qdl, qdl, qdl); break;
       case 8: st = stage_bf16_as_f32(c, w.ln2, bytes, H); break;
-      case 9: st = stage_h2d(c, w.wg, bytes, nbytes); break;
-      case 10: st = stage_h2d(c, w.wu, bytes, nbytes); break;
-      case 11: st = stage_h2d(c, w.wd, bytes, nbytes); break;
+      case 9: st = rows(w.wg, rk * Ic, Ic, H); break;
+      case 10: st = rows(w.wu, rk * Ic, Ic, H); break;
+      case 11: st = cols(w.wd, H, I, rk * Ic, Ic, Il); break;
     }
   }
   if (st) return st;
@@ -1082,6 +1313,7 @@ int myos_logits(myos_ctx* c, float* out) {
 
 int myos_profile_kernels(myos_ctx* c, int iters, float* ms_out, double* bytes_out) {
   if (!c || !ms_out || iters <= 0) return MYOS_ERR_ARG;
+  if (c->tp_size > 1) return fail(c, MYOS_ERR_UNSUPPORTED, "kernel profiling is single-GPU only");
   CK(cudaSetDevice(c->device));
   int st = missing_weight(c);
   if (st) return st;
@@ -1166,6 +1398,7 @@ int myos_forward_token(myos_ctx* c, uint32_t token, size_t pos, float* logits) {
   CK(cudaEventRecord(c->ev0, c->st));
   if ((st = run_steps(c, G_FEED_HEAD, 1))) return st;
   CK(cudaEventRecord(c->ev1, c->st));
+  if ((st = tp_gather_logits(c))) return st;
   if (logits) CK(cudaMemcpyAsync(logits, c->logits, (size_t)c->s.vocab * 4, cudaMemcpyDeviceToHost, c->st));
   if ((st = finish(c))) return st;
   cudaEventElapsedTime(&c->decode_ms, c->ev0, c->ev1);
@@ -1223,6 +1456,7 @@ int prefill_chunk(myos_ctx* c, const uint32_t* d_ids, int n, int p0, void* kcach
 int myos_batch_generate(myos_ctx* c, size_t nseq, const uint32_t* ids, const uint32_t* lens,
                         size_t steps, uint32_t* out_ids) {
   if (!c || !ids || !lens || (steps && !out_ids)) return MYOS_ERR_ARG;
+  if (c->tp_size > 1) return fail(c, MYOS_ERR_UNSUPPORTED, "batched decode is single-GPU only");
   if (!c->pf_ok) return fail(c, MYOS_ERR_SHAPE, "batched decode needs the tensor-core path's shape");
   if (nseq == 0 || nseq > (size_t)c->pf_chunk)
     return fail(c, MYOS_ERR_SHAPE, "batch size must be 1.." + std::to_string(c->pf_chunk));
@@ -1372,6 +1606,7 @@ int myos_prefill(myos_ctx* c, const uint32_t* ids, size_t n, float* logits) {
     if ((st = run_steps(c, G_FEED_HEAD, 1))) return st;
   }
   CK(cudaEventRecord(c->ev1, c->st));
+  if ((st = tp_gather_logits(c))) return st;
   if (logits) CK(cudaMemcpyAsync(logits, c->logits, (size_t)c->s.vocab * 4, cudaMemcpyDeviceToHost, c->st));
   if ((st = finish(c))) return st;
   cudaEventElapsedTime(&c->prefill_ms, c->ev0, c->ev1);
@@ -1390,6 +1625,7 @@ int myos_greedy_decode(myos_ctx* c, size_t steps, uint32_t* out_ids) {
   CK(cudaEventRecord(c->ev0, c->st));
   if (run && (st = run_steps(c, G_ARGMAX_HEAD, run))) return st;
   CK(cudaEventRecord(c->ev1, c->st));
+  if (run && (st = tp_gather_logits(c))) return st;
   if (run) CK(cudaMemcpyAsync(out_ids, c->rec_fed, run * 4, cudaMemcpyDeviceToHost, c->st));
   if ((st = finish(c))) return st;
   cudaEventElapsedTime(&c->decode_ms, c->ev0, c->ev1);
@@ -1412,6 +1648,7 @@ int myos_forced_decode(myos_ctx* c, const uint32_t* ids, size_t steps, uint32_t*
   CK(cudaEventRecord(c->ev0, c->st));
   if ((st = run_steps(c, G_FEED_HEAD, steps))) return st;
   CK(cudaEventRecord(c->ev1, c->st));
+  if ((st = tp_gather_logits(c))) return st;
   CK(cudaMemcpyAsync(argmax_out, c->rec_argmax, steps * 4, cudaMemcpyDeviceToHost, c->st));
   if ((st = finish(c))) return st;
   cudaEventElapsedTime(&c->decode_ms, c->ev0, c->ev1);

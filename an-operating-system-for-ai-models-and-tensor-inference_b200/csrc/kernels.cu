@@ -371,7 +371,7 @@ MYOS_DEV bool better(float v, uint32_t i, float bv, uint32_t bi) {
 
 template <int EPI>
 MYOS_DEV void epilogue(const GemvArgs& a, int row, float v, float v2, float& bv, uint32_t& bi,
-                       int lane) {
+                       int lane, unsigned tp_epoch = 0) {
   if (EPI == EPI_ARGMAX) {
     if (better(v, (uint32_t)row, bv, bi)) {
       bv = v;
@@ -381,7 +381,16 @@ MYOS_DEV void epilogue(const GemvArgs& a, int row, float v, float v2, float& bv,
   if (lane != 0) return;
   if (EPI == EPI_STORE || EPI == EPI_ARGMAX) a.y[row] = v;
   if (EPI == EPI_BIAS) a.y[row] = __fadd_rn(v, a.bias[row]);
-  if (EPI == EPI_RESID) a.y[row] = __fadd_rn(a.y[row], v);
+  if (EPI == EPI_RESID) {
+    const float r = __fadd_rn(a.res_zero ? 0.0f : (a.res ? a.res[row] : a.y[row]), v);
+    if (a.push.n) {
+#pragma unroll
+      for (int p = 0; p < kMaxTp; ++p)
+        if (p < a.push.n) tp_store(a.push.out[p] + 2 * row, r, tp_epoch);
+    } else {
+      a.y[row] = r;
+    }
+  }
   if (EPI == EPI_SWIGLU) a.y[row] = silu_mul(v, v2);
 }
 
@@ -423,6 +432,23 @@ MYOS_DEV void argmax_finish(const GemvArgs& a, float bv, uint32_t bi, float* wbv
         v = pv;
         i = pi;
       }
+    }
+    if (a.tp_cand || a.push.n) {  // this rank's vocab slice: hand over for the global pick
+      const float iv = __uint_as_float(i == 0xffffffffu ? i : i + a.row0);
+      if (a.push.n) {
+        const unsigned e = __ldcg(a.push.seq) + 1u;
+#pragma unroll
+        for (int p = 0; p < kMaxTp; ++p)
+          if (p < a.push.n) {
+            tp_store(a.push.out[p], v, e);
+            tp_store(a.push.out[p] + 2, iv, e);
+          }
+      } else {
+        a.tp_cand[0] = v;
+        a.tp_cand[1] = iv;
+      }
+      *a.counter = 0u;
+      return;
     }
     const uint32_t tok = i == 0xffffffffu ? 0u : i;
     StepCtl* ctl = a.in.ctl;
@@ -587,6 +613,7 @@ __global__ void __launch_bounds__(kThreads, 2) k_gemv_stream(GemvArgs a) {
   if (a.pf_mode) l2_prefetch_slices(a);
   pdl_wait();
   pdl_launch();
+  const unsigned tp_epoch = (EPI == EPI_RESID && a.push.n) ? __ldcg(a.push.seq) + 1u : 0u;
   uint64_t* trow = trace_begin(a.tr, a.in.ctl, t_start);
   if (one) stage_one_trip<kGammaRegs>(xs, a.K, a.in, red, has_g, g0, g1);
   else stage_input(xs, a.K, true, a.in, red);
@@ -623,7 +650,7 @@ __global__ void __launch_bounds__(kThreads, 2) k_gemv_stream(GemvArgs a) {
         o[r] = warp_sum(acc[r]);
         acc[r] = 0.0f;
       }
-      epilogue<EPI>(a, row, o[0], NR > 1 ? o[NR - 1] : 0.0f, bv, bi, lane);
+      epilogue<EPI>(a, row, o[0], NR > 1 ? o[NR - 1] : 0.0f, bv, bi, lane, tp_epoch);
     }
 #pragma unroll
     for (int r = 0; r < NR; ++r)
@@ -1521,6 +1548,98 @@ __global__ void __launch_bounds__(kThreads) k_attn_dec(AttnArgs a) {
 }
 
 // ------------------------------------------------------------------ small kernels
+// Ranks hold contiguous vocab slices in rank order, so the first maximum over
+// their candidates (strict >, then the lower index) is the global one.
+__global__ void k_tp_pick(const float* cands, int n, unsigned* seq, StepCtl* ctl,
+                          uint32_t* rec_fed, uint32_t* rec_argmax) {
+  pdl_wait();
+  pdl_launch();
+  if (threadIdx.x != 0) return;
+  const unsigned e = seq ? __ldcg(seq) + 1u : 0u;
+  float v = -INFINITY;
+  uint32_t i = 0xffffffffu;
+  for (int r = 0; r < n; ++r) {
+    float cv, ciw;
+    if (seq) {  // pushed words (value, epoch), (index bits, epoch)
+      if (!tp_wait_word(cands + 4 * r, e, &ctl->err, &cv) ||
+          !tp_wait_word(cands + 4 * r + 2, e, &ctl->err, &ciw))
+        return;  // error bit set; the step is not advanced
+    } else {
+      cv = cands[2 * r];
+      ciw = cands[2 * r + 1];
+    }
+    const uint32_t ci = __float_as_uint(ciw);
+    if (better(cv, ci, v, i)) {
+      v = cv;
+      i = ci;
+    }
+  }
+  if (seq) *seq = e;
+  const uint32_t s = ctl->step;
+  if (rec_fed) rec_fed[s] = ctl->fed;
+  if (rec_argmax) rec_argmax[s] = ctl->argmax;
+  ctl->argmax = i == 0xffffffffu ? 0u : i;
+  ctl->pos = ctl->pos + 1;
+  ctl->step = s + 1;
+}
+
+cudaError_t launch_tp_pick(const float* cands, int n, unsigned* seq, StepCtl* ctl,
+                           uint32_t* rec_fed, uint32_t* rec_argmax, cudaStream_t st) {
+  k_tp_pick<<<1, 32, 0, st>>>(cands, n, seq, ctl, rec_fed, rec_argmax);
+  return cudaGetLastError();
+}
+
+constexpr int kReduceThreads = 256;
+
+// One element per thread over ceil(H / 256) blocks: every rank's word for it
+// is loaded at once (one round trip), then only words not yet current are
+// polled. The last block to finish advances the epoch.
+__global__ void __launch_bounds__(kReduceThreads) k_tp_reduce(TpReduceArgs r) {
+  pdl_launch();  // the next projection may start streaming its weights
+  pdl_wait();
+  const unsigned e = __ldcg(r.seq) + 1u;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < r.H) {
+    unsigned long long w[kMaxTp];
+#pragma unroll
+    for (int p = 0; p < kMaxTp; ++p)
+      if (p < r.n) w[p] = tp_load(r.inbox + 2 * ((size_t)p * r.H + i));
+    bool ok = true;
+    float s = 0.0f;
+#pragma unroll
+    for (int p = 0; p < kMaxTp; ++p) {
+      if (p >= r.n || !ok) continue;
+      float t = __uint_as_float((unsigned)w[p]);
+      if ((unsigned)(w[p] >> 32) != e)
+        ok = tp_wait_word(r.inbox + 2 * ((size_t)p * r.H + i), e, r.err, &t);
+      s = p == 0 ? t : __fadd_rn(s, t);
+    }
+    if (ok) r.out[i] = s;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(r.done, 1u) == gridDim.x - 1) {
+      *r.done = 0u;
+      if (!(*(volatile uint32_t*)r.err & kErrTpWait)) *r.seq = e;
+    }
+  }
+}
+
+cudaError_t launch_tp_reduce(const TpReduceArgs& r, cudaStream_t st, bool pdl) {
+  if (r.n < 1 || r.n > kMaxTp) return cudaErrorInvalidValue;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((r.H + kReduceThreads - 1) / kReduceThreads);
+  cfg.blockDim = dim3(kReduceThreads);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, k_tp_reduce, r);
+}
+
 __global__ void k_step_end(StepCtl* ctl) {
   pdl_wait();
   pdl_launch();
@@ -1661,12 +1780,16 @@ size_t gemv_smem_bytes(int K) { return (size_t)((K + 7) & ~7) * sizeof(float); }
 // Batch width U for the streaming GEMV: the largest U <= 8 that divides the
 // per-lane chunk count P (so no batch is partly empty), else 8. Two weight
 // matrices (SwiGLU) halve the budget so both buffers fit in registers.
+// Chunks per batch: as deep as the register budget allows (each warp keeps
+// two batches in flight, so depth sets its share of DRAM bandwidth), then
+// the smallest size giving that many batches a row (fewest idle slots in a
+// row's last batch).
 static int pick_batch(int P, int NR) {
   const int umax = NR > 1 ? 4 : 8;
   if (P <= umax) return P < 3 ? 3 : P;
-  for (int u = umax; u >= 3; --u)
-    if (P % u == 0) return u;
-  return umax;
+  const int nbr = (P + umax - 1) / umax;
+  int u = (P + nbr - 1) / nbr;
+  return u < 3 ? 3 : u;
 }
 
 template <int EPI, int NR>
@@ -1726,9 +1849,13 @@ int gemv_grid(int M, int K, int NR, int num_sms) {
 
 cudaError_t launch_gemv(int epi, const GemvArgs& a0, int grid, cudaStream_t st, bool pdl) {
   cudaLaunchAttribute attr[1];
+  if (a0.push.n &&  // the peer push lives in the streaming kernel only
+      ((a0.K % 256) != 0 || ((uintptr_t)a0.w & 15) != 0 || getenv_legacy() || a0.in.part_o ||
+       a0.push.n > kMaxTp))
+    return cudaErrorNotSupported;
   const bool bulk_ok = (a0.K % 256) == 0 && ((uintptr_t)a0.w & 15) == 0 &&
                        (epi != EPI_SWIGLU || ((uintptr_t)a0.w2 & 15) == 0) && gemv_kind() == 0 &&
-                       !a0.in.part_o;
+                       !a0.in.part_o && !a0.push.n;
   if (bulk_ok) {
     GemvArgs a = a0;
     const int NR = epi == EPI_SWIGLU ? 2 : 1;

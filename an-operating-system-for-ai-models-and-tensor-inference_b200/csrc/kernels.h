@@ -49,6 +49,29 @@ struct GemvInput {
 
 enum EpiKind { EPI_STORE = 0, EPI_BIAS = 1, EPI_RESID = 2, EPI_SWIGLU = 3, EPI_ARGMAX = 4 };
 
+// Tensor-parallel push (peer memory): out[p] is this rank's slot in rank
+// p's inbox (8-byte words: value, epoch), seq this rank's exchange counter
+// (the push uses epoch *seq + 1).
+constexpr int kMaxTp = 8;
+struct TpPush {
+  int n;  // ranks; 0: no push
+  float* out[kMaxTp];
+  const unsigned* seq;
+};
+
+// Sum of the ranks' pushed parts: out[i] = sum over ranks p = 0..n-1, in
+// rank order, of inbox word p * H + i once it carries epoch *seq + 1; then
+// *seq is advanced (by the last of the kernel's blocks).
+struct TpReduceArgs {
+  int n, H;
+  const float* inbox;
+  unsigned* seq;
+  unsigned* done;  // blocks finished (reset by the last one)
+  float* out;
+  uint32_t* err;
+};
+cudaError_t launch_tp_reduce(const TpReduceArgs& r, cudaStream_t st, bool pdl);
+
 struct GemvArgs {
   const uint16_t* w;   // [M, K] row-major bf16
   const uint16_t* w2;  // EPI_SWIGLU: up_proj [M, K]
@@ -76,7 +99,26 @@ struct GemvArgs {
   const void* pf_ptr[3];
   size_t pf_bytes[3];
   int pf_mode;
+  // Tensor parallel. EPI_RESID: y[row] = base + v with base = res[row] (res
+  // set), y[row] (res null: in place), or 0 (res_zero: a partial sum for the
+  // allreduce). EPI_ARGMAX with tp_cand: the block-reduced first maximum goes
+  // to tp_cand as (value, row0 + row), the step control is left alone.
+  // With push.n > 0 the EPI_RESID rows (or the EPI_ARGMAX candidate) go to
+  // every rank's inbox instead, and each block arrives on every rank's
+  // counter when done.
+  const float* res;
+  int res_zero;
+  float* tp_cand;
+  uint32_t row0;
+  TpPush push;
 };
+
+// Global first maximum over the tensor-parallel ranks' candidates
+// [(value, index)] x n, then the step control advanced (tp pick). With seq
+// non-null the candidates arrive by push (words of epoch *seq + 1, two per
+// rank) and *seq is advanced after.
+cudaError_t launch_tp_pick(const float* cands, int n, unsigned* seq, StepCtl* ctl,
+                           uint32_t* rec_fed, uint32_t* rec_argmax, cudaStream_t st);
 
 struct AttnArgs {
   const float* q;        // decode: qkv buffer [q | k | v] before RoPE; op: q [Hq*d]

@@ -64,12 +64,24 @@ class Opts(C.Structure):
     ]
 
 
+class TP(C.Structure):
+    """myos_tp: one rank of a tensor-parallel group."""
+    _fields_ = [
+        ("size", C.c_int32),
+        ("rank", C.c_int32),
+        ("unique_id", C.c_uint8 * 128),
+    ]
+
+
 # Every symbol include/myos_cuda.h declares, with (restype, argtypes).
 SIGNATURES = {
     "myos_version": (C.c_char_p, []),
     "myos_shape_qwen25_1_5b": (Shape, []),
     "myos_shape_qwen25_14b": (Shape, []),
     "myos_ctx_create": (C.c_int, [C.POINTER(Shape), C.POINTER(Opts), C.POINTER(C.c_void_p)]),
+    "myos_ctx_create_tp": (C.c_int, [C.POINTER(Shape), C.POINTER(Opts), C.POINTER(TP),
+                                      C.POINTER(C.c_void_p)]),
+    "myos_tp_unique_id": (C.c_int, [_u8p]),
     "myos_ctx_destroy": (None, [C.c_void_p]),
     "myos_last_error": (C.c_char_p, [C.c_void_p]),
     "myos_load_tensor": (C.c_int, [C.c_void_p, C.c_char_p, C.c_int32, _i64p, C.c_int32,

@@ -32,9 +32,23 @@ def shape_from_dict(d: dict) -> _lib.Shape:
                       1 if d.get("tied_head", True) else 0)
 
 
+def tp_unique_id() -> bytes:
+    """A fresh rendezvous token for a tensor-parallel group (myos_tp_unique_id);
+    made on one rank and handed to every rank's Engine(tp=(size, rank, id))."""
+    L = _lib.load()
+    buf = (C.c_uint8 * 128)()
+    st = L.myos_tp_unique_id(buf)
+    if st != 0:
+        raise MyosError(st, "myos_tp_unique_id failed")
+    return bytes(buf)
+
+
 class Engine:
     def __init__(self, shape: dict, max_seq: int, device: int = 0, kv_dtype: str = "f32",
-                 use_graphs: bool = True):
+                 use_graphs: bool = True, tp=None):
+        """tp = (size, rank, unique_id): this process is one rank of a
+        tensor-parallel group (one process per GPU; every rank makes the same
+        calls in the same order). Weights are passed whole on every rank."""
         self.L = _lib.load()
         self.shape = dict(shape)
         self.max_seq = int(max_seq)
@@ -43,7 +57,13 @@ class Engine:
         o = _lib.Opts(int(device), int(max_seq), _lib.KV_BF16 if kv_dtype == "bf16" else _lib.KV_F32,
                       1 if use_graphs else 0)
         h = C.c_void_p()
-        st = self.L.myos_ctx_create(C.byref(s), C.byref(o), C.byref(h))
+        if tp is None:
+            st = self.L.myos_ctx_create(C.byref(s), C.byref(o), C.byref(h))
+        else:
+            size, rank, uid = tp
+            t = _lib.TP(int(size), int(rank))
+            C.memmove(t.unique_id, bytes(uid), 128)
+            st = self.L.myos_ctx_create_tp(C.byref(s), C.byref(o), C.byref(t), C.byref(h))
         if st != 0:
             raise MyosError(st, "myos_ctx_create failed")
         self.h = h

@@ -106,6 +106,36 @@ myos_shape myos_shape_qwen25_14b(void);
  * the workspace (BlockWorkspace::new, qwen25_block.rs:96-114) in HBM. */
 int myos_ctx_create(const myos_shape* shape, const myos_opts* opts, myos_ctx** out);
 void myos_ctx_destroy(myos_ctx* ctx);
+
+/* Tensor parallelism over `size` GPUs, one process (and one context) per
+ * GPU. The reference runs one process on one device and has no sharded
+ * mode; this splits the same token step: q/k/v rows and attention by head,
+ * o_proj and down_proj by input column (each projection's epilogue stores
+ * its rows into every rank's inbox over peer memory and a one-block kernel
+ * sums the ranks' parts in rank order; MYOS_TP_COMM=nccl, or GPUs that
+ * cannot map each other's memory, use NCCL allreduce instead), gate/up by
+ * row, and the output head by vocabulary row with a global first-maximum
+ * pick. A rank's device waits on the others are bounded in time (60 s) and
+ * end the call with MYOS_ERR_TIMEOUT; the context is not usable after that.
+ * Weights are passed
+ * whole to myos_load_tensor / myos_load_safetensors on every rank; each
+ * rank keeps its slice. Every rank makes the same calls with the same
+ * arguments, in the same order (host output pointers may be null on ranks
+ * that do not read them). Needs size | num_q_heads, num_kv_heads,
+ * intermediate and vocab, and (num_q_heads / size) * head_dim a multiple of
+ * 256 (MYOS_ERR_SHAPE otherwise). The GEMM prefill, batched decode, the
+ * persistent step kernel and myos_profile_kernels are single-GPU paths
+ * (prefill runs as token steps). At most 8 ranks (MYOS_ERR_ARG otherwise). */
+typedef struct myos_tp {
+  int32_t size;
+  int32_t rank;
+  uint8_t unique_id[128]; /* from myos_tp_unique_id on one rank, sent to all */
+} myos_tp;
+
+/* A fresh NCCL unique id (the rendezvous token every rank passes in). */
+int myos_tp_unique_id(uint8_t out[128]);
+int myos_ctx_create_tp(const myos_shape* shape, const myos_opts* opts, const myos_tp* tp,
+                       myos_ctx** out);
 const char* myos_last_error(const myos_ctx* ctx);
 
 /* One named tensor from any WeightMap-shaped source

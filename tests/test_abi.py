@@ -50,6 +50,28 @@ def test_version_and_shapes_need_no_gpu():
     assert b["hidden"] == 5120 and b["num_layers"] == 48 and b["tied_head"] == 0
 
 
+def test_tensor_parallel_split_is_checked_before_any_device_work():
+    """myos_ctx_create_tp refuses splits that do not divide the model (and
+    bad ranks) from the shape alone: no GPU, no NCCL."""
+    import ctypes as C
+    L = _lib.load()
+    opts = _lib.Opts(0, 64, _lib.KV_F32, 1)
+
+    def create(shape, size, rank):
+        t = _lib.TP(size, rank)
+        h = C.c_void_p()
+        return L.myos_ctx_create_tp(C.byref(shape), C.byref(opts), C.byref(t), C.byref(h))
+
+    small = L.myos_shape_qwen25_1_5b()  # 12 q heads, 2 kv heads
+    big = L.myos_shape_qwen25_14b()     # 40 q heads, 8 kv heads, head_dim 128
+    assert create(small, 4, 0) == _lib.ERR_SHAPE   # 2 kv heads over 4 ranks
+    assert create(small, 3, 0) == _lib.ERR_SHAPE   # 2 kv heads over 3 ranks
+    assert create(big, 8, 0) == _lib.ERR_SHAPE     # 5 q heads x 128 is not 256-aligned
+    assert create(small, 2, 2) == _lib.ERR_ARG     # rank out of range
+    assert create(small, 0, 0) == _lib.ERR_ARG
+    assert C.sizeof(_lib.TP) == 136
+
+
 def _write(path, entries, pad=True, metadata=None):
     header = {}
     off = 0

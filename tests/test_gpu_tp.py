@@ -1,0 +1,97 @@
+"""Tensor parallelism over two GPUs (one process per GPU, NCCL between
+them): Qwen2.5-1.5B with seeded random-init BF16 weights, a 32-id prompt and
+32 greedy steps, against the oracle under the same pass rule as the
+single-GPU test (greedy ids equal the oracle's before the first step whose
+top-2 gap is below tolerance; teacher-forced argmax equal wherever the gap is
+not; logits within 1e-2 absolute / 1e-3 relative). Both ranks must also
+return identical ids and logits.
+
+The split (heads, MLP columns padded 4480 -> 4608, vocabulary rows) sums
+the projections' partial results across ranks, so the order of the f32
+additions differs from one GPU's; the tolerance covers that.
+"""
+import multiprocessing as mp
+
+import numpy as np
+import pytest
+
+from myos import synth
+
+pytestmark = [pytest.mark.gpu, pytest.mark.slow]
+
+SEED = 1234
+N_PROMPT, N_GEN = 32, 32
+ATOL, RTOL = 1e-2, 1e-3
+TIMEOUT_S = 900
+
+
+def _gpu_count() -> int:
+    import torch
+    return torch.cuda.device_count()
+
+
+def _rank(q, idq, size, rank, shape, forced):
+    from myos import tp
+    try:
+        # rank 0 makes the rendezvous id in its own process (its NCCL hosts
+        # the bootstrap root) and hands it to the other ranks
+        if rank == 0:
+            uid = tp.tp_unique_id()
+            for _ in range(size - 1):
+                idq.put(uid)
+        else:
+            uid = idq.get(timeout=TIMEOUT_S)
+        q.put((rank, tp.run_rank(size, rank, uid, shape, SEED, N_PROMPT, N_GEN, forced=forced)))
+    except Exception as ex:  # reported by the parent
+        q.put((rank, repr(ex)))
+
+
+@pytest.fixture(scope="module")
+def golden(orc):
+    if _gpu_count() < 2:
+        pytest.skip("tensor parallelism needs two GPUs")
+    import ref_fixtures as rf
+    shape = synth.shape_qwen25_1_5b()
+    table = synth.weights(shape, SEED)
+    prompt = synth.prompt_ids(SEED, N_PROMPT, shape["vocab"])
+    wm = rf.load_into_oracle(orc, table)
+    md = orc.Model(rf.oracle_shape(orc, shape), N_PROMPT + N_GEN)
+    assert md.prefill(wm, prompt) == 0
+    pre = md.logits()
+    st, ids, gap, _ = md.greedy_decode(wm, N_GEN)
+    assert st == 0
+    return shape, dict(prefill=pre, ids=np.asarray(ids), gap=np.asarray(gap), final=md.logits())
+
+
+def test_tp2_matches_oracle(golden):
+    shape, g = golden
+    ctx = mp.get_context("spawn")
+    q, idq = ctx.Queue(), ctx.Queue()
+    procs = [ctx.Process(target=_rank, args=(q, idq, 2, r, shape, g["ids"])) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = {}
+    try:
+        for _ in procs:
+            rank, out = q.get(timeout=TIMEOUT_S)
+            res[rank] = out
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    for r in (0, 1):
+        assert isinstance(res[r], dict), res[r]
+    a, b = res[0], res[1]
+    for k in ("prefill", "ids", "final", "forced_argmax", "forced_final"):
+        np.testing.assert_array_equal(a[k], b[k], err_msg=k)
+    np.testing.assert_allclose(a["prefill"], g["prefill"], atol=ATOL, rtol=RTOL)
+    ref, gap = g["ids"], g["gap"]
+    first_close = next((i for i in range(N_GEN) if gap[i] < ATOL), N_GEN)
+    diverge = next((i for i in range(N_GEN) if a["ids"][i] != ref[i]), N_GEN)
+    assert diverge >= first_close, (diverge, first_close)
+    if diverge == N_GEN:
+        np.testing.assert_allclose(a["final"], g["final"], atol=ATOL, rtol=RTOL)
+    bad = [i for i in range(N_GEN) if a["forced_argmax"][i] != ref[i] and gap[i] >= ATOL]
+    assert not bad, bad
+    np.testing.assert_allclose(a["forced_final"], g["final"], atol=ATOL, rtol=RTOL)
