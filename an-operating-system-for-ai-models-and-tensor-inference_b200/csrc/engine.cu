@@ -945,7 +945,7 @@ static int create_impl(myos_ctx* c, const myos_shape* shape, const myos_opts* op
     // up rows adjacent (one [2I, H] projection), a supported head dim.
     const char* e = getenv("MYOS_PREFILL");
     const bool want = !(e && e[0] == 's');
-    bool ok = want && c->tp_size == 1 && pf_attn_supported((int)d, (int)c->G) && H % 64 == 0 && I % 64 == 0 &&
+    bool ok = want && pf_attn_supported((int)d, (int)c->G) && H % 64 == 0 && I % 64 == 0 &&
               c->qd % 64 == 0 && (c->qd + 2 * c->kvd) % 64 == 0;
     for (size_t l = 0; ok && l < L; ++l) ok = c->layers[l].wu == c->layers[l].wg + I * H;
     if (ok) {
@@ -1430,6 +1430,19 @@ int prefill_chunk(myos_ctx* c, const uint32_t* d_ids, int n, int p0, void* kcach
         gemm_bf16_f32(M, N, K, c->pf_A, W, nullptr, c->pf_D, 0.0f, c->pf_ws, c->pf_ws_bytes, st);
     return e == cudaSuccess ? MYOS_OK : fail(c, MYOS_ERR_CUDA, std::string("prefill gemm: ") + cudaGetErrorString(e));
   };
+  // residual += the projection (hi + lo rows of pf_D); under tensor
+  // parallelism each rank's part (rank 0's with the residual) is summed
+  // over the ranks with one NCCL allreduce of the chunk's rows
+  auto resid = [&](int rows, int N) -> int {
+    if (c->tp_size == 1) {
+      CK(pf_resid(c->pf_X, c->pf_D, rows, N, st));
+      return MYOS_OK;
+    }
+    CK(pf_resid_part(c->pf_D, c->tp_rank == 0 ? c->pf_X : nullptr, rows, N, st));
+    if (!tp_allreduce_sum(c->pf_D, c->pf_X, (size_t)rows * N, c->comm, st))
+      return fail(c, MYOS_ERR_NCCL, "allreduce of the prefill residual failed");
+    return MYOS_OK;
+  };
   int rc;
   CK(pf_embed(c->pf_X, c->embed, d_ids, n, H, st));
   for (int l = 0; l < (int)s.num_layers; ++l) {
@@ -1443,12 +1456,12 @@ int prefill_chunk(myos_ctx* c, const uint32_t* d_ids, int n, int p0, void* kcach
     CK(pf_attn(c->pf_att, c->pf_Q, kc, vc, kv_bf16, p0, n, Hq, Hkv, d, S, scale, st));
     CK(pf_norm_split(c->pf_A, c->pf_att, nullptr, n, qd, 0.0f, st));
     if ((rc = gemm(H, qd, w.wo))) return rc;
-    CK(pf_resid(c->pf_X, c->pf_D, n, H, st));
+    if ((rc = resid(n, H))) return rc;
     CK(pf_norm_split(c->pf_A, c->pf_X, w.ln2, n, H, s.rms_eps, st));
     if ((rc = gemm(2 * I, H, w.wg))) return rc;  // gate rows then up rows
     CK(pf_swiglu_split(c->pf_A, c->pf_D, n, I, st));
     if ((rc = gemm(H, I, w.wd))) return rc;
-    CK(pf_resid(c->pf_X, c->pf_D, n, H, st));
+    if ((rc = resid(n, H))) return rc;
   }
   return MYOS_OK;
 }

@@ -216,6 +216,17 @@ __global__ void k_pf_resid(float* X, const float* D, int n, int N) {
         __fadd_rn(X[(size_t)t * N + j], __fadd_rn(D[(size_t)t * N + j], D[(size_t)(n + t) * N + j]));
 }
 
+// Tensor-parallel form: this rank's part of the residual update, written in
+// place over the hi rows of D: X + (hi + lo) on the rank that carries the
+// residual (X non-null), hi + lo elsewhere; the ranks' parts are then summed.
+__global__ void k_pf_resid_part(float* D, const float* X, int n, int N) {
+  const int t = blockIdx.x;
+  for (int j = threadIdx.x; j < N; j += blockDim.x) {
+    const float dl = __fadd_rn(D[(size_t)t * N + j], D[(size_t)(n + t) * N + j]);
+    D[(size_t)t * N + j] = X ? __fadd_rn(X[(size_t)t * N + j], dl) : dl;
+  }
+}
+
 // h = (g / (1 + expf(-g))) * u (swiglu.rs:113-131) from the stacked gate|up
 // projection, written as bf16 halves for the down projection.
 __global__ void k_pf_swiglu_split(uint16_t* A, const float* D, int n, int I) {
@@ -358,6 +369,11 @@ cudaError_t pf_attn(float* out, const float* Q, const void* kc, const void* vc, 
 
 cudaError_t pf_resid(float* X, const float* D, int n, int N, cudaStream_t st) {
   k_pf_resid<<<n, kT, 0, st>>>(X, D, n, N);
+  return cudaGetLastError();
+}
+
+cudaError_t pf_resid_part(float* D, const float* X, int n, int N, cudaStream_t st) {
+  k_pf_resid_part<<<n, kT, 0, st>>>(D, X, n, N);
   return cudaGetLastError();
 }
 

@@ -27,6 +27,9 @@ cudaError_t pf_rows_copy(float* dst, const float* src, const int* src_row, int B
                          cudaStream_t st);
 cudaError_t pf_pos_advance(int* rowpos, int B, cudaStream_t st);
 cudaError_t pf_resid(float* X, const float* D, int n, int N, cudaStream_t st);
+// D[t] = (X ? X[t] : 0) + D[t] + D[n + t] over rows t < n (in place; the
+// tensor-parallel part before the sum over ranks).
+cudaError_t pf_resid_part(float* D, const float* X, int n, int N, cudaStream_t st);
 cudaError_t pf_swiglu_split(uint16_t* A, const float* D, int n, int I, cudaStream_t st);
 
 }  // namespace myos

@@ -111,7 +111,7 @@ void myos_ctx_destroy(myos_ctx* ctx);
  * GPU. The reference runs one process on one device and has no sharded
  * mode; this splits the same token step: q/k/v rows and attention by head,
  * o_proj and down_proj by input column (each projection's epilogue stores
- * its rows into every rank's inbox over peer memory and a one-block kernel
+ * its rows into every rank's inbox over peer memory and a small kernel
  * sums the ranks' parts in rank order; MYOS_TP_COMM=nccl, or GPUs that
  * cannot map each other's memory, use NCCL allreduce instead), gate/up by
  * row, and the output head by vocabulary row with a global first-maximum
@@ -123,9 +123,10 @@ void myos_ctx_destroy(myos_ctx* ctx);
  * arguments, in the same order (host output pointers may be null on ranks
  * that do not read them). Needs size | num_q_heads, num_kv_heads,
  * intermediate and vocab, and (num_q_heads / size) * head_dim a multiple of
- * 256 (MYOS_ERR_SHAPE otherwise). The GEMM prefill, batched decode, the
- * persistent step kernel and myos_profile_kernels are single-GPU paths
- * (prefill runs as token steps). At most 8 ranks (MYOS_ERR_ARG otherwise). */
+ * 256 (MYOS_ERR_SHAPE otherwise). The tensor-core prefill sums each chunk's
+ * residual parts with an NCCL allreduce. Batched decode, the persistent step
+ * kernel and myos_profile_kernels are single-GPU paths (MYOS_ERR_UNSUPPORTED).
+ * At most 8 ranks (MYOS_ERR_ARG otherwise). */
 typedef struct myos_tp {
   int32_t size;
   int32_t rank;
