@@ -91,9 +91,11 @@ struct myos_ctx {
   StepCtl* ctl_host = nullptr;  // pinned mirror for uploads
   // launch geometry
   int grid_qkv = 0, grid_o = 0, grid_gu = 0, grid_down = 0, grid_head = 0;
+  int warps_qkv = 0, warps_o = 0, warps_gu = 0, warps_down = 0, warps_head = 0;
   int attn_chunk = 0, attn_nsplit = 0;
   int defer_merge = 0;  // o_proj staging merges the attention splits
   int l2pf_mode = 0;    // MYOS_L2PF: qkv kernels prefetch the layer's MLP weights into L2
+  int l2pf_mask = 7;    // MYOS_L2PF_MASK: which of them (1 gate, 2 up, 4 down)
   int attn_cluster = 0; // attention splits merge across a thread-block cluster
   // GEMM prefill (chunks of pf_chunk prompt tokens through the tensor cores)
   bool pf_ok = false;
@@ -317,6 +319,7 @@ int launch_kind(myos_ctx* c, int kind, int l, const uint32_t* feed, bool pdl, bo
     h.rec_fed = c->profiling ? nullptr : c->rec_fed;
     h.rec_argmax = c->profiling ? nullptr : c->rec_argmax;
     h.tr = ktrace_at(c, 5 * (int)s.num_layers);
+    h.warps = c->warps_head;
     if (c->tp_size > 1) {
       h.row0 = c->head_row0;
       if (c->tp_p2p) h.push = c->push_c;
@@ -354,12 +357,15 @@ int launch_kind(myos_ctx* c, int kind, int l, const uint32_t* feed, bool pdl, bo
     q.err = &c->ctl->err;
     q.prefetch_cap = prefetch_cap(c, c->grid_qkv);
     q.tr = ktrace_at(c, 5 * l + K_QKV);
+    q.warps = c->warps_qkv;
     if (c->l2pf_mode) {  // this layer's MLP weights, for gate/up and down
       const size_t mat = (size_t)I * H * 2;
-      q.pf_ptr[0] = w.wg;
-      q.pf_ptr[1] = w.wu;
-      q.pf_ptr[2] = w.wd;
-      q.pf_bytes[0] = q.pf_bytes[1] = q.pf_bytes[2] = mat;
+      const uint16_t* m[3] = {w.wg, w.wu, w.wd};
+      for (int r = 0; r < 3; ++r)
+        if (c->l2pf_mask >> r & 1) {
+          q.pf_ptr[r] = m[r];
+          q.pf_bytes[r] = mat;
+        }
       q.pf_mode = c->l2pf_mode;
     }
     CK(launch_gemv(EPI_BIAS, q, c->grid_qkv, c->st, pdl));
@@ -409,6 +415,7 @@ int launch_kind(myos_ctx* c, int kind, int l, const uint32_t* feed, bool pdl, bo
     o.err = &c->ctl->err;
     o.prefetch_cap = prefetch_cap(c, c->grid_o);
     o.tr = ktrace_at(c, 5 * l + K_O);
+    o.warps = c->warps_o;
     tp_partial(c, &o, K_O);
     CK(launch_gemv(EPI_RESID, o, c->grid_o, c->st, pdl));
     if (int st = tp_sum_resid(c, K_O)) return st;
@@ -426,6 +433,7 @@ int launch_kind(myos_ctx* c, int kind, int l, const uint32_t* feed, bool pdl, bo
     gu.err = &c->ctl->err;
     gu.prefetch_cap = prefetch_cap(c, c->grid_gu);
     gu.tr = ktrace_at(c, 5 * l + K_GU);
+    gu.warps = c->warps_gu;
     CK(launch_gemv(EPI_SWIGLU, gu, c->grid_gu, c->st, pdl));
   } else if (kind == K_DOWN) {
     GemvArgs dn = {};
@@ -438,6 +446,7 @@ int launch_kind(myos_ctx* c, int kind, int l, const uint32_t* feed, bool pdl, bo
     dn.err = &c->ctl->err;
     dn.prefetch_cap = prefetch_cap(c, c->grid_down);
     dn.tr = ktrace_at(c, 5 * l + K_DOWN);
+    dn.warps = c->warps_down;
     tp_partial(c, &dn, K_DOWN);
     CK(launch_gemv(EPI_RESID, dn, c->grid_down, c->st, pdl));
     if (int st = tp_sum_resid(c, K_DOWN)) return st;
@@ -809,6 +818,11 @@ static int create_impl(myos_ctx* c, const myos_shape* shape, const myos_opts* op
   c->grid_gu = gemv_grid((int)I, (int)H, 2, c->num_sms);
   c->grid_down = gemv_grid((int)H, (int)I, 1, c->num_sms);
   c->grid_head = gemv_grid((int)c->head_rows, (int)H, 1, c->num_sms);
+  c->warps_qkv = gemv_warps((int)(c->qd + 2 * c->kvd), (int)H, 1, true, c->grid_qkv);
+  c->warps_o = gemv_warps((int)H, (int)c->qd, 1, false, c->grid_o);
+  c->warps_gu = gemv_warps((int)I, (int)H, 2, true, c->grid_gu);
+  c->warps_down = gemv_warps((int)H, (int)I, 1, false, c->grid_down);
+  c->warps_head = gemv_warps((int)c->head_rows, (int)H, 1, true, c->grid_head);
   size_t nsplit = (S + 31) / 32;
   size_t cap = (size_t)c->num_sms / s.num_kv_heads;
   if (cap < 1) cap = 1;
@@ -823,6 +837,7 @@ static int create_impl(myos_ctx* c, const myos_shape* shape, const myos_opts* op
     const bool want = e && e[0] == '1';
     const char* pf = getenv("MYOS_L2PF");
     c->l2pf_mode = pf ? atoi(pf) : 0;
+    if (const char* pm = getenv("MYOS_L2PF_MASK")) c->l2pf_mask = atoi(pm);
     c->defer_merge = want && s.num_q_heads <= 256 &&
                      merge_smem_bytes((int)s.num_q_heads, (int)nsplit, (int)d) <= (96u << 10);
     // MYOS_ATTN_CLUSTER=0 keeps the global-memory last-block merge

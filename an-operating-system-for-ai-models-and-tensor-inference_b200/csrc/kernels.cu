@@ -1841,10 +1841,29 @@ int gemv_grid(int M, int K, int NR, int num_sms) {
     return g < cap ? (g < 1 ? 1 : g) : cap;
   }
   // Up to two blocks per SM, at least MYOS_GEMV_MIN_ROWS (8) rows a block.
+  // MYOS_GEMV_BALANCE=1: past one block per SM, exactly two per SM with the
+  // rows spread over fewer warps (gemv_warps). Measured slower for the 1.5B
+  // step (every extra block stages the whole input vector again: down_proj
+  // 8.7 -> 9.0 us), so off by default.
   const int min_rows = env_int("MYOS_GEMV_MIN_ROWS", 8);
   int g = (M + min_rows - 1) / min_rows;
+  if (g > num_sms && env_int("MYOS_GEMV_BALANCE", 0)) g = 2 * num_sms;
   if (g > 2 * num_sms) g = 2 * num_sms;
   return g < 1 ? 1 : g;
+}
+
+int gemv_warps(int M, int K, int NR, bool has_gamma, int grid) {
+  const int full = kThreads / 32;
+  if (!env_int("MYOS_GEMV_BALANCE", 0) || grid < 1) return full;
+  const int rows = (M + grid - 1) / grid;           // most rows a block holds
+  const int per_warp = (rows + full - 1) / full;    // rows a warp takes at full width
+  int nw = (rows + per_warp - 1) / per_warp;        // fewest warps with that many each
+  const int nchunk = K >> 3, per = has_gamma ? kGammaRegs : kStageOne;
+  const int nw_min = (nchunk + per * 32 - 1) / (per * 32);  // one-trip staging
+  if (nw_min > full) return full;  // staged in several trips: all threads help
+  if (nw < nw_min) nw = nw_min;
+  (void)NR;
+  return nw < 1 ? 1 : (nw > full ? full : nw);
 }
 
 cudaError_t launch_gemv(int epi, const GemvArgs& a0, int grid, cudaStream_t st, bool pdl) {
@@ -1879,6 +1898,7 @@ cudaError_t launch_gemv(int epi, const GemvArgs& a0, int grid, cudaStream_t st, 
   const bool stream = (a.K % 256) == 0 && ((uintptr_t)a.w & 15) == 0 &&
                       (epi != EPI_SWIGLU || ((uintptr_t)a.w2 & 15) == 0) && !getenv_legacy();
   if (stream) {
+    if (a.warps > 0 && a.warps < kThreads / 32) cfg.blockDim = dim3(32 * a.warps);
     const int P = a.K / 256;
     switch (epi) {
       case EPI_STORE: return launch_stream<EPI_STORE, 1>(a, pick_batch(P, 1), cfg);

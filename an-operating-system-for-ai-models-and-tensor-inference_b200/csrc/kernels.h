@@ -111,6 +111,7 @@ struct GemvArgs {
   float* tp_cand;
   uint32_t row0;
   TpPush push;
+  int warps;  // streaming kernel: warps per block (0: the full block); gemv_warps
 };
 
 // Global first maximum over the tensor-parallel ranks' candidates
@@ -167,6 +168,9 @@ size_t gemv_smem_bytes(int K);
 // launch_gemv will pick: the bulk-copy kernel runs one block per SM (fewer
 // when there are fewer stages than SMs).
 int gemv_grid(int M, int K, int NR, int num_sms);
+// Warps per block of the streaming kernel for that grid: rows spread evenly
+// over the warps, and at least enough threads to stage the input in one trip.
+int gemv_warps(int M, int K, int NR, bool has_gamma, int grid);
 size_t attn_smem_bytes(int G, int d);
 int attn_dpl(int d);
 

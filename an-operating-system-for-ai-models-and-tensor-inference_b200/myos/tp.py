@@ -76,6 +76,9 @@ def main() -> None:
     ap.add_argument("--kv", choices=["f32", "bf16"], default="f32")
     ap.add_argument("--seed", type=int, default=1234)
     ap.add_argument("--iters", type=int, default=3)
+    ap.add_argument("--ktrace", default="",
+                    help="write each rank's launch timeline of the last call to PREFIX_r<rank>.bin "
+                         "(MYOS_KTRACE_FILE; keep --n-gen <= 64, see myos.ktrace)")
     args = ap.parse_args()
 
     import torch.distributed as dist
@@ -84,6 +87,8 @@ def main() -> None:
     rank = int(os.environ.get("RANK", "0"))
     size = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", str(rank)))
+    if args.ktrace:
+        os.environ["MYOS_KTRACE_FILE"] = "%s_r%d.bin" % (args.ktrace, rank)
     dist.init_process_group("gloo", rank=rank, world_size=size, timeout=timedelta(seconds=600))
     box = [tp_unique_id() if rank == 0 else None]
     dist.broadcast_object_list(box, src=0)
