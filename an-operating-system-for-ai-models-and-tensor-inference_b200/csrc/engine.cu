@@ -67,6 +67,7 @@ struct myos_ctx {
   cudaStream_t st = nullptr, copy_st = nullptr;
   std::string err;
   size_t qd = 0, kvd = 0, G = 1;
+  size_t qd_pad = 0;  // o_proj input width: qd, or (tensor parallel) qd rounded up to 256
   // HBM
   uint8_t* warena = nullptr;
   size_t warena_bytes = 0;
@@ -399,7 +400,7 @@ int launch_kind(myos_ctx* c, int kind, int l, const uint32_t* feed, bool pdl, bo
     GemvArgs o = {};
     o.w = w.wo;
     o.M = H;
-    o.K = (int)c->qd;
+    o.K = (int)c->qd_pad;
     o.in.x = c->attn;
     o.in.ctl = c->ctl;
     if (c->defer_merge) {  // the staging merges the attention splits
@@ -763,6 +764,10 @@ static int create_impl(myos_ctx* c, const myos_shape* shape, const myos_opts* op
   const myos_shape& s = c->s;
   c->qd = (size_t)s.num_q_heads * s.head_dim;
   c->kvd = (size_t)s.num_kv_heads * s.head_dim;
+  // A tensor-parallel rank's o_proj slice is zero-padded to a multiple of
+  // 256 columns (the streaming GEMV's width), fed by a zero-padded attention
+  // output (14B at 8 ranks: 5 heads x 128 = 640 -> 768).
+  c->qd_pad = c->tp_size > 1 ? (c->qd + 255) / 256 * 256 : c->qd;
   c->G = s.num_q_heads / s.num_kv_heads;
   const size_t H = s.hidden, I = s.intermediate, V = s.vocab, L = s.num_layers;
   // weight arena
@@ -778,7 +783,7 @@ static int create_impl(myos_ctx* c, const myos_shape* shape, const myos_opts* op
   std::vector<size_t> lo(L * 8);
   for (size_t l = 0; l < L; ++l) {
     lo[l * 8 + 0] = take((c->qd + 2 * c->kvd) * H * 2);
-    lo[l * 8 + 1] = take(H * c->qd * 2);
+    lo[l * 8 + 1] = take(H * c->qd_pad * 2);
     lo[l * 8 + 2] = take(I * H * 2);
     lo[l * 8 + 3] = take(I * H * 2);
     lo[l * 8 + 4] = take(H * I * 2);
@@ -814,12 +819,12 @@ static int create_impl(myos_ctx* c, const myos_shape* shape, const myos_opts* op
   CK(cudaMemset(c->vcache, 0, L * c->kv_layer_elems * kv_elt));
   // geometry
   c->grid_qkv = gemv_grid((int)(c->qd + 2 * c->kvd), (int)H, 1, c->num_sms);
-  c->grid_o = gemv_grid((int)H, (int)c->qd, 1, c->num_sms);
+  c->grid_o = gemv_grid((int)H, (int)c->qd_pad, 1, c->num_sms);
   c->grid_gu = gemv_grid((int)I, (int)H, 2, c->num_sms);
   c->grid_down = gemv_grid((int)H, (int)I, 1, c->num_sms);
   c->grid_head = gemv_grid((int)c->head_rows, (int)H, 1, c->num_sms);
   c->warps_qkv = gemv_warps((int)(c->qd + 2 * c->kvd), (int)H, 1, true, c->grid_qkv);
-  c->warps_o = gemv_warps((int)H, (int)c->qd, 1, false, c->grid_o);
+  c->warps_o = gemv_warps((int)H, (int)c->qd_pad, 1, false, c->grid_o);
   c->warps_gu = gemv_warps((int)I, (int)H, 2, true, c->grid_gu);
   c->warps_down = gemv_warps((int)H, (int)I, 1, false, c->grid_down);
   c->warps_head = gemv_warps((int)c->head_rows, (int)H, 1, true, c->grid_head);
@@ -838,7 +843,7 @@ static int create_impl(myos_ctx* c, const myos_shape* shape, const myos_opts* op
     const char* pf = getenv("MYOS_L2PF");
     c->l2pf_mode = pf ? atoi(pf) : 0;
     if (const char* pm = getenv("MYOS_L2PF_MASK")) c->l2pf_mask = atoi(pm);
-    c->defer_merge = want && s.num_q_heads <= 256 &&
+    c->defer_merge = want && c->qd_pad == c->qd && s.num_q_heads <= 256 &&
                      merge_smem_bytes((int)s.num_q_heads, (int)nsplit, (int)d) <= (96u << 10);
     // MYOS_ATTN_CLUSTER=0 keeps the global-memory last-block merge
     const char* ce = getenv("MYOS_ATTN_CLUSTER");
@@ -847,7 +852,8 @@ static int create_impl(myos_ctx* c, const myos_shape* shape, const myos_opts* op
   // workspace
   CK(cudaMalloc(&c->resid, H * 4));
   CK(cudaMalloc(&c->qkv, (c->qd + 2 * c->kvd) * 4));
-  CK(cudaMalloc(&c->attn, c->qd * 4));
+  CK(cudaMalloc(&c->attn, c->qd_pad * 4));
+  CK(cudaMemset(c->attn, 0, c->qd_pad * 4));  // the padding stays zero
   CK(cudaMalloc(&c->act, I * 4));
   CK(cudaMalloc(&c->logits, V * 4));
   CK(cudaMemset(c->logits, 0, V * 4));
@@ -1048,7 +1054,7 @@ int myos_ctx_create_tp(const myos_shape* shape, const myos_opts* opts, const myo
       return MYOS_ERR_ARG;
     const uint32_t N = (uint32_t)tp->size;
     if (shape->num_q_heads % N || shape->num_kv_heads % N || shape->intermediate % N ||
-        shape->vocab % N || (shape->num_q_heads / N) * shape->head_dim % 256)
+        shape->vocab % N || ((shape->num_q_heads / N) * shape->head_dim) % 8)
       return MYOS_ERR_SHAPE;
   }
   myos_ctx* c = new myos_ctx();
@@ -1183,7 +1189,7 @@ int myos_load_tensor(myos_ctx* c, const char* name, int32_t dtype, const int64_t
       case 4: st = stage_bf16_as_f32(c, w.bqkv + qdl, src + rk * kvdl * 2, kvdl); break;
       case 5: st = rows(w.wqkv + (qdl + kvdl) * H, rk * kvdl, kvdl, H); break;
       case 6: st = stage_bf16_as_f32(c, w.bqkv + qdl + kvdl, src + rk * kvdl * 2, kvdl); break;
-      case 7: st = cols(w.wo, H, qd, rk * qdl, qdl, qdl); break;
+      case 7: st = cols(w.wo, H, qd, rk * qdl, qdl, c->qd_pad); break;
       case 8: st = stage_bf16_as_f32(c, w.ln2, bytes, H); break;
       case 9: st = rows(w.wg, rk * Ic, Ic, H); break;
       case 10: st = rows(w.wu, rk * Ic, Ic, H); break;
@@ -1440,9 +1446,9 @@ int prefill_chunk(myos_ctx* c, const uint32_t* d_ids, int n, int p0, void* kcach
   const size_t kv_elt = kv_bf16 ? 2 : 4;
   const float scale = 1.0f / sqrtf((float)d);
   cudaStream_t st = c->st;
-  auto gemm = [&](int N, int K, const uint16_t* W) {
-    const cudaError_t e =
-        gemm_bf16_f32(M, N, K, c->pf_A, W, nullptr, c->pf_D, 0.0f, c->pf_ws, c->pf_ws_bytes, st);
+  auto gemm = [&](int N, int K, const uint16_t* W, int ldw = 0) {
+    const cudaError_t e = gemm_bf16_f32(M, N, K, c->pf_A, W, nullptr, c->pf_D, 0.0f, c->pf_ws,
+                                        c->pf_ws_bytes, st, ldw);
     return e == cudaSuccess ? MYOS_OK : fail(c, MYOS_ERR_CUDA, std::string("prefill gemm: ") + cudaGetErrorString(e));
   };
   // residual += the projection (hi + lo rows of pf_D); under tensor
@@ -1470,7 +1476,7 @@ int prefill_chunk(myos_ctx* c, const uint32_t* d_ids, int n, int p0, void* kcach
     CK(pf_rope_store(c->pf_Q, kc, vc, kv_bf16, c->cos_t, c->sin_t, p0, n, Hq, Hkv, d, S, st));
     CK(pf_attn(c->pf_att, c->pf_Q, kc, vc, kv_bf16, p0, n, Hq, Hkv, d, S, scale, st));
     CK(pf_norm_split(c->pf_A, c->pf_att, nullptr, n, qd, 0.0f, st));
-    if ((rc = gemm(H, qd, w.wo))) return rc;
+    if ((rc = gemm(H, qd, w.wo, (int)c->qd_pad))) return rc;
     if ((rc = resid(n, H))) return rc;
     CK(pf_norm_split(c->pf_A, c->pf_X, w.ln2, n, H, s.rms_eps, st));
     if ((rc = gemm(2 * I, H, w.wg))) return rc;  // gate rows then up rows

@@ -49,13 +49,14 @@ using Kernel = cutlass::gemm::kernel::GemmUniversal<Shape<int, int, int, int>, M
 using Gemm = cutlass::gemm::device::GemmUniversalAdapter<Kernel>;
 
 typename Gemm::Arguments make_args(int M, int N, int K, const uint16_t* A, const uint16_t* W,
-                                   const float* C, float* D, float beta) {
+                                   const float* C, float* D, float beta, int ldw = 0) {
   using StrideA = typename Gemm::GemmKernel::StrideA;
   using StrideB = typename Gemm::GemmKernel::StrideB;
   using StrideC = typename Gemm::GemmKernel::StrideC;
   using StrideD = typename Gemm::GemmKernel::StrideD;
   const StrideA sa = cutlass::make_cute_packed_stride(StrideA{}, {M, K, 1});
-  const StrideB sb = cutlass::make_cute_packed_stride(StrideB{}, {N, K, 1});
+  StrideB sb = cutlass::make_cute_packed_stride(StrideB{}, {N, K, 1});
+  if (ldw > K) cute::get<0>(sb) = ldw;  // W row n starts n * ldw elements in
   const StrideC sc = cutlass::make_cute_packed_stride(StrideC{}, {M, N, 1});
   const StrideD sd = cutlass::make_cute_packed_stride(StrideD{}, {M, N, 1});
   typename Gemm::Arguments args{cutlass::gemm::GemmUniversalMode::kGemm,
@@ -79,9 +80,9 @@ size_t gemm_workspace_bytes(int M, int N, int K) {
 
 cudaError_t gemm_bf16_f32(int M, int N, int K, const uint16_t* A, const uint16_t* W,
                           const float* C, float* D, float beta, void* workspace,
-                          size_t workspace_bytes, cudaStream_t st) {
-  if (!gemm_supported(M, N, K)) return cudaErrorInvalidValue;
-  const typename Gemm::Arguments args = make_args(M, N, K, A, W, C, D, beta);
+                          size_t workspace_bytes, cudaStream_t st, int ldw) {
+  if (!gemm_supported(M, N, K) || (ldw && (ldw < K || ldw % 8))) return cudaErrorInvalidValue;
+  const typename Gemm::Arguments args = make_args(M, N, K, A, W, C, D, beta, ldw);
   Gemm g;
   if (g.can_implement(args) != cutlass::Status::kSuccess) return cudaErrorInvalidValue;
   if (Gemm::get_workspace_size(args) > workspace_bytes) return cudaErrorInvalidValue;

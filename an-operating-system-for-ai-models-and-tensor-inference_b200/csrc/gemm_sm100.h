@@ -7,11 +7,12 @@
 namespace myos {
 
 // D[M,N] = A[M,K] x W[N,K]^T + beta * C (C may be null when beta == 0); A and
-// W bf16 row-major, C and D f32 row-major; stream-ordered, no allocation.
+// W bf16 row-major (W's rows ldw >= K elements apart; 0: K), C and D f32
+// row-major; stream-ordered, no allocation.
 bool gemm_supported(int M, int N, int K);
 size_t gemm_workspace_bytes(int M, int N, int K);
 cudaError_t gemm_bf16_f32(int M, int N, int K, const uint16_t* A, const uint16_t* W,
                           const float* C, float* D, float beta, void* workspace,
-                          size_t workspace_bytes, cudaStream_t st);
+                          size_t workspace_bytes, cudaStream_t st, int ldw = 0);
 
 }  // namespace myos

@@ -122,8 +122,8 @@ void myos_ctx_destroy(myos_ctx* ctx);
  * rank keeps its slice. Every rank makes the same calls with the same
  * arguments, in the same order (host output pointers may be null on ranks
  * that do not read them). Needs size | num_q_heads, num_kv_heads,
- * intermediate and vocab, and (num_q_heads / size) * head_dim a multiple of
- * 256 (MYOS_ERR_SHAPE otherwise). The tensor-core prefill sums each chunk's
+ * intermediate and vocab (MYOS_ERR_SHAPE otherwise); a rank's MLP rows and
+ * o_proj input columns are zero-padded to multiples of 256. The tensor-core prefill sums each chunk's
  * residual parts with an NCCL allreduce. Batched decode, the persistent step
  * kernel and myos_profile_kernels are single-GPU paths (MYOS_ERR_UNSUPPORTED).
  * At most 8 ranks (MYOS_ERR_ARG otherwise). */

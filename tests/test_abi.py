@@ -66,7 +66,8 @@ def test_tensor_parallel_split_is_checked_before_any_device_work():
     big = L.myos_shape_qwen25_14b()     # 40 q heads, 8 kv heads, head_dim 128
     assert create(small, 4, 0) == _lib.ERR_SHAPE   # 2 kv heads over 4 ranks
     assert create(small, 3, 0) == _lib.ERR_SHAPE   # 2 kv heads over 3 ranks
-    assert create(big, 8, 0) == _lib.ERR_SHAPE     # 5 q heads x 128 is not 256-aligned
+    assert create(big, 3, 0) == _lib.ERR_SHAPE     # 40 q heads over 3 ranks
+    assert create(big, 16, 0) == _lib.ERR_ARG      # more than 8 ranks
     assert create(small, 2, 2) == _lib.ERR_ARG     # rank out of range
     assert create(small, 0, 0) == _lib.ERR_ARG
     assert C.sizeof(_lib.TP) == 136

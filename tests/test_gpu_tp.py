@@ -33,7 +33,7 @@ def _gpu_count() -> int:
     return torch.cuda.device_count()
 
 
-def _rank(q, idq, size, rank, shape, forced, comm, kv):
+def _rank(q, idq, size, rank, shape, forced, comm, kv, n_prompt=N_PROMPT, n_gen=N_GEN):
     import os
     if comm:
         os.environ["MYOS_TP_COMM"] = comm
@@ -47,7 +47,7 @@ def _rank(q, idq, size, rank, shape, forced, comm, kv):
                 idq.put(uid)
         else:
             uid = idq.get(timeout=TIMEOUT_S)
-        q.put((rank, tp.run_rank(size, rank, uid, shape, SEED, N_PROMPT, N_GEN, kv=kv,
+        q.put((rank, tp.run_rank(size, rank, uid, shape, SEED, n_prompt, n_gen, kv=kv,
                                  forced=forced)))
     except Exception as ex:  # reported by the parent
         q.put((rank, repr(ex)))
@@ -70,14 +70,11 @@ def golden(orc):
     return shape, dict(prefill=pre, ids=np.asarray(ids), gap=np.asarray(gap), final=md.logits())
 
 
-@pytest.mark.parametrize("comm,kv", [("", "f32"), ("nccl", "bf16")])
-def test_tp2_matches_oracle(golden, comm, kv):
-    shape, g = golden
-    atol, rtol = TOL[kv]
+def _run_ranks(shape, forced, comm, kv, n_prompt, n_gen):
     ctx = mp.get_context("spawn")
     q, idq = ctx.Queue(), ctx.Queue()
-    procs = [ctx.Process(target=_rank, args=(q, idq, 2, r, shape, g["ids"], comm, kv))
-             for r in range(2)]
+    procs = [ctx.Process(target=_rank, args=(q, idq, 2, r, shape, forced, comm, kv, n_prompt,
+                                             n_gen)) for r in range(2)]
     for p in procs:
         p.start()
     res = {}
@@ -95,13 +92,49 @@ def test_tp2_matches_oracle(golden, comm, kv):
     a, b = res[0], res[1]
     for k in ("prefill", "ids", "final", "forced_argmax", "forced_final"):
         np.testing.assert_array_equal(a[k], b[k], err_msg=k)
+    return a
+
+
+def _check(a, g, atol, rtol, n_gen):
     np.testing.assert_allclose(a["prefill"], g["prefill"], atol=atol, rtol=rtol)
     ref, gap = g["ids"], g["gap"]
-    first_close = next((i for i in range(N_GEN) if gap[i] < atol), N_GEN)
-    diverge = next((i for i in range(N_GEN) if a["ids"][i] != ref[i]), N_GEN)
+    first_close = next((i for i in range(n_gen) if gap[i] < atol), n_gen)
+    diverge = next((i for i in range(n_gen) if a["ids"][i] != ref[i]), n_gen)
     assert diverge >= first_close, (diverge, first_close)
-    if diverge == N_GEN:
+    if diverge == n_gen:
         np.testing.assert_allclose(a["final"], g["final"], atol=atol, rtol=rtol)
-    bad = [i for i in range(N_GEN) if a["forced_argmax"][i] != ref[i] and gap[i] >= atol]
+    bad = [i for i in range(n_gen) if a["forced_argmax"][i] != ref[i] and gap[i] >= atol]
     assert not bad, bad
     np.testing.assert_allclose(a["forced_final"], g["final"], atol=atol, rtol=rtol)
+
+
+@pytest.mark.parametrize("comm,kv", [("", "f32"), ("nccl", "bf16")])
+def test_tp2_matches_oracle(golden, comm, kv):
+    shape, g = golden
+    atol, rtol = TOL[kv]
+    a = _run_ranks(shape, g["ids"], comm, kv, N_PROMPT, N_GEN)
+    _check(a, g, atol, rtol, N_GEN)
+
+
+def test_tp2_padded_slices_match_oracle(orc):
+    """A shape whose per-rank slices need the zero padding: 10 q heads over
+    2 ranks is 5 x 128 = 640 o_proj input columns (padded to 768), and
+    intermediate 3456 / 2 = 1728 MLP rows (padded to 1792); 14B at 8 ranks
+    needs the same o_proj padding."""
+    if _gpu_count() < 2:
+        pytest.skip("tensor parallelism needs two GPUs")
+    import ref_fixtures as rf
+    shape = dict(hidden=1280, num_q_heads=10, num_kv_heads=2, head_dim=128, rope_theta=1e6,
+                 intermediate=3456, vocab=32000, num_layers=4, rms_eps=1e-6, tied_head=True)
+    n_prompt, n_gen = 40, 16
+    table = synth.weights(shape, SEED)
+    prompt = synth.prompt_ids(SEED, n_prompt, shape["vocab"])
+    wm = rf.load_into_oracle(orc, table)
+    md = orc.Model(rf.oracle_shape(orc, shape), n_prompt + n_gen)
+    assert md.prefill(wm, prompt) == 0
+    pre = md.logits()
+    st, ids, gap, _ = md.greedy_decode(wm, n_gen)
+    assert st == 0
+    g = dict(prefill=pre, ids=np.asarray(ids), gap=np.asarray(gap), final=md.logits())
+    a = _run_ranks(shape, g["ids"], "", "f32", n_prompt, n_gen)
+    _check(a, g, ATOL, RTOL, n_gen)
