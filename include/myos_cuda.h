@@ -187,7 +187,9 @@ int myos_forced_decode(myos_ctx* ctx, const uint32_t* ids, size_t steps, uint32_
 int myos_kv_len(const myos_ctx* ctx, size_t* len);
 int myos_reset(myos_ctx* ctx);
 
-/* KvCache::key_head / value_head (kv_cache.rs:239-252): head_dim f32 each. */
+/* KvCache::key_head / value_head (kv_cache.rs:239-252): head_dim f32 each.
+ * In a tensor-parallel context `head` counts this rank's KV heads
+ * (global head rank * num_kv_heads / size + head). */
 int myos_kv_head(myos_ctx* ctx, uint32_t layer, uint32_t head, size_t pos, float* k, float* v);
 
 /* BlockWorkspace::logits (qwen25_block.rs:118-125): vocab floats. */
