@@ -1784,8 +1784,14 @@ size_t gemv_smem_bytes(int K) { return (size_t)((K + 7) & ~7) * sizeof(float); }
 // two batches in flight, so depth sets its share of DRAM bandwidth), then
 // the smallest size giving that many batches a row (fewest idle slots in a
 // row's last batch).
+static int env_int(const char* name, int def);
 static int pick_batch(int P, int NR) {
-  const int umax = NR > 1 ? 4 : 8;
+  // NR = 2 keeps both matrices' batches in registers: up to 6 chunks fit
+  // without spilling (-Xptxas -v); 6 measured 10.8 us for the 1.5B gate/up
+  // against 11.95 us at 4 (MYOS_GEMV_UMAX2 overrides)
+  int umax = NR > 1 ? env_int("MYOS_GEMV_UMAX2", 6) : 8;
+  if (umax < 3) umax = 3;
+  if (umax > (NR > 1 ? 6 : 8)) umax = NR > 1 ? 6 : 8;
   if (P <= umax) return P < 3 ? 3 : P;
   const int nbr = (P + umax - 1) / umax;
   int u = (P + nbr - 1) / nbr;
