@@ -134,7 +134,7 @@ MYOS_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* err, uint32_t 
 // a wait is bounded in time rather than in polls; once one wait has given
 // up, later waits of the context return at once with the error bit set.
 constexpr uint32_t kErrTpWait = 4u;
-constexpr uint64_t kTpWaitNs = 60000000000ull;  // 60 s
+constexpr uint64_t kTpWaitNs = 60000000000ull;  // 60 s (default bound)
 
 MYOS_DEV void tp_store(float* slot, float v, unsigned epoch) {
   const unsigned long long w = ((unsigned long long)epoch << 32) | __float_as_uint(v);
@@ -148,15 +148,17 @@ MYOS_DEV unsigned long long tp_load(const float* slot) {
 }
 
 // The value of word `slot` once it carries `epoch`; false (and the error bit)
-// when the time bound passes first, or an earlier wait already gave up.
-MYOS_DEV bool tp_wait_word(const float* slot, unsigned epoch, uint32_t* err, float* v) {
+// when `limit_ns` passes first (0: kTpWaitNs), or an earlier wait gave up.
+MYOS_DEV bool tp_wait_word(const float* slot, unsigned epoch, uint32_t* err, float* v,
+                           uint64_t limit_ns = 0) {
+  if (limit_ns == 0) limit_ns = kTpWaitNs;
   unsigned long long w = tp_load(slot);
   if ((unsigned)(w >> 32) != epoch) {
     const uint64_t t0 = global_ns();
     for (uint32_t i = 1;; ++i) {
       if ((i & 63u) == 0) {
         if (*(volatile uint32_t*)err & kErrTpWait) return false;
-        if (global_ns() - t0 > kTpWaitNs) {
+        if (global_ns() - t0 > limit_ns) {
           atomicOr(err, kErrTpWait);
           return false;
         }

@@ -27,6 +27,7 @@
 #include <vector>
 
 #include "../../include/myos_cuda.h"
+#include "common.cuh"
 #include "gemm_sm100.h"
 #include "kernels.h"
 #include "prefill.h"
@@ -1040,6 +1041,62 @@ int myos_tp_unique_id(uint8_t out[128]) {
   if (!out) return MYOS_ERR_ARG;
   std::string why;
   return tp_unique_id(out, &why) ? MYOS_OK : MYOS_ERR_NCCL;
+}
+
+int myos_tp_reduce_selftest(int32_t device, uint32_t n, uint32_t H, int32_t fill,
+                            uint32_t timeout_ms, float* out) {
+  if (n < 1 || n > (uint32_t)kMaxTp || H == 0 || H > (1u << 20) || (fill && !out) ||
+      timeout_ms == 0 || timeout_ms > 10000)
+    return MYOS_ERR_ARG;
+  int ndev = 0;
+  if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev) {
+    cudaGetLastError();
+    return MYOS_ERR_CUDA;
+  }
+  if (cudaSetDevice(device) != cudaSuccess || kernels_init() != cudaSuccess) return MYOS_ERR_CUDA;
+  const size_t words = (size_t)n * H;
+  // inbox words (value bits, epoch) for ranks 0..n-1, then seq, done, err
+  std::vector<uint64_t> host(words, 0);
+  if (fill)
+    for (size_t p = 0; p < n; ++p)
+      for (size_t i = 0; i < H; ++i) {
+        const float v = 0.25f * (float)(p + 1) + (float)i * (1.0f / 1024.0f);
+        uint32_t bits;
+        memcpy(&bits, &v, 4);
+        host[p * H + i] = (1ull << 32) | bits;  // epoch 1: the first exchange
+      }
+  uint8_t* buf = nullptr;
+  float* d_out = nullptr;
+  int rc = MYOS_OK;
+  uint32_t ctl[3] = {0, 0, 0};
+  if (cudaMalloc(&buf, words * 8 + 256) != cudaSuccess || cudaMalloc(&d_out, (size_t)H * 4) != cudaSuccess) {
+    rc = MYOS_ERR_CUDA;
+  } else if (cudaMemcpy(buf, host.data(), words * 8, cudaMemcpyHostToDevice) != cudaSuccess ||
+             cudaMemset(buf + words * 8, 0, 256) != cudaSuccess) {
+    rc = MYOS_ERR_CUDA;
+  } else {
+    TpReduceArgs r = {};
+    r.n = (int)n;
+    r.H = (int)H;
+    r.inbox = (const float*)buf;
+    r.seq = (unsigned*)(buf + words * 8);
+    r.done = r.seq + 1;
+    r.err = (uint32_t*)(r.seq + 2);
+    r.out = d_out;
+    r.wait_ns = (uint64_t)timeout_ms * 1000000ull;
+    if (launch_tp_reduce(r, 0, false) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess ||
+        cudaMemcpy(ctl, r.seq, sizeof ctl, cudaMemcpyDeviceToHost) != cudaSuccess ||
+        (fill && cudaMemcpy(out, d_out, (size_t)H * 4, cudaMemcpyDeviceToHost) != cudaSuccess))
+      rc = MYOS_ERR_CUDA;
+    else if (ctl[2] & kErrTpWait)
+      rc = MYOS_ERR_TIMEOUT;
+    else if (ctl[0] != 1u || ctl[1] != 0u)  // epoch advanced once, block count reset
+      rc = MYOS_ERR_CUDA;
+  }
+  if (buf) cudaFree(buf);
+  if (d_out) cudaFree(d_out);
+  cudaGetLastError();
+  return rc;
 }
 
 int myos_ctx_create_tp(const myos_shape* shape, const myos_opts* opts, const myos_tp* tp,

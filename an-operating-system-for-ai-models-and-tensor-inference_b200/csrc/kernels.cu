@@ -1611,7 +1611,7 @@ __global__ void __launch_bounds__(kReduceThreads) k_tp_reduce(TpReduceArgs r) {
       if (p >= r.n || !ok) continue;
       float t = __uint_as_float((unsigned)w[p]);
       if ((unsigned)(w[p] >> 32) != e)
-        ok = tp_wait_word(r.inbox + 2 * ((size_t)p * r.H + i), e, r.err, &t);
+        ok = tp_wait_word(r.inbox + 2 * ((size_t)p * r.H + i), e, r.err, &t, r.wait_ns);
       s = p == 0 ? t : __fadd_rn(s, t);
     }
     if (ok) r.out[i] = s;

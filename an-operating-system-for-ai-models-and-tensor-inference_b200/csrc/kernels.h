@@ -69,6 +69,7 @@ struct TpReduceArgs {
   unsigned* done;  // blocks finished (reset by the last one)
   float* out;
   uint32_t* err;
+  uint64_t wait_ns;  // bound on each word's wait (0: 60 s)
 };
 cudaError_t launch_tp_reduce(const TpReduceArgs& r, cudaStream_t st, bool pdl);
 

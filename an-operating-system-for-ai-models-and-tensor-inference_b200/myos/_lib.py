@@ -82,6 +82,8 @@ SIGNATURES = {
     "myos_ctx_create_tp": (C.c_int, [C.POINTER(Shape), C.POINTER(Opts), C.POINTER(TP),
                                       C.POINTER(C.c_void_p)]),
     "myos_tp_unique_id": (C.c_int, [_u8p]),
+    "myos_tp_reduce_selftest": (C.c_int, [C.c_int32, C.c_uint32, C.c_uint32, C.c_int32,
+                                          C.c_uint32, _f32p]),
     "myos_ctx_destroy": (None, [C.c_void_p]),
     "myos_last_error": (C.c_char_p, [C.c_void_p]),
     "myos_load_tensor": (C.c_int, [C.c_void_p, C.c_char_p, C.c_int32, _i64p, C.c_int32,

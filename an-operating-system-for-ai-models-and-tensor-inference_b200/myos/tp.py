@@ -27,6 +27,18 @@ from . import synth
 from .engine import Engine, tp_unique_id
 
 
+def reduce_selftest(n: int, H: int, fill: bool, timeout_ms: int = 1000, device: int = 0):
+    """myos_tp_reduce_selftest: (status, sums or None) of the exchange's
+    reduce kernel over a host-filled (or never-written) inbox on one GPU."""
+    from . import _lib
+    import ctypes as C
+    L = _lib.load()
+    out = np.zeros(H, np.float32)
+    st = L.myos_tp_reduce_selftest(int(device), int(n), int(H), 1 if fill else 0,
+                                   int(timeout_ms), out.ctypes.data_as(C.POINTER(C.c_float)))
+    return st, (out if fill else None)
+
+
 def load_synth(e: Engine, shape: dict, seed: int, threads: int = 0) -> None:
     """The seeded weights of ``synth.weights`` one tensor at a time (host
     memory: the largest tensor, not the model)."""

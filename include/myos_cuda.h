@@ -135,6 +135,17 @@ typedef struct myos_tp {
 
 /* A fresh NCCL unique id (the rendezvous token every rank passes in). */
 int myos_tp_unique_id(uint8_t out[128]);
+
+/* Diagnostics of the tensor-parallel exchange on ONE GPU (no peers, no
+ * NCCL): runs the exchange's reduce kernel over an inbox of n ranks x H
+ * words. fill = 1: the host first writes every word as the first exchange's
+ * (value 0.25 * (p + 1) + i / 1024 for rank p, element i) and out receives
+ * the sums over p in rank order (f32 adds). fill = 0: nothing writes the
+ * inbox, so the kernel's bounded wait must give up after timeout_ms
+ * (1..10000) and the call returns MYOS_ERR_TIMEOUT. No reference
+ * counterpart. */
+int myos_tp_reduce_selftest(int32_t device, uint32_t n, uint32_t H, int32_t fill,
+                            uint32_t timeout_ms, float* out);
 int myos_ctx_create_tp(const myos_shape* shape, const myos_opts* opts, const myos_tp* tp,
                        myos_ctx** out);
 const char* myos_last_error(const myos_ctx* ctx);
