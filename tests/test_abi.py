@@ -166,3 +166,31 @@ def test_writer_roundtrip_matches_python_safetensors(tmp_path):
     q = str(tmp_path / "theirs.safetensors")
     st.save_file({"a": np.ones((3, 2), np.float32)}, q)
     assert myos.check_safetensors(q) == 1
+
+
+def test_struct_layouts_match_the_header(tmp_path):
+    """myos_shape / myos_opts / myos_tp as compiled from the header (gcc)
+    against the ctypes mirrors: same size and field offsets."""
+    import ctypes as C
+    import shutil
+    import subprocess
+    if not shutil.which("gcc"):
+        pytest.skip("gcc not available")
+    structs = {"myos_shape": _lib.Shape, "myos_opts": _lib.Opts, "myos_tp": _lib.TP}
+    lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "myos_cuda.h"', "int main(void) {"]
+    for cname, py in structs.items():
+        lines.append('printf("%s %%zu\\n", sizeof(%s));' % (cname, cname))
+        for field, _ in py._fields_:
+            lines.append('printf("%s.%s %%zu\\n", offsetof(%s, %s));' % (cname, field, cname, field))
+    lines += ["return 0;", "}"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-std=c11", "-I", os.path.join(REPO, "include"), str(src), "-o", str(exe)],
+                   check=True)
+    got = dict(l.split() for l in subprocess.run([str(exe)], capture_output=True, text=True,
+                                                 check=True).stdout.splitlines())
+    for cname, py in structs.items():
+        assert int(got[cname]) == C.sizeof(py), cname
+        for field, _ in py._fields_:
+            assert int(got[f"{cname}.{field}"]) == getattr(py, field).offset, (cname, field)
