@@ -147,7 +147,7 @@ struct myos_ctx {
   // down_proj epilogues push their rows into every rank's inbox, a one-block
   // kernel sums them; the head pushes its candidate the same way.
   bool tp_p2p = false;
-  uint8_t* tp_link = nullptr;         // this rank's inboxes and arrival counters
+  uint8_t* tp_link = nullptr;         // this rank's inboxes, epoch and block counters
   void* tp_peer[kMaxTp] = {};         // every rank's tp_link as mapped here
   TpPush push_o = {}, push_d = {}, push_c = {};
   float *inbox_o = nullptr, *inbox_d = nullptr, *inbox_c = nullptr;  // 8-byte words

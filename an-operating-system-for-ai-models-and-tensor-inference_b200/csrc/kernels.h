@@ -105,8 +105,7 @@ struct GemvArgs {
   // allreduce). EPI_ARGMAX with tp_cand: the block-reduced first maximum goes
   // to tp_cand as (value, row0 + row), the step control is left alone.
   // With push.n > 0 the EPI_RESID rows (or the EPI_ARGMAX candidate) go to
-  // every rank's inbox instead, and each block arrives on every rank's
-  // counter when done.
+  // every rank's inbox instead, as (value, epoch) words of epoch *push.seq + 1.
   const float* res;
   int res_zero;
   float* tp_cand;
