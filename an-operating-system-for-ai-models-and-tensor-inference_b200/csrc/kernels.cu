@@ -1348,7 +1348,11 @@ struct ClusterPartials {
   }
 };
 
-template <typename KT, int D>
+// UNR: unroll factor of the score and p.v loops (0: full / 8). The kernel
+// runs once per layer between large GEMVs, so its instructions are fetched
+// cold each launch; smaller unrolls shrink the code it fetches, in the same
+// arithmetic order.
+template <typename KT, int D, int UNR>
 __global__ void __launch_bounds__(kThreads) k_attn_dec(AttnArgs a) {
   extern __shared__ float4 smem4[];
   float* sm = reinterpret_cast<float*>(smem4);
@@ -1446,7 +1450,7 @@ __global__ void __launch_bounds__(kThreads) k_attn_dec(AttnArgs a) {
       if (lane < nk) {
         const float* kr = ks + lane * ds;
         float p0 = 0.f, p1 = 0.f, p2 = 0.f, p3 = 0.f;
-#pragma unroll
+#pragma unroll(UNR == 0 ? D / 4 : UNR)
         for (int e = 0; e < d; e += 4) {
           const float4 q = *reinterpret_cast<const float4*>(qh + e);
           const float4 k = *reinterpret_cast<const float4*>(kr + e);
@@ -1468,7 +1472,7 @@ __global__ void __launch_bounds__(kThreads) k_attn_dec(AttnArgs a) {
         acc[j].z *= cf;
         acc[j].w *= cf;
       }
-#pragma unroll 8
+#pragma unroll(UNR == 0 ? 8 : UNR)
       for (int t = 0; t < nk; ++t) {
         const float pt = __shfl_sync(0xffffffffu, p, t);
 #pragma unroll
@@ -1959,14 +1963,23 @@ cudaError_t launch_attention(const AttnArgs& a, int kv_bf16, cudaStream_t st, bo
       attrs[cfg.numAttrs].val.clusterDim.z = 1;
       ++cfg.numAttrs;
     }
+    // MYOS_ATTN_UNROLL=4: the compact-code variant of the score and p.v loops
+    const bool u4 = env_int("MYOS_ATTN_UNROLL", 0) == 4;
+#define MYOS_ATTN_LAUNCH(KT, D)                                                      \
+  return u4 ? cudaLaunchKernelEx(&cfg, k_attn_dec<KT, D, 4>, a)                     \
+            : cudaLaunchKernelEx(&cfg, k_attn_dec<KT, D, 0>, a)
     switch (a.d) {
-      case 64: return kv_bf16 ? cudaLaunchKernelEx(&cfg, k_attn_dec<__nv_bfloat16, 64>, a)
-                              : cudaLaunchKernelEx(&cfg, k_attn_dec<float, 64>, a);
-      case 128: return kv_bf16 ? cudaLaunchKernelEx(&cfg, k_attn_dec<__nv_bfloat16, 128>, a)
-                               : cudaLaunchKernelEx(&cfg, k_attn_dec<float, 128>, a);
-      case 256: return kv_bf16 ? cudaLaunchKernelEx(&cfg, k_attn_dec<__nv_bfloat16, 256>, a)
-                               : cudaLaunchKernelEx(&cfg, k_attn_dec<float, 256>, a);
+      case 64:
+        if (kv_bf16) MYOS_ATTN_LAUNCH(__nv_bfloat16, 64);
+        MYOS_ATTN_LAUNCH(float, 64);
+      case 128:
+        if (kv_bf16) MYOS_ATTN_LAUNCH(__nv_bfloat16, 128);
+        MYOS_ATTN_LAUNCH(float, 128);
+      case 256:
+        if (kv_bf16) MYOS_ATTN_LAUNCH(__nv_bfloat16, 256);
+        MYOS_ATTN_LAUNCH(float, 256);
     }
+#undef MYOS_ATTN_LAUNCH
     return cudaErrorInvalidValue;
   }
   // The split merge reuses the tile buffers for (2 nsplit + 1) * G floats.
@@ -2055,12 +2068,16 @@ cudaError_t kernels_init() {
   MYOS_SET((k_gemv_bulk<EPI_RESID, 1>), gemv_max)
   MYOS_SET((k_gemv_bulk<EPI_SWIGLU, 2>), gemv_max)
   MYOS_SET((k_gemv_bulk<EPI_ARGMAX, 1>), gemv_max)
-  MYOS_SET((k_attn_dec<float, 64>), attn_max)
-  MYOS_SET((k_attn_dec<__nv_bfloat16, 64>), attn_max)
-  MYOS_SET((k_attn_dec<float, 128>), attn_max)
-  MYOS_SET((k_attn_dec<__nv_bfloat16, 128>), attn_max)
-  MYOS_SET((k_attn_dec<float, 256>), attn_max)
-  MYOS_SET((k_attn_dec<__nv_bfloat16, 256>), attn_max)
+#define MYOS_SET_ATTN(UNR)                                \
+  MYOS_SET((k_attn_dec<float, 64, UNR>), attn_max)          \
+  MYOS_SET((k_attn_dec<__nv_bfloat16, 64, UNR>), attn_max)  \
+  MYOS_SET((k_attn_dec<float, 128, UNR>), attn_max)         \
+  MYOS_SET((k_attn_dec<__nv_bfloat16, 128, UNR>), attn_max) \
+  MYOS_SET((k_attn_dec<float, 256, UNR>), attn_max)         \
+  MYOS_SET((k_attn_dec<__nv_bfloat16, 256, UNR>), attn_max)
+  MYOS_SET_ATTN(0)
+  MYOS_SET_ATTN(4)
+#undef MYOS_SET_ATTN
   MYOS_SET((k_attn<1, float>), attn_max)
   MYOS_SET((k_attn<2, float>), attn_max)
   MYOS_SET((k_attn<4, float>), attn_max)
