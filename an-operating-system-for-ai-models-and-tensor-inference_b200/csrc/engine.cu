@@ -32,7 +32,7 @@
 #include "kernels.h"
 #include "prefill.h"
 #include "safetensors.h"
-#include "step_kernel.h"
+#include "stream_step.h"
 #include "tp.h"
 
 using namespace myos;
@@ -123,12 +123,15 @@ struct myos_ctx {
   float prefill_ms = 0.f, decode_ms = 0.f;
   int steps_per_graph = 16;
   bool profiling = false;
-  // persistent step kernel (one launch per token), when the shape allows
-  bool mega = false;
-  MegaArgs margs = {};
-  MegaLayer* d_layers = nullptr;
-  unsigned* bar = nullptr;  // [5L] phase counters + attention + head counters
-  uint64_t* trace = nullptr;  // MYOS_TRACE_FILE: per-phase timer stamps of the step kernel
+  // persistent streaming step kernel (all decode steps of a call in one
+  // launch), when the shape allows; MYOS_STEP=kernels keeps one launch per kernel
+  bool stream = false;
+  StreamArgs sargs = {};
+  StreamLayer* d_slayers = nullptr;
+  unsigned* sflags = nullptr;  // [grid] arrival flags, then [Hkv] merge counters
+  float* s_work = nullptr;     // split partials (o | m | l) and head candidates
+  uint64_t* trace = nullptr;   // MYOS_TRACE_FILE: per-phase timer stamps of the step kernel
+  uint64_t* strace = nullptr;  // MYOS_SLOT_TRACE: per-slot stamps (diagnostics)
   std::string trace_file;
   uint64_t* ktrace = nullptr;  // MYOS_KTRACE_FILE: launch timeline of the per-kernel step
   std::string ktrace_file;
@@ -458,17 +461,6 @@ int launch_kind(myos_ctx* c, int kind, int l, const uint32_t* feed, bool pdl, bo
 
 int enqueue_step(myos_ctx* c, bool head, const uint32_t* feed, bool first_pdl) {
   const int L = (int)c->s.num_layers;
-  if (c->mega) {
-    MegaArgs a = c->margs;
-    a.head = head ? 1 : 0;
-    a.feed = feed;
-    // phase counters, and the merge / head counters in case an aborted
-    // launch left them non-zero
-    CK(cudaMemsetAsync(c->bar, 0, ((size_t)5 * L + c->s.num_kv_heads + 1) * sizeof(unsigned),
-                       c->st));
-    CK(launch_step_mega(a, c->st));
-    return MYOS_OK;
-  }
   for (int l = 0; l < L; ++l) {
     for (int k = K_QKV; k <= K_DOWN; ++k) {
       int st = launch_kind(c, k, l, feed, (l > 0 || k > K_QKV) || first_pdl, true);
@@ -495,9 +487,23 @@ double kind_bytes(const myos_ctx* c, int kind) {
   return 0;
 }
 
+// Token steps per launch of the streaming step kernel.
+constexpr size_t kStreamMaxSteps = 1024;
+
 int run_steps(myos_ctx* c, int kind, size_t nsteps) {
   const bool head = kind != G_FEED_NOHEAD;
   const uint32_t* feed = kind == G_ARGMAX_HEAD ? nullptr : c->feed;
+  if (c->stream) {  // one cooperative launch runs the steps back to back
+    StreamArgs a = c->sargs;
+    a.head = head ? 1 : 0;
+    a.feed = feed;
+    for (size_t done = 0; done < nsteps;) {
+      a.nsteps = (int)std::min(nsteps - done, kStreamMaxSteps);
+      CK(launch_step_stream(a, c->st));
+      done += (size_t)a.nsteps;
+    }
+    return MYOS_OK;
+  }
   if (!c->o.use_graphs) {
     for (size_t i = 0; i < nsteps; ++i) {
       int st = enqueue_step(c, head, feed, i > 0);
@@ -567,7 +573,7 @@ int finish(myos_ctx* c) {
     }
   }
   if (c->trace) {  // last step's stamps, for offline analysis
-    const size_t nt = (size_t)c->num_sms * (5 * c->s.num_layers + 1) * 4;
+    const size_t nt = (size_t)c->sargs.grid * (5 * c->s.num_layers + 1) * 8;
     std::vector<uint64_t> h(nt);
     if (cudaMemcpy(h.data(), c->trace, nt * 8, cudaMemcpyDeviceToHost) == cudaSuccess) {
       if (FILE* f = fopen(c->trace_file.c_str(), "wb")) {
@@ -575,11 +581,23 @@ int finish(myos_ctx* c) {
         fclose(f);
       }
     }
+    if (c->strace) {
+      std::vector<uint64_t> hs((size_t)c->sargs.grid * 640 * 4);
+      if (cudaMemcpy(hs.data(), c->strace, hs.size() * 8, cudaMemcpyDeviceToHost) == cudaSuccess)
+        if (FILE* f = fopen((c->trace_file + ".slots").c_str(), "wb")) {
+          fwrite(hs.data(), 8, hs.size(), f);
+          fclose(f);
+        }
+    }
   }
   if (c->ctl_host->err) {
     const uint32_t bits = c->ctl_host->err;
     c->ctl_host->err = 0;
     cudaMemcpy(&c->ctl->err, &c->ctl_host->err, 4, cudaMemcpyHostToDevice);
+    // an abandoned streaming launch leaves its arrival flags and merge
+    // counters partway: start the next launch from zero
+    if (c->sflags)
+      cudaMemset(c->sflags, 0, (2 + (size_t)c->sargs.grid + c->s.num_kv_heads) * sizeof(unsigned));
     return fail(c, MYOS_ERR_TIMEOUT,
                 "a bounded device wait gave up (bits " + std::to_string(bits) + ")");
   }
@@ -877,28 +895,13 @@ static int create_impl(myos_ctx* c, const myos_shape* shape, const myos_opts* op
   CK(cudaMalloc(&c->sin_t, sn.size() * 4));
   CK(cudaMemcpy(c->cos_t, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
   CK(cudaMemcpy(c->sin_t, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice));
-  // persistent step kernel
+  // persistent streaming step kernel (MYOS_STEP=stream; the per-kernel step
+  // stays the default until the streaming one outruns it)
   {
-    // opt-in until it outruns the per-kernel step (MYOS_MEGA=1)
-    const char* e = getenv("MYOS_MEGA");
-    const bool want = e && e[0] == '1';
-    if (want && c->tp_size == 1 && mega_supported((int)H, (int)I, (int)c->qd, (int)c->kvd, (int)d, (int)c->G) &&
-        (size_t)s.num_kv_heads * nsplit <= (size_t)c->num_sms) {
-      std::vector<MegaLayer> hl(L);
-      for (size_t l = 0; l < L; ++l) {
-        const LayerW& w = c->layers[l];
-        hl[l] = MegaLayer{w.wqkv, w.wo, w.wg, w.wu, w.wd, w.bqkv, w.ln1, w.ln2};
-      }
-      CK(cudaMalloc(&c->d_layers, L * sizeof(MegaLayer)));
-      CK(cudaMemcpy(c->d_layers, hl.data(), L * sizeof(MegaLayer), cudaMemcpyHostToDevice));
-      const size_t nbar = 5 * L + s.num_kv_heads + 1;
-      CK(cudaMalloc(&c->bar, nbar * sizeof(unsigned)));
-      CK(cudaMemset(c->bar, 0, nbar * sizeof(unsigned)));
-      float* mpv = nullptr;
-      uint32_t* mpi = nullptr;
-      CK(cudaMalloc(&mpv, (size_t)c->num_sms * 4));
-      CK(cudaMalloc(&mpi, (size_t)c->num_sms * 4));
-      MegaArgs& a = c->margs;
+    const char* e = getenv("MYOS_STEP");
+    const bool want = e && e[0] == 's';
+    if (want && c->tp_size == 1) {
+      StreamArgs a = {};
       a.L = (int)L;
       a.H = (int)H;
       a.I = (int)I;
@@ -911,54 +914,84 @@ static int create_impl(myos_ctx* c, const myos_shape* shape, const myos_opts* op
       a.G = (int)c->G;
       a.eps = s.rms_eps;
       a.scale = 1.0f / sqrtf((float)d);
-      a.embed = c->embed;
-      a.head_w = s.tied_head ? c->embed : c->lm_head;
-      a.final_norm = c->final_norm;
-      a.layers = c->d_layers;
-      a.ctl = c->ctl;
-      a.rec_fed = c->rec_fed;
-      a.rec_argmax = c->rec_argmax;
-      a.resid = c->resid;
-      a.qkv = c->qkv;
-      a.attn = c->attn;
-      a.act = c->act;
-      a.logits = c->logits;
-      a.kcache = c->kcache;
-      a.vcache = c->vcache;
-      a.kv_layer_elems = c->kv_layer_elems;
+      a.grid = c->num_sms;
       a.S = (int)S;
       a.kv_bf16 = opts->kv_dtype == MYOS_KV_BF16;
-      a.cos_t = c->cos_t;
-      a.sin_t = c->sin_t;
-      a.nsplit = c->attn_nsplit;
-      a.chunk = c->attn_chunk;
-      a.part_o = c->part_o;
-      a.part_m = c->part_m;
-      a.part_l = c->part_l;
-      a.attn_cnt = c->bar + 5 * L;
-      a.bar = c->bar;
-      a.head_cnt = c->bar + 5 * L + s.num_kv_heads;
-      a.part_val = mpv;
-      a.part_idx = mpi;
-      a.grid = c->num_sms;
-      {
-        const char* la = getenv("MYOS_MEGA_LA");
-        a.lookahead = la ? atoi(la) : 3;
-        const char* kb = getenv("MYOS_MEGA_PF_KB");
-        a.pf_kb = kb ? atoi(kb) : 1024;
-        const char* pm = getenv("MYOS_MEGA_PF_MODE");
-        a.pf_mode = pm ? atoi(pm) : 0;
-      }
+      // split-KV tasks of 64 keys, at most one per CTA; with at most four
+      // splits per KV head the o_proj staging merges them
+      size_t ns = (S + 63) / 64;
+      const size_t cap = (size_t)c->num_sms / s.num_kv_heads;
+      if (ns > cap) ns = cap;
+      if (ns < 1) ns = 1;
+      a.nsplit = (int)ns;
+      a.chunk = (int)((S + ns - 1) / ns);
+      a.merge_in_stage = ns <= 4 ? 1 : 0;
       int max_smem = 0;
       CK(cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, c->device));
-      // leave room for the kernel's static shared memory
-      if (mega_configure(&a, max_smem - 2048) == cudaSuccess) c->mega = true;
-      if (const char* tf = getenv("MYOS_TRACE_FILE")) {
-        c->trace_file = tf;
-        const size_t nt = (size_t)c->num_sms * (5 * L + 1) * 4;
-        CK(cudaMalloc(&c->trace, nt * 8));
-        CK(cudaMemset(c->trace, 0, nt * 8));
-        a.trace = c->trace;
+      if (c->qd_pad == c->qd && stream_configure(&a, max_smem) == cudaSuccess) {
+        std::vector<StreamLayer> hl(L);
+        for (size_t l = 0; l < L; ++l) {
+          const LayerW& w = c->layers[l];
+          hl[l] = StreamLayer{w.wqkv, w.wo, w.wg, w.wu, w.wd, w.bqkv, w.ln1, w.ln2};
+        }
+        CK(cudaMalloc(&c->d_slayers, L * sizeof(StreamLayer)));
+        CK(cudaMemcpy(c->d_slayers, hl.data(), L * sizeof(StreamLayer), cudaMemcpyHostToDevice));
+        // [0..1] the 64-bit arrival counter, then [grid] per-CTA counts and
+        // [Hkv] merge counters
+        const size_t nflags = 2 + (size_t)a.grid + s.num_kv_heads;
+        CK(cudaMalloc(&c->sflags, nflags * sizeof(unsigned)));
+        CK(cudaMemset(c->sflags, 0, nflags * sizeof(unsigned)));
+        const size_t npart = (size_t)s.num_kv_heads * ns * c->G;
+        CK(cudaMalloc(&c->s_work, (npart * (d + 2) + 2 * (size_t)a.grid) * sizeof(float)));
+        a.embed = c->embed;
+        a.head_w = s.tied_head ? c->embed : c->lm_head;
+        a.final_norm = c->final_norm;
+        a.layers = c->d_slayers;
+        a.ctl = c->ctl;
+        a.rec_fed = c->rec_fed;
+        a.rec_argmax = c->rec_argmax;
+        a.resid = c->resid;
+        a.qkv = c->qkv;
+        a.attn = c->attn;
+        a.act = c->act;
+        a.logits = c->logits;
+        a.kcache = c->kcache;
+        a.vcache = c->vcache;
+        a.kv_layer_elems = c->kv_layer_elems;
+        a.cos_t = c->cos_t;
+        a.sin_t = c->sin_t;
+        a.part_o = c->s_work;
+        a.part_m = a.part_o + npart * d;
+        a.part_l = a.part_m + npart;
+        a.cand_val = a.part_l + npart;
+        a.cand_idx = reinterpret_cast<uint32_t*>(a.cand_val + a.grid);
+        a.bar = reinterpret_cast<unsigned long long*>(c->sflags);
+        a.flags = c->sflags + 2;
+        a.attn_cnt = a.flags + a.grid;
+        a.wait_ns = 1000000000ull;
+        // ring copies outstanding at once, and slots requested into L2 ahead
+        const char* fe = getenv("MYOS_STREAM_INFLIGHT");
+        a.inflight = fe ? std::max(1, std::min(atoi(fe), 4)) : 1;
+        const char* le = getenv("MYOS_STREAM_L2LA");
+        a.l2_la = le ? std::max(0, std::min(atoi(le), 64)) : 0;
+        if (const char* sf = getenv("MYOS_SLOT_TRACE")) {  // slot stamps of one launch step
+          uint64_t* st = nullptr;
+          const size_t nt = (size_t)a.grid * 640 * 4;
+          CK(cudaMalloc(&st, nt * 8));
+          CK(cudaMemset(st, 0, nt * 8));
+          a.strace = st;
+          a.strace_seq0 = (uint32_t)atoi(sf);
+          c->strace = st;
+        }
+        if (const char* tf = getenv("MYOS_TRACE_FILE")) {
+          c->trace_file = tf;
+          const size_t nt = (size_t)a.grid * (5 * L + 1) * 8;
+          CK(cudaMalloc(&c->trace, nt * 8));
+          CK(cudaMemset(c->trace, 0, nt * 8));
+          a.trace = c->trace;
+        }
+        c->sargs = a;
+        c->stream = true;
       }
     }
   }
@@ -1135,8 +1168,8 @@ void myos_ctx_destroy(myos_ctx* c) {
   tp_comm_destroy(c->comm);
   void* dev[] = {c->warena, c->kcache, c->vcache, c->resid, c->qkv, c->attn, c->act, c->logits,
                  c->part_val, c->part_idx, c->part_o, c->part_m, c->part_l, c->counters, c->ctl,
-                 c->feed, c->rec_fed, c->rec_argmax, c->cos_t, c->sin_t, c->d_layers, c->bar,
-                 (void*)c->margs.part_val, (void*)c->margs.part_idx, (void*)c->trace,
+                 c->feed, c->rec_fed, c->rec_argmax, c->cos_t, c->sin_t, c->d_slayers, c->sflags,
+                 c->s_work, (void*)c->trace, (void*)c->strace,
                  (void*)c->ktrace, c->pf_X, c->pf_D, c->pf_Q, c->pf_att, c->pf_A, c->pf_ws,
                  c->bt_k, c->bt_v, c->bt_X, c->bt_D, c->bt_pos, c->bt_rows, c->bt_tok,
                  c->bt_out, c->bt_ids, c->tp_part, c->tp_cand, c->tp_link};

@@ -18,6 +18,7 @@
 #include <stdlib.h>
 
 #include <cooperative_groups.h>
+#include <mutex>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -665,152 +666,6 @@ __global__ void __launch_bounds__(kThreads, 2) k_gemv_stream(GemvArgs a) {
   }
 }
 
-// ------------------------------------------------------------------ bulk-copy GEMV
-// A block owns rows [r0, r1): for each weight matrix that is one contiguous
-// byte range, streamed by a producer warp as stages of rs rows with 1-D bulk
-// copies (the TMA engine) into an nst-deep shared-memory ring. The first nst
-// stages are issued before the programmatic-dependency wait, so they load
-// while the previous kernel is still running. Eight consumer warps take one
-// row each (rs = 8), or split a row's K range (spl = 8 / rs warps per row,
-// partials summed in warp order) and release the slot through an mbarrier.
-constexpr int kConsumerWarps = 8;
-constexpr int kBulkThreads = (kConsumerWarps + 1) * 32;
-
-MYOS_DEV size_t align_up(size_t x, size_t a) { return (x + a - 1) & ~(a - 1); }
-
-template <int EPI, int NR>
-__global__ void __launch_bounds__(kBulkThreads, 1) k_gemv_bulk(GemvArgs a) {
-  extern __shared__ float4 smem4[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>(smem4);
-  __shared__ float red[33];
-  __shared__ float wbv[kBulkThreads / 32];
-  __shared__ uint32_t wbi[kBulkThreads / 32];
-  __shared__ int last_block;
-
-  const int K = a.K, rs = a.rs, spl = a.spl, nst = a.nst;
-  const size_t row_bytes = (size_t)K * 2;
-  const size_t slot_bytes = (size_t)NR * rs * row_bytes;
-  float* xs = reinterpret_cast<float*>(smem);
-  uint8_t* ring = smem + align_up((size_t)K * 4, 128);
-  float* part = reinterpret_cast<float*>(ring + (size_t)nst * slot_bytes);  // [2][NR][8]
-  uint64_t* full = reinterpret_cast<uint64_t*>(part + 2 * NR * kConsumerWarps);
-  uint64_t* empty = full + nst;
-
-  const int G = gridDim.x, b = blockIdx.x;
-  const int r0 = (int)((long long)b * a.M / G);
-  const int r1 = (int)((long long)(b + 1) * a.M / G);
-  const int nstage = (r1 - r0 + rs - 1) / rs;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const bool producer = warp == kConsumerWarps;
-  const uint16_t* wbase[NR];
-  wbase[0] = a.w;
-  if (NR > 1) wbase[NR - 1] = a.w2;
-
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < nst; ++i) {
-      mbar_init(&full[i], 1);
-      mbar_init(&empty[i], kConsumerWarps);
-    }
-    mbar_fence_init();
-  }
-  __syncthreads();
-
-  auto prefetch_stage = [&](int s) {
-    if (s >= nstage) return;
-    const int row0 = r0 + s * rs;
-    const int n = min(rs, r1 - row0);
-#pragma unroll
-    for (int r = 0; r < NR; ++r)
-      prefetch_l2(wbase[r] + (size_t)row0 * K, (uint32_t)(n * row_bytes));
-  };
-  auto issue = [&](int s) {
-    const int slot = s % nst;
-    const int row0 = r0 + s * rs;
-    const int n = min(rs, r1 - row0);
-    const uint32_t bytes = (uint32_t)(n * row_bytes);
-    mbar_arrive_expect_tx(&full[slot], NR * bytes);
-#pragma unroll
-    for (int r = 0; r < NR; ++r)
-      bulk_g2s(ring + (size_t)slot * slot_bytes + (size_t)r * rs * row_bytes,
-               wbase[r] + (size_t)row0 * K, bytes, &full[slot]);
-  };
-  const int la = a.lookahead;
-  if (producer && lane == 0) {
-    const int first = min(nst, nstage);
-    for (int s = 0; s < first; ++s) issue(s);
-    for (int s = nst; s < nst + la; ++s) prefetch_stage(s);
-  }
-  pdl_wait();
-  pdl_launch();
-  stage_input(xs, K, true, a.in, red);
-
-  float bv = -INFINITY;
-  uint32_t bi = 0xffffffffu;
-  if (producer) {
-    if (lane == 0) {
-      for (int s = nst; s < nstage; ++s) {
-        const int slot = s % nst;
-        mbar_wait(&empty[slot], (uint32_t)((s / nst) - 1) & 1u, a.err, kErrWaitEmpty);
-        issue(s);
-        if (la) prefetch_stage(s + la);
-      }
-    }
-    __syncwarp();
-  } else {
-    const float4* xlo = reinterpret_cast<const float4*>(xs);
-    const float4* xhi = reinterpret_cast<const float4*>(xs + (K >> 1));
-    const int rr = warp / spl, cs = warp - rr * spl;
-    const int cps = (K >> 3) / spl;
-    const int c0 = cs * cps;
-    for (int s = 0; s < nstage; ++s) {
-      const int slot = s % nst;
-      mbar_wait(&full[slot], (uint32_t)(s / nst) & 1u, a.err, kErrWaitFull);
-      const int row0 = r0 + s * rs;
-      const int n = min(rs, r1 - row0);
-      float acc[NR];
-#pragma unroll
-      for (int r = 0; r < NR; ++r) acc[r] = 0.0f;
-      if (rr < n) {
-        const uint8_t* base = ring + (size_t)slot * slot_bytes + (size_t)rr * row_bytes;
-#pragma unroll 4
-        for (int c = c0 + lane; c < c0 + cps; c += 32) {
-          const float4 lo = xlo[c], hi = xhi[c];
-#pragma unroll
-          for (int r = 0; r < NR; ++r) {
-            const uint4 u = *reinterpret_cast<const uint4*>(base + (size_t)r * rs * row_bytes +
-                                                            (size_t)c * 16);
-            acc[r] = dot8(u, lo, hi, acc[r]);
-          }
-        }
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[slot]);
-#pragma unroll
-      for (int r = 0; r < NR; ++r) acc[r] = warp_sum(acc[r]);
-      if (spl == 1) {
-        if (rr < n) epilogue<EPI>(a, row0 + rr, acc[0], NR > 1 ? acc[NR - 1] : 0.0f, bv, bi, lane);
-      } else {
-        float* pp = part + (s & 1) * NR * kConsumerWarps;
-        if (lane == 0) {
-#pragma unroll
-          for (int r = 0; r < NR; ++r) pp[r * kConsumerWarps + warp] = acc[r];
-        }
-        named_sync(1, kConsumerWarps * 32);
-        if (cs == 0 && rr < n) {
-          float v[NR];
-#pragma unroll
-          for (int r = 0; r < NR; ++r) {
-            v[r] = 0.0f;
-            for (int q = 0; q < spl; ++q) v[r] += pp[r * kConsumerWarps + rr * spl + q];
-          }
-          epilogue<EPI>(a, row0 + rr, v[0], NR > 1 ? v[NR - 1] : 0.0f, bv, bi, lane);
-        }
-      }
-    }
-  }
-  if (EPI == EPI_ARGMAX) argmax_finish(a, bv, bi, wbv, wbi, &last_block);
-}
-
 // ------------------------------------------------------------------ attention
 template <typename KT>
 MYOS_DEV float kv_load(const KT* p);
@@ -1348,11 +1203,7 @@ struct ClusterPartials {
   }
 };
 
-// UNR: unroll factor of the score and p.v loops (0: full / 8). The kernel
-// runs once per layer between large GEMVs, so its instructions are fetched
-// cold each launch; smaller unrolls shrink the code it fetches, in the same
-// arithmetic order.
-template <typename KT, int D, int UNR>
+template <typename KT, int D>
 __global__ void __launch_bounds__(kThreads) k_attn_dec(AttnArgs a) {
   extern __shared__ float4 smem4[];
   float* sm = reinterpret_cast<float*>(smem4);
@@ -1450,7 +1301,7 @@ __global__ void __launch_bounds__(kThreads) k_attn_dec(AttnArgs a) {
       if (lane < nk) {
         const float* kr = ks + lane * ds;
         float p0 = 0.f, p1 = 0.f, p2 = 0.f, p3 = 0.f;
-#pragma unroll(UNR == 0 ? D / 4 : UNR)
+#pragma unroll
         for (int e = 0; e < d; e += 4) {
           const float4 q = *reinterpret_cast<const float4*>(qh + e);
           const float4 k = *reinterpret_cast<const float4*>(kr + e);
@@ -1472,7 +1323,7 @@ __global__ void __launch_bounds__(kThreads) k_attn_dec(AttnArgs a) {
         acc[j].z *= cf;
         acc[j].w *= cf;
       }
-#pragma unroll(UNR == 0 ? 8 : UNR)
+#pragma unroll 8
       for (int t = 0; t < nk; ++t) {
         const float pt = __shfl_sync(0xffffffffu, p, t);
 #pragma unroll
@@ -1739,17 +1590,13 @@ __global__ void k_rope(float* y, const float* x, int len, int d, const float* cs
 }
 
 // ------------------------------------------------------------------ launchers
-// MYOS_GEMV_KIND selects the GEMV implementation for A/B timing:
-// "stream" (default: register double buffer, the fastest measured),
-// "bulk" (bulk-copy ring, limited by the per-SM copy-engine rate),
-// "legacy" (row at a time).
+// MYOS_GEMV_KIND=legacy selects the row-at-a-time GEMV (every width) instead
+// of the streaming one for A/B timing.
 static int gemv_kind() {
   static int v = -1;
   if (v < 0) {
     const char* e = getenv("MYOS_GEMV_KIND");
-    v = 1;
-    if (e && e[0] == 'b') v = 0;
-    if (e && e[0] == 'l') v = 2;
+    v = (e && e[0] == 'l') ? 2 : 1;
   }
   return v;
 }
@@ -1814,42 +1661,12 @@ static cudaError_t launch_stream(const GemvArgs& a, int U, cudaLaunchConfig_t& c
   }
 }
 
-// Tuning knobs (read at launch; a captured graph keeps the values it saw):
-// MYOS_BULK_STAGE_KB target stage size, MYOS_BULK_RING_KB ring size,
-// MYOS_BULK_LOOKAHEAD stages prefetched into L2 ahead of the ring,
-// MYOS_BULK_GRID_MULT blocks per SM.
 static int env_int(const char* name, int def) {
   const char* e = getenv(name);
   return e && *e ? atoi(e) : def;
 }
 
-// Bulk-pipeline geometry: rows per stage so a stage is about STAGE_KB, as
-// many stages as fit in RING_KB (2..16).
-static void bulk_geometry(int K, int NR, int* rs, int* spl, int* nst, size_t* smem) {
-  const size_t row_bytes = (size_t)K * 2;
-  const size_t stage_target = (size_t)env_int("MYOS_BULK_STAGE_KB", 24) << 10;
-  int r = 8;
-  while (r > 1 && (size_t)NR * r * row_bytes > stage_target) r >>= 1;
-  const size_t slot = (size_t)NR * r * row_bytes;
-  int n = (int)(((size_t)env_int("MYOS_BULK_RING_KB", 96) << 10) / slot);
-  if (n < 2) n = 2;
-  if (n > 16) n = 16;
-  *rs = r;
-  *spl = kConsumerWarps / r;
-  *nst = n;
-  *smem = ((size_t)K * 4 + 127) / 128 * 128 + (size_t)n * slot + 2 * NR * kConsumerWarps * 4 +
-          2 * (size_t)n * 8 + 16;
-}
-
 int gemv_grid(int M, int K, int NR, int num_sms) {
-  if (K % 256 == 0 && gemv_kind() == 0) {
-    int rs, spl, nst;
-    size_t smem;
-    bulk_geometry(K, NR, &rs, &spl, &nst, &smem);
-    const int g = (M + rs - 1) / rs;
-    const int cap = num_sms * env_int("MYOS_BULK_GRID_MULT", 1);
-    return g < cap ? (g < 1 ? 1 : g) : cap;
-  }
   // Up to two blocks per SM, at least MYOS_GEMV_MIN_ROWS (8) rows a block.
   // MYOS_GEMV_BALANCE=1: past one block per SM, exactly two per SM with the
   // rows spread over fewer warps (gemv_warps). Measured slower for the 1.5B
@@ -1882,25 +1699,6 @@ cudaError_t launch_gemv(int epi, const GemvArgs& a0, int grid, cudaStream_t st, 
       ((a0.K % 256) != 0 || ((uintptr_t)a0.w & 15) != 0 || getenv_legacy() || a0.in.part_o ||
        a0.push.n > kMaxTp))
     return cudaErrorNotSupported;
-  const bool bulk_ok = (a0.K % 256) == 0 && ((uintptr_t)a0.w & 15) == 0 &&
-                       (epi != EPI_SWIGLU || ((uintptr_t)a0.w2 & 15) == 0) && gemv_kind() == 0 &&
-                       !a0.in.part_o && !a0.push.n;
-  if (bulk_ok) {
-    GemvArgs a = a0;
-    const int NR = epi == EPI_SWIGLU ? 2 : 1;
-    size_t smem;
-    bulk_geometry(a.K, NR, &a.rs, &a.spl, &a.nst, &smem);
-    a.lookahead = env_int("MYOS_BULK_LOOKAHEAD", 0);
-    cudaLaunchConfig_t cfg = make_cfg(dim3(grid), dim3(kBulkThreads), smem, st, pdl, attr);
-    switch (epi) {
-      case EPI_STORE: return cudaLaunchKernelEx(&cfg, k_gemv_bulk<EPI_STORE, 1>, a);
-      case EPI_BIAS: return cudaLaunchKernelEx(&cfg, k_gemv_bulk<EPI_BIAS, 1>, a);
-      case EPI_RESID: return cudaLaunchKernelEx(&cfg, k_gemv_bulk<EPI_RESID, 1>, a);
-      case EPI_SWIGLU: return cudaLaunchKernelEx(&cfg, k_gemv_bulk<EPI_SWIGLU, 2>, a);
-      case EPI_ARGMAX: return cudaLaunchKernelEx(&cfg, k_gemv_bulk<EPI_ARGMAX, 1>, a);
-    }
-    return cudaErrorInvalidValue;
-  }
   const GemvArgs& a = a0;
   size_t smem = gemv_smem_bytes(a.K);
   if (a.in.part_o) smem += merge_smem_bytes(a.K / a.in.m_d, a.in.m_nsplit, a.in.m_d);
@@ -1963,11 +1761,7 @@ cudaError_t launch_attention(const AttnArgs& a, int kv_bf16, cudaStream_t st, bo
       attrs[cfg.numAttrs].val.clusterDim.z = 1;
       ++cfg.numAttrs;
     }
-    // MYOS_ATTN_UNROLL=4: the compact-code variant of the score and p.v loops
-    const bool u4 = env_int("MYOS_ATTN_UNROLL", 0) == 4;
-#define MYOS_ATTN_LAUNCH(KT, D)                                                      \
-  return u4 ? cudaLaunchKernelEx(&cfg, k_attn_dec<KT, D, 4>, a)                     \
-            : cudaLaunchKernelEx(&cfg, k_attn_dec<KT, D, 0>, a)
+#define MYOS_ATTN_LAUNCH(KT, D) return cudaLaunchKernelEx(&cfg, k_attn_dec<KT, D>, a)
     switch (a.d) {
       case 64:
         if (kv_bf16) MYOS_ATTN_LAUNCH(__nv_bfloat16, 64);
@@ -2030,14 +1824,27 @@ cudaError_t launch_rmsnorm(float* y, const float* x, const float* gamma, int n, 
   return cudaGetLastError();
 }
 
+static std::mutex g_init_mu;
+static unsigned long long g_init_mask = 0;  // devices whose limits are raised (under g_init_mu)
+
+static cudaError_t raise_limits();
+
 cudaError_t kernels_init() {
-  // Dynamic shared-memory limits are per device: raise them once for each.
-  static unsigned long long done_mask = 0;
+  // Dynamic shared-memory limits are per device: raise them once for each,
+  // and count a device done only after every attribute call succeeded. The
+  // lock keeps a second host thread from launching a large-smem kernel
+  // before the first has raised the limit.
   int dev = 0;
   cudaError_t status = cudaGetDevice(&dev);
   if (status != cudaSuccess) return status;
-  if (dev < 64 && (done_mask >> dev) & 1ull) return cudaSuccess;
-  if (dev < 64) done_mask |= 1ull << dev;
+  std::lock_guard<std::mutex> lock(g_init_mu);
+  if (dev < 64 && (g_init_mask >> dev) & 1ull) return cudaSuccess;
+  status = raise_limits();
+  if (status == cudaSuccess && dev < 64) g_init_mask |= 1ull << dev;
+  return status;
+}
+
+static cudaError_t raise_limits() {
   const int gemv_max = 200 * 1024;  // staged K up to 51200 floats
   const int attn_max = 200 * 1024;
   cudaError_t e;
@@ -2063,21 +1870,12 @@ cudaError_t kernels_init() {
   MYOS_SET_STREAM(EPI_SWIGLU, 2)
   MYOS_SET_STREAM(EPI_ARGMAX, 1)
 #undef MYOS_SET_STREAM
-  MYOS_SET((k_gemv_bulk<EPI_STORE, 1>), gemv_max)
-  MYOS_SET((k_gemv_bulk<EPI_BIAS, 1>), gemv_max)
-  MYOS_SET((k_gemv_bulk<EPI_RESID, 1>), gemv_max)
-  MYOS_SET((k_gemv_bulk<EPI_SWIGLU, 2>), gemv_max)
-  MYOS_SET((k_gemv_bulk<EPI_ARGMAX, 1>), gemv_max)
-#define MYOS_SET_ATTN(UNR)                                \
-  MYOS_SET((k_attn_dec<float, 64, UNR>), attn_max)          \
-  MYOS_SET((k_attn_dec<__nv_bfloat16, 64, UNR>), attn_max)  \
-  MYOS_SET((k_attn_dec<float, 128, UNR>), attn_max)         \
-  MYOS_SET((k_attn_dec<__nv_bfloat16, 128, UNR>), attn_max) \
-  MYOS_SET((k_attn_dec<float, 256, UNR>), attn_max)         \
-  MYOS_SET((k_attn_dec<__nv_bfloat16, 256, UNR>), attn_max)
-  MYOS_SET_ATTN(0)
-  MYOS_SET_ATTN(4)
-#undef MYOS_SET_ATTN
+  MYOS_SET((k_attn_dec<float, 64>), attn_max)
+  MYOS_SET((k_attn_dec<__nv_bfloat16, 64>), attn_max)
+  MYOS_SET((k_attn_dec<float, 128>), attn_max)
+  MYOS_SET((k_attn_dec<__nv_bfloat16, 128>), attn_max)
+  MYOS_SET((k_attn_dec<float, 256>), attn_max)
+  MYOS_SET((k_attn_dec<__nv_bfloat16, 256>), attn_max)
   MYOS_SET((k_attn<1, float>), attn_max)
   MYOS_SET((k_attn<2, float>), attn_max)
   MYOS_SET((k_attn<4, float>), attn_max)

@@ -87,11 +87,6 @@ struct GemvArgs {
   unsigned* counter;
   uint32_t* rec_fed;
   uint32_t* rec_argmax;
-  // bulk-copy pipeline geometry (filled by launch_gemv)
-  int rs;              // rows per stage
-  int spl;             // consumer warps per row (K split)
-  int nst;             // stages in the shared-memory ring
-  int lookahead;       // stages prefetched into L2 beyond the ring
   uint32_t* err;       // bounded-wait failure bits (nullable)
   KTrace tr;
   // Weights of later kernels to pull into L2 while this one waits on its
@@ -164,9 +159,7 @@ cudaError_t launch_rmsnorm(float* y, const float* x, const float* gamma, int n, 
 cudaError_t kernels_init();  // raises dynamic shared-memory limits once per device
 
 size_t gemv_smem_bytes(int K);
-// Grid for an M x K GEMV (NR = 2 for gate|up) with the implementation
-// launch_gemv will pick: the bulk-copy kernel runs one block per SM (fewer
-// when there are fewer stages than SMs).
+// Grid for an M x K GEMV (NR = 2 for gate|up): up to two blocks per SM.
 int gemv_grid(int M, int K, int NR, int num_sms);
 // Warps per block of the streaming kernel for that grid: rows spread evenly
 // over the warps, and at least enough threads to stage the input in one trip.

@@ -64,6 +64,15 @@ extern "C" int myos_dev_gqa_attn_f32_noalloc(float* d_y, const float* d_q, const
                                              size_t seq, int32_t mask_kind, size_t query_pos,
                                              void* stream) {
   if (!d_y || !d_q || !d_k || !d_v) return MYOS_ERR_ARG;
+  // GqaMask has two variants: Full (0) and Causal (1).
+  if (mask_kind != 0 && mask_kind != 1) return MYOS_ERR_ARG;
+  // Every buffer holds f32 (4-byte aligned); with d % 4 == 0 the kernel reads
+  // K and V rows as 16-byte vectors, so those two start on 16 bytes. A
+  // misaligned pointer is refused here, before any device work, instead of
+  // faulting the caller's context.
+  const uintptr_t any = (uintptr_t)d_y | (uintptr_t)d_q | (uintptr_t)d_k | (uintptr_t)d_v;
+  if ((any & 3) != 0) return MYOS_ERR_ARG;
+  if (d % 4 == 0 && (((uintptr_t)d_k | (uintptr_t)d_v) & 15) != 0) return MYOS_ERR_ARG;
   // Shape rules of tensor_core::gqa_attn_f32 (gqa.rs:174-218), as the
   // host-slice entry point applies them.
   if (hq == 0 || hkv == 0 || d == 0 || seq == 0 || hq % hkv != 0) return MYOS_ERR_SHAPE;

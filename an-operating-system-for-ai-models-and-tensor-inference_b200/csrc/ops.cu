@@ -119,6 +119,7 @@ int myos_rmsnorm_bf16_weight(float* y, size_t y_len, const uint8_t* w, size_t w_
 int myos_gqa_attn_f32(float* y, size_t y_len, const float* q, size_t q_len, const float* k,
                       size_t k_len, const float* v, size_t v_len, size_t hq, size_t hkv,
                       size_t d, size_t seq, int32_t mask_kind, size_t query_pos) {
+  if (mask_kind != 0 && mask_kind != 1) return MYOS_ERR_ARG;  // GqaMask: Full or Causal
   if (hq == 0 || hkv == 0 || d == 0 || seq == 0 || hq % hkv != 0) return MYOS_ERR_SHAPE;
   size_t qe, kve;
   if (!mul_ok(hq, d, &qe) || !mul_ok(hkv, seq, &kve) || !mul_ok(kve, d, &kve)) return MYOS_ERR_SHAPE;

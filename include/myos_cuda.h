@@ -233,7 +233,8 @@ int myos_gemv_bf16(float* y, size_t y_len, const uint8_t* w, size_t w_len, const
 /* tensor_core::rmsnorm_bf16_weight (bf16.rs:231-249). */
 int myos_rmsnorm_bf16_weight(float* y, size_t y_len, const uint8_t* w, size_t w_len,
                              const float* x, size_t x_len, float eps);
-/* tensor_core::gqa_attn_f32 (gqa.rs:174-218). mask_kind 0 = Full, 1 = Causal. */
+/* tensor_core::gqa_attn_f32 (gqa.rs:174-218). mask_kind 0 = Full, 1 = Causal (any
+ * other value: MYOS_ERR_ARG). */
 int myos_gqa_attn_f32(float* y, size_t y_len, const float* q, size_t q_len, const float* k,
                       size_t k_len, const float* v, size_t v_len, size_t num_q_heads,
                       size_t num_kv_heads, size_t head_dim, size_t seq_len, int32_t mask_kind,
@@ -291,8 +292,11 @@ int myos_batch_generate(myos_ctx* ctx, size_t nseq, const uint32_t* ids, const u
  * them on its stream first. The first call on a device resolves the array's
  * address (cudaGetSymbolAddress); make that call before any stream capture.
  * Calls share the array: calls that run concurrently (different streams or
- * unordered threads) race and corrupt each other's results. stream may be 0;
- * asynchronous (no sync). */
+ * unordered threads) race and corrupt each other's results. Every pointer
+ * must be 4-byte aligned, and with d % 4 == 0 d_k and d_v 16-byte aligned
+ * (their rows are read as 16-byte vectors); mask_kind is 0 (Full) or 1
+ * (Causal). Other values return MYOS_ERR_ARG before any device work.
+ * stream may be 0; asynchronous (no sync). */
 int myos_dev_gqa_attn_f32_noalloc(float* d_y, const float* d_q, const float* d_k,
                                   const float* d_v, size_t hq, size_t hkv, size_t d, size_t seq,
                                   int32_t mask_kind, size_t query_pos, void* stream);

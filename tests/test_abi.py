@@ -194,3 +194,38 @@ def test_struct_layouts_match_the_header(tmp_path):
         assert int(got[cname]) == C.sizeof(py), cname
         for field, _ in py._fields_:
             assert int(got[f"{cname}.{field}"]) == getattr(py, field).offset, (cname, field)
+
+
+def test_attention_argument_checks_need_no_gpu():
+    """Both attention entry points refuse a mask kind other than Full (0) or
+    Causal (1), and the no-allocation one refuses device pointers that are
+    not 4-byte aligned, or K/V rows that are not 16-byte aligned when d % 4
+    == 0, before any device work. The pointer values are never dereferenced:
+    the checks return first, so no device is needed."""
+    import ctypes as C
+    L = _lib.load()
+    hq, hkv, d, seq = 12, 2, 128, 16
+    f = C.POINTER(C.c_float)
+    y = np.zeros(hq * d, np.float32)
+    q = np.zeros(hq * d, np.float32)
+    k = np.zeros(hkv * seq * d, np.float32)
+    for mask in (2, -1):
+        st = L.myos_gqa_attn_f32(y.ctypes.data_as(f), y.size, q.ctypes.data_as(f), q.size,
+                                 k.ctypes.data_as(f), k.size, k.ctypes.data_as(f), k.size,
+                                 hq, hkv, d, seq, mask, 0)
+        assert st == _lib.ERR_ARG, _lib.status_name(st)
+    base = 1 << 40  # 256-byte aligned stand-in addresses
+    ok = dict(d_y=base, d_q=base + 4096, d_k=base + 8192, d_v=base + (1 << 20))
+
+    def noalloc(mask=0, dd=d, **over):
+        p = dict(ok, **over)
+        return L.myos_dev_gqa_attn_f32_noalloc(p["d_y"], p["d_q"], p["d_k"], p["d_v"], hq, hkv,
+                                               dd, seq, mask, 0, None)
+
+    assert noalloc(mask=2) == _lib.ERR_ARG
+    assert noalloc(d_k=ok["d_k"] + 4) == _lib.ERR_ARG   # K rows not on 16 bytes
+    assert noalloc(d_v=ok["d_v"] + 8) == _lib.ERR_ARG   # V rows not on 16 bytes
+    assert noalloc(d_y=ok["d_y"] + 2) == _lib.ERR_ARG   # not even f32-aligned
+    assert noalloc(d_q=ok["d_q"] + 1) == _lib.ERR_ARG
+    # shape errors are reported before any device work as well
+    assert noalloc(dd=0) == _lib.ERR_SHAPE

@@ -86,10 +86,17 @@ def test_noalloc_rejects_beyond_scratch():
     import torch
 
     L = _lib.load()
-    dy = torch.full((64 * 256,), float("nan"), device="cuda")
+    hq, hkv, d, seq = 64, 8, 256, 4096
+    # Buffers of the full declared size, so that the call reads only memory it
+    # owns even if the scratch size or the split rule ever changed and the
+    # request were accepted.
+    dq = torch.zeros(hq * d, device="cuda")
+    dk = torch.zeros(hkv * seq * d, device="cuda")
+    dv = torch.zeros(hkv * seq * d, device="cuda")
+    dy = torch.full((hq * d,), float("nan"), device="cuda")
     # 8 KV heads x 64 splits x 8 query heads x 256 lanes of f32 partials = 4 MiB
-    st = L.myos_dev_gqa_attn_f32_noalloc(dy.data_ptr(), dy.data_ptr(), dy.data_ptr(),
-                                         dy.data_ptr(), 64, 8, 256, 4096, 0, 0, None)
+    st = L.myos_dev_gqa_attn_f32_noalloc(dy.data_ptr(), dq.data_ptr(), dk.data_ptr(),
+                                         dv.data_ptr(), hq, hkv, d, seq, 0, 0, None)
     assert st == _lib.ERR_SCRATCH_LIMIT, _lib.status_name(st)
     torch.cuda.synchronize()
     assert torch.isnan(dy).all(), "a rejected call wrote its output"
