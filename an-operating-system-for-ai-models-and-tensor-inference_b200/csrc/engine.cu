@@ -112,7 +112,8 @@ struct myos_ctx {
   float *bt_X = nullptr, *bt_D = nullptr;
   size_t bt_D_bytes = 0;
   int *bt_pos = nullptr, *bt_rows = nullptr;
-  uint32_t *bt_tok = nullptr, *bt_out = nullptr, *bt_ids = nullptr;
+  uint32_t *bt_tok = nullptr, *bt_out = nullptr, *bt_ids = nullptr, *bt_feed = nullptr;
+  size_t bt_feed_bytes = 0;
   size_t bt_out_n = 0, bt_ids_n = 0;
   size_t prefetch_total = 0;  // bulk L2 prefetch (MYOS_PREFETCH_MB); measured slower, off
   // loaded-tensor bookkeeping
@@ -1172,7 +1173,7 @@ void myos_ctx_destroy(myos_ctx* c) {
                  c->s_work, (void*)c->trace, (void*)c->strace,
                  (void*)c->ktrace, c->pf_X, c->pf_D, c->pf_Q, c->pf_att, c->pf_A, c->pf_ws,
                  c->bt_k, c->bt_v, c->bt_X, c->bt_D, c->bt_pos, c->bt_rows, c->bt_tok,
-                 c->bt_out, c->bt_ids, c->tp_part, c->tp_cand, c->tp_link};
+                 c->bt_out, c->bt_ids, c->bt_feed, c->tp_part, c->tp_cand, c->tp_link};
   for (void* p : dev)
     if (p) cudaFree(p);
   for (int i = 0; i < 2; ++i) {
@@ -1577,8 +1578,13 @@ int prefill_chunk(myos_ctx* c, const uint32_t* d_ids, int n, int p0, void* kcach
   return MYOS_OK;
 }
 
-int myos_batch_generate(myos_ctx* c, size_t nseq, const uint32_t* ids, const uint32_t* lens,
-                        size_t steps, uint32_t* out_ids) {
+// Batched decode of independent sequences: greedy (feed null: each step's
+// token is the argmax of the sequence's current logits) or teacher-forced
+// (feed [nseq][steps]: step s embeds feed[b][s]); out_ids[b][s] is the
+// argmax of sequence b's logits before step s either way. logits, when
+// non-null, receives each sequence's final logits [nseq][vocab].
+static int batch_run(myos_ctx* c, size_t nseq, const uint32_t* ids, const uint32_t* lens,
+                     size_t steps, const uint32_t* feed, uint32_t* out_ids, float* logits) {
   if (!c || !ids || !lens || (steps && !out_ids)) return MYOS_ERR_ARG;
   if (c->tp_size > 1) return fail(c, MYOS_ERR_UNSUPPORTED, "batched decode is single-GPU only");
   if (!c->pf_ok) return fail(c, MYOS_ERR_SHAPE, "batched decode needs the tensor-core path's shape");
@@ -1593,6 +1599,9 @@ int myos_batch_generate(myos_ctx* c, size_t nseq, const uint32_t* ids, const uin
   }
   for (size_t i = 0; i < total; ++i)
     if (ids[i] >= s.vocab) return fail(c, MYOS_ERR_TOKEN, "token id is out of range");
+  if (feed)
+    for (size_t i = 0; i < nseq * steps; ++i)
+      if (feed[i] >= s.vocab) return fail(c, MYOS_ERR_TOKEN, "token id is out of range");
   if (maxlen + steps > c->o.max_seq) return fail(c, MYOS_ERR_CACHE_FULL, "kv cache is full");
   int st = missing_weight(c);
   if (st) return st;
@@ -1628,9 +1637,20 @@ int myos_batch_generate(myos_ctx* c, size_t nseq, const uint32_t* ids, const uin
   c->bt_ids_n = have_ids / 4;
   const size_t ws = gemm_workspace_bytes(M, V, H);
   if (ws > c->pf_ws_bytes && (st = grow(c, &c->pf_ws, &c->pf_ws_bytes, ws))) return st;
+  // teacher-forced tokens, transposed to [steps][nseq] so each step's column
+  // is one contiguous copy
+  std::vector<uint32_t> feed_t;
+  if (feed && steps) {
+    if ((st = grow(c, &c->bt_feed, &c->bt_feed_bytes, nseq * steps * 4))) return st;
+    feed_t.resize(nseq * steps);
+    for (size_t b = 0; b < nseq; ++b)
+      for (size_t t = 0; t < steps; ++t) feed_t[t * nseq + b] = feed[b * steps + t];
+  }
 
   CK(cudaStreamWaitEvent(stq, c->load_ev, 0));
   CK(cudaMemcpyAsync(c->bt_ids, ids, total * 4, cudaMemcpyHostToDevice, stq));
+  if (!feed_t.empty())
+    CK(cudaMemcpyAsync(c->bt_feed, feed_t.data(), feed_t.size() * 4, cudaMemcpyHostToDevice, stq));
   std::vector<int> pos(B);
   CK(cudaEventRecord(c->ev0, stq));
   // 1. each prompt through the GEMM prefill into its own slab; its last
@@ -1668,6 +1688,9 @@ int myos_batch_generate(myos_ctx* c, size_t nseq, const uint32_t* ids, const uin
   //    logits; each is then forwarded (model_core greedy_decode, per sequence)
   if ((st = head(0))) return st;
   for (size_t step = 0; step < steps; ++step) {
+    if (feed)  // teacher-forced: this step embeds the given token, not the argmax
+      CK(cudaMemcpyAsync(c->bt_tok, c->bt_feed + step * B, (size_t)B * 4, cudaMemcpyDeviceToDevice,
+                         stq));
     CK(pf_embed(c->bt_X, c->embed, c->bt_tok, B, H, stq));
     for (int l = 0; l < L; ++l) {
       const LayerW& w = c->layers[l];
@@ -1695,9 +1718,29 @@ int myos_batch_generate(myos_ctx* c, size_t nseq, const uint32_t* ids, const uin
   CK(cudaEventRecord(c->ev1, stq));
   if (steps)
     CK(cudaMemcpyAsync(out_ids, c->bt_out, (size_t)B * steps * 4, cudaMemcpyDeviceToHost, stq));
+  std::vector<float> halves;
+  if (logits) {  // final logits: the hi and lo rows of the head GEMM summed
+    halves.resize((size_t)M * V);
+    CK(cudaMemcpyAsync(halves.data(), c->bt_D, halves.size() * 4, cudaMemcpyDeviceToHost, stq));
+  }
   if ((st = finish(c))) return st;
+  for (size_t b = 0; logits && b < (size_t)B; ++b)
+    for (size_t v = 0; v < (size_t)V; ++v)
+      logits[b * V + v] = halves[b * V + v] + halves[(B + b) * (size_t)V + v];
   cudaEventElapsedTime(&c->decode_ms, c->ev0, c->ev1);
   return MYOS_OK;
+}
+
+int myos_batch_generate(myos_ctx* c, size_t nseq, const uint32_t* ids, const uint32_t* lens,
+                        size_t steps, uint32_t* out_ids) {
+  return batch_run(c, nseq, ids, lens, steps, nullptr, out_ids, nullptr);
+}
+
+int myos_batch_forced_decode(myos_ctx* c, size_t nseq, const uint32_t* ids, const uint32_t* lens,
+                             size_t steps, const uint32_t* feed, uint32_t* argmax_out,
+                             float* logits) {
+  if (steps && !feed) return MYOS_ERR_ARG;
+  return batch_run(c, nseq, ids, lens, steps, feed, argmax_out, logits);
 }
 
 int myos_prefill(myos_ctx* c, const uint32_t* ids, size_t n, float* logits) {

@@ -110,6 +110,7 @@ SIGNATURES = {
     "myos_greedy_token": (C.c_int, [_f32p, sz, _u32p]),
     "myos_dev_gemv_bf16": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, sz, sz, C.c_void_p]),
     "myos_batch_generate": (C.c_int, [C.c_void_p, sz, _u32p, _u32p, sz, _u32p]),
+    "myos_batch_forced_decode": (C.c_int, [C.c_void_p, sz, _u32p, _u32p, sz, _u32p, _u32p, _f32p]),
     "myos_dev_gqa_attn_f32_noalloc": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                                 sz, sz, sz, sz, C.c_int32, sz, C.c_void_p]),
 }

@@ -143,6 +143,24 @@ class Engine:
                                                out.ctypes.data_as(_lib._u32p)))
         return out[:len(prompts) * steps].reshape(len(prompts), steps)
 
+    def batch_forced(self, prompts, feed, want_logits: bool = False):
+        """Teacher-forced batched decode (myos_batch_forced_decode): feed is
+        [len(prompts), steps]; returns (argmax [len(prompts), steps], final
+        logits [len(prompts), vocab] or None)."""
+        lens = np.array([len(p) for p in prompts], np.uint32)
+        ids = np.ascontiguousarray(np.concatenate([np.asarray(p, np.uint32) for p in prompts]),
+                                   np.uint32)
+        feed = np.ascontiguousarray(feed, np.uint32).reshape(len(prompts), -1)
+        steps = feed.shape[1]
+        am = np.zeros(max(feed.size, 1), np.uint32)
+        lg = np.zeros(len(prompts) * self.shape["vocab"], np.float32) if want_logits else None
+        self._check(self.L.myos_batch_forced_decode(
+            self.h, len(prompts), ids.ctypes.data_as(_lib._u32p), lens.ctypes.data_as(_lib._u32p),
+            steps, feed.ctypes.data_as(_lib._u32p), am.ctypes.data_as(_lib._u32p),
+            lg.ctypes.data_as(_lib._f32p) if lg is not None else None))
+        am = am[:feed.size].reshape(len(prompts), steps)
+        return am, (lg.reshape(len(prompts), -1) if lg is not None else None)
+
     def forced_decode(self, ids) -> np.ndarray:
         ids = np.ascontiguousarray(ids, np.uint32)
         am = np.zeros(max(ids.size, 1), np.uint32)

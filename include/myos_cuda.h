@@ -272,6 +272,17 @@ int myos_dev_gemv_bf16(float* d_y, const void* d_w, const float* d_x, size_t m, 
 int myos_batch_generate(myos_ctx* ctx, size_t nseq, const uint32_t* ids, const uint32_t* lens,
                         size_t steps, uint32_t* out_ids);
 
+/* The teacher-forced form of myos_batch_generate (the per-sequence
+ * myos_forced_decode, model_core forward_token fed given ids, for a batch):
+ * step s of sequence b embeds feed[b*steps + s] instead of the argmax, and
+ * argmax_out[b*steps + s] receives the argmax of b's logits before step s
+ * (the prediction the fed token is scored against). logits, when non-null,
+ * receives every sequence's final logits [nseq][vocab]. Same rules and
+ * errors as myos_batch_generate; feed ids must be < vocab. */
+int myos_batch_forced_decode(myos_ctx* ctx, size_t nseq, const uint32_t* ids, const uint32_t* lens,
+                             size_t steps, const uint32_t* feed, uint32_t* argmax_out,
+                             float* logits);
+
 /* Size of the fixed device array that myos_dev_gqa_attn_f32_noalloc takes its
  * scratch from (one per device). */
 #define MYOS_NOALLOC_SCRATCH_BYTES (2u << 20)
