@@ -129,8 +129,10 @@ struct myos_ctx {
   bool stream = false;
   StreamArgs sargs = {};
   StreamLayer* d_slayers = nullptr;
-  unsigned* sflags = nullptr;  // [grid] arrival flags, then [Hkv] merge counters
-  float* s_work = nullptr;     // split partials (o | m | l) and head candidates
+  unsigned* sflags = nullptr;  // [grid] per-CTA phase counts (epoch base)
+  uint64_t* s_words = nullptr; // phase hand-over words (value, epoch)
+  size_t s_words_bytes = 0;
+  uint64_t s_phases = 0;       // phases run since the words were last zeroed
   uint64_t* trace = nullptr;   // MYOS_TRACE_FILE: per-phase timer stamps of the step kernel
   uint64_t* strace = nullptr;  // MYOS_SLOT_TRACE: per-slot stamps (diagnostics)
   std::string trace_file;
@@ -498,9 +500,17 @@ int run_steps(myos_ctx* c, int kind, size_t nsteps) {
     StreamArgs a = c->sargs;
     a.head = head ? 1 : 0;
     a.feed = feed;
+    const uint64_t per_step = 5 * (uint64_t)c->s.num_layers + (head ? 1 : 0);
     for (size_t done = 0; done < nsteps;) {
       a.nsteps = (int)std::min(nsteps - done, kStreamMaxSteps);
+      // epochs are 32-bit phase counts: restart them long before they wrap
+      if (c->s_phases + per_step * a.nsteps >= (1ull << 31)) {
+        CK(cudaMemsetAsync(c->sflags, 0, (size_t)c->sargs.grid * sizeof(unsigned), c->st));
+        CK(cudaMemsetAsync(c->s_words, 0, c->s_words_bytes, c->st));
+        c->s_phases = 0;
+      }
       CK(launch_step_stream(a, c->st));
+      c->s_phases += per_step * a.nsteps;
       done += (size_t)a.nsteps;
     }
     return MYOS_OK;
@@ -595,10 +605,14 @@ int finish(myos_ctx* c) {
     const uint32_t bits = c->ctl_host->err;
     c->ctl_host->err = 0;
     cudaMemcpy(&c->ctl->err, &c->ctl_host->err, 4, cudaMemcpyHostToDevice);
-    // an abandoned streaming launch leaves its arrival flags and merge
-    // counters partway: start the next launch from zero
-    if (c->sflags)
-      cudaMemset(c->sflags, 0, (2 + (size_t)c->sargs.grid + c->s.num_kv_heads) * sizeof(unsigned));
+    // an abandoned streaming launch leaves its phase counts and words
+    // partway: start the next launch from zero (no stale word can then
+    // carry an epoch a later phase expects)
+    if (c->sflags) {
+      cudaMemset(c->sflags, 0, (size_t)c->sargs.grid * sizeof(unsigned));
+      cudaMemset(c->s_words, 0, c->s_words_bytes);
+      c->s_phases = 0;
+    }
     return fail(c, MYOS_ERR_TIMEOUT,
                 "a bounded device wait gave up (bits " + std::to_string(bits) + ")");
   }
@@ -918,15 +932,14 @@ static int create_impl(myos_ctx* c, const myos_shape* shape, const myos_opts* op
       a.grid = c->num_sms;
       a.S = (int)S;
       a.kv_bf16 = opts->kv_dtype == MYOS_KV_BF16;
-      // split-KV tasks of 64 keys, at most one per CTA; with at most four
-      // splits per KV head the o_proj staging merges them
-      size_t ns = (S + 63) / 64;
+      // split-KV tasks of one 32-key tile (its keys prefetched while q, k
+      // and v are awaited), at most one per CTA
+      size_t ns = (S + 31) / 32;
       const size_t cap = (size_t)c->num_sms / s.num_kv_heads;
       if (ns > cap) ns = cap;
       if (ns < 1) ns = 1;
       a.nsplit = (int)ns;
       a.chunk = (int)((S + ns - 1) / ns);
-      a.merge_in_stage = ns <= 4 ? 1 : 0;
       int max_smem = 0;
       CK(cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, c->device));
       if (c->qd_pad == c->qd && stream_configure(&a, max_smem) == cudaSuccess) {
@@ -937,13 +950,13 @@ static int create_impl(myos_ctx* c, const myos_shape* shape, const myos_opts* op
         }
         CK(cudaMalloc(&c->d_slayers, L * sizeof(StreamLayer)));
         CK(cudaMemcpy(c->d_slayers, hl.data(), L * sizeof(StreamLayer), cudaMemcpyHostToDevice));
-        // [0..1] the 64-bit arrival counter, then [grid] per-CTA counts and
-        // [Hkv] merge counters
-        const size_t nflags = 2 + (size_t)a.grid + s.num_kv_heads;
-        CK(cudaMalloc(&c->sflags, nflags * sizeof(unsigned)));
-        CK(cudaMemset(c->sflags, 0, nflags * sizeof(unsigned)));
-        const size_t npart = (size_t)s.num_kv_heads * ns * c->G;
-        CK(cudaMalloc(&c->s_work, (npart * (d + 2) + 2 * (size_t)a.grid) * sizeof(float)));
+        // [grid] per-CTA phase counts, then the hand-over words
+        CK(cudaMalloc(&c->sflags, (size_t)a.grid * sizeof(unsigned)));
+        CK(cudaMemset(c->sflags, 0, (size_t)a.grid * sizeof(unsigned)));
+        c->s_words_bytes = stream_word_count(a) * sizeof(uint64_t);
+        CK(cudaMalloc(&c->s_words, c->s_words_bytes));
+        CK(cudaMemset(c->s_words, 0, c->s_words_bytes));
+        stream_set_words(&a, c->s_words);
         a.embed = c->embed;
         a.head_w = s.tied_head ? c->embed : c->lm_head;
         a.final_norm = c->final_norm;
@@ -961,14 +974,7 @@ static int create_impl(myos_ctx* c, const myos_shape* shape, const myos_opts* op
         a.kv_layer_elems = c->kv_layer_elems;
         a.cos_t = c->cos_t;
         a.sin_t = c->sin_t;
-        a.part_o = c->s_work;
-        a.part_m = a.part_o + npart * d;
-        a.part_l = a.part_m + npart;
-        a.cand_val = a.part_l + npart;
-        a.cand_idx = reinterpret_cast<uint32_t*>(a.cand_val + a.grid);
-        a.bar = reinterpret_cast<unsigned long long*>(c->sflags);
-        a.flags = c->sflags + 2;
-        a.attn_cnt = a.flags + a.grid;
+        a.flags = c->sflags;
         a.wait_ns = 1000000000ull;
         // ring copies outstanding at once, and slots requested into L2 ahead
         const char* fe = getenv("MYOS_STREAM_INFLIGHT");
@@ -1170,7 +1176,7 @@ void myos_ctx_destroy(myos_ctx* c) {
   void* dev[] = {c->warena, c->kcache, c->vcache, c->resid, c->qkv, c->attn, c->act, c->logits,
                  c->part_val, c->part_idx, c->part_o, c->part_m, c->part_l, c->counters, c->ctl,
                  c->feed, c->rec_fed, c->rec_argmax, c->cos_t, c->sin_t, c->d_slayers, c->sflags,
-                 c->s_work, (void*)c->trace, (void*)c->strace,
+                 c->s_words, (void*)c->trace, (void*)c->strace,
                  (void*)c->ktrace, c->pf_X, c->pf_D, c->pf_Q, c->pf_att, c->pf_A, c->pf_ws,
                  c->bt_k, c->bt_v, c->bt_X, c->bt_D, c->bt_pos, c->bt_rows, c->bt_tok,
                  c->bt_out, c->bt_ids, c->bt_feed, c->tp_part, c->tp_cand, c->tp_link};

@@ -11,30 +11,37 @@
 //     owns a contiguous row range of every weight matrix;
 //   * a producer warp copies the CTA's rows, matrix after matrix in step
 //     order, with 1-D bulk copies (cp.async.bulk, the TMA engine) into a
-//     4-slot shared-memory ring of ~45 KB slots. It waits for a free slot
-//     and keeps few copies outstanding (every queued request in the memory
-//     system delays the consumers' barrier and staging accesses), never for
-//     activations: during a phase boundary (grid barrier, input staging,
-//     attention) HBM keeps filling the ring with the next phases' weights;
-//   * 15 consumer warps stage each phase's input vector in shared memory
-//     with cp.async (RMSNorm fused, crates/tensor_core/src/bf16.rs:231-270),
-//     dot every ring slot's rows against it (bf16 weights promoted exactly,
-//     f32 FMA, fixed reduction order: deterministic) and apply the epilogue:
-//     QKV bias (bf16.rs:147-158), residual add (qwen25_block.rs:172-178),
-//     SiLU(gate) * up (swiglu.rs:113-131,254-261), logits and the
-//     first-maximum argmax (model_core/src/lib.rs:157-167);
+//     4-slot shared-memory ring of ~45 KB slots. It waits only for a free
+//     slot and keeps few copies outstanding (every queued request in the
+//     memory system delays the consumers' dependent accesses), never for
+//     activations, so HBM keeps filling the ring while the consumers wait on
+//     the previous phase or run attention;
+//   * consumer warps stage each phase's input vector in shared memory
+//     (RMSNorm fused, crates/tensor_core/src/bf16.rs:231-270), dot every
+//     ring slot's rows against it (bf16 weights promoted exactly, f32 FMA,
+//     fixed reduction order: deterministic) and apply the epilogue: QKV bias
+//     (bf16.rs:147-158), residual add (qwen25_block.rs:172-178), SiLU(gate)
+//     * up (swiglu.rs:113-131,254-261), logits and the first-maximum argmax
+//     (model_core/src/lib.rs:157-167);
 //   * attention (gqa.rs:174-307) runs as split-KV tasks (KV head, key range)
 //     on the first CTAs, with RoPE (rope.rs:145-184) and the KV store
-//     (kv_cache.rs:149-302) fused; the split partials are merged in the
-//     o_proj input staging (few splits) or by the last task of a KV head;
-//   * phases are separated by a grid barrier of per-CTA arrival flags
-//     (monotonic counts, no atomics); every wait is bounded in time, and a
-//     wait that gives up raises kErrStream in ctl->err and ends the launch;
-//   * several token steps run per launch: the greedy token is reduced by
-//     every CTA from the per-CTA head candidates, so the next step starts
-//     without a host round trip or a relaunch.
-// With most of shared memory taken by the ring, L1 is small: the kernel is
-// written to keep its state in registers (no local-memory stack).
+//     (kv_cache.rs:149-302) fused; the tasks of a KV head then merge its
+//     query heads' split partials among themselves;
+//   * there is no grid barrier: every vector a phase hands to the next (q|k|v,
+//     split partials, attention output, residual, activations, head
+//     candidates) is stored as 8-byte words (value bits, epoch), where the
+//     epoch numbers the producing phase. An aligned 8-byte store is seen
+//     whole, so a reader polls the words it needs until each carries the
+//     expected epoch: the data is its own flag, with no fence, counter or
+//     separate staging round trip. Every phase needs the whole output of the
+//     one before, so no word is rewritten while a reader may still want its
+//     previous value. Every wait is bounded in time; a wait that gives up
+//     raises kErrStream in ctl->err and ends the launch;
+//   * several token steps run per launch: every CTA reduces the greedy token
+//     from the per-CTA head candidates, so the next step starts without a
+//     host round trip or a relaunch.
+// With most of shared memory taken by the ring, L1 is small: the kernel keeps
+// its state in registers (no local-memory stack).
 #include <math.h>
 
 #include <algorithm>
@@ -47,7 +54,7 @@ namespace myos {
 namespace {
 
 #ifndef MYOS_STREAM_WARPS
-#define MYOS_STREAM_WARPS 15  // consumer warps (16 warps in all: 128 registers a thread)
+#define MYOS_STREAM_WARPS 11  // consumer warps (12 warps in all: 168 registers a thread)
 #endif
 constexpr int kNCW = MYOS_STREAM_WARPS;
 constexpr int kCT = kNCW * 32;      // consumer threads
@@ -57,25 +64,16 @@ constexpr int kGMax = 8;            // query heads per KV head
 constexpr int kD = 128;             // head dim of the supported shapes
 constexpr int kBar = 1;             // named barrier of the consumer warps
 constexpr int kMaxLayers = 128;
+constexpr int kDotBatch = 4;        // slot chunks a lane loads before its FMAs
+constexpr int kStageMax = 3;        // 8-value chunks a consumer thread stages per round
 
 MYOS_DEV void csync() { named_sync(kBar, kCT); }
-
-MYOS_DEV float4 ldcg4(const float* p) { return __ldcg(reinterpret_cast<const float4*>(p)); }
 
 MYOS_DEV void cpa16(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src)
                : "memory");
 }
 MYOS_DEV void cpa_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
-
-MYOS_DEV uint32_t ld_acquire(const unsigned* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-MYOS_DEV void st_release(unsigned* p, uint32_t v) {
-  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
 
 MYOS_DEV float silu_mul(float g, float u) {
   // z / (1 + expf(-z)), then one multiply (swiglu.rs:113-115, 254-261)
@@ -89,6 +87,23 @@ MYOS_DEV bool better(float v, uint32_t i, float bv, uint32_t bi) {
   return v > -INFINITY && (v > bv || (v == bv && i < bi));
 }
 
+// ---------------------------------------------------------------- epoch words
+MYOS_DEV uint64_t word(float v, uint32_t e) {
+  return ((uint64_t)e << 32) | __float_as_uint(v);
+}
+MYOS_DEV float word_val(uint64_t w) { return __uint_as_float((uint32_t)w); }
+MYOS_DEV uint32_t word_epoch(uint64_t w) { return (uint32_t)(w >> 32); }
+
+MYOS_DEV void put_word(uint64_t* p, uint64_t w) {
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+MYOS_DEV void put_words2(uint64_t* p, uint64_t a, uint64_t b) {  // p 16-byte aligned
+  asm volatile("st.relaxed.gpu.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(a), "l"(b) : "memory");
+}
+MYOS_DEV void get_words2(const uint64_t* p, uint64_t& a, uint64_t& b) {  // p 16-byte aligned
+  asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+
 // ---------------------------------------------------------------- shared state
 // Dynamic shared memory: [ring: kNS x slot_bytes][scr][part][res][bias][layer
 // table], at the offsets stream_configure puts in the arguments (no pointer
@@ -99,7 +114,7 @@ __shared__ uint32_t s_wbi[kNCW];
 __shared__ uint64_t s_full[kNS];       // ring: slot landed
 __shared__ uint64_t s_empty[kNS];      // ring: slot consumed by every consumer warp
 __shared__ volatile int s_abort;       // a wait gave up: every role stops
-__shared__ uint32_t s_tok[2];          // reduced greedy token; last-task flag of a merge
+__shared__ uint32_t s_tok;             // reduced greedy token
 
 MYOS_DEV uint8_t* smem_base() {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -186,6 +201,28 @@ MYOS_DEV bool ring_wait(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
   }
 }
 
+// A word poll gave up (time bound, this CTA aborted, or another CTA raised
+// the error bit): raise the bit here too.
+MYOS_DEV bool poll_failed(const StreamArgs& a, uint64_t t0) {
+  if (s_abort || (*(volatile uint32_t*)&a.ctl->err & kErrStream) || global_ns() - t0 > a.wait_ns) {
+    give_up(a);
+    return true;
+  }
+  return false;
+}
+
+// Two adjacent words (16-byte aligned) once both carry epoch e.
+MYOS_DEV bool poll2(const StreamArgs& a, const uint64_t* p, uint32_t e, uint64_t& w0, uint64_t& w1) {
+  get_words2(p, w0, w1);
+  if (word_epoch(w0) == e && word_epoch(w1) == e) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t i = 1;; ++i) {
+    get_words2(p, w0, w1);
+    if (word_epoch(w0) == e && word_epoch(w1) == e) return true;
+    if ((i & 31u) == 0 && poll_failed(a, t0)) return false;
+  }
+}
+
 // ---------------------------------------------------------------- trace
 MYOS_DEV uint64_t* trace_row(const StreamArgs& a, int t, int ph) {
   return (a.trace && t == a.nsteps - 1) ? a.trace + ((size_t)blockIdx.x * (5 * a.L + 1) + ph) * 8
@@ -193,16 +230,6 @@ MYOS_DEV uint64_t* trace_row(const StreamArgs& a, int t, int ph) {
 }
 MYOS_DEV void mark(uint64_t* row, int k) {
   if (row && threadIdx.x == 0) row[k] = global_ns();
-}
-
-// Optional per-slot stamps of the last step: [grid][kSlotTrace][4] =
-// (producer issued, consumer warp 0 saw it landed, warp 0 released it, -).
-constexpr int kSlotTrace = 640;
-MYOS_DEV void slot_mark(const StreamArgs& a, uint32_t seq, int k) {
-  if (!a.strace) return;
-  const uint32_t base = a.strace_seq0;
-  if (seq < base || seq - base >= (uint32_t)kSlotTrace) return;
-  a.strace[((size_t)blockIdx.x * kSlotTrace + (seq - base)) * 4 + k] = global_ns();
 }
 
 // ---------------------------------------------------------------- producer
@@ -274,10 +301,9 @@ MYOS_DEV void cur_issue(const StreamArgs& a, const Cursor& c, int slot, bool to_
     bulk_g2s(dst + (size_t)g.rps * g.K * 2, g.w1 + (size_t)c.r * g.K, bytes, &s_full[slot]);
 }
 
-// At most a.inflight copies outstanding (issued, not landed): one ~45 KB
-// copy per SM already keeps HBM streaming, and more only lengthen every
-// queue. Landed slots wait in the ring for the consumers. With a.l2_la > 0
-// the slot that many places ahead is also requested into L2.
+// At most a.inflight copies outstanding (issued, not landed): more only
+// lengthen every queue. Landed slots wait in the ring for the consumers.
+// With a.l2_la > 0 the slot that many places ahead is also requested into L2.
 MYOS_DEV void producer(const StreamArgs& a) {
   uint32_t seq = 0;
   bool ok = true;
@@ -302,7 +328,6 @@ MYOS_DEV void producer(const StreamArgs& a) {
       }
     }
     cur_issue(a, c, slot, false);
-    slot_mark(a, seq, 0);
     ++seq;
     cur_next(a, c);
     if (a.l2_la && pf.t < a.nsteps) {
@@ -315,55 +340,6 @@ MYOS_DEV void producer(const StreamArgs& a) {
   // all of them on the normal path; after an abort this drains them).
   const uint32_t first = seq > (uint32_t)kNS ? seq - kNS : 0u;
   for (uint32_t q = first; q < seq; ++q) mbar_wait(&s_full[q % kNS], (q / kNS) & 1u, nullptr, 0u);
-}
-
-// ---------------------------------------------------------------- grid barrier
-// One 64-bit arrival counter per context, never reset: every CTA adds 1 per
-// barrier, so after barrier n of this CTA (counting all launches, flags[b]
-// holds the count at launch start) the counter reaches grid * n once every
-// CTA has arrived. Arrival: the consumer barrier orders every consumer
-// thread's writes before thread 0's release add (cumulative at gpu scope).
-// One poller per CTA keeps the counter's line from being flooded.
-MYOS_DEV void red_release_add(unsigned long long* p, unsigned long long v) {
-  asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-MYOS_DEV unsigned long long ld_acquire64(const unsigned long long* p) {
-  unsigned long long v;
-  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
-
-MYOS_DEV void arrive(const StreamArgs& a, uint32_t count, uint64_t* tr = nullptr) {
-  csync();
-  if (threadIdx.x == 0) {
-    mark(tr, 3);
-    red_release_add(a.bar, 1ull);
-    mark(tr, 4);
-  }
-  (void)count;
-}
-
-// Wait until every CTA arrived at `count` barriers. The outcome is read
-// after the consumer barrier, so it is uniform.
-MYOS_DEV bool wait_all(const StreamArgs& a, uint32_t count) {
-  if (threadIdx.x == 0) {
-    const unsigned long long target = (unsigned long long)a.grid * count;
-    if (ld_acquire64(a.bar) < target) {
-      const uint64_t t0 = global_ns();
-      for (uint32_t i = 1;; ++i) {
-        if (ld_acquire64(a.bar) >= target) break;
-        if ((i & 63u) == 0) {
-          if (s_abort || (*(volatile uint32_t*)&a.ctl->err & kErrStream) ||
-              global_ns() - t0 > a.wait_ns) {
-            give_up(a);
-            break;
-          }
-        }
-      }
-    }
-  }
-  csync();
-  return !s_abort;
 }
 
 // ---------------------------------------------------------------- reductions
@@ -389,52 +365,83 @@ MYOS_DEV float cons_sum(float v) {
 // norm weight gamma [K] sits right after xs (gs = xs + K), the raw bf16
 // embedding row after that.
 
-// Before the phase's barrier: the norm weight depends on no kernel.
+// The norm weight depends on no earlier phase: copied while the input is
+// still being produced.
 MYOS_DEV void gamma_issue(float* gs, const float* gamma, int K) {
   for (int c = threadIdx.x; c < (K >> 2); c += kCT) cpa16(gs + 4 * c, gamma + 4 * c);
 }
 
-// xs <- x (f32, written by other CTAs: cp.async reads through L2) or the
-// bf16 embedding row erow; with norm, x = gamma * (x * inv), inv = 1 /
-// sqrtf(mean(x^2) + eps) (gamma already issued into gs). raw_store (CTA 0 of
-// the first layer): the un-normalised row is also written there (the
-// residual stream starts as the embedding). keep: the un-normalised elements
-// [k0, k1) also go there (this CTA's residual rows, for the o_proj and down
-// epilogues, so they need no load of their own).
-MYOS_DEV void stage(float* xs, int K, const float* x, const uint16_t* erow, bool norm, float eps,
-                    float* raw_store, float* keep, int k0, int k1, uint64_t* tr) {
+// xs <- the words w[0..K) of epoch e (every thread polls its own chunks of 8
+// values, all of its loads in flight at once, then reloads only stale pairs
+// until each carries e), or the bf16 embedding row erow; with norm, x =
+// gamma * (x * inv), inv = 1 / sqrtf(mean(x^2) + eps) (gamma already issued
+// into gs). keep: the un-normalised elements [k0, k1) also go there (this
+// CTA's residual rows, for the o_proj and down epilogues). Each thread
+// reads back only the chunks it wrote, so no barrier is needed before the
+// final one. Returns false (uniformly) when a poll gave up.
+MYOS_DEV bool stage(const StreamArgs& a, float* xs, int K, const uint64_t* w, uint32_t e,
+                    const uint16_t* erow, bool norm, float* keep, int k0, int k1, uint64_t* tr) {
   const int nchunk = K >> 3, half = K >> 1;
   float* gs = xs + K;
   uint16_t* eb = reinterpret_cast<uint16_t*>(gs + K);
-  for (int c = threadIdx.x; c < nchunk; c += kCT) {
-    if (erow) {
-      cpa16(eb + 8 * c, erow + 8 * c);
-    } else {
-      cpa16(xs + 4 * c, x + 8 * c);
-      cpa16(xs + half + 4 * c, x + 8 * c + 4);
+  if (erow) {
+    for (int c = threadIdx.x; c < nchunk; c += kCT) cpa16(eb + 8 * c, erow + 8 * c);
+    cpa_wait_all();  // this thread's chunks (and its share of gamma)
+    for (int c = threadIdx.x; c < nchunk; c += kCT) {
+      const uint4 u = *reinterpret_cast<const uint4*>(eb + 8 * c);
+      reinterpret_cast<float4*>(xs)[c] = make_float4(bf16_lo(u.x), bf16_hi(u.x), bf16_lo(u.y), bf16_hi(u.y));
+      reinterpret_cast<float4*>(xs + half)[c] = make_float4(bf16_lo(u.z), bf16_hi(u.z), bf16_lo(u.w), bf16_hi(u.w));
     }
+  } else {
+    // rounds of kStageMax chunks per thread (every load of a round in flight)
+    const uint64_t t0 = global_ns();
+    for (int base = 0; base < nchunk; base += kStageMax * kCT) {
+      uint64_t v[kStageMax][8];
+#pragma unroll
+      for (int i = 0; i < kStageMax; ++i) {
+        const int c = base + threadIdx.x + i * kCT;
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (c < nchunk) get_words2(w + 8 * c + 2 * j, v[i][2 * j], v[i][2 * j + 1]);
+          else v[i][2 * j] = v[i][2 * j + 1] = (uint64_t)e << 32;
+      }
+      for (uint32_t it = 1;; ++it) {
+        bool stale = false;
+#pragma unroll
+        for (int i = 0; i < kStageMax; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            if (word_epoch(v[i][2 * j]) != e || word_epoch(v[i][2 * j + 1]) != e) {
+              stale = true;
+              get_words2(w + 8 * (base + threadIdx.x + i * kCT) + 2 * j, v[i][2 * j], v[i][2 * j + 1]);
+            }
+        if (!stale) break;
+        if ((it & 31u) == 0 && poll_failed(a, t0)) break;
+      }
+#pragma unroll
+      for (int i = 0; i < kStageMax; ++i) {
+        const int c = base + threadIdx.x + i * kCT;
+        if (c < nchunk) {
+          reinterpret_cast<float4*>(xs)[c] =
+              make_float4(word_val(v[i][0]), word_val(v[i][1]), word_val(v[i][2]), word_val(v[i][3]));
+          reinterpret_cast<float4*>(xs + half)[c] =
+              make_float4(word_val(v[i][4]), word_val(v[i][5]), word_val(v[i][6]), word_val(v[i][7]));
+        }
+      }
+      if (s_abort) break;
+    }
+    cpa_wait_all();  // this thread's share of gamma
   }
-  cpa_wait_all();  // this thread's chunks (and its share of gamma)
   mark(tr, 5);
   float ss = 0.0f;
   for (int c = threadIdx.x; c < nchunk; c += kCT) {
-    float4* lo = reinterpret_cast<float4*>(xs + 4 * c);
-    float4* hi = reinterpret_cast<float4*>(xs + half + 4 * c);
-    if (erow) {
-      const uint4 u = *reinterpret_cast<const uint4*>(eb + 8 * c);
-      *lo = make_float4(bf16_lo(u.x), bf16_hi(u.x), bf16_lo(u.y), bf16_hi(u.y));
-      *hi = make_float4(bf16_lo(u.z), bf16_hi(u.z), bf16_lo(u.w), bf16_hi(u.w));
-    }
-    const float4 p = *lo, q = *hi;
-    if (raw_store) {
-      reinterpret_cast<float4*>(raw_store)[2 * c] = p;
-      reinterpret_cast<float4*>(raw_store)[2 * c + 1] = q;
-    }
+    const float4 p = reinterpret_cast<const float4*>(xs)[c];
+    const float4 q = reinterpret_cast<const float4*>(xs + half)[c];
     if (keep && 8 * c + 8 > k0 && 8 * c < k1) {
-      const float v[8] = {p.x, p.y, p.z, p.w, q.x, q.y, q.z, q.w};
+      const float vv[8] = {p.x, p.y, p.z, p.w, q.x, q.y, q.z, q.w};
 #pragma unroll
-      for (int e = 0; e < 8; ++e)
-        if (8 * c + e >= k0 && 8 * c + e < k1) keep[8 * c + e - k0] = v[e];
+      for (int k = 0; k < 8; ++k)
+        if (8 * c + k >= k0 && 8 * c + k < k1) keep[8 * c + k - k0] = vv[k];
     }
     if (norm) {
       ss = fmaf(p.x, p.x, ss);
@@ -448,12 +455,12 @@ MYOS_DEV void stage(float* xs, int K, const float* x, const uint16_t* erow, bool
     }
   }
   if (norm) {
-    ss = cons_sum(ss);
+    ss = cons_sum(ss);  // gamma of every thread is in shared memory after this barrier
     mark(tr, 6);
-    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), eps)));
+    const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)K), a.eps)));
     for (int c = threadIdx.x; c < nchunk; c += kCT) {
-      float4* lo = reinterpret_cast<float4*>(xs + 4 * c);
-      float4* hi = reinterpret_cast<float4*>(xs + half + 4 * c);
+      float4* lo = reinterpret_cast<float4*>(xs) + c;
+      float4* hi = reinterpret_cast<float4*>(xs + half) + c;
       const float4 p = *lo, q = *hi;
       const float4 ga = *reinterpret_cast<const float4*>(gs + 8 * c);
       const float4 gb = *reinterpret_cast<const float4*>(gs + 8 * c + 4);
@@ -464,122 +471,41 @@ MYOS_DEV void stage(float* xs, int K, const float* x, const uint16_t* erow, bool
     }
   }
   csync();
-}
-
-// o_proj input as the merge of the split-KV partials of the splits holding
-// keys 0..pos. Per head h (KV head g = h / G): M = max_q m_q, f_q =
-// expf(m_q - M), L = sum_q l_q f_q, x = (sum_q o_q f_q) / L, sums in split
-// order (the reference's e / sum, gqa.rs:283-307, reassociated).
-MYOS_DEV void stage_merge(const StreamArgs& a, float* xs, int pos) {
-  const int G = a.G, d = kD, ns = a.nsplit, Hq = a.Hq, Hkv = a.Hkv, K = a.qd;
-  int ne = (pos + a.chunk) / a.chunk;
-  if (ne > ns) ne = ns;
-  float* po = xs + K;                         // [Hkv][ns][G][d] (valid splits)
-  float* fs = po + (size_t)Hkv * ns * G * d;  // [Hkv][ns][G]
-  float* ls = fs + Hkv * ns * G;
-  float* Ls = ls + Hkv * ns * G;              // [Hq]
-  const int per_g = ne * G * d;
-  const int q4 = per_g >> 2;
-  for (int i = threadIdx.x; i < Hkv * q4; i += kCT) {
-    const int g = i / q4, r = i - g * q4;
-    const size_t off = (size_t)g * ns * G * d + 4 * (size_t)r;
-    cpa16(po + off, a.part_o + off);
-  }
-  const int per_m = ne * G;
-  for (int i = threadIdx.x; i < Hkv * per_m; i += kCT) {
-    const int g = i / per_m, r = i - g * per_m;
-    const int off = g * ns * G + r;
-    fs[off] = __ldcg(a.part_m + off);
-    ls[off] = __ldcg(a.part_l + off);
-  }
-  cpa_wait_all();
-  csync();
-  if (threadIdx.x < Hq) {
-    const int h = threadIdx.x, g = h / G, hh = h - g * G;
-    float M = -INFINITY;
-    for (int q = 0; q < ne; ++q) M = fmaxf(M, fs[(g * ns + q) * G + hh]);
-    float L = 0.0f;
-    for (int q = 0; q < ne; ++q) {
-      const int i = (g * ns + q) * G + hh;
-      const float f = fs[i] == -INFINITY ? 0.0f : expf(fs[i] - M);
-      fs[i] = f;
-      L = fmaf(ls[i], f, L);
-    }
-    Ls[h] = L;
-  }
-  csync();
-  for (int o = threadIdx.x; o < K; o += kCT) {
-    const int h = o / d, e = o - h * d, g = h / G, hh = h - g * G;
-    float O = 0.0f;
-    for (int q = 0; q < ne; ++q) {
-      const int i = (g * ns + q) * G + hh;
-      O = fmaf(po[(size_t)i * d + e], fs[i], O);
-    }
-    const float v = __fdiv_rn(O, Ls[h]);
-    const int c = o >> 3, r = o & 7;
-    xs[r < 4 ? (c * 4 + r) : ((K >> 1) + c * 4 + (r - 4))] = v;
-  }
-  csync();
+  return !s_abort;
 }
 
 // ---------------------------------------------------------------- GEMV over ring slots
-// A warp keeps the same chunk columns of the input for every row it
-// computes in a phase (chunks c = c0 + lane + 32 j, j < nj, of [c0, c1)), so
-// its lanes hold those input values in registers for the whole phase and
-// read only weights from the ring: shared-memory traffic is then the bulk
-// copy in and one read of each weight (re-reading the f32 input per weight
-// chunk would triple it and make the consumers bound by shared memory).
-constexpr int kXMax = 8;  // input chunks a lane holds (K / warps-per-row / 256 <= 8)
-
-struct XRegs {
-  float4 lo[kXMax], hi[kXMax];
-  int nj;     // chunks this lane holds
-  int cbase;  // c0 + lane
-};
-
-MYOS_DEV void x_load(XRegs& x, const float* xs, int K, int c0, int c1, int lane) {
-  const float4* xlo = reinterpret_cast<const float4*>(xs);
-  const float4* xhi = reinterpret_cast<const float4*>(xs + (K >> 1));
-  x.cbase = c0 + lane;
-  x.nj = x.cbase < c1 ? (c1 - x.cbase + 31) / 32 : 0;
-#pragma unroll
-  for (int j = 0; j < kXMax; ++j) {
-    if (j < x.nj) {
-      x.lo[j] = xlo[x.cbase + 32 * j];
-      x.hi[j] = xhi[x.cbase + 32 * j];
-    }
-  }
-}
-
-// Row i of a slot (NR matrices: rows of matrix r at offset r * rps * K * 2)
-// against the lane's input chunks: weight loads of four chunks issued at
-// once, two accumulators per matrix, then the warp's shuffle tree.
+// Row i of a slot (NR matrices: rows of matrix r at offset r * rps * K * 2),
+// chunks [c0, c1) of 16 bytes: lane-strided, loads of kDotBatch chunks
+// issued at once, two accumulators per matrix, then the warp's shuffle tree.
 template <int NR>
-MYOS_DEV void dot_row(const uint8_t* sp, int rps, int K, int i, const XRegs& x, float& o0,
-                      float& o1) {
+MYOS_DEV void dot_part(const uint8_t* sp, int rps, int K, int i, int c0, int c1, const float4* xlo,
+                       const float4* xhi, int lane, float& o0, float& o1) {
   const size_t rowb = (size_t)K * 2;
-  const uint4* w0 = reinterpret_cast<const uint4*>(sp + (size_t)i * rowb) + x.cbase;
-  const uint4* w1 = reinterpret_cast<const uint4*>(sp + (size_t)(rps + i) * rowb) + x.cbase;
+  const uint4* w0 = reinterpret_cast<const uint4*>(sp + (size_t)i * rowb);
+  const uint4* w1 = reinterpret_cast<const uint4*>(sp + (size_t)(rps + i) * rowb);
   float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;
+  for (int cb = c0 + lane; cb < c1; cb += 32 * kDotBatch) {
+    uint4 u0[kDotBatch], u1[kDotBatch];
 #pragma unroll
-  for (int h = 0; h < kXMax; h += 4) {
-    uint4 u0[4], u1[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      if (h + j < x.nj) {
-        u0[j] = w0[32 * (h + j)];
-        if (NR == 2) u1[j] = w1[32 * (h + j)];
+    for (int j = 0; j < kDotBatch; ++j) {
+      const int c = cb + 32 * j;
+      if (c < c1) {
+        u0[j] = w0[c];
+        if (NR == 2) u1[j] = w1[c];
       }
     }
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      if (h + j < x.nj) {
+    for (int j = 0; j < kDotBatch; ++j) {
+      const int c = cb + 32 * j;
+      if (c < c1) {
+        const float4 lo = xlo[c], hi = xhi[c];
         if (j & 1) {
-          a1 = dot8(u0[j], x.lo[h + j], x.hi[h + j], a1);
-          if (NR == 2) b1 = dot8(u1[j], x.lo[h + j], x.hi[h + j], b1);
+          a1 = dot8(u0[j], lo, hi, a1);
+          if (NR == 2) b1 = dot8(u1[j], lo, hi, b1);
         } else {
-          a0 = dot8(u0[j], x.lo[h + j], x.hi[h + j], a0);
-          if (NR == 2) b0 = dot8(u1[j], x.lo[h + j], x.hi[h + j], b0);
+          a0 = dot8(u0[j], lo, hi, a0);
+          if (NR == 2) b0 = dot8(u1[j], lo, hi, b0);
         }
       }
     }
@@ -600,12 +526,13 @@ MYOS_DEV void keep_best(Best& b, float v, uint32_t row) {
   }
 }
 
-// Epilogue of one finished row (one thread writes).
+// Epilogue of one finished row (one thread writes); e is this phase's epoch.
 template <int KIND>
-MYOS_DEV void epi_row(const StreamArgs& a, int row, int r0, float v, float u) {
-  if (KIND == SK_QKV) a.qkv[row] = __fadd_rn(v, biasrows(a)[row - r0]);
-  if (KIND == SK_O || KIND == SK_DOWN) a.resid[row] = __fadd_rn(resrows(a)[row - r0], v);
-  if (KIND == SK_GU) a.act[row] = silu_mul(v, u);
+MYOS_DEV void epi_row(const StreamArgs& a, int row, int r0, float v, float u, uint32_t e) {
+  if (KIND == SK_QKV) put_word(a.w_qkv + row, word(__fadd_rn(v, biasrows(a)[row - r0]), e));
+  if (KIND == SK_O || KIND == SK_DOWN)
+    put_word(a.w_resid + row, word(__fadd_rn(resrows(a)[row - r0], v), e));
+  if (KIND == SK_GU) put_word(a.w_act + row, word(silu_mul(v, u), e));
   if (KIND == SK_HEAD) a.logits[row] = v;
 }
 
@@ -615,7 +542,7 @@ MYOS_DEV void epi_row(const StreamArgs& a, int row, int r0, float v, float u) {
 // the outcome is read from the shared abort flag after the final barrier,
 // so every consumer thread returns the same answer.
 template <int KIND>
-MYOS_DEV bool consume_gemv(const StreamArgs& a, int l, uint32_t& seq, Best& best) {
+MYOS_DEV bool consume_gemv(const StreamArgs& a, int l, uint32_t& seq, Best& best, uint32_t e) {
   constexpr int NR = KIND == SK_GU ? 2 : 1;
   const Geo g = geo(a, KIND, l);
   int r0, r1;
@@ -625,8 +552,8 @@ MYOS_DEV bool consume_gemv(const StreamArgs& a, int l, uint32_t& seq, Best& best
   const int rr = warp / wpr, pt = warp - rr * wpr;
   const int nchunk = g.K >> 3;
   const int c0 = pt * nchunk / wpr, c1 = (pt + 1) * nchunk / wpr;
-  XRegs x;
-  x_load(x, scr(a), g.K, c0, c1, lane);
+  const float4* xlo = reinterpret_cast<const float4*>(scr(a));
+  const float4* xhi = reinterpret_cast<const float4*>(scr(a) + (g.K >> 1));
   for (int r = r0; r < r1; r += g.rps) {
     const int n = min(g.rps, r1 - r);
     const int slot = (int)(seq % kNS);
@@ -635,15 +562,14 @@ MYOS_DEV bool consume_gemv(const StreamArgs& a, int l, uint32_t& seq, Best& best
       if (lane == 0) give_up(a);
       break;
     }
-    if (warp == 0 && lane == 0) slot_mark(a, seq, 1);
     const uint8_t* sp = ring_slot(a, slot);
     if (rr < rg) {
       for (int i = rr; i < n; i += rg) {
         float o0, o1 = 0.f;
-        dot_row<NR>(sp, g.rps, g.K, i, x, o0, o1);
+        dot_part<NR>(sp, g.rps, g.K, i, c0, c1, xlo, xhi, lane, o0, o1);
         const int row = r + i;
         if (wpr == 1) {
-          if (lane == 0) epi_row<KIND>(a, row, r0, o0, o1);
+          if (lane == 0) epi_row<KIND>(a, row, r0, o0, o1, e);
           if (KIND == SK_HEAD) keep_best(best, o0, (uint32_t)row);  // same value in every lane
         } else if (lane == 0) {
           float* pp = part(a) + ((size_t)(row - r0) * wpr + pt) * NR;
@@ -654,7 +580,6 @@ MYOS_DEV bool consume_gemv(const StreamArgs& a, int l, uint32_t& seq, Best& best
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&s_empty[slot]);
-    if (warp == 0 && lane == 0) slot_mark(a, seq, 2);
     ++seq;
   }
   csync();  // slots consumed (the staged input may be overwritten after this)
@@ -667,7 +592,7 @@ MYOS_DEV bool consume_gemv(const StreamArgs& a, int l, uint32_t& seq, Best& best
         v += pp[p * NR];
         if (NR == 2) u += pp[p * NR + 1];
       }
-      epi_row<KIND>(a, r0 + i, r0, v, u);
+      epi_row<KIND>(a, r0 + i, r0, v, u, e);
       if (KIND == SK_HEAD) keep_best(best, v, (uint32_t)(r0 + i));
     }
   }
@@ -734,69 +659,26 @@ MYOS_DEV void tile_issue(const AttnSm<KT>& s, const KT* kc, const KT* vc, int t0
   }
 }
 
-// Before the QKV barrier: the first tile's cached keys and the rotation row
-// depend on nothing this step computes.
-template <typename KT>
-MYOS_DEV void attn_prefetch(const StreamArgs& a, int l, int pos) {
-  const int task = blockIdx.x, g = task / a.nsplit, s = task - g * a.nsplit;
-  const int kb = s * a.chunk, ke = min(kb + a.chunk, pos + 1);
-  if (kb >= ke) return;
-  AttnSm<KT> at(scr(a), a.G, a.tile);
-  const size_t lo = (size_t)l * a.kv_layer_elems + (size_t)g * a.S * kD;
-  const KT* kc = reinterpret_cast<const KT*>(a.kcache) + lo;
-  const KT* vc = reinterpret_cast<const KT*>(a.vcache) + lo;
-  tile_issue<KT>(at, kc, vc, kb, min(a.tile, ke - kb), pos);
-  const float4* c4 = reinterpret_cast<const float4*>(a.cos_t + (size_t)pos * (kD / 2));
-  const float4* s4 = reinterpret_cast<const float4*>(a.sin_t + (size_t)pos * (kD / 2));
-  for (int i = threadIdx.x; i < kD / 8; i += kCT) {
-    cpa16(reinterpret_cast<float4*>(at.cs) + i, c4 + i);
-    cpa16(reinterpret_cast<float4*>(at.sn) + i, s4 + i);
-  }
-}
-
-// One warp merges one head over the splits q < ne (global partials):
-// M = max m_q, f_q = expf(m_q - M), L = sum l_q f_q, out = (sum o_q f_q) / L
-// in split order.
-MYOS_DEV void merge_head_global(const StreamArgs& a, int g, int h, int ne, int lane, float* out) {
-  const int ns = a.nsplit, G = a.G;
-  const size_t base = (size_t)g * ns * G + h;
-  float M = -INFINITY;
-  for (int q0 = 0; q0 < ne; q0 += 32)
-    M = fmaxf(M, warp_max(q0 + lane < ne ? __ldcg(a.part_m + base + (size_t)(q0 + lane) * G) : -INFINITY));
-  float Lp = 0.0f;
-  float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int q0 = 0; q0 < ne; q0 += 32) {
-    const int q = q0 + lane;
-    const float mq = q < ne ? __ldcg(a.part_m + base + (size_t)q * G) : -INFINITY;
-    const float f = mq == -INFINITY ? 0.0f : expf(mq - M);
-    if (q < ne) Lp = fmaf(__ldcg(a.part_l + base + (size_t)q * G), f, Lp);
-    const int nr = min(32, ne - q0);
-    for (int u = 0; u < nr; ++u) {
-      const float fu = __shfl_sync(0xffffffffu, f, u);
-      const float4 po = ldcg4(a.part_o + (base + (size_t)(q0 + u) * G) * kD + 4 * lane);
-      O.x = fmaf(po.x, fu, O.x);
-      O.y = fmaf(po.y, fu, O.y);
-      O.z = fmaf(po.z, fu, O.z);
-      O.w = fmaf(po.w, fu, O.w);
-    }
-  }
-  const float L = warp_sum(Lp);
-  *reinterpret_cast<float4*>(out + 4 * lane) =
-      make_float4(__fdiv_rn(O.x, L), __fdiv_rn(O.y, L), __fdiv_rn(O.z, L), __fdiv_rn(O.w, L));
+// Words of split partial (g, s, head h): o [d] then m, l.
+MYOS_DEV uint64_t* part_words(const StreamArgs& a, int g, int s, int h) {
+  return a.w_part + (((size_t)g * a.nsplit + s) * a.G + h) * (kD + 2);
 }
 
 // Split-KV task (KV head g, split s) of layer l at position pos: RoPE of q
 // and the new key (rope.rs:145-184), the KV store at pos, then for each
 // 32-key tile: scores (q . k) * scale (gqa.rs:189-191) lane per key, an
 // online softmax per head (one warp each), p . v lane per 4 dims. Writes the
-// task's (unnormalised output, max, sum) per head; without the staging
-// merge the last task of the KV head merges them into attn.
+// task's (unnormalised output, max, sum) per head as words of epoch e; then
+// the tasks that hold keys merge the KV head's query heads among themselves
+// (head h by task h mod ne): M = max m_q, f_q = expf(m_q - M), L = sum l_q
+// f_q, out = (sum o_q f_q) / L in split order (the reference's e / sum,
+// gqa.rs:283-307, reassociated), written as attention-output words.
 template <typename KT>
-MYOS_DEV void attn_task(const StreamArgs& a, int l, int pos) {
+MYOS_DEV bool attn_task(const StreamArgs& a, int l, int pos, uint32_t e_qkv, uint32_t e) {
   const int task = blockIdx.x, G = a.G, ns = a.nsplit;
   const int g = task / ns, s = task - g * ns;
   const int kb = s * a.chunk, ke = min(kb + a.chunk, pos + 1);
-  if (kb >= ke) return;
+  if (kb >= ke) return true;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr int half = kD / 2;
   AttnSm<KT> at(scr(a), G, a.tile);
@@ -805,18 +687,58 @@ MYOS_DEV void attn_task(const StreamArgs& a, int l, int pos) {
   KT* kc = reinterpret_cast<KT*>(a.kcache) + lo;
   KT* vc = reinterpret_cast<KT*>(a.vcache) + lo;
   const bool has_new = pos >= kb && pos < ke;
-  // q of the G heads; the new k and v when this split holds position pos
-  const int nq4 = G * kD / 4, d4 = kD / 4;
-  const float4* q4 = reinterpret_cast<const float4*>(a.qkv + (size_t)g * G * kD);
-  const float4* k4 = reinterpret_cast<const float4*>(a.qkv + (size_t)(a.Hq + g) * kD);
-  const float4* v4 = reinterpret_cast<const float4*>(a.qkv + (size_t)(a.Hq + a.Hkv + g) * kD);
-  for (int i = threadIdx.x; i < nq4 + (has_new ? 2 * d4 : 0); i += kCT) {
-    if (i < nq4) cpa16(reinterpret_cast<float4*>(at.qs) + i, q4 + i);
-    else if (i < nq4 + d4) cpa16(reinterpret_cast<float4*>(at.kn) + (i - nq4), k4 + (i - nq4));
-    else cpa16(reinterpret_cast<float4*>(at.vn) + (i - nq4 - d4), v4 + (i - nq4 - d4));
+  // the first tile's cached keys and the rotation row depend on nothing this
+  // step computes: in flight while q, k and v are polled
+  tile_issue<KT>(at, kc, vc, kb, min(a.tile, ke - kb), pos);
+  {
+    const float4* c4 = reinterpret_cast<const float4*>(a.cos_t + (size_t)pos * half);
+    const float4* s4 = reinterpret_cast<const float4*>(a.sin_t + (size_t)pos * half);
+    for (int i = threadIdx.x; i < half / 4; i += kCT) {
+      cpa16(reinterpret_cast<float4*>(at.cs) + i, c4 + i);
+      cpa16(reinterpret_cast<float4*>(at.sn) + i, s4 + i);
+    }
+  }
+  // q of the G heads; the new k and v when this split holds position pos:
+  // every pair's load in flight at once, then only stale pairs reloaded
+  {
+    const int nq = G * kD, npair = (nq + (has_new ? 2 * kD : 0)) / 2;
+    constexpr int kPairs = 4;  // (kGMax + 2) * kD / 2 pairs over the consumer threads
+    uint64_t v[kPairs][2];
+    const uint64_t* src[kPairs];
+#pragma unroll
+    for (int r = 0; r < kPairs; ++r) {
+      const int i = 2 * ((int)threadIdx.x + r * kCT);
+      src[r] = i < nq ? a.w_qkv + (size_t)g * G * kD + i
+                      : (i < nq + kD ? a.w_qkv + (size_t)(a.Hq + g) * kD + (i - nq)
+                                     : a.w_qkv + (size_t)(a.Hq + a.Hkv + g) * kD + (i - nq - kD));
+      if (i / 2 < npair) get_words2(src[r], v[r][0], v[r][1]);
+      else v[r][0] = v[r][1] = (uint64_t)e_qkv << 32;
+    }
+    const uint64_t t0 = global_ns();
+    for (uint32_t it = 1;; ++it) {
+      bool stale = false;
+#pragma unroll
+      for (int r = 0; r < kPairs; ++r)
+        if (word_epoch(v[r][0]) != e_qkv || word_epoch(v[r][1]) != e_qkv) {
+          stale = true;
+          get_words2(src[r], v[r][0], v[r][1]);
+        }
+      if (!stale) break;
+      if ((it & 31u) == 0 && poll_failed(a, t0)) break;
+    }
+#pragma unroll
+    for (int r = 0; r < kPairs; ++r) {
+      const int i = 2 * ((int)threadIdx.x + r * kCT);
+      if (i / 2 < npair) {
+        float* dst = i < nq ? at.qs + i : (i < nq + kD ? at.kn + (i - nq) : at.vn + (i - nq - kD));
+        dst[0] = word_val(v[r][0]);
+        dst[1] = word_val(v[r][1]);
+      }
+    }
   }
   cpa_wait_all();
   csync();
+  if (s_abort) return false;
   // NeoX rotation in place: y0 = x0*c - x1*s, y1 = x1*c + x0*s
   for (int i = threadIdx.x; i < (G + (has_new ? 1 : 0)) * half; i += kCT) {
     const int h = i / half, p = i - h * half;
@@ -827,13 +749,13 @@ MYOS_DEV void attn_task(const StreamArgs& a, int l, int pos) {
   }
   csync();
   if (has_new) {  // KvCache::store for this position, then the tile copy of it
-    for (int e = threadIdx.x; e < kD; e += kCT) {
-      const KT kq = kv_from<KT>(at.kn[e]), vq = kv_from<KT>(at.vn[e]);
-      kc[(size_t)pos * kD + e] = kq;
-      vc[(size_t)pos * kD + e] = vq;
+    for (int i = threadIdx.x; i < kD; i += kCT) {
+      const KT kq = kv_from<KT>(at.kn[i]), vq = kv_from<KT>(at.vn[i]);
+      kc[(size_t)pos * kD + i] = kq;
+      vc[(size_t)pos * kD + i] = vq;
       if (pos - kb < a.tile) {
-        at.kt[(pos - kb) * ds + e] = kq;
-        at.vt[(pos - kb) * ds + e] = vq;
+        at.kt[(pos - kb) * ds + i] = kq;
+        at.vt[(pos - kb) * ds + i] = vq;
       }
     }
     csync();
@@ -842,14 +764,14 @@ MYOS_DEV void attn_task(const StreamArgs& a, int l, int pos) {
   float m_run = -INFINITY, l_run = 0.0f;
   for (int t0 = kb; t0 < ke; t0 += a.tile) {
     const int nk = min(a.tile, ke - t0);
-    if (t0 != kb) {  // later tiles (the first was prefetched)
+    if (t0 != kb) {  // later tiles
       csync();
       tile_issue<KT>(at, kc, vc, t0, nk, pos);
       cpa_wait_all();
       if (has_new && pos >= t0 && pos < t0 + nk)
-        for (int e = threadIdx.x; e < kD; e += kCT) {
-          at.kt[(pos - t0) * ds + e] = kv_from<KT>(at.kn[e]);
-          at.vt[(pos - t0) * ds + e] = kv_from<KT>(at.vn[e]);
+        for (int i = threadIdx.x; i < kD; i += kCT) {
+          at.kt[(pos - t0) * ds + i] = kv_from<KT>(at.kn[i]);
+          at.vt[(pos - t0) * ds + i] = kv_from<KT>(at.vn[i]);
         }
       csync();
     }
@@ -860,9 +782,9 @@ MYOS_DEV void attn_task(const StreamArgs& a, int l, int pos) {
         const KT* kr = at.kt + lane * ds;
         float p0 = 0.f, p1 = 0.f, p2 = 0.f, p3 = 0.f;
 #pragma unroll 8
-        for (int e = 0; e < kD; e += 4) {
-          const float4 q = *reinterpret_cast<const float4*>(qh + e);
-          const float4 k = ld4<KT>(kr + e);
+        for (int i = 0; i < kD; i += 4) {
+          const float4 q = *reinterpret_cast<const float4*>(qh + i);
+          const float4 k = ld4<KT>(kr + i);
           p0 = fmaf(q.x, k.x, p0);
           p1 = fmaf(q.y, k.y, p1);
           p2 = fmaf(q.z, k.z, p2);
@@ -890,36 +812,108 @@ MYOS_DEV void attn_task(const StreamArgs& a, int l, int pos) {
       }
     }
   }
-  const size_t pb = ((size_t)g * ns + s) * G;  // partial row of (g, s, head 0)
   if (warp < G) {
-    *reinterpret_cast<float4*>(a.part_o + (pb + warp) * kD + 4 * lane) = acc;
-    if (lane == 0) {
-      a.part_m[pb + warp] = m_run;
-      a.part_l[pb + warp] = l_run;
-    }
+    uint64_t* pw = part_words(a, g, s, warp);
+    put_words2(pw + 4 * lane, word(acc.x, e), word(acc.y, e));
+    put_words2(pw + 4 * lane + 2, word(acc.z, e), word(acc.w, e));
+    if (lane == 0) put_words2(pw + kD, word(m_run, e), word(l_run, e));
   }
-  if (!a.merge_in_stage) {
-    const int ne = min(ns, (pos + a.chunk) / a.chunk);  // splits holding keys
-    csync();
-    if (threadIdx.x == 0) {
-      __threadfence();
-      const unsigned prev = atomicAdd(a.attn_cnt + g, 1u);
-      s_tok[1] = prev == (unsigned)(ne - 1);  // this task is the last of KV head g
+  // merge: this task takes heads h = s, s + ne, ... of KV head g, one warp
+  // each; every split's words of a round in flight at once
+  const int ne = min(ns, (pos + a.chunk) / a.chunk);  // splits holding keys
+  bool ok = true;
+  for (int h = s + ne * warp; h < G && ok; h += ne * kNCW) {
+    float M = -INFINITY, Lp = 0.0f, f = 0.0f;
+    if (ne <= 32) {  // every split's (max, sum) in one round, lane q holding split q
+      uint64_t wm = (uint64_t)e << 32, wl = (uint64_t)e << 32;
+      if (lane < ne) ok = poll2(a, part_words(a, g, lane, h) + kD, e, wm, wl);
+      ok = __all_sync(0xffffffffu, ok);
+      const float mq = lane < ne ? word_val(wm) : -INFINITY;
+      M = warp_max(mq);
+      f = mq == -INFINITY ? 0.0f : expf(mq - M);
+      if (lane < ne) Lp = word_val(wl) * f;
+    } else {  // more splits than lanes: the maxima first, then the factors per round
+      for (int q0 = 0; q0 < ne && ok; q0 += 32) {
+        uint64_t wm = (uint64_t)e << 32, wl = (uint64_t)e << 32;
+        if (q0 + lane < ne) ok = poll2(a, part_words(a, g, q0 + lane, h) + kD, e, wm, wl);
+        ok = __all_sync(0xffffffffu, ok);
+        M = fmaxf(M, warp_max(q0 + lane < ne ? word_val(wm) : -INFINITY));
+      }
     }
-    csync();
-    if (s_tok[1]) {
-      __threadfence();
-      if (warp < G) merge_head_global(a, g, warp, ne, lane, a.attn + ((size_t)g * G + warp) * kD);
-      if (threadIdx.x == 0) a.attn_cnt[g] = 0u;
+    if (!ok) break;
+    float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+    constexpr int kB = 4;  // splits per round of o loads
+    for (int q0 = 0; q0 < ne && ok; q0 += 32) {
+      if (ne > 32) {
+        uint64_t wm = (uint64_t)e << 32, wl = (uint64_t)e << 32;
+        if (q0 + lane < ne) ok = poll2(a, part_words(a, g, q0 + lane, h) + kD, e, wm, wl);
+        ok = __all_sync(0xffffffffu, ok);
+        const float mq = q0 + lane < ne ? word_val(wm) : -INFINITY;
+        f = mq == -INFINITY ? 0.0f : expf(mq - M);
+        if (q0 + lane < ne) Lp = fmaf(word_val(wl), f, Lp);
+      }
+      const int nr = min(32, ne - q0);
+      for (int u0 = 0; u0 < nr && ok; u0 += kB) {
+        uint64_t o[kB][4];
+#pragma unroll
+        for (int u = 0; u < kB; ++u) {
+          const uint64_t* po = part_words(a, g, q0 + u0 + u, h) + 4 * lane;
+          if (u0 + u < nr) {
+            get_words2(po, o[u][0], o[u][1]);
+            get_words2(po + 2, o[u][2], o[u][3]);
+          } else {
+            o[u][0] = o[u][1] = o[u][2] = o[u][3] = (uint64_t)e << 32;
+          }
+        }
+        const uint64_t t0 = global_ns();
+        for (uint32_t it = 1;; ++it) {
+          bool stale = false;
+#pragma unroll
+          for (int u = 0; u < kB; ++u) {
+            const uint64_t* po = part_words(a, g, q0 + u0 + u, h) + 4 * lane;
+            if (word_epoch(o[u][0]) != e || word_epoch(o[u][1]) != e) {
+              stale = true;
+              get_words2(po, o[u][0], o[u][1]);
+            }
+            if (word_epoch(o[u][2]) != e || word_epoch(o[u][3]) != e) {
+              stale = true;
+              get_words2(po + 2, o[u][2], o[u][3]);
+            }
+          }
+          if (!stale) break;
+          if ((it & 31u) == 0 && poll_failed(a, t0)) {
+            ok = false;
+            break;
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < kB; ++u) {
+          const float fu = __shfl_sync(0xffffffffu, f, (u0 + u) & 31);
+          if (u0 + u < nr) {
+            O.x = fmaf(word_val(o[u][0]), fu, O.x);
+            O.y = fmaf(word_val(o[u][1]), fu, O.y);
+            O.z = fmaf(word_val(o[u][2]), fu, O.z);
+            O.w = fmaf(word_val(o[u][3]), fu, O.w);
+          }
+        }
+        ok = __all_sync(0xffffffffu, ok);
+      }
     }
+    if (!ok) break;
+    const float L = warp_sum(Lp);
+    uint64_t* out = a.w_attn + ((size_t)g * G + h) * kD + 4 * lane;
+    put_words2(out, word(__fdiv_rn(O.x, L), e), word(__fdiv_rn(O.y, L), e));
+    put_words2(out + 2, word(__fdiv_rn(O.z, L), e), word(__fdiv_rn(O.w, L), e));
   }
+  csync();
+  return !s_abort;
 }
 
 // ---------------------------------------------------------------- head
-// This CTA's first maximum goes to the candidates; after the barrier every
-// CTA takes the first maximum over all candidates (the (value desc, index
-// asc) order is total, so the order of comparisons does not matter).
-MYOS_DEV void head_candidate(const StreamArgs& a, Best best) {
+// This CTA's first maximum goes to the candidate words; every CTA then takes
+// the first maximum over all candidates (the (value desc, index asc) order
+// is total, so the order of comparisons does not matter).
+MYOS_DEV void head_candidate(const StreamArgs& a, Best best, uint32_t e) {
   for (int o = 16; o > 0; o >>= 1) {
     const float ov = __shfl_xor_sync(0xffffffffu, best.v, o);
     const uint32_t oi = __shfl_xor_sync(0xffffffffu, best.i, o);
@@ -942,21 +936,23 @@ MYOS_DEV void head_candidate(const StreamArgs& a, Best best) {
         v = s_wbv[w];
         i = s_wbi[w];
       }
-    a.cand_val[blockIdx.x] = v;
-    a.cand_idx[blockIdx.x] = i;
+    put_words2(a.w_cand + 2 * blockIdx.x, word(v, e), word(__uint_as_float(i), e));
   }
 }
 
-// The greedy token (0 when no logit qualifies).
-MYOS_DEV uint32_t head_pick(const StreamArgs& a) {
+// The greedy token (0 when no logit qualifies); false when a poll gave up.
+MYOS_DEV bool head_pick(const StreamArgs& a, uint32_t e, uint32_t& tok) {
   if (threadIdx.x < 32) {
     const int lane = threadIdx.x;
     float v = -INFINITY;
     uint32_t i = 0xffffffffu;
-    for (int q = lane; q < a.grid; q += 32) {
-      const float pv = __ldcg(a.cand_val + q);
-      const uint32_t pi = __ldcg(a.cand_idx + q);
-      if (better(pv, pi, v, i)) {
+    bool ok = true;
+    for (int q = lane; q < a.grid && ok; q += 32) {
+      uint64_t wv, wi;
+      ok = poll2(a, a.w_cand + 2 * q, e, wv, wi);
+      const float pv = word_val(wv);
+      const uint32_t pi = (uint32_t)wi;
+      if (ok && better(pv, pi, v, i)) {
         v = pv;
         i = pi;
       }
@@ -969,12 +965,12 @@ MYOS_DEV uint32_t head_pick(const StreamArgs& a) {
         i = oi;
       }
     }
-    if (lane == 0) s_tok[0] = i == 0xffffffffu ? 0u : i;
+    if (lane == 0) s_tok = i == 0xffffffffu ? 0u : i;
   }
   csync();
-  const uint32_t tok = s_tok[0];
+  tok = s_tok;
   csync();  // s_tok is rewritten by the next head
-  return tok;
+  return !s_abort;
 }
 
 // ---------------------------------------------------------------- consumers
@@ -982,7 +978,7 @@ template <typename KT>
 MYOS_DEV void consumers(const StreamArgs& a) {
   const uint32_t pos0 = a.ctl->pos, step0 = a.ctl->step;
   uint32_t argmax = a.ctl->argmax;
-  uint32_t nbar = __ldcg(a.flags + blockIdx.x);  // barriers this CTA arrived at so far
+  uint32_t ph = a.flags[blockIdx.x];  // phases this CTA has run (epoch of the last one)
   uint32_t seq = 0;
   const bool attn_cta = (int)blockIdx.x < a.Hkv * a.nsplit;
   uint32_t fed = 0;
@@ -997,89 +993,84 @@ MYOS_DEV void consumers(const StreamArgs& a) {
       // ---- QKV: RMSNorm(ln1) of the residual (layer 0: the token's embedding row)
       {
         uint64_t* tr = trace_row(a, t, 5 * l);
+        const uint32_t e_in = ph;  // the last down phase (layer 0: none)
+        ++ph;
         gamma_issue(scr(a) + a.H, layer(a, l).ln1, a.H);
-        {  // bias rows: depend on nothing, loaded before the barrier
+        {  // bias rows: depend on nothing
           int q0, q1;
           rows_of(a.qd + 2 * a.kvd, a.grid, &q0, &q1);
           for (int i = threadIdx.x; i < q1 - q0; i += kCT)
             biasrows(a)[i] = __ldg(layer(a, l).bqkv + q0 + i);
         }
-        if (t > 0 || l > 0) {
-          if (!wait_all(a, nbar)) return;
-        } else {
-          csync();
-        }
         mark(tr, 0);
         // the raw rows hr0..hr1 are the residual the o_proj epilogue adds to
-        stage(scr(a), a.H, a.resid, l == 0 ? a.embed + (size_t)tok * a.H : nullptr, true, a.eps,
-              (l == 0 && blockIdx.x == 0) ? a.resid : nullptr, resrows(a), hr0, hr1, tr);
+        if (!stage(a, scr(a), a.H, a.w_resid, e_in, l == 0 ? a.embed + (size_t)tok * a.H : nullptr,
+                   true, resrows(a), hr0, hr1, tr))
+          return;
         mark(tr, 1);
-        if (!consume_gemv<SK_QKV>(a, l, seq, best)) return;
+        if (!consume_gemv<SK_QKV>(a, l, seq, best, ph)) return;
         mark(tr, 2);
-        arrive(a, ++nbar, tr);
       }
       // ---- attention
+      const uint32_t e_qkv = ph;
+      ++ph;
       if (attn_cta) {
         uint64_t* tr = trace_row(a, t, 5 * l + 1);
-        attn_prefetch<KT>(a, l, pos);
-        if (!wait_all(a, nbar)) return;
         mark(tr, 0);
-        attn_task<KT>(a, l, pos);
+        if (!attn_task<KT>(a, l, pos, e_qkv, ph)) return;
         mark(tr, 2);
       }
-      arrive(a, ++nbar);
       // ---- o_proj: residual += W_o . attention output
       {
         uint64_t* tr = trace_row(a, t, 5 * l + 2);
-        if (!wait_all(a, nbar)) return;
+        const uint32_t e_in = ph;
+        ++ph;
         mark(tr, 0);
-        if (a.merge_in_stage) stage_merge(a, scr(a), pos);
-        else stage(scr(a), a.qd, a.attn, nullptr, false, 0.f, nullptr, nullptr, 0, 0, tr);
+        if (!stage(a, scr(a), a.qd, a.w_attn, e_in, nullptr, false, nullptr, 0, 0, tr)) return;
         mark(tr, 1);
-        if (!consume_gemv<SK_O>(a, l, seq, best)) return;
+        if (!consume_gemv<SK_O>(a, l, seq, best, ph)) return;
         mark(tr, 2);
-        arrive(a, ++nbar, tr);
       }
       // ---- gate/up: RMSNorm(ln2), SiLU(gate) * up
       {
         uint64_t* tr = trace_row(a, t, 5 * l + 3);
+        const uint32_t e_in = ph;
+        ++ph;
         gamma_issue(scr(a) + a.H, layer(a, l).ln2, a.H);
-        if (!wait_all(a, nbar)) return;
         mark(tr, 0);
         // the raw rows hr0..hr1 (after o_proj) are the residual of the down epilogue
-        stage(scr(a), a.H, a.resid, nullptr, true, a.eps, nullptr, resrows(a), hr0, hr1, tr);
+        if (!stage(a, scr(a), a.H, a.w_resid, e_in, nullptr, true, resrows(a), hr0, hr1, tr)) return;
         mark(tr, 1);
-        if (!consume_gemv<SK_GU>(a, l, seq, best)) return;
+        if (!consume_gemv<SK_GU>(a, l, seq, best, ph)) return;
         mark(tr, 2);
-        arrive(a, ++nbar, tr);
       }
       // ---- down: residual += W_down . act
       {
         uint64_t* tr = trace_row(a, t, 5 * l + 4);
-        if (!wait_all(a, nbar)) return;
+        const uint32_t e_in = ph;
+        ++ph;
         mark(tr, 0);
-        stage(scr(a), a.I, a.act, nullptr, false, 0.f, nullptr, nullptr, 0, 0, tr);
+        if (!stage(a, scr(a), a.I, a.w_act, e_in, nullptr, false, nullptr, 0, 0, tr)) return;
         mark(tr, 1);
-        if (!consume_gemv<SK_DOWN>(a, l, seq, best)) return;
+        if (!consume_gemv<SK_DOWN>(a, l, seq, best, ph)) return;
         mark(tr, 2);
-        arrive(a, ++nbar, tr);
       }
     }
     // ---- head: final RMSNorm, logits, first maximum over the vocabulary
     if (a.head) {
       uint64_t* tr = trace_row(a, t, 5 * a.L);
       Best best = {-INFINITY, 0xffffffffu};
+      const uint32_t e_in = ph;
+      ++ph;
       gamma_issue(scr(a) + a.H, a.final_norm, a.H);
-      if (!wait_all(a, nbar)) return;
       mark(tr, 0);
-      stage(scr(a), a.H, a.resid, nullptr, true, a.eps, nullptr, nullptr, 0, 0, tr);
+      if (!stage(a, scr(a), a.H, a.w_resid, e_in, nullptr, true, nullptr, 0, 0, tr)) return;
       mark(tr, 1);
-      if (!consume_gemv<SK_HEAD>(a, 0, seq, best)) return;
-      head_candidate(a, best);
+      if (!consume_gemv<SK_HEAD>(a, 0, seq, best, ph)) return;
+      head_candidate(a, best, ph);
       mark(tr, 2);
-      arrive(a, ++nbar, tr);
-      if (!wait_all(a, nbar)) return;
-      const uint32_t next = head_pick(a);
+      uint32_t next;
+      if (!head_pick(a, ph, next)) return;
       if (blockIdx.x == 0 && threadIdx.x == 0) {
         if (a.rec_fed) a.rec_fed[step0 + t] = tok;
         if (a.rec_argmax) a.rec_argmax[step0 + t] = argmax;
@@ -1087,8 +1078,8 @@ MYOS_DEV void consumers(const StreamArgs& a) {
       argmax = next;
     }
   }
-  // this CTA's barrier count for the next launch; cursor and greedy state
-  if (threadIdx.x == 0) a.flags[blockIdx.x] = nbar;
+  // this CTA's phase count for the next launch; cursor and greedy state
+  if (threadIdx.x == 0) a.flags[blockIdx.x] = ph;
   if (blockIdx.x == 0 && threadIdx.x == 0) {
     StepCtl* c = a.ctl;
     c->fed = fed;
@@ -1107,7 +1098,7 @@ __global__ void __launch_bounds__(kST, 1) k_step_stream(const __grid_constant__ 
     }
     mbar_fence_init();
     s_abort = 0;
-    s_tok[0] = s_tok[1] = 0u;
+    s_tok = 0u;
   }
   StreamLayer* lt = reinterpret_cast<StreamLayer*>(smem_base() + a.off_lay);
   for (int i = threadIdx.x; i < a.L; i += kST) lt[i] = a.layers[i];
@@ -1127,22 +1118,33 @@ size_t stream_smem_bytes(const StreamArgs& a) {
   return (size_t)a.off_lay + (size_t)a.L * sizeof(StreamLayer);
 }
 
+size_t stream_word_count(const StreamArgs& a) {
+  return (size_t)a.H + (size_t)(a.qd + 2 * a.kvd) + (size_t)a.Hkv * a.nsplit * a.G * (kD + 2) +
+         (size_t)a.qd + (size_t)a.I + 2 * (size_t)a.grid;
+}
+
+void stream_set_words(StreamArgs* a, uint64_t* base) {
+  a->w_resid = base;
+  a->w_qkv = a->w_resid + a->H;
+  a->w_part = a->w_qkv + (a->qd + 2 * a->kvd);
+  a->w_attn = a->w_part + (size_t)a->Hkv * a->nsplit * a->G * (kD + 2);
+  a->w_act = a->w_attn + a->qd;
+  a->w_cand = a->w_act + a->I;
+}
+
 cudaError_t stream_configure(StreamArgs* a, int max_smem) {
   if (a->d != kD || a->G > kGMax || a->G < 1 || a->H % 256 || a->qd % 256 || a->I % 256 ||
       a->L > kMaxLayers || a->grid < 1 || a->grid > kCT || a->Hkv * a->nsplit > a->grid ||
-      a->Hq > kCT)
+      a->Hq > kCT || a->kvd % 256)
     return cudaErrorNotSupported;
   const size_t kv = a->kv_bf16 ? 2 : 4;
   // scratch: the largest staged input (with gamma and the bf16 embedding row
-  // after a hidden-width one), the attention tiles, the o_proj merge
+  // after a hidden-width one), the attention tiles
   a->tile = 32;
   const size_t ds_bytes = kD * kv + 16;
   const size_t attn = (size_t)a->G * kD * 4 + 2 * (size_t)a->tile * ds_bytes + 3 * kD * 4;
   const size_t x = std::max((size_t)std::max(a->qd, a->I) * 4, (size_t)a->H * 10);
-  const size_t merge = (size_t)a->qd * 4 + (size_t)a->Hkv * a->nsplit * a->G * (kD + 2) * 4 +
-                       (size_t)a->Hq * 4;
   size_t scr = std::max(x, attn);
-  if (a->merge_in_stage) scr = std::max(scr, merge);
   scr = (scr + 1023) / 1024 * 1024;
   // rows per slot for each matrix kind, then the split of rows over warps
   const int Ks[5] = {a->H, a->qd, a->H, a->I, a->H};
@@ -1162,8 +1164,6 @@ cudaError_t stream_configure(StreamArgs* a, int max_smem) {
     int r = (int)(slot / ((size_t)Ks[k] * 2 * NRs[k]));
     if (r > kNCW) r = kNCW;
     const int wpr = std::max(1, kNCW / r);
-    // every lane holds at most kXMax input chunks of its part of a row
-    if ((Ks[k] / 8 + wpr - 1) / wpr > 32 * kXMax) return cudaErrorNotSupported;
     a->rps[k] = r;
     a->wpr[k] = wpr;
     if (wpr > 1) prt = std::max(prt, ((Ms[k] + a->grid - 1) / a->grid) * wpr * NRs[k]);

@@ -44,15 +44,12 @@ struct StreamArgs {
   const float *cos_t, *sin_t;  // [S][d/2], host-built with libm
   // split-KV attention: tasks (KV head, split) on CTAs 0..Hkv*nsplit-1
   int nsplit, chunk, tile;
-  int merge_in_stage;         // 1: the o_proj staging merges the splits
-  float *part_o, *part_m, *part_l;
-  unsigned* attn_cnt;         // [Hkv] last-arriver merge counters, zero between launches
-  // head: per-CTA first-maximum candidates
-  float* cand_val;
-  uint32_t* cand_idx;
-  // grid-wide barrier: bar = arrivals of every CTA (monotonic, 64-bit),
-  // flags[b] = barriers CTA b had arrived at when its last launch ended
-  unsigned long long* bar;
+  // phase hand-over words (value bits, epoch): residual [H], q|k|v [qd+2kvd],
+  // split partials [Hkv][nsplit][G][d+2], attention output [qd], activations
+  // [I], head candidates [grid][2]; one allocation of stream_word_count
+  // words, zeroed before first use and after a failed launch
+  uint64_t *w_resid, *w_qkv, *w_part, *w_attn, *w_act, *w_cand;
+  // flags[b] = phases CTA b had run when its last launch ended (the epoch base)
   unsigned* flags;
   // geometry (stream_configure)
   int grid, ns, slot_bytes, scr_bytes, part_floats;
@@ -70,6 +67,9 @@ struct StreamArgs {
 // rps, wpr, tile) from the shape fields; fails when the layout does not fit
 // max_smem bytes of shared memory.
 cudaError_t stream_configure(StreamArgs* a, int max_smem);
+// Words of the hand-over buffers, and their layout from one base pointer.
+size_t stream_word_count(const StreamArgs& a);
+void stream_set_words(StreamArgs* a, uint64_t* base);
 size_t stream_smem_bytes(const StreamArgs& a);
 int stream_threads();
 cudaError_t launch_step_stream(const StreamArgs& a, cudaStream_t st);
