@@ -49,6 +49,14 @@ MYOS_DEV void prefetch_l2(const void* p, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
+// Prefetch a byte range from one thread, in <=64 KiB pieces.
+MYOS_DEV void prefetch_range_1(const void* base, size_t bytes) {
+  uintptr_t a = (uintptr_t)base;
+  uintptr_t p = (a + 15) & ~(uintptr_t)15;
+  const uintptr_t end = (a + bytes) & ~(uintptr_t)15;
+  for (; p < end; p += 65536) prefetch_l2((const void*)p, (uint32_t)(end - p < 65536 ? end - p : 65536));
+}
+
 // Prefetch a byte range split into <=64 KiB pieces across the block's threads.
 MYOS_DEV void prefetch_range(const void* base, size_t bytes) {
   uintptr_t a = (uintptr_t)base;

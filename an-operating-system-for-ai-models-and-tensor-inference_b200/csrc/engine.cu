@@ -99,6 +99,13 @@ struct myos_ctx {
   int l2pf_mode = 0;    // MYOS_L2PF: qkv kernels prefetch the layer's MLP weights into L2
   int l2pf_mask = 7;    // MYOS_L2PF_MASK: which of them (1 gate, 2 up, 4 down)
   int attn_cluster = 0; // attention splits merge across a thread-block cluster
+  // fused MLP (k_mlp: gate|up, SwiGLU and down_proj in one launch per layer)
+  // when the shape allows and MYOS_MLP is not 0; grid 0 keeps the two GEMVs
+  int grid_mlp = 0;
+  float* mlp_part = nullptr;                  // [hidden][grid_mlp] down_proj shares
+  unsigned long long* mlp_arrive = nullptr;   // grid-wide arrival count
+  uint16_t* mlp_wd = nullptr;  // [L][grid_mlp][hidden][64] down_proj by block (null: in place)
+  int mlp_pf_rows = 0;  // MYOS_MLP_PF (default 32): gate/up rows per MLP block that o_proj pulls into L2
   // GEMM prefill (chunks of pf_chunk prompt tokens through the tensor cores)
   bool pf_ok = false;
   int pf_chunk = 0;
@@ -402,6 +409,7 @@ int launch_kind(myos_ctx* c, int kind, int l, const uint32_t* feed, bool pdl, bo
     at.defer_merge = c->defer_merge;
     at.cluster = c->attn_cluster;
     at.tr = ktrace_at(c, 5 * l + K_ATTN);
+
     CK(launch_attention(at, kv_bf16, c->st, pdl));
   } else if (kind == K_O) {
     GemvArgs o = {};
@@ -424,9 +432,37 @@ int launch_kind(myos_ctx* c, int kind, int l, const uint32_t* feed, bool pdl, bo
     o.prefetch_cap = prefetch_cap(c, c->grid_o);
     o.tr = ktrace_at(c, 5 * l + K_O);
     o.warps = c->warps_o;
+    if (c->grid_mlp && c->mlp_pf_rows > 0) {  // the first gate/up rows of every MLP block
+      o.pf_ptr[0] = w.wg;
+      o.pf_ptr[1] = w.wu;
+      o.pf_bytes[0] = (size_t)c->mlp_pf_rows * H * 2;
+      o.pf_stride = (size_t)kMlpSlice * H * 2;
+      o.pf_n = c->grid_mlp;
+      o.pf_mode = 3;
+    }
     tp_partial(c, &o, K_O);
     CK(launch_gemv(EPI_RESID, o, c->grid_o, c->st, pdl));
     if (int st = tp_sum_resid(c, K_O)) return st;
+  } else if (kind == K_GU && c->grid_mlp) {
+    MlpArgs m = {};
+    m.wg = w.wg;
+    m.wu = w.wu;
+    m.wd = w.wd;
+    m.wd_slices = c->mlp_wd ? c->mlp_wd + (size_t)l * H * I : nullptr;
+    m.gamma = w.ln2;
+    m.eps = s.rms_eps;
+    m.H = H;
+    m.I = I;
+    m.resid = c->resid;
+    m.part = c->mlp_part;
+    m.arrive = c->mlp_arrive;
+    m.ctl = c->ctl;
+    m.err = &c->ctl->err;
+    m.wait_ns = 1000000000ull;
+    m.tr = ktrace_at(c, 5 * l + K_GU);
+    CK(launch_mlp(m, c->grid_mlp, c->st, pdl));
+  } else if (kind == K_DOWN && c->grid_mlp) {
+    // part of the fused MLP launch
   } else if (kind == K_GU) {
     GemvArgs gu = {};
     gu.w = w.wg;
@@ -483,8 +519,10 @@ double kind_bytes(const myos_ctx* c, int kind) {
     case K_ATTN: return 2.0 * s.num_kv_heads * (double)(c->len + 1) * s.head_dim * kv_elt +
                         (qd + 2 * kvd) * 4 + qd * 4;
     case K_O: return H * qd * 2 + qd * 4 + H * 8;
-    case K_GU: return 2 * I * H * 2 + H * 8 + I * 4;
-    case K_DOWN: return H * I * 2 + I * 4 + H * 8;
+    case K_GU:  // the fused MLP: gate, up and down weights, the residual read and written
+      if (c->grid_mlp) return 3 * I * H * 2 + H * 8;
+      return 2 * I * H * 2 + H * 8 + I * 4;
+    case K_DOWN: return c->grid_mlp ? 0 : H * I * 2 + I * 4 + H * 8;
     case K_HEAD: return V * H * 2 + H * 8 + V * 4;
   }
   return 0;
@@ -608,6 +646,8 @@ int finish(myos_ctx* c) {
     // an abandoned streaming launch leaves its phase counts and words
     // partway: start the next launch from zero (no stale word can then
     // carry an epoch a later phase expects)
+    // an arrival count left partway would misplace the next MLP launch's target
+    if (c->mlp_arrive) cudaMemset(c->mlp_arrive, 0, sizeof(unsigned long long));
     if (c->sflags) {
       cudaMemset(c->sflags, 0, (size_t)c->sargs.grid * sizeof(unsigned));
       cudaMemset(c->s_words, 0, c->s_words_bytes);
@@ -899,6 +939,20 @@ static int create_impl(myos_ctx* c, const myos_shape* shape, const myos_opts* op
   CK(cudaMalloc(&c->part_l, (size_t)s.num_kv_heads * nsplit * c->G * 4));
   CK(cudaMalloc(&c->counters, (1 + s.num_kv_heads) * 4));
   CK(cudaMemset(c->counters, 0, (1 + s.num_kv_heads) * 4));
+  {
+    const char* e = getenv("MYOS_MLP");
+    if (c->tp_size == 1 && !(e && e[0] == '0')) c->grid_mlp = mlp_grid((int)H, (int)I, c->num_sms);
+    if (c->grid_mlp) {
+      CK(cudaMalloc(&c->mlp_part, (size_t)H * c->grid_mlp * 4));
+      CK(cudaMalloc(&c->mlp_arrive, sizeof(unsigned long long)));
+      CK(cudaMemset(c->mlp_arrive, 0, sizeof(unsigned long long)));
+      // a second copy of down_proj, by block (MYOS_MLP=i reads it in place)
+      if (!(e && e[0] == 'i')) CK(cudaMalloc(&c->mlp_wd, (size_t)L * H * I * 2));
+      const char* pe = getenv("MYOS_MLP_PF");
+      c->mlp_pf_rows = pe ? atoi(pe) : 32;
+      if (c->mlp_pf_rows < 0 || c->mlp_pf_rows > kMlpSlice) c->mlp_pf_rows = 0;
+    }
+  }
   CK(cudaMalloc(&c->ctl, sizeof(StepCtl)));
   CK(cudaMemset(c->ctl, 0, sizeof(StepCtl)));
   CK(cudaMalloc(&c->feed, (S + 1) * 4));
@@ -1176,7 +1230,7 @@ void myos_ctx_destroy(myos_ctx* c) {
   void* dev[] = {c->warena, c->kcache, c->vcache, c->resid, c->qkv, c->attn, c->act, c->logits,
                  c->part_val, c->part_idx, c->part_o, c->part_m, c->part_l, c->counters, c->ctl,
                  c->feed, c->rec_fed, c->rec_argmax, c->cos_t, c->sin_t, c->d_slayers, c->sflags,
-                 c->s_words, (void*)c->trace, (void*)c->strace,
+                 c->s_words, (void*)c->trace, (void*)c->strace, c->mlp_part, c->mlp_arrive, c->mlp_wd,
                  (void*)c->ktrace, c->pf_X, c->pf_D, c->pf_Q, c->pf_att, c->pf_A, c->pf_ws,
                  c->bt_k, c->bt_v, c->bt_X, c->bt_D, c->bt_pos, c->bt_rows, c->bt_tok,
                  c->bt_out, c->bt_ids, c->bt_feed, c->tp_part, c->tp_cand, c->tp_link};
@@ -1290,7 +1344,11 @@ int myos_load_tensor(myos_ctx* c, const char* name, int32_t dtype, const int64_t
       case 8: st = stage_bf16_as_f32(c, w.ln2, bytes, H); break;
       case 9: st = rows(w.wg, rk * Ic, Ic, H); break;
       case 10: st = rows(w.wu, rk * Ic, Ic, H); break;
-      case 11: st = cols(w.wd, H, I, rk * Ic, Ic, Il); break;
+      case 11:
+        st = cols(w.wd, H, I, rk * Ic, Ic, Il);
+        if (!st && c->mlp_wd)  // the fused MLP's copy, by block
+          CK(launch_mlp_relayout(w.wd, c->mlp_wd + (size_t)layer * H * I, (int)H, (int)I, c->copy_st));
+        break;
     }
   }
   if (st) return st;
@@ -1445,6 +1503,11 @@ int myos_profile_kernels(myos_ctx* c, int iters, float* ms_out, double* bytes_ou
   const int L = (int)c->s.num_layers;
   c->profiling = true;
   for (int kind = K_QKV; kind <= K_HEAD; ++kind) {
+    if (kind == K_DOWN && c->grid_mlp) {  // runs inside the fused MLP (timed as gate_up)
+      ms_out[kind] = 0.f;
+      if (bytes_out) bytes_out[kind] = 0.0;
+      continue;
+    }
     // one untimed pass to warm instruction caches and the launch path
     for (int l = 0; l < L; ++l)
       if ((st = launch_kind(c, kind, l, nullptr, false, false))) break;

@@ -164,7 +164,7 @@ MYOS_DEV void gamma_preload(const GemvInput& in, int K, float4 (&g0)[NG], float4
   }
 }
 
-template <int NG>
+template <int NG, int NS = kStageOne>
 MYOS_DEV void stage_one_trip(float* xs, int K, const GemvInput& in, float* red, bool has_g,
                              const float4 (&g0)[NG], const float4 (&g1)[NG]) {
   const int nt = blockDim.x, nchunk = K >> 3, half = K >> 1;
@@ -176,9 +176,9 @@ MYOS_DEV void stage_one_trip(float* xs, int K, const GemvInput& in, float* red, 
     erow = in.embed + (size_t)tok * (size_t)K;
     if (blockIdx.x == 0 && threadIdx.x == 0) in.ctl->fed = tok;
   }
-  float4 lo[kStageOne], hi[kStageOne];
+  float4 lo[NS], hi[NS];
 #pragma unroll
-  for (int i = 0; i < kStageOne; ++i) {
+  for (int i = 0; i < NS; ++i) {
     const int c = threadIdx.x + i * nt;
     if (c < nchunk) {
       if (erow) {
@@ -191,7 +191,7 @@ MYOS_DEV void stage_one_trip(float* xs, int K, const GemvInput& in, float* red, 
   }
   if (erow && in.x_store && blockIdx.x == 0) {  // block 0 also stores the embedding row
 #pragma unroll
-    for (int i = 0; i < kStageOne; ++i) {
+    for (int i = 0; i < NS; ++i) {
       const int c = threadIdx.x + i * nt;
       if (c < nchunk) {
         reinterpret_cast<float4*>(in.x_store)[2 * c] = lo[i];
@@ -202,7 +202,7 @@ MYOS_DEV void stage_one_trip(float* xs, int K, const GemvInput& in, float* red, 
   if (has_g) {
     float ss = 0.0f;
 #pragma unroll
-    for (int i = 0; i < kStageOne; ++i) {
+    for (int i = 0; i < NS; ++i) {
       if (threadIdx.x + i * nt < nchunk) {
         ss = fmaf(lo[i].x, lo[i].x, ss);
         ss = fmaf(lo[i].y, lo[i].y, ss);
@@ -226,7 +226,7 @@ MYOS_DEV void stage_one_trip(float* xs, int K, const GemvInput& in, float* red, 
     }
   }
 #pragma unroll
-  for (int i = 0; i < kStageOne; ++i) {
+  for (int i = 0; i < NS; ++i) {
     const int c = threadIdx.x + i * nt;
     if (c < nchunk) {
       xlo[c] = lo[i];
@@ -544,6 +544,13 @@ __global__ void __launch_bounds__(kThreads) k_gemv(GemvArgs a) {
 // overlaps the predecessor kernel and the input staging.
 // This block's slice of each range in a.pf_ptr, requested into L2.
 MYOS_DEV void l2_prefetch_slices(const GemvArgs& a) {
+  if (a.pf_mode == 3) {
+    const int nr = 2 * a.pf_n;
+    for (int r = blockIdx.x + gridDim.x * threadIdx.x; r < nr; r += gridDim.x * blockDim.x)
+      prefetch_range_1(static_cast<const char*>(a.pf_ptr[r / a.pf_n]) + (size_t)(r % a.pf_n) * a.pf_stride,
+                       a.pf_bytes[0]);
+    return;
+  }
   for (int r = 0; r < 3; ++r) {
     if (!a.pf_ptr[r]) continue;
     const size_t n = a.pf_bytes[r];
@@ -664,6 +671,195 @@ __global__ void __launch_bounds__(kThreads, 2) k_gemv_stream(GemvArgs a) {
     __syncthreads();
     trace_end(trow);
   }
+}
+
+// ------------------------------------------------------------------ fused MLP
+// One block per SM, 16 warps. A warp's work is a sequence of weight batches,
+// each 2P 16-byte chunks per lane, double-buffered in registers exactly as
+// in k_gemv_stream (the first batch is issued before the dependency wait):
+//   batches 0..3: one (gate, up) row pair each (row c0 + warp + 16 i); the
+//     lane-strided dot products and SiLU(gate)*up are those of the gate|up
+//     GEMV, so the activations are the same bits;
+//   then: down_proj rows in groups of four, eight lanes per row, each lane
+//     one 16-byte chunk of the block's 64 columns against the activations of
+//     those 8 columns (held in registers); the 8 lanes' products are summed
+//     by a fixed xor tree into part[row][b].
+// Reduction: after the grid-wide arrival, warp w of block b sums part[row][.]
+// for the rows [b H / grid, (b+1) H / grid) assigned to it, lane-strided in
+// block order then a fixed shuffle tree, and adds the sum to resid[row]
+// (the reference's x + mlp, qwen25_block.rs:287).
+constexpr int kMlpThreads = 512;
+constexpr int kMlpWarps = kMlpThreads / 32;
+constexpr int kMlpRowsPerWarp = kMlpSlice / kMlpWarps;  // gate|up rows per warp
+
+MYOS_DEV unsigned long long ld_acquire_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+template <int P>
+MYOS_DEV void mlp_load(uint4 (&buf)[2 * P], const MlpArgs& a, int c0, int bt, int warp, int lane,
+                       int gpw) {
+  constexpr int UB = 2 * P;
+  if (bt < kMlpRowsPerWarp) {
+    const size_t r = (size_t)(c0 + warp + kMlpWarps * bt);
+    const uint4* g = reinterpret_cast<const uint4*>(a.wg + r * a.H) + lane;
+    const uint4* u = reinterpret_cast<const uint4*>(a.wu + r * a.H) + lane;
+#pragma unroll
+    for (int i = 0; i < P; ++i) {
+      buf[i] = ld_stream(g + 32 * i);
+      buf[P + i] = ld_stream(u + 32 * i);
+    }
+  } else {
+    const int j = bt - kMlpRowsPerWarp;
+    // row r of the block's slice at base + r * ld (64 columns, 128 bytes)
+    const uint16_t* base = a.wd_slices ? a.wd_slices + (size_t)blockIdx.x * a.H * kMlpSlice : a.wd + c0;
+    const size_t ld = a.wd_slices ? (size_t)kMlpSlice : (size_t)a.I;
+#pragma unroll
+    for (int i = 0; i < UB; ++i) {
+      const int gi = j * UB + i;
+      const int row = 4 * (warp + kMlpWarps * gi) + (lane >> 3);
+      if (gi < gpw && row < a.H)
+        buf[i] = ld_stream(reinterpret_cast<const uint4*>(base + (size_t)row * ld) + (lane & 7));
+      else
+        buf[i] = make_uint4(0u, 0u, 0u, 0u);
+    }
+  }
+}
+
+__global__ void k_mlp_relayout(const uint4* wd, uint4* dst, int H, int I) {
+  const size_t per_blk = (size_t)H * (kMlpSlice / 8);  // 16-byte chunks of one slice
+  const size_t n = per_blk * (size_t)(I / kMlpSlice);
+  for (size_t t = blockIdx.x * (size_t)blockDim.x + threadIdx.x; t < n;
+       t += (size_t)gridDim.x * blockDim.x) {
+    const size_t blk = t / per_blk, rem = t - blk * per_blk;
+    const size_t row = rem / (kMlpSlice / 8), ch = rem - row * (kMlpSlice / 8);
+    dst[t] = wd[(row * (size_t)I + blk * kMlpSlice) / 8 + ch];
+  }
+}
+
+template <int P>
+__global__ void __launch_bounds__(kMlpThreads, 1) k_mlp(MlpArgs a) {
+  extern __shared__ float4 smem4[];
+  float* xs = reinterpret_cast<float*>(smem4);  // [H] normed input, split layout
+  __shared__ float red[33];
+  __shared__ __align__(16) float acts[kMlpSlice];
+  __shared__ int wait_failed;
+  constexpr int UB = 2 * P;
+  const int b = blockIdx.x, nblk = gridDim.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int H = a.H, c0 = b * kMlpSlice;
+  const int gpw = (H / 4 + kMlpWarps - 1) / kMlpWarps;  // down row groups per warp
+  const int nbt = kMlpRowsPerWarp + (gpw + UB - 1) / UB;
+
+  const uint64_t t_start = a.tr.buf ? global_ns() : 0;
+  GemvInput in = {};
+  in.x = a.resid;
+  in.ctl = a.ctl;
+  in.gamma = a.gamma;
+  in.eps = a.eps;
+  float4 g0[1], g1[1];  // H <= 8 * kMlpThreads: one chunk per thread
+  gamma_preload<1>(in, H, g0, g1);
+  uint4 cur[UB], nxt[UB];
+  mlp_load<P>(cur, a, c0, 0, warp, lane, gpw);
+  if (threadIdx.x == 0) wait_failed = 0;
+  pdl_wait();
+  pdl_launch();
+  uint64_t* trow = trace_begin(a.tr, a.ctl, t_start);
+  stage_one_trip<1, 1>(xs, H, in, red, true, g0, g1);
+  trace_mark(trow, 3);  // input staged
+
+  const float4* xlo = reinterpret_cast<const float4*>(xs);
+  const float4* xhi = reinterpret_cast<const float4*>(xs + (H >> 1));
+  float4 alo = make_float4(0.f, 0.f, 0.f, 0.f), ahi = alo;
+  for (int bt = 0; bt < nbt; ++bt) {
+    if (bt + 1 < nbt) mlp_load<P>(nxt, a, c0, bt + 1, warp, lane, gpw);
+    if (bt < kMlpRowsPerWarp) {
+      float g = 0.0f, u = 0.0f;
+#pragma unroll
+      for (int i = 0; i < P; ++i) {
+        const float4 lo = xlo[lane + 32 * i], hi = xhi[lane + 32 * i];
+        g = dot8(cur[i], lo, hi, g);
+        u = dot8(cur[P + i], lo, hi, u);
+      }
+      g = warp_sum(g);
+      u = warp_sum(u);
+      if (lane == 0) acts[warp + kMlpWarps * bt] = silu_mul(g, u);
+      if (bt == kMlpRowsPerWarp - 1) {  // every warp: all activations of the block
+        __syncthreads();
+        alo = reinterpret_cast<const float4*>(acts)[2 * (lane & 7)];
+        ahi = reinterpret_cast<const float4*>(acts)[2 * (lane & 7) + 1];
+        trace_mark(trow, 4);  // activations done
+      }
+    } else {
+      const int j = bt - kMlpRowsPerWarp;
+#pragma unroll
+      for (int i = 0; i < UB; ++i) {
+        float v = dot8(cur[i], alo, ahi, 0.0f);
+        v += __shfl_xor_sync(0xffffffffu, v, 1);
+        v += __shfl_xor_sync(0xffffffffu, v, 2);
+        v += __shfl_xor_sync(0xffffffffu, v, 4);
+        const int gi = j * UB + i;
+        const int row = 4 * (warp + kMlpWarps * gi) + (lane >> 3);
+        if ((lane & 7) == 0 && gi < gpw && row < H) a.part[(size_t)row * nblk + b] = v;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < UB; ++i) cur[i] = nxt[i];
+  }
+
+  // this warp's first output row: its residual does not change until the
+  // sums below, so read it while the other blocks finish
+  const int q0 = (int)((long long)b * H / nblk), q1 = (int)((long long)(b + 1) * H / nblk);
+  const float res0 = (lane == 0 && q0 + warp < q1) ? __ldcg(a.resid + q0 + warp) : 0.0f;
+  // grid-wide arrival: every block's shares written before any block sums
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const unsigned long long old = atomicAdd(a.arrive, 1ull);
+    const unsigned long long target = (old / (unsigned long long)nblk + 1ull) * (unsigned long long)nblk;
+    if (ld_acquire_u64(a.arrive) < target) {
+      const uint64_t t0 = global_ns();
+      for (uint32_t i = 1;; ++i) {
+        if (ld_acquire_u64(a.arrive) >= target) break;
+        if ((i & 63u) == 0 && global_ns() - t0 > a.wait_ns) {
+          atomicOr(a.err, kErrMlpWait);
+          wait_failed = 1;
+          break;
+        }
+      }
+    }
+    __threadfence();
+  }
+  __syncthreads();
+  trace_mark(trow, 5);  // all shares written
+  if (!wait_failed) {
+    for (int row = q0 + warp; row < q1; row += kMlpWarps) {
+      const float* pr = a.part + (size_t)row * nblk;
+      constexpr int kP = 8;  // nblk <= 256: every load of the lane in flight at once
+      float v[kP];
+#pragma unroll
+      for (int i = 0; i < kP; ++i) v[i] = lane + 32 * i < nblk ? __ldcg(pr + lane + 32 * i) : 0.0f;
+      float s = 0.0f;
+#pragma unroll
+      for (int i = 0; i < kP; ++i) s += v[i];
+      s = warp_sum(s);
+      if (lane == 0) a.resid[row] = __fadd_rn(row == q0 + warp ? res0 : __ldcg(a.resid + row), s);
+    }
+  }
+  if (a.tr.buf) {  // block-uniform
+    __syncthreads();
+    trace_end(trow);
+  }
+}
+
+int mlp_grid(int H, int I, int num_sms) {
+  if (H != 1024 && H != 1280 && H != 1536) return 0;
+  if (I % kMlpSlice != 0) return 0;
+  const int g = I / kMlpSlice;
+  if (g > num_sms || g > 256 || 4 * g < 3 * num_sms) return 0;
+  return g;
 }
 
 // ------------------------------------------------------------------ attention
@@ -1725,6 +1921,26 @@ cudaError_t launch_gemv(int epi, const GemvArgs& a0, int grid, cudaStream_t st, 
     case EPI_ARGMAX: return cudaLaunchKernelEx(&cfg, k_gemv<EPI_ARGMAX>, a);
   }
   return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_mlp(const MlpArgs& a, int grid, cudaStream_t st, bool pdl) {
+  if (grid <= 0 || grid * kMlpSlice != a.I || a.H % 256 != 0 || !a.arrive || !a.err)
+    return cudaErrorInvalidValue;
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg =
+      make_cfg(dim3(grid), dim3(kMlpThreads), gemv_smem_bytes(a.H), st, pdl, attr);
+  switch (a.H / 256) {
+    case 4: return cudaLaunchKernelEx(&cfg, k_mlp<4>, a);
+    case 5: return cudaLaunchKernelEx(&cfg, k_mlp<5>, a);
+    case 6: return cudaLaunchKernelEx(&cfg, k_mlp<6>, a);
+  }
+  return cudaErrorInvalidValue;
+}
+
+cudaError_t launch_mlp_relayout(const uint16_t* wd, uint16_t* dst, int H, int I, cudaStream_t st) {
+  if (I % kMlpSlice != 0 || ((uintptr_t)wd & 15) || ((uintptr_t)dst & 15)) return cudaErrorInvalidValue;
+  k_mlp_relayout<<<1184, 256, 0, st>>>(reinterpret_cast<const uint4*>(wd), reinterpret_cast<uint4*>(dst), H, I);
+  return cudaGetLastError();
 }
 
 int attn_dpl(int d) { return d <= 32 ? 1 : d <= 64 ? 2 : d <= 128 ? 4 : 8; }

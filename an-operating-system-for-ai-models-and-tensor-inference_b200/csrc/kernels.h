@@ -91,10 +91,14 @@ struct GemvArgs {
   KTrace tr;
   // Weights of later kernels to pull into L2 while this one waits on its
   // inputs (each block takes an equal slice of each range); pf_mode 1: one
-  // prefetch per 128-byte line from every thread, 2: bulk prefetches.
+  // prefetch per 128-byte line from every thread, 2: bulk prefetches;
+  // 3: strided ranges, pf_ptr[m] + i * pf_stride of pf_bytes[0] bytes for
+  // m < 2 and i < pf_n, one bulk prefetch sequence per range.
   const void* pf_ptr[3];
   size_t pf_bytes[3];
   int pf_mode;
+  size_t pf_stride;
+  int pf_n;
   // Tensor parallel. EPI_RESID: y[row] = base + v with base = res[row] (res
   // set), y[row] (res null: in place), or 0 (res_zero: a partial sum for the
   // allreduce). EPI_ARGMAX with tp_cand: the block-reduced first maximum goes
@@ -143,6 +147,41 @@ struct AttnArgs {
 
 // Shared memory of the attention-merge staging beyond the staged input.
 size_t merge_smem_bytes(int Hq, int nsplit, int d);
+
+// Fused MLP of one decode layer (qwen25_block.rs:250-287: RMSNorm(ln2),
+// gate|up, SiLU(gate)*up, down_proj, residual add) in one launch. Block b
+// owns the intermediate columns [64b, 64b + 64): it computes their
+// activations from RMSNorm(resid) and their share of every down_proj output
+// row, W_down[:, 64b:64b+64] . act[64b:64b+64], into part[row][b]. After
+// every block has arrived (a grid-wide count; all blocks are resident, one
+// per SM), block b sums the shares of its output rows in block order and
+// adds them to the residual. The intermediate vector never leaves the SM
+// and down_proj needs no staging of it.
+constexpr int kMlpSlice = 64;     // intermediate columns per block
+constexpr uint32_t kErrMlpWait = 16u;
+struct MlpArgs {
+  const uint16_t *wg, *wu, *wd;  // gate, up [I][H]; down [H][I]
+  // down_proj re-laid out by block, [grid][H][64] (mlp_relayout), so a block
+  // streams one contiguous range; null: read wd's columns in place
+  const uint16_t* wd_slices;
+  const float* gamma;            // ln2, promoted f32
+  float eps;
+  int H, I;
+  float* resid;                  // [H], updated in place
+  float* part;                   // [H][grid] per-block shares of the down rows
+  unsigned long long* arrive;    // arrivals so far; a multiple of the grid between launches
+  StepCtl* ctl;
+  uint32_t* err;
+  uint64_t wait_ns;              // bound of the arrival wait
+  KTrace tr;
+};
+// Blocks of the fused MLP for this shape, or 0 when it does not apply
+// (hidden not 1024/1280/1536, I not a multiple of 64, or I/64 outside
+// [3/4, 1] of the SM count).
+int mlp_grid(int H, int I, int num_sms);
+cudaError_t launch_mlp(const MlpArgs& a, int grid, cudaStream_t st, bool pdl);
+// dst[b][r][c] = wd[r][64 b + c] for the I / 64 column slices of a [H][I] matrix.
+cudaError_t launch_mlp_relayout(const uint16_t* wd, uint16_t* dst, int H, int I, cudaStream_t st);
 
 // Launchers. pdl=true attaches a programmatic-serialization edge to the
 // previous launch in the stream.

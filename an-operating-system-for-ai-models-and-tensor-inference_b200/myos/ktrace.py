@@ -37,6 +37,8 @@ def summarize(path: str, layers: int, first: int = 8, last: int = 56) -> dict:
         for sl in range(ns):
             k = KINDS[sl % 5] if sl < 5 * layers else "head"
             start, wait, end = r[sl, 0], r[sl, 1], r[sl, 2]
+            if end == 0:  # no launch in this slot (down_proj inside the fused MLP)
+                continue
             gap = wait - prev_end if prev_end is not None else 0.0
             agg[k] += [gap, end - wait, wait - start]
             prev_end = end
@@ -44,6 +46,8 @@ def summarize(path: str, layers: int, first: int = 8, last: int = 56) -> dict:
     out = {"token_us": float(np.mean([t[s + 1, 0, 1] - t[s, 0, 1]
                                       for s in range(first, last)]) / 1e3)}
     for k, v in agg.items():
+        if not v.any():
+            continue
         per = n * (layers if k != "head" else 1)
         out[k] = {"gap_us": round(v[0] / per / 1e3, 2), "run_us": round(v[1] / per / 1e3, 2),
                   "prewait_us": round(v[2] / per / 1e3, 2)}
