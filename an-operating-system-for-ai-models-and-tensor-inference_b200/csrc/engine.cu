@@ -127,6 +127,7 @@ struct myos_ctx {
   std::vector<uint8_t> have;  // per layer x suffix, then embed, final norm, lm_head
   size_t len = 0;             // KV cursor (host mirror of ctl->pos)
   std::map<std::pair<int, int>, cudaGraphExec_t> graphs;
+  std::map<std::pair<int, int>, uint64_t> graph_kernels;  // kernels captured in each graph
   cudaEvent_t ev0 = nullptr, ev1 = nullptr, ev2 = nullptr;
   float prefill_ms = 0.f, decode_ms = 0.f;
   int steps_per_graph = 16;
@@ -569,7 +570,11 @@ int run_steps(myos_ctx* c, int kind, size_t nsteps) {
       cudaGraph_t g;
       CK(cudaStreamBeginCapture(c->st, cudaStreamCaptureModeThreadLocal));
       int st = MYOS_OK;
+      const uint64_t before = launches_total();  // a capture launches nothing
       for (int i = 0; i < chunk && st == MYOS_OK; ++i) st = enqueue_step(c, head, feed, i > 0);
+      const uint64_t captured = launches_total() - before;
+      launches_uncount(captured);
+      c->graph_kernels[key] = captured;
       cudaError_t ce = cudaStreamEndCapture(c->st, &g);
       if (st) return st;
       if (ce != cudaSuccess)
@@ -581,7 +586,7 @@ int run_steps(myos_ctx* c, int kind, size_t nsteps) {
         return fail(c, MYOS_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(ce));
       it = c->graphs.emplace(key, ge).first;
     }
-    CK(cudaGraphLaunch(it->second, c->st));
+    CK(counted(cudaGraphLaunch(it->second, c->st), c->graph_kernels[key]));
     done += (size_t)chunk;
   }
   return MYOS_OK;
@@ -648,6 +653,7 @@ int finish(myos_ctx* c) {
     // carry an epoch a later phase expects)
     // an arrival count left partway would misplace the next MLP launch's target
     if (c->mlp_arrive) cudaMemset(c->mlp_arrive, 0, sizeof(unsigned long long));
+    cudaMemset(c->counters, 0, (1 + c->s.num_kv_heads) * 4);
     if (c->sflags) {
       cudaMemset(c->sflags, 0, (size_t)c->sargs.grid * sizeof(unsigned));
       cudaMemset(c->s_words, 0, c->s_words_bytes);
@@ -1503,7 +1509,7 @@ int myos_profile_kernels(myos_ctx* c, int iters, float* ms_out, double* bytes_ou
   const int L = (int)c->s.num_layers;
   c->profiling = true;
   for (int kind = K_QKV; kind <= K_HEAD; ++kind) {
-    if (kind == K_DOWN && c->grid_mlp) {  // runs inside the fused MLP (timed as gate_up)
+    if (kind_bytes(c, kind) == 0.0) {  // runs inside a fused launch (timed with it)
       ms_out[kind] = 0.f;
       if (bytes_out) bytes_out[kind] = 0.0;
       continue;
@@ -1532,6 +1538,12 @@ int myos_profile_kernels(myos_ctx* c, int iters, float* ms_out, double* bytes_ou
   CK(cudaMemcpyAsync(c->ctl, &saved, sizeof saved, cudaMemcpyHostToDevice, c->st));
   CK(cudaMemcpyAsync(c->logits, saved_logits.data(), c->s.vocab * 4, cudaMemcpyHostToDevice, c->st));
   return finish(c);
+}
+
+int myos_launch_count(uint64_t* out) {
+  if (!out) return MYOS_ERR_ARG;
+  *out = launches_total();
+  return MYOS_OK;
 }
 
 int myos_last_timing(const myos_ctx* c, float* prefill_ms, float* decode_ms) {

@@ -19,6 +19,7 @@
 #include <cute/tensor.hpp>
 
 #include "gemm_sm100.h"
+#include "kernels.h"
 
 namespace myos {
 namespace {
@@ -88,7 +89,7 @@ cudaError_t gemm_bf16_f32(int M, int N, int K, const uint16_t* A, const uint16_t
   if (Gemm::get_workspace_size(args) > workspace_bytes) return cudaErrorInvalidValue;
   if (g.initialize(args, workspace, st) != cutlass::Status::kSuccess) return cudaErrorInvalidValue;
   if (g.run(st) != cutlass::Status::kSuccess) return cudaErrorLaunchFailure;
-  return cudaGetLastError();
+  return counted(cudaGetLastError());
 }
 
 }  // namespace myos

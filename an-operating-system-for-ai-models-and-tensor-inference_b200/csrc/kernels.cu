@@ -18,6 +18,7 @@
 #include <stdlib.h>
 
 #include <cooperative_groups.h>
+#include <atomic>
 #include <mutex>
 
 #include "common.cuh"
@@ -699,8 +700,9 @@ MYOS_DEV unsigned long long ld_acquire_u64(const unsigned long long* p) {
 }
 
 template <int P>
-MYOS_DEV void mlp_load(uint4 (&buf)[2 * P], const MlpArgs& a, int c0, int bt, int warp, int lane,
+MYOS_DEV void mlp_load(uint4 (&buf)[2 * P], const MlpArgs& a, int slice, int bt, int warp, int lane,
                        int gpw) {
+  const int c0 = slice * kMlpSlice;
   constexpr int UB = 2 * P;
   if (bt < kMlpRowsPerWarp) {
     const size_t r = (size_t)(c0 + warp + kMlpWarps * bt);
@@ -714,7 +716,7 @@ MYOS_DEV void mlp_load(uint4 (&buf)[2 * P], const MlpArgs& a, int c0, int bt, in
   } else {
     const int j = bt - kMlpRowsPerWarp;
     // row r of the block's slice at base + r * ld (64 columns, 128 bytes)
-    const uint16_t* base = a.wd_slices ? a.wd_slices + (size_t)blockIdx.x * a.H * kMlpSlice : a.wd + c0;
+    const uint16_t* base = a.wd_slices ? a.wd_slices + (size_t)slice * a.H * kMlpSlice : a.wd + c0;
     const size_t ld = a.wd_slices ? (size_t)kMlpSlice : (size_t)a.I;
 #pragma unroll
     for (int i = 0; i < UB; ++i) {
@@ -762,7 +764,7 @@ __global__ void __launch_bounds__(kMlpThreads, 1) k_mlp(MlpArgs a) {
   float4 g0[1], g1[1];  // H <= 8 * kMlpThreads: one chunk per thread
   gamma_preload<1>(in, H, g0, g1);
   uint4 cur[UB], nxt[UB];
-  mlp_load<P>(cur, a, c0, 0, warp, lane, gpw);
+  mlp_load<P>(cur, a, b, 0, warp, lane, gpw);
   if (threadIdx.x == 0) wait_failed = 0;
   pdl_wait();
   pdl_launch();
@@ -774,7 +776,7 @@ __global__ void __launch_bounds__(kMlpThreads, 1) k_mlp(MlpArgs a) {
   const float4* xhi = reinterpret_cast<const float4*>(xs + (H >> 1));
   float4 alo = make_float4(0.f, 0.f, 0.f, 0.f), ahi = alo;
   for (int bt = 0; bt < nbt; ++bt) {
-    if (bt + 1 < nbt) mlp_load<P>(nxt, a, c0, bt + 1, warp, lane, gpw);
+    if (bt + 1 < nbt) mlp_load<P>(nxt, a, b, bt + 1, warp, lane, gpw);
     if (bt < kMlpRowsPerWarp) {
       float g = 0.0f, u = 0.0f;
 #pragma unroll
@@ -1240,10 +1242,10 @@ __global__ void __launch_bounds__(kThreads) k_attn(AttnArgs a) {
 // the last block of the KV head to finish, one warp per head, splits in order.
 template <typename KT>
 MYOS_DEV void dec_tile_issue(const KT* kc, const KT* vc, int d, int t0, int nk, int skip,
-                             float* ks, float* vs, uint4* raw) {
+                             float* ks, float* vs, uint4* raw, int tid, int nt) {
   constexpr int per = 16 / sizeof(KT);  // elements per 16-byte piece
   const int ppr = d / per, ds = d + 4;
-  for (int i = threadIdx.x; i < nk * ppr; i += blockDim.x) {
+  for (int i = tid; i < nk * ppr; i += nt) {
     const int tt = i / ppr, e = (i - tt * ppr) * per;
     if (t0 + tt == skip) continue;
     const KT* ksrc = kc + (size_t)(t0 + tt) * d + e;
@@ -1262,11 +1264,11 @@ MYOS_DEV void dec_tile_issue(const KT* kc, const KT* vc, int d, int t0, int nk, 
 // copied them.
 template <typename KT>
 MYOS_DEV void dec_tile_finish(int d, int t0, int nk, int skip, float* ks, float* vs,
-                              const uint4* raw) {
+                              const uint4* raw, int tid, int nt) {
   cpa_wait_all();
   if (sizeof(KT) == 4) return;
   const int ppr = d / 8, ds = d + 4;
-  for (int i = threadIdx.x; i < nk * ppr; i += blockDim.x) {
+  for (int i = tid; i < nk * ppr; i += nt) {
     const int tt = i / ppr, e = (i - tt * ppr) * 8;
     if (t0 + tt == skip) continue;
     float4 lo, hi;
@@ -1425,7 +1427,7 @@ __global__ void __launch_bounds__(kThreads) k_attn_dec(AttnArgs a) {
   const bool has_new = pos >= kb && pos < ke;
   if (a.defer_merge && kb >= ke) return;  // no keys: the merge skips this split
   const uint64_t t_start = a.tr.buf ? global_ns() : 0;
-  if (kb < ke) dec_tile_issue<KT>(kc, vc, d, kb, min(kTile, ke - kb), pos, ks, vs, raw);
+  if (kb < ke) dec_tile_issue<KT>(kc, vc, d, kb, min(kTile, ke - kb), pos, ks, vs, raw, threadIdx.x, blockDim.x);
   const float4* c4 = reinterpret_cast<const float4*>(a.cos_t + (size_t)pos * half);
   const float4* s4 = reinterpret_cast<const float4*>(a.sin_t + (size_t)pos * half);
   for (int i = threadIdx.x; i < (half >> 2); i += blockDim.x) {
@@ -1447,7 +1449,7 @@ __global__ void __launch_bounds__(kThreads) k_attn_dec(AttnArgs a) {
     else if (i < nq4 + d4) cpa16(reinterpret_cast<float4*>(kn) + (i - nq4), k4 + (i - nq4));
     else cpa16(reinterpret_cast<float4*>(vn) + (i - nq4 - d4), v4 + (i - nq4 - d4));
   }
-  if (kb < ke) dec_tile_finish<KT>(d, kb, min(kTile, ke - kb), pos, ks, vs, raw);
+  if (kb < ke) dec_tile_finish<KT>(d, kb, min(kTile, ke - kb), pos, ks, vs, raw, threadIdx.x, blockDim.x);
   cpa_wait_all();
   __syncthreads();
   trace_mark(trow, 3);  // q, new k/v and the first tile in shared memory
@@ -1482,8 +1484,8 @@ __global__ void __launch_bounds__(kThreads) k_attn_dec(AttnArgs a) {
     const int nk = min(kTile, ke - t0);
     if (t0 != kb) {  // later tiles
       __syncthreads();
-      dec_tile_issue<KT>(kc, vc, d, t0, nk, pos, ks, vs, raw);
-      dec_tile_finish<KT>(d, t0, nk, pos, ks, vs, raw);
+      dec_tile_issue<KT>(kc, vc, d, t0, nk, pos, ks, vs, raw, threadIdx.x, blockDim.x);
+      dec_tile_finish<KT>(d, t0, nk, pos, ks, vs, raw, threadIdx.x, blockDim.x);
       if (has_new && pos >= t0 && pos < t0 + nk)
         for (int e = threadIdx.x; e < d; e += blockDim.x) {
           ks[(pos - t0) * ds + e] = kn[e];
@@ -1637,7 +1639,7 @@ __global__ void k_tp_pick(const float* cands, int n, unsigned* seq, StepCtl* ctl
 cudaError_t launch_tp_pick(const float* cands, int n, unsigned* seq, StepCtl* ctl,
                            uint32_t* rec_fed, uint32_t* rec_argmax, cudaStream_t st) {
   k_tp_pick<<<1, 32, 0, st>>>(cands, n, seq, ctl, rec_fed, rec_argmax);
-  return cudaGetLastError();
+  return counted(cudaGetLastError());
 }
 
 constexpr int kReduceThreads = 256;
@@ -1688,7 +1690,7 @@ cudaError_t launch_tp_reduce(const TpReduceArgs& r, cudaStream_t st, bool pdl) {
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, k_tp_reduce, r);
+  return counted(cudaLaunchKernelEx(&cfg, k_tp_reduce, r));
 }
 
 __global__ void k_step_end(StepCtl* ctl) {
@@ -1848,12 +1850,12 @@ static int pick_batch(int P, int NR) {
 template <int EPI, int NR>
 static cudaError_t launch_stream(const GemvArgs& a, int U, cudaLaunchConfig_t& cfg) {
   switch (U) {
-    case 3: return cudaLaunchKernelEx(&cfg, k_gemv_stream<EPI, NR, 3>, a);
-    case 4: return cudaLaunchKernelEx(&cfg, k_gemv_stream<EPI, NR, 4>, a);
-    case 5: return cudaLaunchKernelEx(&cfg, k_gemv_stream<EPI, NR, 5>, a);
-    case 6: return cudaLaunchKernelEx(&cfg, k_gemv_stream<EPI, NR, 6>, a);
-    case 7: return cudaLaunchKernelEx(&cfg, k_gemv_stream<EPI, NR, 7>, a);
-    default: return cudaLaunchKernelEx(&cfg, k_gemv_stream<EPI, NR, 8>, a);
+    case 3: return counted(cudaLaunchKernelEx(&cfg, k_gemv_stream<EPI, NR, 3>, a));
+    case 4: return counted(cudaLaunchKernelEx(&cfg, k_gemv_stream<EPI, NR, 4>, a));
+    case 5: return counted(cudaLaunchKernelEx(&cfg, k_gemv_stream<EPI, NR, 5>, a));
+    case 6: return counted(cudaLaunchKernelEx(&cfg, k_gemv_stream<EPI, NR, 6>, a));
+    case 7: return counted(cudaLaunchKernelEx(&cfg, k_gemv_stream<EPI, NR, 7>, a));
+    default: return counted(cudaLaunchKernelEx(&cfg, k_gemv_stream<EPI, NR, 8>, a));
   }
 }
 
@@ -1914,11 +1916,11 @@ cudaError_t launch_gemv(int epi, const GemvArgs& a0, int grid, cudaStream_t st, 
     return cudaErrorInvalidValue;
   }
   switch (epi) {
-    case EPI_STORE: return cudaLaunchKernelEx(&cfg, k_gemv<EPI_STORE>, a);
-    case EPI_BIAS: return cudaLaunchKernelEx(&cfg, k_gemv<EPI_BIAS>, a);
-    case EPI_RESID: return cudaLaunchKernelEx(&cfg, k_gemv<EPI_RESID>, a);
-    case EPI_SWIGLU: return cudaLaunchKernelEx(&cfg, k_gemv<EPI_SWIGLU>, a);
-    case EPI_ARGMAX: return cudaLaunchKernelEx(&cfg, k_gemv<EPI_ARGMAX>, a);
+    case EPI_STORE: return counted(cudaLaunchKernelEx(&cfg, k_gemv<EPI_STORE>, a));
+    case EPI_BIAS: return counted(cudaLaunchKernelEx(&cfg, k_gemv<EPI_BIAS>, a));
+    case EPI_RESID: return counted(cudaLaunchKernelEx(&cfg, k_gemv<EPI_RESID>, a));
+    case EPI_SWIGLU: return counted(cudaLaunchKernelEx(&cfg, k_gemv<EPI_SWIGLU>, a));
+    case EPI_ARGMAX: return counted(cudaLaunchKernelEx(&cfg, k_gemv<EPI_ARGMAX>, a));
   }
   return cudaErrorInvalidValue;
 }
@@ -1930,9 +1932,9 @@ cudaError_t launch_mlp(const MlpArgs& a, int grid, cudaStream_t st, bool pdl) {
   cudaLaunchConfig_t cfg =
       make_cfg(dim3(grid), dim3(kMlpThreads), gemv_smem_bytes(a.H), st, pdl, attr);
   switch (a.H / 256) {
-    case 4: return cudaLaunchKernelEx(&cfg, k_mlp<4>, a);
-    case 5: return cudaLaunchKernelEx(&cfg, k_mlp<5>, a);
-    case 6: return cudaLaunchKernelEx(&cfg, k_mlp<6>, a);
+    case 4: return counted(cudaLaunchKernelEx(&cfg, k_mlp<4>, a));
+    case 5: return counted(cudaLaunchKernelEx(&cfg, k_mlp<5>, a));
+    case 6: return counted(cudaLaunchKernelEx(&cfg, k_mlp<6>, a));
   }
   return cudaErrorInvalidValue;
 }
@@ -1940,7 +1942,7 @@ cudaError_t launch_mlp(const MlpArgs& a, int grid, cudaStream_t st, bool pdl) {
 cudaError_t launch_mlp_relayout(const uint16_t* wd, uint16_t* dst, int H, int I, cudaStream_t st) {
   if (I % kMlpSlice != 0 || ((uintptr_t)wd & 15) || ((uintptr_t)dst & 15)) return cudaErrorInvalidValue;
   k_mlp_relayout<<<1184, 256, 0, st>>>(reinterpret_cast<const uint4*>(wd), reinterpret_cast<uint4*>(dst), H, I);
-  return cudaGetLastError();
+  return counted(cudaGetLastError());
 }
 
 int attn_dpl(int d) { return d <= 32 ? 1 : d <= 64 ? 2 : d <= 128 ? 4 : 8; }
@@ -1958,8 +1960,8 @@ size_t merge_smem_bytes(int Hq, int nsplit, int d) {
 
 template <int DPL>
 static cudaError_t launch_attn_dpl(const AttnArgs& a, int kv_bf16, cudaLaunchConfig_t& cfg) {
-  if (kv_bf16) return cudaLaunchKernelEx(&cfg, k_attn<DPL, __nv_bfloat16>, a);
-  return cudaLaunchKernelEx(&cfg, k_attn<DPL, float>, a);
+  if (kv_bf16) return counted(cudaLaunchKernelEx(&cfg, k_attn<DPL, __nv_bfloat16>, a));
+  return counted(cudaLaunchKernelEx(&cfg, k_attn<DPL, float>, a));
 }
 
 cudaError_t launch_attention(const AttnArgs& a, int kv_bf16, cudaStream_t st, bool pdl) {
@@ -1977,7 +1979,7 @@ cudaError_t launch_attention(const AttnArgs& a, int kv_bf16, cudaStream_t st, bo
       attrs[cfg.numAttrs].val.clusterDim.z = 1;
       ++cfg.numAttrs;
     }
-#define MYOS_ATTN_LAUNCH(KT, D) return cudaLaunchKernelEx(&cfg, k_attn_dec<KT, D>, a)
+#define MYOS_ATTN_LAUNCH(KT, D) return counted(cudaLaunchKernelEx(&cfg, k_attn_dec<KT, D>, a))
     switch (a.d) {
       case 64:
         if (kv_bf16) MYOS_ATTN_LAUNCH(__nv_bfloat16, 64);
@@ -2008,13 +2010,13 @@ cudaError_t launch_attention(const AttnArgs& a, int kv_bf16, cudaStream_t st, bo
 cudaError_t launch_step_end(StepCtl* ctl, cudaStream_t st, bool pdl) {
   cudaLaunchAttribute attr[1];
   cudaLaunchConfig_t cfg = make_cfg(dim3(1), dim3(32), 0, st, pdl, attr);
-  return cudaLaunchKernelEx(&cfg, k_step_end, ctl);
+  return counted(cudaLaunchKernelEx(&cfg, k_step_end, ctl));
 }
 
 cudaError_t launch_argmax(const float* v, int n, float* part_val, uint32_t* part_idx,
                           unsigned* counter, uint32_t* out, int grid, cudaStream_t st) {
   k_argmax<<<grid, kThreads, 0, st>>>(v, n, part_val, part_idx, counter, out);
-  return cudaGetLastError();
+  return counted(cudaGetLastError());
 }
 
 cudaError_t launch_swiglu_mul(float* h, const float* gate, const float* up, int n,
@@ -2023,7 +2025,7 @@ cudaError_t launch_swiglu_mul(float* h, const float* gate, const float* up, int 
   if (grid > 1184) grid = 1184;
   if (grid < 1) grid = 1;
   k_swiglu_mul<<<grid, kThreads, 0, st>>>(h, gate, up, n);
-  return cudaGetLastError();
+  return counted(cudaGetLastError());
 }
 
 cudaError_t launch_rope(float* y, const float* x, int len, int head_dim, const float* cos_row,
@@ -2031,14 +2033,23 @@ cudaError_t launch_rope(float* y, const float* x, int len, int head_dim, const f
   int grid = (len + kThreads - 1) / kThreads;
   if (grid < 1) grid = 1;
   k_rope<<<grid, kThreads, 0, st>>>(y, x, len, head_dim, cos_row, sin_row);
-  return cudaGetLastError();
+  return counted(cudaGetLastError());
 }
 
 cudaError_t launch_rmsnorm(float* y, const float* x, const float* gamma, int n, float eps,
                            cudaStream_t st) {
   k_rmsnorm<<<1, kThreads, 0, st>>>(y, x, gamma, n, eps);
-  return cudaGetLastError();
+  return counted(cudaGetLastError());
 }
+
+static std::atomic<uint64_t> g_launches{0};
+
+cudaError_t counted(cudaError_t e, uint64_t n) {
+  if (e == cudaSuccess) g_launches.fetch_add(n, std::memory_order_relaxed);
+  return e;
+}
+void launches_uncount(uint64_t n) { g_launches.fetch_sub(n, std::memory_order_relaxed); }
+uint64_t launches_total() { return g_launches.load(std::memory_order_relaxed); }
 
 static std::mutex g_init_mu;
 static unsigned long long g_init_mask = 0;  // devices whose limits are raised (under g_init_mu)

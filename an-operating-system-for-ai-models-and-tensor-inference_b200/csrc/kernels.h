@@ -197,6 +197,13 @@ cudaError_t launch_rmsnorm(float* y, const float* x, const float* gamma, int n, 
                            cudaStream_t st);
 cudaError_t kernels_init();  // raises dynamic shared-memory limits once per device
 
+// Kernel launches the library has enqueued in this process (diagnostics):
+// every launcher counts a successful launch; a CUDA graph replay counts the
+// kernels captured in it, the capture itself counts none.
+cudaError_t counted(cudaError_t e, uint64_t n = 1);
+void launches_uncount(uint64_t n);
+uint64_t launches_total();
+
 size_t gemv_smem_bytes(int K);
 // Grid for an M x K GEMV (NR = 2 for gate|up): up to two blocks per SM.
 int gemv_grid(int M, int K, int NR, int num_sms);

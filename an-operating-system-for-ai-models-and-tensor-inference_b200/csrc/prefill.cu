@@ -13,6 +13,7 @@
 
 #include "common.cuh"
 #include "prefill.h"
+#include "kernels.h"
 
 namespace myos {
 namespace {
@@ -300,35 +301,35 @@ __global__ void k_pos_advance(int* rowpos, int B) {
 cudaError_t pf_row_argmax(uint32_t* tok, uint32_t* out, int out_stride, int step, const float* D,
                           int B, int V, cudaStream_t st) {
   k_row_argmax<<<B, kT, 0, st>>>(tok, out, out_stride, step, D, B, V);
-  return cudaGetLastError();
+  return counted(cudaGetLastError());
 }
 
 cudaError_t pf_rows_copy(float* dst, const float* src, const int* src_row, int B, int K,
                          cudaStream_t st) {
   k_rows_copy<<<B, kT, 0, st>>>(dst, src, src_row, K);
-  return cudaGetLastError();
+  return counted(cudaGetLastError());
 }
 
 cudaError_t pf_pos_advance(int* rowpos, int B, cudaStream_t st) {
   k_pos_advance<<<(B + 127) / 128, 128, 0, st>>>(rowpos, B);
-  return cudaGetLastError();
+  return counted(cudaGetLastError());
 }
 
 cudaError_t pf_embed(float* X, const uint16_t* embed, const uint32_t* ids, int n, int K,
                      cudaStream_t st) {
   k_pf_embed<<<n, kT, 0, st>>>(X, embed, ids, K);
-  return cudaGetLastError();
+  return counted(cudaGetLastError());
 }
 
 cudaError_t pf_norm_split(uint16_t* A, const float* X, const float* gamma, int n, int K, float eps,
                           cudaStream_t st) {
   k_pf_norm_split<<<n, kT, 0, st>>>(A, X, gamma, n, K, eps);
-  return cudaGetLastError();
+  return counted(cudaGetLastError());
 }
 
 cudaError_t pf_bias(float* Q, const float* D, const float* bias, int n, int N, cudaStream_t st) {
   k_pf_bias<<<n, kT, 0, st>>>(Q, D, bias, n, N);
-  return cudaGetLastError();
+  return counted(cudaGetLastError());
 }
 
 cudaError_t pf_rope_store(float* Q, void* kc, void* vc, int kv_bf16, const float* cos_t,
@@ -341,7 +342,7 @@ cudaError_t pf_rope_store(float* Q, void* kc, void* vc, int kv_bf16, const float
   else
     k_pf_rope_store<float><<<n, kT, 0, st>>>(Q, (float*)kc, (float*)vc, cos_t, sin_t, p0, Hq, Hkv,
                                              d, S, rowpos, rowstride);
-  return cudaGetLastError();
+  return counted(cudaGetLastError());
 }
 
 bool pf_attn_supported(int d, int G) { return (d == 64 || d == 128) && G <= 8; }
@@ -359,7 +360,7 @@ cudaError_t pf_attn(float* out, const float* Q, const void* kc, const void* vc, 
     else                                                                                    \
       k_pf_attn<float, D><<<grid, kT, 0, st>>>(out, Q, (const float*)kc, (const float*)vc, \
                                                p0, Hq, Hkv, S, scale, rowpos, rowstride);   \
-    return cudaGetLastError();                                                              \
+    return counted(cudaGetLastError());                                                              \
   }
   MYOS_PF_ATTN(64)
   MYOS_PF_ATTN(128)
@@ -369,17 +370,17 @@ cudaError_t pf_attn(float* out, const float* Q, const void* kc, const void* vc, 
 
 cudaError_t pf_resid(float* X, const float* D, int n, int N, cudaStream_t st) {
   k_pf_resid<<<n, kT, 0, st>>>(X, D, n, N);
-  return cudaGetLastError();
+  return counted(cudaGetLastError());
 }
 
 cudaError_t pf_resid_part(float* D, const float* X, int n, int N, cudaStream_t st) {
   k_pf_resid_part<<<n, kT, 0, st>>>(D, X, n, N);
-  return cudaGetLastError();
+  return counted(cudaGetLastError());
 }
 
 cudaError_t pf_swiglu_split(uint16_t* A, const float* D, int n, int I, cudaStream_t st) {
   k_pf_swiglu_split<<<n, kT, 0, st>>>(A, D, n, I);
-  return cudaGetLastError();
+  return counted(cudaGetLastError());
 }
 
 }  // namespace myos

@@ -1200,8 +1200,8 @@ cudaError_t launch_step_stream(const StreamArgs& a, cudaStream_t st) {
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (a.kv_bf16) return cudaLaunchKernelEx(&cfg, k_step_stream<__nv_bfloat16>, a);
-  return cudaLaunchKernelEx(&cfg, k_step_stream<float>, a);
+  if (a.kv_bf16) return counted(cudaLaunchKernelEx(&cfg, k_step_stream<__nv_bfloat16>, a));
+  return counted(cudaLaunchKernelEx(&cfg, k_step_stream<float>, a));
 }
 
 }  // namespace myos

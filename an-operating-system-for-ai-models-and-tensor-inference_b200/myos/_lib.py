@@ -100,6 +100,7 @@ SIGNATURES = {
     "myos_kv_head": (C.c_int, [C.c_void_p, C.c_uint32, C.c_uint32, sz, _f32p, _f32p]),
     "myos_logits": (C.c_int, [C.c_void_p, _f32p]),
     "myos_last_timing": (C.c_int, [C.c_void_p, _f32p, _f32p]),
+    "myos_launch_count": (C.c_int, [C.POINTER(C.c_uint64)]),
     "myos_profile_kernels": (C.c_int, [C.c_void_p, C.c_int, _f32p, C.POINTER(C.c_double)]),
     "myos_gemv_bf16": (C.c_int, [_f32p, sz, _u8p, sz, _f32p, sz, sz, sz]),
     "myos_rmsnorm_bf16_weight": (C.c_int, [_f32p, sz, _u8p, sz, _f32p, sz, C.c_float]),

@@ -204,6 +204,13 @@ class Engine:
         self._check(self.L.myos_last_timing(self.h, C.byref(p), C.byref(d)))
         return p.value, d.value
 
+    def launch_count(self) -> int:
+        """Kernel launches the library has enqueued in this process so far
+        (graph replays count the kernels captured in them)."""
+        n = C.c_uint64()
+        self._check(self.L.myos_launch_count(C.byref(n)))
+        return int(n.value)
+
 
 def greedy_token(logits) -> int:
     """model_core::greedy_token (lib.rs:157-167) on the device."""

@@ -110,6 +110,7 @@ pub mod ffi {
         pub fn myos_logits(ctx: *mut myos_ctx, out: *mut f32) -> c_int;
         pub fn myos_profile_kernels(ctx: *mut myos_ctx, iters: c_int, ms_out: *mut f32, bytes_out: *mut f64) -> c_int;
         pub fn myos_last_timing(ctx: *const myos_ctx, prefill_ms: *mut f32, decode_ms: *mut f32) -> c_int;
+        pub fn myos_launch_count(out: *mut u64) -> c_int;
         pub fn myos_gemv_bf16(y: *mut f32, y_len: usize, w: *const u8, w_len: usize, x: *const f32, x_len: usize, m: usize, k: usize) -> c_int;
         pub fn myos_rmsnorm_bf16_weight(y: *mut f32, y_len: usize, w: *const u8, w_len: usize, x: *const f32, x_len: usize, eps: f32) -> c_int;
         pub fn myos_gqa_attn_f32(y: *mut f32, y_len: usize, q: *const f32, q_len: usize, k: *const f32, k_len: usize, v: *const f32, v_len: usize, num_q_heads: usize, num_kv_heads: usize, head_dim: usize, seq_len: usize, mask_kind: i32, query_pos: usize) -> c_int;

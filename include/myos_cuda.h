@@ -221,6 +221,12 @@ int myos_profile_kernels(myos_ctx* ctx, int iters, float* ms_out, double* bytes_
 /* Device time of the last prefill / decode call, from CUDA events (ms). */
 int myos_last_timing(const myos_ctx* ctx, float* prefill_ms, float* decode_ms);
 
+/* Kernel launches this library has enqueued in the calling process, all
+ * contexts and devices together (a CUDA graph replay adds the kernels
+ * captured in it). Diagnostics for benchmarks; no counterpart in the
+ * reference, which runs on the CPU. */
+int myos_launch_count(uint64_t* out);
+
 /* ---------------------------------------------------------------------------
  * tensor_core operators on host slices (crates/tensor_core/src/lib.rs:54-74).
  * Same argument meaning and error behaviour as the Rust functions; the work
