@@ -170,6 +170,85 @@ struct myos_ctx {
 
 namespace {
 
+// Tensor name -> (layer, suffix) or global (0 embed, 1 final norm, 2
+// lm_head) for the model shape s; false for names the model never reads
+// (qwen25_layout.rs:15-207 keys).
+bool parse_tensor_name(const myos_shape& s, const std::string& n, int* layer, int* suffix,
+                       int* global) {
+  *layer = *suffix = *global = -1;
+  if (n == kEmbed) {
+    *global = 0;
+  } else if (n == kFinalNorm) {
+    *global = 1;
+  } else if (n == kLmHead) {
+    if (s.tied_head) return false;
+    *global = 2;
+  } else if (n.compare(0, 13, "model.layers.") == 0) {
+    const size_t dot = n.find('.', 13);
+    if (dot == std::string::npos) return false;
+    const std::string idx = n.substr(13, dot - 13);
+    if (idx.empty() || idx.find_first_not_of("0123456789") != std::string::npos) return false;
+    if (idx.size() > 1 && idx[0] == '0') return false;
+    const unsigned long li = strtoul(idx.c_str(), nullptr, 10);
+    if (li >= s.num_layers) return false;
+    const std::string suf = n.substr(dot + 1);
+    for (int k = 0; k < kSuffixes; ++k)
+      if (suf == kSuffix[k]) *suffix = k;
+    if (*suffix < 0) return false;
+    *layer = (int)li;
+  } else {
+    return false;
+  }
+  return true;
+}
+
+// How rank rk of N holds a tensor of the whole model f: heads (q/k/v rows,
+// o_proj columns), MLP columns (gate/up rows, down_proj columns) and head
+// vocabulary rows are split in rank order; the o_proj input and MLP widths
+// are padded to multiples of 256 with zeros; everything else is replicated.
+// The loader and myos_tp_slice both use it.
+myos_tp_part tp_part(const myos_shape& f, uint32_t N, uint32_t rk, int global, int suffix) {
+  const uint64_t H = f.hidden, I = f.intermediate, V = f.vocab;
+  const uint64_t qd = (uint64_t)f.num_q_heads * f.head_dim, kvd = (uint64_t)f.num_kv_heads * f.head_dim;
+  const uint64_t qdl = qd / N, kvdl = kvd / N, Ic = I / N, Vl = V / N;
+  const uint64_t Il = N > 1 ? (Ic + 255) / 256 * 256 : Ic, qdp = N > 1 ? (qdl + 255) / 256 * 256 : qdl;
+  myos_tp_part p = {};
+  auto whole = [&](uint64_t r, uint64_t cl, bool mtx) {
+    p.rows = r;
+    p.cols = cl;
+    p.nrows = p.store_rows = r;
+    p.ncols = p.store_cols = cl;
+    p.matrix = mtx ? 1 : 0;
+    p.kept = 1;
+  };
+  auto rowpart = [&](uint64_t r, uint64_t cl, bool mtx, uint64_t r0, uint64_t nr, uint64_t sr) {
+    whole(r, cl, mtx);
+    p.row0 = r0;
+    p.nrows = nr;
+    p.store_rows = sr;
+  };
+  auto colpart = [&](uint64_t r, uint64_t cl, uint64_t c0, uint64_t nc, uint64_t sc) {
+    whole(r, cl, true);
+    p.col0 = c0;
+    p.ncols = nc;
+    p.store_cols = sc;
+  };
+  if (global == 0) whole(V, H, true);
+  else if (global == 1) whole(H, 1, false);
+  else if (global == 2) rowpart(V, H, true, rk * Vl, Vl, Vl);
+  else switch (suffix) {
+    case 0: case 8: whole(H, 1, false); break;
+    case 1: rowpart(qd, H, true, rk * qdl, qdl, qdl); break;
+    case 2: rowpart(qd, 1, false, rk * qdl, qdl, qdl); break;
+    case 3: case 5: rowpart(kvd, H, true, rk * kvdl, kvdl, kvdl); break;
+    case 4: case 6: rowpart(kvd, 1, false, rk * kvdl, kvdl, kvdl); break;
+    case 7: colpart(H, qd, rk * qdl, qdl, qdp); break;
+    case 9: case 10: rowpart(I, H, true, rk * Ic, Ic, Il); break;
+    case 11: colpart(H, I, rk * Ic, Ic, Il); break;
+  }
+  return p;
+}
+
 int fail(myos_ctx* c, int code, const std::string& msg) {
   if (c) c->err = msg;
   return code;
@@ -1267,43 +1346,12 @@ int myos_load_tensor(myos_ctx* c, const char* name, int32_t dtype, const int64_t
   const uint64_t qd = (uint64_t)s.num_q_heads * s.head_dim, kvd = (uint64_t)s.num_kv_heads * s.head_dim;
   std::string n(name);
   int layer = -1, suffix = -1, global = -1;  // global: 0 embed, 1 final norm, 2 lm_head
-  std::vector<uint64_t> expect;
-  if (n == kEmbed) {
-    global = 0;
-    expect = {V, H};
-  } else if (n == kFinalNorm) {
-    global = 1;
-    expect = {H};
-  } else if (n == kLmHead) {
-    if (s.tied_head) return MYOS_OK;  // the tied model never reads it (qwen25_block.rs:290-301)
-    global = 2;
-    expect = {V, H};
-  } else if (n.compare(0, 13, "model.layers.") == 0) {
-    size_t dot = n.find('.', 13);
-    if (dot == std::string::npos) return MYOS_OK;
-    std::string idx = n.substr(13, dot - 13);
-    if (idx.empty() || idx.find_first_not_of("0123456789") != std::string::npos) return MYOS_OK;
-    if (idx.size() > 1 && idx[0] == '0') return MYOS_OK;
-    unsigned long li = strtoul(idx.c_str(), nullptr, 10);
-    if (li >= s.num_layers) return MYOS_OK;
-    std::string suf = n.substr(dot + 1);
-    for (int k = 0; k < kSuffixes; ++k)
-      if (suf == kSuffix[k]) suffix = k;
-    if (suffix < 0) return MYOS_OK;  // e.g. o_proj.bias: never read
-    layer = (int)li;
-    switch (suffix) {
-      case 0: case 8: expect = {H}; break;
-      case 1: expect = {qd, H}; break;
-      case 2: expect = {qd}; break;
-      case 3: case 5: expect = {kvd, H}; break;
-      case 4: case 6: expect = {kvd}; break;
-      case 7: expect = {H, qd}; break;
-      case 9: case 10: expect = {I, H}; break;
-      case 11: expect = {H, I}; break;
-    }
-  } else {
-    return MYOS_OK;
-  }
+  // names the model never reads (e.g. o_proj.bias, the tied model's lm_head:
+  // qwen25_block.rs:290-301) are accepted and skipped
+  if (!parse_tensor_name(s, n, &layer, &suffix, &global)) return MYOS_OK;
+  const myos_tp_part p = tp_part(s, (uint32_t)c->tp_size, (uint32_t)c->tp_rank, global, suffix);
+  std::vector<uint64_t> expect = {p.rows};
+  if (p.matrix) expect.push_back(p.cols);
   if (dtype != MYOS_BF16)
     return fail(c, MYOS_ERR_WEIGHT_DTYPE, "tensor dtype is not bf16: " + n);
   unsigned __int128 numel = 1;
@@ -1330,28 +1378,32 @@ int myos_load_tensor(myos_ctx* c, const char* name, int32_t dtype, const int64_t
     for (uint64_t r = 0; r < nrows; ++r) memcpy(&tmp[r * ld], src + (r * ncols + c0) * 2, nc * 2);
     return stage_h2d(c, dst, tmp.data(), tmp.size() * 2);
   };
-  const uint64_t rk = (uint64_t)c->tp_rank, qdl = c->qd, kvdl = c->kvd, Ic = c->i_cut,
-                 Il = c->s.intermediate;
+  auto vec = [&](float* dst) { return stage_bf16_as_f32(c, dst, src + p.row0 * 2, p.nrows); };
+  auto mat = [&](void* dst) {
+    if (p.col0 == 0 && p.ncols == p.cols) return rows(dst, p.row0, p.nrows, p.cols);
+    return cols((uint16_t*)dst, p.rows, p.cols, p.col0, p.ncols, p.store_cols);
+  };
+  const uint64_t qdl = c->qd, kvdl = c->kvd;
   int st = MYOS_OK;
-  if (global == 0) st = stage_h2d(c, c->embed, bytes, nbytes);
-  else if (global == 1) st = stage_bf16_as_f32(c, c->final_norm, bytes, H);
-  else if (global == 2) st = rows(c->lm_head, c->head_row0, c->head_rows, H);
+  if (global == 0) st = mat(c->embed);
+  else if (global == 1) st = vec(c->final_norm);
+  else if (global == 2) st = mat(c->lm_head);
   else {
     const LayerW& w = c->layers[layer];
     switch (suffix) {
-      case 0: st = stage_bf16_as_f32(c, w.ln1, bytes, H); break;
-      case 1: st = rows(w.wqkv, rk * qdl, qdl, H); break;
-      case 2: st = stage_bf16_as_f32(c, w.bqkv, src + rk * qdl * 2, qdl); break;
-      case 3: st = rows(w.wqkv + qdl * H, rk * kvdl, kvdl, H); break;
-      case 4: st = stage_bf16_as_f32(c, w.bqkv + qdl, src + rk * kvdl * 2, kvdl); break;
-      case 5: st = rows(w.wqkv + (qdl + kvdl) * H, rk * kvdl, kvdl, H); break;
-      case 6: st = stage_bf16_as_f32(c, w.bqkv + qdl + kvdl, src + rk * kvdl * 2, kvdl); break;
-      case 7: st = cols(w.wo, H, qd, rk * qdl, qdl, c->qd_pad); break;
-      case 8: st = stage_bf16_as_f32(c, w.ln2, bytes, H); break;
-      case 9: st = rows(w.wg, rk * Ic, Ic, H); break;
-      case 10: st = rows(w.wu, rk * Ic, Ic, H); break;
+      case 0: st = vec(w.ln1); break;
+      case 1: st = mat(w.wqkv); break;
+      case 2: st = vec(w.bqkv); break;
+      case 3: st = mat(w.wqkv + qdl * H); break;
+      case 4: st = vec(w.bqkv + qdl); break;
+      case 5: st = mat(w.wqkv + (qdl + kvdl) * H); break;
+      case 6: st = vec(w.bqkv + qdl + kvdl); break;
+      case 7: st = mat(w.wo); break;
+      case 8: st = vec(w.ln2); break;
+      case 9: st = mat(w.wg); break;
+      case 10: st = mat(w.wu); break;
       case 11:
-        st = cols(w.wd, H, I, rk * Ic, Ic, Il);
+        st = mat(w.wd);
         if (!st && c->mlp_wd)  // the fused MLP's copy, by block
           CK(launch_mlp_relayout(w.wd, c->mlp_wd + (size_t)layer * H * I, (int)H, (int)I, c->copy_st));
         break;
@@ -1538,6 +1590,22 @@ int myos_profile_kernels(myos_ctx* c, int iters, float* ms_out, double* bytes_ou
   CK(cudaMemcpyAsync(c->ctl, &saved, sizeof saved, cudaMemcpyHostToDevice, c->st));
   CK(cudaMemcpyAsync(c->logits, saved_logits.data(), c->s.vocab * 4, cudaMemcpyHostToDevice, c->st));
   return finish(c);
+}
+
+int myos_tp_slice(const myos_shape* shape, int32_t size, int32_t rank, const char* name,
+                  myos_tp_part* out) {
+  if (!shape || !name || !out) return MYOS_ERR_ARG;
+  if (size < 1 || size > kMaxTp || rank < 0 || rank >= size) return MYOS_ERR_ARG;
+  if (check_shape(*shape)) return MYOS_ERR_SHAPE;
+  const uint32_t N = (uint32_t)size;
+  if (shape->num_q_heads % N || shape->num_kv_heads % N || shape->intermediate % N ||
+      shape->vocab % N || ((shape->num_q_heads / N) * shape->head_dim) % 8)
+    return MYOS_ERR_SHAPE;
+  *out = myos_tp_part{};
+  int layer, suffix, global;
+  if (!parse_tensor_name(*shape, name, &layer, &suffix, &global)) return MYOS_OK;  // kept = 0
+  *out = tp_part(*shape, N, (uint32_t)rank, global, suffix);
+  return MYOS_OK;
 }
 
 int myos_launch_count(uint64_t* out) {

@@ -73,6 +73,15 @@ class TP(C.Structure):
     ]
 
 
+class TPPart(C.Structure):
+    """myos_tp_part: how a tensor-parallel rank holds one tensor."""
+    _fields_ = [(n, C.c_uint64) for n in ("rows", "cols", "row0", "nrows", "col0", "ncols",
+                                          "store_rows", "store_cols")] + [
+        ("matrix", C.c_int32),
+        ("kept", C.c_int32),
+    ]
+
+
 # Every symbol include/myos_cuda.h declares, with (restype, argtypes).
 SIGNATURES = {
     "myos_version": (C.c_char_p, []),
@@ -82,6 +91,8 @@ SIGNATURES = {
     "myos_ctx_create_tp": (C.c_int, [C.POINTER(Shape), C.POINTER(Opts), C.POINTER(TP),
                                       C.POINTER(C.c_void_p)]),
     "myos_tp_unique_id": (C.c_int, [_u8p]),
+    "myos_tp_slice": (C.c_int, [C.POINTER(Shape), C.c_int32, C.c_int32, C.c_char_p,
+                                C.POINTER(TPPart)]),
     "myos_tp_reduce_selftest": (C.c_int, [C.c_int32, C.c_uint32, C.c_uint32, C.c_int32,
                                           C.c_uint32, _f32p]),
     "myos_ctx_destroy": (None, [C.c_void_p]),

@@ -49,6 +49,8 @@ def _lib_synth():
                                             C.c_void_p, C.c_size_t, C.c_int]
         L.myos_synth_uniform_u32.argtypes = [C.c_uint64, C.c_uint64, C.c_uint32, C.c_void_p,
                                              C.c_size_t]
+        L.myos_synth_normal_bf16_block.argtypes = [C.c_uint64, C.c_uint64, C.c_float, C.c_float,
+                                                   C.c_void_p] + [C.c_size_t] * 6 + [C.c_int]
         _synth = L
     return _synth
 
@@ -98,6 +100,19 @@ def normal_bf16(seed: int, stream: int, n: int, mean: float, std: float,
     out = np.empty(n, np.uint16)
     _lib_synth().myos_synth_normal_bf16(seed, stream, mean, std,
                                         out.ctypes.data_as(C.c_void_p), n, threads)
+    return out
+
+
+def normal_bf16_block(seed: int, stream: int, rows: int, cols: int, row0: int, nrows: int,
+                      col0: int, ncols: int, mean: float, std: float,
+                      threads: int = 0) -> np.ndarray:
+    """A rows x cols buffer holding only block [row0, +nrows) x [col0, +ncols)
+    of normal_bf16(seed, stream, rows * cols, ...) (same values); the rest
+    is uninitialised."""
+    out = np.empty(rows * cols, np.uint16)
+    _lib_synth().myos_synth_normal_bf16_block(seed, stream, mean, std,
+                                              out.ctypes.data_as(C.c_void_p), rows, cols, row0,
+                                              nrows, col0, ncols, threads)
     return out
 
 

@@ -39,13 +39,38 @@ def reduce_selftest(n: int, H: int, fill: bool, timeout_ms: int = 1000, device: 
     return st, (out if fill else None)
 
 
-def load_synth(e: Engine, shape: dict, seed: int, threads: int = 0) -> None:
+def slice_of(shape: dict, size: int, rank: int, name: str):
+    """myos_tp_slice: how rank `rank` of `size` holds tensor `name` (a
+    myos_tp_part with rows, cols, row0, nrows, col0, ncols, store_rows,
+    store_cols, matrix, kept)."""
+    from . import _lib
+    import ctypes as C
+    L = _lib.load()
+    part = _lib.TPPart()
+    from .engine import shape_from_dict
+    st = L.myos_tp_slice(C.byref(shape_from_dict(shape)), int(size), int(rank),
+                         name.encode(), C.byref(part))
+    if st != 0:
+        raise ValueError("myos_tp_slice(%s, %d, %d) failed: %d" % (name, size, rank, st))
+    return part
+
+
+def load_synth(e: Engine, shape: dict, seed: int, threads: int = 0, size: int = 1,
+               rank: int = 0) -> None:
     """The seeded weights of ``synth.weights`` one tensor at a time (host
-    memory: the largest tensor, not the model)."""
+    memory: the largest tensor, not the model). With size > 1 only the block
+    of each tensor that this rank keeps (myos_tp_slice) is generated; the
+    library reads nothing else of the buffer it is given."""
     for stream, (name, dims, is_norm) in enumerate(synth.tensor_specs(shape)):
-        n = int(np.prod(dims))
         mean, std = (1.0, 0.01) if is_norm else (0.0, 0.02)
-        data = synth.normal_bf16(seed, stream, n, mean, std, threads)
+        if size > 1:
+            p = slice_of(shape, size, rank, name)
+            if not p.kept:
+                continue
+            data = synth.normal_bf16_block(seed, stream, p.rows, p.cols, p.row0, p.nrows,
+                                           p.col0, p.ncols, mean, std, threads)
+        else:
+            data = synth.normal_bf16(seed, stream, int(np.prod(dims)), mean, std, threads)
         e.load_tensor(name, tuple(dims), data.view(np.uint8))
 
 
@@ -59,7 +84,7 @@ def run_rank(size: int, rank: int, uid: bytes, shape: dict, seed: int, n_prompt:
     e = Engine(shape, n_prompt + n_gen, device=rank if device is None else device, kv_dtype=kv,
                tp=(size, rank, uid))
     try:
-        load_synth(e, shape, seed, threads)
+        load_synth(e, shape, seed, threads, size, rank)
         out = {"prefill_ms": [], "decode_ms": []}
         for it in range(iters):
             e.reset()

@@ -82,6 +82,21 @@ pub mod ffi {
     }
 
     #[repr(C)]
+    #[derive(Clone, Copy, Debug, Default, PartialEq)]
+    pub struct myos_tp_part {
+        pub rows: u64,
+        pub cols: u64,
+        pub row0: u64,
+        pub nrows: u64,
+        pub col0: u64,
+        pub ncols: u64,
+        pub store_rows: u64,
+        pub store_cols: u64,
+        pub matrix: i32,
+        pub kept: i32,
+    }
+
+    #[repr(C)]
     pub struct myos_ctx {
         _private: [u8; 0],
     }
@@ -93,6 +108,7 @@ pub mod ffi {
         pub fn myos_ctx_create(shape: *const myos_shape, opts: *const myos_opts, out: *mut *mut myos_ctx) -> c_int;
         pub fn myos_ctx_destroy(ctx: *mut myos_ctx);
         pub fn myos_tp_unique_id(out: *mut u8) -> c_int;
+        pub fn myos_tp_slice(shape: *const myos_shape, size: i32, rank: i32, name: *const c_char, out: *mut myos_tp_part) -> c_int;
         pub fn myos_tp_reduce_selftest(device: i32, n: u32, h: u32, fill: i32, timeout_ms: u32, out: *mut f32) -> c_int;
         pub fn myos_ctx_create_tp(shape: *const myos_shape, opts: *const myos_opts, tp: *const myos_tp, out: *mut *mut myos_ctx) -> c_int;
         pub fn myos_last_error(ctx: *const myos_ctx) -> *const c_char;

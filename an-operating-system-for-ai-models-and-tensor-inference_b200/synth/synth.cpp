@@ -110,6 +110,28 @@ void myos_synth_normal_bf16(uint64_t seed, uint64_t stream, float mean, float st
   });
 }
 
+// Block [row0, row0 + nrows) x [col0, col0 + ncols) of the rows x cols
+// tensor myos_synth_normal_bf16 makes, written at its place in out (a
+// rows x cols buffer); the rest of out is left as it was. Same values as the
+// whole tensor (element i is a pure function of seed, stream and i).
+void myos_synth_normal_bf16_block(uint64_t seed, uint64_t stream, float mean, float std_dev,
+                                  uint16_t* out, size_t rows, size_t cols, size_t row0,
+                                  size_t nrows, size_t col0, size_t ncols, int threads) {
+  if (nrows == 0 || ncols == 0 || row0 + nrows > rows || col0 + ncols > cols) return;
+  parallel_for(nrows, default_threads(threads), [&](size_t a, size_t b) {
+    for (size_t r = row0 + a; r < row0 + b; ++r) {
+      const size_t first = r * cols + col0, last = first + ncols;  // elements [first, last)
+      for (size_t p = first / 2; 2 * p < last; ++p) {
+        double z0, z1;
+        normal_pair(p, stream, seed, &z0, &z1);
+        const size_t i = 2 * p;
+        if (i >= first) out[i] = f32_to_bf16_rne((float)((double)mean + (double)std_dev * z0));
+        if (i + 1 < last) out[i + 1] = f32_to_bf16_rne((float)((double)mean + (double)std_dev * z1));
+      }
+    }
+  });
+}
+
 // f32 variant (activations for the GEMV microbench).
 void myos_synth_normal_f32(uint64_t seed, uint64_t stream, float mean, float std_dev, float* out,
                            size_t n, int threads) {

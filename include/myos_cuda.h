@@ -146,6 +146,33 @@ int myos_tp_unique_id(uint8_t out[128]);
  * counterpart. */
 int myos_tp_reduce_selftest(int32_t device, uint32_t n, uint32_t H, int32_t fill,
                             uint32_t timeout_ms, float* out);
+
+/* How a tensor-parallel rank holds one named tensor of the whole model:
+ * of the [rows, cols] tensor (matrix = 0: a vector, cols = 1) it keeps rows
+ * [row0, row0 + nrows) and columns [col0, col0 + ncols), stored in an
+ * extent of store_rows x store_cols whose extra rows/columns are zero (the
+ * o_proj input and MLP widths are padded to multiples of 256). Heads (q/k/v
+ * rows, o_proj columns), MLP columns (gate/up rows, down_proj columns) and
+ * the untied head's vocabulary rows are split in rank order; embedding and
+ * norms are whole on every rank. kept = 0: the model never reads the
+ * tensor. This is the slicing myos_load_tensor applies to the whole tensor
+ * it is given, so a loader can produce just the kept part (the rest of the
+ * buffer it passes is not read). No counterpart in the reference, which
+ * runs the whole model in one process. */
+typedef struct myos_tp_part {
+  uint64_t rows;
+  uint64_t cols;
+  uint64_t row0;
+  uint64_t nrows;
+  uint64_t col0;
+  uint64_t ncols;
+  uint64_t store_rows;
+  uint64_t store_cols;
+  int32_t matrix;
+  int32_t kept;
+} myos_tp_part;
+int myos_tp_slice(const myos_shape* shape, int32_t size, int32_t rank, const char* name,
+                  myos_tp_part* out);
 int myos_ctx_create_tp(const myos_shape* shape, const myos_opts* opts, const myos_tp* tp,
                        myos_ctx** out);
 const char* myos_last_error(const myos_ctx* ctx);

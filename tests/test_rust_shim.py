@@ -56,7 +56,7 @@ def test_every_c_function_has_a_matching_rust_declaration():
 
 
 def test_structs_match_field_for_field():
-    for s in ("myos_shape", "myos_opts", "myos_tp"):
+    for s in ("myos_shape", "myos_opts", "myos_tp", "myos_tp_part"):
         assert c_struct(s) == rust_struct(s), s
 
 
