@@ -1819,6 +1819,7 @@ static int batch_run(myos_ctx* c, size_t nseq, const uint32_t* ids, const uint32
     pos[b] = (int)lens[b];
   }
   CK(cudaMemcpyAsync(c->bt_pos, pos.data(), (size_t)B * 4, cudaMemcpyHostToDevice, stq));
+  CK(cudaEventRecord(c->ev2, stq));  // prompts done: prefill_ms ends, decode_ms starts
   auto head = [&](int step) -> int {
     CK(pf_norm_split(c->pf_A, c->bt_X, c->final_norm, B, H, s.rms_eps, stq));
     const cudaError_t e = gemm_bf16_f32(M, V, H, c->pf_A, head_w, nullptr, c->bt_D, 0.0f, c->pf_ws,
@@ -1876,7 +1877,8 @@ static int batch_run(myos_ctx* c, size_t nseq, const uint32_t* ids, const uint32
   for (size_t b = 0; logits && b < (size_t)B; ++b)
     for (size_t v = 0; v < (size_t)V; ++v)
       logits[b * V + v] = halves[b * V + v] + halves[(B + b) * (size_t)V + v];
-  cudaEventElapsedTime(&c->decode_ms, c->ev0, c->ev1);
+  cudaEventElapsedTime(&c->prefill_ms, c->ev0, c->ev2);
+  cudaEventElapsedTime(&c->decode_ms, c->ev2, c->ev1);
   return MYOS_OK;
 }
 

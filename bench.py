@@ -6,13 +6,20 @@ random-init BF16 weights, a 128-id uniform prompt, 128 greedy decode steps,
 batch 1. A step is one S1 request: reset, prefill the prompt, decode 128.
 Headline metric: decode tok/s (T_decode = n_gen / t_decode,
 crates/runtime/src/meter.rs:48-78), with prefill tok/s and the HBM
-roofline fraction beside it.
+roofline fraction beside it. The same line carries the other configs as
+blocks: ``gemv_micro`` (config 1: each decode matrix alone, x ~ N(0,1)),
+``long_ctx`` (config 2: 4096-id prompt + 256 steps, bf16 KV), ``dp``
+(config 3: 64 sequences of 512 + 128, split by sequence over the ranks) and
+``tp`` (config 4: Qwen2.5-14B, 512 + 128, tensor-parallel over the ranks).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                   [--n-prompt P --n-gen G]   (smaller cases for profiler captures)
+                  [--no-extra]               (S1 only)
 
-N>1 runs one independent S1 replica per GPU (the path has no exchange
-step: independent sequences, weak scaling), timed as the max over ranks.
+N>1 runs one independent S1 replica per GPU (the S1 path has no exchange
+step: independent sequences, weak scaling), timed as the max over ranks;
+the dp block splits its 64 sequences over the ranks and the tp block shards
+the 14B model over them (both: fixed total work).
 ``--impl reference`` times the reference's CPU ``--threads`` path (the C++
 restatement under oracle/, bit-identical to it on the reference's own
 known-answer tests) on the host cores, rank 0 only.
@@ -36,7 +43,12 @@ sys.path.insert(0, REPO)
 SEED = 1234
 N_PROMPT, N_GEN = 128, 128
 METRIC = "decode tok/s Qwen2.5-1.5B bf16 b=1; % HBM roofline; prefill tok/s"
-PUBLISHED_DECODE = 15.4880  # reference T_decode, knife 9, 8 threads (CPU)
+# The reference's own S1 cost card: T_decode 15.4880 tok/s on 8 CPU threads
+# (arena/s1-myos-bf16-t8-k9-cost-card.md:23).
+PUBLISHED_DECODE = 15.4880
+LONG_SEED, LONG_PROMPT, LONG_GEN = 1238, 4096, 256
+DP_SEED, DP_SEQ, DP_PROMPT, DP_GEN = 5000, 64, 512, 128
+TP_SEED, TP_PROMPT, TP_GEN = 1234, 512, 128
 
 
 def measured_peaks():
@@ -140,8 +152,10 @@ def aggregate_tok_s(world: int, tokens_per_rank_step: int, steps: int, max_ms: f
 
 
 # ---------------------------------------------------------------- CPU baseline
-def cpu_decode_sample(shape, table, prompt, n_decode: int, threads: int, max_seq: int):
-    """Reference --threads path (oracle restatement): prefill + n_decode greedy."""
+def cpu_decode_sample(shape, table, prompt, n_decode: int, threads: int, max_seq: int,
+                      decode_threads=None):
+    """Reference --threads path (oracle restatement): prefill + n_decode greedy
+    (the decode on decode_threads threads when given)."""
     from oracle import oracle as orc
     sys.path.insert(0, os.path.join(REPO, "tests"))
     import ref_fixtures as rf
@@ -153,8 +167,12 @@ def cpu_decode_sample(shape, table, prompt, n_decode: int, threads: int, max_seq
     t0 = time.perf_counter()
     assert md.prefill(wm, prompt) == 0
     t1 = time.perf_counter()
+    if decode_threads:
+        orc.set_threads(decode_threads)
+        t1 = time.perf_counter()
     st, ids, _, _ = md.greedy_decode(wm, n_decode)
     t2 = time.perf_counter()
+    orc.set_threads(threads)
     assert st == 0
     return {"t_prefill": t1 - t0, "t_decode": t2 - t1, "ids": ids}
 
@@ -167,6 +185,16 @@ def host_threads() -> int:
     return max(1, min(n, 64))  # GEMV_THREADS_MAX
 
 
+def s1_config(args, world):
+    """The config dict both arms print (the driver compares them)."""
+    return {"workload": f"S1: Qwen2.5-1.5B, {args.n_prompt}-id prompt + {args.n_gen} greedy "
+                        f"steps, batch 1",
+            "seed": SEED, "kv_dtype": args.kv,
+            "decode_positions": f"{args.n_prompt}..{args.n_prompt + args.n_gen - 1}",
+            "parallelism": f"replicas x{world} (independent sequences)",
+            "l2": "each decode step streams 3.09 GB of weights (> 126 MB L2); no flush"}
+
+
 # ---------------------------------------------------------------- arms
 def run_reference(args, world, rank):
     if rank != 0:
@@ -175,17 +203,18 @@ def run_reference(args, world, rank):
     shape = synth.shape_qwen25_1_5b()
     threads = host_threads()
     table = synth.weights(shape, SEED, threads=threads)
-    prompt = synth.prompt_ids(SEED, N_PROMPT, shape["vocab"])
-    n_dec = args.ref_decode
+    prompt = synth.prompt_ids(SEED, args.n_prompt, shape["vocab"])
+    n_dec = min(args.ref_decode, args.n_gen)
+    max_seq = args.n_prompt + args.n_gen
     for _ in range(args.warmup):
-        cpu_decode_sample(shape, table, prompt, 1, threads, N_PROMPT + N_GEN)
-    samples = [cpu_decode_sample(shape, table, prompt, n_dec, threads, N_PROMPT + N_GEN)
+        cpu_decode_sample(shape, table, prompt, 1, threads, max_seq)
+    samples = [cpu_decode_sample(shape, table, prompt, n_dec, threads, max_seq)
                for _ in range(args.steps)]
     t_dec = sum(s["t_decode"] for s in samples)
     t_pre = sum(s["t_prefill"] for s in samples)
     value = n_dec * len(samples) / t_dec
-    sample = (f"per step: prefill {N_PROMPT} ids + {n_dec} greedy decode steps of S1 "
-              f"(of {N_GEN}); {threads} threads")
+    sample = (f"per step: prefill {args.n_prompt} ids + {n_dec} greedy decode steps of S1 "
+              f"(positions {args.n_prompt}..{args.n_prompt + n_dec - 1}); {threads} threads")
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "tok/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -193,9 +222,8 @@ def run_reference(args, world, rank):
         "higher_is_better": True, "scaling": "weak",
         "vs_baseline": round(value / PUBLISHED_DECODE, 4), "dtype": "bf16 weights, f32 compute",
         "data": "synthetic (seeded random-init Qwen2.5-1.5B weights, uniform prompt ids)",
-        "config": {"workload": "S1: Qwen2.5-1.5B, 128-id prompt + 128 greedy steps, batch 1",
-                   "seed": SEED, "parallelism": "cpu row-split threads"},
-        "prefill_tok_s": round(N_PROMPT * len(samples) / t_pre, 3),
+        "config": s1_config(args, world),
+        "prefill_tok_s": round(args.n_prompt * len(samples) / t_pre, 3),
         "cpu_baseline": {"value": round(value, 4), "unit": "tok/s", "cores": threads,
                          "kind": "port", "sample": sample},
         "e2e": {"value": round(value, 4), "unit": "tok/s", "h2d_bytes_per_step": 0,
@@ -203,6 +231,178 @@ def run_reference(args, world, rank):
     }
     print(json.dumps(line))
     return 0
+
+
+# ---------------------------------------------------------------- extra blocks
+def gemv_micro(local: int, peak: float) -> dict:
+    """Config 1: each 1.5B decode matrix alone through myos_dev_gemv_bf16,
+    bf16 W ~ N(0, 0.02), f32 x ~ N(0, 1). Launches run back to back over
+    enough copies of the matrix that together exceed the 126 MB L2 (each
+    launch reads a copy the previous ones evicted); CUDA events around the
+    whole run on the launching stream, divided by the launch count."""
+    import ctypes as C
+
+    import torch
+
+    from myos import _lib
+    L = _lib.load()
+    dev = torch.device("cuda", local)
+    torch.manual_seed(SEED)
+    st = torch.cuda.current_stream(dev)
+    mats = [("W_q", 1536, 1536), ("W_k", 256, 1536), ("W_v", 256, 1536), ("W_o", 1536, 1536),
+            ("gate_up", 2 * 8960, 1536), ("down", 1536, 8960), ("lm_head", 151936, 1536)]
+    out = {}
+    for name, m, k in mats:
+        nbytes_w = m * k * 2
+        copies = max(2, -(-(320 << 20) // nbytes_w))  # > 2.5 x L2 in total
+        w = (torch.randn(copies, m, k, device=dev) * 0.02).to(torch.bfloat16)
+        x = torch.randn(k, device=dev, dtype=torch.float32)
+        y = torch.empty(copies, m, device=dev, dtype=torch.float32)
+
+        def call(i):
+            rc = L.myos_dev_gemv_bf16(C.c_void_p(y[i].data_ptr()), C.c_void_p(w[i].data_ptr()),
+                                      C.c_void_p(x.data_ptr()), m, k, C.c_void_p(st.cuda_stream))
+            if rc != 0:
+                raise RuntimeError(f"myos_dev_gemv_bf16 {name}: status {rc}")
+
+        for i in range(copies):
+            call(i)
+        n = max(copies, 40)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for j in range(n):
+            call(j % copies)
+        e1.record(st)
+        e1.synchronize()
+        ms = e0.elapsed_time(e1) / n
+        ref = w[0].float() @ x
+        err = float((y[0] - ref).abs().max() / ref.abs().max())
+        nbytes = nbytes_w + k * 4 + m * 4
+        out[name] = {"m": m, "k": k, "us": round(ms * 1e3, 2),
+                     "gbs": round(nbytes / (ms / 1e3) / 1e9, 1),
+                     "frac": round(nbytes / (ms / 1e3) / 1e9 / peak, 4),
+                     "max_rel_err_vs_torch_f32": float(f"{err:.3g}")}
+        del w, x, y
+    torch.cuda.empty_cache()
+    out["note"] = ("y = W x alone (the engine fuses the q/k/v biases and the gate|up pair into "
+                   "its kernels; gate_up here is the stacked [2*8960, 1536] matrix); mean over "
+                   ">= 40 back-to-back launches reading rotating copies (> 2.5x L2), launch "
+                   "overhead included")
+    return out
+
+
+def long_ctx(shape, table, local: int) -> dict:
+    """Config 2: 4096-id prompt, 256 greedy steps, bf16 KV cache of 4352 slots."""
+    import myos
+    from myos import synth
+    prompt = synth.prompt_ids(LONG_SEED, LONG_PROMPT, shape["vocab"])
+    e = myos.Engine(shape, LONG_PROMPT + LONG_GEN, device=local, kv_dtype="bf16")
+    try:
+        e.load_table(table)
+        e.reset()
+        e.prefill(prompt, want_logits=False)
+        e.greedy_decode(32)  # graphs captured, clocks up
+        e.reset()
+        e.prefill(prompt, want_logits=False)
+        p_ms, _ = e.last_timing()
+        e.greedy_decode(LONG_GEN)
+        _, d_ms = e.last_timing()
+        e.reset()
+        e.prefill(prompt, want_logits=False)
+        prof = e.profile_kernels(iters=2)
+    finally:
+        e.close()
+    return {"workload": f"{LONG_PROMPT}-id prompt (seed {LONG_SEED}) + {LONG_GEN} greedy steps, "
+                        f"bf16 KV, {LONG_PROMPT + LONG_GEN} slots",
+            "prefill_tok_s": round(LONG_PROMPT / (p_ms / 1e3), 1),
+            "decode_tok_s": round(LONG_GEN / (d_ms / 1e3), 2),
+            "attention_us_at_4097_keys": round(prof["attention"][0] * 1e3, 2),
+            "kernels_us": {k: round(v[0] * 1e3, 2) for k, v in prof.items()}}
+
+
+def dp_block(shape, table, world, rank, local, pg) -> dict:
+    """Config 3: 64 sequences of 512 + 128 split by sequence over the ranks,
+    each rank's share decoded as one batch (myos_batch_generate); device
+    time of the slowest rank, prefill and decode separately."""
+    import myos
+    from myos import dp
+    idx = dp.shard(DP_SEQ, world, rank)
+    prompts = dp.prompts_for(idx, DP_PROMPT, shape["vocab"], DP_SEED)
+    e = myos.Engine(shape, DP_PROMPT + DP_GEN, device=local)
+    try:
+        e.load_table(table)
+        e.batch_generate(prompts[:2], 4)  # warm
+        barrier(pg)
+        e.batch_generate(prompts, DP_GEN)
+        p_ms, d_ms = e.last_timing()
+    finally:
+        e.close()
+    p_ms = max_over_ranks(pg, p_ms, local)
+    d_ms = max_over_ranks(pg, d_ms, local)
+    return {"workload": f"{DP_SEQ} sequences x ({DP_PROMPT}-id prompt + {DP_GEN} greedy steps), "
+                        f"split by sequence over {world} rank(s), batched GEMM decode, f32 KV",
+            "sequences_per_rank": len(idx), "prefill_ms": round(p_ms, 2),
+            "decode_ms": round(d_ms, 2),
+            "decode_tok_s": round(DP_SEQ * DP_GEN / (d_ms / 1e3), 1),
+            "ms_per_step": round(d_ms / DP_GEN, 3),
+            "scaling": "strong (64 sequences in total at every N)"}
+
+
+def tp_block(world, rank, local, pg) -> dict:
+    """Config 4: Qwen2.5-14B (untied head), 512 + 128, tensor-parallel over
+    the ranks (peer-memory exchange after o_proj and down_proj). Each rank
+    generates only its slice of the seeded weights."""
+    import myos
+    from myos import synth
+    from myos.engine import tp_unique_id
+    from myos.tp import load_synth
+    shape = synth.shape_qwen25_14b()
+    prompt = synth.prompt_ids(TP_SEED, TP_PROMPT, shape["vocab"])
+    if world > 1:
+        import torch
+        uid = [tp_unique_id() if rank == 0 else None]
+        pg.broadcast_object_list(uid, src=0, group=pg.new_group(backend="gloo"))
+        tp = (world, rank, uid[0])
+    else:
+        tp = None
+    e = myos.Engine(shape, TP_PROMPT + TP_GEN, device=local, tp=tp)
+    try:
+        t0 = time.perf_counter()
+        load_synth(e, shape, TP_SEED, max(1, host_threads() // world), world, rank)
+        load_s = time.perf_counter() - t0
+        e.reset()
+        e.prefill(prompt, want_logits=False)
+        e.greedy_decode(16)  # graphs captured
+        barrier(pg)
+        e.reset()
+        e.prefill(prompt, want_logits=False)
+        p_ms, _ = e.last_timing()
+        ids = e.greedy_decode(TP_GEN)
+        _, d_ms = e.last_timing()
+    finally:
+        e.close()
+    p_ms = max_over_ranks(pg, p_ms, local)
+    d_ms = max_over_ranks(pg, d_ms, local)
+    out = {"workload": f"Qwen2.5-14B, {TP_PROMPT}-id prompt + {TP_GEN} greedy steps, batch 1, "
+                       f"tensor-parallel x{world}, f32 KV",
+           "ranks": world, "prefill_tok_s": round(TP_PROMPT / (p_ms / 1e3), 1),
+           "decode_tok_s": round(TP_GEN / (d_ms / 1e3), 2),
+           "ms_per_token": round(d_ms / TP_GEN, 4), "weight_load_s": round(load_s, 1),
+           "ids_head": [int(i) for i in ids[:8]],
+           "scaling": "strong (one 14B sequence at every N)"}
+    gold = os.path.join(REPO, "tests", "golden", "q14b_512.npz")
+    if os.path.exists(gold):  # the oracle's greedy ids for this prompt (first 16 steps)
+        import numpy as np
+        g = np.load(gold)
+        if int(g["n_prompt"]) == TP_PROMPT and int(g["weight_seed"]) == TP_SEED and \
+                int(g["prompt_seeds"][0]) == TP_SEED:
+            want, gap = np.asarray(g["ids"])[0], np.asarray(g["gap"])[0]
+            n = min(len(want), len(ids))
+            k = next((i for i in range(n) if int(ids[i]) != int(want[i])), n)
+            out["ids_match_oracle_golden_prefix"] = f"{k} of {n}"
+            if k < n:  # a divergence is allowed only at a near tie of the oracle's logits
+                out["divergence_at_near_tie"] = bool(gap[k] < 1e-2)
+    return out
 
 
 def run_ours(args, world, rank, local, pg):
@@ -237,12 +437,14 @@ def run_ours(args, world, rank, local, pg):
     barrier(pg)
     clocks = ClockSampler(local)
     clocks.start()
+    launches0 = eng.launch_count()
     pre_ms, dec_ms = [], []
     ids = None
     for _ in range(args.steps):
         p, d, ids = one_step()
         pre_ms.append(p)
         dec_ms.append(d)
+    launches = eng.launch_count() - launches0
     clk = clocks.stop()
     barrier(pg)
     tot_dec = max_over_ranks(pg, sum(dec_ms), local)
@@ -260,17 +462,26 @@ def run_ours(args, world, rank, local, pg):
     wall = max_over_ranks(pg, time.perf_counter() - t0, local)
     e2e = world * n_gen * args.steps / wall
 
-    # dominant kernel (gate/up GEMV: ~60% of the weight bytes) timed alone
+    # per-kind kernels timed alone (back to back with PDL, as in the step);
+    # the dominant one is the kind with the most device time per token
     eng.reset()
     eng.prefill(prompt, want_logits=False)
     prof = eng.profile_kernels(iters=3)
     peak, peak_kind = measured_peaks()
-    gu_ms, gu_bytes = prof["gate_up"]
-    achieved = gu_bytes / (gu_ms / 1000.0) / 1e9
+    per_token = {k: v[0] * (1 if k == "head" else shape["num_layers"]) for k, v in prof.items()}
+    dom = max(per_token, key=per_token.get)
+    dom_ms, dom_bytes = prof[dom]
+    fused_mlp = dom == "gate_up" and prof["down"][0] == 0.0
+    labels = {"gate_up": ("fused MLP (RMSNorm, gate|up, SiLU*up, down_proj, residual; k_mlp)"
+                          if fused_mlp else "gate_up GEMV (RMSNorm+gate|up+SiLU*up)"),
+              "head": "head GEMV + argmax", "qkv": "qkv GEMV", "down": "down GEMV",
+              "o_proj": "o_proj GEMV", "attention": "decode attention"}
+    achieved = dom_bytes / (dom_ms / 1000.0) / 1e9
     traffic = None
     tp = os.path.join(REPO, "profiles", "traffic.json")
     if os.path.exists(tp):
-        traffic = json.load(open(tp)).get("gate_up_bytes_per_launch")
+        tj = json.load(open(tp))
+        traffic = tj.get("mlp_bytes_per_launch" if fused_mlp else f"{dom}_bytes_per_launch")
     step_bytes = synth.weight_bytes(shape)
     step_gbs = step_bytes * n_gen * args.steps / (sum(dec_ms) / 1000.0) / 1e9
 
@@ -278,50 +489,67 @@ def run_ours(args, world, rank, local, pg):
     if rank == 0 and world == 1 and not args.no_cpu:
         t = host_threads()
         smp = cpu_decode_sample(shape, table, prompt, args.cpu_decode, t, n_prompt + n_gen)
+        figs = {}
+        for nt, nd in ((8, 8), (1, 2)):  # the reference's default --threads 8, and one thread
+            sm = cpu_decode_sample(shape, table, prompt, nd, t, n_prompt + n_gen, decode_threads=nt)
+            figs[f"threads_{nt}"] = {"decode_tok_s": round(nd / sm["t_decode"], 4),
+                                     "sample": f"{nd} greedy steps after the {n_prompt}-id prefill"}
         cpu = {"value": round(args.cpu_decode / smp["t_decode"], 4), "unit": "tok/s", "cores": t,
                "kind": "port",
                "sample": f"prefill {n_prompt} ids + {args.cpu_decode} greedy steps of S1 on the "
                          f"reference's --threads path restated in C++ (oracle/), {t} threads",
                "prefill_tok_s": round(n_prompt / smp["t_prefill"], 3),
-               "ids_match_gpu_prefix": bool(np.array_equal(smp["ids"], ids[:args.cpu_decode]))}
+               "ids_match_gpu_prefix": bool(np.array_equal(smp["ids"], ids[:args.cpu_decode])),
+               **figs}
+    eng.close()
+
+    blocks = {}
+    if not args.no_extra:
+        if world == 1 and rank == 0:
+            blocks["gemv_micro"] = gemv_micro(local, peak)
+            blocks["long_ctx"] = long_ctx(shape, table, local)
+        blocks["dp"] = dp_block(shape, table, world, rank, local, pg)
+        del table
+        blocks["tp"] = tp_block(world, rank, local, pg)
 
     if rank == 0:
-        launches_per_token = 5 * shape["num_layers"] + 1
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world,
             "steps": args.steps, "warmup": max(args.warmup, 3),
             "ms_per_step": round((tot_pre + tot_dec) / args.steps, 3),
             "higher_is_better": True, "scaling": "weak",
             "vs_baseline": round(value / PUBLISHED_DECODE, 2),
-            "dtype": "bf16 weights, f32 activations/accumulate",
+            "dtype": "bf16 weights, f32 activations/accumulate (prefill: activations as hi+lo "
+                     "bf16 pairs into the tensor cores, 16 of 24 mantissa bits)",
             "data": "synthetic (seeded random-init Qwen2.5-1.5B BF16 weights, uniform prompt ids)",
-            "config": {"workload": f"S1: Qwen2.5-1.5B, {n_prompt}-id prompt + {n_gen} greedy "
-                                   f"steps, batch 1",
-                       "seed": SEED, "kv_dtype": args.kv,
-                       "parallelism": f"replicas x{world} (independent sequences)",
-                       "l2": "each decode step streams 3.09 GB of weights (> 126 MB L2); no flush"},
+            "config": s1_config(args, world),
             "prefill_tok_s": round(prefill_tps, 1),
             "decode_ms_per_token": round(tot_dec / (args.steps * n_gen), 4),
             "step_hbm": {"bytes_per_token": step_bytes, "achieved_gbs": round(step_gbs, 1),
                          "frac_of_measured": round(step_gbs / peak, 4),
                          "frac_of_8tbs_nominal": round(step_gbs / 8000.0, 4)},
-            "roofline": {"bound": "hbm", "kernel": "gate_up GEMV (RMSNorm+gate|up+SiLU*up)",
+            "roofline": {"bound": "hbm", "kernel": labels.get(dom, dom),
                          "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "traffic": traffic,
+                         "traffic_source": "profiles/traffic.json (one ncu capture, per launch)",
                          "peak_source": peak_kind,
-                         "bytes_per_launch": gu_bytes, "ms_per_launch": round(gu_ms, 5)},
-            "kernels": {k: {"ms": round(v[0], 5), "gbs": round(v[1] / (v[0] / 1000) / 1e9, 1)}
+                         "bytes_per_launch": dom_bytes, "ms_per_launch": round(dom_ms, 5),
+                         "share_of_token": round(per_token[dom] / (tot_dec / (args.steps * n_gen)), 4)},
+            "kernels": {k: {"ms": round(v[0], 5),
+                            "gbs": round(v[1] / (v[0] / 1000) / 1e9, 1) if v[0] else None}
                         for k, v in prof.items()},
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": n_prompt * 4,
                     "d2h_bytes_per_step": n_gen * 4,
                     "note": "generated tokens / wall time of reset+prefill(host ids)+"
                             "greedy_decode(host ids) through the C ABI"},
-            "gpu_launches": launches_per_token * (n_prompt + n_gen) * args.steps,
+            "gpu_launches": launches,
+            "gpu_launches_note": "kernels this rank's library enqueued in the timed region "
+                                 "(myos_launch_count; graph replays count their kernels)",
             "clocks": clk,
         }
+        line.update(blocks)
         print(json.dumps(line))
-    eng.close()
     return 0
 
 
@@ -333,8 +561,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--kv", choices=["f32", "bf16"], default="f32")
     ap.add_argument("--cpu-decode", type=int, default=16)
-    ap.add_argument("--ref-decode", type=int, default=8)
+    ap.add_argument("--ref-decode", type=int, default=N_GEN)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-extra", action="store_true")
     ap.add_argument("--n-prompt", type=int, default=N_PROMPT)
     ap.add_argument("--n-gen", type=int, default=N_GEN)
     args = ap.parse_args()
