@@ -1151,7 +1151,7 @@ static int create_impl(myos_ctx* c, const myos_shape* shape, const myos_opts* op
     for (size_t l = 0; ok && l < L; ++l) ok = c->layers[l].wu == c->layers[l].wg + I * H;
     if (ok) {
       const int nc = 128;
-      const size_t M = 2 * (size_t)nc;
+      const size_t M = kSplitParts * (size_t)nc;
       const size_t kmax = std::max(H, std::max((size_t)c->qd, I));
       const size_t nmax = std::max(c->qd + 2 * c->kvd, std::max(H, 2 * I));
       const int shapes[4][2] = {{(int)(c->qd + 2 * c->kvd), (int)H}, {(int)H, (int)c->qd},
@@ -1676,7 +1676,7 @@ int prefill_chunk(myos_ctx* c, const uint32_t* d_ids, int n, int p0, void* kcach
   const myos_shape& s = c->s;
   const int H = (int)s.hidden, I = (int)s.intermediate, qd = (int)c->qd;
   const int Nq = (int)(c->qd + 2 * c->kvd), Hq = (int)s.num_q_heads, Hkv = (int)s.num_kv_heads;
-  const int d = (int)s.head_dim, S = S_ ? S_ : (int)c->o.max_seq, M = 2 * n;
+  const int d = (int)s.head_dim, S = S_ ? S_ : (int)c->o.max_seq, M = kSplitParts * n;
   if (!kcache) {
     kcache = c->kcache;
     vcache = c->vcache;
@@ -1691,7 +1691,7 @@ int prefill_chunk(myos_ctx* c, const uint32_t* d_ids, int n, int p0, void* kcach
                                         c->pf_ws_bytes, st, ldw);
     return e == cudaSuccess ? MYOS_OK : fail(c, MYOS_ERR_CUDA, std::string("prefill gemm: ") + cudaGetErrorString(e));
   };
-  // residual += the projection (hi + lo rows of pf_D); under tensor
+  // residual += the projection (the three partial rows of pf_D); under tensor
   // parallelism each rank's part (rank 0's with the residual) is summed
   // over the ranks with one NCCL allreduce of the chunk's rows
   auto resid = [&](int rows, int N) -> int {
@@ -1757,7 +1757,7 @@ static int batch_run(myos_ctx* c, size_t nseq, const uint32_t* ids, const uint32
   CK(cudaSetDevice(c->device));
   const int B = (int)nseq, H = (int)s.hidden, I = (int)s.intermediate, qd = (int)c->qd;
   const int Nq = (int)(c->qd + 2 * c->kvd), Hq = (int)s.num_q_heads, Hkv = (int)s.num_kv_heads;
-  const int d = (int)s.head_dim, V = (int)s.vocab, L = (int)s.num_layers, M = 2 * B;
+  const int d = (int)s.head_dim, V = (int)s.vocab, L = (int)s.num_layers, M = kSplitParts * B;
   const int Sb = (int)(maxlen + steps);  // slots per sequence
   const int kv_bf16 = c->o.kv_dtype == MYOS_KV_BF16;
   const size_t kv_elt = kv_bf16 ? 2 : 4;
@@ -1868,15 +1868,16 @@ static int batch_run(myos_ctx* c, size_t nseq, const uint32_t* ids, const uint32
   CK(cudaEventRecord(c->ev1, stq));
   if (steps)
     CK(cudaMemcpyAsync(out_ids, c->bt_out, (size_t)B * steps * 4, cudaMemcpyDeviceToHost, stq));
-  std::vector<float> halves;
-  if (logits) {  // final logits: the hi and lo rows of the head GEMM summed
-    halves.resize((size_t)M * V);
-    CK(cudaMemcpyAsync(halves.data(), c->bt_D, halves.size() * 4, cudaMemcpyDeviceToHost, stq));
+  std::vector<float> parts;
+  if (logits) {  // final logits: the three partial rows of the head GEMM summed
+    parts.resize((size_t)M * V);
+    CK(cudaMemcpyAsync(parts.data(), c->bt_D, parts.size() * 4, cudaMemcpyDeviceToHost, stq));
   }
   if ((st = finish(c))) return st;
   for (size_t b = 0; logits && b < (size_t)B; ++b)
     for (size_t v = 0; v < (size_t)V; ++v)
-      logits[b * V + v] = halves[b * V + v] + halves[(B + b) * (size_t)V + v];
+      logits[b * V + v] = (parts[b * V + v] + parts[(B + b) * (size_t)V + v]) +
+                          parts[(2 * B + b) * (size_t)V + v];
   cudaEventElapsedTime(&c->prefill_ms, c->ev0, c->ev2);
   cudaEventElapsedTime(&c->decode_ms, c->ev2, c->ev1);
   return MYOS_OK;

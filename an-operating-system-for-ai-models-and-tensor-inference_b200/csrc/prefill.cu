@@ -4,11 +4,11 @@
 // RoPE and KV store, per-position causal GQA, GEMM o_proj + residual,
 // RMSNorm, GEMM gate|up, SwiGLU, GEMM down + residual.
 //
-// Activations reach the tensor cores as stacked bf16 halves: row t of A is
-// hi = bf16(x_t) and row n + t is lo = bf16(x_t - hi) (both exact
-// roundings), so D[t] + D[n + t] is the projection of the activation to 16
-// mantissa bits with exact products. The element-wise steps keep the
-// reference's operation order (no contraction).
+// Activations reach the tensor cores as three stacked bf16 terms (prefill.h
+// kSplitParts): rows t, n + t and 2n + t of A hold hi, mid and lo of x_t,
+// whose sum is x_t exactly, so (D[t] + D[n + t]) + D[2n + t] is the
+// projection of the full f32 activation with exact products. The
+// element-wise steps keep the reference's operation order (no contraction).
 #include <math.h>
 
 #include "common.cuh"
@@ -24,11 +24,21 @@ MYOS_DEV uint16_t bf16_rn(float v) {
   return __bfloat16_as_ushort(__float2bfloat16_rn(v));
 }
 
+// Row t of A's three blocks: hi, mid, lo with hi + mid + lo == y exactly.
 MYOS_DEV void put_split(uint16_t* A, int n, int t, int K, int j, float y) {
   const uint16_t hi = bf16_rn(y);
-  const float hv = __uint_as_float((uint32_t)hi << 16);
+  const float r1 = __fsub_rn(y, __uint_as_float((uint32_t)hi << 16));
+  const uint16_t mid = bf16_rn(r1);
+  const float r2 = __fsub_rn(r1, __uint_as_float((uint32_t)mid << 16));
   A[(size_t)t * K + j] = hi;
-  A[(size_t)(n + t) * K + j] = bf16_rn(__fsub_rn(y, hv));
+  A[(size_t)(n + t) * K + j] = mid;
+  A[(size_t)(2 * n + t) * K + j] = bf16_rn(r2);
+}
+
+// The projection of row t: its three partial outputs, (hi + mid) + lo.
+MYOS_DEV float part_sum(const float* D, int n, int t, int N, int j) {
+  return __fadd_rn(__fadd_rn(D[(size_t)t * N + j], D[(size_t)(n + t) * N + j]),
+                   D[(size_t)(2 * n + t) * N + j]);
 }
 
 MYOS_DEV float bsum(float v, float* red) { return block_sum(v, red); }
@@ -40,8 +50,8 @@ __global__ void k_pf_embed(float* X, const uint16_t* embed, const uint32_t* ids,
   for (int j = threadIdx.x; j < K; j += blockDim.x) X[(size_t)t * K + j] = bf16_at(row + j);
 }
 
-// A[t], A[n + t] = halves of gamma * (x * inv), inv = 1 / sqrtf(mean(x^2) + eps)
-// (bf16.rs:231-270); gamma null: halves of x.
+// A[t], A[n + t], A[2n + t] = the three bf16 terms of gamma * (x * inv),
+// inv = 1 / sqrtf(mean(x^2) + eps) (bf16.rs:231-270); gamma null: of x.
 __global__ void __launch_bounds__(kT) k_pf_norm_split(uint16_t* A, const float* X, const float* gamma,
                                                       int n, int K, float eps) {
   __shared__ float red[33];
@@ -58,12 +68,11 @@ __global__ void __launch_bounds__(kT) k_pf_norm_split(uint16_t* A, const float* 
     put_split(A, n, t, K, j, gamma ? __fmul_rn(gamma[j], __fmul_rn(x[j], inv)) : x[j]);
 }
 
-// Q[t] = (D[t] + D[n + t]) + bias: the projection, then the bias (bf16.rs:147-158).
+// Q[t] = projection + bias (bf16.rs:147-158).
 __global__ void k_pf_bias(float* Q, const float* D, const float* bias, int n, int N) {
   const int t = blockIdx.x;
   for (int j = threadIdx.x; j < N; j += blockDim.x)
-    Q[(size_t)t * N + j] =
-        __fadd_rn(__fadd_rn(D[(size_t)t * N + j], D[(size_t)(n + t) * N + j]), bias[j]);
+    Q[(size_t)t * N + j] = __fadd_rn(part_sum(D, n, t, N, j), bias[j]);
 }
 
 // NeoX rotation of token t's q heads and KV heads at position p0 + t
@@ -209,39 +218,38 @@ __global__ void __launch_bounds__(kT) k_pf_attn(float* out, const float* Q, cons
   }
 }
 
-// X[t] += D[t] + D[n + t] (residual after o_proj / down_proj).
+// X[t] += projection (residual after o_proj / down_proj).
 __global__ void k_pf_resid(float* X, const float* D, int n, int N) {
   const int t = blockIdx.x;
   for (int j = threadIdx.x; j < N; j += blockDim.x)
-    X[(size_t)t * N + j] =
-        __fadd_rn(X[(size_t)t * N + j], __fadd_rn(D[(size_t)t * N + j], D[(size_t)(n + t) * N + j]));
+    X[(size_t)t * N + j] = __fadd_rn(X[(size_t)t * N + j], part_sum(D, n, t, N, j));
 }
 
 // Tensor-parallel form: this rank's part of the residual update, written in
-// place over the hi rows of D: X + (hi + lo) on the rank that carries the
-// residual (X non-null), hi + lo elsewhere; the ranks' parts are then summed.
+// place over the hi rows of D: X + projection on the rank that carries the
+// residual (X non-null), the projection elsewhere; the ranks' parts are then summed.
 __global__ void k_pf_resid_part(float* D, const float* X, int n, int N) {
   const int t = blockIdx.x;
   for (int j = threadIdx.x; j < N; j += blockDim.x) {
-    const float dl = __fadd_rn(D[(size_t)t * N + j], D[(size_t)(n + t) * N + j]);
+    const float dl = part_sum(D, n, t, N, j);
     D[(size_t)t * N + j] = X ? __fadd_rn(X[(size_t)t * N + j], dl) : dl;
   }
 }
 
 // h = (g / (1 + expf(-g))) * u (swiglu.rs:113-131) from the stacked gate|up
-// projection, written as bf16 halves for the down projection.
+// projection, written as three bf16 terms for the down projection.
 __global__ void k_pf_swiglu_split(uint16_t* A, const float* D, int n, int I) {
   const int t = blockIdx.x, N = 2 * I;
   for (int j = threadIdx.x; j < I; j += blockDim.x) {
-    const float g = __fadd_rn(D[(size_t)t * N + j], D[(size_t)(n + t) * N + j]);
-    const float u = __fadd_rn(D[(size_t)t * N + I + j], D[(size_t)(n + t) * N + I + j]);
+    const float g = part_sum(D, n, t, N, j);
+    const float u = part_sum(D, n, t, N, I + j);
     const float s = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
     put_split(A, n, t, I, j, __fmul_rn(s, u));
   }
 }
 
-// Greedy token of each row from the stacked logit halves: logits_b[j] =
-// D[b][j] + D[B + b][j]; the first maximum with strict >, NaN and -inf never
+// Greedy token of each row from the stacked logit parts: logits_b[j] =
+// (D[b][j] + D[B + b][j]) + D[2B + b][j]; the first maximum with strict >, NaN and -inf never
 // win, none -> 0 (model_core/src/lib.rs:157-167). Records the token.
 __global__ void __launch_bounds__(kT) k_row_argmax(uint32_t* tok, uint32_t* out, int out_stride,
                                                    int step, const float* D, int B, int V) {
@@ -251,7 +259,7 @@ __global__ void __launch_bounds__(kT) k_row_argmax(uint32_t* tok, uint32_t* out,
   float bv = -INFINITY;
   uint32_t bi = 0xffffffffu;
   for (int j = threadIdx.x; j < V; j += blockDim.x) {
-    const float v = __fadd_rn(D[(size_t)b * V + j], D[(size_t)(B + b) * V + j]);
+    const float v = part_sum(D, B, b, V, j);
     if (v > bv) {  // j grows per thread: strict > keeps the first
       bv = v;
       bi = (uint32_t)j;

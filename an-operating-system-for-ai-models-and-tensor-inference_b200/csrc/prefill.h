@@ -5,6 +5,13 @@
 
 namespace myos {
 
+// Each f32 activation enters the tensor cores as the exact sum of three
+// bf16 terms (hi = bf16(x), mid = bf16(x - hi), lo = bf16(x - hi - mid):
+// 8 + 8 + 8 significand bits, every subtraction exact in f32), stacked as
+// row blocks [hi; mid; lo] of A, so one GEMM pass over the weights gives
+// three partial outputs whose sum (hi + mid) + lo the consumers form.
+constexpr int kSplitParts = 3;
+
 cudaError_t pf_embed(float* X, const uint16_t* embed, const uint32_t* ids, int n, int K,
                      cudaStream_t st);
 cudaError_t pf_norm_split(uint16_t* A, const float* X, const float* gamma, int n, int K, float eps,
@@ -19,7 +26,7 @@ bool pf_attn_supported(int d, int G);
 cudaError_t pf_attn(float* out, const float* Q, const void* kc, const void* vc, int kv_bf16, int p0,
                     int n, int Hq, int Hkv, int d, int S, float scale, cudaStream_t st,
                     const int* rowpos = nullptr, size_t rowstride = 0);
-// Greedy token per row of stacked logit halves D[2B, V]; tok[b], and
+// Greedy token per row of stacked logit parts D[3B, V]; tok[b], and
 // out[b * out_stride + step] when out is non-null.
 cudaError_t pf_row_argmax(uint32_t* tok, uint32_t* out, int out_stride, int step, const float* D,
                           int B, int V, cudaStream_t st);

@@ -297,8 +297,9 @@ int myos_dev_gemv_bf16(float* d_y, const void* d_w, const float* d_x, size_t m, 
  * ids[off_b .. off_b + lens[b]) (prompts concatenated in order);
  * out_ids[b * steps + s] receives its s-th generated id. Every prompt runs
  * through the tensor-core prefill into its own KV slab; each decode step then
- * runs the projections and the head of all sequences as GEMMs (the bf16
- * halves of nseq activations stacked, M = 2 nseq). 1 <= nseq <= 128 and
+ * runs the projections and the head of all sequences as GEMMs (each f32
+ * activation as three stacked bf16 terms that sum to it exactly,
+ * M = 3 nseq). 1 <= nseq <= 128 and
  * lens[b] + steps <= max_seq; needs a shape the GEMM prefill supports
  * (MYOS_ERR_SHAPE otherwise). The context's own cache and cursor are not
  * touched. */
