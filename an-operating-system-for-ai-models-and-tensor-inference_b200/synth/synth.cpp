@@ -71,9 +71,11 @@ inline uint16_t f32_to_bf16_rne(float f) {
   return (uint16_t)(u >> 16);
 }
 
+// fn(a, b) over [0, n) split across threads; `work` (default n) is the
+// amount of work behind the n items, and below 2^16 of it one thread runs all.
 template <class F>
-void parallel_for(size_t n, int threads, F&& fn) {
-  if (threads <= 1 || n < (1u << 16)) {
+void parallel_for(size_t n, int threads, F&& fn, size_t work = 0) {
+  if (threads <= 1 || (work ? work : n) < (1u << 16)) {
     fn(0, n);
     return;
   }
@@ -119,17 +121,28 @@ void myos_synth_normal_bf16_block(uint64_t seed, uint64_t stream, float mean, fl
                                   size_t nrows, size_t col0, size_t ncols, int threads) {
   if (nrows == 0 || ncols == 0 || row0 + nrows > rows || col0 + ncols > cols) return;
   parallel_for(nrows, default_threads(threads), [&](size_t a, size_t b) {
+    auto value = [&](double z) { return f32_to_bf16_rne((float)((double)mean + (double)std_dev * z)); };
     for (size_t r = row0 + a; r < row0 + b; ++r) {
       const size_t first = r * cols + col0, last = first + ncols;  // elements [first, last)
-      for (size_t p = first / 2; 2 * p < last; ++p) {
-        double z0, z1;
+      size_t p = first / 2;
+      double z0, z1;
+      if (first & 1) {  // the row starts with the second value of a pair
         normal_pair(p, stream, seed, &z0, &z1);
-        const size_t i = 2 * p;
-        if (i >= first) out[i] = f32_to_bf16_rne((float)((double)mean + (double)std_dev * z0));
-        if (i + 1 < last) out[i + 1] = f32_to_bf16_rne((float)((double)mean + (double)std_dev * z1));
+        out[first] = value(z1);
+        ++p;
+      }
+      const size_t pend = last / 2;  // pairs wholly inside the row
+      for (; p < pend; ++p) {  // the whole-tensor loop's body, without edge tests
+        normal_pair(p, stream, seed, &z0, &z1);
+        out[2 * p] = value(z0);
+        out[2 * p + 1] = value(z1);
+      }
+      if ((last & 1) && 2 * pend >= first) {  // the row ends with the first value of a pair
+        normal_pair(pend, stream, seed, &z0, &z1);
+        out[last - 1] = value(z0);
       }
     }
-  });
+  }, nrows * ncols);
 }
 
 // f32 variant (activations for the GEMV microbench).
