@@ -109,10 +109,12 @@ struct myos_ctx {
   // GEMM prefill (chunks of pf_chunk prompt tokens through the tensor cores)
   bool pf_ok = false;
   int pf_chunk = 0;
-  float *pf_X = nullptr, *pf_D = nullptr, *pf_Q = nullptr, *pf_att = nullptr;
+  float *pf_X = nullptr, *pf_D = nullptr, *pf_Q = nullptr;
   uint16_t* pf_A = nullptr;
   void* pf_ws = nullptr;
   size_t pf_ws_bytes = 0;
+  size_t pf_D_elems = 0;  // capacity of pf_D in floats
+  bool pf_splitk = true;  // MYOS_SPLITK=0: one K slice per projection
   // batched decode (myos_batch_generate): per-sequence KV slabs and buffers
   void *bt_k = nullptr, *bt_v = nullptr;
   size_t bt_kv_bytes = 0;
@@ -121,6 +123,11 @@ struct myos_ctx {
   int *bt_pos = nullptr, *bt_rows = nullptr;
   uint32_t *bt_tok = nullptr, *bt_out = nullptr, *bt_ids = nullptr, *bt_feed = nullptr;
   size_t bt_feed_bytes = 0;
+  float* at_o = nullptr;     // split attention partials of the GEMM path (o)
+  float2* at_ml = nullptr;   // ... and their (max, sum of exponentials)
+  size_t at_o_bytes = 0, at_ml_bytes = 0;
+  float2* bt_amax = nullptr;  // per-chunk argmax candidates of the batched head
+  size_t bt_amax_bytes = 0;
   size_t bt_out_n = 0, bt_ids_n = 0;
   size_t prefetch_total = 0;  // bulk L2 prefetch (MYOS_PREFETCH_MB); measured slower, off
   // loaded-tensor bookkeeping
@@ -1161,11 +1168,14 @@ static int create_impl(myos_ctx* c, const myos_shape* shape, const myos_opts* op
       CK(cudaMalloc(&c->pf_X, (size_t)nc * H * 4));
       CK(cudaMalloc(&c->pf_A, M * kmax * 2));
       CK(cudaMalloc(&c->pf_D, M * nmax * 4));
+      c->pf_D_elems = M * nmax;
+      const char* sk = getenv("MYOS_SPLITK");
+      c->pf_splitk = !(sk && sk[0] == '0');
       CK(cudaMalloc(&c->pf_Q, (size_t)nc * (c->qd + 2 * c->kvd) * 4));
-      CK(cudaMalloc(&c->pf_att, (size_t)nc * c->qd * 4));
       CK(cudaMalloc(&c->pf_ws, ws));
       c->pf_ws_bytes = ws;
       c->pf_chunk = nc;
+      CK(pf_init());
       c->pf_ok = true;
     }
   }
@@ -1316,9 +1326,10 @@ void myos_ctx_destroy(myos_ctx* c) {
                  c->part_val, c->part_idx, c->part_o, c->part_m, c->part_l, c->counters, c->ctl,
                  c->feed, c->rec_fed, c->rec_argmax, c->cos_t, c->sin_t, c->d_slayers, c->sflags,
                  c->s_words, (void*)c->trace, (void*)c->strace, c->mlp_part, c->mlp_arrive, c->mlp_wd,
-                 (void*)c->ktrace, c->pf_X, c->pf_D, c->pf_Q, c->pf_att, c->pf_A, c->pf_ws,
+                 (void*)c->ktrace, c->pf_X, c->pf_D, c->pf_Q, c->pf_A, c->pf_ws,
                  c->bt_k, c->bt_v, c->bt_X, c->bt_D, c->bt_pos, c->bt_rows, c->bt_tok,
-                 c->bt_out, c->bt_ids, c->bt_feed, c->tp_part, c->tp_cand, c->tp_link};
+                 c->bt_out, c->bt_ids, c->bt_feed, c->tp_part, c->tp_cand, c->tp_link,
+                 c->at_o, (void*)c->at_ml, (void*)c->bt_amax};
   for (void* p : dev)
     if (p) cudaFree(p);
   for (int i = 0; i < 2; ++i) {
@@ -1667,6 +1678,25 @@ int myos_forward_token(myos_ctx* c, uint32_t token, size_t pos, float* logits) {
   return MYOS_OK;
 }
 
+// Split-attention partials for `rows` rows of up to max_keys keys each.
+static int attn_scratch(myos_ctx* c, int rows, int max_keys) {
+  int ch = 0;
+  const size_t ns = (size_t)pf_attn_splits(max_keys, &ch);
+  const size_t heads = (size_t)rows * c->s.num_q_heads * ns;
+  int st = grow(c, &c->at_o, &c->at_o_bytes, heads * c->s.head_dim * 4);
+  if (!st) st = grow(c, &c->at_ml, &c->at_ml_bytes, heads * sizeof(float2));
+  return st;
+}
+
+// K slices for an [M, N, K] projection of the GEMM path: enough to put an
+// output tile (or slice) on every SM, bounded by pf_D's room for partials.
+static int pf_splits(const myos_ctx* c, int M, int N, int K) {
+  if (!c->pf_splitk) return 1;
+  int sp = gemm_pick_splits(M, N, K, c->num_sms);
+  while (sp > 1 && ((size_t)sp * M * N > c->pf_D_elems || (K / 64) % sp)) --sp;
+  return sp;
+}
+
 // One chunk of n prompt tokens at positions p0.. through every layer
 // (GEMM prefill); leaves the chunk's residual rows in pf_X and their K/V in
 // the cache.
@@ -1686,43 +1716,49 @@ int prefill_chunk(myos_ctx* c, const uint32_t* d_ids, int n, int p0, void* kcach
   const size_t kv_elt = kv_bf16 ? 2 : 4;
   const float scale = 1.0f / sqrtf((float)d);
   cudaStream_t st = c->st;
+  // sp: the K slices of the projection now in pf_D (split-K when its output
+  // tiles would leave SMs idle and pf_D has room for the partials)
+  int sp = 1;
   auto gemm = [&](int N, int K, const uint16_t* W, int ldw = 0) {
+    sp = pf_splits(c, M, N, K);
     const cudaError_t e = gemm_bf16_f32(M, N, K, c->pf_A, W, nullptr, c->pf_D, 0.0f, c->pf_ws,
-                                        c->pf_ws_bytes, st, ldw);
+                                        c->pf_ws_bytes, st, ldw, sp);
     return e == cudaSuccess ? MYOS_OK : fail(c, MYOS_ERR_CUDA, std::string("prefill gemm: ") + cudaGetErrorString(e));
   };
-  // residual += the projection (the three partial rows of pf_D); under tensor
-  // parallelism each rank's part (rank 0's with the residual) is summed
-  // over the ranks with one NCCL allreduce of the chunk's rows
-  auto resid = [&](int rows, int N) -> int {
+  // residual += the projection (the partial rows of pf_D), then the next
+  // RMSNorm's split input from the updated rows (gamma null: none); under
+  // tensor parallelism each rank's part (rank 0's with the residual) is
+  // summed over the ranks with one NCCL allreduce of the chunk's rows
+  auto resid = [&](int rows, int N, const float* gamma) -> int {
     if (c->tp_size == 1) {
-      CK(pf_resid(c->pf_X, c->pf_D, rows, N, st));
+      CK(pf_resid_norm(c->pf_X, c->pf_D, sp, gamma, c->pf_A, rows, N, s.rms_eps, st));
       return MYOS_OK;
     }
-    CK(pf_resid_part(c->pf_D, c->tp_rank == 0 ? c->pf_X : nullptr, rows, N, st));
+    CK(pf_resid_part(c->pf_D, c->tp_rank == 0 ? c->pf_X : nullptr, rows, N, sp, st));
     if (!tp_allreduce_sum(c->pf_D, c->pf_X, (size_t)rows * N, c->comm, st))
       return fail(c, MYOS_ERR_NCCL, "allreduce of the prefill residual failed");
+    if (gamma) CK(pf_norm_split(c->pf_A, c->pf_X, gamma, rows, N, s.rms_eps, st));
     return MYOS_OK;
   };
   int rc;
+  if ((rc = attn_scratch(c, n, p0 + n))) return rc;
   CK(pf_embed(c->pf_X, c->embed, d_ids, n, H, st));
+  CK(pf_norm_split(c->pf_A, c->pf_X, c->layers[0].ln1, n, H, s.rms_eps, st));
   for (int l = 0; l < (int)s.num_layers; ++l) {
     const LayerW& w = c->layers[l];
     void* kc = (uint8_t*)kcache + (size_t)l * layer_elems * kv_elt;
     void* vc = (uint8_t*)vcache + (size_t)l * layer_elems * kv_elt;
-    CK(pf_norm_split(c->pf_A, c->pf_X, w.ln1, n, H, s.rms_eps, st));
     if ((rc = gemm(Nq, H, w.wqkv))) return rc;
-    CK(pf_bias(c->pf_Q, c->pf_D, w.bqkv, n, Nq, st));
-    CK(pf_rope_store(c->pf_Q, kc, vc, kv_bf16, c->cos_t, c->sin_t, p0, n, Hq, Hkv, d, S, st));
-    CK(pf_attn(c->pf_att, c->pf_Q, kc, vc, kv_bf16, p0, n, Hq, Hkv, d, S, scale, st));
-    CK(pf_norm_split(c->pf_A, c->pf_att, nullptr, n, qd, 0.0f, st));
+    CK(pf_qkv_post(c->pf_Q, c->pf_D, sp, w.bqkv, kc, vc, kv_bf16, c->cos_t, c->sin_t, p0, n, Hq,
+                   Hkv, d, S, st));
+    CK(pf_attn(c->pf_A, c->at_o, c->at_ml, c->pf_Q, kc, vc, kv_bf16, p0, n, Hq, Hkv, d, S, scale,
+               p0 + n, st));
     if ((rc = gemm(H, qd, w.wo, (int)c->qd_pad))) return rc;
-    if ((rc = resid(n, H))) return rc;
-    CK(pf_norm_split(c->pf_A, c->pf_X, w.ln2, n, H, s.rms_eps, st));
+    if ((rc = resid(n, H, w.ln2))) return rc;
     if ((rc = gemm(2 * I, H, w.wg))) return rc;  // gate rows then up rows
-    CK(pf_swiglu_split(c->pf_A, c->pf_D, n, I, st));
+    CK(pf_swiglu_split(c->pf_A, c->pf_D, n, I, sp, st));
     if ((rc = gemm(H, I, w.wd))) return rc;
-    if ((rc = resid(n, H))) return rc;
+    if ((rc = resid(n, H, l + 1 < (int)s.num_layers ? c->layers[l + 1].ln1 : nullptr))) return rc;
   }
   return MYOS_OK;
 }
@@ -1784,6 +1820,11 @@ static int batch_run(myos_ctx* c, size_t nseq, const uint32_t* ids, const uint32
   c->bt_out_n = have_out / 4;
   if ((st = grow(c, &c->bt_ids, &have_ids, total * 4))) return st;
   c->bt_ids_n = have_ids / 4;
+  if ((st = grow(c, &c->bt_amax, &c->bt_amax_bytes,
+                 (size_t)B * pf_argmax_chunks(V) * sizeof(float2))))
+    return st;
+  const int max_keys = (int)(maxlen + steps);  // keys of the last step's longest row
+  if (steps && (st = attn_scratch(c, B, max_keys))) return st;
   const size_t ws = gemm_workspace_bytes(M, V, H);
   if (ws > c->pf_ws_bytes && (st = grow(c, &c->pf_ws, &c->pf_ws_bytes, ws))) return st;
   // teacher-forced tokens, transposed to [steps][nseq] so each step's column
@@ -1820,50 +1861,51 @@ static int batch_run(myos_ctx* c, size_t nseq, const uint32_t* ids, const uint32
   }
   CK(cudaMemcpyAsync(c->bt_pos, pos.data(), (size_t)B * 4, cudaMemcpyHostToDevice, stq));
   CK(cudaEventRecord(c->ev2, stq));  // prompts done: prefill_ms ends, decode_ms starts
-  auto head = [&](int step) -> int {
-    CK(pf_norm_split(c->pf_A, c->bt_X, c->final_norm, B, H, s.rms_eps, stq));
+  auto head = [&](int step, bool normed) -> int {
+    if (!normed) CK(pf_norm_split(c->pf_A, c->bt_X, c->final_norm, B, H, s.rms_eps, stq));
     const cudaError_t e = gemm_bf16_f32(M, V, H, c->pf_A, head_w, nullptr, c->bt_D, 0.0f, c->pf_ws,
                                         c->pf_ws_bytes, stq);
     if (e != cudaSuccess) return fail(c, MYOS_ERR_CUDA, std::string("batch head gemm: ") + cudaGetErrorString(e));
-    CK(pf_row_argmax(c->bt_tok, step < (int)steps ? c->bt_out : nullptr, (int)steps, step, c->bt_D, B,
-                     V, stq));
+    CK(pf_row_argmax(c->bt_tok, step < (int)steps ? c->bt_out : nullptr, (int)steps, step, c->bt_D,
+                     c->bt_amax, B, V, stq));
     return MYOS_OK;
   };
+  int sp = 1;  // K slices of the projection now in pf_D
   auto gemm = [&](int N, int K, const uint16_t* W) -> int {
-    const cudaError_t e =
-        gemm_bf16_f32(M, N, K, c->pf_A, W, nullptr, c->pf_D, 0.0f, c->pf_ws, c->pf_ws_bytes, stq);
+    sp = pf_splits(c, M, N, K);
+    const cudaError_t e = gemm_bf16_f32(M, N, K, c->pf_A, W, nullptr, c->pf_D, 0.0f, c->pf_ws,
+                                        c->pf_ws_bytes, stq, 0, sp);
     return e == cudaSuccess ? MYOS_OK : fail(c, MYOS_ERR_CUDA, std::string("batch gemm: ") + cudaGetErrorString(e));
   };
   // 2. greedy: token s of every sequence is the argmax of its current
   //    logits; each is then forwarded (model_core greedy_decode, per sequence)
-  if ((st = head(0))) return st;
+  if ((st = head(0, false))) return st;
   for (size_t step = 0; step < steps; ++step) {
     if (feed)  // teacher-forced: this step embeds the given token, not the argmax
       CK(cudaMemcpyAsync(c->bt_tok, c->bt_feed + step * B, (size_t)B * 4, cudaMemcpyDeviceToDevice,
                          stq));
     CK(pf_embed(c->bt_X, c->embed, c->bt_tok, B, H, stq));
+    CK(pf_norm_split(c->pf_A, c->bt_X, c->layers[0].ln1, B, H, s.rms_eps, stq));
     for (int l = 0; l < L; ++l) {
       const LayerW& w = c->layers[l];
       void* kc = (uint8_t*)c->bt_k + (size_t)l * layer_elems * kv_elt;
       void* vc = (uint8_t*)c->bt_v + (size_t)l * layer_elems * kv_elt;
-      CK(pf_norm_split(c->pf_A, c->bt_X, w.ln1, B, H, s.rms_eps, stq));
       if ((st = gemm(Nq, H, w.wqkv))) return st;
-      CK(pf_bias(c->pf_Q, c->pf_D, w.bqkv, B, Nq, stq));
-      CK(pf_rope_store(c->pf_Q, kc, vc, kv_bf16, c->cos_t, c->sin_t, 0, B, Hq, Hkv, d, Sb, stq,
-                       c->bt_pos, seq_elems));
-      CK(pf_attn(c->pf_att, c->pf_Q, kc, vc, kv_bf16, 0, B, Hq, Hkv, d, Sb, scale, stq, c->bt_pos,
-                 seq_elems));
-      CK(pf_norm_split(c->pf_A, c->pf_att, nullptr, B, qd, 0.0f, stq));
+      CK(pf_qkv_post(c->pf_Q, c->pf_D, sp, w.bqkv, kc, vc, kv_bf16, c->cos_t, c->sin_t, 0, B, Hq,
+                     Hkv, d, Sb, stq, c->bt_pos, seq_elems));
+      CK(pf_attn(c->pf_A, c->at_o, c->at_ml, c->pf_Q, kc, vc, kv_bf16, 0, B, Hq, Hkv, d, Sb, scale,
+                 max_keys, stq, c->bt_pos, seq_elems));
       if ((st = gemm(H, qd, w.wo))) return st;
-      CK(pf_resid(c->bt_X, c->pf_D, B, H, stq));
-      CK(pf_norm_split(c->pf_A, c->bt_X, w.ln2, B, H, s.rms_eps, stq));
+      CK(pf_resid_norm(c->bt_X, c->pf_D, sp, w.ln2, c->pf_A, B, H, s.rms_eps, stq));
       if ((st = gemm(2 * I, H, w.wg))) return st;
-      CK(pf_swiglu_split(c->pf_A, c->pf_D, B, I, stq));
+      CK(pf_swiglu_split(c->pf_A, c->pf_D, B, I, sp, stq));
       if ((st = gemm(H, I, w.wd))) return st;
-      CK(pf_resid(c->bt_X, c->pf_D, B, H, stq));
+      // the last layer's update goes on to the final norm of the head
+      CK(pf_resid_norm(c->bt_X, c->pf_D, sp, l + 1 < L ? c->layers[l + 1].ln1 : c->final_norm,
+                       c->pf_A, B, H, s.rms_eps, stq));
     }
     CK(pf_pos_advance(c->bt_pos, B, stq));
-    if ((st = head((int)step + 1))) return st;
+    if ((st = head((int)step + 1, true))) return st;
   }
   CK(cudaEventRecord(c->ev1, stq));
   if (steps)

@@ -52,18 +52,27 @@ using Kernel = cutlass::gemm::kernel::GemmUniversal<Shape<int, int, int, int>, M
 using Gemm = cutlass::gemm::device::GemmUniversalAdapter<Kernel>;
 
 typename Gemm::Arguments make_args(int M, int N, int K, const uint16_t* A, const uint16_t* W,
-                                   const float* C, float* D, float beta, int ldw = 0) {
+                                   const float* C, float* D, float beta, int ldw = 0,
+                                   int splits = 1) {
   using StrideA = typename Gemm::GemmKernel::StrideA;
   using StrideB = typename Gemm::GemmKernel::StrideB;
   using StrideC = typename Gemm::GemmKernel::StrideC;
   using StrideD = typename Gemm::GemmKernel::StrideD;
-  const StrideA sa = cutlass::make_cute_packed_stride(StrideA{}, {M, K, 1});
-  StrideB sb = cutlass::make_cute_packed_stride(StrideB{}, {N, K, 1});
-  if (ldw > K) cute::get<0>(sb) = ldw;  // W row n starts n * ldw elements in
-  const StrideC sc = cutlass::make_cute_packed_stride(StrideC{}, {M, N, 1});
-  const StrideD sd = cutlass::make_cute_packed_stride(StrideD{}, {M, N, 1});
+  // Split-K as the batch mode: batch l multiplies the K slice
+  // [l * Kc, (l + 1) * Kc) of A and W (the same rows, Kc elements further on)
+  // and writes its own [M, N] block of D, so D holds `splits` partial
+  // products that the consumer adds in a fixed order.
+  const int Kc = K / splits;
+  StrideA sa = cutlass::make_cute_packed_stride(StrideA{}, {M, Kc, splits});
+  cute::get<0>(sa) = K;
+  cute::get<2>(sa) = Kc;
+  StrideB sb = cutlass::make_cute_packed_stride(StrideB{}, {N, Kc, splits});
+  cute::get<0>(sb) = ldw > K ? ldw : K;  // W row n starts n * ldw elements in
+  cute::get<2>(sb) = Kc;
+  const StrideC sc = cutlass::make_cute_packed_stride(StrideC{}, {M, N, splits});
+  const StrideD sd = cutlass::make_cute_packed_stride(StrideD{}, {M, N, splits});
   typename Gemm::Arguments args{cutlass::gemm::GemmUniversalMode::kGemm,
-                                {M, N, K, 1},
+                                {M, N, Kc, splits},
                                 {reinterpret_cast<const ElementA*>(A), sa,
                                  reinterpret_cast<const ElementB*>(W), sb},
                                 {{1.0f, beta}, C ? C : D, sc, D, sd}};
@@ -81,11 +90,29 @@ size_t gemm_workspace_bytes(int M, int N, int K) {
   return Gemm::get_workspace_size(make_args(M, N, K, nullptr, nullptr, nullptr, nullptr, 0.0f));
 }
 
+int gemm_pick_splits(int M, int N, int K, int sms) {
+  // One 128 x 128 output tile per CTA: a projection with fewer tiles than
+  // SMs streams its weights through a fraction of the chip (each SM pulls
+  // its tile's K extent alone), so the K extent is cut into slices of whole
+  // 64-wide k-blocks until the tiles x slices fill the SMs once, keeping at
+  // least four k-blocks per slice.
+  const long tiles = (long)((M + 127) / 128) * ((N + 127) / 128);
+  if (K % 64 != 0 || tiles * 2 > sms) return 1;
+  const int kb = K / 64;
+  int best = 1;
+  for (int s = 2; s <= kMaxSplits; ++s)
+    if (kb % s == 0 && kb / s >= 4 && tiles * s <= sms) best = s;
+  return best;
+}
+
 cudaError_t gemm_bf16_f32(int M, int N, int K, const uint16_t* A, const uint16_t* W,
                           const float* C, float* D, float beta, void* workspace,
-                          size_t workspace_bytes, cudaStream_t st, int ldw) {
+                          size_t workspace_bytes, cudaStream_t st, int ldw, int splits) {
   if (!gemm_supported(M, N, K) || (ldw && (ldw < K || ldw % 8))) return cudaErrorInvalidValue;
-  const typename Gemm::Arguments args = make_args(M, N, K, A, W, C, D, beta, ldw);
+  if (splits < 1 || splits > kMaxSplits || K % splits || (K / splits) % 8 ||
+      (splits > 1 && (C || beta != 0.0f)))
+    return cudaErrorInvalidValue;
+  const typename Gemm::Arguments args = make_args(M, N, K, A, W, C, D, beta, ldw, splits);
   Gemm g;
   if (g.can_implement(args) != cutlass::Status::kSuccess) return cudaErrorInvalidValue;
   if (Gemm::get_workspace_size(args) > workspace_bytes) return cudaErrorInvalidValue;

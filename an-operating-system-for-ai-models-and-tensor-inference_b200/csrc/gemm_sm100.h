@@ -9,10 +9,19 @@ namespace myos {
 // D[M,N] = A[M,K] x W[N,K]^T + beta * C (C may be null when beta == 0); A and
 // W bf16 row-major (W's rows ldw >= K elements apart; 0: K), C and D f32
 // row-major; stream-ordered, no allocation.
+//
+// splits > 1 (split-K; C null, beta 0): K is cut into `splits` equal slices
+// (K / splits a multiple of 8) and D receives `splits` consecutive [M, N]
+// blocks, block l = A[:, l*Kc:(l+1)*Kc] x W[:, l*Kc:(l+1)*Kc]^T; the caller
+// adds them.
+constexpr int kMaxSplits = 8;
 bool gemm_supported(int M, int N, int K);
 size_t gemm_workspace_bytes(int M, int N, int K);
+// Slices that let an [M, N] output's 128 x 128 tiles fill `sms` SMs once
+// (1 when the tiles already cover half of them or K is not 64-aligned).
+int gemm_pick_splits(int M, int N, int K, int sms);
 cudaError_t gemm_bf16_f32(int M, int N, int K, const uint16_t* A, const uint16_t* W,
                           const float* C, float* D, float beta, void* workspace,
-                          size_t workspace_bytes, cudaStream_t st, int ldw = 0);
+                          size_t workspace_bytes, cudaStream_t st, int ldw = 0, int splits = 1);
 
 }  // namespace myos

@@ -11,12 +11,17 @@
 // element-wise steps keep the reference's operation order (no contraction).
 #include <math.h>
 
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 #include "prefill.h"
+#include "gemm_sm100.h"
 #include "kernels.h"
 
 namespace myos {
 namespace {
+
+namespace cg = cooperative_groups;
 
 constexpr int kT = 256;
 
@@ -35,10 +40,47 @@ MYOS_DEV void put_split(uint16_t* A, int n, int t, int K, int j, float y) {
   A[(size_t)(2 * n + t) * K + j] = bf16_rn(r2);
 }
 
-// The projection of row t: its three partial outputs, (hi + mid) + lo.
-MYOS_DEV float part_sum(const float* D, int n, int t, int N, int j) {
-  return __fadd_rn(__fadd_rn(D[(size_t)t * N + j], D[(size_t)(n + t) * N + j]),
-                   D[(size_t)(2 * n + t) * N + j]);
+// The projection of row t from D's partial outputs: `sp` K slices (blocks of
+// 3n rows, gemm_sm100.h split-K), each with its hi, mid and lo rows; summed
+// (hi + mid) + lo within a slice, then slice by slice in order.
+MYOS_DEV float part_sum(const float* D, int n, int t, int N, int j, int sp) {
+  const size_t blk = (size_t)kSplitParts * n * N;
+  float acc = 0.0f;
+  for (int l = 0; l < sp; ++l) {
+    const float* Dl = D + (size_t)l * blk;
+    const float v = __fadd_rn(__fadd_rn(Dl[(size_t)t * N + j], Dl[(size_t)(n + t) * N + j]),
+                              Dl[(size_t)(2 * n + t) * N + j]);
+    acc = l ? __fadd_rn(acc, v) : v;
+  }
+  return acc;
+}
+
+// part_sum of columns j..j+3 (N % 4 == 0, j % 4 == 0): every slice's three
+// partial rows are loaded before any is added, so the loads overlap.
+MYOS_DEV float4 part_sum4(const float* D, int n, int t, int N, int j, int sp) {
+  const size_t blk = (size_t)kSplitParts * n * N;
+  float4 a[kMaxSplits], b[kMaxSplits], c[kMaxSplits];
+#pragma unroll
+  for (int l = 0; l < kMaxSplits; ++l)
+    if (l < sp) {
+      const float* Dl = D + (size_t)l * blk;
+      a[l] = __ldcs(reinterpret_cast<const float4*>(Dl + (size_t)t * N + j));
+      b[l] = __ldcs(reinterpret_cast<const float4*>(Dl + (size_t)(n + t) * N + j));
+      c[l] = __ldcs(reinterpret_cast<const float4*>(Dl + (size_t)(2 * n + t) * N + j));
+    }
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int l = 0; l < kMaxSplits; ++l)
+    if (l < sp) {
+      const float4 v = make_float4(__fadd_rn(__fadd_rn(a[l].x, b[l].x), c[l].x),
+                                   __fadd_rn(__fadd_rn(a[l].y, b[l].y), c[l].y),
+                                   __fadd_rn(__fadd_rn(a[l].z, b[l].z), c[l].z),
+                                   __fadd_rn(__fadd_rn(a[l].w, b[l].w), c[l].w));
+      acc = l ? make_float4(__fadd_rn(acc.x, v.x), __fadd_rn(acc.y, v.y), __fadd_rn(acc.z, v.z),
+                            __fadd_rn(acc.w, v.w))
+              : v;
+    }
+  return acc;
 }
 
 MYOS_DEV float bsum(float v, float* red) { return block_sum(v, red); }
@@ -68,48 +110,48 @@ __global__ void __launch_bounds__(kT) k_pf_norm_split(uint16_t* A, const float* 
     put_split(A, n, t, K, j, gamma ? __fmul_rn(gamma[j], __fmul_rn(x[j], inv)) : x[j]);
 }
 
-// Q[t] = projection + bias (bf16.rs:147-158).
-__global__ void k_pf_bias(float* Q, const float* D, const float* bias, int n, int N) {
-  const int t = blockIdx.x;
-  for (int j = threadIdx.x; j < N; j += blockDim.x)
-    Q[(size_t)t * N + j] = __fadd_rn(part_sum(D, n, t, N, j), bias[j]);
-}
-
-// NeoX rotation of token t's q heads and KV heads at position p0 + t
-// (rope.rs:145-184), then K and V stored at that slot (KvCache::store_at).
+// Token t's q|k|v row from the QKV projection: projection + bias
+// (bf16.rs:147-158); the NeoX rotation of the q heads and KV heads at the
+// row's position (rope.rs:145-184); q into Q, K and V stored at that slot of
+// the cache (KvCache::store_at). Row t is token t of one sequence (position
+// p0 + t), or (rowpos non-null) the next token of sequence t at position
+// rowpos[t] with its cache rowstride elements on. Block (t, y) takes
+// 256 / d heads, one thread per rotation pair (p, p + d/2).
 template <typename KT>
-__global__ void k_pf_rope_store(float* Q, KT* kc, KT* vc, const float* cos_t, const float* sin_t,
-                                int p0, int Hq, int Hkv, int d, int S, const int* rowpos,
-                                size_t rowstride) {
-  // row t is token t of one sequence (position p0 + t), or with rowpos the
-  // next token of sequence t (position rowpos[t], cache rowstride elements on)
-  const int t = blockIdx.x, pos = rowpos ? rowpos[t] : p0 + t, half = d >> 1;
-  const int N = (Hq + 2 * Hkv) * d;
-  if (rowpos) {
-    kc += (size_t)t * rowstride;
-    vc += (size_t)t * rowstride;
+__global__ void __launch_bounds__(128) k_pf_qkv_post(float* Q, const float* D, int sp,
+                                                     const float* bias, KT* kc, KT* vc,
+                                                     const float* cos_t, const float* sin_t, int p0,
+                                                     int Hq, int Hkv, int d, int S,
+                                                     const int* rowpos, size_t rowstride) {
+  const int t = blockIdx.x, n = gridDim.x, half = d >> 1;
+  const int h = blockIdx.y * (256 / d) + threadIdx.x / half, p = threadIdx.x % half;
+  if (h >= Hq + 2 * Hkv) return;
+  const int pos = rowpos ? rowpos[t] : p0 + t;
+  const int N = (Hq + 2 * Hkv) * d, j = h * d + p;
+  float x0 = __fadd_rn(part_sum(D, n, t, N, j, sp), bias[j]);
+  float x1 = __fadd_rn(part_sum(D, n, t, N, j + half, sp), bias[j + half]);
+  if (h < Hq + Hkv) {  // q and k heads rotate
+    const float cs = cos_t[(size_t)pos * half + p], sn = sin_t[(size_t)pos * half + p];
+    const float y0 = __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn));
+    const float y1 = __fadd_rn(__fmul_rn(x1, cs), __fmul_rn(x0, sn));
+    x0 = y0;
+    x1 = y1;
   }
   float* q = Q + (size_t)t * N;
-  const float* cs = cos_t + (size_t)pos * half;
-  const float* sn = sin_t + (size_t)pos * half;
-  for (int i = threadIdx.x; i < (Hq + Hkv) * half; i += blockDim.x) {
-    const int h = i / half, p = i - h * half;
-    float* x = q + h * d;  // heads 0..Hq-1 are q, Hq.. are k
-    const float x0 = x[p], x1 = x[p + half];
-    x[p] = __fsub_rn(__fmul_rn(x0, cs[p]), __fmul_rn(x1, sn[p]));
-    x[p + half] = __fadd_rn(__fmul_rn(x1, cs[p]), __fmul_rn(x0, sn[p]));
-  }
-  __syncthreads();
-  for (int i = threadIdx.x; i < Hkv * d; i += blockDim.x) {
-    const int g = i / d, e = i - g * d;
-    const size_t slot = ((size_t)g * S + pos) * d + e;
-    if constexpr (sizeof(KT) == 4) {
-      kc[slot] = q[(Hq + g) * d + e];
-      vc[slot] = q[(Hq + Hkv + g) * d + e];
-    } else {
-      kc[slot] = __float2bfloat16_rn(q[(Hq + g) * d + e]);
-      vc[slot] = __float2bfloat16_rn(q[(Hq + Hkv + g) * d + e]);
-    }
+  q[j] = x0;
+  q[j + half] = x1;
+  if (h < Hq) return;
+  const bool is_k = h < Hq + Hkv;
+  const int g = is_k ? h - Hq : h - Hq - Hkv;
+  KT* cache = is_k ? kc : vc;
+  if (rowpos) cache += (size_t)t * rowstride;
+  const size_t slot = ((size_t)g * S + pos) * d + p;
+  if constexpr (sizeof(KT) == 4) {
+    cache[slot] = x0;
+    cache[slot + half] = x1;
+  } else {
+    cache[slot] = __float2bfloat16_rn(x0);
+    cache[slot + half] = __float2bfloat16_rn(x1);
   }
 }
 
@@ -125,50 +167,109 @@ MYOS_DEV float4 kv4<__nv_bfloat16>(const __nv_bfloat16* p) {
   return make_float4(bf16_lo(u.x), bf16_hi(u.x), bf16_lo(u.y), bf16_hi(u.y));
 }
 
-// Causal GQA for token t (position p0 + t) and KV head g: keys 0..pos from
-// the cache, online softmax over tiles of 32 (one warp per query head, lane
-// per key), p * v accumulated per lane over dims [4 lane, 4 lane + 4)
-// (+128 for d > 128); out = sum / L (gqa.rs:174-218, reassociated).
+// Causal GQA per row, split over the keys. Row t (token t at position
+// p0 + t of one sequence, or with rowpos the next token of sequence t at
+// rowpos[t], its cache rowstride elements on) and KV head g: block
+// (s, g, t) takes keys [s * ch, min((s + 1) * ch, pos + 1)) in tiles of 32
+// (one warp per query head, lane per key for the scores, online softmax
+// over the tiles, lane per D/32 dims for p * v) and leaves the unnormalised
+// partial: o_part[row][head][s][D], ml[row][head][s] = (running max, sum of
+// exponentials). k_pf_attn_merge combines the splits (gqa.rs:174-218,
+// reassociated: the softmax is taken split by split, then rescaled).
+constexpr int kAttnTile = 32;
+
+MYOS_DEV void cp_async16(void* smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(
+                   (uint32_t)__cvta_generic_to_shared(smem)),
+               "l"(gmem)
+               : "memory");
+}
+MYOS_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+MYOS_DEV void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// Shared memory of k_pf_attn_split: q heads of the group, then two buffers of
+// (K tile, V tile), rows padded to D + 4 floats.
+template <int D>
+constexpr size_t attn_smem_bytes() {
+  return (size_t)(8 * D + 2 * 2 * kAttnTile * (D + 4)) * sizeof(float);
+}
+
 template <typename KT, int D>
-__global__ void __launch_bounds__(kT) k_pf_attn(float* out, const float* Q, const KT* kcache,
-                                                const KT* vcache, int p0, int Hq, int Hkv, int S,
-                                                float scale, const int* rowpos, size_t rowstride) {
-  constexpr int kTile = 32, ds = D + 4;
-  __shared__ __align__(16) float qs[8 * D];
-  __shared__ __align__(16) float ks[kTile * ds];
-  __shared__ __align__(16) float vs[kTile * ds];
-  const int t = blockIdx.x, g = blockIdx.y, G = Hq / Hkv, pos = rowpos ? rowpos[t] : p0 + t;
+__global__ void __launch_bounds__(kT, 3) k_pf_attn_split(float* o_part, float2* ml, const float* Q,
+                                                         const KT* kcache, const KT* vcache, int p0,
+                                                         int Hq, int Hkv, int S, float scale, int ch,
+                                                         int ns, const int* rowpos,
+                                                         size_t rowstride) {
+  constexpr int ds = D + 4, V4 = D / 4, E = D / 32;  // E dims per lane in p * v
+  constexpr int kPer = (kAttnTile * V4 + kT - 1) / kT;  // float4s of K (and of V) per thread
+  extern __shared__ __align__(16) float sm[];
+  float* qs = sm;
+  const int sidx = blockIdx.x, g = blockIdx.y, t = blockIdx.z, G = Hq / Hkv;
+  const int pos = rowpos ? rowpos[t] : p0 + t;
+  const int k0 = sidx * ch;
+  if (k0 > pos) return;  // this row has fewer splits (whole block)
+  const int k1 = min(k0 + ch, pos + 1);
   if (rowpos) {
     kcache += (size_t)t * rowstride;
     vcache += (size_t)t * rowstride;
   }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int N = (Hq + 2 * Hkv) * D;
-  const float* q = Q + (size_t)t * N + (size_t)g * G * D;
-  for (int i = threadIdx.x; i < G * D; i += blockDim.x) qs[i] = q[i];
   const KT* kc = kcache + (size_t)g * S * D;
   const KT* vc = vcache + (size_t)g * S * D;
-  float4 acc[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
-  float m_run = -INFINITY, l_run = 0.0f;
-  for (int t0 = 0; t0 <= pos; t0 += kTile) {
-    const int nk = min(kTile, pos + 1 - t0);
-    __syncthreads();  // qs staged / previous tile consumed
-    for (int i = threadIdx.x; i < nk * (D / 4); i += blockDim.x) {
-      const int tt = i / (D / 4), e = (i - tt * (D / 4)) * 4;
-      *reinterpret_cast<float4*>(ks + tt * ds + e) = kv4<KT>(kc + (size_t)(t0 + tt) * D + e);
-      *reinterpret_cast<float4*>(vs + tt * ds + e) = kv4<KT>(vc + (size_t)(t0 + tt) * D + e);
+  // tile i -> buffer i & 1: f32 rows go straight to shared memory with
+  // asynchronous copies (the next tile's copies overlap this tile's math);
+  // bf16 rows are widened through registers
+  auto stage = [&](int t0, int buf) {
+    float* ks = sm + 8 * D + buf * 2 * kAttnTile * ds;
+    float* vs = ks + kAttnTile * ds;
+    const int nk = min(kAttnTile, k1 - t0);
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int idx = threadIdx.x + i * kT, tt = idx / V4, e = (idx - tt * V4) * 4;
+      if (tt < nk) {
+        if constexpr (sizeof(KT) == 4) {
+          cp_async16(ks + tt * ds + e, kc + (size_t)(t0 + tt) * D + e);
+          cp_async16(vs + tt * ds + e, vc + (size_t)(t0 + tt) * D + e);
+        } else {
+          *reinterpret_cast<float4*>(ks + tt * ds + e) = kv4<KT>(kc + (size_t)(t0 + tt) * D + e);
+          *reinterpret_cast<float4*>(vs + tt * ds + e) = kv4<KT>(vc + (size_t)(t0 + tt) * D + e);
+        }
+      }
     }
-    __syncthreads();
+    cp_async_commit();
+  };
+  stage(k0, 0);
+  const float* q = Q + (size_t)t * N + (size_t)g * G * D;
+  for (int i = threadIdx.x; i < G * V4; i += blockDim.x)
+    reinterpret_cast<float4*>(qs)[i] = reinterpret_cast<const float4*>(q)[i];
+  float acc[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) acc[e] = 0.0f;
+  float m_run = -INFINITY, l_run = 0.0f;
+  int buf = 0;
+  for (int t0 = k0; t0 < k1; t0 += kAttnTile, buf ^= 1) {
+    if (t0 + kAttnTile < k1) {
+      stage(t0 + kAttnTile, buf ^ 1);
+      cp_async_wait<1>();  // this tile's group has landed
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();  // every thread's copies of this tile (and qs) are visible
+    const float* ks = sm + 8 * D + buf * 2 * kAttnTile * ds;
+    const float* vs = ks + kAttnTile * ds;
+    const int nk = min(kAttnTile, k1 - t0);
     if (warp < G) {
       const float* qh = qs + warp * D;
       float sc = -INFINITY;
       if (lane < nk) {
-        const float* kr = ks + lane * ds;
+        const float* kp = ks + lane * ds;
         float p0s = 0.f, p1 = 0.f, p2 = 0.f, p3 = 0.f;
 #pragma unroll
         for (int e = 0; e < D; e += 4) {
           const float4 a = *reinterpret_cast<const float4*>(qh + e);
-          const float4 b = *reinterpret_cast<const float4*>(kr + e);
+          const float4 b = *reinterpret_cast<const float4*>(kp + e);
           p0s = fmaf(a.x, b.x, p0s);
           p1 = fmaf(a.y, b.y, p1);
           p2 = fmaf(a.z, b.z, p2);
@@ -178,101 +279,247 @@ __global__ void __launch_bounds__(kT) k_pf_attn(float* out, const float* Q, cons
       }
       const float mn = fmaxf(m_run, warp_max(sc));
       const float cf = expf(m_run - mn);
-      const float p = lane < nk ? expf(sc - mn) : 0.0f;
-      l_run = fmaf(l_run, cf, warp_sum(p));
+      const float pk = lane < nk ? expf(sc - mn) : 0.0f;
+      l_run = fmaf(l_run, cf, warp_sum(pk));
       m_run = mn;
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        acc[j].x *= cf;
-        acc[j].y *= cf;
-        acc[j].z *= cf;
-        acc[j].w *= cf;
-      }
+      for (int e = 0; e < E; ++e) acc[e] *= cf;
 #pragma unroll 8
       for (int k = 0; k < nk; ++k) {
-        const float pk = __shfl_sync(0xffffffffu, p, k);
+        const float pb = __shfl_sync(0xffffffffu, pk, k);
+        const float* vr_ = vs + k * ds + lane * E;
 #pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          const int e = 4 * lane + 128 * j;
-          if (e < D) {
-            const float4 v = *reinterpret_cast<const float4*>(vs + k * ds + e);
-            acc[j].x = fmaf(pk, v.x, acc[j].x);
-            acc[j].y = fmaf(pk, v.y, acc[j].y);
-            acc[j].z = fmaf(pk, v.z, acc[j].z);
-            acc[j].w = fmaf(pk, v.w, acc[j].w);
-          }
-        }
+        for (int e = 0; e < E; ++e) acc[e] = fmaf(pb, vr_[e], acc[e]);
       }
     }
+    __syncthreads();  // this buffer is consumed before the next stage reuses it
   }
   if (warp < G) {
-    float* o = out + (size_t)t * Hq * D + (size_t)(g * G + warp) * D;
+    const size_t slot = ((size_t)t * Hq + (size_t)g * G + warp) * ns + sidx;
+    float* o = o_part + slot * D + lane * E;
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      const int e = 4 * lane + 128 * j;
-      if (e < D)
-        *reinterpret_cast<float4*>(o + e) =
-            make_float4(__fdiv_rn(acc[j].x, l_run), __fdiv_rn(acc[j].y, l_run),
-                        __fdiv_rn(acc[j].z, l_run), __fdiv_rn(acc[j].w, l_run));
-    }
+    for (int e = 0; e < E; ++e) o[e] = acc[e];
+    if (lane == 0) ml[slot] = make_float2(m_run, l_run);
   }
 }
 
-// X[t] += projection (residual after o_proj / down_proj).
-__global__ void k_pf_resid(float* X, const float* D, int n, int N) {
-  const int t = blockIdx.x;
-  for (int j = threadIdx.x; j < N; j += blockDim.x)
-    X[(size_t)t * N + j] = __fadd_rn(X[(size_t)t * N + j], part_sum(D, n, t, N, j));
+// out = (sum over splits of o_s * e^(m_s - M)) / (sum of l_s * e^(m_s - M)),
+// M the largest split maximum; written into A as the three bf16 terms of the
+// o_proj input (row length Hq * D). One warp per (row, head): lanes hold the
+// split weights (s = lane, lane + 32), then D/32 dims each, splits in order.
+template <int D>
+__global__ void __launch_bounds__(128) k_pf_attn_merge(uint16_t* A, const float* o_part,
+                                                       const float2* ml, int p0, int Hq, int ch,
+                                                       int ns, const int* rowpos) {
+  constexpr int E = D / 32;
+  const int t = blockIdx.x, n = gridDim.x, lane = threadIdx.x & 31;
+  const int h = blockIdx.y * 4 + (threadIdx.x >> 5);
+  if (h >= Hq) return;
+  const int pos = rowpos ? rowpos[t] : p0 + t;
+  const int nsr = min(ns, pos / ch + 1);  // splits holding keys of this row
+  const size_t base = ((size_t)t * Hq + h) * ns;
+  const float2 a0 = lane < nsr ? ml[base + lane] : make_float2(-INFINITY, 0.0f);
+  const float2 a1 = lane + 32 < nsr ? ml[base + lane + 32] : make_float2(-INFINITY, 0.0f);
+  const float M = warp_max(fmaxf(a0.x, a1.x));
+  const float w0 = lane < nsr ? expf(a0.x - M) : 0.0f;
+  const float w1 = lane + 32 < nsr ? expf(a1.x - M) : 0.0f;
+  const float L = warp_sum(fmaf(a1.y, w1, __fmul_rn(a0.y, w0)));
+  float o[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) o[e] = 0.0f;
+  const float* op = o_part + base * D + lane * E;
+#pragma unroll 4
+  for (int s = 0; s < nsr; ++s) {
+    const float w = __shfl_sync(0xffffffffu, s < 32 ? w0 : w1, s & 31);
+#pragma unroll
+    for (int e = 0; e < E; ++e) o[e] = fmaf(op[(size_t)s * D + e], w, o[e]);
+  }
+#pragma unroll
+  for (int e = 0; e < E; ++e) put_split(A, n, t, Hq * D, h * D + lane * E + e, __fdiv_rn(o[e], L));
+}
+
+// X[t] += projection (the residual after o_proj / down_proj); then, with
+// gamma, A[t], A[n + t], A[2n + t] = the three bf16 terms of
+// gamma * (x * inv), inv = 1 / sqrtf(mean(x^2) + eps) of the updated row (the
+// next RMSNorm, bf16.rs:231-270). A row is one cluster of kResidParts
+// blocks, block r owning the r-th quarter of the columns (four adjacent
+// columns per thread and step, held in registers); the quarters' sums of
+// squares meet in distributed shared memory and are added in rank order.
+constexpr int kResidParts = 4, kResidThreads = 128, kResidVec = 4;
+__global__ void __cluster_dims__(kResidParts, 1, 1) __launch_bounds__(kResidThreads)
+    k_pf_resid_norm(float* X, const float* D, int sp, const float* gamma, uint16_t* A, int N,
+                    float eps) {
+  __shared__ float red[33];
+  __shared__ float part_ss;
+  const int r = blockIdx.x, t = blockIdx.y, n = gridDim.y;
+  const int w = N / kResidParts, c0 = r * w;  // N % (4 * kResidParts) == 0
+  float* x = X + (size_t)t * N;
+  float4 v[kResidVec];
+  float ss = 0.0f;
+#pragma unroll
+  for (int i = 0; i < kResidVec; ++i) {
+    const int j = c0 + 4 * (threadIdx.x + i * kResidThreads);
+    if (j < c0 + w) {
+      const float4 p = part_sum4(D, n, t, N, j, sp);
+      const float4 o = *reinterpret_cast<const float4*>(x + j);
+      v[i] = make_float4(__fadd_rn(o.x, p.x), __fadd_rn(o.y, p.y), __fadd_rn(o.z, p.z),
+                         __fadd_rn(o.w, p.w));
+      *reinterpret_cast<float4*>(x + j) = v[i];
+      ss = fmaf(v[i].x, v[i].x, ss);
+      ss = fmaf(v[i].y, v[i].y, ss);
+      ss = fmaf(v[i].z, v[i].z, ss);
+      ss = fmaf(v[i].w, v[i].w, ss);
+    }
+  }
+  if (!gamma) return;  // the whole cluster (gamma is uniform)
+  ss = bsum(ss, red);
+  if (threadIdx.x == 0) part_ss = ss;
+  cg::cluster_group cl = cg::this_cluster();
+  cl.sync();
+  float tot = 0.0f;
+#pragma unroll
+  for (int q = 0; q < kResidParts; ++q) tot = __fadd_rn(tot, *cl.map_shared_rank(&part_ss, q));
+  cl.sync();  // every peer has read this block's part_ss
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, (float)N), eps)));
+#pragma unroll
+  for (int i = 0; i < kResidVec; ++i) {
+    const int j = c0 + 4 * (threadIdx.x + i * kResidThreads);
+    if (j < c0 + w) {
+      put_split(A, n, t, N, j, __fmul_rn(gamma[j], __fmul_rn(v[i].x, inv)));
+      put_split(A, n, t, N, j + 1, __fmul_rn(gamma[j + 1], __fmul_rn(v[i].y, inv)));
+      put_split(A, n, t, N, j + 2, __fmul_rn(gamma[j + 2], __fmul_rn(v[i].z, inv)));
+      put_split(A, n, t, N, j + 3, __fmul_rn(gamma[j + 3], __fmul_rn(v[i].w, inv)));
+    }
+  }
 }
 
 // Tensor-parallel form: this rank's part of the residual update, written in
-// place over the hi rows of D: X + projection on the rank that carries the
-// residual (X non-null), the projection elsewhere; the ranks' parts are then summed.
-__global__ void k_pf_resid_part(float* D, const float* X, int n, int N) {
+// place over the first hi rows of D: X + projection on the rank that carries
+// the residual (X non-null), the projection elsewhere; the ranks' parts are
+// then summed.
+__global__ void k_pf_resid_part(float* D, const float* X, int n, int N, int sp) {
   const int t = blockIdx.x;
   for (int j = threadIdx.x; j < N; j += blockDim.x) {
-    const float dl = part_sum(D, n, t, N, j);
+    const float dl = part_sum(D, n, t, N, j, sp);  // reads D[t][j] before it is replaced
     D[(size_t)t * N + j] = X ? __fadd_rn(X[(size_t)t * N + j], dl) : dl;
   }
 }
 
 // h = (g / (1 + expf(-g))) * u (swiglu.rs:113-131) from the stacked gate|up
-// projection, written as three bf16 terms for the down projection.
-__global__ void k_pf_swiglu_split(uint16_t* A, const float* D, int n, int I) {
-  const int t = blockIdx.x, N = 2 * I;
-  for (int j = threadIdx.x; j < I; j += blockDim.x) {
-    const float g = part_sum(D, n, t, N, j);
-    const float u = part_sum(D, n, t, N, I + j);
-    const float s = __fdiv_rn(g, __fadd_rn(1.0f, expf(-g)));
-    put_split(A, n, t, I, j, __fmul_rn(s, u));
+// projection, written as three bf16 terms for the down projection; four
+// adjacent columns per thread (I % 4 == 0), partials summed as part_sum does.
+__global__ void __launch_bounds__(kT) k_pf_swiglu_split(uint16_t* A, const float* D, int I, int sp) {
+  const int t = blockIdx.x, n = gridDim.x, N = 2 * I;
+  const int j = 4 * (blockIdx.y * blockDim.x + threadIdx.x);
+  if (j >= I) return;
+  float g[4], u[4];
+  for (int l = 0; l < sp; ++l) {
+    const float* Dl = D + (size_t)l * kSplitParts * n * N;
+    const float* r0 = Dl + (size_t)t * N;
+    const float* r1 = Dl + (size_t)(n + t) * N;
+    const float* r2 = Dl + (size_t)(2 * n + t) * N;
+    const float4 g0 = __ldcs(reinterpret_cast<const float4*>(r0 + j));
+    const float4 g1 = __ldcs(reinterpret_cast<const float4*>(r1 + j));
+    const float4 g2 = __ldcs(reinterpret_cast<const float4*>(r2 + j));
+    const float4 u0 = __ldcs(reinterpret_cast<const float4*>(r0 + I + j));
+    const float4 u1 = __ldcs(reinterpret_cast<const float4*>(r1 + I + j));
+    const float4 u2 = __ldcs(reinterpret_cast<const float4*>(r2 + I + j));
+    const float ga[4] = {g0.x, g0.y, g0.z, g0.w}, gb[4] = {g1.x, g1.y, g1.z, g1.w},
+                gc[4] = {g2.x, g2.y, g2.z, g2.w};
+    const float ua[4] = {u0.x, u0.y, u0.z, u0.w}, ub[4] = {u1.x, u1.y, u1.z, u1.w},
+                uc[4] = {u2.x, u2.y, u2.z, u2.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float gv = __fadd_rn(__fadd_rn(ga[i], gb[i]), gc[i]);
+      const float uv = __fadd_rn(__fadd_rn(ua[i], ub[i]), uc[i]);
+      g[i] = l ? __fadd_rn(g[i], gv) : gv;
+      u[i] = l ? __fadd_rn(u[i], uv) : uv;
+    }
   }
+  uint16_t hi[4], mid[4], lo[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float s = __fdiv_rn(g[i], __fadd_rn(1.0f, expf(-g[i])));
+    const float y = __fmul_rn(s, u[i]);
+    hi[i] = bf16_rn(y);
+    const float e1 = __fsub_rn(y, __uint_as_float((uint32_t)hi[i] << 16));
+    mid[i] = bf16_rn(e1);
+    lo[i] = bf16_rn(__fsub_rn(e1, __uint_as_float((uint32_t)mid[i] << 16)));
+  }
+  auto pack = [](const uint16_t* v) {
+    return make_uint2((uint32_t)v[0] | ((uint32_t)v[1] << 16), (uint32_t)v[2] | ((uint32_t)v[3] << 16));
+  };
+  *reinterpret_cast<uint2*>(A + (size_t)t * I + j) = pack(hi);
+  *reinterpret_cast<uint2*>(A + (size_t)(n + t) * I + j) = pack(mid);
+  *reinterpret_cast<uint2*>(A + (size_t)(2 * n + t) * I + j) = pack(lo);
 }
 
 // Greedy token of each row from the stacked logit parts: logits_b[j] =
-// (D[b][j] + D[B + b][j]) + D[2B + b][j]; the first maximum with strict >, NaN and -inf never
-// win, none -> 0 (model_core/src/lib.rs:157-167). Records the token.
-__global__ void __launch_bounds__(kT) k_row_argmax(uint32_t* tok, uint32_t* out, int out_stride,
-                                                   int step, const float* D, int B, int V) {
+// (D[b][j] + D[B + b][j]) + D[2B + b][j]; the first maximum with strict >,
+// NaN and -inf never win, none -> 0 (model_core/src/lib.rs:157-167).
+// Stage 1: block (b, c) takes columns [c * kArgChunk, (c + 1) * kArgChunk)
+// and leaves its best (value, index) in part[b][c]; stage 2 picks among a
+// row's chunks (larger value, or equal value and smaller index) and records
+// the token.
+constexpr int kArgChunk = 4096;
+MYOS_DEV void amax_take(float& bv, uint32_t& bi, float v, uint32_t i) {
+  if (v > bv || (v == bv && i < bi)) {
+    bv = v;
+    bi = i;
+  }
+}
+
+__global__ void __launch_bounds__(kT) k_row_argmax_part(float2* part, const float* D, int B, int V,
+                                                        int vec) {
   __shared__ float bvs[kT / 32];
   __shared__ uint32_t bis[kT / 32];
-  const int b = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int b = blockIdx.x, c = blockIdx.y, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int j0 = c * kArgChunk, j1 = min(V, j0 + kArgChunk);
+  const float* r0 = D + (size_t)b * V;
+  const float* r1 = D + (size_t)(B + b) * V;
+  const float* r2 = D + (size_t)(2 * B + b) * V;
   float bv = -INFINITY;
   uint32_t bi = 0xffffffffu;
-  for (int j = threadIdx.x; j < V; j += blockDim.x) {
-    const float v = part_sum(D, B, b, V, j);
-    if (v > bv) {  // j grows per thread: strict > keeps the first
-      bv = v;
-      bi = (uint32_t)j;
+  if (vec) {  // V % 4 == 0: four adjacent columns per thread, all loads issued first
+    constexpr int kPer = kArgChunk / 4 / kT;
+    float4 a[kPer], bb[kPer], cc[kPer];
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int j = j0 + 4 * (threadIdx.x + i * kT);
+      if (j < j1) {
+        a[i] = __ldcs(reinterpret_cast<const float4*>(r0 + j));
+        bb[i] = __ldcs(reinterpret_cast<const float4*>(r1 + j));
+        cc[i] = __ldcs(reinterpret_cast<const float4*>(r2 + j));
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {  // j grows per thread: strict > keeps the first
+      const int j = j0 + 4 * (threadIdx.x + i * kT);
+      if (j < j1) {
+        const float v0 = __fadd_rn(__fadd_rn(a[i].x, bb[i].x), cc[i].x);
+        const float v1 = __fadd_rn(__fadd_rn(a[i].y, bb[i].y), cc[i].y);
+        const float v2 = __fadd_rn(__fadd_rn(a[i].z, bb[i].z), cc[i].z);
+        const float v3 = __fadd_rn(__fadd_rn(a[i].w, bb[i].w), cc[i].w);
+        if (v0 > bv) { bv = v0; bi = (uint32_t)j; }
+        if (v1 > bv) { bv = v1; bi = (uint32_t)j + 1; }
+        if (v2 > bv) { bv = v2; bi = (uint32_t)j + 2; }
+        if (v3 > bv) { bv = v3; bi = (uint32_t)j + 3; }
+      }
+    }
+  } else {
+    for (int j = j0 + threadIdx.x; j < j1; j += kT) {
+      const float v = __fadd_rn(__fadd_rn(r0[j], r1[j]), r2[j]);
+      if (v > bv) {
+        bv = v;
+        bi = (uint32_t)j;
+      }
     }
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
     const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
-    if (ov > bv || (ov == bv && oi < bi)) {
-      bv = ov;
-      bi = oi;
-    }
+    amax_take(bv, bi, ov, oi);
   }
   if (lane == 0) {
     bvs[warp] = bv;
@@ -282,12 +529,28 @@ __global__ void __launch_bounds__(kT) k_row_argmax(uint32_t* tok, uint32_t* out,
   if (threadIdx.x == 0) {
     float v = -INFINITY;
     uint32_t i = 0xffffffffu;
-    for (int w = 0; w < kT / 32; ++w)
-      if (bvs[w] > v || (bvs[w] == v && bis[w] < i)) {
-        v = bvs[w];
-        i = bis[w];
-      }
-    const uint32_t t = i == 0xffffffffu ? 0u : i;
+    for (int w = 0; w < kT / 32; ++w) amax_take(v, i, bvs[w], bis[w]);
+    part[(size_t)b * gridDim.y + c] = make_float2(v, __uint_as_float(i));
+  }
+}
+
+__global__ void k_row_argmax_fin(uint32_t* tok, uint32_t* out, int out_stride, int step,
+                                 const float2* part, int nc) {
+  const int b = blockIdx.x, lane = threadIdx.x;
+  float bv = -INFINITY;
+  uint32_t bi = 0xffffffffu;
+  for (int c = lane; c < nc; c += 32) {
+    const float2 p = part[(size_t)b * nc + c];
+    amax_take(bv, bi, p.x, __float_as_uint(p.y));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    amax_take(bv, bi, ov, oi);
+  }
+  if (lane == 0) {
+    const uint32_t t = bi == 0xffffffffu ? 0u : bi;
     tok[b] = t;
     if (out) out[(size_t)b * out_stride + step] = t;
   }
@@ -306,9 +569,14 @@ __global__ void k_pos_advance(int* rowpos, int B) {
 
 }  // namespace
 
+int pf_argmax_chunks(int V) { return (V + kArgChunk - 1) / kArgChunk; }
+
 cudaError_t pf_row_argmax(uint32_t* tok, uint32_t* out, int out_stride, int step, const float* D,
-                          int B, int V, cudaStream_t st) {
-  k_row_argmax<<<B, kT, 0, st>>>(tok, out, out_stride, step, D, B, V);
+                          float2* part, int B, int V, cudaStream_t st) {
+  const int nc = pf_argmax_chunks(V);
+  k_row_argmax_part<<<dim3(B, nc), kT, 0, st>>>(part, D, B, V, V % 4 == 0);
+  if (cudaError_t e = counted(cudaGetLastError())) return e;
+  k_row_argmax_fin<<<B, 32, 0, st>>>(tok, out, out_stride, step, part, nc);
   return counted(cudaGetLastError());
 }
 
@@ -335,59 +603,97 @@ cudaError_t pf_norm_split(uint16_t* A, const float* X, const float* gamma, int n
   return counted(cudaGetLastError());
 }
 
-cudaError_t pf_bias(float* Q, const float* D, const float* bias, int n, int N, cudaStream_t st) {
-  k_pf_bias<<<n, kT, 0, st>>>(Q, D, bias, n, N);
-  return counted(cudaGetLastError());
-}
-
-cudaError_t pf_rope_store(float* Q, void* kc, void* vc, int kv_bf16, const float* cos_t,
-                          const float* sin_t, int p0, int n, int Hq, int Hkv, int d, int S,
-                          cudaStream_t st, const int* rowpos, size_t rowstride) {
+cudaError_t pf_qkv_post(float* Q, const float* D, int sp, const float* bias, void* kc, void* vc,
+                        int kv_bf16, const float* cos_t, const float* sin_t, int p0, int n, int Hq,
+                        int Hkv, int d, int S, cudaStream_t st, const int* rowpos,
+                        size_t rowstride) {
+  if ((d != 64 && d != 128) || sp < 1 || sp > kMaxSplits) return cudaErrorInvalidValue;
+  const dim3 grid(n, (Hq + 2 * Hkv + 256 / d - 1) / (256 / d));
   if (kv_bf16)
-    k_pf_rope_store<__nv_bfloat16><<<n, kT, 0, st>>>(Q, (__nv_bfloat16*)kc, (__nv_bfloat16*)vc,
-                                                      cos_t, sin_t, p0, Hq, Hkv, d, S, rowpos,
-                                                      rowstride);
+    k_pf_qkv_post<__nv_bfloat16><<<grid, 128, 0, st>>>(Q, D, sp, bias, (__nv_bfloat16*)kc,
+                                                        (__nv_bfloat16*)vc, cos_t, sin_t, p0, Hq,
+                                                        Hkv, d, S, rowpos, rowstride);
   else
-    k_pf_rope_store<float><<<n, kT, 0, st>>>(Q, (float*)kc, (float*)vc, cos_t, sin_t, p0, Hq, Hkv,
-                                             d, S, rowpos, rowstride);
+    k_pf_qkv_post<float><<<grid, 128, 0, st>>>(Q, D, sp, bias, (float*)kc, (float*)vc, cos_t,
+                                               sin_t, p0, Hq, Hkv, d, S, rowpos, rowstride);
   return counted(cudaGetLastError());
 }
 
 bool pf_attn_supported(int d, int G) { return (d == 64 || d == 128) && G <= 8; }
 
-cudaError_t pf_attn(float* out, const float* Q, const void* kc, const void* vc, int kv_bf16, int p0,
-                    int n, int Hq, int Hkv, int d, int S, float scale, cudaStream_t st,
-                    const int* rowpos, size_t rowstride) {
-  const dim3 grid(n, Hkv);
-#define MYOS_PF_ATTN(D)                                                                     \
-  if (d == D) {                                                                             \
-    if (kv_bf16)                                                                            \
-      k_pf_attn<__nv_bfloat16, D><<<grid, kT, 0, st>>>(out, Q, (const __nv_bfloat16*)kc,    \
-                                                       (const __nv_bfloat16*)vc, p0, Hq,    \
-                                                       Hkv, S, scale, rowpos, rowstride);   \
-    else                                                                                    \
-      k_pf_attn<float, D><<<grid, kT, 0, st>>>(out, Q, (const float*)kc, (const float*)vc, \
-                                               p0, Hq, Hkv, S, scale, rowpos, rowstride);   \
-    return counted(cudaGetLastError());                                                              \
+cudaError_t pf_init() {
+#define MYOS_PF_SMEM(KT, D)                                                                \
+  if (cudaError_t e = cudaFuncSetAttribute(k_pf_attn_split<KT, D>,                         \
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize,    \
+                                           (int)attn_smem_bytes<D>()))                     \
+    return e;
+  MYOS_PF_SMEM(float, 64)
+  MYOS_PF_SMEM(float, 128)
+  MYOS_PF_SMEM(__nv_bfloat16, 64)
+  MYOS_PF_SMEM(__nv_bfloat16, 128)
+#undef MYOS_PF_SMEM
+  return cudaSuccess;
+}
+
+int pf_attn_splits(int max_keys, int* ch) {
+  // two 32-key tiles per split (the second's copies overlap the first's
+  // math), or more so that a row has at most kAttnMaxSplits of them
+  int c = 2 * kAttnTile;
+  while ((max_keys + c - 1) / c > kAttnMaxSplits) c += kAttnTile;
+  *ch = c;
+  return (max_keys + c - 1) / c;
+}
+
+cudaError_t pf_attn(uint16_t* A, float* o_part, float2* ml, const float* Q, const void* kc,
+                    const void* vc, int kv_bf16, int p0, int n, int Hq, int Hkv, int d, int S,
+                    float scale, int max_keys, cudaStream_t st, const int* rowpos,
+                    size_t rowstride) {
+  if (!pf_attn_supported(d, Hq / Hkv) || max_keys < 1) return cudaErrorInvalidValue;
+  int ch = 0;
+  const int ns = pf_attn_splits(max_keys, &ch);
+  const dim3 grid(ns, Hkv, n);
+#define MYOS_PF_ATTN(D)                                                                          \
+  if (d == D) {                                                                                  \
+    const size_t smem = attn_smem_bytes<D>();                                                    \
+    if (kv_bf16)                                                                                 \
+      k_pf_attn_split<__nv_bfloat16, D><<<grid, kT, smem, st>>>(                                 \
+          o_part, ml, Q, (const __nv_bfloat16*)kc, (const __nv_bfloat16*)vc, p0, Hq, Hkv, S,     \
+          scale, ch, ns, rowpos, rowstride);                                                     \
+    else                                                                                         \
+      k_pf_attn_split<float, D><<<grid, kT, smem, st>>>(o_part, ml, Q, (const float*)kc,         \
+                                                        (const float*)vc, p0, Hq, Hkv, S, scale, \
+                                                        ch, ns, rowpos, rowstride);              \
   }
   MYOS_PF_ATTN(64)
   MYOS_PF_ATTN(128)
 #undef MYOS_PF_ATTN
-  return cudaErrorInvalidValue;
-}
-
-cudaError_t pf_resid(float* X, const float* D, int n, int N, cudaStream_t st) {
-  k_pf_resid<<<n, kT, 0, st>>>(X, D, n, N);
+  if (cudaError_t e = counted(cudaGetLastError())) return e;
+  const dim3 mgrid(n, (Hq + 3) / 4);
+  if (d == 64)
+    k_pf_attn_merge<64><<<mgrid, 128, 0, st>>>(A, o_part, ml, p0, Hq, ch, ns, rowpos);
+  else
+    k_pf_attn_merge<128><<<mgrid, 128, 0, st>>>(A, o_part, ml, p0, Hq, ch, ns, rowpos);
   return counted(cudaGetLastError());
 }
 
-cudaError_t pf_resid_part(float* D, const float* X, int n, int N, cudaStream_t st) {
-  k_pf_resid_part<<<n, kT, 0, st>>>(D, X, n, N);
+cudaError_t pf_resid_norm(float* X, const float* D, int sp, const float* gamma, uint16_t* A, int n,
+                          int N, float eps, cudaStream_t st) {
+  if (N % (4 * kResidParts) || N > 4 * kResidVec * kResidThreads * kResidParts || sp < 1 ||
+      sp > kMaxSplits)
+    return cudaErrorInvalidValue;
+  k_pf_resid_norm<<<dim3(kResidParts, n), kResidThreads, 0, st>>>(X, D, sp, gamma, A, N, eps);
   return counted(cudaGetLastError());
 }
 
-cudaError_t pf_swiglu_split(uint16_t* A, const float* D, int n, int I, cudaStream_t st) {
-  k_pf_swiglu_split<<<n, kT, 0, st>>>(A, D, n, I);
+cudaError_t pf_resid_part(float* D, const float* X, int n, int N, int sp, cudaStream_t st) {
+  k_pf_resid_part<<<n, kT, 0, st>>>(D, X, n, N, sp);
+  return counted(cudaGetLastError());
+}
+
+cudaError_t pf_swiglu_split(uint16_t* A, const float* D, int n, int I, int sp, cudaStream_t st) {
+  if (I % 4) return cudaErrorInvalidValue;
+  const dim3 grid(n, (I / 4 + kT - 1) / kT);
+  k_pf_swiglu_split<<<grid, kT, 0, st>>>(A, D, I, sp);
   return counted(cudaGetLastError());
 }
 

@@ -16,27 +16,48 @@ cudaError_t pf_embed(float* X, const uint16_t* embed, const uint32_t* ids, int n
                      cudaStream_t st);
 cudaError_t pf_norm_split(uint16_t* A, const float* X, const float* gamma, int n, int K, float eps,
                           cudaStream_t st);
-cudaError_t pf_bias(float* Q, const float* D, const float* bias, int n, int N, cudaStream_t st);
-// Rows are tokens p0.. of one sequence, or (rowpos non-null) the next token
-// of sequence t at position rowpos[t] with its cache rowstride elements on.
-cudaError_t pf_rope_store(float* Q, void* kc, void* vc, int kv_bf16, const float* cos_t,
-                          const float* sin_t, int p0, int n, int Hq, int Hkv, int d, int S,
-                          cudaStream_t st, const int* rowpos = nullptr, size_t rowstride = 0);
+// Projection outputs D hold `sp` K slices of 3n partial rows each
+// (gemm_sm100.h split-K); the consumers below add them in a fixed order.
+//
+// Q[t] = QKV projection + bias, then RoPE of the q and k heads and the K/V
+// store. Rows are tokens p0.. of one sequence, or (rowpos non-null) the next
+// token of sequence t at position rowpos[t] with its cache rowstride
+// elements on.
+cudaError_t pf_qkv_post(float* Q, const float* D, int sp, const float* bias, void* kc, void* vc,
+                        int kv_bf16, const float* cos_t, const float* sin_t, int p0, int n, int Hq,
+                        int Hkv, int d, int S, cudaStream_t st, const int* rowpos = nullptr,
+                        size_t rowstride = 0);
 bool pf_attn_supported(int d, int G);
-cudaError_t pf_attn(float* out, const float* Q, const void* kc, const void* vc, int kv_bf16, int p0,
-                    int n, int Hq, int Hkv, int d, int S, float scale, cudaStream_t st,
-                    const int* rowpos = nullptr, size_t rowstride = 0);
+// Raises the shared-memory limit of the split attention (once per device,
+// with that device current, before the first pf_attn there).
+cudaError_t pf_init();
+// Causal GQA per row, split over the keys, then merged into A as the o_proj
+// input's three terms. Splits of 64 keys (longer past kAttnMaxSplits); the
+// partials o_part (rows * Hq * splits * d floats) and ml (rows * Hq * splits)
+// come from the caller, sized by pf_attn_splits(max_keys) for the largest
+// position + 1 of any row.
+constexpr int kAttnMaxSplits = 64;
+int pf_attn_splits(int max_keys, int* ch);
+cudaError_t pf_attn(uint16_t* A, float* o_part, float2* ml, const float* Q, const void* kc,
+                    const void* vc, int kv_bf16, int p0, int n, int Hq, int Hkv, int d, int S,
+                    float scale, int max_keys, cudaStream_t st, const int* rowpos = nullptr,
+                    size_t rowstride = 0);
 // Greedy token per row of stacked logit parts D[3B, V]; tok[b], and
-// out[b * out_stride + step] when out is non-null.
+// out[b * out_stride + step] when out is non-null. part: B * pf_argmax_chunks(V)
+// float2 of scratch.
+int pf_argmax_chunks(int V);
 cudaError_t pf_row_argmax(uint32_t* tok, uint32_t* out, int out_stride, int step, const float* D,
-                          int B, int V, cudaStream_t st);
+                          float2* part, int B, int V, cudaStream_t st);
 cudaError_t pf_rows_copy(float* dst, const float* src, const int* src_row, int B, int K,
                          cudaStream_t st);
 cudaError_t pf_pos_advance(int* rowpos, int B, cudaStream_t st);
-cudaError_t pf_resid(float* X, const float* D, int n, int N, cudaStream_t st);
-// D[t] = (X ? X[t] : 0) + D[t] + D[n + t] over rows t < n (in place; the
-// tensor-parallel part before the sum over ranks).
-cudaError_t pf_resid_part(float* D, const float* X, int n, int N, cudaStream_t st);
-cudaError_t pf_swiglu_split(uint16_t* A, const float* D, int n, int I, cudaStream_t st);
+// X[t] += projection; with gamma also A = the three bf16 terms of
+// RMSNorm(X[t]) * gamma (the next projection's input).
+cudaError_t pf_resid_norm(float* X, const float* D, int sp, const float* gamma, uint16_t* A, int n,
+                          int N, float eps, cudaStream_t st);
+// D[t] = (X ? X[t] : 0) + projection over rows t < n (in place over the first
+// hi rows; the tensor-parallel part before the sum over ranks).
+cudaError_t pf_resid_part(float* D, const float* X, int n, int N, int sp, cudaStream_t st);
+cudaError_t pf_swiglu_split(uint16_t* A, const float* D, int n, int I, int sp, cudaStream_t st);
 
 }  // namespace myos
