@@ -115,6 +115,7 @@ struct myos_ctx {
   size_t pf_ws_bytes = 0;
   size_t pf_D_elems = 0;  // capacity of pf_D in floats
   bool pf_splitk = true;  // MYOS_SPLITK=0: one K slice per projection
+  bool pf_pair = true;    // MYOS_GEMM_PAIR=0: no 2-SM tiles
   // batched decode (myos_batch_generate): per-sequence KV slabs and buffers
   void *bt_k = nullptr, *bt_v = nullptr;
   size_t bt_kv_bytes = 0;
@@ -122,6 +123,7 @@ struct myos_ctx {
   size_t bt_D_bytes = 0;
   int *bt_pos = nullptr, *bt_rows = nullptr;
   uint32_t *bt_tok = nullptr, *bt_out = nullptr, *bt_ids = nullptr, *bt_feed = nullptr;
+  int* bt_step = nullptr;  // device step index of the batched step graph
   size_t bt_feed_bytes = 0;
   float* at_o = nullptr;     // split attention partials of the GEMM path (o)
   float2* at_ml = nullptr;   // ... and their (max, sum of exponentials)
@@ -1171,6 +1173,8 @@ static int create_impl(myos_ctx* c, const myos_shape* shape, const myos_opts* op
       c->pf_D_elems = M * nmax;
       const char* sk = getenv("MYOS_SPLITK");
       c->pf_splitk = !(sk && sk[0] == '0');
+      const char* gp = getenv("MYOS_GEMM_PAIR");
+      c->pf_pair = !(gp && gp[0] == '0');
       CK(cudaMalloc(&c->pf_Q, (size_t)nc * (c->qd + 2 * c->kvd) * 4));
       CK(cudaMalloc(&c->pf_ws, ws));
       c->pf_ws_bytes = ws;
@@ -1329,7 +1333,7 @@ void myos_ctx_destroy(myos_ctx* c) {
                  (void*)c->ktrace, c->pf_X, c->pf_D, c->pf_Q, c->pf_A, c->pf_ws,
                  c->bt_k, c->bt_v, c->bt_X, c->bt_D, c->bt_pos, c->bt_rows, c->bt_tok,
                  c->bt_out, c->bt_ids, c->bt_feed, c->tp_part, c->tp_cand, c->tp_link,
-                 c->at_o, (void*)c->at_ml, (void*)c->bt_amax};
+                 c->at_o, (void*)c->at_ml, (void*)c->bt_amax, c->bt_step};
   for (void* p : dev)
     if (p) cudaFree(p);
   for (int i = 0; i < 2; ++i) {
@@ -1697,6 +1701,19 @@ static int pf_splits(const myos_ctx* c, int M, int N, int K) {
   return sp;
 }
 
+// One projection of the GEMM path: D = pf_A x W^T on SM pairs (wide N) or on
+// single SMs with K slices (sp null: never sliced, D holds one [M, N]
+// block); *sp receives the slices now in D.
+static cudaError_t pf_gemm(const myos_ctx* c, int M, int N, int K, const uint16_t* W, float* D,
+                           cudaStream_t st, int ldw, int* sp) {
+  const int pair = c->pf_pair && gemm_pick_pair(M, N, c->num_sms);
+  int one = 1;
+  if (!sp) sp = &one;
+  else *sp = pair ? 1 : pf_splits(c, M, N, K);
+  return gemm_bf16_f32(M, N, K, c->pf_A, W, nullptr, D, 0.0f, c->pf_ws, c->pf_ws_bytes, st, ldw,
+                       *sp, pair);
+}
+
 // One chunk of n prompt tokens at positions p0.. through every layer
 // (GEMM prefill); leaves the chunk's residual rows in pf_X and their K/V in
 // the cache.
@@ -1720,9 +1737,7 @@ int prefill_chunk(myos_ctx* c, const uint32_t* d_ids, int n, int p0, void* kcach
   // tiles would leave SMs idle and pf_D has room for the partials)
   int sp = 1;
   auto gemm = [&](int N, int K, const uint16_t* W, int ldw = 0) {
-    sp = pf_splits(c, M, N, K);
-    const cudaError_t e = gemm_bf16_f32(M, N, K, c->pf_A, W, nullptr, c->pf_D, 0.0f, c->pf_ws,
-                                        c->pf_ws_bytes, st, ldw, sp);
+    const cudaError_t e = pf_gemm(c, M, N, K, W, c->pf_D, st, ldw, &sp);
     return e == cudaSuccess ? MYOS_OK : fail(c, MYOS_ERR_CUDA, std::string("prefill gemm: ") + cudaGetErrorString(e));
   };
   // residual += the projection (the partial rows of pf_D), then the next
@@ -1814,6 +1829,8 @@ static int batch_run(myos_ctx* c, size_t nseq, const uint32_t* ids, const uint32
   if ((st = grow(c, &c->bt_pos, &have_small, (size_t)c->pf_chunk * 4))) return st;
   if ((st = grow(c, &c->bt_rows, &h2, (size_t)c->pf_chunk * 4))) return st;
   if ((st = grow(c, &c->bt_tok, &h3, (size_t)c->pf_chunk * 4))) return st;
+  size_t have_step = c->bt_step ? sizeof(int) : 0;
+  if ((st = grow(c, &c->bt_step, &have_step, sizeof(int)))) return st;
   (void)h4;
   size_t have_out = c->bt_out_n * 4, have_ids = c->bt_ids_n * 4;
   if ((st = grow(c, &c->bt_out, &have_out, std::max<size_t>(1, (size_t)B * steps) * 4))) return st;
@@ -1863,8 +1880,7 @@ static int batch_run(myos_ctx* c, size_t nseq, const uint32_t* ids, const uint32
   CK(cudaEventRecord(c->ev2, stq));  // prompts done: prefill_ms ends, decode_ms starts
   auto head = [&](int step, bool normed) -> int {
     if (!normed) CK(pf_norm_split(c->pf_A, c->bt_X, c->final_norm, B, H, s.rms_eps, stq));
-    const cudaError_t e = gemm_bf16_f32(M, V, H, c->pf_A, head_w, nullptr, c->bt_D, 0.0f, c->pf_ws,
-                                        c->pf_ws_bytes, stq);
+    const cudaError_t e = pf_gemm(c, M, V, H, head_w, c->bt_D, stq, 0, nullptr);
     if (e != cudaSuccess) return fail(c, MYOS_ERR_CUDA, std::string("batch head gemm: ") + cudaGetErrorString(e));
     CK(pf_row_argmax(c->bt_tok, step < (int)steps ? c->bt_out : nullptr, (int)steps, step, c->bt_D,
                      c->bt_amax, B, V, stq));
@@ -1872,18 +1888,19 @@ static int batch_run(myos_ctx* c, size_t nseq, const uint32_t* ids, const uint32
   };
   int sp = 1;  // K slices of the projection now in pf_D
   auto gemm = [&](int N, int K, const uint16_t* W) -> int {
-    sp = pf_splits(c, M, N, K);
-    const cudaError_t e = gemm_bf16_f32(M, N, K, c->pf_A, W, nullptr, c->pf_D, 0.0f, c->pf_ws,
-                                        c->pf_ws_bytes, stq, 0, sp);
+    const cudaError_t e = pf_gemm(c, M, N, K, W, c->pf_D, stq, 0, &sp);
     return e == cudaSuccess ? MYOS_OK : fail(c, MYOS_ERR_CUDA, std::string("batch gemm: ") + cudaGetErrorString(e));
   };
   // 2. greedy: token s of every sequence is the argmax of its current
   //    logits; each is then forwarded (model_core greedy_decode, per sequence)
   if ((st = head(0, false))) return st;
-  for (size_t step = 0; step < steps; ++step) {
+  // One step reads everything that changes from step to step on the device
+  // (positions, tokens, the step index bt_step), so the same launches serve
+  // every step: captured once as a CUDA graph and replayed.
+  CK(cudaMemsetAsync(c->bt_step, 0, sizeof(int), stq));
+  auto step_body = [&]() -> int {
     if (feed)  // teacher-forced: this step embeds the given token, not the argmax
-      CK(cudaMemcpyAsync(c->bt_tok, c->bt_feed + step * B, (size_t)B * 4, cudaMemcpyDeviceToDevice,
-                         stq));
+      CK(pf_feed(c->bt_tok, c->bt_feed, c->bt_step, B, stq));
     CK(pf_embed(c->bt_X, c->embed, c->bt_tok, B, H, stq));
     CK(pf_norm_split(c->pf_A, c->bt_X, c->layers[0].ln1, B, H, s.rms_eps, stq));
     for (int l = 0; l < L; ++l) {
@@ -1904,8 +1921,37 @@ static int batch_run(myos_ctx* c, size_t nseq, const uint32_t* ids, const uint32
       CK(pf_resid_norm(c->bt_X, c->pf_D, sp, l + 1 < L ? c->layers[l + 1].ln1 : c->final_norm,
                        c->pf_A, B, H, s.rms_eps, stq));
     }
-    CK(pf_pos_advance(c->bt_pos, B, stq));
-    if ((st = head((int)step + 1, true))) return st;
+    CK(pf_pos_advance(c->bt_pos, B, stq, c->bt_step));  // bt_step: this step + 1
+    const cudaError_t e = pf_gemm(c, M, V, H, head_w, c->bt_D, stq, 0, nullptr);
+    if (e != cudaSuccess)
+      return fail(c, MYOS_ERR_CUDA, std::string("batch head gemm: ") + cudaGetErrorString(e));
+    CK(pf_row_argmax(c->bt_tok, c->bt_out, (int)steps, 0, c->bt_D, c->bt_amax, B, V, stq,
+                     c->bt_step));
+    return MYOS_OK;
+  };
+  if (c->o.use_graphs && steps > 1) {
+    cudaGraph_t g;
+    CK(cudaStreamBeginCapture(stq, cudaStreamCaptureModeRelaxed));
+    const uint64_t before = launches_total();  // a capture launches nothing
+    st = step_body();
+    const uint64_t captured = launches_total() - before;
+    launches_uncount(captured);
+    cudaError_t ce = cudaStreamEndCapture(stq, &g);
+    if (st) return st;
+    if (ce != cudaSuccess)
+      return fail(c, MYOS_ERR_CUDA, std::string("batch graph capture: ") + cudaGetErrorString(ce));
+    cudaGraphExec_t ge;
+    ce = cudaGraphInstantiate(&ge, g, 0);
+    cudaGraphDestroy(g);
+    if (ce != cudaSuccess)
+      return fail(c, MYOS_ERR_CUDA, std::string("batch graph instantiate: ") + cudaGetErrorString(ce));
+    for (size_t step = 0; step < steps && ce == cudaSuccess; ++step)
+      ce = counted(cudaGraphLaunch(ge, stq), captured);
+    cudaGraphExecDestroy(ge);  // released once its replays complete
+    CK(ce);
+  } else {
+    for (size_t step = 0; step < steps; ++step)
+      if ((st = step_body())) return st;
   }
   CK(cudaEventRecord(c->ev1, stq));
   if (steps)

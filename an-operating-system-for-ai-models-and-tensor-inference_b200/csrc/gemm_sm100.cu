@@ -20,6 +20,8 @@
 #include <cutlass/util/packed_stride.hpp>
 #include <cute/tensor.hpp>
 
+#include <algorithm>
+
 #include "gemm_sm100.h"
 #include "kernels.h"
 
@@ -33,31 +35,43 @@ using ElementB = cutlass::bfloat16_t;
 using LayoutA = cutlass::layout::RowMajor;     // activations: K contiguous
 using LayoutB = cutlass::layout::ColumnMajor;  // W[N,K] row-major is K x N column-major
 using LayoutC = cutlass::layout::RowMajor;
-using MmaTile = Shape<_128, _128, _64>;
-using ClusterShape = Shape<_1, _1, _1>;
+// Two instantiations: one SM per 128 x 128 output tile (MMA M = 128), and a
+// pair of SMs per 256 x 256 tile (tcgen05 cta_group::2 on a 2 x 1 cluster:
+// each SM stages half of A's rows and half of W's rows, the pair's MMA reads
+// both; no multicast at this cluster shape). The pair reads each weight tile
+// once for up to 256 activation rows, so it is the choice when M > 128 and N
+// is wide enough to occupy the SMs without K slices.
+template <class MmaTile, class ClusterShape, class KSched, class ESched>
+struct Cfg {
+  using Epilogue = typename cutlass::epilogue::collective::CollectiveBuilder<
+      cutlass::arch::Sm100, cutlass::arch::OpClassTensorOp, MmaTile, ClusterShape,
+      cutlass::epilogue::collective::EpilogueTileAuto, float, float, float, LayoutC, 4, float,
+      LayoutC, 4, ESched>::CollectiveOp;
+  using Mainloop = typename cutlass::gemm::collective::CollectiveBuilder<
+      cutlass::arch::Sm100, cutlass::arch::OpClassTensorOp, ElementA, LayoutA, 8, ElementB,
+      LayoutB, 8, float, MmaTile, ClusterShape,
+      cutlass::gemm::collective::StageCountAutoCarveout<static_cast<int>(
+          sizeof(typename Epilogue::SharedStorage))>,
+      KSched>::CollectiveOp;
+  using Kernel =
+      cutlass::gemm::kernel::GemmUniversal<Shape<int, int, int, int>, Mainloop, Epilogue>;
+  using Gemm = cutlass::gemm::device::GemmUniversalAdapter<Kernel>;
+};
+using Gemm = Cfg<Shape<_128, _128, _64>, Shape<_1, _1, _1>,
+                 cutlass::gemm::collective::KernelScheduleAuto,
+                 cutlass::epilogue::collective::EpilogueScheduleAuto>::Gemm;
+using Gemm2 = Cfg<Shape<_256, _256, _64>, Shape<_2, _1, _1>,
+                  cutlass::gemm::KernelTmaWarpSpecialized2SmSm100,
+                  cutlass::epilogue::TmaWarpSpecialized2Sm>::Gemm;
 
-using Epilogue = typename cutlass::epilogue::collective::CollectiveBuilder<
-    cutlass::arch::Sm100, cutlass::arch::OpClassTensorOp, MmaTile, ClusterShape,
-    cutlass::epilogue::collective::EpilogueTileAuto, float, float, float, LayoutC, 4, float,
-    LayoutC, 4, cutlass::epilogue::collective::EpilogueScheduleAuto>::CollectiveOp;
-
-using Mainloop = typename cutlass::gemm::collective::CollectiveBuilder<
-    cutlass::arch::Sm100, cutlass::arch::OpClassTensorOp, ElementA, LayoutA, 8, ElementB, LayoutB,
-    8, float, MmaTile, ClusterShape,
-    cutlass::gemm::collective::StageCountAutoCarveout<static_cast<int>(
-        sizeof(typename Epilogue::SharedStorage))>,
-    cutlass::gemm::collective::KernelScheduleAuto>::CollectiveOp;
-
-using Kernel = cutlass::gemm::kernel::GemmUniversal<Shape<int, int, int, int>, Mainloop, Epilogue>;
-using Gemm = cutlass::gemm::device::GemmUniversalAdapter<Kernel>;
-
-typename Gemm::Arguments make_args(int M, int N, int K, const uint16_t* A, const uint16_t* W,
-                                   const float* C, float* D, float beta, int ldw = 0,
-                                   int splits = 1) {
-  using StrideA = typename Gemm::GemmKernel::StrideA;
-  using StrideB = typename Gemm::GemmKernel::StrideB;
-  using StrideC = typename Gemm::GemmKernel::StrideC;
-  using StrideD = typename Gemm::GemmKernel::StrideD;
+template <class G>
+typename G::Arguments make_args(int M, int N, int K, const uint16_t* A, const uint16_t* W,
+                                const float* C, float* D, float beta, int ldw = 0,
+                                int splits = 1) {
+  using StrideA = typename G::GemmKernel::StrideA;
+  using StrideB = typename G::GemmKernel::StrideB;
+  using StrideC = typename G::GemmKernel::StrideC;
+  using StrideD = typename G::GemmKernel::StrideD;
   // Split-K as the batch mode: batch l multiplies the K slice
   // [l * Kc, (l + 1) * Kc) of A and W (the same rows, Kc elements further on)
   // and writes its own [M, N] block of D, so D holds `splits` partial
@@ -71,12 +85,25 @@ typename Gemm::Arguments make_args(int M, int N, int K, const uint16_t* A, const
   cute::get<2>(sb) = Kc;
   const StrideC sc = cutlass::make_cute_packed_stride(StrideC{}, {M, N, splits});
   const StrideD sd = cutlass::make_cute_packed_stride(StrideD{}, {M, N, splits});
-  typename Gemm::Arguments args{cutlass::gemm::GemmUniversalMode::kGemm,
+  typename G::Arguments args{cutlass::gemm::GemmUniversalMode::kGemm,
                                 {M, N, Kc, splits},
                                 {reinterpret_cast<const ElementA*>(A), sa,
                                  reinterpret_cast<const ElementB*>(W), sb},
                                 {{1.0f, beta}, C ? C : D, sc, D, sd}};
   return args;
+}
+
+template <class G>
+cudaError_t run(int M, int N, int K, const uint16_t* A, const uint16_t* W, const float* C, float* D,
+                float beta, void* workspace, size_t workspace_bytes, cudaStream_t st, int ldw,
+                int splits) {
+  const typename G::Arguments args = make_args<G>(M, N, K, A, W, C, D, beta, ldw, splits);
+  G g;
+  if (g.can_implement(args) != cutlass::Status::kSuccess) return cudaErrorInvalidValue;
+  if (G::get_workspace_size(args) > workspace_bytes) return cudaErrorInvalidValue;
+  if (g.initialize(args, workspace, st) != cutlass::Status::kSuccess) return cudaErrorInvalidValue;
+  if (g.run(st) != cutlass::Status::kSuccess) return cudaErrorLaunchFailure;
+  return counted(cudaGetLastError());
 }
 
 }  // namespace
@@ -87,7 +114,16 @@ bool gemm_supported(int M, int N, int K) {
 }
 
 size_t gemm_workspace_bytes(int M, int N, int K) {
-  return Gemm::get_workspace_size(make_args(M, N, K, nullptr, nullptr, nullptr, nullptr, 0.0f));
+  return std::max(
+      Gemm::get_workspace_size(make_args<Gemm>(M, N, K, nullptr, nullptr, nullptr, nullptr, 0.0f)),
+      Gemm2::get_workspace_size(make_args<Gemm2>(M, N, K, nullptr, nullptr, nullptr, nullptr, 0.0f)));
+}
+
+int gemm_pick_pair(int M, int N, int sms) {
+  // 256 x 256 pair tiles when the rows need more than one 128-row tile and
+  // the pairs cover at least two thirds of the SMs without K slices
+  const long pairs = (long)((M + 255) / 256) * ((N + 255) / 256);
+  return M > 128 && 2 * pairs * 3 >= 2L * sms;
 }
 
 int gemm_pick_splits(int M, int N, int K, int sms) {
@@ -107,18 +143,14 @@ int gemm_pick_splits(int M, int N, int K, int sms) {
 
 cudaError_t gemm_bf16_f32(int M, int N, int K, const uint16_t* A, const uint16_t* W,
                           const float* C, float* D, float beta, void* workspace,
-                          size_t workspace_bytes, cudaStream_t st, int ldw, int splits) {
+                          size_t workspace_bytes, cudaStream_t st, int ldw, int splits, int pair) {
   if (!gemm_supported(M, N, K) || (ldw && (ldw < K || ldw % 8))) return cudaErrorInvalidValue;
   if (splits < 1 || splits > kMaxSplits || K % splits || (K / splits) % 8 ||
       (splits > 1 && (C || beta != 0.0f)))
     return cudaErrorInvalidValue;
-  const typename Gemm::Arguments args = make_args(M, N, K, A, W, C, D, beta, ldw, splits);
-  Gemm g;
-  if (g.can_implement(args) != cutlass::Status::kSuccess) return cudaErrorInvalidValue;
-  if (Gemm::get_workspace_size(args) > workspace_bytes) return cudaErrorInvalidValue;
-  if (g.initialize(args, workspace, st) != cutlass::Status::kSuccess) return cudaErrorInvalidValue;
-  if (g.run(st) != cutlass::Status::kSuccess) return cudaErrorLaunchFailure;
-  return counted(cudaGetLastError());
+  if (pair)
+    return run<Gemm2>(M, N, K, A, W, C, D, beta, workspace, workspace_bytes, st, ldw, splits);
+  return run<Gemm>(M, N, K, A, W, C, D, beta, workspace, workspace_bytes, st, ldw, splits);
 }
 
 }  // namespace myos

@@ -535,8 +535,12 @@ __global__ void __launch_bounds__(kT) k_row_argmax_part(float2* part, const floa
 }
 
 __global__ void k_row_argmax_fin(uint32_t* tok, uint32_t* out, int out_stride, int step,
-                                 const float2* part, int nc) {
+                                 const int* d_step, const float2* part, int nc) {
   const int b = blockIdx.x, lane = threadIdx.x;
+  if (d_step) {  // the step index lives on the device (graph replays)
+    step = *d_step;
+    if (step >= out_stride) out = nullptr;
+  }
   float bv = -INFINITY;
   uint32_t bi = 0xffffffffu;
   for (int c = lane; c < nc; c += 32) {
@@ -562,9 +566,17 @@ __global__ void k_rows_copy(float* dst, const float* src, const int* src_row, in
     dst[(size_t)b * K + j] = src[(size_t)src_row[b] * K + j];
 }
 
-__global__ void k_pos_advance(int* rowpos, int B) {
+__global__ void k_pos_advance(int* rowpos, int B, int* d_step) {
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b < B) rowpos[b] += 1;
+  if (d_step && b == 0) *d_step += 1;
+}
+
+// Teacher-forced token of each row at the device-held step: tok[b] =
+// feed_t[step * B + b].
+__global__ void k_feed(uint32_t* tok, const uint32_t* feed_t, const int* d_step, int B) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b < B) tok[b] = feed_t[(size_t)(*d_step) * B + b];
 }
 
 }  // namespace
@@ -572,11 +584,11 @@ __global__ void k_pos_advance(int* rowpos, int B) {
 int pf_argmax_chunks(int V) { return (V + kArgChunk - 1) / kArgChunk; }
 
 cudaError_t pf_row_argmax(uint32_t* tok, uint32_t* out, int out_stride, int step, const float* D,
-                          float2* part, int B, int V, cudaStream_t st) {
+                          float2* part, int B, int V, cudaStream_t st, const int* d_step) {
   const int nc = pf_argmax_chunks(V);
   k_row_argmax_part<<<dim3(B, nc), kT, 0, st>>>(part, D, B, V, V % 4 == 0);
   if (cudaError_t e = counted(cudaGetLastError())) return e;
-  k_row_argmax_fin<<<B, 32, 0, st>>>(tok, out, out_stride, step, part, nc);
+  k_row_argmax_fin<<<B, 32, 0, st>>>(tok, out, out_stride, step, d_step, part, nc);
   return counted(cudaGetLastError());
 }
 
@@ -586,8 +598,14 @@ cudaError_t pf_rows_copy(float* dst, const float* src, const int* src_row, int B
   return counted(cudaGetLastError());
 }
 
-cudaError_t pf_pos_advance(int* rowpos, int B, cudaStream_t st) {
-  k_pos_advance<<<(B + 127) / 128, 128, 0, st>>>(rowpos, B);
+cudaError_t pf_pos_advance(int* rowpos, int B, cudaStream_t st, int* d_step) {
+  k_pos_advance<<<(B + 127) / 128, 128, 0, st>>>(rowpos, B, d_step);
+  return counted(cudaGetLastError());
+}
+
+cudaError_t pf_feed(uint32_t* tok, const uint32_t* feed_t, const int* d_step, int B,
+                    cudaStream_t st) {
+  k_feed<<<(B + 127) / 128, 128, 0, st>>>(tok, feed_t, d_step, B);
   return counted(cudaGetLastError());
 }
 

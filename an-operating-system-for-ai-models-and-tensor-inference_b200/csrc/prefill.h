@@ -44,13 +44,19 @@ cudaError_t pf_attn(uint16_t* A, float* o_part, float2* ml, const float* Q, cons
                     size_t rowstride = 0);
 // Greedy token per row of stacked logit parts D[3B, V]; tok[b], and
 // out[b * out_stride + step] when out is non-null. part: B * pf_argmax_chunks(V)
-// float2 of scratch.
+// float2 of scratch. d_step non-null: step = *d_step, read on the device, and
+// out written only while step < out_stride.
 int pf_argmax_chunks(int V);
 cudaError_t pf_row_argmax(uint32_t* tok, uint32_t* out, int out_stride, int step, const float* D,
-                          float2* part, int B, int V, cudaStream_t st);
+                          float2* part, int B, int V, cudaStream_t st,
+                          const int* d_step = nullptr);
+// tok[b] = feed_t[*d_step * B + b] (teacher-forced batched steps).
+cudaError_t pf_feed(uint32_t* tok, const uint32_t* feed_t, const int* d_step, int B,
+                    cudaStream_t st);
 cudaError_t pf_rows_copy(float* dst, const float* src, const int* src_row, int B, int K,
                          cudaStream_t st);
-cudaError_t pf_pos_advance(int* rowpos, int B, cudaStream_t st);
+// rowpos[b] += 1 for b < B, and *d_step += 1 when d_step is non-null.
+cudaError_t pf_pos_advance(int* rowpos, int B, cudaStream_t st, int* d_step = nullptr);
 // X[t] += projection; with gamma also A = the three bf16 terms of
 // RMSNorm(X[t]) * gamma (the next projection's input).
 cudaError_t pf_resid_norm(float* X, const float* D, int sp, const float* gamma, uint16_t* A, int n,
