@@ -1767,7 +1767,7 @@ int prefill_chunk(myos_ctx* c, const uint32_t* d_ids, int n, int p0, void* kcach
     CK(pf_qkv_post(c->pf_Q, c->pf_D, sp, w.bqkv, kc, vc, kv_bf16, c->cos_t, c->sin_t, p0, n, Hq,
                    Hkv, d, S, st));
     CK(pf_attn(c->pf_A, c->at_o, c->at_ml, c->pf_Q, kc, vc, kv_bf16, p0, n, Hq, Hkv, d, S, scale,
-               p0 + n, st));
+               p0 + n, c->num_sms, st));
     if ((rc = gemm(H, qd, w.wo, (int)c->qd_pad))) return rc;
     if ((rc = resid(n, H, w.ln2))) return rc;
     if ((rc = gemm(2 * I, H, w.wg))) return rc;  // gate rows then up rows
@@ -1911,7 +1911,7 @@ static int batch_run(myos_ctx* c, size_t nseq, const uint32_t* ids, const uint32
       CK(pf_qkv_post(c->pf_Q, c->pf_D, sp, w.bqkv, kc, vc, kv_bf16, c->cos_t, c->sin_t, 0, B, Hq,
                      Hkv, d, Sb, stq, c->bt_pos, seq_elems));
       CK(pf_attn(c->pf_A, c->at_o, c->at_ml, c->pf_Q, kc, vc, kv_bf16, 0, B, Hq, Hkv, d, Sb, scale,
-                 max_keys, stq, c->bt_pos, seq_elems));
+                 max_keys, c->num_sms, stq, c->bt_pos, seq_elems));
       if ((st = gemm(H, qd, w.wo))) return st;
       CK(pf_resid_norm(c->bt_X, c->pf_D, sp, w.ln2, c->pf_A, B, H, s.rms_eps, stq));
       if ((st = gemm(2 * I, H, w.wg))) return st;

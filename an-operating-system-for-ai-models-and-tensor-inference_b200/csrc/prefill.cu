@@ -11,6 +11,8 @@
 // element-wise steps keep the reference's operation order (no contraction).
 #include <math.h>
 
+#include <algorithm>
+
 #include <cooperative_groups.h>
 
 #include "common.cuh"
@@ -188,43 +190,90 @@ MYOS_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "mem
 template <int N>
 MYOS_DEV void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
-// Shared memory of k_pf_attn_split: q heads of the group, then two buffers of
-// (K tile, V tile), rows padded to D + 4 floats.
+// Shared memory of k_pf_attn_split: two slots of (q heads of the group, K
+// tile, V tile) with K/V rows padded to D + 4 floats, the per-warp partial
+// scores, the tile's probabilities [key][head] and the heads' rescale factors.
+constexpr int kAttnWarps = kT / 32;
+template <int D>
+constexpr int attn_slot_floats() {
+  return 8 * D + 2 * kAttnTile * (D + 4);
+}
 template <int D>
 constexpr size_t attn_smem_bytes() {
-  return (size_t)(8 * D + 2 * 2 * kAttnTile * (D + 4)) * sizeof(float);
+  return (size_t)(2 * attn_slot_floats<D>() + kAttnWarps * 8 * kAttnTile + kAttnTile * 8 + 8) *
+         sizeof(float);
 }
 
+// One (row, KV head, split) item of the split attention and its tiles.
+struct AttnItem {
+  int item, tile, nt;  // item index (>= n_items: none), tile within it, its tiles
+  int t, g, s, k0, k1;
+};
+
+// Causal GQA per row, split over the keys (see pf_attn), on a persistent
+// grid: block b takes items b, b + gridDim.x, ... (item = (row t, KV head g,
+// split s), s fastest) and walks their 32-key tiles as one stream, the next
+// tile's copies (q, K, V; asynchronous for f32) in flight while this one is
+// computed, across item boundaries. Per tile: scores: warp w takes dims
+// [w D/8, (w+1) D/8) of every head, lane = key (each K element is read from
+// shared memory once, the q values are broadcasts), the 8 partial sums meet
+// in shared memory in warp order; softmax: warp h owns head h's running max
+// and sum; p * v: lane = (key group, head pair, 4 dims) of warp w's dims, so
+// each V element read serves two heads, the key groups summed by shuffles
+// when the item ends.
 template <typename KT, int D>
-__global__ void __launch_bounds__(kT, 3) k_pf_attn_split(float* o_part, float2* ml, const float* Q,
+__global__ void __launch_bounds__(kT, 2) k_pf_attn_split(float* o_part, float2* ml, const float* Q,
                                                          const KT* kcache, const KT* vcache, int p0,
-                                                         int Hq, int Hkv, int S, float scale, int ch,
-                                                         int ns, const int* rowpos,
+                                                         int n, int Hq, int Hkv, int S, float scale,
+                                                         int ch, int ns, const int* rowpos,
                                                          size_t rowstride) {
-  constexpr int ds = D + 4, V4 = D / 4, E = D / 32;  // E dims per lane in p * v
+  constexpr int ds = D + 4, V4 = D / 4;
+  constexpr int DW = D / kAttnWarps;    // dims per warp (16 or 8)
+  constexpr int CW = DW / 4;            // float4 chunks per warp
+  constexpr int LK = CW * 4;            // lanes per key group in p * v (chunk x head pair)
+  constexpr int KG = 32 / LK;           // key groups (2 or 4)
+  constexpr int SLOT = attn_slot_floats<D>();
   constexpr int kPer = (kAttnTile * V4 + kT - 1) / kT;  // float4s of K (and of V) per thread
   extern __shared__ __align__(16) float sm[];
-  float* qs = sm;
-  const int sidx = blockIdx.x, g = blockIdx.y, t = blockIdx.z, G = Hq / Hkv;
-  const int pos = rowpos ? rowpos[t] : p0 + t;
-  const int k0 = sidx * ch;
-  if (k0 > pos) return;  // this row has fewer splits (whole block)
-  const int k1 = min(k0 + ch, pos + 1);
-  if (rowpos) {
-    kcache += (size_t)t * rowstride;
-    vcache += (size_t)t * rowstride;
-  }
+  float* red = sm + 2 * SLOT;                    // [warps][8][32]
+  float* pr = red + kAttnWarps * 8 * kAttnTile;  // [32][8]
+  float* cfs = pr + kAttnTile * 8;               // [8]
+  const int G = Hq / Hkv, n_items = n * Hkv * ns;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int N = (Hq + 2 * Hkv) * D;
-  const KT* kc = kcache + (size_t)g * S * D;
-  const KT* vc = vcache + (size_t)g * S * D;
-  // tile i -> buffer i & 1: f32 rows go straight to shared memory with
-  // asynchronous copies (the next tile's copies overlap this tile's math);
-  // bf16 rows are widened through registers
-  auto stage = [&](int t0, int buf) {
-    float* ks = sm + 8 * D + buf * 2 * kAttnTile * ds;
+
+  auto open_item = [&](AttnItem& it, int item) {  // first non-empty item from `item` on
+    for (; item < n_items; item += gridDim.x) {
+      const int s = item % ns, g = (item / ns) % Hkv, t = item / (ns * Hkv);
+      const int pos = rowpos ? rowpos[t] : p0 + t, k0 = s * ch;
+      if (k0 > pos) continue;  // this row has fewer splits
+      it.item = item;
+      it.tile = 0;
+      it.t = t;
+      it.g = g;
+      it.s = s;
+      it.k0 = k0;
+      it.k1 = min(k0 + ch, pos + 1);
+      it.nt = (it.k1 - k0 + kAttnTile - 1) / kAttnTile;
+      return;
+    }
+    it.item = n_items;
+  };
+  auto advance = [&](AttnItem it) {
+    if (++it.tile < it.nt) return it;
+    open_item(it, it.item + gridDim.x);
+    return it;
+  };
+  auto stage = [&](const AttnItem& it, int slot) {
+    float* qs = sm + slot * SLOT;
+    float* ks = qs + 8 * D;
     float* vs = ks + kAttnTile * ds;
-    const int nk = min(kAttnTile, k1 - t0);
+    const size_t cofs = (rowpos ? (size_t)it.t * rowstride : 0) + (size_t)it.g * S * D;
+    const KT* kc = kcache + cofs;
+    const KT* vc = vcache + cofs;
+    const int t0 = it.k0 + it.tile * kAttnTile, nk = min(kAttnTile, it.k1 - t0);
+    const float* q = Q + (size_t)it.t * N + (size_t)it.g * G * D;
+    for (int i = threadIdx.x; i < G * V4; i += kT) cp_async16(qs + 4 * i, q + 4 * i);
 #pragma unroll
     for (int i = 0; i < kPer; ++i) {
       const int idx = threadIdx.x + i * kT, tt = idx / V4, e = (idx - tt * V4) * 4;
@@ -240,66 +289,122 @@ __global__ void __launch_bounds__(kT, 3) k_pf_attn_split(float* o_part, float2* 
     }
     cp_async_commit();
   };
-  stage(k0, 0);
-  const float* q = Q + (size_t)t * N + (size_t)g * G * D;
-  for (int i = threadIdx.x; i < G * V4; i += blockDim.x)
-    reinterpret_cast<float4*>(qs)[i] = reinterpret_cast<const float4*>(q)[i];
-  float acc[E];
-#pragma unroll
-  for (int e = 0; e < E; ++e) acc[e] = 0.0f;
-  float m_run = -INFINITY, l_run = 0.0f;
-  int buf = 0;
-  for (int t0 = k0; t0 < k1; t0 += kAttnTile, buf ^= 1) {
-    if (t0 + kAttnTile < k1) {
-      stage(t0 + kAttnTile, buf ^ 1);
+
+  // p * v lane roles
+  const int kg = lane / LK, hp = (lane % LK) / CW, cq = lane % CW;
+  const int dv = warp * DW + cq * 4;  // this lane's 4 dims
+  float4 acc[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
+  float m_run = -INFINITY, l_run = 0.0f;  // warp h < G: head h
+
+  AttnItem cur;
+  open_item(cur, blockIdx.x);
+  if (cur.item >= n_items) return;
+  stage(cur, 0);
+  AttnItem nxt = advance(cur);
+  int slot = 0;
+  while (cur.item < n_items) {
+    if (nxt.item < n_items) {
+      stage(nxt, slot ^ 1);
       cp_async_wait<1>();  // this tile's group has landed
     } else {
       cp_async_wait<0>();
     }
-    __syncthreads();  // every thread's copies of this tile (and qs) are visible
-    const float* ks = sm + 8 * D + buf * 2 * kAttnTile * ds;
+    __syncthreads();  // every thread's copies of this tile are visible
+    const float* qs = sm + slot * SLOT;
+    const float* ks = qs + 8 * D;
     const float* vs = ks + kAttnTile * ds;
-    const int nk = min(kAttnTile, k1 - t0);
-    if (warp < G) {
-      const float* qh = qs + warp * D;
+    const int nk = min(kAttnTile, cur.k1 - (cur.k0 + cur.tile * kAttnTile));
+    {  // partial scores of key `lane` over this warp's dims, heads < G
+      float sc[8];
+#pragma unroll
+      for (int h = 0; h < 8; ++h) sc[h] = 0.0f;
+      if (lane < nk) {
+#pragma unroll
+        for (int c = 0; c < CW; ++c) {
+          const int e = warp * DW + 4 * c;
+          const float4 kv = *reinterpret_cast<const float4*>(ks + lane * ds + e);
+#pragma unroll
+          for (int h = 0; h < 8; ++h) {
+            if (h < G) {
+              const float4 qv = *reinterpret_cast<const float4*>(qs + h * D + e);
+              sc[h] = fmaf(qv.x, kv.x, sc[h]);
+              sc[h] = fmaf(qv.y, kv.y, sc[h]);
+              sc[h] = fmaf(qv.z, kv.z, sc[h]);
+              sc[h] = fmaf(qv.w, kv.w, sc[h]);
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int h = 0; h < 8; ++h) red[(warp * 8 + h) * kAttnTile + lane] = sc[h];
+    }
+    __syncthreads();
+    if (warp < G) {  // online softmax of head `warp` over this tile
       float sc = -INFINITY;
       if (lane < nk) {
-        const float* kp = ks + lane * ds;
-        float p0s = 0.f, p1 = 0.f, p2 = 0.f, p3 = 0.f;
+        float v = 0.0f;
 #pragma unroll
-        for (int e = 0; e < D; e += 4) {
-          const float4 a = *reinterpret_cast<const float4*>(qh + e);
-          const float4 b = *reinterpret_cast<const float4*>(kp + e);
-          p0s = fmaf(a.x, b.x, p0s);
-          p1 = fmaf(a.y, b.y, p1);
-          p2 = fmaf(a.z, b.z, p2);
-          p3 = fmaf(a.w, b.w, p3);
-        }
-        sc = __fmul_rn((p0s + p1) + (p2 + p3), scale);
+        for (int w = 0; w < kAttnWarps; ++w) v = __fadd_rn(v, red[(w * 8 + warp) * kAttnTile + lane]);
+        sc = __fmul_rn(v, scale);
       }
       const float mn = fmaxf(m_run, warp_max(sc));
       const float cf = expf(m_run - mn);
       const float pk = lane < nk ? expf(sc - mn) : 0.0f;
       l_run = fmaf(l_run, cf, warp_sum(pk));
       m_run = mn;
-#pragma unroll
-      for (int e = 0; e < E; ++e) acc[e] *= cf;
-#pragma unroll 8
-      for (int k = 0; k < nk; ++k) {
-        const float pb = __shfl_sync(0xffffffffu, pk, k);
-        const float* vr_ = vs + k * ds + lane * E;
-#pragma unroll
-        for (int e = 0; e < E; ++e) acc[e] = fmaf(pb, vr_[e], acc[e]);
+      pr[lane * 8 + warp] = pk;
+      if (lane == 0) cfs[warp] = cf;
+    } else {
+      pr[lane * 8 + warp] = 0.0f;
+      if (lane == 0) cfs[warp] = 1.0f;
+    }
+    __syncthreads();
+    {  // p * v for heads 2hp, 2hp + 1 on dims dv..dv+3, keys kg, kg + KG, ...
+      const float c0 = cfs[2 * hp], c1 = cfs[2 * hp + 1];
+      acc[0].x *= c0; acc[0].y *= c0; acc[0].z *= c0; acc[0].w *= c0;
+      acc[1].x *= c1; acc[1].y *= c1; acc[1].z *= c1; acc[1].w *= c1;
+#pragma unroll 4
+      for (int k = kg; k < nk; k += KG) {
+        const float4 v = *reinterpret_cast<const float4*>(vs + k * ds + dv);
+        const float2 pp = *reinterpret_cast<const float2*>(pr + k * 8 + 2 * hp);
+        acc[0].x = fmaf(pp.x, v.x, acc[0].x);
+        acc[0].y = fmaf(pp.x, v.y, acc[0].y);
+        acc[0].z = fmaf(pp.x, v.z, acc[0].z);
+        acc[0].w = fmaf(pp.x, v.w, acc[0].w);
+        acc[1].x = fmaf(pp.y, v.x, acc[1].x);
+        acc[1].y = fmaf(pp.y, v.y, acc[1].y);
+        acc[1].z = fmaf(pp.y, v.z, acc[1].z);
+        acc[1].w = fmaf(pp.y, v.w, acc[1].w);
       }
     }
-    __syncthreads();  // this buffer is consumed before the next stage reuses it
-  }
-  if (warp < G) {
-    const size_t slot = ((size_t)t * Hq + (size_t)g * G + warp) * ns + sidx;
-    float* o = o_part + slot * D + lane * E;
+    if (cur.tile + 1 == cur.nt) {  // the item is done: its partial out, then a fresh state
+      // key groups summed in a fixed order (xor tree over the group bits)
 #pragma unroll
-    for (int e = 0; e < E; ++e) o[e] = acc[e];
-    if (lane == 0) ml[slot] = make_float2(m_run, l_run);
+      for (int o = LK; o < 32; o <<= 1)
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          acc[j].x += __shfl_xor_sync(0xffffffffu, acc[j].x, o);
+          acc[j].y += __shfl_xor_sync(0xffffffffu, acc[j].y, o);
+          acc[j].z += __shfl_xor_sync(0xffffffffu, acc[j].z, o);
+          acc[j].w += __shfl_xor_sync(0xffffffffu, acc[j].w, o);
+        }
+      const size_t base = ((size_t)cur.t * Hq + (size_t)cur.g * G) * ns + cur.s;
+      if (kg == 0) {
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int h = 2 * hp + j;
+          if (h < G) *reinterpret_cast<float4*>(o_part + (base + (size_t)h * ns) * D + dv) = acc[j];
+        }
+      }
+      if (warp < G && lane == 0) ml[base + (size_t)warp * ns] = make_float2(m_run, l_run);
+      acc[0] = acc[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+      m_run = -INFINITY;
+      l_run = 0.0f;
+    }
+    __syncthreads();  // this slot, the scores and the probabilities are consumed
+    cur = nxt;
+    nxt = advance(nxt);
+    slot ^= 1;
   }
 }
 
@@ -664,23 +769,24 @@ int pf_attn_splits(int max_keys, int* ch) {
 
 cudaError_t pf_attn(uint16_t* A, float* o_part, float2* ml, const float* Q, const void* kc,
                     const void* vc, int kv_bf16, int p0, int n, int Hq, int Hkv, int d, int S,
-                    float scale, int max_keys, cudaStream_t st, const int* rowpos,
+                    float scale, int max_keys, int sms, cudaStream_t st, const int* rowpos,
                     size_t rowstride) {
-  if (!pf_attn_supported(d, Hq / Hkv) || max_keys < 1) return cudaErrorInvalidValue;
+  if (!pf_attn_supported(d, Hq / Hkv) || max_keys < 1 || sms < 1) return cudaErrorInvalidValue;
   int ch = 0;
   const int ns = pf_attn_splits(max_keys, &ch);
-  const dim3 grid(ns, Hkv, n);
+  const long items = (long)n * Hkv * ns;
+  const dim3 grid((unsigned)std::min<long>(items, 2L * sms));  // two resident blocks per SM
 #define MYOS_PF_ATTN(D)                                                                          \
   if (d == D) {                                                                                  \
     const size_t smem = attn_smem_bytes<D>();                                                    \
     if (kv_bf16)                                                                                 \
       k_pf_attn_split<__nv_bfloat16, D><<<grid, kT, smem, st>>>(                                 \
-          o_part, ml, Q, (const __nv_bfloat16*)kc, (const __nv_bfloat16*)vc, p0, Hq, Hkv, S,     \
+          o_part, ml, Q, (const __nv_bfloat16*)kc, (const __nv_bfloat16*)vc, p0, n, Hq, Hkv, S,  \
           scale, ch, ns, rowpos, rowstride);                                                     \
     else                                                                                         \
       k_pf_attn_split<float, D><<<grid, kT, smem, st>>>(o_part, ml, Q, (const float*)kc,         \
-                                                        (const float*)vc, p0, Hq, Hkv, S, scale, \
-                                                        ch, ns, rowpos, rowstride);              \
+                                                        (const float*)vc, p0, n, Hq, Hkv, S,     \
+                                                        scale, ch, ns, rowpos, rowstride);       \
   }
   MYOS_PF_ATTN(64)
   MYOS_PF_ATTN(128)

@@ -40,8 +40,8 @@ constexpr int kAttnMaxSplits = 64;
 int pf_attn_splits(int max_keys, int* ch);
 cudaError_t pf_attn(uint16_t* A, float* o_part, float2* ml, const float* Q, const void* kc,
                     const void* vc, int kv_bf16, int p0, int n, int Hq, int Hkv, int d, int S,
-                    float scale, int max_keys, cudaStream_t st, const int* rowpos = nullptr,
-                    size_t rowstride = 0);
+                    float scale, int max_keys, int sms, cudaStream_t st,
+                    const int* rowpos = nullptr, size_t rowstride = 0);
 // Greedy token per row of stacked logit parts D[3B, V]; tok[b], and
 // out[b * out_stride + step] when out is non-null. part: B * pf_argmax_chunks(V)
 // float2 of scratch. d_step non-null: step = *d_step, read on the device, and
