@@ -105,7 +105,7 @@ struct myos_ctx {
   float* mlp_part = nullptr;                  // [hidden][grid_mlp] down_proj shares
   unsigned long long* mlp_arrive = nullptr;   // grid-wide arrival count
   uint16_t* mlp_wd = nullptr;  // [L][grid_mlp][hidden][64] down_proj by block (null: in place)
-  int mlp_pf_rows = 0;  // MYOS_MLP_PF (default 32): gate/up rows per MLP block that o_proj pulls into L2
+  int mlp_pf_rows = 0;  // MYOS_MLP_PF (default 64): gate/up rows per MLP block that o_proj pulls into L2
   // GEMM prefill (chunks of pf_chunk prompt tokens through the tensor cores)
   bool pf_ok = false;
   int pf_chunk = 0;
@@ -1043,7 +1043,7 @@ static int create_impl(myos_ctx* c, const myos_shape* shape, const myos_opts* op
       // a second copy of down_proj, by block (MYOS_MLP=i reads it in place)
       if (!(e && e[0] == 'i')) CK(cudaMalloc(&c->mlp_wd, (size_t)L * H * I * 2));
       const char* pe = getenv("MYOS_MLP_PF");
-      c->mlp_pf_rows = pe ? atoi(pe) : 32;
+      c->mlp_pf_rows = pe ? atoi(pe) : kMlpSlice;
       if (c->mlp_pf_rows < 0 || c->mlp_pf_rows > kMlpSlice) c->mlp_pf_rows = 0;
     }
   }
