@@ -396,8 +396,9 @@ MYOS_DEV void epilogue(const GemvArgs& a, int row, float v, float v2, float& bv,
   if (EPI == EPI_SWIGLU) a.y[row] = silu_mul(v, v2);
 }
 
-// Block-level first maximum, then the last block to arrive reduces the
-// per-block results in block order and advances the step control
+// Block-level first maximum, then the last block to arrive picks among the
+// per-block results (all its threads, the same total order) and advances
+// the step control
 // (greedy_token then KvCache::advance, qwen25_block.rs:765-780).
 MYOS_DEV void argmax_finish(const GemvArgs& a, float bv, uint32_t bi, float* wbv, uint32_t* wbi,
                             int* last_block) {
@@ -423,18 +424,41 @@ MYOS_DEV void argmax_finish(const GemvArgs& a, float bv, uint32_t bi, float* wbv
     *last_block = prev == (unsigned)(G - 1);
   }
   __syncthreads();
-  if (*last_block && threadIdx.x == 0) {
-    __threadfence();
-    float v = -INFINITY;
-    uint32_t i = 0xffffffffu;
-    for (int q = 0; q < G; ++q) {
-      const float pv = __ldcg(a.part_val + q);
-      const uint32_t pi = __ldcg(a.part_idx + q);
-      if (better(pv, pi, v, i)) {
-        v = pv;
-        i = pi;
-      }
+  if (!*last_block) return;  // block-uniform
+  // The last block picks among the G block candidates with every thread:
+  // "better" is a total order (larger value, then smaller index; NaN never
+  // wins), so the pick does not depend on the reduction order.
+  __threadfence();
+  float v = -INFINITY;
+  uint32_t i = 0xffffffffu;
+  for (int q = threadIdx.x; q < G; q += blockDim.x) {
+    const float pv = __ldcg(a.part_val + q);
+    const uint32_t pi = __ldcg(a.part_idx + q);
+    if (better(pv, pi, v, i)) {
+      v = pv;
+      i = pi;
     }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+    const uint32_t oi = __shfl_xor_sync(0xffffffffu, i, o);
+    if (better(ov, oi, v, i)) {
+      v = ov;
+      i = oi;
+    }
+  }
+  if (lane == 0) {
+    wbv[warp] = v;
+    wbi[warp] = i;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 0; w < nw; ++w)
+      if (better(wbv[w], wbi[w], v, i)) {
+        v = wbv[w];
+        i = wbi[w];
+      }
     if (a.tp_cand || a.push.n) {  // this rank's vocab slice: hand over for the global pick
       const float iv = __uint_as_float(i == 0xffffffffu ? i : i + a.row0);
       if (a.push.n) {
@@ -1281,11 +1305,17 @@ MYOS_DEV void dec_tile_finish(int d, int t0, int nk, int skip, float* ks, float*
   }
 }
 
+// Per-tile work areas of k_attn_dec after the partials: the warps' partial
+// scores [8 warps][8 heads][kTile], the probabilities [kTile][8] and the
+// heads' rescale factors [8].
+constexpr int kDecWarps = kThreads / 32;
+constexpr size_t kDecWork = (size_t)kDecWarps * 8 * kTile + (size_t)kTile * 8 + 8;
+
 size_t attn_dec_smem_bytes(int G, int d) {
-  // q, two padded tiles, new k/v, rotation row, raw bf16 tile rows, and the
-  // block's partial (output, max, sum) for the cluster merge
+  // q, two padded tiles, new k/v, rotation row, raw bf16 tile rows, the
+  // block's partial (output, max, sum) for the cluster merge, the tile work
   return ((size_t)G * d + 2 * kTile * (d + 4) + 3 * (size_t)d + (size_t)kTile * d +
-          (size_t)G * d + 2 * kMaxG) * sizeof(float);
+          (size_t)G * d + 2 * kMaxG + kDecWork) * sizeof(float);
 }
 
 // One warp merges one head over the splits q < ne that hold keys:
@@ -1402,7 +1432,7 @@ struct ClusterPartials {
 };
 
 template <typename KT, int D>
-__global__ void __launch_bounds__(kThreads) k_attn_dec(AttnArgs a) {
+__global__ void __launch_bounds__(kThreads, 1) k_attn_dec(AttnArgs a) {
   extern __shared__ float4 smem4[];
   float* sm = reinterpret_cast<float*>(smem4);
   constexpr int d = D, half = D / 2, ds = D + 4;  // head dim fixed at compile time
@@ -1478,8 +1508,21 @@ __global__ void __launch_bounds__(kThreads) k_attn_dec(AttnArgs a) {
   }
 
   trace_mark(trow, 4);  // rotated, new key stored
+  // Tile work layout (8 warps): scores: warp w takes dims [w D/8, (w+1) D/8)
+  // of every head, lane = key, each K element read from shared memory once
+  // (q values are broadcasts); the 8 partial sums meet in shared memory and
+  // are added in warp order; softmax: warp h < G owns head h's running max
+  // and sum; p * v: lane = (key group kg, head pair hp, 4 dims) of warp w's
+  // dims, so each V element read serves two heads; the key groups are summed
+  // by shuffles after the last tile.
+  constexpr int DW = D / kDecWarps, CW = DW / 4, LK = CW * 4, KG = 32 / LK;
+  float* red = reinterpret_cast<float*>(raw) + kTile * d + G * d + 2 * kMaxG;  // [8][8][kTile]
+  float* pr = red + kDecWarps * 8 * kTile;                                    // [kTile][8]
+  float* cfs = pr + kTile * 8;                                                // [8]
+  const int kg = lane / LK, hp = (lane % LK) / CW, cq = lane % CW;
+  const int dv = warp * DW + cq * 4;  // this lane's 4 dims in p * v
   float4 acc[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
-  float m_run = -INFINITY, l_run = 0.0f;
+  float m_run = -INFINITY, l_run = 0.0f;  // warp h < G: head h
   for (int t0 = kb; t0 < ke; t0 += kTile) {
     const int nk = min(kTile, ke - t0);
     if (t0 != kb) {  // later tiles
@@ -1493,51 +1536,80 @@ __global__ void __launch_bounds__(kThreads) k_attn_dec(AttnArgs a) {
         }
       __syncthreads();
     }
-    if (warp < G) {
-      const float* qh = qs + warp * d;
+    {  // partial scores of key `lane` over this warp's dims, heads < G
+      float sc[8];
+#pragma unroll
+      for (int h = 0; h < 8; ++h) sc[h] = 0.0f;
+      if (lane < nk) {
+#pragma unroll
+        for (int c = 0; c < CW; ++c) {
+          const int e = warp * DW + 4 * c;
+          const float4 kv = *reinterpret_cast<const float4*>(ks + lane * ds + e);
+#pragma unroll
+          for (int h = 0; h < 8; ++h) {
+            if (h < G) {
+              const float4 qv = *reinterpret_cast<const float4*>(qs + h * d + e);
+              sc[h] = fmaf(qv.x, kv.x, sc[h]);
+              sc[h] = fmaf(qv.y, kv.y, sc[h]);
+              sc[h] = fmaf(qv.z, kv.z, sc[h]);
+              sc[h] = fmaf(qv.w, kv.w, sc[h]);
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int h = 0; h < 8; ++h) red[(warp * 8 + h) * kTile + lane] = sc[h];
+    }
+    __syncthreads();
+    if (warp < G) {  // online softmax of head `warp` over this tile
       float sc = -INFINITY;
       if (lane < nk) {
-        const float* kr = ks + lane * ds;
-        float p0 = 0.f, p1 = 0.f, p2 = 0.f, p3 = 0.f;
+        float v = 0.0f;
 #pragma unroll
-        for (int e = 0; e < d; e += 4) {
-          const float4 q = *reinterpret_cast<const float4*>(qh + e);
-          const float4 k = *reinterpret_cast<const float4*>(kr + e);
-          p0 = fmaf(q.x, k.x, p0);
-          p1 = fmaf(q.y, k.y, p1);
-          p2 = fmaf(q.z, k.z, p2);
-          p3 = fmaf(q.w, k.w, p3);
-        }
-        sc = __fmul_rn((p0 + p1) + (p2 + p3), a.scale);
+        for (int w = 0; w < kDecWarps; ++w) v = __fadd_rn(v, red[(w * 8 + warp) * kTile + lane]);
+        sc = __fmul_rn(v, a.scale);
       }
       const float mn = fmaxf(m_run, warp_max(sc));
       const float cf = expf(m_run - mn);  // 0 on the first tile (m_run = -inf)
       const float p = lane < nk ? expf(sc - mn) : 0.0f;
       l_run = fmaf(l_run, cf, warp_sum(p));
       m_run = mn;
-      for (int j = 0; j < 2; ++j) {
-        acc[j].x *= cf;
-        acc[j].y *= cf;
-        acc[j].z *= cf;
-        acc[j].w *= cf;
-      }
-#pragma unroll 8
-      for (int t = 0; t < nk; ++t) {
-        const float pt = __shfl_sync(0xffffffffu, p, t);
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          const int e = 4 * lane + 128 * j;
-          if (e < d) {
-            const float4 v = *reinterpret_cast<const float4*>(vs + t * ds + e);
-            acc[j].x = fmaf(pt, v.x, acc[j].x);
-            acc[j].y = fmaf(pt, v.y, acc[j].y);
-            acc[j].z = fmaf(pt, v.z, acc[j].z);
-            acc[j].w = fmaf(pt, v.w, acc[j].w);
-          }
-        }
+      pr[lane * 8 + warp] = p;
+      if (lane == 0) cfs[warp] = cf;
+    } else {
+      pr[lane * 8 + warp] = 0.0f;
+      if (lane == 0) cfs[warp] = 1.0f;
+    }
+    __syncthreads();
+    {  // p * v for heads 2hp, 2hp + 1 on dims dv..dv+3, keys kg, kg + KG, ...
+      const float c0 = cfs[2 * hp], c1 = cfs[2 * hp + 1];
+      acc[0].x *= c0; acc[0].y *= c0; acc[0].z *= c0; acc[0].w *= c0;
+      acc[1].x *= c1; acc[1].y *= c1; acc[1].z *= c1; acc[1].w *= c1;
+#pragma unroll 4
+      for (int t = kg; t < nk; t += KG) {
+        const float4 v = *reinterpret_cast<const float4*>(vs + t * ds + dv);
+        const float2 pp = *reinterpret_cast<const float2*>(pr + t * 8 + 2 * hp);
+        acc[0].x = fmaf(pp.x, v.x, acc[0].x);
+        acc[0].y = fmaf(pp.x, v.y, acc[0].y);
+        acc[0].z = fmaf(pp.x, v.z, acc[0].z);
+        acc[0].w = fmaf(pp.x, v.w, acc[0].w);
+        acc[1].x = fmaf(pp.y, v.x, acc[1].x);
+        acc[1].y = fmaf(pp.y, v.y, acc[1].y);
+        acc[1].z = fmaf(pp.y, v.z, acc[1].z);
+        acc[1].w = fmaf(pp.y, v.w, acc[1].w);
       }
     }
   }
+  // key groups summed in a fixed order (xor tree over the group bits)
+#pragma unroll
+  for (int o = LK; o < 32; o <<= 1)
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      acc[j].x += __shfl_xor_sync(0xffffffffu, acc[j].x, o);
+      acc[j].y += __shfl_xor_sync(0xffffffffu, acc[j].y, o);
+      acc[j].z += __shfl_xor_sync(0xffffffffu, acc[j].z, o);
+      acc[j].w += __shfl_xor_sync(0xffffffffu, acc[j].w, o);
+    }
   trace_mark(trow, 5);  // tiles done
   const int ne = min(ns, (pos + a.chunk) / a.chunk);  // splits that hold keys
   if (a.cluster) {
@@ -1546,15 +1618,13 @@ __global__ void __launch_bounds__(kThreads) k_attn_dec(AttnArgs a) {
     float* pso = reinterpret_cast<float*>(raw) + kTile * d;  // [G][d]
     float* psm = pso + G * d;                                // [kMaxG]
     float* psl = psm + kMaxG;
-    if (warp < G) {
-      for (int j = 0; j < 2; ++j) {
-        const int e = 4 * lane + 128 * j;
-        if (e < d) *reinterpret_cast<float4*>(pso + warp * d + e) = acc[j];
-      }
-      if (lane == 0) {
-        psm[warp] = m_run;
-        psl[warp] = l_run;
-      }
+    if (kg == 0)
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+        if (2 * hp + j < G) *reinterpret_cast<float4*>(pso + (2 * hp + j) * d + dv) = acc[j];
+    if (warp < G && lane == 0) {
+      psm[warp] = m_run;
+      psl[warp] = l_run;
     }
     cg::this_cluster().sync();
     trace_mark(trow, 6);  // partials visible across the cluster
@@ -1568,15 +1638,14 @@ __global__ void __launch_bounds__(kThreads) k_attn_dec(AttnArgs a) {
     cg::this_cluster().sync();  // peers' shared memory stays valid until every read is done
   } else {
     const size_t pb = ((size_t)g * ns + s) * G;  // partial row of (g, s, head 0)
-    if (warp < G) {
-      for (int j = 0; j < 2; ++j) {
-        const int e = 4 * lane + 128 * j;
-        if (e < d) *reinterpret_cast<float4*>(a.part_o + (pb + warp) * d + e) = acc[j];
-      }
-      if (lane == 0) {
-        a.part_m[pb + warp] = m_run;
-        a.part_l[pb + warp] = l_run;
-      }
+    if (kg == 0)
+#pragma unroll
+      for (int j = 0; j < 2; ++j)
+        if (2 * hp + j < G)
+          *reinterpret_cast<float4*>(a.part_o + (pb + 2 * hp + j) * d + dv) = acc[j];
+    if (warp < G && lane == 0) {
+      a.part_m[pb + warp] = m_run;
+      a.part_l[pb + warp] = l_run;
     }
     if (!a.defer_merge) {
       __threadfence();
