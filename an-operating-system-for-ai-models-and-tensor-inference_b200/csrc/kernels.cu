@@ -1311,11 +1311,17 @@ MYOS_DEV void dec_tile_finish(int d, int t0, int nk, int skip, float* ks, float*
 constexpr int kDecWarps = kThreads / 32;
 constexpr size_t kDecWork = (size_t)kDecWarps * 8 * kTile + (size_t)kTile * 8 + 8;
 
+// Cluster merge inbox of k_attn_dec: the partials (output, max, sum) the
+// cluster's blocks push for the heads this block merges, slot w * ns + q for
+// its w-th head and split q (at most 2 * kMaxG slots: ceil(G / ns) * ns).
+constexpr int kDecInbox = 2 * kMaxG;
+
 size_t attn_dec_smem_bytes(int G, int d) {
   // q, two padded tiles, new k/v, rotation row, raw bf16 tile rows, the
-  // block's partial (output, max, sum) for the cluster merge, the tile work
+  // block's partial (output, max, sum), the tile work, the merge inbox
   return ((size_t)G * d + 2 * kTile * (d + 4) + 3 * (size_t)d + (size_t)kTile * d +
-          (size_t)G * d + 2 * kMaxG + kDecWork) * sizeof(float);
+          (size_t)G * d + 2 * kMaxG + kDecWork + (size_t)kDecInbox * (d + 2)) *
+         sizeof(float);
 }
 
 // One warp merges one head over the splits q < ne that hold keys:
@@ -1420,14 +1426,14 @@ struct GlobalPartials {
   }
 };
 
-// Split partials in the shared memory of the cluster's blocks (rank q = split q).
-struct ClusterPartials {
-  float *pso, *psm, *psl;  // this block's copies; peers hold theirs at the same offsets
-  int h, d;
-  MYOS_DEV float m(int q) const { return cg::this_cluster().map_shared_rank(psm, q)[h]; }
-  MYOS_DEV float l(int q) const { return cg::this_cluster().map_shared_rank(psl, q)[h]; }
+// Split partials pushed into this block's shared memory (split q at q).
+struct LocalPartials {
+  const float *po, *pm, *pl;
+  int d;
+  MYOS_DEV float m(int q) const { return pm[q]; }
+  MYOS_DEV float l(int q) const { return pl[q]; }
   MYOS_DEV float4 o(int q, int e) const {
-    return *reinterpret_cast<const float4*>(cg::this_cluster().map_shared_rank(pso, q) + h * d + e);
+    return *reinterpret_cast<const float4*>(po + (size_t)q * d + e);
   }
 };
 
@@ -1613,29 +1619,38 @@ __global__ void __launch_bounds__(kThreads, 1) k_attn_dec(AttnArgs a) {
   trace_mark(trow, 5);  // tiles done
   const int ne = min(ns, (pos + a.chunk) / a.chunk);  // splits that hold keys
   if (a.cluster) {
-    // The blocks of KV head g form one cluster (rank = split): partials stay
-    // in shared memory and the merge reads them across the cluster.
-    float* pso = reinterpret_cast<float*>(raw) + kTile * d;  // [G][d]
-    float* psm = pso + G * d;                                // [kMaxG]
-    float* psl = psm + kMaxG;
+    // The blocks of KV head g form one cluster (rank = split). Each block
+    // pushes its partial of head h into the shared memory of block h % ns
+    // (which merges head h, as its (h / ns)-th head) with remote stores;
+    // after one cluster barrier the merge reads only local shared memory,
+    // and no block touches a peer's memory again.
+    float* in_o = red + kDecWork;                // [kDecInbox][d]
+    float* in_m = in_o + (size_t)kDecInbox * d;  // [kDecInbox]
+    float* in_l = in_m + kDecInbox;              // [kDecInbox]
+    cg::cluster_group cl = cg::this_cluster();
     if (kg == 0)
 #pragma unroll
-      for (int j = 0; j < 2; ++j)
-        if (2 * hp + j < G) *reinterpret_cast<float4*>(pso + (2 * hp + j) * d + dv) = acc[j];
+      for (int j = 0; j < 2; ++j) {
+        const int h = 2 * hp + j;
+        if (h < G) {
+          float* dst = cl.map_shared_rank(in_o, h % ns) + (size_t)((h / ns) * ns + s) * d + dv;
+          *reinterpret_cast<float4*>(dst) = acc[j];
+        }
+      }
     if (warp < G && lane == 0) {
-      psm[warp] = m_run;
-      psl[warp] = l_run;
+      const int slot = (warp / ns) * ns + s, r = warp % ns;
+      *cl.map_shared_rank(in_m + slot, r) = m_run;
+      *cl.map_shared_rank(in_l + slot, r) = l_run;
     }
-    cg::this_cluster().sync();
-    trace_mark(trow, 6);  // partials visible across the cluster
-    // block s merges heads s, s + ns, ... one warp each
+    cl.sync();
+    trace_mark(trow, 6);  // partials pushed and visible
+    // block s merges heads s, s + ns, ... (its w-th head on warp w)
     const int h = s + ns * warp;
     if (h < G) {
-      ClusterPartials src = {pso, psm, psl, h, d};
+      LocalPartials src = {in_o + (size_t)warp * ns * d, in_m + warp * ns, in_l + warp * ns, d};
       merge_head(src, ne, d, lane, a.out + ((size_t)g * G + h) * d);
     }
     trace_mark(trow, 7);  // merged
-    cg::this_cluster().sync();  // peers' shared memory stays valid until every read is done
   } else {
     const size_t pb = ((size_t)g * ns + s) * G;  // partial row of (g, s, head 0)
     if (kg == 0)
