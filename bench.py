@@ -519,8 +519,9 @@ def run_ours(args, world, rank, local, pg):
             "ms_per_step": round((tot_pre + tot_dec) / args.steps, 3),
             "higher_is_better": True, "scaling": "weak",
             "vs_baseline": round(value / PUBLISHED_DECODE, 2),
-            "dtype": "bf16 weights, f32 activations/accumulate (prefill: activations as hi+lo "
-                     "bf16 pairs into the tensor cores, 16 of 24 mantissa bits)",
+            "dtype": "bf16 weights, f32 activations/accumulate (prefill and batched decode: each "
+                     "f32 activation as three bf16 terms hi+mid+lo that sum to it exactly, into "
+                     "the tensor cores with f32 accumulation)",
             "data": "synthetic (seeded random-init Qwen2.5-1.5B BF16 weights, uniform prompt ids)",
             "config": s1_config(args, world),
             "prefill_tok_s": round(prefill_tps, 1),
