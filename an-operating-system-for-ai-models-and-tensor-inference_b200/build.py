@@ -76,7 +76,8 @@ def build(force: bool = False, verbose: bool = False) -> dict:
         if force or _stale(o, [s] + hdrs):
             cmd = [nvcc()] + NVCC_FLAGS + ["-c", s, "-o", o]
             if src == "gemm_sm100.cu":
-                cmd = [nvcc()] + NVCC_FLAGS + cutlass_include() + ["-c", s, "-o", o]
+                cmd = [nvcc()] + NVCC_FLAGS + cutlass_include() + [
+                    "-DCUTLASS_ENABLE_GDC_FOR_SM100=1", "-c", s, "-o", o]
             if src.endswith(".cpp"):
                 cmd = [nvcc()] + NVCC_FLAGS + ["-x", "cu", "-c", s, "-o", o]
             if verbose:

@@ -1711,7 +1711,7 @@ static cudaError_t pf_gemm(const myos_ctx* c, int M, int N, int K, const uint16_
   if (!sp) sp = &one;
   else *sp = pair ? 1 : pf_splits(c, M, N, K);
   return gemm_bf16_f32(M, N, K, c->pf_A, W, nullptr, D, 0.0f, c->pf_ws, c->pf_ws_bytes, st, ldw,
-                       *sp, pair);
+                       *sp, pair, pf_pdl());
 }
 
 // One chunk of n prompt tokens at positions p0.. through every layer

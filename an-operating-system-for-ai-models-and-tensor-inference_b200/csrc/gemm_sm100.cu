@@ -12,6 +12,9 @@
 // exact; only the f32 accumulation order differs from the reference's.
 // (CUTLASS's stream-K tile scheduler measured slower here than one output
 // tile per CTA: 5.27 vs 4.86 ms for a 128-token prefill.)
+#ifndef CUTLASS_ENABLE_GDC_FOR_SM100
+#error "gemm_sm100.cu needs CUTLASS_ENABLE_GDC_FOR_SM100 (programmatic dependent launch waits)"
+#endif
 #include <cutlass/cutlass.h>
 #include <cutlass/epilogue/collective/collective_builder.hpp>
 #include <cutlass/gemm/collective/collective_builder.hpp>
@@ -96,13 +99,16 @@ typename G::Arguments make_args(int M, int N, int K, const uint16_t* A, const ui
 template <class G>
 cudaError_t run(int M, int N, int K, const uint16_t* A, const uint16_t* W, const float* C, float* D,
                 float beta, void* workspace, size_t workspace_bytes, cudaStream_t st, int ldw,
-                int splits) {
+                int splits, bool pdl) {
   const typename G::Arguments args = make_args<G>(M, N, K, A, W, C, D, beta, ldw, splits);
   G g;
   if (g.can_implement(args) != cutlass::Status::kSuccess) return cudaErrorInvalidValue;
   if (G::get_workspace_size(args) > workspace_bytes) return cudaErrorInvalidValue;
   if (g.initialize(args, workspace, st) != cutlass::Status::kSuccess) return cudaErrorInvalidValue;
-  if (g.run(st) != cutlass::Status::kSuccess) return cudaErrorLaunchFailure;
+  // pdl: launched with a programmatic edge to the previous kernel; the
+  // kernel's loading warps wait for it (griddepcontrol.wait, compiled in by
+  // CUTLASS_ENABLE_GDC_FOR_SM100) before their first global read
+  if (g.run(st, nullptr, pdl) != cutlass::Status::kSuccess) return cudaErrorLaunchFailure;
   return counted(cudaGetLastError());
 }
 
@@ -143,14 +149,15 @@ int gemm_pick_splits(int M, int N, int K, int sms) {
 
 cudaError_t gemm_bf16_f32(int M, int N, int K, const uint16_t* A, const uint16_t* W,
                           const float* C, float* D, float beta, void* workspace,
-                          size_t workspace_bytes, cudaStream_t st, int ldw, int splits, int pair) {
+                          size_t workspace_bytes, cudaStream_t st, int ldw, int splits, int pair,
+                          bool pdl) {
   if (!gemm_supported(M, N, K) || (ldw && (ldw < K || ldw % 8))) return cudaErrorInvalidValue;
   if (splits < 1 || splits > kMaxSplits || K % splits || (K / splits) % 8 ||
       (splits > 1 && (C || beta != 0.0f)))
     return cudaErrorInvalidValue;
   if (pair)
-    return run<Gemm2>(M, N, K, A, W, C, D, beta, workspace, workspace_bytes, st, ldw, splits);
-  return run<Gemm>(M, N, K, A, W, C, D, beta, workspace, workspace_bytes, st, ldw, splits);
+    return run<Gemm2>(M, N, K, A, W, C, D, beta, workspace, workspace_bytes, st, ldw, splits, pdl);
+  return run<Gemm>(M, N, K, A, W, C, D, beta, workspace, workspace_bytes, st, ldw, splits, pdl);
 }
 
 }  // namespace myos

@@ -12,6 +12,7 @@
 #include <math.h>
 
 #include <algorithm>
+#include <cstdlib>
 
 #include <cooperative_groups.h>
 
@@ -24,6 +25,33 @@ namespace myos {
 namespace {
 
 namespace cg = cooperative_groups;
+
+// Programmatic dependent launch between the kernels of the GEMM path: each
+// kernel waits for the previous kernel of the stream to finish (and its
+// memory to be visible) before its first global access, then lets the next
+// one be scheduled, so launches overlap their predecessors' tails.
+bool g_pdl = true;  // MYOS_GEMM_PDL=0 at pf_init: plain stream order
+
+MYOS_DEV void pdl_begin() {
+  pdl_wait();
+  pdl_launch();
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch(void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                   Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = g_pdl ? 1 : 0;
+  return counted(cudaLaunchKernelEx(&cfg, k, static_cast<KArgs>(args)...));
+}
 
 constexpr int kT = 256;
 
@@ -89,6 +117,7 @@ MYOS_DEV float bsum(float v, float* red) { return block_sum(v, red); }
 
 // X[t] = embedding row of ids[t] (exact promotion).
 __global__ void k_pf_embed(float* X, const uint16_t* embed, const uint32_t* ids, int K) {
+  pdl_begin();  // the previous kernel of the stream has finished (PDL)
   const int t = blockIdx.x;
   const uint16_t* row = embed + (size_t)ids[t] * K;
   for (int j = threadIdx.x; j < K; j += blockDim.x) X[(size_t)t * K + j] = bf16_at(row + j);
@@ -98,6 +127,7 @@ __global__ void k_pf_embed(float* X, const uint16_t* embed, const uint32_t* ids,
 // inv = 1 / sqrtf(mean(x^2) + eps) (bf16.rs:231-270); gamma null: of x.
 __global__ void __launch_bounds__(kT) k_pf_norm_split(uint16_t* A, const float* X, const float* gamma,
                                                       int n, int K, float eps) {
+  pdl_begin();  // the previous kernel of the stream has finished (PDL)
   __shared__ float red[33];
   const int t = blockIdx.x;
   const float* x = X + (size_t)t * K;
@@ -125,6 +155,7 @@ __global__ void __launch_bounds__(128) k_pf_qkv_post(float* Q, const float* D, i
                                                      const float* cos_t, const float* sin_t, int p0,
                                                      int Hq, int Hkv, int d, int S,
                                                      const int* rowpos, size_t rowstride) {
+  pdl_begin();  // the previous kernel of the stream has finished (PDL)
   const int t = blockIdx.x, n = gridDim.x, half = d >> 1;
   const int h = blockIdx.y * (256 / d) + threadIdx.x / half, p = threadIdx.x % half;
   if (h >= Hq + 2 * Hkv) return;
@@ -227,6 +258,7 @@ __global__ void __launch_bounds__(kT, 2) k_pf_attn_split(float* o_part, float2* 
                                                          int n, int Hq, int Hkv, int S, float scale,
                                                          int ch, int ns, const int* rowpos,
                                                          size_t rowstride) {
+  pdl_begin();  // the previous kernel of the stream has finished (PDL)
   constexpr int ds = D + 4, V4 = D / 4;
   constexpr int DW = D / kAttnWarps;    // dims per warp (16 or 8)
   constexpr int CW = DW / 4;            // float4 chunks per warp
@@ -416,6 +448,7 @@ template <int D>
 __global__ void __launch_bounds__(128) k_pf_attn_merge(uint16_t* A, const float* o_part,
                                                        const float2* ml, int p0, int Hq, int ch,
                                                        int ns, const int* rowpos) {
+  pdl_begin();  // the previous kernel of the stream has finished (PDL)
   constexpr int E = D / 32;
   const int t = blockIdx.x, n = gridDim.x, lane = threadIdx.x & 31;
   const int h = blockIdx.y * 4 + (threadIdx.x >> 5);
@@ -454,6 +487,7 @@ constexpr int kResidParts = 4, kResidThreads = 128, kResidVec = 4;
 __global__ void __cluster_dims__(kResidParts, 1, 1) __launch_bounds__(kResidThreads)
     k_pf_resid_norm(float* X, const float* D, int sp, const float* gamma, uint16_t* A, int N,
                     float eps) {
+  pdl_begin();  // the previous kernel of the stream has finished (PDL)
   __shared__ float red[33];
   __shared__ float part_ss;
   const int r = blockIdx.x, t = blockIdx.y, n = gridDim.y;
@@ -503,6 +537,7 @@ __global__ void __cluster_dims__(kResidParts, 1, 1) __launch_bounds__(kResidThre
 // the residual (X non-null), the projection elsewhere; the ranks' parts are
 // then summed.
 __global__ void k_pf_resid_part(float* D, const float* X, int n, int N, int sp) {
+  pdl_begin();  // the previous kernel of the stream has finished (PDL)
   const int t = blockIdx.x;
   for (int j = threadIdx.x; j < N; j += blockDim.x) {
     const float dl = part_sum(D, n, t, N, j, sp);  // reads D[t][j] before it is replaced
@@ -514,6 +549,7 @@ __global__ void k_pf_resid_part(float* D, const float* X, int n, int N, int sp) 
 // projection, written as three bf16 terms for the down projection; four
 // adjacent columns per thread (I % 4 == 0), partials summed as part_sum does.
 __global__ void __launch_bounds__(kT) k_pf_swiglu_split(uint16_t* A, const float* D, int I, int sp) {
+  pdl_begin();  // the previous kernel of the stream has finished (PDL)
   const int t = blockIdx.x, n = gridDim.x, N = 2 * I;
   const int j = 4 * (blockIdx.y * blockDim.x + threadIdx.x);
   if (j >= I) return;
@@ -576,6 +612,7 @@ MYOS_DEV void amax_take(float& bv, uint32_t& bi, float v, uint32_t i) {
 
 __global__ void __launch_bounds__(kT) k_row_argmax_part(float2* part, const float* D, int B, int V,
                                                         int vec) {
+  pdl_begin();  // the previous kernel of the stream has finished (PDL)
   __shared__ float bvs[kT / 32];
   __shared__ uint32_t bis[kT / 32];
   const int b = blockIdx.x, c = blockIdx.y, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -641,6 +678,7 @@ __global__ void __launch_bounds__(kT) k_row_argmax_part(float2* part, const floa
 
 __global__ void k_row_argmax_fin(uint32_t* tok, uint32_t* out, int out_stride, int step,
                                  const int* d_step, const float2* part, int nc) {
+  pdl_begin();  // the previous kernel of the stream has finished (PDL)
   const int b = blockIdx.x, lane = threadIdx.x;
   if (d_step) {  // the step index lives on the device (graph replays)
     step = *d_step;
@@ -666,12 +704,14 @@ __global__ void k_row_argmax_fin(uint32_t* tok, uint32_t* out, int out_stride, i
 }
 
 __global__ void k_rows_copy(float* dst, const float* src, const int* src_row, int K) {
+  pdl_begin();  // the previous kernel of the stream has finished (PDL)
   const int b = blockIdx.x;
   for (int j = threadIdx.x; j < K; j += blockDim.x)
     dst[(size_t)b * K + j] = src[(size_t)src_row[b] * K + j];
 }
 
 __global__ void k_pos_advance(int* rowpos, int B, int* d_step) {
+  pdl_begin();  // the previous kernel of the stream has finished (PDL)
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b < B) rowpos[b] += 1;
   if (d_step && b == 0) *d_step += 1;
@@ -680,6 +720,7 @@ __global__ void k_pos_advance(int* rowpos, int B, int* d_step) {
 // Teacher-forced token of each row at the device-held step: tok[b] =
 // feed_t[step * B + b].
 __global__ void k_feed(uint32_t* tok, const uint32_t* feed_t, const int* d_step, int B) {
+  pdl_begin();  // the previous kernel of the stream has finished (PDL)
   const int b = blockIdx.x * blockDim.x + threadIdx.x;
   if (b < B) tok[b] = feed_t[(size_t)(*d_step) * B + b];
 }
@@ -691,39 +732,39 @@ int pf_argmax_chunks(int V) { return (V + kArgChunk - 1) / kArgChunk; }
 cudaError_t pf_row_argmax(uint32_t* tok, uint32_t* out, int out_stride, int step, const float* D,
                           float2* part, int B, int V, cudaStream_t st, const int* d_step) {
   const int nc = pf_argmax_chunks(V);
-  k_row_argmax_part<<<dim3(B, nc), kT, 0, st>>>(part, D, B, V, V % 4 == 0);
-  if (cudaError_t e = counted(cudaGetLastError())) return e;
-  k_row_argmax_fin<<<B, 32, 0, st>>>(tok, out, out_stride, step, d_step, part, nc);
-  return counted(cudaGetLastError());
+  if (cudaError_t e = launch(k_row_argmax_part, dim3(B, nc), kT, 0, st, part, D, B, V,
+                             (int)(V % 4 == 0)))
+    return e;
+  return launch(k_row_argmax_fin, B, 32, 0, st, tok, out, out_stride, step, d_step, part, nc);
 }
 
 cudaError_t pf_rows_copy(float* dst, const float* src, const int* src_row, int B, int K,
                          cudaStream_t st) {
-  k_rows_copy<<<B, kT, 0, st>>>(dst, src, src_row, K);
-  return counted(cudaGetLastError());
+  return launch(k_rows_copy, B, kT, 0, st,
+                dst, src, src_row, K);
 }
 
 cudaError_t pf_pos_advance(int* rowpos, int B, cudaStream_t st, int* d_step) {
-  k_pos_advance<<<(B + 127) / 128, 128, 0, st>>>(rowpos, B, d_step);
-  return counted(cudaGetLastError());
+  return launch(k_pos_advance, (B + 127) / 128, 128, 0, st,
+                rowpos, B, d_step);
 }
 
 cudaError_t pf_feed(uint32_t* tok, const uint32_t* feed_t, const int* d_step, int B,
                     cudaStream_t st) {
-  k_feed<<<(B + 127) / 128, 128, 0, st>>>(tok, feed_t, d_step, B);
-  return counted(cudaGetLastError());
+  return launch(k_feed, (B + 127) / 128, 128, 0, st,
+                tok, feed_t, d_step, B);
 }
 
 cudaError_t pf_embed(float* X, const uint16_t* embed, const uint32_t* ids, int n, int K,
                      cudaStream_t st) {
-  k_pf_embed<<<n, kT, 0, st>>>(X, embed, ids, K);
-  return counted(cudaGetLastError());
+  return launch(k_pf_embed, n, kT, 0, st,
+                X, embed, ids, K);
 }
 
 cudaError_t pf_norm_split(uint16_t* A, const float* X, const float* gamma, int n, int K, float eps,
                           cudaStream_t st) {
-  k_pf_norm_split<<<n, kT, 0, st>>>(A, X, gamma, n, K, eps);
-  return counted(cudaGetLastError());
+  return launch(k_pf_norm_split, n, kT, 0, st,
+                A, X, gamma, n, K, eps);
 }
 
 cudaError_t pf_qkv_post(float* Q, const float* D, int sp, const float* bias, void* kc, void* vc,
@@ -733,18 +774,20 @@ cudaError_t pf_qkv_post(float* Q, const float* D, int sp, const float* bias, voi
   if ((d != 64 && d != 128) || sp < 1 || sp > kMaxSplits) return cudaErrorInvalidValue;
   const dim3 grid(n, (Hq + 2 * Hkv + 256 / d - 1) / (256 / d));
   if (kv_bf16)
-    k_pf_qkv_post<__nv_bfloat16><<<grid, 128, 0, st>>>(Q, D, sp, bias, (__nv_bfloat16*)kc,
-                                                        (__nv_bfloat16*)vc, cos_t, sin_t, p0, Hq,
-                                                        Hkv, d, S, rowpos, rowstride);
-  else
-    k_pf_qkv_post<float><<<grid, 128, 0, st>>>(Q, D, sp, bias, (float*)kc, (float*)vc, cos_t,
-                                               sin_t, p0, Hq, Hkv, d, S, rowpos, rowstride);
-  return counted(cudaGetLastError());
+    return launch(k_pf_qkv_post<__nv_bfloat16>, grid, 128, 0, st, Q, D, sp, bias,
+                  (__nv_bfloat16*)kc, (__nv_bfloat16*)vc, cos_t, sin_t, p0, Hq, Hkv, d, S, rowpos,
+                  rowstride);
+  return launch(k_pf_qkv_post<float>, grid, 128, 0, st, Q, D, sp, bias, (float*)kc, (float*)vc,
+                cos_t, sin_t, p0, Hq, Hkv, d, S, rowpos, rowstride);
 }
 
 bool pf_attn_supported(int d, int G) { return (d == 64 || d == 128) && G <= 8; }
 
+bool pf_pdl() { return g_pdl; }
+
 cudaError_t pf_init() {
+  const char* pe = getenv("MYOS_GEMM_PDL");
+  g_pdl = !(pe && pe[0] == '0');
 #define MYOS_PF_SMEM(KT, D)                                                                \
   if (cudaError_t e = cudaFuncSetAttribute(k_pf_attn_split<KT, D>,                         \
                                            cudaFuncAttributeMaxDynamicSharedMemorySize,    \
@@ -776,28 +819,25 @@ cudaError_t pf_attn(uint16_t* A, float* o_part, float2* ml, const float* Q, cons
   const int ns = pf_attn_splits(max_keys, &ch);
   const long items = (long)n * Hkv * ns;
   const dim3 grid((unsigned)std::min<long>(items, 2L * sms));  // two resident blocks per SM
-#define MYOS_PF_ATTN(D)                                                                          \
-  if (d == D) {                                                                                  \
-    const size_t smem = attn_smem_bytes<D>();                                                    \
-    if (kv_bf16)                                                                                 \
-      k_pf_attn_split<__nv_bfloat16, D><<<grid, kT, smem, st>>>(                                 \
-          o_part, ml, Q, (const __nv_bfloat16*)kc, (const __nv_bfloat16*)vc, p0, n, Hq, Hkv, S,  \
-          scale, ch, ns, rowpos, rowstride);                                                     \
-    else                                                                                         \
-      k_pf_attn_split<float, D><<<grid, kT, smem, st>>>(o_part, ml, Q, (const float*)kc,         \
-                                                        (const float*)vc, p0, n, Hq, Hkv, S,     \
-                                                        scale, ch, ns, rowpos, rowstride);       \
+  cudaError_t e = cudaSuccess;
+#define MYOS_PF_ATTN(D)                                                                         \
+  if (d == D) {                                                                                 \
+    const size_t smem = attn_smem_bytes<D>();                                                   \
+    e = kv_bf16 ? launch(k_pf_attn_split<__nv_bfloat16, D>, grid, kT, smem, st, o_part, ml, Q,  \
+                         (const __nv_bfloat16*)kc, (const __nv_bfloat16*)vc, p0, n, Hq, Hkv, S, \
+                         scale, ch, ns, rowpos, rowstride)                                      \
+                : launch(k_pf_attn_split<float, D>, grid, kT, smem, st, o_part, ml, Q,          \
+                         (const float*)kc, (const float*)vc, p0, n, Hq, Hkv, S, scale, ch, ns,  \
+                         rowpos, rowstride);                                                    \
   }
   MYOS_PF_ATTN(64)
   MYOS_PF_ATTN(128)
 #undef MYOS_PF_ATTN
-  if (cudaError_t e = counted(cudaGetLastError())) return e;
+  if (e != cudaSuccess) return e;
   const dim3 mgrid(n, (Hq + 3) / 4);
   if (d == 64)
-    k_pf_attn_merge<64><<<mgrid, 128, 0, st>>>(A, o_part, ml, p0, Hq, ch, ns, rowpos);
-  else
-    k_pf_attn_merge<128><<<mgrid, 128, 0, st>>>(A, o_part, ml, p0, Hq, ch, ns, rowpos);
-  return counted(cudaGetLastError());
+    return launch(k_pf_attn_merge<64>, mgrid, 128, 0, st, A, o_part, ml, p0, Hq, ch, ns, rowpos);
+  return launch(k_pf_attn_merge<128>, mgrid, 128, 0, st, A, o_part, ml, p0, Hq, ch, ns, rowpos);
 }
 
 cudaError_t pf_resid_norm(float* X, const float* D, int sp, const float* gamma, uint16_t* A, int n,
@@ -805,20 +845,20 @@ cudaError_t pf_resid_norm(float* X, const float* D, int sp, const float* gamma, 
   if (N % (4 * kResidParts) || N > 4 * kResidVec * kResidThreads * kResidParts || sp < 1 ||
       sp > kMaxSplits)
     return cudaErrorInvalidValue;
-  k_pf_resid_norm<<<dim3(kResidParts, n), kResidThreads, 0, st>>>(X, D, sp, gamma, A, N, eps);
-  return counted(cudaGetLastError());
+  return launch(k_pf_resid_norm, dim3(kResidParts, n), kResidThreads, 0, st,
+                X, D, sp, gamma, A, N, eps);
 }
 
 cudaError_t pf_resid_part(float* D, const float* X, int n, int N, int sp, cudaStream_t st) {
-  k_pf_resid_part<<<n, kT, 0, st>>>(D, X, n, N, sp);
-  return counted(cudaGetLastError());
+  return launch(k_pf_resid_part, n, kT, 0, st,
+                D, X, n, N, sp);
 }
 
 cudaError_t pf_swiglu_split(uint16_t* A, const float* D, int n, int I, int sp, cudaStream_t st) {
   if (I % 4) return cudaErrorInvalidValue;
   const dim3 grid(n, (I / 4 + kT - 1) / kT);
-  k_pf_swiglu_split<<<grid, kT, 0, st>>>(A, D, I, sp);
-  return counted(cudaGetLastError());
+  return launch(k_pf_swiglu_split, grid, kT, 0, st,
+                A, D, I, sp);
 }
 
 }  // namespace myos

@@ -29,8 +29,12 @@ cudaError_t pf_qkv_post(float* Q, const float* D, int sp, const float* bias, voi
                         size_t rowstride = 0);
 bool pf_attn_supported(int d, int G);
 // Raises the shared-memory limit of the split attention (once per device,
-// with that device current, before the first pf_attn there).
+// with that device current, before the first pf_attn there) and reads
+// MYOS_GEMM_PDL (0: launch the GEMM path without programmatic dependent
+// launch).
 cudaError_t pf_init();
+// Whether the GEMM path's kernels (and its GEMMs) launch with PDL.
+bool pf_pdl();
 // Causal GQA per row, split over the keys, then merged into A as the o_proj
 // input's three terms. Splits of 64 keys (longer past kAttnMaxSplits); the
 // partials o_part (rows * Hq * splits * d floats) and ml (rows * Hq * splits)
