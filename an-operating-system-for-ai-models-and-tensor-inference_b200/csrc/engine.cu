@@ -1159,7 +1159,15 @@ static int create_impl(myos_ctx* c, const myos_shape* shape, const myos_opts* op
               c->qd % 64 == 0 && (c->qd + 2 * c->kvd) % 64 == 0;
     for (size_t l = 0; ok && l < L; ++l) ok = c->layers[l].wu == c->layers[l].wg + I * H;
     if (ok) {
-      const int nc = 128;
+      // prompt tokens per chunk (MYOS_PF_CHUNK: 64..512, a multiple of 64).
+      // 256: M = 768 rows fill the SM-pair tiles, and each chunk reads the
+      // weights once for twice the tokens of 128 (a 4096-id prompt 17.8k ->
+      // 19.9k tok/s, 64 x 512-id prompts 44.7k -> 55.8k)
+      int nc = 256;
+      if (const char* pc = getenv("MYOS_PF_CHUNK")) {
+        const int v = atoi(pc);
+        if (v >= 64 && v <= 512 && v % 64 == 0) nc = v;
+      }
       const size_t M = kSplitParts * (size_t)nc;
       const size_t kmax = std::max(H, std::max((size_t)c->qd, I));
       const size_t nmax = std::max(c->qd + 2 * c->kvd, std::max(H, 2 * I));
