@@ -115,7 +115,6 @@ struct myos_ctx {
   size_t pf_ws_bytes = 0;
   size_t pf_D_elems = 0;  // capacity of pf_D in floats
   bool pf_splitk = true;  // MYOS_SPLITK=0: one K slice per projection
-  bool pf_pair = true;    // MYOS_GEMM_PAIR=0: no 2-SM tiles
   // batched decode (myos_batch_generate): per-sequence KV slabs and buffers
   void *bt_k = nullptr, *bt_v = nullptr;
   size_t bt_kv_bytes = 0;
@@ -1160,9 +1159,8 @@ static int create_impl(myos_ctx* c, const myos_shape* shape, const myos_opts* op
     for (size_t l = 0; ok && l < L; ++l) ok = c->layers[l].wu == c->layers[l].wg + I * H;
     if (ok) {
       // prompt tokens per chunk (MYOS_PF_CHUNK: 64..512, a multiple of 64).
-      // 256: M = 768 rows fill the SM-pair tiles, and each chunk reads the
-      // weights once for twice the tokens of 128 (a 4096-id prompt 17.8k ->
-      // 19.9k tok/s, 64 x 512-id prompts 44.7k -> 55.8k)
+      // 256: each chunk reads the weights once for twice the tokens of 128
+      // (M = 768 rows: six full 128-row tiles)
       int nc = 256;
       if (const char* pc = getenv("MYOS_PF_CHUNK")) {
         const int v = atoi(pc);
@@ -1181,8 +1179,6 @@ static int create_impl(myos_ctx* c, const myos_shape* shape, const myos_opts* op
       c->pf_D_elems = M * nmax;
       const char* sk = getenv("MYOS_SPLITK");
       c->pf_splitk = !(sk && sk[0] == '0');
-      const char* gp = getenv("MYOS_GEMM_PAIR");
-      c->pf_pair = !(gp && gp[0] == '0');
       CK(cudaMalloc(&c->pf_Q, (size_t)nc * (c->qd + 2 * c->kvd) * 4));
       CK(cudaMalloc(&c->pf_ws, ws));
       c->pf_ws_bytes = ws;
@@ -1709,17 +1705,16 @@ static int pf_splits(const myos_ctx* c, int M, int N, int K) {
   return sp;
 }
 
-// One projection of the GEMM path: D = pf_A x W^T on SM pairs (wide N) or on
-// single SMs with K slices (sp null: never sliced, D holds one [M, N]
+// One projection of the GEMM path: D = pf_A x W^T with K slices when its
+// tiles would leave SMs idle (sp null: never sliced, D holds one [M, N]
 // block); *sp receives the slices now in D.
 static cudaError_t pf_gemm(const myos_ctx* c, int M, int N, int K, const uint16_t* W, float* D,
                            cudaStream_t st, int ldw, int* sp) {
-  const int pair = c->pf_pair && gemm_pick_pair(M, N, c->num_sms);
   int one = 1;
   if (!sp) sp = &one;
-  else *sp = pair ? 1 : pf_splits(c, M, N, K);
+  else *sp = pf_splits(c, M, N, K);
   return gemm_bf16_f32(M, N, K, c->pf_A, W, nullptr, D, 0.0f, c->pf_ws, c->pf_ws_bytes, st, ldw,
-                       *sp, pair, pf_pdl());
+                       *sp, pf_pdl());
 }
 
 // One chunk of n prompt tokens at positions p0.. through every layer

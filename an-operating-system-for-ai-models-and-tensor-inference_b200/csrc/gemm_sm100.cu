@@ -23,7 +23,6 @@
 #include <cutlass/util/packed_stride.hpp>
 #include <cute/tensor.hpp>
 
-#include <algorithm>
 
 #include "gemm_sm100.h"
 #include "kernels.h"
@@ -38,34 +37,25 @@ using ElementB = cutlass::bfloat16_t;
 using LayoutA = cutlass::layout::RowMajor;     // activations: K contiguous
 using LayoutB = cutlass::layout::ColumnMajor;  // W[N,K] row-major is K x N column-major
 using LayoutC = cutlass::layout::RowMajor;
-// Two instantiations: one SM per 128 x 128 output tile (MMA M = 128), and a
-// pair of SMs per 256 x 256 tile (tcgen05 cta_group::2 on a 2 x 1 cluster:
-// each SM stages half of A's rows and half of W's rows, the pair's MMA reads
-// both; no multicast at this cluster shape). The pair reads each weight tile
-// once for up to 256 activation rows, so it is the choice when M > 128 and N
-// is wide enough to occupy the SMs without K slices.
-template <class MmaTile, class ClusterShape, class KSched, class ESched>
-struct Cfg {
-  using Epilogue = typename cutlass::epilogue::collective::CollectiveBuilder<
-      cutlass::arch::Sm100, cutlass::arch::OpClassTensorOp, MmaTile, ClusterShape,
-      cutlass::epilogue::collective::EpilogueTileAuto, float, float, float, LayoutC, 4, float,
-      LayoutC, 4, ESched>::CollectiveOp;
-  using Mainloop = typename cutlass::gemm::collective::CollectiveBuilder<
-      cutlass::arch::Sm100, cutlass::arch::OpClassTensorOp, ElementA, LayoutA, 8, ElementB,
-      LayoutB, 8, float, MmaTile, ClusterShape,
-      cutlass::gemm::collective::StageCountAutoCarveout<static_cast<int>(
-          sizeof(typename Epilogue::SharedStorage))>,
-      KSched>::CollectiveOp;
-  using Kernel =
-      cutlass::gemm::kernel::GemmUniversal<Shape<int, int, int, int>, Mainloop, Epilogue>;
-  using Gemm = cutlass::gemm::device::GemmUniversalAdapter<Kernel>;
-};
-using Gemm = Cfg<Shape<_128, _128, _64>, Shape<_1, _1, _1>,
-                 cutlass::gemm::collective::KernelScheduleAuto,
-                 cutlass::epilogue::collective::EpilogueScheduleAuto>::Gemm;
-using Gemm2 = Cfg<Shape<_256, _256, _64>, Shape<_2, _1, _1>,
-                  cutlass::gemm::KernelTmaWarpSpecialized2SmSm100,
-                  cutlass::epilogue::TmaWarpSpecialized2Sm>::Gemm;
+// One SM per 128 x 128 output tile, no clusters. (Measured against it and
+// dropped: 128 x 256 tiles for the wide projections, slower.)
+using MmaTile = Shape<_128, _128, _64>;
+using ClusterShape = Shape<_1, _1, _1>;
+
+using Epilogue = typename cutlass::epilogue::collective::CollectiveBuilder<
+    cutlass::arch::Sm100, cutlass::arch::OpClassTensorOp, MmaTile, ClusterShape,
+    cutlass::epilogue::collective::EpilogueTileAuto, float, float, float, LayoutC, 4, float,
+    LayoutC, 4, cutlass::epilogue::collective::EpilogueScheduleAuto>::CollectiveOp;
+
+using Mainloop = typename cutlass::gemm::collective::CollectiveBuilder<
+    cutlass::arch::Sm100, cutlass::arch::OpClassTensorOp, ElementA, LayoutA, 8, ElementB, LayoutB,
+    8, float, MmaTile, ClusterShape,
+    cutlass::gemm::collective::StageCountAutoCarveout<static_cast<int>(
+        sizeof(typename Epilogue::SharedStorage))>,
+    cutlass::gemm::collective::KernelScheduleAuto>::CollectiveOp;
+
+using Kernel = cutlass::gemm::kernel::GemmUniversal<Shape<int, int, int, int>, Mainloop, Epilogue>;
+using Gemm = cutlass::gemm::device::GemmUniversalAdapter<Kernel>;
 
 template <class G>
 typename G::Arguments make_args(int M, int N, int K, const uint16_t* A, const uint16_t* W,
@@ -120,16 +110,8 @@ bool gemm_supported(int M, int N, int K) {
 }
 
 size_t gemm_workspace_bytes(int M, int N, int K) {
-  return std::max(
-      Gemm::get_workspace_size(make_args<Gemm>(M, N, K, nullptr, nullptr, nullptr, nullptr, 0.0f)),
-      Gemm2::get_workspace_size(make_args<Gemm2>(M, N, K, nullptr, nullptr, nullptr, nullptr, 0.0f)));
-}
-
-int gemm_pick_pair(int M, int N, int sms) {
-  // 256 x 256 pair tiles when the rows need more than one 128-row tile and
-  // the pairs cover at least two thirds of the SMs without K slices
-  const long pairs = (long)((M + 255) / 256) * ((N + 255) / 256);
-  return M > 128 && 2 * pairs * 3 >= 2L * sms;
+  return Gemm::get_workspace_size(
+      make_args<Gemm>(M, N, K, nullptr, nullptr, nullptr, nullptr, 0.0f));
 }
 
 int gemm_pick_splits(int M, int N, int K, int sms) {
@@ -149,14 +131,11 @@ int gemm_pick_splits(int M, int N, int K, int sms) {
 
 cudaError_t gemm_bf16_f32(int M, int N, int K, const uint16_t* A, const uint16_t* W,
                           const float* C, float* D, float beta, void* workspace,
-                          size_t workspace_bytes, cudaStream_t st, int ldw, int splits, int pair,
-                          bool pdl) {
+                          size_t workspace_bytes, cudaStream_t st, int ldw, int splits, bool pdl) {
   if (!gemm_supported(M, N, K) || (ldw && (ldw < K || ldw % 8))) return cudaErrorInvalidValue;
   if (splits < 1 || splits > kMaxSplits || K % splits || (K / splits) % 8 ||
       (splits > 1 && (C || beta != 0.0f)))
     return cudaErrorInvalidValue;
-  if (pair)
-    return run<Gemm2>(M, N, K, A, W, C, D, beta, workspace, workspace_bytes, st, ldw, splits, pdl);
   return run<Gemm>(M, N, K, A, W, C, D, beta, workspace, workspace_bytes, st, ldw, splits, pdl);
 }
 

@@ -20,14 +20,11 @@ size_t gemm_workspace_bytes(int M, int N, int K);
 // Slices that let an [M, N] output's 128 x 128 tiles fill `sms` SMs once
 // (1 when the tiles already cover half of them or K is not 64-aligned).
 int gemm_pick_splits(int M, int N, int K, int sms);
-// 1: run the projection on SM pairs with 256 x 256 tiles (M > 128 and wide N),
-// 0: one SM per 128 x 128 tile.
-int gemm_pick_pair(int M, int N, int sms);
 // pdl: launch with a programmatic edge to the previous kernel in the stream
 // (the GEMM reads nothing before that kernel has finished).
 cudaError_t gemm_bf16_f32(int M, int N, int K, const uint16_t* A, const uint16_t* W,
                           const float* C, float* D, float beta, void* workspace,
                           size_t workspace_bytes, cudaStream_t st, int ldw = 0, int splits = 1,
-                          int pair = 0, bool pdl = false);
+                          bool pdl = false);
 
 }  // namespace myos
