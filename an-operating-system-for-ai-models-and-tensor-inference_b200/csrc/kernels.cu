@@ -1374,23 +1374,26 @@ MYOS_DEV void merge_head(const Src& src, int ne, int d, int lane, float* out) {
     M = fmaxf(M, warp_max(q0 + lane < ne ? src.m(q0 + lane) : -INFINITY));
   float Lp = 0.0f;
   float4 O[2] = {make_float4(0.f, 0.f, 0.f, 0.f), make_float4(0.f, 0.f, 0.f, 0.f)};
+  // kMergeBatch splits' outputs in flight per round of loads (the merge
+  // of many splits is a chain of L2 round trips)
+  constexpr int kMergeBatch = 16;
   for (int q0 = 0; q0 < ne; q0 += 32) {
     const int q = q0 + lane;
     const float mq = q < ne ? src.m(q) : -INFINITY;
     const float f = mq == -INFINITY ? 0.0f : expf(mq - M);
     if (q < ne) Lp = fmaf(src.l(q), f, Lp);
     const int nr = min(32, ne - q0);
-    for (int u0 = 0; u0 < nr; u0 += 8) {
-      float4 po[2][8];
+    for (int u0 = 0; u0 < nr; u0 += kMergeBatch) {
+      float4 po[2][kMergeBatch];
 #pragma unroll
-      for (int u = 0; u < 8; ++u)
+      for (int u = 0; u < kMergeBatch; ++u)
 #pragma unroll
         for (int j = 0; j < 2; ++j) {
           const int e = 4 * lane + 128 * j;
           po[j][u] = (u0 + u < nr && e < d) ? src.o(q0 + u0 + u, e) : make_float4(0.f, 0.f, 0.f, 0.f);
         }
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
+      for (int u = 0; u < kMergeBatch; ++u) {
         const float fu = __shfl_sync(0xffffffffu, f, (u0 + u) & 31);
         if (u0 + u < nr)
 #pragma unroll
