@@ -1536,7 +1536,9 @@ __global__ void __launch_bounds__(kThreads, 1) k_attn_dec(AttnArgs a) {
     const int nk = min(kTile, ke - t0);
     if (t0 != kb) {  // later tiles
       __syncthreads();
-      dec_tile_issue<KT>(kc, vc, d, t0, nk, pos, ks, vs, raw, threadIdx.x, blockDim.x);
+      // f32 rows are copied straight into ks/vs now; bf16 rows were copied
+      // into `raw` while the previous tile was computed
+      if (sizeof(KT) == 4) dec_tile_issue<KT>(kc, vc, d, t0, nk, pos, ks, vs, raw, threadIdx.x, blockDim.x);
       dec_tile_finish<KT>(d, t0, nk, pos, ks, vs, raw, threadIdx.x, blockDim.x);
       if (has_new && pos >= t0 && pos < t0 + nk)
         for (int e = threadIdx.x; e < d; e += blockDim.x) {
@@ -1545,6 +1547,11 @@ __global__ void __launch_bounds__(kThreads, 1) k_attn_dec(AttnArgs a) {
         }
       __syncthreads();
     }
+    // bf16: the next tile's rows into `raw` (widened by every thread after
+    // this tile, so `raw` is free), in flight during this tile's math
+    if (sizeof(KT) == 2 && t0 + kTile < ke)
+      dec_tile_issue<KT>(kc, vc, d, t0 + kTile, min(kTile, ke - t0 - kTile), pos, ks, vs, raw,
+                         threadIdx.x, blockDim.x);
     {  // partial scores of key `lane` over this warp's dims, heads < G
       float sc[8];
 #pragma unroll
