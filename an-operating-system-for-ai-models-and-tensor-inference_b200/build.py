@@ -37,9 +37,9 @@ def cutlass_include() -> list:
             return ["-I" + os.path.join(root, "include"),
                     "-I" + os.path.join(root, "tools", "util", "include")]
     raise RuntimeError("CUTLASS headers (sm100 collectives) not found")
-CUDA_SOURCES = ["kernels.cu", "stream_step.cu", "engine.cu", "ops.cu", "noalloc.cu",
+CUDA_SOURCES = ["kernels.cu", "engine.cu", "ops.cu", "noalloc.cu",
                 "prefill.cu", "gemm_sm100.cu", "safetensors.cpp", "tp.cpp"]
-HEADERS = ["common.cuh", "kernels.h", "safetensors.h", "stream_step.h", "prefill.h",
+HEADERS = ["common.cuh", "kernels.h", "safetensors.h", "prefill.h",
            "gemm_sm100.h", "tp.h"]
 
 

@@ -32,7 +32,6 @@
 #include "kernels.h"
 #include "prefill.h"
 #include "safetensors.h"
-#include "stream_step.h"
 #include "tp.h"
 
 using namespace myos;
@@ -96,8 +95,6 @@ struct myos_ctx {
   int warps_qkv = 0, warps_o = 0, warps_gu = 0, warps_down = 0, warps_head = 0;
   int attn_chunk = 0, attn_nsplit = 0;
   int defer_merge = 0;  // o_proj staging merges the attention splits
-  int l2pf_mode = 0;    // MYOS_L2PF: qkv kernels prefetch the layer's MLP weights into L2
-  int l2pf_mask = 7;    // MYOS_L2PF_MASK: which of them (1 gate, 2 up, 4 down)
   int attn_cluster = 0; // attention splits merge across a thread-block cluster
   // fused MLP (k_mlp: gate|up, SwiGLU and down_proj in one launch per layer)
   // when the shape allows and MYOS_MLP is not 0; grid 0 keeps the two GEMVs
@@ -140,18 +137,6 @@ struct myos_ctx {
   float prefill_ms = 0.f, decode_ms = 0.f;
   int steps_per_graph = 16;
   bool profiling = false;
-  // persistent streaming step kernel (all decode steps of a call in one
-  // launch), when the shape allows; MYOS_STEP=kernels keeps one launch per kernel
-  bool stream = false;
-  StreamArgs sargs = {};
-  StreamLayer* d_slayers = nullptr;
-  unsigned* sflags = nullptr;  // [grid] per-CTA phase counts (epoch base)
-  uint64_t* s_words = nullptr; // phase hand-over words (value, epoch)
-  size_t s_words_bytes = 0;
-  uint64_t s_phases = 0;       // phases run since the words were last zeroed
-  uint64_t* trace = nullptr;   // MYOS_TRACE_FILE: per-phase timer stamps of the step kernel
-  uint64_t* strace = nullptr;  // MYOS_SLOT_TRACE: per-slot stamps (diagnostics)
-  std::string trace_file;
   uint64_t* ktrace = nullptr;  // MYOS_KTRACE_FILE: launch timeline of the per-kernel step
   std::string ktrace_file;
   std::vector<uint64_t> ktrace_init;
@@ -461,16 +446,6 @@ int launch_kind(myos_ctx* c, int kind, int l, const uint32_t* feed, bool pdl, bo
     q.prefetch_cap = prefetch_cap(c, c->grid_qkv);
     q.tr = ktrace_at(c, 5 * l + K_QKV);
     q.warps = c->warps_qkv;
-    if (c->l2pf_mode) {  // this layer's MLP weights, for gate/up and down
-      const size_t mat = (size_t)I * H * 2;
-      const uint16_t* m[3] = {w.wg, w.wu, w.wd};
-      for (int r = 0; r < 3; ++r)
-        if (c->l2pf_mask >> r & 1) {
-          q.pf_ptr[r] = m[r];
-          q.pf_bytes[r] = mat;
-        }
-      q.pf_mode = c->l2pf_mode;
-    }
     CK(launch_gemv(EPI_BIAS, q, c->grid_qkv, c->st, pdl));
   } else if (kind == K_ATTN) {
     AttnArgs at = {};
@@ -526,7 +501,7 @@ int launch_kind(myos_ctx* c, int kind, int l, const uint32_t* feed, bool pdl, bo
       o.pf_bytes[0] = (size_t)c->mlp_pf_rows * H * 2;
       o.pf_stride = (size_t)kMlpSlice * H * 2;
       o.pf_n = c->grid_mlp;
-      o.pf_mode = 3;
+      o.pf_mode = 1;
     }
     tp_partial(c, &o, K_O);
     CK(launch_gemv(EPI_RESID, o, c->grid_o, c->st, pdl));
@@ -616,31 +591,9 @@ double kind_bytes(const myos_ctx* c, int kind) {
   return 0;
 }
 
-// Token steps per launch of the streaming step kernel.
-constexpr size_t kStreamMaxSteps = 1024;
-
 int run_steps(myos_ctx* c, int kind, size_t nsteps) {
   const bool head = kind != G_FEED_NOHEAD;
   const uint32_t* feed = kind == G_ARGMAX_HEAD ? nullptr : c->feed;
-  if (c->stream) {  // one cooperative launch runs the steps back to back
-    StreamArgs a = c->sargs;
-    a.head = head ? 1 : 0;
-    a.feed = feed;
-    const uint64_t per_step = 5 * (uint64_t)c->s.num_layers + (head ? 1 : 0);
-    for (size_t done = 0; done < nsteps;) {
-      a.nsteps = (int)std::min(nsteps - done, kStreamMaxSteps);
-      // epochs are 32-bit phase counts: restart them long before they wrap
-      if (c->s_phases + per_step * a.nsteps >= (1ull << 31)) {
-        CK(cudaMemsetAsync(c->sflags, 0, (size_t)c->sargs.grid * sizeof(unsigned), c->st));
-        CK(cudaMemsetAsync(c->s_words, 0, c->s_words_bytes, c->st));
-        c->s_phases = 0;
-      }
-      CK(launch_step_stream(a, c->st));
-      c->s_phases += per_step * a.nsteps;
-      done += (size_t)a.nsteps;
-    }
-    return MYOS_OK;
-  }
   if (!c->o.use_graphs) {
     for (size_t i = 0; i < nsteps; ++i) {
       int st = enqueue_step(c, head, feed, i > 0);
@@ -713,39 +666,13 @@ int finish(myos_ctx* c) {
       }
     }
   }
-  if (c->trace) {  // last step's stamps, for offline analysis
-    const size_t nt = (size_t)c->sargs.grid * (5 * c->s.num_layers + 1) * 8;
-    std::vector<uint64_t> h(nt);
-    if (cudaMemcpy(h.data(), c->trace, nt * 8, cudaMemcpyDeviceToHost) == cudaSuccess) {
-      if (FILE* f = fopen(c->trace_file.c_str(), "wb")) {
-        fwrite(h.data(), 8, nt, f);
-        fclose(f);
-      }
-    }
-    if (c->strace) {
-      std::vector<uint64_t> hs((size_t)c->sargs.grid * 640 * 4);
-      if (cudaMemcpy(hs.data(), c->strace, hs.size() * 8, cudaMemcpyDeviceToHost) == cudaSuccess)
-        if (FILE* f = fopen((c->trace_file + ".slots").c_str(), "wb")) {
-          fwrite(hs.data(), 8, hs.size(), f);
-          fclose(f);
-        }
-    }
-  }
   if (c->ctl_host->err) {
     const uint32_t bits = c->ctl_host->err;
     c->ctl_host->err = 0;
     cudaMemcpy(&c->ctl->err, &c->ctl_host->err, 4, cudaMemcpyHostToDevice);
-    // an abandoned streaming launch leaves its phase counts and words
-    // partway: start the next launch from zero (no stale word can then
-    // carry an epoch a later phase expects)
     // an arrival count left partway would misplace the next MLP launch's target
     if (c->mlp_arrive) cudaMemset(c->mlp_arrive, 0, sizeof(unsigned long long));
     cudaMemset(c->counters, 0, (1 + c->s.num_kv_heads) * 4);
-    if (c->sflags) {
-      cudaMemset(c->sflags, 0, (size_t)c->sargs.grid * sizeof(unsigned));
-      cudaMemset(c->s_words, 0, c->s_words_bytes);
-      c->s_phases = 0;
-    }
     return fail(c, MYOS_ERR_TIMEOUT,
                 "a bounded device wait gave up (bits " + std::to_string(bits) + ")");
   }
@@ -1007,9 +934,6 @@ static int create_impl(myos_ctx* c, const myos_shape* shape, const myos_opts* op
     // then reads all partials; measured slower for the 1.5B step).
     const char* e = getenv("MYOS_DEFER_MERGE");
     const bool want = e && e[0] == '1';
-    const char* pf = getenv("MYOS_L2PF");
-    c->l2pf_mode = pf ? atoi(pf) : 0;
-    if (const char* pm = getenv("MYOS_L2PF_MASK")) c->l2pf_mask = atoi(pm);
     c->defer_merge = want && c->qd_pad == c->qd && s.num_q_heads <= 256 &&
                      merge_smem_bytes((int)s.num_q_heads, (int)nsplit, (int)d) <= (96u << 10);
     // MYOS_ATTN_CLUSTER=0 keeps the global-memory last-block merge
@@ -1057,98 +981,6 @@ static int create_impl(myos_ctx* c, const myos_shape* shape, const myos_opts* op
   CK(cudaMalloc(&c->sin_t, sn.size() * 4));
   CK(cudaMemcpy(c->cos_t, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
   CK(cudaMemcpy(c->sin_t, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice));
-  // persistent streaming step kernel (MYOS_STEP=stream; the per-kernel step
-  // stays the default until the streaming one outruns it)
-  {
-    const char* e = getenv("MYOS_STEP");
-    const bool want = e && e[0] == 's';
-    if (want && c->tp_size == 1) {
-      StreamArgs a = {};
-      a.L = (int)L;
-      a.H = (int)H;
-      a.I = (int)I;
-      a.V = (int)V;
-      a.qd = (int)c->qd;
-      a.kvd = (int)c->kvd;
-      a.Hq = (int)s.num_q_heads;
-      a.Hkv = (int)s.num_kv_heads;
-      a.d = (int)d;
-      a.G = (int)c->G;
-      a.eps = s.rms_eps;
-      a.scale = 1.0f / sqrtf((float)d);
-      a.grid = c->num_sms;
-      a.S = (int)S;
-      a.kv_bf16 = opts->kv_dtype == MYOS_KV_BF16;
-      // split-KV tasks of one 32-key tile (its keys prefetched while q, k
-      // and v are awaited), at most one per CTA
-      size_t ns = (S + 31) / 32;
-      const size_t cap = (size_t)c->num_sms / s.num_kv_heads;
-      if (ns > cap) ns = cap;
-      if (ns < 1) ns = 1;
-      a.nsplit = (int)ns;
-      a.chunk = (int)((S + ns - 1) / ns);
-      int max_smem = 0;
-      CK(cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, c->device));
-      if (c->qd_pad == c->qd && stream_configure(&a, max_smem) == cudaSuccess) {
-        std::vector<StreamLayer> hl(L);
-        for (size_t l = 0; l < L; ++l) {
-          const LayerW& w = c->layers[l];
-          hl[l] = StreamLayer{w.wqkv, w.wo, w.wg, w.wu, w.wd, w.bqkv, w.ln1, w.ln2};
-        }
-        CK(cudaMalloc(&c->d_slayers, L * sizeof(StreamLayer)));
-        CK(cudaMemcpy(c->d_slayers, hl.data(), L * sizeof(StreamLayer), cudaMemcpyHostToDevice));
-        // [grid] per-CTA phase counts, then the hand-over words
-        CK(cudaMalloc(&c->sflags, (size_t)a.grid * sizeof(unsigned)));
-        CK(cudaMemset(c->sflags, 0, (size_t)a.grid * sizeof(unsigned)));
-        c->s_words_bytes = stream_word_count(a) * sizeof(uint64_t);
-        CK(cudaMalloc(&c->s_words, c->s_words_bytes));
-        CK(cudaMemset(c->s_words, 0, c->s_words_bytes));
-        stream_set_words(&a, c->s_words);
-        a.embed = c->embed;
-        a.head_w = s.tied_head ? c->embed : c->lm_head;
-        a.final_norm = c->final_norm;
-        a.layers = c->d_slayers;
-        a.ctl = c->ctl;
-        a.rec_fed = c->rec_fed;
-        a.rec_argmax = c->rec_argmax;
-        a.resid = c->resid;
-        a.qkv = c->qkv;
-        a.attn = c->attn;
-        a.act = c->act;
-        a.logits = c->logits;
-        a.kcache = c->kcache;
-        a.vcache = c->vcache;
-        a.kv_layer_elems = c->kv_layer_elems;
-        a.cos_t = c->cos_t;
-        a.sin_t = c->sin_t;
-        a.flags = c->sflags;
-        a.wait_ns = 1000000000ull;
-        // ring copies outstanding at once, and slots requested into L2 ahead
-        const char* fe = getenv("MYOS_STREAM_INFLIGHT");
-        a.inflight = fe ? std::max(1, std::min(atoi(fe), 4)) : 1;
-        const char* le = getenv("MYOS_STREAM_L2LA");
-        a.l2_la = le ? std::max(0, std::min(atoi(le), 64)) : 0;
-        if (const char* sf = getenv("MYOS_SLOT_TRACE")) {  // slot stamps of one launch step
-          uint64_t* st = nullptr;
-          const size_t nt = (size_t)a.grid * 640 * 4;
-          CK(cudaMalloc(&st, nt * 8));
-          CK(cudaMemset(st, 0, nt * 8));
-          a.strace = st;
-          a.strace_seq0 = (uint32_t)atoi(sf);
-          c->strace = st;
-        }
-        if (const char* tf = getenv("MYOS_TRACE_FILE")) {
-          c->trace_file = tf;
-          const size_t nt = (size_t)a.grid * (5 * L + 1) * 8;
-          CK(cudaMalloc(&c->trace, nt * 8));
-          CK(cudaMemset(c->trace, 0, nt * 8));
-          a.trace = c->trace;
-        }
-        c->sargs = a;
-        c->stream = true;
-      }
-    }
-  }
   {
     // GEMM prefill: hidden, q and MLP widths 16-byte aligned for TMA, gate and
     // up rows adjacent (one [2I, H] projection), a supported head dim.
@@ -1332,8 +1164,7 @@ void myos_ctx_destroy(myos_ctx* c) {
   tp_comm_destroy(c->comm);
   void* dev[] = {c->warena, c->kcache, c->vcache, c->resid, c->qkv, c->attn, c->act, c->logits,
                  c->part_val, c->part_idx, c->part_o, c->part_m, c->part_l, c->counters, c->ctl,
-                 c->feed, c->rec_fed, c->rec_argmax, c->cos_t, c->sin_t, c->d_slayers, c->sflags,
-                 c->s_words, (void*)c->trace, (void*)c->strace, c->mlp_part, c->mlp_arrive, c->mlp_wd,
+                 c->feed, c->rec_fed, c->rec_argmax, c->cos_t, c->sin_t, c->mlp_part, c->mlp_arrive, c->mlp_wd,
                  (void*)c->ktrace, c->pf_X, c->pf_D, c->pf_Q, c->pf_A, c->pf_ws,
                  c->bt_k, c->bt_v, c->bt_X, c->bt_D, c->bt_pos, c->bt_rows, c->bt_tok,
                  c->bt_out, c->bt_ids, c->bt_feed, c->tp_part, c->tp_cand, c->tp_link,

@@ -567,28 +567,12 @@ __global__ void __launch_bounds__(kThreads) k_gemv(GemvArgs a) {
 // is in flight while batch b is consumed, across row boundaries. Batch 0 is
 // issued before the programmatic-dependency wait, so its DRAM latency
 // overlaps the predecessor kernel and the input staging.
-// This block's slice of each range in a.pf_ptr, requested into L2.
+// This block's share of the strided ranges in a.pf_ptr, requested into L2.
 MYOS_DEV void l2_prefetch_slices(const GemvArgs& a) {
-  if (a.pf_mode == 3) {
-    const int nr = 2 * a.pf_n;
-    for (int r = blockIdx.x + gridDim.x * threadIdx.x; r < nr; r += gridDim.x * blockDim.x)
-      prefetch_range_1(static_cast<const char*>(a.pf_ptr[r / a.pf_n]) + (size_t)(r % a.pf_n) * a.pf_stride,
-                       a.pf_bytes[0]);
-    return;
-  }
-  for (int r = 0; r < 3; ++r) {
-    if (!a.pf_ptr[r]) continue;
-    const size_t n = a.pf_bytes[r];
-    const size_t b0 = (n * blockIdx.x / gridDim.x) & ~(size_t)127;
-    const size_t b1 = blockIdx.x + 1 == gridDim.x ? n : (n * (blockIdx.x + 1) / gridDim.x) & ~(size_t)127;
-    const char* base = static_cast<const char*>(a.pf_ptr[r]);
-    if (a.pf_mode == 1) {
-      for (size_t o = b0 + (size_t)threadIdx.x * 128; o < b1; o += (size_t)blockDim.x * 128)
-        asm volatile("prefetch.global.L2 [%0];" ::"l"(base + o));
-    } else {
-      prefetch_range(base + b0, b1 - b0);
-    }
-  }
+  const int nr = 2 * a.pf_n;
+  for (int r = blockIdx.x + gridDim.x * threadIdx.x; r < nr; r += gridDim.x * blockDim.x)
+    prefetch_range_1(static_cast<const char*>(a.pf_ptr[r / a.pf_n]) + (size_t)(r % a.pf_n) * a.pf_stride,
+                     a.pf_bytes[0]);
 }
 
 template <int NR, int U>

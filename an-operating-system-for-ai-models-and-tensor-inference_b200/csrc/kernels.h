@@ -89,13 +89,12 @@ struct GemvArgs {
   uint32_t* rec_argmax;
   uint32_t* err;       // bounded-wait failure bits (nullable)
   KTrace tr;
-  // Weights of later kernels to pull into L2 while this one waits on its
-  // inputs (each block takes an equal slice of each range); pf_mode 1: one
-  // prefetch per 128-byte line from every thread, 2: bulk prefetches;
-  // 3: strided ranges, pf_ptr[m] + i * pf_stride of pf_bytes[0] bytes for
-  // m < 2 and i < pf_n, one bulk prefetch sequence per range.
-  const void* pf_ptr[3];
-  size_t pf_bytes[3];
+  // Weights of a later kernel to pull into L2 while this one waits on its
+  // inputs (pf_mode 1): the ranges pf_ptr[m] + i * pf_stride of pf_bytes[0]
+  // bytes for m < 2 and i < pf_n, one bulk prefetch sequence per range,
+  // spread over the blocks.
+  const void* pf_ptr[2];
+  size_t pf_bytes[1];
   int pf_mode;
   size_t pf_stride;
   int pf_n;

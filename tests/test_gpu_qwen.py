@@ -45,12 +45,9 @@ def golden(model, orc):
     return dict(prefill_logits=prefill_logits, ids=ids, gap=gap, final=md.logits())
 
 
-@pytest.mark.parametrize("step", ["kernels", "stream"])
 @pytest.mark.parametrize("kv", ["f32", "bf16"])
-def test_s1_greedy_ids_and_logits(model, golden, kv, step, monkeypatch):
+def test_s1_greedy_ids_and_logits(model, golden, kv):
     shape, table, prompt = model
-    # one launch per kernel, or the persistent streaming step (one launch per call)
-    monkeypatch.setenv("MYOS_STEP", step)
     e = myos.Engine(shape, N_PROMPT + N_GEN, kv_dtype=kv)
     e.load_table(table)
     atol, rtol = TOL[kv]
