@@ -1585,19 +1585,21 @@ __global__ void __launch_bounds__(kThreads, 1) k_attn_dec(AttnArgs a) {
       const float c0 = cfs[2 * hp], c1 = cfs[2 * hp + 1];
       acc[0].x *= c0; acc[0].y *= c0; acc[0].z *= c0; acc[0].w *= c0;
       acc[1].x *= c1; acc[1].y *= c1; acc[1].z *= c1; acc[1].w *= c1;
+      float2 a0 = make_float2(acc[0].x, acc[0].y), a1 = make_float2(acc[0].z, acc[0].w);
+      float2 b0 = make_float2(acc[1].x, acc[1].y), b1 = make_float2(acc[1].z, acc[1].w);
 #pragma unroll 4
-      for (int t = kg; t < nk; t += KG) {
+      for (int t = kg; t < nk; t += KG) {  // packed f32x2 FMAs, per element as fmaf
         const float4 v = *reinterpret_cast<const float4*>(vs + t * ds + dv);
         const float2 pp = *reinterpret_cast<const float2*>(pr + t * 8 + 2 * hp);
-        acc[0].x = fmaf(pp.x, v.x, acc[0].x);
-        acc[0].y = fmaf(pp.x, v.y, acc[0].y);
-        acc[0].z = fmaf(pp.x, v.z, acc[0].z);
-        acc[0].w = fmaf(pp.x, v.w, acc[0].w);
-        acc[1].x = fmaf(pp.y, v.x, acc[1].x);
-        acc[1].y = fmaf(pp.y, v.y, acc[1].y);
-        acc[1].z = fmaf(pp.y, v.z, acc[1].z);
-        acc[1].w = fmaf(pp.y, v.w, acc[1].w);
+        const float2 v01 = make_float2(v.x, v.y), v23 = make_float2(v.z, v.w);
+        const float2 px = make_float2(pp.x, pp.x), py = make_float2(pp.y, pp.y);
+        a0 = __ffma2_rn(px, v01, a0);
+        a1 = __ffma2_rn(px, v23, a1);
+        b0 = __ffma2_rn(py, v01, b0);
+        b1 = __ffma2_rn(py, v23, b1);
       }
+      acc[0] = make_float4(a0.x, a0.y, a1.x, a1.y);
+      acc[1] = make_float4(b0.x, b0.y, b1.x, b1.y);
     }
   }
   // key groups summed in a fixed order (xor tree over the group bits)

@@ -346,29 +346,30 @@ __global__ void __launch_bounds__(kT, 2) k_pf_attn_split(float* o_part, float2* 
     const float* ks = qs + 8 * D;
     const float* vs = ks + kAttnTile * ds;
     const int nk = min(kAttnTile, cur.k1 - (cur.k0 + cur.tile * kAttnTile));
-    {  // partial scores of key `lane` over this warp's dims, heads < G
-      float sc[8];
+    {  // partial scores of key `lane` over this warp's dims, heads < G: even
+       // and odd dims summed apart (packed f32x2 FMAs), then added
+      float2 sc[8];
 #pragma unroll
-      for (int h = 0; h < 8; ++h) sc[h] = 0.0f;
+      for (int h = 0; h < 8; ++h) sc[h] = make_float2(0.0f, 0.0f);
       if (lane < nk) {
 #pragma unroll
         for (int c = 0; c < CW; ++c) {
           const int e = warp * DW + 4 * c;
           const float4 kv = *reinterpret_cast<const float4*>(ks + lane * ds + e);
+          const float2 k01 = make_float2(kv.x, kv.y), k23 = make_float2(kv.z, kv.w);
 #pragma unroll
           for (int h = 0; h < 8; ++h) {
             if (h < G) {
               const float4 qv = *reinterpret_cast<const float4*>(qs + h * D + e);
-              sc[h] = fmaf(qv.x, kv.x, sc[h]);
-              sc[h] = fmaf(qv.y, kv.y, sc[h]);
-              sc[h] = fmaf(qv.z, kv.z, sc[h]);
-              sc[h] = fmaf(qv.w, kv.w, sc[h]);
+              sc[h] = __ffma2_rn(make_float2(qv.x, qv.y), k01, sc[h]);
+              sc[h] = __ffma2_rn(make_float2(qv.z, qv.w), k23, sc[h]);
             }
           }
         }
       }
 #pragma unroll
-      for (int h = 0; h < 8; ++h) red[(warp * 8 + h) * kAttnTile + lane] = sc[h];
+      for (int h = 0; h < 8; ++h)
+        red[(warp * 8 + h) * kAttnTile + lane] = __fadd_rn(sc[h].x, sc[h].y);
     }
     __syncthreads();
     if (warp < G) {  // online softmax of head `warp` over this tile
@@ -395,19 +396,21 @@ __global__ void __launch_bounds__(kT, 2) k_pf_attn_split(float* o_part, float2* 
       const float c0 = cfs[2 * hp], c1 = cfs[2 * hp + 1];
       acc[0].x *= c0; acc[0].y *= c0; acc[0].z *= c0; acc[0].w *= c0;
       acc[1].x *= c1; acc[1].y *= c1; acc[1].z *= c1; acc[1].w *= c1;
+      float2 a0 = make_float2(acc[0].x, acc[0].y), a1 = make_float2(acc[0].z, acc[0].w);
+      float2 b0 = make_float2(acc[1].x, acc[1].y), b1 = make_float2(acc[1].z, acc[1].w);
 #pragma unroll 4
-      for (int k = kg; k < nk; k += KG) {
+      for (int k = kg; k < nk; k += KG) {  // packed f32x2 FMAs, per element as fmaf
         const float4 v = *reinterpret_cast<const float4*>(vs + k * ds + dv);
         const float2 pp = *reinterpret_cast<const float2*>(pr + k * 8 + 2 * hp);
-        acc[0].x = fmaf(pp.x, v.x, acc[0].x);
-        acc[0].y = fmaf(pp.x, v.y, acc[0].y);
-        acc[0].z = fmaf(pp.x, v.z, acc[0].z);
-        acc[0].w = fmaf(pp.x, v.w, acc[0].w);
-        acc[1].x = fmaf(pp.y, v.x, acc[1].x);
-        acc[1].y = fmaf(pp.y, v.y, acc[1].y);
-        acc[1].z = fmaf(pp.y, v.z, acc[1].z);
-        acc[1].w = fmaf(pp.y, v.w, acc[1].w);
+        const float2 v01 = make_float2(v.x, v.y), v23 = make_float2(v.z, v.w);
+        const float2 px = make_float2(pp.x, pp.x), py = make_float2(pp.y, pp.y);
+        a0 = __ffma2_rn(px, v01, a0);
+        a1 = __ffma2_rn(px, v23, a1);
+        b0 = __ffma2_rn(py, v01, b0);
+        b1 = __ffma2_rn(py, v23, b1);
       }
+      acc[0] = make_float4(a0.x, a0.y, a1.x, a1.y);
+      acc[1] = make_float4(b0.x, b0.y, b1.x, b1.y);
     }
     if (cur.tile + 1 == cur.nt) {  // the item is done: its partial out, then a fresh state
       // key groups summed in a fixed order (xor tree over the group bits)
