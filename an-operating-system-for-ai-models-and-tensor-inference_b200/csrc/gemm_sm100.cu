@@ -24,6 +24,8 @@
 #include <cute/tensor.hpp>
 
 
+#include <cstdlib>
+
 #include "gemm_sm100.h"
 #include "kernels.h"
 
@@ -56,6 +58,27 @@ using Mainloop = typename cutlass::gemm::collective::CollectiveBuilder<
 
 using Kernel = cutlass::gemm::kernel::GemmUniversal<Shape<int, int, int, int>, Mainloop, Epilogue>;
 using Gemm = cutlass::gemm::device::GemmUniversalAdapter<Kernel>;
+
+// 64 x 128 tiles (MMA M = 64) for row counts that are a multiple of 64 but
+// not of 128 (three bf16 terms of 64 sequences: 192 rows), where 128-row
+// tiles would compute a third of their second tile for nothing.
+using MmaTile64 = Shape<_64, _128, _64>;
+
+using Epilogue64 = typename cutlass::epilogue::collective::CollectiveBuilder<
+    cutlass::arch::Sm100, cutlass::arch::OpClassTensorOp, MmaTile64, ClusterShape,
+    cutlass::epilogue::collective::EpilogueTileAuto, float, float, float, LayoutC, 4, float,
+    LayoutC, 4, cutlass::epilogue::collective::EpilogueScheduleAuto>::CollectiveOp;
+
+using Mainloop64 = typename cutlass::gemm::collective::CollectiveBuilder<
+    cutlass::arch::Sm100, cutlass::arch::OpClassTensorOp, ElementA, LayoutA, 8, ElementB, LayoutB,
+    8, float, MmaTile64, ClusterShape,
+    cutlass::gemm::collective::StageCountAutoCarveout<static_cast<int>(
+        sizeof(typename Epilogue64::SharedStorage))>,
+    cutlass::gemm::collective::KernelScheduleAuto>::CollectiveOp;
+
+using Kernel64 =
+    cutlass::gemm::kernel::GemmUniversal<Shape<int, int, int, int>, Mainloop64, Epilogue64>;
+using Gemm64 = cutlass::gemm::device::GemmUniversalAdapter<Kernel64>;
 
 template <class G>
 typename G::Arguments make_args(int M, int N, int K, const uint16_t* A, const uint16_t* W,
@@ -110,8 +133,19 @@ bool gemm_supported(int M, int N, int K) {
 }
 
 size_t gemm_workspace_bytes(int M, int N, int K) {
-  return Gemm::get_workspace_size(
-      make_args<Gemm>(M, N, K, nullptr, nullptr, nullptr, nullptr, 0.0f));
+  const size_t a =
+      Gemm::get_workspace_size(make_args<Gemm>(M, N, K, nullptr, nullptr, nullptr, nullptr, 0.0f));
+  const size_t b = Gemm64::get_workspace_size(
+      make_args<Gemm64>(M, N, K, nullptr, nullptr, nullptr, nullptr, 0.0f));
+  return a > b ? a : b;
+}
+
+bool gemm_use64(int M) {
+  static const bool off = [] {
+    const char* e = getenv("MYOS_GEMM_M64");
+    return e && e[0] == '0';
+  }();
+  return !off && M % 128 != 0 && M % 64 == 0;
 }
 
 int gemm_pick_splits(int M, int N, int K, int sms) {
@@ -120,7 +154,8 @@ int gemm_pick_splits(int M, int N, int K, int sms) {
   // its tile's K extent alone), so the K extent is cut into slices of whole
   // 64-wide k-blocks until the tiles x slices fill the SMs once, keeping at
   // least four k-blocks per slice.
-  const long tiles = (long)((M + 127) / 128) * ((N + 127) / 128);
+  const int tm = gemm_use64(M) ? 64 : 128;
+  const long tiles = (long)((M + tm - 1) / tm) * ((N + 127) / 128);
   if (K % 64 != 0 || tiles * 2 > sms) return 1;
   const int kb = K / 64;
   int best = 1;
@@ -136,6 +171,8 @@ cudaError_t gemm_bf16_f32(int M, int N, int K, const uint16_t* A, const uint16_t
   if (splits < 1 || splits > kMaxSplits || K % splits || (K / splits) % 8 ||
       (splits > 1 && (C || beta != 0.0f)))
     return cudaErrorInvalidValue;
+  if (gemm_use64(M))
+    return run<Gemm64>(M, N, K, A, W, C, D, beta, workspace, workspace_bytes, st, ldw, splits, pdl);
   return run<Gemm>(M, N, K, A, W, C, D, beta, workspace, workspace_bytes, st, ldw, splits, pdl);
 }
 
