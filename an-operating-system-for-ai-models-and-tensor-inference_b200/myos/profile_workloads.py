@@ -1,6 +1,9 @@
 """Fixed workloads of the tensor-core (GEMM) path for launch-list and ncu
 captures, on seeded synthetic Qwen2.5-1.5B weights.
 
+    python -m myos.profile_workloads decode NGEN
+        S1: a 128-id prompt, one warm greedy decode of NGEN steps, then the
+        measured one (token steps replayed from CUDA graphs)
     python -m myos.profile_workloads prefill
         three warm 128-id prefills, then the measured one
     python -m myos.profile_workloads batched NSEQ NPROMPT NGEN
@@ -44,6 +47,26 @@ def prefill() -> None:
         e.close()
 
 
+def decode(ngen: int) -> None:
+    shape = synth.shape_qwen25_1_5b()
+    e = Engine(shape, 128 + 2 * ngen)
+    try:
+        e.load_table(synth.weights(shape, 1234))
+        prompt = synth.prompt_ids(1234, 128, shape["vocab"])
+        e.reset()
+        e.prefill(prompt, want_logits=False)
+        e.greedy_decode(ngen)
+        e.reset()
+        e.prefill(prompt, want_logits=False)
+        c0 = _count()
+        e.greedy_decode(ngen)
+        c1 = _count()
+        _, d_ms = e.last_timing()
+        print(f"skip={c0} count={c1 - c0} decode_ms_per_token={d_ms / max(ngen, 1):.4f}", flush=True)
+    finally:
+        e.close()
+
+
 def batched(nseq: int, nprompt: int, ngen: int) -> None:
     shape = synth.shape_qwen25_1_5b()
     e = Engine(shape, max(256, nprompt + ngen))
@@ -64,6 +87,9 @@ def batched(nseq: int, nprompt: int, ngen: int) -> None:
 
 
 def main(argv) -> int:
+    if len(argv) == 2 and argv[0] == "decode":
+        decode(int(argv[1]))
+        return 0
     if len(argv) >= 1 and argv[0] == "prefill":
         prefill()
         return 0
