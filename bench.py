@@ -234,6 +234,36 @@ def run_reference(args, world, rank):
 
 
 # ---------------------------------------------------------------- extra blocks
+def in_step_times(shape, table, local: int, prompt, kind: str):
+    """The dominant kind's in-step run time (ms): a separate context created
+    with MYOS_KTRACE_FILE records %globaltimer stamps per kernel of a 64-step
+    decode; the mean over steps 8..55 of first dependency release to last
+    block end (myos.ktrace)."""
+    import tempfile
+
+    import myos
+    from myos import ktrace
+    path = os.path.join(tempfile.mkdtemp(prefix="myos_kt_"), "trace.bin")
+    old = os.environ.get("MYOS_KTRACE_FILE")
+    os.environ["MYOS_KTRACE_FILE"] = path
+    try:
+        e = myos.Engine(shape, len(prompt) + 64, device=local)
+    finally:
+        if old is None:
+            os.environ.pop("MYOS_KTRACE_FILE", None)
+        else:
+            os.environ["MYOS_KTRACE_FILE"] = old
+    try:
+        e.load_table(table)
+        e.reset()
+        e.prefill(prompt, want_logits=False)
+        e.greedy_decode(64)
+    finally:
+        e.close()
+    summ = ktrace.summarize(path, shape["num_layers"])
+    return summ[kind]["run_us"] / 1000.0 if kind in summ else None
+
+
 def gemv_micro(local: int, peak: float) -> dict:
     """Config 1: each 1.5B decode matrix alone through myos_dev_gemv_bf16,
     bf16 W ~ N(0, 0.02), f32 x ~ N(0, 1). Launches run back to back over
@@ -477,6 +507,7 @@ def run_ours(args, world, rank, local, pg):
               "head": "head GEMV + argmax", "qkv": "qkv GEMV", "down": "down GEMV",
               "o_proj": "o_proj GEMV", "attention": "decode attention"}
     achieved = dom_bytes / (dom_ms / 1000.0) / 1e9
+    in_step = in_step_times(shape, table, local, prompt, dom) if world == 1 else None
     traffic = None
     tp = os.path.join(REPO, "profiles", "traffic.json")
     if os.path.exists(tp):
@@ -535,7 +566,17 @@ def run_ours(args, world, rank, local, pg):
                          "traffic_source": "profiles/traffic.json (one ncu capture, per launch)",
                          "peak_source": peak_kind,
                          "bytes_per_launch": dom_bytes, "ms_per_launch": round(dom_ms, 5),
-                         "share_of_token": round(per_token[dom] / (tot_dec / (args.steps * n_gen)), 4)},
+                         "share_of_token": round(per_token[dom] / (tot_dec / (args.steps * n_gen)), 4),
+                         "timing": "per-kind launches back to back with PDL (profile_kernels), "
+                                   "without the previous kernel's L2 prefetch",
+                         "in_step": None if in_step is None else {
+                             "ms_per_launch": round(in_step, 5),
+                             "achieved": round(dom_bytes / (in_step / 1000.0) / 1e9, 1),
+                             "frac": round(dom_bytes / (in_step / 1000.0) / 1e9 / peak, 4),
+                             "timing": "device %globaltimer stamps of a traced 64-step decode "
+                                       "(MYOS_KTRACE_FILE): first dependency release to last "
+                                       "block end, steps 8..55; part of the weights arrive "
+                                       "through the L2 prefetch the previous kernel issues"}},
             "kernels": {k: {"ms": round(v[0], 5),
                             "gbs": round(v[1] / (v[0] / 1000) / 1e9, 1) if v[0] else None}
                         for k, v in prof.items()},
