@@ -112,6 +112,7 @@ struct myos_ctx {
   size_t pf_ws_bytes = 0;
   size_t pf_D_elems = 0;  // capacity of pf_D in floats
   bool pf_splitk = true;  // MYOS_SPLITK=0: one K slice per projection
+  bool pf_m64 = true;     // MYOS_GEMM_M64=0: 128-row tiles only
   // batched decode (myos_batch_generate): per-sequence KV slabs and buffers
   void *bt_k = nullptr, *bt_v = nullptr;
   size_t bt_kv_bytes = 0;
@@ -1011,6 +1012,8 @@ static int create_impl(myos_ctx* c, const myos_shape* shape, const myos_opts* op
       c->pf_D_elems = M * nmax;
       const char* sk = getenv("MYOS_SPLITK");
       c->pf_splitk = !(sk && sk[0] == '0');
+      const char* m64 = getenv("MYOS_GEMM_M64");
+      c->pf_m64 = !(m64 && m64[0] == '0');
       CK(cudaMalloc(&c->pf_Q, (size_t)nc * (c->qd + 2 * c->kvd) * 4));
       CK(cudaMalloc(&c->pf_ws, ws));
       c->pf_ws_bytes = ws;
@@ -1531,7 +1534,7 @@ static int attn_scratch(myos_ctx* c, int rows, int max_keys) {
 // output tile (or slice) on every SM, bounded by pf_D's room for partials.
 static int pf_splits(const myos_ctx* c, int M, int N, int K) {
   if (!c->pf_splitk) return 1;
-  int sp = gemm_pick_splits(M, N, K, c->num_sms);
+  int sp = gemm_pick_splits(M, N, K, c->num_sms, c->pf_m64);
   while (sp > 1 && ((size_t)sp * M * N > c->pf_D_elems || (K / 64) % sp)) --sp;
   return sp;
 }
@@ -1545,7 +1548,7 @@ static cudaError_t pf_gemm(const myos_ctx* c, int M, int N, int K, const uint16_
   if (!sp) sp = &one;
   else *sp = pf_splits(c, M, N, K);
   return gemm_bf16_f32(M, N, K, c->pf_A, W, nullptr, D, 0.0f, c->pf_ws, c->pf_ws_bytes, st, ldw,
-                       *sp, pf_pdl());
+                       *sp, pf_pdl(), c->pf_m64);
 }
 
 // One chunk of n prompt tokens at positions p0.. through every layer

@@ -24,8 +24,6 @@
 #include <cute/tensor.hpp>
 
 
-#include <cstdlib>
-
 #include "gemm_sm100.h"
 #include "kernels.h"
 
@@ -140,21 +138,15 @@ size_t gemm_workspace_bytes(int M, int N, int K) {
   return a > b ? a : b;
 }
 
-bool gemm_use64(int M) {
-  static const bool off = [] {
-    const char* e = getenv("MYOS_GEMM_M64");
-    return e && e[0] == '0';
-  }();
-  return !off && M % 128 != 0 && M % 64 == 0;
-}
+bool gemm_use64(int M, bool allow) { return allow && M % 128 != 0 && M % 64 == 0; }
 
-int gemm_pick_splits(int M, int N, int K, int sms) {
+int gemm_pick_splits(int M, int N, int K, int sms, bool m64) {
   // One 128 x 128 output tile per CTA: a projection with fewer tiles than
   // SMs streams its weights through a fraction of the chip (each SM pulls
   // its tile's K extent alone), so the K extent is cut into slices of whole
   // 64-wide k-blocks until the tiles x slices fill the SMs once, keeping at
   // least four k-blocks per slice.
-  const int tm = gemm_use64(M) ? 64 : 128;
+  const int tm = gemm_use64(M, m64) ? 64 : 128;
   const long tiles = (long)((M + tm - 1) / tm) * ((N + 127) / 128);
   if (K % 64 != 0 || tiles * 2 > sms) return 1;
   const int kb = K / 64;
@@ -166,12 +158,13 @@ int gemm_pick_splits(int M, int N, int K, int sms) {
 
 cudaError_t gemm_bf16_f32(int M, int N, int K, const uint16_t* A, const uint16_t* W,
                           const float* C, float* D, float beta, void* workspace,
-                          size_t workspace_bytes, cudaStream_t st, int ldw, int splits, bool pdl) {
+                          size_t workspace_bytes, cudaStream_t st, int ldw, int splits, bool pdl,
+                          bool m64) {
   if (!gemm_supported(M, N, K) || (ldw && (ldw < K || ldw % 8))) return cudaErrorInvalidValue;
   if (splits < 1 || splits > kMaxSplits || K % splits || (K / splits) % 8 ||
       (splits > 1 && (C || beta != 0.0f)))
     return cudaErrorInvalidValue;
-  if (gemm_use64(M))
+  if (gemm_use64(M, m64))
     return run<Gemm64>(M, N, K, A, W, C, D, beta, workspace, workspace_bytes, st, ldw, splits, pdl);
   return run<Gemm>(M, N, K, A, W, C, D, beta, workspace, workspace_bytes, st, ldw, splits, pdl);
 }

@@ -19,15 +19,16 @@ bool gemm_supported(int M, int N, int K);
 size_t gemm_workspace_bytes(int M, int N, int K);
 // Slices that let an [M, N] output's 128 x 128 tiles fill `sms` SMs once
 // (1 when the tiles already cover half of them or K is not 64-aligned).
-int gemm_pick_splits(int M, int N, int K, int sms);
-// Whether an M-row projection runs on 64 x 128 tiles (M a multiple of 64
-// but not of 128; MYOS_GEMM_M64=0: never) instead of 128 x 128.
-bool gemm_use64(int M);
+// m64: 64-row tiles allowed (as gemm_use64).
+int gemm_pick_splits(int M, int N, int K, int sms, bool m64 = true);
+// Whether an M-row projection runs on 64 x 128 tiles (allowed, and M a
+// multiple of 64 but not of 128) instead of 128 x 128.
+bool gemm_use64(int M, bool allow);
 // pdl: launch with a programmatic edge to the previous kernel in the stream
 // (the GEMM reads nothing before that kernel has finished).
 cudaError_t gemm_bf16_f32(int M, int N, int K, const uint16_t* A, const uint16_t* W,
                           const float* C, float* D, float beta, void* workspace,
                           size_t workspace_bytes, cudaStream_t st, int ldw = 0, int splits = 1,
-                          bool pdl = false);
+                          bool pdl = false, bool m64 = true);
 
 }  // namespace myos
