@@ -80,6 +80,7 @@ struct myos_ctx {
   float *part_val = nullptr, *part_o = nullptr, *part_m = nullptr, *part_l = nullptr;
   uint32_t* part_idx = nullptr;
   unsigned* counters = nullptr;  // [0] head, [1..Hkv] attention
+  unsigned long long* attn_arrive = nullptr;  // [Hkv] split arrivals (distributed merge)
   StepCtl* ctl = nullptr;
   uint32_t *feed = nullptr, *rec_fed = nullptr, *rec_argmax = nullptr;
   float *cos_t = nullptr, *sin_t = nullptr;
@@ -468,6 +469,7 @@ int launch_kind(myos_ctx* c, int kind, int l, const uint32_t* feed, bool pdl, bo
     at.part_m = c->part_m;
     at.part_l = c->part_l;
     at.counters = c->counters + 1;
+    at.arrive = c->attn_arrive;
     at.out = c->attn;
     at.decode = 1;
     at.defer_merge = c->defer_merge;
@@ -674,6 +676,8 @@ int finish(myos_ctx* c) {
     // an arrival count left partway would misplace the next MLP launch's target
     if (c->mlp_arrive) cudaMemset(c->mlp_arrive, 0, sizeof(unsigned long long));
     cudaMemset(c->counters, 0, (1 + c->s.num_kv_heads) * 4);
+    // arrival counts left partway would misplace the next launch's targets
+    cudaMemset(c->attn_arrive, 0, c->s.num_kv_heads * sizeof(unsigned long long));
     return fail(c, MYOS_ERR_TIMEOUT,
                 "a bounded device wait gave up (bits " + std::to_string(bits) + ")");
   }
@@ -925,6 +929,7 @@ static int create_impl(myos_ctx* c, const myos_shape* shape, const myos_opts* op
   c->warps_head = gemv_warps((int)c->head_rows, (int)H, 1, true, c->grid_head);
   size_t nsplit = (S + 31) / 32;
   size_t cap = (size_t)c->num_sms / s.num_kv_heads;
+  if (cap > 160) cap = 160;  // the split merge takes at most 160 splits
   if (cap < 1) cap = 1;
   if (nsplit > cap) nsplit = cap;
   c->attn_nsplit = (int)nsplit;
@@ -957,6 +962,8 @@ static int create_impl(myos_ctx* c, const myos_shape* shape, const myos_opts* op
   CK(cudaMalloc(&c->part_l, (size_t)s.num_kv_heads * nsplit * c->G * 4));
   CK(cudaMalloc(&c->counters, (1 + s.num_kv_heads) * 4));
   CK(cudaMemset(c->counters, 0, (1 + s.num_kv_heads) * 4));
+  CK(cudaMalloc(&c->attn_arrive, s.num_kv_heads * sizeof(unsigned long long)));
+  CK(cudaMemset(c->attn_arrive, 0, s.num_kv_heads * sizeof(unsigned long long)));
   {
     const char* e = getenv("MYOS_MLP");
     if (c->tp_size == 1 && !(e && e[0] == '0')) c->grid_mlp = mlp_grid((int)H, (int)I, c->num_sms);
@@ -1166,7 +1173,7 @@ void myos_ctx_destroy(myos_ctx* c) {
     if (c->tp_peer[p] && c->tp_peer[p] != c->tp_link) cudaIpcCloseMemHandle(c->tp_peer[p]);
   tp_comm_destroy(c->comm);
   void* dev[] = {c->warena, c->kcache, c->vcache, c->resid, c->qkv, c->attn, c->act, c->logits,
-                 c->part_val, c->part_idx, c->part_o, c->part_m, c->part_l, c->counters, c->ctl,
+                 c->part_val, c->part_idx, c->part_o, c->part_m, c->part_l, c->counters, (void*)c->attn_arrive, c->ctl,
                  c->feed, c->rec_fed, c->rec_argmax, c->cos_t, c->sin_t, c->mlp_part, c->mlp_arrive, c->mlp_wd,
                  (void*)c->ktrace, c->pf_X, c->pf_D, c->pf_Q, c->pf_A, c->pf_ws,
                  c->bt_k, c->bt_v, c->bt_X, c->bt_D, c->bt_pos, c->bt_rows, c->bt_tok,

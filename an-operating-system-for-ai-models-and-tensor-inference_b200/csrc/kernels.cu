@@ -1659,18 +1659,120 @@ __global__ void __launch_bounds__(kThreads, 1) k_attn_dec(AttnArgs a) {
       a.part_l[pb + warp] = l_run;
     }
     if (!a.defer_merge) {
+      // The last G blocks of KV head g to arrive merge one query head each
+      // (h = 0 for the last), once every split's partial is written: warp w
+      // folds splits [w per, (w + 1) per) (one round of loads), then warp 0
+      // combines the 8 warp results in warp order. Each wait is bounded.
       __threadfence();
       __syncthreads();
-      if (threadIdx.x == 0) last_block = atomicAdd(a.counters + g, 1u) == (unsigned)(ns - 1);
-      __syncthreads();
-      if (last_block) {
-        __threadfence();
-        // warp h merges head h over the splits that hold keys, in split order
-        if (warp < G) {
-          GlobalPartials src = {a.part_m, a.part_l, a.part_o, (size_t)g * ns * G + warp, G, d};
-          merge_head(src, ne, d, lane, a.out + ((size_t)g * G + warp) * d);
+      if (threadIdx.x == 0) {
+        last_block = -1;
+        const unsigned long long old = atomicAdd(a.arrive + g, 1ull);
+        const int k = ns - 1 - (int)(old % (unsigned long long)ns);
+        if (k < G) {
+          const unsigned long long target = (old / (unsigned long long)ns + 1ull) * ns;
+          bool ok = true;
+          if (ld_acquire_u64(a.arrive + g) < target) {
+            const uint64_t t0 = global_ns();
+            for (uint32_t i = 1;; ++i) {
+              if (ld_acquire_u64(a.arrive + g) >= target) break;
+              if ((i & 63u) == 0 && global_ns() - t0 > 1000000000ull) {
+                atomicOr(&a.ctl->err, kErrAttnWait);
+                ok = false;
+                break;
+              }
+            }
+          }
+          if (ok) last_block = k;
         }
-        if (threadIdx.x == 0) a.counters[g] = 0u;
+      }
+      __syncthreads();
+      if (last_block >= 0) {
+        __threadfence();
+        const int h = last_block;
+        const size_t hb = (size_t)g * ns * G + h;  // partial row of split q: hb + q * G
+        constexpr int JD = D > 128 ? 2 : 1;
+        const int per = (ne + kDecWarps - 1) / kDecWarps;  // <= 20 (ne <= 160)
+        const int q0 = warp * per, q1 = min(ne, q0 + per);
+        float* wo = red;                          // [8][D] warp outputs
+        float* wm = red + kDecWarps * D;          // [8] warp maxima
+        float* wl = wm + kDecWarps;               // [8] warp sums
+        const int q = q0 + lane;
+        const float mq = q < q1 ? __ldcg(a.part_m + hb + (size_t)q * G) : -INFINITY;
+        const float lq = q < q1 ? __ldcg(a.part_l + hb + (size_t)q * G) : 0.0f;
+        constexpr int kW = 20;
+        float4 po[JD][kW];
+#pragma unroll
+        for (int u = 0; u < kW; ++u)
+#pragma unroll
+          for (int j = 0; j < JD; ++j) {
+            const int e = 4 * lane + 128 * j;
+            po[j][u] = (q0 + u < q1 && e < D)
+                           ? __ldcg(reinterpret_cast<const float4*>(a.part_o + (hb + (size_t)(q0 + u) * G) * D + e))
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+        const float Mw = warp_max(mq);
+        const float fq = mq == -INFINITY ? 0.0f : expf(mq - Mw);
+        const float Lw = warp_sum(lq * fq);
+        float4 Ow[JD];
+#pragma unroll
+        for (int j = 0; j < JD; ++j) Ow[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int u = 0; u < kW; ++u) {
+          const float fu = __shfl_sync(0xffffffffu, fq, u);
+          if (q0 + u < q1)
+#pragma unroll
+            for (int j = 0; j < JD; ++j) {
+              Ow[j].x = fmaf(po[j][u].x, fu, Ow[j].x);
+              Ow[j].y = fmaf(po[j][u].y, fu, Ow[j].y);
+              Ow[j].z = fmaf(po[j][u].z, fu, Ow[j].z);
+              Ow[j].w = fmaf(po[j][u].w, fu, Ow[j].w);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < JD; ++j) {
+          const int e = 4 * lane + 128 * j;
+          if (e < D) *reinterpret_cast<float4*>(wo + warp * D + e) = Ow[j];
+        }
+        if (lane == 0) {
+          wm[warp] = Mw;
+          wl[warp] = Lw;
+        }
+        __syncthreads();
+        if (warp == 0) {
+          float M = -INFINITY;
+#pragma unroll
+          for (int w = 0; w < kDecWarps; ++w) M = fmaxf(M, wm[w]);
+          float L = 0.0f;
+          float4 O[JD];
+#pragma unroll
+          for (int j = 0; j < JD; ++j) O[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+          for (int w = 0; w < kDecWarps; ++w) {
+            const float f = wm[w] == -INFINITY ? 0.0f : expf(wm[w] - M);
+            L = fmaf(wl[w], f, L);
+#pragma unroll
+            for (int j = 0; j < JD; ++j) {
+              const int e = 4 * lane + 128 * j;
+              if (e < D) {
+                const float4 o = *reinterpret_cast<const float4*>(wo + w * D + e);
+                O[j].x = fmaf(o.x, f, O[j].x);
+                O[j].y = fmaf(o.y, f, O[j].y);
+                O[j].z = fmaf(o.z, f, O[j].z);
+                O[j].w = fmaf(o.w, f, O[j].w);
+              }
+            }
+          }
+          float* outp = a.out + ((size_t)g * G + h) * D;
+#pragma unroll
+          for (int j = 0; j < JD; ++j) {
+            const int e = 4 * lane + 128 * j;
+            if (e < D)
+              *reinterpret_cast<float4*>(outp + e) =
+                  make_float4(__fdiv_rn(O[j].x, L), __fdiv_rn(O[j].y, L), __fdiv_rn(O[j].z, L),
+                              __fdiv_rn(O[j].w, L));
+          }
+        }
       }
     }
   }

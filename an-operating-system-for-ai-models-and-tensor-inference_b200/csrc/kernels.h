@@ -135,6 +135,9 @@ struct AttnArgs {
   float* part_m;         // [Hkv][nsplit][G]
   float* part_l;
   unsigned* counters;    // [Hkv], zero between launches
+  // decode, more than 8 splits: arrivals per KV head (monotonic; each launch
+  // adds nsplit), the last G blocks to arrive each merge one query head
+  unsigned long long* arrive;
   float* out;            // [Hq*d]
   int decode;
   int defer_merge;       // decode: write the split partials only; the o_proj
@@ -158,6 +161,7 @@ size_t merge_smem_bytes(int Hq, int nsplit, int d);
 // and down_proj needs no staging of it.
 constexpr int kMlpSlice = 64;     // intermediate columns per block
 constexpr uint32_t kErrMlpWait = 16u;
+constexpr uint32_t kErrAttnWait = 32u;  // a split-merge arrival wait gave up
 struct MlpArgs {
   const uint16_t *wg, *wu, *wd;  // gate, up [I][H]; down [H][I]
   // down_proj re-laid out by block, [grid][H][64] (mlp_relayout), so a block
