@@ -31,6 +31,9 @@ namespace cg = cooperative_groups;
 // memory to be visible) before its first global access, then lets the next
 // one be scheduled, so launches overlap their predecessors' tails.
 bool g_pdl = true;  // MYOS_GEMM_PDL=0 at pf_init: plain stream order
+// prompt chunks whose rows reach at least this many keys use the row-tiled
+// attention (MYOS_PF_ATTN_ROWS_MIN at pf_init; the per-row split kernel below)
+int g_rows_min = 1024;
 
 MYOS_DEV void pdl_begin() {
   pdl_wait();
@@ -443,6 +446,182 @@ __global__ void __launch_bounds__(kT, 2) k_pf_attn_split(float* o_part, float2* 
   }
 }
 
+// Causal GQA for a chunk of prompt rows, tiled over rows as well as keys
+// (D = 128, long contexts): block (ti, g, s) takes rows [16 ti, 16 ti + 16),
+// every query head of KV head g (warp h = head h) and the keys [s ch,
+// (s + 1) ch) at or before each row's position. Each 32-key tile of K and V
+// is staged once for all 16 x G query vectors. Scores: lane (rr, kk) holds
+// rows 4 rr..4 rr+3 x keys kk, kk+8, kk+16, kk+24 (conflict-free reads of the
+// padded rows); online softmax per row across the 8 lanes of its group;
+// p * v: lane = 4 dims x all 16 rows. Writes the same split partials as
+// k_pf_attn_split (merged by k_pf_attn_merge).
+constexpr int kRowTile = 16;
+template <int D>
+constexpr size_t attn_rows_smem_bytes(int G) {
+  return ((size_t)G * kRowTile * (D + 4) + 2 * kAttnTile * (D + 4) +
+          (size_t)G * kAttnTile * kRowTile + (size_t)G * kRowTile) *
+         sizeof(float);
+}
+
+template <typename KT>
+__global__ void __launch_bounds__(256) k_pf_attn_rows(float* o_part, float2* ml, const float* Q,
+                                                      const KT* kcache, const KT* vcache, int p0,
+                                                      int n, int Hq, int Hkv, int S, float scale,
+                                                      int ch, int ns) {
+  pdl_begin();  // the previous kernel of the stream has finished (PDL)
+  constexpr int D = 128, ds = D + 4, V4 = D / 4;
+  const int ti = blockIdx.x, g = blockIdx.y, sidx = blockIdx.z, G = Hq / Hkv;
+  const int r0 = ti * kRowTile, r1 = min(n, r0 + kRowTile);
+  const int k0 = sidx * ch;
+  if (k0 > p0 + r1 - 1) return;  // every row of the tile ends before this split
+  const int k1 = min(k0 + ch, p0 + r1);  // keys of the tile's last row end at p0 + r1 - 1
+  extern __shared__ __align__(16) float sm[];
+  float* qs = sm;                                 // [G][16][ds]
+  float* ks = qs + (size_t)G * kRowTile * ds;     // [32][ds]
+  float* vs = ks + kAttnTile * ds;                // [32][ds]
+  float* ps = vs + kAttnTile * ds;                // [G][32 keys][16 rows]
+  float* rsc = ps + (size_t)G * kAttnTile * kRowTile;  // [G][16] rescale factors
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nt = blockDim.x;
+  const int N = (Hq + 2 * Hkv) * D;
+  // q rows of the G heads (rows past n read as zeros)
+  for (int i = threadIdx.x; i < G * kRowTile * V4; i += nt) {
+    const int h = i / (kRowTile * V4), rem = i - h * kRowTile * V4, r = rem / V4,
+              e = (rem - r * V4) * 4;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (r0 + r < n) v = *reinterpret_cast<const float4*>(Q + (size_t)(r0 + r) * N + (size_t)(g * G + h) * D + e);
+    *reinterpret_cast<float4*>(qs + ((size_t)h * kRowTile + r) * ds + e) = v;
+  }
+  const KT* kc = kcache + (size_t)g * S * D;
+  const KT* vc = vcache + (size_t)g * S * D;
+  const int h = warp;                  // this warp's query head (warps >= G only load)
+  const int rr = lane >> 3, kk = lane & 7;
+  float m_run[4], l_run[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    m_run[i] = -INFINITY;
+    l_run[i] = 0.0f;
+  }
+  float4 o[kRowTile];  // p * v: rows 0..15 x dims 4 lane..4 lane+3
+#pragma unroll
+  for (int r = 0; r < kRowTile; ++r) o[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int t0 = k0; t0 < k1; t0 += kAttnTile) {
+    const int nk = min(kAttnTile, k1 - t0);
+    __syncthreads();  // the previous tile is consumed (and q staged)
+    for (int i = threadIdx.x; i < kAttnTile * V4; i += nt) {
+      const int tt = i / V4, e = (i - tt * V4) * 4;
+      float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
+      if (tt < nk) {
+        kv = kv4<KT>(kc + (size_t)(t0 + tt) * D + e);
+        vv = kv4<KT>(vc + (size_t)(t0 + tt) * D + e);
+      }
+      *reinterpret_cast<float4*>(ks + tt * ds + e) = kv;
+      *reinterpret_cast<float4*>(vs + tt * ds + e) = vv;
+    }
+    __syncthreads();
+    if (h < G) {
+      // scores of rows 4rr+i and keys kk+8j
+      float2 sc[4][4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) sc[i][j] = make_float2(0.f, 0.f);
+      const float* qh = qs + ((size_t)h * kRowTile + 4 * rr) * ds;
+#pragma unroll 4
+      for (int e = 0; e < D; e += 4) {
+        float4 qv[4], kv[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) qv[i] = *reinterpret_cast<const float4*>(qh + i * ds + e);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) kv[j] = *reinterpret_cast<const float4*>(ks + (kk + 8 * j) * ds + e);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            sc[i][j] = __ffma2_rn(make_float2(qv[i].x, qv[i].y), make_float2(kv[j].x, kv[j].y), sc[i][j]);
+            sc[i][j] = __ffma2_rn(make_float2(qv[i].z, qv[i].w), make_float2(kv[j].z, kv[j].w), sc[i][j]);
+          }
+      }
+      // mask, online softmax per row (its 32 keys live in the 8 lanes kk)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int r = 4 * rr + i, pos = p0 + r0 + r;
+        float s[4], mt = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int key = kk + 8 * j, kp = t0 + key;
+          s[j] = (key < nk && kp <= pos && r0 + r < n)
+                     ? __fmul_rn(__fadd_rn(sc[i][j].x, sc[i][j].y), scale)
+                     : -INFINITY;
+          mt = fmaxf(mt, s[j]);
+        }
+        mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 1));
+        mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 2));
+        mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 4));
+        const float mn = fmaxf(m_run[i], mt);
+        const float cf = mn == -INFINITY ? 1.0f : expf(m_run[i] - mn);
+        float ls = 0.0f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float p = s[j] == -INFINITY ? 0.0f : expf(s[j] - mn);
+          ps[((size_t)h * kAttnTile + kk + 8 * j) * kRowTile + r] = p;
+          ls += p;
+        }
+        ls += __shfl_xor_sync(0xffffffffu, ls, 1);
+        ls += __shfl_xor_sync(0xffffffffu, ls, 2);
+        ls += __shfl_xor_sync(0xffffffffu, ls, 4);
+        l_run[i] = fmaf(l_run[i], cf, ls);
+        m_run[i] = mn;
+        if (kk == 0) rsc[h * kRowTile + r] = cf;
+      }
+      __syncwarp();
+      // p * v: this lane's 4 dims for all 16 rows
+      const float* rs = rsc + h * kRowTile;
+#pragma unroll
+      for (int r = 0; r < kRowTile; ++r) {
+        const float c = rs[r];
+        o[r].x *= c;
+        o[r].y *= c;
+        o[r].z *= c;
+        o[r].w *= c;
+      }
+      const float* ph = ps + (size_t)h * kAttnTile * kRowTile;
+      for (int k = 0; k < nk; ++k) {
+        const float4 v = *reinterpret_cast<const float4*>(vs + k * ds + 4 * lane);
+        const float2 v01 = make_float2(v.x, v.y), v23 = make_float2(v.z, v.w);
+#pragma unroll
+        for (int r4 = 0; r4 < kRowTile; r4 += 4) {
+          const float4 p = *reinterpret_cast<const float4*>(ph + k * kRowTile + r4);
+          const float pr[4] = {p.x, p.y, p.z, p.w};
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            float2 a = make_float2(o[r4 + u].x, o[r4 + u].y), b = make_float2(o[r4 + u].z, o[r4 + u].w);
+            a = __ffma2_rn(make_float2(pr[u], pr[u]), v01, a);
+            b = __ffma2_rn(make_float2(pr[u], pr[u]), v23, b);
+            o[r4 + u] = make_float4(a.x, a.y, b.x, b.y);
+          }
+        }
+      }
+      __syncwarp();  // ps and rsc are rewritten by the next tile
+    }
+  }
+  if (h < G) {
+#pragma unroll
+    for (int r = 0; r < kRowTile; ++r) {
+      if (r0 + r >= n || p0 + r0 + r < k0) continue;  // no keys of this split for the row
+      const size_t slot = ((size_t)(r0 + r) * Hq + (size_t)g * G + h) * ns + sidx;
+      *reinterpret_cast<float4*>(o_part + slot * D + 4 * lane) = o[r];
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int r = 4 * rr + i;
+      if (kk == 0 && r0 + r < n && p0 + r0 + r >= k0) {
+        const size_t slot = ((size_t)(r0 + r) * Hq + (size_t)g * G + h) * ns + sidx;
+        ml[slot] = make_float2(m_run[i], l_run[i]);
+      }
+    }
+  }
+}
+
 // out = (sum over splits of o_s * e^(m_s - M)) / (sum of l_s * e^(m_s - M)),
 // M the largest split maximum; written into A as the three bf16 terms of the
 // o_proj input (row length Hq * D). One warp per (row, head): lanes hold the
@@ -801,6 +980,15 @@ cudaError_t pf_init() {
   MYOS_PF_SMEM(__nv_bfloat16, 64)
   MYOS_PF_SMEM(__nv_bfloat16, 128)
 #undef MYOS_PF_SMEM
+  const int rows_smem = (int)attn_rows_smem_bytes<128>(8);
+  if (cudaError_t e = cudaFuncSetAttribute(
+          k_pf_attn_rows<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, rows_smem))
+    return e;
+  if (cudaError_t e = cudaFuncSetAttribute(k_pf_attn_rows<__nv_bfloat16>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, rows_smem))
+    return e;
+  const char* rm = getenv("MYOS_PF_ATTN_ROWS_MIN");
+  g_rows_min = rm ? atoi(rm) : 1024;
   return cudaSuccess;
 }
 
@@ -818,6 +1006,23 @@ cudaError_t pf_attn(uint16_t* A, float* o_part, float2* ml, const float* Q, cons
                     float scale, int max_keys, int sms, cudaStream_t st, const int* rowpos,
                     size_t rowstride) {
   if (!pf_attn_supported(d, Hq / Hkv) || max_keys < 1 || sms < 1) return cudaErrorInvalidValue;
+  if (!rowpos && d == 128 && max_keys >= g_rows_min) {  // a long prompt chunk: row tiles
+    int ch = 256;
+    while ((max_keys + ch - 1) / ch > kAttnMaxSplits) ch += 256;
+    const int ns = (max_keys + ch - 1) / ch, G = Hq / Hkv;
+    const dim3 grid((n + kRowTile - 1) / kRowTile, Hkv, ns);
+    const size_t smem = attn_rows_smem_bytes<128>(G);
+    cudaError_t e = kv_bf16
+                        ? launch(k_pf_attn_rows<__nv_bfloat16>, grid, 32 * G, smem, st, o_part, ml,
+                                 Q, (const __nv_bfloat16*)kc, (const __nv_bfloat16*)vc, p0, n, Hq,
+                                 Hkv, S, scale, ch, ns)
+                        : launch(k_pf_attn_rows<float>, grid, 32 * G, smem, st, o_part, ml, Q,
+                                 (const float*)kc, (const float*)vc, p0, n, Hq, Hkv, S, scale, ch,
+                                 ns);
+    if (e != cudaSuccess) return e;
+    return launch(k_pf_attn_merge<128>, dim3(n, (Hq + 3) / 4), 128, 0, st, A, o_part, ml, p0, Hq,
+                  ch, ns, rowpos);
+  }
   int ch = 0;
   const int ns = pf_attn_splits(max_keys, &ch);
   const long items = (long)n * Hkv * ns;
