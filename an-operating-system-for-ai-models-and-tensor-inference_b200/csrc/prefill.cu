@@ -34,6 +34,10 @@ bool g_pdl = true;  // MYOS_GEMM_PDL=0 at pf_init: plain stream order
 // prompt chunks whose rows reach at least this many keys use the row-tiled
 // attention (MYOS_PF_ATTN_ROWS_MIN at pf_init; the per-row split kernel below)
 int g_rows_min = 1024;
+// the per-row split attention with keys split over the warps
+// (k_pf_attn_warps; D = 128, 5..8 query heads per KV head); MYOS_PF_ATTN_WARPS
+// at pf_init, 0: the dims-split k_pf_attn_split
+bool g_attn_warps = true;
 
 MYOS_DEV void pdl_begin() {
   pdl_wait();
@@ -443,6 +447,237 @@ __global__ void __launch_bounds__(kT, 2) k_pf_attn_split(float* o_part, float2* 
     cur = nxt;
     nxt = advance(nxt);
     slot ^= 1;
+  }
+}
+
+// One step of the halving exchange that sums a warp's partial dot products:
+// of the first N values a lane keeps the half its `bit` selects (the upper
+// half when set), adds its partner's (lane ^ off) copy of that half and
+// stores the sums in s[0, N/2). After N = 32, 16, 8, 4, 2 with off = N / 2,
+// lane L holds the warp-wide sum of value L.
+template <int N>
+MYOS_DEV void halve_sum(float (&s)[32], bool bit, int off) {
+#pragma unroll
+  for (int i = 0; i < N / 2; ++i) {
+    const float lo = s[i], hi = s[i + N / 2];
+    const float keep = bit ? hi : lo, send = bit ? lo : hi;
+    s[i] = __fadd_rn(keep, __shfl_xor_sync(0xffffffffu, send, off));
+  }
+}
+
+// The split attention of k_pf_attn_split (same items, persistent grid,
+// double-buffered 32-key tiles, same partial outputs for k_pf_attn_merge)
+// with a tile's work split by keys instead of dims (D = 128, G query heads
+// per KV head): warp w owns keys 4w..4w+3 of every tile and keeps its own
+// running max, sum and p * v accumulator per head; lane = 4 dims of every
+// head, q held in registers for the item. The 4 keys x 8 heads partial dot
+// products over a lane's dims are summed across the warp by the halving
+// exchange, leaving (head h, key j) in lane 4h + j, where the online
+// softmax runs over the warp's 4 keys with two shuffles. A tile needs no
+// block barrier besides the staging one; when an item ends the 8 warps'
+// states meet in shared memory and are combined in warp order.
+// Shared memory of k_pf_attn_warps: three slots of (q heads of the group,
+// K tile, V tile), rows unpadded.
+constexpr int kWarpsSlot = 8 * 128 + 2 * kAttnTile * 128;
+constexpr size_t kWarpsSmem = 3 * kWarpsSlot * sizeof(float);
+
+template <typename KT, int G>
+__global__ void __launch_bounds__(kT, 2) k_pf_attn_warps(float* o_part, float2* ml, const float* Q,
+                                                         const KT* kcache, const KT* vcache, int p0,
+                                                         int n, int Hq, int Hkv, int S, float scale,
+                                                         int ch, int ns, const int* rowpos,
+                                                         size_t rowstride) {
+  pdl_begin();  // the previous kernel of the stream has finished (PDL)
+  constexpr int D = 128, ds = D, V4 = D / 4;  // rows unpadded: a warp reads whole rows
+  constexpr int SLOT = kWarpsSlot;
+  constexpr int kPer = (kAttnTile * V4 + kT - 1) / kT;  // float4s of K (and of V) per thread
+  constexpr int KW = kAttnTile / kAttnWarps;            // keys of a warp per tile
+  static_assert(KW == 4 && G >= 1 && G <= 8, "4 keys x 8 heads fill the 32 lanes");
+  static_assert(kAttnWarps * G * D + 2 * kAttnWarps * 8 <= SLOT, "warp states fit a slot");
+  extern __shared__ __align__(16) float sm[];
+  const int n_items = n * Hkv * ns;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int N = (Hq + 2 * Hkv) * D;
+
+  auto open_item = [&](AttnItem& it, int item) {  // first non-empty item from `item` on
+    for (; item < n_items; item += gridDim.x) {
+      const int s = item % ns, g = (item / ns) % Hkv, t = item / (ns * Hkv);
+      const int pos = rowpos ? rowpos[t] : p0 + t, k0 = s * ch;
+      if (k0 > pos) continue;  // this row has fewer splits
+      it.item = item;
+      it.tile = 0;
+      it.t = t;
+      it.g = g;
+      it.s = s;
+      it.k0 = k0;
+      it.k1 = min(k0 + ch, pos + 1);
+      it.nt = (it.k1 - k0 + kAttnTile - 1) / kAttnTile;
+      return;
+    }
+    it.item = n_items;
+  };
+  auto advance = [&](AttnItem it) {
+    if (++it.tile < it.nt) return it;
+    open_item(it, it.item + gridDim.x);
+    return it;
+  };
+  auto stage = [&](const AttnItem& it, int slot) {
+    float* qs = sm + slot * SLOT;
+    float* ks = qs + 8 * D;
+    float* vs = ks + kAttnTile * ds;
+    const size_t cofs = (rowpos ? (size_t)it.t * rowstride : 0) + (size_t)it.g * S * D;
+    const KT* kc = kcache + cofs;
+    const KT* vc = vcache + cofs;
+    const int t0 = it.k0 + it.tile * kAttnTile, nk = min(kAttnTile, it.k1 - t0);
+    const float* q = Q + (size_t)it.t * N + (size_t)it.g * G * D;
+    for (int i = threadIdx.x; i < G * V4; i += kT) cp_async16(qs + 4 * i, q + 4 * i);
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int idx = threadIdx.x + i * kT, tt = idx / V4, e = (idx - tt * V4) * 4;
+      if (tt < nk) {
+        if constexpr (sizeof(KT) == 4) {
+          cp_async16(ks + tt * ds + e, kc + (size_t)(t0 + tt) * D + e);
+          cp_async16(vs + tt * ds + e, vc + (size_t)(t0 + tt) * D + e);
+        } else {
+          *reinterpret_cast<float4*>(ks + tt * ds + e) = kv4<KT>(kc + (size_t)(t0 + tt) * D + e);
+          *reinterpret_cast<float4*>(vs + tt * ds + e) = kv4<KT>(vc + (size_t)(t0 + tt) * D + e);
+        }
+      }
+    }
+    cp_async_commit();
+  };
+
+  const int hl = lane >> 2, jl = lane & 3;  // the (head, key) of this lane's summed score
+  const int kb = warp * KW;                 // this warp's first key of a tile
+  float4 q[G], acc[G];
+  float m_h = -INFINITY, l_h = 0.0f;  // head hl over this warp's keys of the item
+
+  AttnItem cur;
+  open_item(cur, blockIdx.x);
+  if (cur.item >= n_items) return;
+  stage(cur, 0);
+  AttnItem nxt = advance(cur);
+  if (nxt.item < n_items) stage(nxt, 1);
+  else cp_async_commit();  // an empty group keeps one group per tile
+  int slot = 0;
+  while (cur.item < n_items) {
+    const AttnItem nxt2 = advance(nxt);
+    if (nxt2.item < n_items) stage(nxt2, slot == 0 ? 2 : slot - 1);
+    else cp_async_commit();
+    cp_async_wait<2>();  // this tile's group has landed; two more in flight
+    __syncthreads();     // every thread's copies of this tile are visible
+    const float* qs = sm + slot * SLOT;
+    const float* ks = qs + 8 * D;
+    const float* vs = ks + kAttnTile * ds;
+    const int nk = min(kAttnTile, cur.k1 - (cur.k0 + cur.tile * kAttnTile));
+    if (cur.tile == 0) {  // a new item: its q, a fresh state
+#pragma unroll
+      for (int h = 0; h < G; ++h) {
+        q[h] = *reinterpret_cast<const float4*>(qs + h * D + 4 * lane);
+        acc[h] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      m_h = -INFINITY;
+      l_h = 0.0f;
+    }
+    if (kb < nk) {  // warp-uniform: this warp has keys in the tile
+      float s[32];  // value 4h + j: head h, key kb + j, over this lane's dims
+#pragma unroll
+      for (int j = 0; j < KW; ++j) {
+        float4 kv = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (kb + j < nk) kv = *reinterpret_cast<const float4*>(ks + (kb + j) * ds + 4 * lane);
+        const float2 k01 = make_float2(kv.x, kv.y), k23 = make_float2(kv.z, kv.w);
+#pragma unroll
+        for (int h = 0; h < 8; ++h) {
+          if (h < G) {
+            float2 t = __ffma2_rn(make_float2(q[h].x, q[h].y), k01, make_float2(0.f, 0.f));
+            t = __ffma2_rn(make_float2(q[h].z, q[h].w), k23, t);
+            s[4 * h + j] = __fadd_rn(t.x, t.y);
+          } else {
+            s[4 * h + j] = 0.0f;
+          }
+        }
+      }
+      halve_sum<32>(s, lane & 16, 16);
+      halve_sum<16>(s, lane & 8, 8);
+      halve_sum<8>(s, lane & 4, 4);
+      halve_sum<4>(s, lane & 2, 2);
+      halve_sum<2>(s, lane & 1, 1);
+      // online softmax of head hl over the warp's keys of this tile
+      const bool valid = hl < G && kb + jl < nk;
+      const float sc = valid ? __fmul_rn(s[0], scale) : -INFINITY;
+      float mx = fmaxf(sc, __shfl_xor_sync(0xffffffffu, sc, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      const float mn = fmaxf(m_h, mx);
+      const float cf = mn == -INFINITY ? 1.0f : expf(m_h - mn);
+      const float p = valid ? expf(sc - mn) : 0.0f;
+      float ps = __fadd_rn(p, __shfl_xor_sync(0xffffffffu, p, 1));
+      ps = __fadd_rn(ps, __shfl_xor_sync(0xffffffffu, ps, 2));
+      l_h = fmaf(l_h, cf, ps);
+      m_h = mn;
+      // p * v on this lane's 4 dims of every head
+#pragma unroll
+      for (int h = 0; h < G; ++h) {
+        const float c = __shfl_sync(0xffffffffu, cf, 4 * h);
+        acc[h].x *= c;
+        acc[h].y *= c;
+        acc[h].z *= c;
+        acc[h].w *= c;
+      }
+#pragma unroll
+      for (int j = 0; j < KW; ++j) {
+        if (kb + j < nk) {  // warp-uniform
+          const float4 v = *reinterpret_cast<const float4*>(vs + (kb + j) * ds + 4 * lane);
+          const float2 v01 = make_float2(v.x, v.y), v23 = make_float2(v.z, v.w);
+#pragma unroll
+          for (int h = 0; h < G; ++h) {
+            const float pj = __shfl_sync(0xffffffffu, p, 4 * h + j);
+            const float2 pp = make_float2(pj, pj);
+            const float2 a01 = __ffma2_rn(pp, v01, make_float2(acc[h].x, acc[h].y));
+            const float2 a23 = __ffma2_rn(pp, v23, make_float2(acc[h].z, acc[h].w));
+            acc[h] = make_float4(a01.x, a01.y, a23.x, a23.y);
+          }
+        }
+      }
+    }
+    if (cur.tile + 1 == cur.nt) {  // the item is done: combine the warps' states
+      __syncthreads();             // every warp is done with this slot's tile
+      float* wacc = sm + slot * SLOT;             // [warp][head][D]
+      float* wml = wacc + kAttnWarps * G * D;     // [warp][head] (max, sum)
+#pragma unroll
+      for (int h = 0; h < G; ++h)
+        *reinterpret_cast<float4*>(wacc + (warp * G + h) * D + 4 * lane) = acc[h];
+      if (jl == 0 && hl < G) {
+        wml[2 * (warp * G + hl)] = m_h;
+        wml[2 * (warp * G + hl) + 1] = l_h;
+      }
+      __syncthreads();
+      const size_t base = ((size_t)cur.t * Hq + (size_t)cur.g * G) * ns + cur.s;
+      for (int o = threadIdx.x; o < G * V4; o += kT) {  // (head, 4 dims)
+        const int h = o / V4, e = (o - h * V4) * 4;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, wml[2 * (w * G + h)]);
+        float L = 0.0f;
+        float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int w = 0; w < kAttnWarps; ++w) {
+          const float mw = wml[2 * (w * G + h)];
+          const float f = mw == -INFINITY ? 0.0f : expf(mw - M);
+          const float4 a = *reinterpret_cast<const float4*>(wacc + (w * G + h) * D + e);
+          L = fmaf(wml[2 * (w * G + h) + 1], f, L);
+          O.x = fmaf(a.x, f, O.x);
+          O.y = fmaf(a.y, f, O.y);
+          O.z = fmaf(a.z, f, O.z);
+          O.w = fmaf(a.w, f, O.w);
+        }
+        *reinterpret_cast<float4*>(o_part + (base + (size_t)h * ns) * D + e) = O;
+        if (e == 0) ml[base + (size_t)h * ns] = make_float2(M, L);
+      }
+    }
+    __syncthreads();  // this slot is consumed
+    cur = nxt;
+    nxt = nxt2;
+    slot = slot == 2 ? 0 : slot + 1;
   }
 }
 
@@ -979,7 +1214,27 @@ cudaError_t pf_init() {
   MYOS_PF_SMEM(float, 128)
   MYOS_PF_SMEM(__nv_bfloat16, 64)
   MYOS_PF_SMEM(__nv_bfloat16, 128)
+#define MYOS_PF_SMEM_W(KT, G)                                                              \
+  if (cudaError_t e = cudaFuncSetAttribute(k_pf_attn_warps<KT, G>,                         \
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize,    \
+                                           (int)kWarpsSmem))                               \
+    return e;                                                                              \
+  if (cudaError_t e = cudaFuncSetAttribute(k_pf_attn_warps<KT, G>,                         \
+                                           cudaFuncAttributePreferredSharedMemoryCarveout, \
+                                           100))                                           \
+    return e;
+  MYOS_PF_SMEM_W(float, 5)
+  MYOS_PF_SMEM_W(float, 6)
+  MYOS_PF_SMEM_W(float, 7)
+  MYOS_PF_SMEM_W(float, 8)
+  MYOS_PF_SMEM_W(__nv_bfloat16, 5)
+  MYOS_PF_SMEM_W(__nv_bfloat16, 6)
+  MYOS_PF_SMEM_W(__nv_bfloat16, 7)
+  MYOS_PF_SMEM_W(__nv_bfloat16, 8)
+#undef MYOS_PF_SMEM_W
 #undef MYOS_PF_SMEM
+  const char* aw = getenv("MYOS_PF_ATTN_WARPS");
+  g_attn_warps = !(aw && aw[0] == '0');
   const int rows_smem = (int)attn_rows_smem_bytes<128>(8);
   if (cudaError_t e = cudaFuncSetAttribute(
           k_pf_attn_rows<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, rows_smem))
@@ -1028,6 +1283,26 @@ cudaError_t pf_attn(uint16_t* A, float* o_part, float2* ml, const float* Q, cons
   const long items = (long)n * Hkv * ns;
   const dim3 grid((unsigned)std::min<long>(items, 2L * sms));  // two resident blocks per SM
   cudaError_t e = cudaSuccess;
+  const int G = Hq / Hkv;
+  if (g_attn_warps && d == 128 && G >= 5 && G <= 8) {
+    const size_t smem = kWarpsSmem;
+#define MYOS_PF_ATTN_W(GG)                                                                     \
+  if (G == GG)                                                                                 \
+    e = kv_bf16 ? launch(k_pf_attn_warps<__nv_bfloat16, GG>, grid, kT, smem, st, o_part, ml, Q, \
+                         (const __nv_bfloat16*)kc, (const __nv_bfloat16*)vc, p0, n, Hq, Hkv, S, \
+                         scale, ch, ns, rowpos, rowstride)                                      \
+                : launch(k_pf_attn_warps<float, GG>, grid, kT, smem, st, o_part, ml, Q,         \
+                         (const float*)kc, (const float*)vc, p0, n, Hq, Hkv, S, scale, ch, ns,  \
+                         rowpos, rowstride);
+    MYOS_PF_ATTN_W(5)
+    MYOS_PF_ATTN_W(6)
+    MYOS_PF_ATTN_W(7)
+    MYOS_PF_ATTN_W(8)
+#undef MYOS_PF_ATTN_W
+    if (e != cudaSuccess) return e;
+    return launch(k_pf_attn_merge<128>, dim3(n, (Hq + 3) / 4), 128, 0, st, A, o_part, ml, p0, Hq,
+                  ch, ns, rowpos);
+  }
 #define MYOS_PF_ATTN(D)                                                                         \
   if (d == D) {                                                                                 \
     const size_t smem = attn_smem_bytes<D>();                                                   \

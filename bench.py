@@ -74,11 +74,22 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
         except Exception:
             self.proc = None
+
+    def ready(self, timeout_s: float = 15.0):
+        """Wait until nvidia-smi prints its first sample (its start-up can
+        outlast a short timed region), then drop what came before, so that
+        every kept sample falls inside the region that follows."""
+        if not self.proc:
+            return
+        t0 = time.time()
+        while not self.lines and time.time() - t0 < timeout_s and self.proc.poll() is None:
+            time.sleep(0.02)
+        self.lines = []
 
     def _read(self):
         for line in self.proc.stdout:
@@ -464,9 +475,10 @@ def run_ours(args, world, rank, local, pg):
     for _ in range(max(args.warmup, 3)):
         one_step()
     # device-timed region (CUDA events inside the library's stream)
-    barrier(pg)
     clocks = ClockSampler(local)
     clocks.start()
+    clocks.ready()
+    barrier(pg)
     launches0 = eng.launch_count()
     pre_ms, dec_ms = [], []
     ids = None
