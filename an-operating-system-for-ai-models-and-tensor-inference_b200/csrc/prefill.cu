@@ -38,6 +38,14 @@ int g_rows_min = 1024;
 // (k_pf_attn_warps; D = 128, 5..8 query heads per KV head); MYOS_PF_ATTN_WARPS
 // at pf_init, 0: the dims-split k_pf_attn_split
 bool g_attn_warps = true;
+// with it, the last split of a (row, KV head) merges the splits
+// (MYOS_PF_MERGE_FUSED at pf_init, 0: a separate merge launch)
+bool g_merge_fused = true;
+// items per block up to which the merge is fused (measured: a 128-id prompt
+// chunk, 1.7 items a block, 2.52 -> 2.46 ms; 64 batched rows at 512 keys,
+// 3.9 items, 2.775 -> 2.783 ms per step; 256-row chunks of 512-id prompts,
+// 14 items, 645 -> 726 ms)
+constexpr int kMergeFusedItems = 2;
 
 MYOS_DEV void pdl_begin() {
   pdl_wait();
@@ -450,6 +458,37 @@ __global__ void __launch_bounds__(kT, 2) k_pf_attn_split(float* o_part, float2* 
   }
 }
 
+// out = (sum over splits of o_s * e^(m_s - M)) / (sum of l_s * e^(m_s - M)),
+// M the largest split maximum, for query head h of row t over its nsr
+// splits; written into A as the three bf16 terms of the o_proj input (n
+// rows, row length Hq * D). One warp: lanes hold the split weights (s =
+// lane, lane + 32), then D/32 dims each, splits in order. The partials are
+// read through L2 (other blocks may have written them in this launch).
+template <int D>
+MYOS_DEV void merge_head(uint16_t* A, const float* o_part, const float2* ml, int n, int t, int h,
+                         int Hq, int ns, int nsr, int lane) {
+  constexpr int E = D / 32;
+  const size_t base = ((size_t)t * Hq + h) * ns;
+  const float2 a0 = lane < nsr ? __ldcg(ml + base + lane) : make_float2(-INFINITY, 0.0f);
+  const float2 a1 = lane + 32 < nsr ? __ldcg(ml + base + lane + 32) : make_float2(-INFINITY, 0.0f);
+  const float M = warp_max(fmaxf(a0.x, a1.x));
+  const float w0 = lane < nsr ? expf(a0.x - M) : 0.0f;
+  const float w1 = lane + 32 < nsr ? expf(a1.x - M) : 0.0f;
+  const float L = warp_sum(fmaf(a1.y, w1, __fmul_rn(a0.y, w0)));
+  float o[E];
+#pragma unroll
+  for (int e = 0; e < E; ++e) o[e] = 0.0f;
+  const float* op = o_part + base * D + lane * E;
+#pragma unroll 4
+  for (int s = 0; s < nsr; ++s) {
+    const float w = __shfl_sync(0xffffffffu, s < 32 ? w0 : w1, s & 31);
+#pragma unroll
+    for (int e = 0; e < E; ++e) o[e] = fmaf(__ldcg(op + (size_t)s * D + e), w, o[e]);
+  }
+#pragma unroll
+  for (int e = 0; e < E; ++e) put_split(A, n, t, Hq * D, h * D + lane * E + e, __fdiv_rn(o[e], L));
+}
+
 // One step of the halving exchange that sums a warp's partial dot products:
 // of the first N values a lane keeps the half its `bit` selects (the upper
 // half when set), adds its partner's (lane ^ off) copy of that half and
@@ -486,7 +525,8 @@ __global__ void __launch_bounds__(kT, 2) k_pf_attn_warps(float* o_part, float2* 
                                                          const KT* kcache, const KT* vcache, int p0,
                                                          int n, int Hq, int Hkv, int S, float scale,
                                                          int ch, int ns, const int* rowpos,
-                                                         size_t rowstride) {
+                                                         size_t rowstride, uint16_t* A,
+                                                         unsigned* arrive) {
   pdl_begin();  // the previous kernel of the stream has finished (PDL)
   constexpr int D = 128, ds = D, V4 = D / 4;  // rows unpadded: a warp reads whole rows
   constexpr int SLOT = kWarpsSlot;
@@ -673,6 +713,24 @@ __global__ void __launch_bounds__(kT, 2) k_pf_attn_warps(float* o_part, float2* 
         *reinterpret_cast<float4*>(o_part + (base + (size_t)h * ns) * D + e) = O;
         if (e == 0) ml[base + (size_t)h * ns] = make_float2(M, L);
       }
+      if (arrive) {  // the last split of (row, KV head) to finish merges them
+        __shared__ int merge_n;
+        __syncthreads();  // the block's partials are written ...
+        if (threadIdx.x == 0) {
+          __threadfence();  // ... and visible device-wide before it counts
+          const int pos = rowpos ? rowpos[cur.t] : p0 + cur.t;
+          const int nsr = min(ns, pos / ch + 1);  // splits holding keys of this row
+          unsigned* cnt = arrive + (size_t)cur.t * Hkv + cur.g;
+          const bool last = atomicAdd(cnt, 1u) == (unsigned)(nsr - 1);
+          if (last) *cnt = 0u;  // ready for the next launch
+          merge_n = last ? nsr : 0;
+        }
+        __syncthreads();
+        if (merge_n && warp < G) {
+          __threadfence();
+          merge_head<D>(A, o_part, ml, n, cur.t, cur.g * G + warp, Hq, ns, merge_n, lane);
+        }
+      }
     }
     __syncthreads();  // this slot is consumed
     cur = nxt;
@@ -857,40 +915,17 @@ __global__ void __launch_bounds__(256) k_pf_attn_rows(float* o_part, float2* ml,
   }
 }
 
-// out = (sum over splits of o_s * e^(m_s - M)) / (sum of l_s * e^(m_s - M)),
-// M the largest split maximum; written into A as the three bf16 terms of the
-// o_proj input (row length Hq * D). One warp per (row, head): lanes hold the
-// split weights (s = lane, lane + 32), then D/32 dims each, splits in order.
+// One warp per (row, head) over merge_head (the kernel form of the merge).
 template <int D>
 __global__ void __launch_bounds__(128) k_pf_attn_merge(uint16_t* A, const float* o_part,
                                                        const float2* ml, int p0, int Hq, int ch,
                                                        int ns, const int* rowpos) {
   pdl_begin();  // the previous kernel of the stream has finished (PDL)
-  constexpr int E = D / 32;
   const int t = blockIdx.x, n = gridDim.x, lane = threadIdx.x & 31;
   const int h = blockIdx.y * 4 + (threadIdx.x >> 5);
   if (h >= Hq) return;
   const int pos = rowpos ? rowpos[t] : p0 + t;
-  const int nsr = min(ns, pos / ch + 1);  // splits holding keys of this row
-  const size_t base = ((size_t)t * Hq + h) * ns;
-  const float2 a0 = lane < nsr ? ml[base + lane] : make_float2(-INFINITY, 0.0f);
-  const float2 a1 = lane + 32 < nsr ? ml[base + lane + 32] : make_float2(-INFINITY, 0.0f);
-  const float M = warp_max(fmaxf(a0.x, a1.x));
-  const float w0 = lane < nsr ? expf(a0.x - M) : 0.0f;
-  const float w1 = lane + 32 < nsr ? expf(a1.x - M) : 0.0f;
-  const float L = warp_sum(fmaf(a1.y, w1, __fmul_rn(a0.y, w0)));
-  float o[E];
-#pragma unroll
-  for (int e = 0; e < E; ++e) o[e] = 0.0f;
-  const float* op = o_part + base * D + lane * E;
-#pragma unroll 4
-  for (int s = 0; s < nsr; ++s) {
-    const float w = __shfl_sync(0xffffffffu, s < 32 ? w0 : w1, s & 31);
-#pragma unroll
-    for (int e = 0; e < E; ++e) o[e] = fmaf(op[(size_t)s * D + e], w, o[e]);
-  }
-#pragma unroll
-  for (int e = 0; e < E; ++e) put_split(A, n, t, Hq * D, h * D + lane * E + e, __fdiv_rn(o[e], L));
+  merge_head<D>(A, o_part, ml, n, t, h, Hq, ns, min(ns, pos / ch + 1), lane);
 }
 
 // X[t] += projection (the residual after o_proj / down_proj); then, with
@@ -1235,6 +1270,8 @@ cudaError_t pf_init() {
 #undef MYOS_PF_SMEM
   const char* aw = getenv("MYOS_PF_ATTN_WARPS");
   g_attn_warps = !(aw && aw[0] == '0');
+  const char* mf = getenv("MYOS_PF_MERGE_FUSED");
+  g_merge_fused = !(mf && mf[0] == '0');
   const int rows_smem = (int)attn_rows_smem_bytes<128>(8);
   if (cudaError_t e = cudaFuncSetAttribute(
           k_pf_attn_rows<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, rows_smem))
@@ -1259,7 +1296,7 @@ int pf_attn_splits(int max_keys, int* ch) {
 cudaError_t pf_attn(uint16_t* A, float* o_part, float2* ml, const float* Q, const void* kc,
                     const void* vc, int kv_bf16, int p0, int n, int Hq, int Hkv, int d, int S,
                     float scale, int max_keys, int sms, cudaStream_t st, const int* rowpos,
-                    size_t rowstride) {
+                    size_t rowstride, unsigned* arrive) {
   if (!pf_attn_supported(d, Hq / Hkv) || max_keys < 1 || sms < 1) return cudaErrorInvalidValue;
   if (!rowpos && d == 128 && max_keys >= g_rows_min) {  // a long prompt chunk: row tiles
     int ch = 256;
@@ -1286,20 +1323,23 @@ cudaError_t pf_attn(uint16_t* A, float* o_part, float2* ml, const float* Q, cons
   const int G = Hq / Hkv;
   if (g_attn_warps && d == 128 && G >= 5 && G <= 8) {
     const size_t smem = kWarpsSmem;
+    // the merge sits on a block's path at an item's end: fused only while a
+    // block has few items (many items: one merge launch is cheaper)
+    if (!g_merge_fused || items > kMergeFusedItems * (long)grid.x) arrive = nullptr;
 #define MYOS_PF_ATTN_W(GG)                                                                     \
   if (G == GG)                                                                                 \
     e = kv_bf16 ? launch(k_pf_attn_warps<__nv_bfloat16, GG>, grid, kT, smem, st, o_part, ml, Q, \
                          (const __nv_bfloat16*)kc, (const __nv_bfloat16*)vc, p0, n, Hq, Hkv, S, \
-                         scale, ch, ns, rowpos, rowstride)                                      \
+                         scale, ch, ns, rowpos, rowstride, A, arrive)                           \
                 : launch(k_pf_attn_warps<float, GG>, grid, kT, smem, st, o_part, ml, Q,         \
                          (const float*)kc, (const float*)vc, p0, n, Hq, Hkv, S, scale, ch, ns,  \
-                         rowpos, rowstride);
+                         rowpos, rowstride, A, arrive);
     MYOS_PF_ATTN_W(5)
     MYOS_PF_ATTN_W(6)
     MYOS_PF_ATTN_W(7)
     MYOS_PF_ATTN_W(8)
 #undef MYOS_PF_ATTN_W
-    if (e != cudaSuccess) return e;
+    if (e != cudaSuccess || arrive) return e;
     return launch(k_pf_attn_merge<128>, dim3(n, (Hq + 3) / 4), 128, 0, st, A, o_part, ml, p0, Hq,
                   ch, ns, rowpos);
   }
