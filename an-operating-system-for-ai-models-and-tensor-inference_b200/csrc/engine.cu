@@ -128,6 +128,8 @@ struct myos_ctx {
   size_t at_o_bytes = 0, at_ml_bytes = 0;
   unsigned* at_arrive = nullptr;  // per (row, KV head) split arrivals (zero between launches)
   size_t at_arrive_bytes = 0;
+  unsigned* at_work = nullptr;    // the split attention's item queue (zero between launches)
+  size_t at_work_bytes = 0;
   float2* bt_amax = nullptr;  // per-chunk argmax candidates of the batched head
   size_t bt_amax_bytes = 0;
   size_t bt_out_n = 0, bt_ids_n = 0;
@@ -1180,7 +1182,7 @@ void myos_ctx_destroy(myos_ctx* c) {
                  (void*)c->ktrace, c->pf_X, c->pf_D, c->pf_Q, c->pf_A, c->pf_ws,
                  c->bt_k, c->bt_v, c->bt_X, c->bt_D, c->bt_pos, c->bt_rows, c->bt_tok,
                  c->bt_out, c->bt_ids, c->bt_feed, c->tp_part, c->tp_cand, c->tp_link,
-                 c->at_o, (void*)c->at_ml, (void*)c->at_arrive, (void*)c->bt_amax, c->bt_step};
+                 c->at_o, (void*)c->at_ml, (void*)c->at_arrive, (void*)c->at_work, (void*)c->bt_amax, c->bt_step};
   for (void* p : dev)
     if (p) cudaFree(p);
   for (int i = 0; i < 2; ++i) {
@@ -1540,6 +1542,10 @@ static int attn_scratch(myos_ctx* c, int rows, int max_keys) {
   if (!st) st = grow(c, &c->at_arrive, &c->at_arrive_bytes,
                      (size_t)rows * c->s.num_kv_heads * sizeof(unsigned));
   if (!st && c->at_arrive_bytes != had) CK(cudaMemsetAsync(c->at_arrive, 0, c->at_arrive_bytes, c->st));
+  if (!st && !c->at_work) {
+    st = grow(c, &c->at_work, &c->at_work_bytes, 2 * sizeof(unsigned));
+    if (!st) CK(cudaMemsetAsync(c->at_work, 0, c->at_work_bytes, c->st));
+  }
   return st;
 }
 
@@ -1617,7 +1623,7 @@ int prefill_chunk(myos_ctx* c, const uint32_t* d_ids, int n, int p0, void* kcach
     CK(pf_qkv_post(c->pf_Q, c->pf_D, sp, w.bqkv, kc, vc, kv_bf16, c->cos_t, c->sin_t, p0, n, Hq,
                    Hkv, d, S, st));
     CK(pf_attn(c->pf_A, c->at_o, c->at_ml, c->pf_Q, kc, vc, kv_bf16, p0, n, Hq, Hkv, d, S, scale,
-               p0 + n, c->num_sms, st, nullptr, 0, c->at_arrive));
+               p0 + n, c->num_sms, st, nullptr, 0, c->at_arrive, c->at_work));
     if ((rc = gemm(H, qd, w.wo, (int)c->qd_pad))) return rc;
     if ((rc = resid(n, H, w.ln2))) return rc;
     if ((rc = gemm(2 * I, H, w.wg))) return rc;  // gate rows then up rows
@@ -1761,7 +1767,7 @@ static int batch_run(myos_ctx* c, size_t nseq, const uint32_t* ids, const uint32
       CK(pf_qkv_post(c->pf_Q, c->pf_D, sp, w.bqkv, kc, vc, kv_bf16, c->cos_t, c->sin_t, 0, B, Hq,
                      Hkv, d, Sb, stq, c->bt_pos, seq_elems));
       CK(pf_attn(c->pf_A, c->at_o, c->at_ml, c->pf_Q, kc, vc, kv_bf16, 0, B, Hq, Hkv, d, Sb, scale,
-                 max_keys, c->num_sms, stq, c->bt_pos, seq_elems, c->at_arrive));
+                 max_keys, c->num_sms, stq, c->bt_pos, seq_elems, c->at_arrive, c->at_work));
       if ((st = gemm(H, qd, w.wo))) return st;
       CK(pf_resid_norm(c->bt_X, c->pf_D, sp, w.ln2, c->pf_A, B, H, s.rms_eps, stq));
       if ((st = gemm(2 * I, H, w.wg))) return st;

@@ -46,6 +46,14 @@ bool g_merge_fused = true;
 // 3.9 items, 2.775 -> 2.783 ms per step; 256-row chunks of 512-id prompts,
 // 14 items, 645 -> 726 ms)
 constexpr int kMergeFusedItems = 2;
+// with it, blocks past their first item take items from a shared queue
+// (MYOS_PF_ATTN_DYN at pf_init, 0: a fixed stride over the items) when a
+// block has more than kAttnDynItems items on average (measured: 256-row
+// chunks of 512-id prompts, 14 items a block, 64 prompts 658 -> 607 ms; 64
+// batched rows, 3.9 items, 2.821 -> 2.848 ms per step; a 128-id chunk, 1.7
+// items, 2.49 -> 2.57 ms: the first pending item's atomic delays every block)
+bool g_attn_dyn = true;
+constexpr int kAttnDynItems = 4;
 
 MYOS_DEV void pdl_begin() {
   pdl_wait();
@@ -526,7 +534,7 @@ __global__ void __launch_bounds__(kT, 2) k_pf_attn_warps(float* o_part, float2* 
                                                          int n, int Hq, int Hkv, int S, float scale,
                                                          int ch, int ns, const int* rowpos,
                                                          size_t rowstride, uint16_t* A,
-                                                         unsigned* arrive) {
+                                                         unsigned* arrive, unsigned* work) {
   pdl_begin();  // the previous kernel of the stream has finished (PDL)
   constexpr int D = 128, ds = D, V4 = D / 4;  // rows unpadded: a warp reads whole rows
   constexpr int SLOT = kWarpsSlot;
@@ -539,11 +547,31 @@ __global__ void __launch_bounds__(kT, 2) k_pf_attn_warps(float* o_part, float2* 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int N = (Hq + 2 * Hkv) * D;
 
+  // Static items (work null): block b takes the non-empty items among b,
+  // b + grid, ... Dynamic items: block b starts on item b (or the queue's
+  // first non-empty one), then takes the queue's next: work[0] counts the
+  // items handed out past the grid, work[1] the blocks done, and the last
+  // block done resets both. Thread 0 takes an item a tile ahead of its use
+  // (`pending`, passed through shared memory at the tile's end barrier).
+  __shared__ int s_q[2];
+  int pending = n_items;
+  auto item_empty = [&](int item) {  // a split past its row's last key
+    const int t = item / (ns * Hkv);
+    return (item % ns) * ch > (rowpos ? rowpos[t] : p0 + t);
+  };
+  auto take = [&](unsigned ticket) {  // thread 0: the first non-empty item from a ticket on
+    int i = (int)gridDim.x + (int)ticket;
+    while (i < n_items && item_empty(i)) i = (int)gridDim.x + (int)atomicAdd(work, 1u);
+    return min(i, n_items);
+  };
   auto open_item = [&](AttnItem& it, int item) {  // first non-empty item from `item` on
     for (; item < n_items; item += gridDim.x) {
       const int s = item % ns, g = (item / ns) % Hkv, t = item / (ns * Hkv);
       const int pos = rowpos ? rowpos[t] : p0 + t, k0 = s * ch;
-      if (k0 > pos) continue;  // this row has fewer splits
+      if (k0 > pos) {  // this row has fewer splits
+        if (work) break;  // (never: the queue hands out non-empty items)
+        continue;
+      }
       it.item = item;
       it.tile = 0;
       it.t = t;
@@ -556,9 +584,14 @@ __global__ void __launch_bounds__(kT, 2) k_pf_attn_warps(float* o_part, float2* 
     }
     it.item = n_items;
   };
-  auto advance = [&](AttnItem it) {
+  auto advance = [&](AttnItem it, bool& used) {
     if (++it.tile < it.nt) return it;
-    open_item(it, it.item + gridDim.x);
+    if (work) {
+      used = true;
+      open_item(it, pending);
+    } else {
+      open_item(it, it.item + gridDim.x);
+    }
     return it;
   };
   auto stage = [&](const AttnItem& it, int slot) {
@@ -593,19 +626,43 @@ __global__ void __launch_bounds__(kT, 2) k_pf_attn_warps(float* o_part, float2* 
   float m_h = -INFINITY, l_h = 0.0f;  // head hl over this warp's keys of the item
 
   AttnItem cur;
-  open_item(cur, blockIdx.x);
-  if (cur.item >= n_items) return;
-  stage(cur, 0);
-  AttnItem nxt = advance(cur);
-  if (nxt.item < n_items) stage(nxt, 1);
-  else cp_async_commit();  // an empty group keeps one group per tile
+  if (work) {
+    if (threadIdx.x == 0) {
+      const int first = item_empty(blockIdx.x) ? take(atomicAdd(work, 1u)) : (int)blockIdx.x;
+      s_q[0] = first;
+      s_q[1] = first < n_items ? take(atomicAdd(work, 1u)) : n_items;
+    }
+    __syncthreads();
+    open_item(cur, s_q[0]);
+    pending = s_q[1];
+  } else {
+    open_item(cur, blockIdx.x);
+  }
+  AttnItem nxt = cur;
+  if (cur.item < n_items) {
+    stage(cur, 0);
+    bool used = false;
+    nxt = advance(cur, used);
+    if (nxt.item < n_items) stage(nxt, 1);
+    else cp_async_commit();  // an empty group keeps one group per tile
+    if (used) {              // block-uniform: refill the pending item
+      __syncthreads();
+      if (threadIdx.x == 0) s_q[1] = pending < n_items ? take(atomicAdd(work, 1u)) : n_items;
+      __syncthreads();
+      pending = s_q[1];
+    }
+  }
   int slot = 0;
   while (cur.item < n_items) {
-    const AttnItem nxt2 = advance(nxt);
+    bool used = false;
+    const AttnItem nxt2 = advance(nxt, used);
     if (nxt2.item < n_items) stage(nxt2, slot == 0 ? 2 : slot - 1);
     else cp_async_commit();
     cp_async_wait<2>();  // this tile's group has landed; two more in flight
     __syncthreads();     // every thread's copies of this tile are visible
+    // the refill's ticket now, its use at the tile's end (latency hidden)
+    const bool refill = used && threadIdx.x == 0 && pending < n_items;
+    const unsigned ticket = refill ? atomicAdd(work, 1u) : 0u;
     const float* qs = sm + slot * SLOT;
     const float* ks = qs + 8 * D;
     const float* vs = ks + kAttnTile * ds;
@@ -732,10 +789,16 @@ __global__ void __launch_bounds__(kT, 2) k_pf_attn_warps(float* o_part, float2* 
         }
       }
     }
+    if (used && threadIdx.x == 0) s_q[1] = refill ? take(ticket) : n_items;
     __syncthreads();  // this slot is consumed
+    if (used) pending = s_q[1];
     cur = nxt;
     nxt = nxt2;
     slot = slot == 2 ? 0 : slot + 1;
+  }
+  if (work && threadIdx.x == 0 && atomicAdd(work + 1, 1u) == gridDim.x - 1) {
+    work[0] = 0u;  // every block has taken its last item: the queue is
+    work[1] = 0u;  // ready for the next launch
   }
 }
 
@@ -1272,6 +1335,8 @@ cudaError_t pf_init() {
   g_attn_warps = !(aw && aw[0] == '0');
   const char* mf = getenv("MYOS_PF_MERGE_FUSED");
   g_merge_fused = !(mf && mf[0] == '0');
+  const char* ad = getenv("MYOS_PF_ATTN_DYN");
+  g_attn_dyn = !(ad && ad[0] == '0');
   const int rows_smem = (int)attn_rows_smem_bytes<128>(8);
   if (cudaError_t e = cudaFuncSetAttribute(
           k_pf_attn_rows<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, rows_smem))
@@ -1296,7 +1361,7 @@ int pf_attn_splits(int max_keys, int* ch) {
 cudaError_t pf_attn(uint16_t* A, float* o_part, float2* ml, const float* Q, const void* kc,
                     const void* vc, int kv_bf16, int p0, int n, int Hq, int Hkv, int d, int S,
                     float scale, int max_keys, int sms, cudaStream_t st, const int* rowpos,
-                    size_t rowstride, unsigned* arrive) {
+                    size_t rowstride, unsigned* arrive, unsigned* work) {
   if (!pf_attn_supported(d, Hq / Hkv) || max_keys < 1 || sms < 1) return cudaErrorInvalidValue;
   if (!rowpos && d == 128 && max_keys >= g_rows_min) {  // a long prompt chunk: row tiles
     int ch = 256;
@@ -1326,14 +1391,15 @@ cudaError_t pf_attn(uint16_t* A, float* o_part, float2* ml, const float* Q, cons
     // the merge sits on a block's path at an item's end: fused only while a
     // block has few items (many items: one merge launch is cheaper)
     if (!g_merge_fused || items > kMergeFusedItems * (long)grid.x) arrive = nullptr;
+    if (!g_attn_dyn || items <= kAttnDynItems * (long)grid.x) work = nullptr;
 #define MYOS_PF_ATTN_W(GG)                                                                     \
   if (G == GG)                                                                                 \
     e = kv_bf16 ? launch(k_pf_attn_warps<__nv_bfloat16, GG>, grid, kT, smem, st, o_part, ml, Q, \
                          (const __nv_bfloat16*)kc, (const __nv_bfloat16*)vc, p0, n, Hq, Hkv, S, \
-                         scale, ch, ns, rowpos, rowstride, A, arrive)                           \
+                         scale, ch, ns, rowpos, rowstride, A, arrive, work)                     \
                 : launch(k_pf_attn_warps<float, GG>, grid, kT, smem, st, o_part, ml, Q,         \
                          (const float*)kc, (const float*)vc, p0, n, Hq, Hkv, S, scale, ch, ns,  \
-                         rowpos, rowstride, A, arrive);
+                         rowpos, rowstride, A, arrive, work);
     MYOS_PF_ATTN_W(5)
     MYOS_PF_ATTN_W(6)
     MYOS_PF_ATTN_W(7)

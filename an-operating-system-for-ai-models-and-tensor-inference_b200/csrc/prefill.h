@@ -41,14 +41,16 @@ bool pf_pdl();
 // come from the caller, sized by pf_attn_splits(max_keys) for the largest
 // position + 1 of any row. arrive (n * Hkv zeroed counters, left zeroed):
 // where the key-split kernel runs, the last split of each (row, KV head) to
-// finish merges that row's heads itself instead of a merge launch.
+// finish merges that row's heads itself instead of a merge launch. work (2
+// zeroed counters, left zeroed): the key-split kernel's blocks take items
+// past their first from a shared queue instead of a fixed stride.
 constexpr int kAttnMaxSplits = 64;
 int pf_attn_splits(int max_keys, int* ch);
 cudaError_t pf_attn(uint16_t* A, float* o_part, float2* ml, const float* Q, const void* kc,
                     const void* vc, int kv_bf16, int p0, int n, int Hq, int Hkv, int d, int S,
                     float scale, int max_keys, int sms, cudaStream_t st,
                     const int* rowpos = nullptr, size_t rowstride = 0,
-                    unsigned* arrive = nullptr);
+                    unsigned* arrive = nullptr, unsigned* work = nullptr);
 // Greedy token per row of stacked logit parts D[3B, V]; tok[b], and
 // out[b * out_stride + step] when out is non-null. part: B * pf_argmax_chunks(V)
 // float2 of scratch. d_step non-null: step = *d_step, read on the device, and
