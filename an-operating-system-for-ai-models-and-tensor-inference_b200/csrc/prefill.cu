@@ -42,9 +42,10 @@ bool g_attn_warps = true;
 // (MYOS_PF_MERGE_FUSED at pf_init, 0: a separate merge launch)
 bool g_merge_fused = true;
 // items per block up to which the merge is fused (measured: a 128-id prompt
-// chunk, 1.7 items a block, 2.52 -> 2.46 ms; 64 batched rows at 512 keys,
-// 3.9 items, 2.775 -> 2.783 ms per step; 256-row chunks of 512-id prompts,
-// 14 items, 645 -> 726 ms)
+// chunk, 1.7 items a block, 2.52 -> 2.46 ms; 32 batched rows at 512 keys,
+// 1.95 items, 2.24-2.34 -> 2.075 ms per step; 64 batched rows, 3.9 items,
+// 2.775 -> 2.783 ms per step; 256-row chunks of 512-id prompts, 14 items,
+// 645 -> 726 ms)
 constexpr int kMergeFusedItems = 2;
 // with it, blocks past their first item take items from a shared queue
 // (MYOS_PF_ATTN_DYN at pf_init, 0: a fixed stride over the items) when a
